@@ -1,0 +1,519 @@
+"""Benchmark of the B200 MoE FFN layer (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+A step is one MoE layer (router logits, top-k/softmax, dispatch, grouped
+gate/up + GeGLU, down, weighted combine) over one batch of T tokens, through
+the library's public C ABI (mrml_moe_forward).  The headline workload is
+config 2 of the task (Gemma-4-26B-A4B MoE shape: H=2816, E=128, K=8, I=704,
+Q4_0 experts) at decode batch T=64; T=1, T=8 and the config-3 prefill
+(H=1024, E=16, K=2, I=512, Q8_0, T=2048, Zipf-skewed logits) are reported
+under "also".  Data are synthetic (seeded N(0,0.02) weights quantised with
+the reference's rules, N(0,1) activations).
+
+Timing: W untimed warm-up steps, then K steps between CUDA events on the
+launch stream, bracketed by a barrier and torch.cuda.synchronize(); the
+max over ranks is reported.  Consecutive steps rotate over independent layer
+copies whose weights together exceed the 126 MB L2, so every step streams its
+experts from HBM.  `value` is tokens/s with inputs resident in HBM; `e2e`
+adds, every step, the host->device copy of x from pinned memory and the
+device->host copy of the layer output.
+
+With --gpus N > 1 every rank runs its own replica of the layer on its own
+tokens (weak scaling; no collective on the data path).
+
+--impl reference times the reference's CPU algorithm (the C restatement
+under oracle/, the reference's Rust cannot be built here) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _load(name, path):
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def package():
+    moe = _load("mrml_moe_b200", os.path.join(ROOT, "qt_llama.cpp_b200", "mrml_moe.py"))
+    synth = _load("mrml_moe_b200_synth", os.path.join(ROOT, "qt_llama.cpp_b200", "synth.py"))
+    return moe, synth
+
+
+WORKLOADS = {
+    # name: (wtype, H, I, E, K, T, routing)
+    "c2_t64": (2, 2816, 704, 128, 8, 64, "router"),
+    "c2_t8": (2, 2816, 704, 128, 8, 8, "router"),
+    "c2_t1": (2, 2816, 704, 128, 8, 1, "router"),
+    "c3_prefill": (8, 1024, 512, 16, 2, 2048, "zipf_logits"),
+    "c1_t4": (8, 1024, 512, 16, 2, 4, "router"),
+}
+KERNELS = {
+    "router": ["router_logits", "router_topk", "quantize", "dispatch", "gate_up", "down", "combine"],
+    "zipf_logits": ["route_from_logits", "quantize", "dispatch", "gate_up", "down", "combine"],
+}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.gpu)],
+                    capture_output=True, text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([v.strip() for v in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 2 + i and s[2 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+class LayerSet:
+    """Independent copies of one MoE layer on the device (weights + router),
+    enough of them that their weights exceed L2, plus per-step inputs."""
+
+    def __init__(self, moe, synth, device, name, n_inputs, seed=0):
+        import torch
+
+        wtype, H, I, E, K, T, routing = WORKLOADS[name]
+        self.moe, self.device, self.name = moe, device, name
+        self.wtype, self.H, self.I, self.E, self.K, self.T, self.routing = wtype, H, I, E, K, T, routing
+        bb = 18 if wtype == 2 else 34
+        layer_bytes = E * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
+        self.n_layers = max(2, -(-4 * L2_BYTES // layer_bytes))
+        self.layers = []
+        for l in range(self.n_layers):
+            gu, dn = synth.expert_weights_device(seed * 100 + l + 1, wtype, H, I, E, device, moe.quantize)
+            g = torch.Generator(device=device)
+            g.manual_seed(seed * 100 + l + 1000)
+            W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
+            self.layers.append((gu, dn, W))
+        g = torch.Generator(device=device)
+        g.manual_seed(seed + 77)
+        self.xs = [torch.randn((T, H), generator=g, device=device) for _ in range(n_inputs)]
+        if routing == "zipf_logits":
+            bias = torch.from_numpy(synth.zipf_bias(seed + 5, E)).to(device)
+            self.logit_in = [torch.randn((T, E), generator=g, device=device) + bias[None, :] for _ in range(n_inputs)]
+        self.logits = torch.empty(T, E, device=device)
+        self.ids = torch.empty(T, K, dtype=torch.int32, device=device)
+        self.probs = torch.empty(T, K, device=device)
+        self.out = torch.empty(T, H, device=device)
+        self.ws = moe.new_workspace(H, I, E, K, T, device)
+        self.layer_bytes = layer_bytes
+
+    def step(self, i, x=None, out=None):
+        gu, dn, W = self.layers[i % self.n_layers]
+        x = self.xs[i % len(self.xs)] if x is None else x
+        out = self.out if out is None else out
+        m = self.moe
+        if self.routing == "router":
+            m.forward(self.wtype, W, x, x, gu, dn, None, self.logits, self.ids, self.probs, out, self.H, self.I,
+                      self.E, self.K, self.T, self.ws)
+        else:
+            m.route_from_logits(self.logit_in[i % len(self.logit_in)], self.ids, self.probs, self.E, self.K, self.T)
+            m.experts(self.wtype, gu, dn, self.ids, self.probs, None, x, out, self.H, self.I, self.E, self.K, self.T,
+                      self.ws)
+
+    def n_kernels(self):
+        return len(KERNELS[self.routing])
+
+    def unique_experts(self, i):
+        """Experts hit (with alpha > 1e-4) by step i's routing, and the pair count."""
+        self.step(i)
+        ids = self.ids.cpu().numpy()
+        probs = self.probs.cpu().numpy()
+        hit = ids[probs > 1e-4]
+        return len(np.unique(hit)), int(hit.size)
+
+
+def dist_setup(n_gpus):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_steps(ls, steps, warmup, world, start_index=0):
+    """Device time (ms) of `steps` consecutive steps after `warmup` ones."""
+    import torch
+
+    for i in range(warmup):
+        ls.step(start_index + i)
+    barrier(world)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(steps):
+        ls.step(start_index + warmup + i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1), world)
+
+
+def time_kernels(ls, steps, start_index=0):
+    """Per-kernel device times (ms, summed over steps) via the library's
+    profiling hook, which records events around every launch on the stream
+    the kernels run on."""
+    import ctypes
+
+    import torch
+
+    lib = ls.moe.load_library()
+    nk = ls.n_kernels()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * nk * steps)]
+    for e in evs:  # materialise the cudaEvent_t handles
+        e.record()
+    torch.cuda.synchronize()
+    handles = (ctypes.c_void_p * len(evs))(*[e.cuda_event for e in evs])
+    st = lib.mrml_moe_profile_events(handles, len(evs))
+    assert st == 0
+    try:
+        for i in range(steps):
+            ls.step(start_index + i)
+    finally:
+        lib.mrml_moe_profile_events(None, 0)
+    torch.cuda.synchronize()
+    totals = [0.0] * nk
+    for i in range(steps):
+        for k in range(nk):
+            j = 2 * (i * nk + k)
+            totals[k] += evs[j].elapsed_time(evs[j + 1])
+    return dict(zip(KERNELS[ls.routing], totals))
+
+
+def time_e2e(ls, steps, warmup, world):
+    """Same steps through the public API with host buffers: H2D of x from
+    pinned memory and D2H of the output inside the timed region."""
+    import torch
+
+    T, H = ls.T, ls.H
+    host_x = [ls.xs[i % len(ls.xs)].cpu().pin_memory() for i in range(max(steps, 1))]
+    host_out = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    dx = torch.empty((T, H), device=ls.device)
+    s = torch.cuda.current_stream()
+
+    def one(i):
+        dx.copy_(host_x[i % len(host_x)], non_blocking=True)
+        ls.step(i, x=dx)
+        host_out.copy_(ls.out, non_blocking=True)
+
+    for i in range(warmup):
+        one(i)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(steps):
+        one(warmup + i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    return ms, T * H * 4, T * H * 4
+
+
+def algorithmic_bytes(ls, unique, pairs):
+    """Bytes the layer must move at minimum (weights of the experts hit once,
+    router weights, activations in and out, routing outputs)."""
+    wtype, H, I, E, K, T = ls.wtype, ls.H, ls.I, ls.E, ls.K, ls.T
+    bb = 18 if wtype == 2 else 34
+    gu_e = 2 * I * (H // 32) * bb
+    dn_e = H * (I // 32) * bb
+    router = E * H * 4 if ls.routing == "router" else T * E * 4
+    layer = unique * (gu_e + dn_e) + router + T * H * 4 * 2 + T * E * 4 + T * K * 8
+    gate_up = unique * gu_e + T * H + T * (H // 32) * 8 + pairs * I * 4
+    return layer, gate_up
+
+
+def cpu_baseline(oracle, ls, budget_s=12.0):
+    """The reference's CPU algorithm (oracle port) on a bounded sample of the
+    workload's tokens, all host threads, per-token like forward_token."""
+    import torch
+
+    wtype, H, I, E, K, T = ls.wtype, ls.H, ls.I, ls.E, ls.K, ls.T
+    gu, dn, W = ls.layers[0]
+    gu_h, dn_h, W_h = gu.cpu().numpy(), dn.cpu().numpy(), W.cpu().numpy()
+    x = ls.xs[0].cpu().numpy()
+    threads = os.cpu_count() or 1
+    done = 0
+    t0 = time.perf_counter()
+    while done < T and time.perf_counter() - t0 < budget_s:
+        xt = x[done:done + 1]
+        if ls.routing == "router":
+            _, ids, probs = oracle.router(W_h, xt, H, E, K, 1)
+        else:
+            ids, probs = oracle.route_from_logits(ls.logit_in[0][done:done + 1].cpu().numpy(), E, K, 1)
+        oracle.experts(wtype, gu_h, dn_h, ids, probs, None, xt, H, I, E, K, 1, threads)
+        done += 1
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{done} of the {T} tokens of step 0, one token at a time (model.rs forward_token order), "
+                      f"{dt:.1f} s"}
+
+
+def run_ours(args):
+    import torch
+
+    rank, world, local = dist_setup(args.gpus)
+    moe, synth = package()
+    device = torch.device("cuda", local)
+    moe.load_library()
+    steps, warmup = args.steps, args.warmup
+    hbm_peak, peak_kind = peaks()
+
+    ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
+    unique, pairs = ls.unique_experts(0)
+    with ClockSampler(local) as clk:
+        ms = time_steps(ls, steps, warmup, world)
+    kern = time_kernels(ls, steps)
+    e2e_ms, h2d, d2h = time_e2e(ls, steps, warmup, world)
+
+    T = ls.T
+    value = world * T * steps / (ms / 1e3)
+    layer_bytes, gate_up_bytes = algorithmic_bytes(ls, unique, pairs)
+    gu_ms = kern["gate_up"] / steps
+    top = max(kern, key=kern.get)
+    total_kern = sum(kern.values())
+    line = {
+        "metric": "MoE-layer tokens/sec (decode batch 64, Gemma-4-26B-A4B MoE shape); % of HBM roofline",
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": round(ms / steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q4_0 weights x q8_0 activations, int32 block dots, f32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights quantised with the reference's Q4_0 rules, N(0,1) x)",
+        "config": {"workload": args.workload, "hidden": ls.H, "experts": ls.E, "top_k": ls.K, "expert_ffn": ls.I,
+                   "tokens_per_step": T, "weights": "Q4_0" if ls.wtype == 2 else "Q8_0",
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": f"inputs larger than L2: steps rotate over {ls.n_layers} layer copies "
+                         f"({ls.n_layers * ls.layer_bytes / 1e6:.0f} MB of weights)",
+                   "unique_experts_step0": unique},
+        "roofline": {"bound": "hbm", "kernel": "gate_up", "achieved": round(gate_up_bytes / (gu_ms / 1e3) / 1e9, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(gate_up_bytes / (gu_ms / 1e3) / 1e9 / hbm_peak, 4),
+                     "traffic": traffic_from_profile(args.workload), "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": gate_up_bytes, "ms_per_launch": round(gu_ms, 5)},
+        "layer_roofline": {"achieved": round(layer_bytes / (ms / steps / 1e3) / 1e9, 1), "peak": hbm_peak,
+                           "unit": "GB/s", "frac": round(layer_bytes / (ms / steps / 1e3) / 1e9 / hbm_peak, 4),
+                           "algorithmic_bytes_per_step": layer_bytes},
+        "kernel_share": {k: round(v / total_kern, 4) for k, v in kern.items()},
+        "kernel_ms_per_step": {k: round(v / steps, 5) for k, v in kern.items()},
+        "top_kernel": top,
+        "e2e": {"value": round(world * T * steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": ls.n_kernels() * steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
+        line["cpu_baseline"] = cpu_baseline(oracle, ls)
+    if not args.no_also and world == 1:
+        also = {}
+        for name in ("c2_t1", "c2_t8", "c3_prefill"):
+            if name == args.workload:
+                continue
+            del ls
+            torch.cuda.empty_cache()
+            ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank)
+            u, p = ls.unique_experts(0)
+            n = max(steps, 20)
+            m = time_steps(ls, n, max(warmup, 3), world)
+            k = time_kernels(ls, n)
+            lb, gb = algorithmic_bytes(ls, u, p)
+            also[name] = {"tokens_per_s": round(ls.T * n / (m / 1e3), 1), "ms_per_step": round(m / n, 5),
+                          "layer_hbm_frac": round(lb / (m / n / 1e3) / 1e9 / hbm_peak, 4),
+                          "gate_up_hbm_frac": round(gb / (k["gate_up"] / n / 1e3) / 1e9 / hbm_peak, 4),
+                          "kernel_ms_per_step": {kk: round(v / n, 5) for kk, v in k.items()},
+                          "unique_experts_step0": u}
+        line["also"] = also
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def traffic_from_profile(workload):
+    """DRAM bytes per gate_up launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload, {}).get("gate_up")
+    except Exception:
+        return None
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    moe, synth = package()
+    oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
+    wtype, H, I, E, K, T, routing = WORKLOADS[args.workload]
+    # Inputs: the same generator as our arm (device-quantised with the
+    # reference's rules when a GPU is present; host numpy otherwise).
+    if torch.cuda.is_available():
+        dev = torch.device("cuda", 0)
+        gu, dn = synth.expert_weights_device(1, wtype, H, I, E, dev, moe.quantize)
+        gu, dn = gu.cpu().numpy(), dn.cpu().numpy()
+    else:
+        gu, dn = synth.expert_weights(1, wtype, H, I, E)
+    W = synth.normal(1000, E * H, 0.02).reshape(E, H)
+    x = synth.normal(77, T * H).reshape(T, H)
+    bias = synth.zipf_bias(5, E)
+    threads = os.cpu_count() or 1
+    per_step = max(1, min(T, 4))
+
+    def one(i):
+        t0 = (i * per_step) % T
+        xt = x[t0:t0 + per_step]
+        n = xt.shape[0]
+        if routing == "router":
+            _, ids, probs = oracle.router(W, xt, H, E, K, n)
+        else:
+            lg = (synth.normal(900 + i, n * E).reshape(n, E) + bias[None, :]).astype(np.float32)
+            ids, probs = oracle.route_from_logits(lg, E, K, n)
+        for t in range(n):  # forward_token processes one token at a time
+            oracle.experts(wtype, gu, dn, ids[t:t + 1], probs[t:t + 1], None, xt[t:t + 1], H, I, E, K, 1, threads)
+        return n
+
+    for i in range(args.warmup):
+        one(i)
+    t0 = time.perf_counter()
+    tokens = sum(one(args.warmup + i) for i in range(args.steps))
+    dt = time.perf_counter() - t0
+    v = tokens / dt
+    line = {
+        "impl": "reference",
+        "metric": "MoE-layer tokens/sec (decode batch 64, Gemma-4-26B-A4B MoE shape); % of HBM roofline",
+        "value": round(v, 3), "unit": "tokens/s", "higher_is_better": True, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "config": {"workload": args.workload, "hidden": H, "experts": E, "top_k": K, "expert_ffn": I,
+                   "tokens_per_step": per_step},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{per_step} tokens of the {T}-token batch per step, one token at a time"},
+        "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference is Rust (no toolchain here); the oracle/ C restatement of its CPU MoE path is timed",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-also", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

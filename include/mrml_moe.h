@@ -1,0 +1,135 @@
+/*
+ * mrml_moe.h — C ABI of libmrml_moe_b200.so, the B200 (sm_100a) mixture-of-
+ * experts FFN path of the MRML Gemma-4 engine.
+ *
+ * The library is a drop-in for the MoE operator calls of the reference's
+ * Rust operator surface (crates/mrml-tensor/src/cuda.rs):
+ *
+ *   CudaDevice::moe_router            cuda.rs:2808-2838  -> mrml_moe_router (T = 1)
+ *   CudaDevice::moe_router_batch      cuda.rs:2882-2912  -> mrml_moe_router
+ *   CudaDevice::moe_topk_q4_0         cuda.rs:2772-2806  -> mrml_moe_experts (T = 1)
+ *   CudaDevice::moe_topk_batch_q4_0   cuda.rs:2840-2880  -> mrml_moe_experts
+ *
+ * replacing the bodies of the raw launchers launch_rust_moe_router
+ * (cuda.rs:849-897) and launch_rust_moe_topk (cuda.rs:1129-1220).
+ *
+ * Results equal the reference's CPU MoE path (model.rs:1804-1829 router,
+ * model.rs:2111-2165 experts and combine): expert ids and their order are
+ * bit-identical, and the layer output agrees within rel-L2 1e-4.
+ *
+ * Conventions
+ *  - All tensor pointers are device pointers; the caller owns them.  Nothing
+ *    here allocates, frees or synchronises: every call only enqueues work on
+ *    `stream` and is safe to capture into a CUDA graph.
+ *  - Every entry point returns MRML_OK (0) or a negative mrml_status; it
+ *    never aborts the process.  A device-side failure (a bounded wait that
+ *    gave up, an expert id out of range) is recorded in the workspace and
+ *    read back with mrml_moe_device_status.
+ *  - Shapes: H hidden size, I expert FFN size, E experts, K experts per
+ *    token, T tokens.  Expert weights use the GGUF layout the reference
+ *    uploads unchanged (model.rs:726-741): gate_up is [E][2I][H/32] blocks
+ *    (rows [0,I) gate, [I,2I) up) and down is [E][H][I/32] blocks.
+ *    H and I must be multiples of 32; weight pointers 16-byte aligned.
+ *  - Limits: 1 <= K <= 64, K <= E <= 256.
+ */
+#ifndef MRML_MOE_H
+#define MRML_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *mrml_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+typedef enum {
+  MRML_OK = 0,
+  MRML_ERR_INVALID_ARGUMENT = -1,  /* null pointer, bad shape, misaligned weights */
+  MRML_ERR_UNSUPPORTED = -2,       /* weight type or size outside the limits above */
+  MRML_ERR_WORKSPACE_TOO_SMALL = -3,
+  MRML_ERR_CUDA = -4,              /* a CUDA runtime call failed; see cudaGetLastError */
+  MRML_ERR_DEVICE = -5,            /* the device is not an sm_100 GPU */
+  MRML_ERR_DEVICE_TIMEOUT = -6,    /* reported by mrml_moe_device_status */
+  MRML_ERR_BAD_EXPERT_ID = -7,     /* reported by mrml_moe_device_status */
+} mrml_status;
+
+/* GGML type ids (crates/mrml-tensor/src/types.rs:7-27). */
+enum { MRML_Q4_0 = 2, MRML_Q8_0 = 8 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mrml_moe_version(void);
+
+/* Text for a status code (static storage). */
+const char *mrml_moe_status_string(int status);
+
+/* Bytes of device workspace that mrml_moe_router / mrml_moe_experts /
+ * mrml_moe_forward need for these shapes (a multiple of 256).  The
+ * workspace must be 256-byte aligned and may be reused by calls that are
+ * ordered on one stream; concurrent calls need separate workspaces. */
+size_t mrml_moe_workspace_bytes(int H, int I, int E, int K, int T);
+
+/* Clears the status words at the start of a workspace (an async memset on
+ * `stream`).  Call once after allocating a workspace, before its first use. */
+int mrml_moe_workspace_init(void *workspace, size_t workspace_bytes, mrml_stream_t stream);
+
+/* Router: logits[T][E] = x[T][H] . W[E][H]^T, then per token the K best
+ * experts (logit descending, ties to the lower id) and their renormalised
+ * softmax weights ids[T][K], probs[T][K].
+ * Replaces launch_rust_moe_router (cuda.rs:849-897), which always used K=8;
+ * semantics of model.rs:1804-1829.  The ids equal the reference's sequential
+ * f32 logits' ranking bit for bit; logits are within the reference's own
+ * rounding error of it (exact for any expert whose rank was close). */
+int mrml_moe_router(const float *W, const float *x, float *logits, int32_t *ids, float *probs, int H, int E, int K,
+                    int T, void *workspace, size_t workspace_bytes, mrml_stream_t stream);
+
+/* Top-K and softmax from caller-supplied logits[T][E] (model.rs:1816-1829).
+ * Needs no workspace. */
+int mrml_moe_route_from_logits(const float *logits, int32_t *ids, float *probs, int E, int K, int T,
+                               mrml_stream_t stream);
+
+/* Experts and combine: out[T][H] = sum_k probs[t,k] * down_e(geglu(gate_e x,
+ * up_e x)) * down_scale[e], with x quantised to Q8_0 and act re-quantised to
+ * Q8_0 exactly as the reference CPU path does (model.rs:2111-2165); slots
+ * with probs <= 1e-4 are skipped.  down_scale may be NULL (all 1.0).
+ * out is overwritten (the reference's GPU path memsets and accumulates).
+ * Replaces launch_rust_moe_topk (cuda.rs:1129-1220); wtype Q4_0 is the
+ * reference's format, Q8_0 is an extension with the same structure. */
+int mrml_moe_experts(int wtype, const uint8_t *gate_up, const uint8_t *down, const int32_t *ids, const float *probs,
+                     const float *down_scale, const float *x, float *out, int H, int I, int E, int K, int T,
+                     void *workspace, size_t workspace_bytes, mrml_stream_t stream);
+
+/* The whole layer: mrml_moe_router on (router_w, router_x) followed by
+ * mrml_moe_experts on x.  router_x and x may be the same pointer. */
+int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, const float *x, const uint8_t *gate_up,
+                     const uint8_t *down, const float *down_scale, float *logits, int32_t *ids, float *probs,
+                     float *out, int H, int I, int E, int K, int T, void *workspace, size_t workspace_bytes,
+                     mrml_stream_t stream);
+
+/* GGUF block quantisers on the device, byte-identical to the reference's
+ * host quantisers: Q8_0 quant.rs:193-228, Q4_0 quant.rs:372-389.
+ * n is a multiple of 32; dst holds n/32*34 (Q8_0) or n/32*18 (Q4_0) bytes. */
+int mrml_moe_quantize_q8_0(const float *src, uint8_t *dst, size_t n, mrml_stream_t stream);
+int mrml_moe_quantize_q4_0(const float *src, uint8_t *dst, size_t n, mrml_stream_t stream);
+
+/* Profiling hook for benchmarks.  With n_events > 0, the following calls on
+ * this host thread record events[2i] (a cudaEvent_t) on their stream just
+ * before their i-th kernel launch and events[2i+1] just after it, counting
+ * launches across calls, until the list is used up or the hook is reset
+ * with mrml_moe_profile_events(NULL, 0).  Per call: mrml_moe_router 2
+ * launches, mrml_moe_route_from_logits 1, mrml_moe_experts 5,
+ * mrml_moe_forward 7 (router_logits, router_topk, quantize, dispatch,
+ * gate_up, down, combine). */
+int mrml_moe_profile_events(void **events, int n_events);
+
+/* Synchronises `stream`, reads and clears the device status word of a
+ * workspace: MRML_OK, MRML_ERR_DEVICE_TIMEOUT or MRML_ERR_BAD_EXPERT_ID.
+ * *recomputed_tokens (may be NULL) receives how many router tokens needed
+ * the exact sequential logit fallback since the last call.  Not capturable. */
+int mrml_moe_device_status(void *workspace, mrml_stream_t stream, int *recomputed_tokens);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MRML_MOE_H */

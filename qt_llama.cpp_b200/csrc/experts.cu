@@ -1,0 +1,541 @@
+// experts.cu — token dispatch, grouped expert products and combine for the
+// MRML MoE layer on sm_100a.
+//
+// Reference arithmetic (crates/mrml-tensor): the layer input of each token is
+// quantised to Q8_0 (quant.rs:193-228, called at model.rs:2114-2115); every
+// expert row is a block dot sum += (float)isum_b * (d_w * d_a) over the quant
+// blocks in order (quant.rs:335-369, 564-577); act = geglu(gate, up)
+// (ops.rs:99-114) is re-quantised to Q8_0 before the down rows (ops.rs:
+// 175-177); the combine adds alpha*down*scale[e] slot by slot (model.rs:
+// 2117-2165), skipping slots with alpha <= 1e-4.
+//
+// The f32 accumulation is kept in the reference's block order, without
+// contraction, because act is re-quantised: any reordering of that sum flips
+// int8 roundings of act and moves the layer output by up to ~5e-4 relative.
+//
+// B200 design: the reference re-streams an expert's weights once per
+// (token, slot).  Here (token, slot) pairs are first grouped by expert
+// (a stable counting sort), and each CTA streams one tile of one expert's
+// rows from HBM exactly once with the TMA bulk-copy engine, then applies it
+// to every token routed to that expert.  Integer block dots use dp4a; the
+// int32 block sum becomes an f32 through the 1.5*2^23 bit trick.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mrml {
+
+// ---------------------------------------------------------------------------
+// Q8_0 quantisation of the layer input (quant.rs:193-228), one warp per
+// 32-element block, lane = element.  Output in a GPU layout: int8 values
+// [T][H], the decoded f16 scale d [T][H/32] as f32, and the block's sum of
+// q values [T][H/32] (used to fold the Q4_0 "-8" offset into the dot).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void quantize_block_warp(float v, int8_t* q_out, float* d_out, int32_t* sum_out,
+                                                    uint32_t* d16_out) {
+  const int lane = threadIdx.x & 31;
+  float amax = fabsf(v);
+  if (!(amax > 0.f)) amax = 0.f;  // `a > max_val` ignores NaN
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = __fdiv_rn(amax, 127.0f);
+  const uint32_t d16 = f32_to_f16_trunc(scale);
+  const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+  float r = round_half_away(__fmul_rn(v, id));
+  if (r != r) r = 0.f;
+  r = fminf(fmaxf(r, -128.f), 127.f);
+  const int q = (int)r;
+  q_out[lane] = (int8_t)q;
+  int s = q;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) {
+    if (d_out) *d_out = f16_bits_to_f32(d16);
+    if (sum_out) *sum_out = s;
+    if (d16_out) *d16_out = d16;
+  }
+}
+
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int8_t* __restrict__ xq, float* __restrict__ xd,
+                                     int32_t* __restrict__ xsum, long long n_blocks) {
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps) {
+    const float v = x[b * 32 + (threadIdx.x & 31)];
+    quantize_block_warp(v, xq + b * 32, xd + b, xsum + b, nullptr);
+  }
+}
+
+// GGUF-format quantisers (block bytes exactly as the reference writes them).
+__global__ void quantize_q8_0_gguf_kernel(const float* __restrict__ x, uint8_t* __restrict__ dst, long long n_blocks) {
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31;
+  for (long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps) {
+    __shared__ int8_t q[8][32];
+    const int w = threadIdx.x >> 5;
+    uint32_t d16 = 0;
+    quantize_block_warp(x[b * 32 + lane], q[w], nullptr, nullptr, &d16);
+    d16 = __shfl_sync(0xffffffffu, d16, 0);
+    __syncwarp();
+    uint8_t* o = dst + b * 34;
+    if (lane < 2) o[lane] = (uint8_t)(lane == 0 ? d16 & 0xff : d16 >> 8);
+    o[2 + lane] = (uint8_t)q[w][lane];
+    __syncwarp();
+  }
+}
+
+// quant.rs:372-389: d = max|v| / 8 (truncating f16), q = clamp(round(v/d),
+// -8, 7) + 8, low nibble = element j, high nibble = element j + 16.
+__global__ void quantize_q4_0_gguf_kernel(const float* __restrict__ x, uint8_t* __restrict__ dst, long long n_blocks) {
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31;
+  for (long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps) {
+    const float v = x[b * 32 + lane];
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = amax > 0.f ? __fdiv_rn(amax, 8.0f) : 0.f;
+    const uint32_t d16 = f32_to_f16_trunc(scale);
+    const float inv = scale > 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+    float r = round_half_away(__fmul_rn(v, inv));
+    if (r != r) r = 0.f;
+    const int q = (int)fminf(fmaxf(r, -8.f), 7.f) + 8;
+    const int hi = __shfl_down_sync(0xffffffffu, q, 16);
+    uint8_t* o = dst + b * 18;
+    if (lane < 16) o[2 + lane] = (uint8_t)(q | (hi << 4));
+    if (lane < 2) o[lane] = (uint8_t)(lane == 0 ? d16 & 0xff : d16 >> 8);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch: a stable counting sort of the (token, slot) pairs p = t*K + k by
+// expert id, skipping slots with alpha <= 1e-4 (model.rs:2119).  Produces
+// offsets[E+1], sorted[n] (pair ids, grouped by expert, ascending p within an
+// expert) and pos[T*K] (the sorted position of each pair, -1 if skipped).
+// One CTA of 1024 threads; pairs are ranked chunk by chunk with warp match.
+// ---------------------------------------------------------------------------
+constexpr int kDispatchThreads = 1024;
+
+__global__ void __launch_bounds__(kDispatchThreads)
+    dispatch_kernel(const int32_t* __restrict__ ids, const float* __restrict__ probs, int n_pairs, int E,
+                    int32_t* __restrict__ offsets, int32_t* __restrict__ sorted, int32_t* __restrict__ pos,
+                    int* __restrict__ err) {
+  extern __shared__ int32_t dsm[];
+  int32_t* cnt = dsm;                  // [E] totals, then running bases
+  int32_t* wcnt = dsm + E;             // [32][E] per-warp counts of the current chunk
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < E * 33; i += blockDim.x) dsm[i] = 0;
+  __syncthreads();
+  // Pass 1: totals per expert.
+  for (int p = tid; p < n_pairs; p += blockDim.x) {
+    const int e = ids[p];
+    if (probs[p] > 0.0001f) {
+      if (e >= 0 && e < E)
+        atomicAdd(&cnt[e], 1);
+      else
+        set_error(err, kDevBadExpert);
+    }
+  }
+  __syncthreads();
+  // Exclusive scan of the totals (E is small; one thread).
+  if (tid == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = cnt[e];
+      offsets[e] = run;
+      cnt[e] = run;
+      run += c;
+    }
+    offsets[E] = run;
+  }
+  __syncthreads();
+  // Pass 2: stable scatter, 1024 pairs at a time.
+  for (int base = 0; base < n_pairs; base += blockDim.x) {
+    const int p = base + tid;
+    int e = -1;
+    if (p < n_pairs) {
+      const int id = ids[p];
+      if (probs[p] > 0.0001f && id >= 0 && id < E) e = id;
+      if (e < 0) pos[p] = -1;
+    }
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wcnt[warp * E + e] = __popc(peers);
+    __syncthreads();
+    // Per expert: exclusive prefix over warps, in place.
+    for (int x = tid; x < E; x += blockDim.x) {
+      int run = cnt[x];
+      for (int w = 0; w < 32; ++w) {
+        const int c = wcnt[w * E + x];
+        wcnt[w * E + x] = run;
+        run += c;
+      }
+      cnt[x] = run;
+    }
+    __syncthreads();
+    if (e >= 0) {
+      const int dst = wcnt[warp * E + e] + rank;
+      sorted[dst] = p;
+      pos[p] = dst;
+    }
+    __syncthreads();
+    for (int i = tid; i < 32 * E; i += blockDim.x) wcnt[i] = 0;
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One row-block product for `ntok` tokens is not done here; each thread runs
+// one (row, token) chain over the row's blocks in order, as the reference
+// does, so its f32 result is bit-identical to vec_dot_*.
+// ---------------------------------------------------------------------------
+template <int WT>
+__device__ __forceinline__ float row_dot_chain(const uint8_t* __restrict__ row, int nb, const int8_t* __restrict__ aq,
+                                               const float* __restrict__ ad, const int32_t* __restrict__ abias) {
+  float sum = 0.f;
+  for (int b = 0; b < nb; ++b) {
+    const int4* av = reinterpret_cast<const int4*>(aq + b * 32);
+    const int4 a0 = av[0], a1 = av[1];
+    int acc = abias[b];
+    uint32_t d16;
+    if constexpr (WT == kQ4_0) {
+      const Q4Block w = load_q4_block(row + b * 18);
+      d16 = w.d16;
+      acc = dp4a_us(w.qs[0] & 0x0f0f0f0fu, (uint32_t)a0.x, acc);
+      acc = dp4a_us(w.qs[1] & 0x0f0f0f0fu, (uint32_t)a0.y, acc);
+      acc = dp4a_us(w.qs[2] & 0x0f0f0f0fu, (uint32_t)a0.z, acc);
+      acc = dp4a_us(w.qs[3] & 0x0f0f0f0fu, (uint32_t)a0.w, acc);
+      acc = dp4a_us((w.qs[0] >> 4) & 0x0f0f0f0fu, (uint32_t)a1.x, acc);
+      acc = dp4a_us((w.qs[1] >> 4) & 0x0f0f0f0fu, (uint32_t)a1.y, acc);
+      acc = dp4a_us((w.qs[2] >> 4) & 0x0f0f0f0fu, (uint32_t)a1.z, acc);
+      acc = dp4a_us((w.qs[3] >> 4) & 0x0f0f0f0fu, (uint32_t)a1.w, acc);
+    } else {
+      const Q8Block w = load_q8_block(row + b * 34);
+      d16 = w.d16;
+      acc = dp4a_ss(w.qs[0], (uint32_t)a0.x, acc);
+      acc = dp4a_ss(w.qs[1], (uint32_t)a0.y, acc);
+      acc = dp4a_ss(w.qs[2], (uint32_t)a0.z, acc);
+      acc = dp4a_ss(w.qs[3], (uint32_t)a0.w, acc);
+      acc = dp4a_ss(w.qs[4], (uint32_t)a1.x, acc);
+      acc = dp4a_ss(w.qs[5], (uint32_t)a1.y, acc);
+      acc = dp4a_ss(w.qs[6], (uint32_t)a1.z, acc);
+      acc = dp4a_ss(w.qs[7], (uint32_t)a1.w, acc);
+    }
+    const float isum = __fsub_rn(__int_as_float(acc), kMagicF);  // exact
+    const float s = __fmul_rn(f16_bits_to_f32(d16), ad[b]);
+    sum = __fadd_rn(sum, __fmul_rn(isum, s));
+  }
+  return sum;
+}
+
+// Bias folded into each dp4a chain: the float-conversion magic, and for Q4_0
+// the "-8" nibble offset times the activation block's q sum.
+template <int WT>
+__device__ __forceinline__ int32_t act_bias(int32_t qsum) {
+  return WT == kQ4_0 ? kMagicI - 8 * qsum : kMagicI;
+}
+
+// ---------------------------------------------------------------------------
+// Gate/up + GeGLU.  grid (I/32, E); CTA (tile, e) streams gate rows
+// [32*tile, 32*tile+32) and the matching up rows of expert e once (two bulk
+// copies), then runs them against every token routed to e, `tok_chunk` tokens
+// at a time.  act[(sorted position) * I + row] = gelu(gate) * up.
+// ---------------------------------------------------------------------------
+constexpr int kGateUpThreads = 256;
+constexpr int kTileRows = 32;
+
+struct GateUpSmem {
+  size_t w_off, xq_off, xd_off, xb_off, res_off, total;
+};
+
+__host__ __device__ inline GateUpSmem gate_up_smem_layout(int wtype, int H, int tok_chunk) {
+  GateUpSmem L;
+  const size_t rowb = (size_t)(H / 32) * block_bytes(wtype);
+  size_t off = 16;  // mbarrier
+  L.w_off = off;
+  off += 2 * kTileRows * rowb + 16;
+  off = (off + 15) & ~(size_t)15;
+  L.xq_off = off;
+  off += (size_t)tok_chunk * H;
+  L.xd_off = off;
+  off += (size_t)tok_chunk * (H / 32) * 4;
+  L.xb_off = off;
+  off += (size_t)tok_chunk * (H / 32) * 4;
+  L.res_off = off;
+  off += (size_t)tok_chunk * 2 * kTileRows * 4;
+  L.total = off;
+  return L;
+}
+
+template <int WT>
+__global__ void __launch_bounds__(kGateUpThreads)
+    gate_up_kernel(const uint8_t* __restrict__ gate_up, const int32_t* __restrict__ offsets,
+                   const int32_t* __restrict__ sorted, const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                   const int32_t* __restrict__ xsum, float* __restrict__ act, int H, int I, int K, int tok_chunk,
+                   int* __restrict__ err) {
+  const int e = blockIdx.y, tile = blockIdx.x;
+  const int beg = offsets[e], n_e = offsets[e + 1] - beg;
+  if (n_e <= 0) return;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const GateUpSmem L = gate_up_smem_layout(WT, H, tok_chunk);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* wsm = smem + L.w_off;
+  int8_t* xq_s = reinterpret_cast<int8_t*>(smem + L.xq_off);
+  float* xd_s = reinterpret_cast<float*>(smem + L.xd_off);
+  int32_t* xb_s = reinterpret_cast<int32_t*>(smem + L.xb_off);
+  float* res = reinterpret_cast<float*>(smem + L.res_off);
+
+  const int nb = H / 32;
+  const size_t rowb = (size_t)nb * block_bytes(WT);
+  const uint32_t half_bytes = (uint32_t)(kTileRows * rowb);
+  const uint8_t* gsrc = gate_up + ((size_t)e * 2 * I + (size_t)tile * kTileRows) * rowb;
+  const uint8_t* usrc = gate_up + ((size_t)e * 2 * I + I + (size_t)tile * kTileRows) * rowb;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar, 2 * half_bytes);
+    bulk_g2s(wsm, gsrc, half_bytes, bar);
+    bulk_g2s(wsm + half_bytes, usrc, half_bytes, bar);
+  }
+
+  bool weights_ready = false;
+  for (int c0 = 0; c0 < n_e; c0 += tok_chunk) {
+    const int nc = min(tok_chunk, n_e - c0);
+    // Stage the chunk's quantised activations (16-byte vectors).
+    const int vec_per_tok = H / 16;
+    for (int i = tid; i < nc * vec_per_tok; i += blockDim.x) {
+      const int j = i / vec_per_tok, v = i % vec_per_tok;
+      const int t = sorted[beg + c0 + j] / K;
+      reinterpret_cast<int4*>(xq_s + (size_t)j * H)[v] = reinterpret_cast<const int4*>(xq + (size_t)t * H)[v];
+    }
+    for (int i = tid; i < nc * nb; i += blockDim.x) {
+      const int j = i / nb, b = i % nb;
+      const int t = sorted[beg + c0 + j] / K;
+      xd_s[j * nb + b] = xd[(size_t)t * nb + b];
+      xb_s[j * nb + b] = act_bias<WT>(xsum[(size_t)t * nb + b]);
+    }
+    __syncthreads();
+    if (!weights_ready) {
+      if (!mbar_wait_bounded(bar, 0, err)) {
+        // The copy never completed: leave without touching the weights.
+        return;
+      }
+      weights_ready = true;
+    }
+    // (row, token) chains: rho < 32 gate rows, rho >= 32 up rows.
+    const int rho = tid & (2 * kTileRows - 1);
+    for (int j = tid / (2 * kTileRows); j < nc; j += kGateUpThreads / (2 * kTileRows)) {
+      res[j * 2 * kTileRows + rho] =
+          row_dot_chain<WT>(wsm + (size_t)rho * rowb, nb, xq_s + (size_t)j * H, xd_s + j * nb, xb_s + j * nb);
+    }
+    __syncthreads();
+    for (int i = tid; i < nc * kTileRows; i += blockDim.x) {
+      const int j = i / kTileRows, r = i % kTileRows;
+      const float g = res[j * 2 * kTileRows + r];
+      const float u = res[j * 2 * kTileRows + kTileRows + r];
+      act[(size_t)(beg + c0 + j) * I + tile * kTileRows + r] = __fmul_rn(gelu_approx(g), u);
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Down.  grid (H/32, E); CTA (tile, e) streams 32 down rows of expert e once,
+// re-quantises the act rows of the expert's tokens to Q8_0 in shared memory
+// (ops.rs:175-177) and writes ydown[(sorted position) * H + row].
+// ---------------------------------------------------------------------------
+constexpr int kDownThreads = 256;
+
+struct DownSmem {
+  size_t w_off, xq_off, xd_off, xb_off, total;
+};
+
+__host__ __device__ inline DownSmem down_smem_layout(int wtype, int I, int tok_chunk) {
+  DownSmem L;
+  const size_t rowb = (size_t)(I / 32) * block_bytes(wtype);
+  size_t off = 16;
+  L.w_off = off;
+  off += kTileRows * rowb + 16;
+  off = (off + 15) & ~(size_t)15;
+  L.xq_off = off;
+  off += (size_t)tok_chunk * I;
+  L.xd_off = off;
+  off += (size_t)tok_chunk * (I / 32) * 4;
+  L.xb_off = off;
+  off += (size_t)tok_chunk * (I / 32) * 4;
+  L.total = off;
+  return L;
+}
+
+template <int WT>
+__global__ void __launch_bounds__(kDownThreads)
+    down_kernel(const uint8_t* __restrict__ down, const int32_t* __restrict__ offsets, const float* __restrict__ act,
+                float* __restrict__ ydown, int H, int I, int tok_chunk, int* __restrict__ err) {
+  const int e = blockIdx.y, tile = blockIdx.x;
+  const int beg = offsets[e], n_e = offsets[e + 1] - beg;
+  if (n_e <= 0) return;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const DownSmem L = down_smem_layout(WT, I, tok_chunk);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* wsm = smem + L.w_off;
+  int8_t* xq_s = reinterpret_cast<int8_t*>(smem + L.xq_off);
+  float* xd_s = reinterpret_cast<float*>(smem + L.xd_off);
+  int32_t* xb_s = reinterpret_cast<int32_t*>(smem + L.xb_off);
+
+  const int nb = I / 32;
+  const size_t rowb = (size_t)nb * block_bytes(WT);
+  const uint32_t bytes = (uint32_t)(kTileRows * rowb);
+  const uint8_t* src = down + ((size_t)e * H + (size_t)tile * kTileRows) * rowb;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_g2s(wsm, src, bytes, bar);
+  }
+  bool weights_ready = false;
+  for (int c0 = 0; c0 < n_e; c0 += tok_chunk) {
+    const int nc = min(tok_chunk, n_e - c0);
+    // Re-quantise act rows to Q8_0, one warp per 32-element block.
+    for (int blk = warp; blk < nc * nb; blk += kDownThreads / 32) {
+      const int j = blk / nb, b = blk % nb;
+      const float v = act[(size_t)(beg + c0 + j) * I + b * 32 + lane];
+      int32_t qsum_dummy;
+      quantize_block_warp(v, xq_s + (size_t)j * I + b * 32, xd_s + j * nb + b, &qsum_dummy, nullptr);
+      if (lane == 0) xb_s[j * nb + b] = act_bias<WT>(qsum_dummy);
+    }
+    __syncthreads();
+    if (!weights_ready) {
+      if (!mbar_wait_bounded(bar, 0, err)) return;
+      weights_ready = true;
+    }
+    const int rho = tid & (kTileRows - 1);
+    for (int j = tid / kTileRows; j < nc; j += kDownThreads / kTileRows) {
+      ydown[(size_t)(beg + c0 + j) * H + tile * kTileRows + rho] =
+          row_dot_chain<WT>(wsm + (size_t)rho * rowb, nb, xq_s + (size_t)j * I, xd_s + j * nb, xb_s + j * nb);
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Combine (model.rs:2163-2165): out[t,i] = sum over k ascending of
+// (alpha_k * down_k[i]) * scale[e_k], starting from 0, skipped slots left out.
+// ---------------------------------------------------------------------------
+__global__ void combine_kernel(const float* __restrict__ ydown, const int32_t* __restrict__ pos,
+                               const int32_t* __restrict__ ids, const float* __restrict__ probs,
+                               const float* __restrict__ down_scale, float* __restrict__ out, int H, int K, int T) {
+  const int t = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T || i >= H) return;
+  float o = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const int p = pos[t * K + k];
+    if (p < 0) continue;
+    const float alpha = probs[t * K + k];
+    const float scale = down_scale ? down_scale[ids[t * K + k]] : 1.0f;
+    o = __fadd_rn(o, __fmul_rn(__fmul_rn(alpha, ydown[(size_t)p * H + i]), scale));
+  }
+  out[(size_t)t * H + i] = o;
+}
+
+}  // namespace mrml
+
+// ------------------------------------------------------------ launchers ---
+namespace mrml {
+
+static int grid_for_blocks(long long warps_needed) {
+  long long g = (warps_needed + 7) / 8;
+  if (g > 148 * 16) g = 148 * 16;
+  return (int)(g < 1 ? 1 : g);
+}
+
+cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
+                                 cudaStream_t s) {
+  quantize_rows_kernel<<<grid_for_blocks(n_blocks), 256, 0, s>>>(x, xq, xd, xsum, n_blocks);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s) {
+  if (wtype == kQ8_0)
+    quantize_q8_0_gguf_kernel<<<grid_for_blocks(n_blocks), 256, 0, s>>>(x, dst, n_blocks);
+  else
+    quantize_q4_0_gguf_kernel<<<grid_for_blocks(n_blocks), 256, 0, s>>>(x, dst, n_blocks);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* offsets,
+                            int32_t* sorted, int32_t* pos, int* err, cudaStream_t s) {
+  const size_t smem = (size_t)33 * E * sizeof(int32_t);
+  if (smem > 48 * 1024) {
+    cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (st != cudaSuccess) return st;
+  }
+  dispatch_kernel<<<1, kDispatchThreads, smem, s>>>(ids, probs, n_pairs, E, offsets, sorted, pos, err);
+  return cudaPeekAtLastError();
+}
+
+constexpr size_t kMaxSmem = 227 * 1024;
+
+int gate_up_tok_chunk(int wtype, int H) {
+  for (int c = 16; c >= 1; c >>= 1)
+    if (gate_up_smem_layout(wtype, H, c).total <= kMaxSmem) return c;
+  return 0;
+}
+
+int down_tok_chunk(int wtype, int I) {
+  for (int c = 16; c >= 1; c >>= 1)
+    if (down_smem_layout(wtype, I, c).total <= kMaxSmem) return c;
+  return 0;
+}
+
+cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* offsets, const int32_t* sorted,
+                           const int8_t* xq, const float* xd, const int32_t* xsum, float* act, int H, int I, int E,
+                           int K, int* err, cudaStream_t s) {
+  const int chunk = gate_up_tok_chunk(wtype, H);
+  const size_t smem = gate_up_smem_layout(wtype, H, chunk).total;
+  const dim3 grid(I / kTileRows, E);
+  if (wtype == kQ4_0) {
+    cudaError_t st = cudaFuncSetAttribute(gate_up_kernel<kQ4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (st != cudaSuccess) return st;
+    gate_up_kernel<kQ4_0><<<grid, kGateUpThreads, smem, s>>>(gate_up, offsets, sorted, xq, xd, xsum, act, H, I, K,
+                                                             chunk, err);
+  } else {
+    cudaError_t st = cudaFuncSetAttribute(gate_up_kernel<kQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (st != cudaSuccess) return st;
+    gate_up_kernel<kQ8_0><<<grid, kGateUpThreads, smem, s>>>(gate_up, offsets, sorted, xq, xd, xsum, act, H, I, K,
+                                                             chunk, err);
+  }
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_down(int wtype, const uint8_t* down, const int32_t* offsets, const float* act, float* ydown, int H,
+                        int I, int E, int* err, cudaStream_t s) {
+  const int chunk = down_tok_chunk(wtype, I);
+  const size_t smem = down_smem_layout(wtype, I, chunk).total;
+  const dim3 grid(H / kTileRows, E);
+  if (wtype == kQ4_0) {
+    cudaError_t st = cudaFuncSetAttribute(down_kernel<kQ4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (st != cudaSuccess) return st;
+    down_kernel<kQ4_0><<<grid, kDownThreads, smem, s>>>(down, offsets, act, ydown, H, I, chunk, err);
+  } else {
+    cudaError_t st = cudaFuncSetAttribute(down_kernel<kQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (st != cudaSuccess) return st;
+    down_kernel<kQ8_0><<<grid, kDownThreads, smem, s>>>(down, offsets, act, ydown, H, I, chunk, err);
+  }
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,
+                           const float* down_scale, float* out, int H, int K, int T, cudaStream_t s) {
+  const dim3 grid((H + 255) / 256, T);
+  combine_kernel<<<grid, 256, 0, s>>>(ydown, pos, ids, probs, down_scale, out, H, K, T);
+  return cudaPeekAtLastError();
+}
+
+}  // namespace mrml

@@ -1,0 +1,278 @@
+// mrml_moe.cu — the C ABI of libmrml_moe_b200.so (declared in
+// include/mrml_moe.h): argument checks, the workspace layout and the order
+// of kernel launches on the caller's stream.
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/mrml_moe.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+using mrml::kQ4_0;
+using mrml::kQ8_0;
+
+constexpr int kMaxE = 256;
+constexpr int kMaxK = 64;
+
+// Optional per-launch profiling events (thread-local; see
+// mrml_moe_profile_events).  Slot 2i is recorded before launch i of a call,
+// slot 2i+1 after it.
+thread_local cudaEvent_t* t_events = nullptr;
+thread_local int t_n_events = 0;
+thread_local int t_next_event = 0;
+
+struct LaunchMark {
+  cudaStream_t s;
+  explicit LaunchMark(cudaStream_t st) : s(st) {
+    if (t_events && t_next_event + 1 < t_n_events) cudaEventRecord(t_events[t_next_event], s);
+  }
+  ~LaunchMark() {
+    if (t_events && t_next_event + 1 < t_n_events) {
+      cudaEventRecord(t_events[t_next_event + 1], s);
+      t_next_event += 2;
+    }
+  }
+};
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Workspace regions (each 256-byte aligned), in order.
+struct Workspace {
+  int* status;     // [0] device status word, [1] router recompute counter
+  int8_t* xq;      // [T][H]        Q8_0 values of the layer input
+  float* xd;       // [T][H/32]     decoded Q8_0 scales
+  int32_t* xsum;   // [T][H/32]     sums of the Q8_0 values per block
+  float* bounds;   // [T][E]        router error bounds
+  int32_t* offsets;  // [E+1]       per-expert start in the sorted pair list
+  int32_t* sorted;   // [T*K]       pair ids grouped by expert
+  int32_t* pos;      // [T*K]       sorted position of each pair (-1 skipped)
+  float* act;        // [T*K][I]    geglu output per sorted pair
+  float* ydown;      // [T*K][H]    down output per sorted pair (unscaled)
+  size_t bytes;
+};
+
+Workspace carve(void* base, int H, int I, int E, int K, int T) {
+  Workspace w;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(n);
+    return r;
+  };
+  const size_t nb = (size_t)H / 32, tk = (size_t)T * K;
+  w.status = reinterpret_cast<int*>(take(256));
+  w.xq = reinterpret_cast<int8_t*>(take((size_t)T * H));
+  w.xd = reinterpret_cast<float*>(take((size_t)T * nb * 4));
+  w.xsum = reinterpret_cast<int32_t*>(take((size_t)T * nb * 4));
+  w.bounds = reinterpret_cast<float*>(take((size_t)T * E * 4));
+  w.offsets = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
+  w.sorted = reinterpret_cast<int32_t*>(take(tk * 4));
+  w.pos = reinterpret_cast<int32_t*>(take(tk * 4));
+  w.act = reinterpret_cast<float*>(take(tk * I * 4));
+  w.ydown = reinterpret_cast<float*>(take(tk * H * 4));
+  w.bytes = off;
+  return w;
+}
+
+// Once per device: is it an sm_100 part?
+int check_device() {
+  static int verdict[64] = {0};  // 0 unknown, 1 ok, -1 wrong arch
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MRML_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return MRML_ERR_DEVICE;
+  if (verdict[dev] == 0) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return MRML_ERR_CUDA;
+    verdict[dev] = major == 10 ? 1 : -1;
+  }
+  return verdict[dev] == 1 ? MRML_OK : MRML_ERR_DEVICE;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? MRML_OK : MRML_ERR_CUDA; }
+
+#define MRML_TRY(expr)                 \
+  do {                                 \
+    const int _st = (expr);            \
+    if (_st != MRML_OK) return _st;    \
+  } while (0)
+
+int check_router_args(const float* W, const float* x, const float* logits, const int32_t* ids, const float* probs,
+                      int H, int E, int K, int T) {
+  if (H <= 0 || E <= 0 || K <= 0 || T < 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (K > E) return MRML_ERR_INVALID_ARGUMENT;
+  if (E > kMaxE || K > kMaxK) return MRML_ERR_UNSUPPORTED;
+  if (T > 0 && (!W || !x || !logits || !ids || !probs)) return MRML_ERR_INVALID_ARGUMENT;
+  return MRML_OK;
+}
+
+int check_expert_args(int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids, const float* probs,
+                      const float* x, const float* out, int H, int I, int E, int K, int T) {
+  if (wtype != MRML_Q4_0 && wtype != MRML_Q8_0) return MRML_ERR_UNSUPPORTED;
+  if (H <= 0 || I <= 0 || E <= 0 || K <= 0 || T < 0 || K > E) return MRML_ERR_INVALID_ARGUMENT;
+  if (H % 32 != 0 || I % 32 != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (E > kMaxE || K > kMaxK) return MRML_ERR_UNSUPPORTED;
+  if ((long long)T * K > (1ll << 30)) return MRML_ERR_UNSUPPORTED;
+  if (T > 0 && (!gate_up || !down || !ids || !probs || !x || !out)) return MRML_ERR_INVALID_ARGUMENT;
+  if (T > 0 && (!aligned16(gate_up) || !aligned16(down) || !aligned16(x))) return MRML_ERR_INVALID_ARGUMENT;
+  if (mrml::gate_up_tok_chunk(wtype, H) == 0 || mrml::down_tok_chunk(wtype, I) == 0) return MRML_ERR_UNSUPPORTED;
+  return MRML_OK;
+}
+
+int check_workspace(void* ws, size_t ws_bytes, int H, int I, int E, int K, int T) {
+  if (!ws) return MRML_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)ws & 255u) != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (ws_bytes < carve(nullptr, H, I, E, K, T).bytes) return MRML_ERR_WORKSPACE_TOO_SMALL;
+  return MRML_OK;
+}
+
+#define MRML_LAUNCH(expr)              \
+  do {                                 \
+    LaunchMark _mark(s);               \
+    MRML_TRY(cuda_status(expr));       \
+  } while (0)
+
+int run_router(const Workspace& w, const float* W, const float* x, float* logits, int32_t* ids, float* probs, int H,
+               int E, int K, int T, cudaStream_t s) {
+  MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, w.bounds, H, E, T, s));
+  MRML_LAUNCH(mrml::launch_router_topk(W, x, logits, w.bounds, ids, probs, H, E, K, T, w.status + 1, s));
+  return MRML_OK;
+}
+
+int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids,
+                const float* probs, const float* down_scale, const float* x, float* out, int H, int I, int E, int K,
+                int T, cudaStream_t s) {
+  MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
+  MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, w.offsets, w.sorted, w.pos, w.status, s));
+  MRML_LAUNCH(
+      mrml::launch_gate_up(wtype, gate_up, w.offsets, w.sorted, w.xq, w.xd, w.xsum, w.act, H, I, E, K, w.status, s));
+  MRML_LAUNCH(mrml::launch_down(wtype, down, w.offsets, w.act, w.ydown, H, I, E, w.status, s));
+  MRML_LAUNCH(mrml::launch_combine(w.ydown, w.pos, ids, probs, down_scale, out, H, K, T, s));
+  return MRML_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mrml_moe_version(void) { return 100; }
+
+const char* mrml_moe_status_string(int status) {
+  switch (status) {
+    case MRML_OK: return "ok";
+    case MRML_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case MRML_ERR_UNSUPPORTED: return "unsupported shape or weight type";
+    case MRML_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case MRML_ERR_CUDA: return "CUDA runtime error";
+    case MRML_ERR_DEVICE: return "device is not an sm_100 GPU";
+    case MRML_ERR_DEVICE_TIMEOUT: return "a device-side wait timed out";
+    case MRML_ERR_BAD_EXPERT_ID: return "expert id out of range";
+    default: return "unknown status";
+  }
+}
+
+size_t mrml_moe_workspace_bytes(int H, int I, int E, int K, int T) {
+  if (H <= 0 || I <= 0 || E <= 0 || K <= 0 || T < 0) return 0;
+  return carve(nullptr, H, I, E, K, T).bytes;
+}
+
+int mrml_moe_router(const float* W, const float* x, float* logits, int32_t* ids, float* probs, int H, int E, int K,
+                    int T, void* workspace, size_t workspace_bytes, mrml_stream_t stream) {
+  MRML_TRY(check_router_args(W, x, logits, ids, probs, H, E, K, T));
+  if (T == 0) return MRML_OK;
+  MRML_TRY(check_device());
+  // The router needs only the status words and the bounds region; size the
+  // check with the smallest expert shape.
+  MRML_TRY(check_workspace(workspace, workspace_bytes, 32, 32, E, K, T));
+  const Workspace w = carve(workspace, 32, 32, E, K, T);
+  return run_router(w, W, x, logits, ids, probs, H, E, K, T, (cudaStream_t)stream);
+}
+
+int mrml_moe_route_from_logits(const float* logits, int32_t* ids, float* probs, int E, int K, int T,
+                               mrml_stream_t stream) {
+  if (E <= 0 || K <= 0 || T < 0 || K > E) return MRML_ERR_INVALID_ARGUMENT;
+  if (E > kMaxE || K > kMaxK) return MRML_ERR_UNSUPPORTED;
+  if (T == 0) return MRML_OK;
+  if (!logits || !ids || !probs) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_router_topk(nullptr, nullptr, const_cast<float*>(logits), nullptr, ids, probs, 0, E, K, T,
+                                       nullptr, s));
+  return MRML_OK;
+}
+
+int mrml_moe_experts(int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids, const float* probs,
+                     const float* down_scale, const float* x, float* out, int H, int I, int E, int K, int T,
+                     void* workspace, size_t workspace_bytes, mrml_stream_t stream) {
+  MRML_TRY(check_expert_args(wtype, gate_up, down, ids, probs, x, out, H, I, E, K, T));
+  if (T == 0) return MRML_OK;
+  MRML_TRY(check_device());
+  MRML_TRY(check_workspace(workspace, workspace_bytes, H, I, E, K, T));
+  const Workspace w = carve(workspace, H, I, E, K, T);
+  return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, (cudaStream_t)stream);
+}
+
+int mrml_moe_forward(int wtype, const float* router_w, const float* router_x, const float* x, const uint8_t* gate_up,
+                     const uint8_t* down, const float* down_scale, float* logits, int32_t* ids, float* probs,
+                     float* out, int H, int I, int E, int K, int T, void* workspace, size_t workspace_bytes,
+                     mrml_stream_t stream) {
+  MRML_TRY(check_router_args(router_w, router_x, logits, ids, probs, H, E, K, T));
+  MRML_TRY(check_expert_args(wtype, gate_up, down, ids, probs, x, out, H, I, E, K, T));
+  if (T == 0) return MRML_OK;
+  MRML_TRY(check_device());
+  MRML_TRY(check_workspace(workspace, workspace_bytes, H, I, E, K, T));
+  const Workspace w = carve(workspace, H, I, E, K, T);
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_TRY(run_router(w, router_w, router_x, logits, ids, probs, H, E, K, T, s));
+  return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s);
+}
+
+int mrml_moe_quantize_q8_0(const float* src, uint8_t* dst, size_t n, mrml_stream_t stream) {
+  if (n % 32 != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (n == 0) return MRML_OK;
+  if (!src || !dst) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  return cuda_status(mrml::launch_quantize_gguf(kQ8_0, src, dst, (long long)(n / 32), (cudaStream_t)stream));
+}
+
+int mrml_moe_quantize_q4_0(const float* src, uint8_t* dst, size_t n, mrml_stream_t stream) {
+  if (n % 32 != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (n == 0) return MRML_OK;
+  if (!src || !dst) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  return cuda_status(mrml::launch_quantize_gguf(kQ4_0, src, dst, (long long)(n / 32), (cudaStream_t)stream));
+}
+
+int mrml_moe_profile_events(void** events, int n_events) {
+  if (n_events < 0 || (n_events > 0 && !events)) return MRML_ERR_INVALID_ARGUMENT;
+  t_events = n_events > 0 ? reinterpret_cast<cudaEvent_t*>(events) : nullptr;
+  t_n_events = n_events;
+  t_next_event = 0;
+  return MRML_OK;
+}
+
+int mrml_moe_workspace_init(void* workspace, size_t workspace_bytes, mrml_stream_t stream) {
+  if (!workspace || workspace_bytes < 256 || ((uintptr_t)workspace & 255u) != 0) return MRML_ERR_INVALID_ARGUMENT;
+  return cuda_status(cudaMemsetAsync(workspace, 0, 256, (cudaStream_t)stream));
+}
+
+int mrml_moe_device_status(void* workspace, mrml_stream_t stream, int* recomputed_tokens) {
+  if (!workspace) return MRML_ERR_INVALID_ARGUMENT;
+  int host[2] = {0, 0};
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return MRML_ERR_CUDA;
+  if (cudaMemcpy(host, workspace, sizeof(host), cudaMemcpyDeviceToHost) != cudaSuccess) return MRML_ERR_CUDA;
+  if (cudaMemset(workspace, 0, sizeof(host)) != cudaSuccess) return MRML_ERR_CUDA;
+  if (recomputed_tokens) *recomputed_tokens = host[1];
+  switch (host[0]) {
+    case mrml::kDevOk: return MRML_OK;
+    case mrml::kDevTimeout: return MRML_ERR_DEVICE_TIMEOUT;
+    case mrml::kDevBadExpert: return MRML_ERR_BAD_EXPERT_ID;
+    default: return MRML_ERR_CUDA;
+  }
+}
+
+}  // extern "C"

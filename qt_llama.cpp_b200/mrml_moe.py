@@ -1,0 +1,230 @@
+"""Host-side mirror of the reference's MoE operator surface over the C ABI.
+
+The reference host is Rust (crates/mrml-tensor/src/cuda.rs); its MoE calls
+are methods of `CudaDevice`:
+
+    moe_router(weights, input, logits, ids, probs, dim, n_experts)        cuda.rs:2808
+    moe_router_batch(weights, input, logits, ids, probs, dim, n_experts, batch)   :2882
+    moe_topk_q4_0(gate_up, down, ids, weights, scales, x_in, act, out,
+                  dim, exp_ffn_dim, n_active)                             cuda.rs:2772
+    moe_topk_batch_q4_0(..., batch)                                       cuda.rs:2840
+
+`MoeDevice` below keeps those names, argument meanings and size assertions
+(the reference asserts buffer lengths and panics on a failed launch; here a
+failed assertion raises AssertionError and a failed launch raises MoeError).
+Tensors are torch CUDA tensors, used only as device memory; every call goes
+through libmrml_moe_b200.so with the tensors' raw pointers.  There is no CPU
+fallback: without the library or an sm_100 GPU every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmrml_moe_b200.so")
+
+MRML_OK = 0
+MRML_Q4_0 = 2
+MRML_Q8_0 = 8
+
+# Every symbol include/mrml_moe.h declares, with its ctypes signature.
+_c = ctypes
+_vp, _i, _sz, _f = _c.c_void_p, _c.c_int, _c.c_size_t, _c.c_float
+SIGNATURES = {
+    "mrml_moe_version": (_i, []),
+    "mrml_moe_status_string": (_c.c_char_p, [_i]),
+    "mrml_moe_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "mrml_moe_workspace_init": (_i, [_vp, _sz, _vp]),
+    "mrml_moe_router": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "mrml_moe_route_from_logits": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "mrml_moe_experts": (
+        _i,
+        [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp],
+    ),
+    "mrml_moe_forward": (
+        _i,
+        [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp],
+    ),
+    "mrml_moe_quantize_q8_0": (_i, [_vp, _vp, _sz, _vp]),
+    "mrml_moe_quantize_q4_0": (_i, [_vp, _vp, _sz, _vp]),
+    "mrml_moe_device_status": (_i, [_vp, _vp, _c.POINTER(_c.c_int)]),
+    "mrml_moe_profile_events": (_i, [_c.POINTER(_vp), _i]),
+}
+
+
+class MoeError(RuntimeError):
+    """A C-ABI call returned a non-zero mrml_status."""
+
+    def __init__(self, what: str, status: int, text: str):
+        super().__init__(f"{what} failed: {text} ({status})")
+        self.status = status
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libmrml_moe_b200.so (built in-tree by __graft_entry__.build)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise OSError(f"{path} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'`")
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def _check(what: str, status: int) -> None:
+    if status != MRML_OK:
+        text = load_library().mrml_moe_status_string(status).decode()
+        raise MoeError(what, status, text)
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    if stream is None:
+        import torch
+
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream or None
+
+
+def workspace_bytes(H: int, I: int, E: int, K: int, T: int) -> int:
+    return int(load_library().mrml_moe_workspace_bytes(H, I, E, K, T))
+
+
+def new_workspace(H: int, I: int, E: int, K: int, T: int, device=None):
+    """A zero-initialised, 256-byte aligned device workspace (torch uint8)."""
+    import torch
+
+    n = max(256, workspace_bytes(H, I, E, K, T))
+    ws = torch.zeros(n, dtype=torch.uint8, device=device or "cuda")
+    assert ws.data_ptr() % 256 == 0
+    return ws
+
+
+def router(W, x, logits, ids, probs, H, E, K, T, ws, stream=None):
+    lib = load_library()
+    _check(
+        "mrml_moe_router",
+        lib.mrml_moe_router(_ptr(W), _ptr(x), _ptr(logits), _ptr(ids), _ptr(probs), H, E, K, T, _ptr(ws),
+                            ws.numel(), _stream_ptr(stream)),
+    )
+
+
+def route_from_logits(logits, ids, probs, E, K, T, stream=None):
+    lib = load_library()
+    _check(
+        "mrml_moe_route_from_logits",
+        lib.mrml_moe_route_from_logits(_ptr(logits), _ptr(ids), _ptr(probs), E, K, T, _stream_ptr(stream)),
+    )
+
+
+def experts(wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, ws, stream=None):
+    lib = load_library()
+    _check(
+        "mrml_moe_experts",
+        lib.mrml_moe_experts(wtype, _ptr(gate_up), _ptr(down), _ptr(ids), _ptr(probs), _ptr(down_scale), _ptr(x),
+                             _ptr(out), H, I, E, K, T, _ptr(ws), ws.numel(), _stream_ptr(stream)),
+    )
+
+
+def forward(wtype, router_w, router_x, x, gate_up, down, down_scale, logits, ids, probs, out, H, I, E, K, T, ws,
+            stream=None):
+    lib = load_library()
+    _check(
+        "mrml_moe_forward",
+        lib.mrml_moe_forward(wtype, _ptr(router_w), _ptr(router_x), _ptr(x), _ptr(gate_up), _ptr(down),
+                             _ptr(down_scale), _ptr(logits), _ptr(ids), _ptr(probs), _ptr(out), H, I, E, K, T,
+                             _ptr(ws), ws.numel(), _stream_ptr(stream)),
+    )
+
+
+def quantize(wtype, src, dst, stream=None):
+    lib = load_library()
+    fn = lib.mrml_moe_quantize_q4_0 if wtype == MRML_Q4_0 else lib.mrml_moe_quantize_q8_0
+    _check("mrml_moe_quantize", fn(_ptr(src), _ptr(dst), src.numel(), _stream_ptr(stream)))
+
+
+def device_status(ws, stream=None):
+    """(status, recomputed_tokens); synchronises the stream."""
+    lib = load_library()
+    rec = ctypes.c_int(0)
+    st = lib.mrml_moe_device_status(_ptr(ws), _stream_ptr(stream), ctypes.byref(rec))
+    return st, rec.value
+
+
+class MoeDevice:
+    """The reference's `CudaDevice` MoE methods (cuda.rs:2772-2912) on the
+    B200 library.  Holds one workspace, grown on demand; grow it (call
+    `reserve`) before capturing a CUDA graph."""
+
+    def __init__(self, device_id: int = 0):
+        import torch
+
+        self.device = torch.device("cuda", device_id)
+        self._ws = None
+        self._ws_shape = None
+
+    def reserve(self, H: int, I: int, E: int, K: int, T: int):
+        need = workspace_bytes(H, I, E, K, T)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = new_workspace(H, I, E, K, T, self.device)
+        return self._ws
+
+    # cuda.rs:2808-2838 (T = 1, K = 8)
+    def moe_router(self, d_weights, d_input, d_logits, d_ids, d_probabilities, dim, n_experts, k=8):
+        assert d_weights.numel() >= dim * n_experts
+        assert d_input.numel() >= dim
+        assert d_logits.numel() >= n_experts
+        assert d_ids.numel() >= k
+        assert d_probabilities.numel() >= k
+        ws = self.reserve(32, 32, n_experts, k, 1)
+        router(d_weights, d_input, d_logits, d_ids, d_probabilities, dim, n_experts, k, 1, ws)
+
+    # cuda.rs:2882-2912
+    def moe_router_batch(self, weights, input, logits, ids, probabilities, dim, n_experts, batch, k=8):
+        assert input.numel() == dim * batch
+        assert logits.numel() == n_experts * batch
+        assert ids.numel() == k * batch
+        assert probabilities.numel() == k * batch
+        ws = self.reserve(32, 32, n_experts, k, batch)
+        router(weights, input, logits, ids, probabilities, dim, n_experts, k, batch, ws)
+
+    # cuda.rs:2772-2806.  `d_act_scratch` is accepted for signature parity;
+    # the library uses its own workspace for the GeGLU activations.
+    def moe_topk_q4_0(self, d_gate_up_exps, d_down_exps, d_active_exp_ids, d_active_exp_weights,
+                      d_down_exps_scale, d_x_in, d_act_scratch, d_out_moe, dim, exp_ffn_dim, n_active,
+                      n_experts=None, wtype=MRML_Q4_0):
+        E = n_experts or self._infer_experts(d_gate_up_exps, dim, exp_ffn_dim, wtype)
+        ws = self.reserve(dim, exp_ffn_dim, E, n_active, 1)
+        experts(wtype, d_gate_up_exps, d_down_exps, d_active_exp_ids, d_active_exp_weights, d_down_exps_scale,
+                d_x_in, d_out_moe, dim, exp_ffn_dim, E, n_active, 1, ws)
+
+    # cuda.rs:2840-2880
+    def moe_topk_batch_q4_0(self, gate_up, down, ids, weights, scales, input, act, output, dim, exp_dim,
+                            n_active, batch, n_experts=None, wtype=MRML_Q4_0):
+        assert ids.numel() == batch * n_active
+        assert weights.numel() == batch * n_active
+        assert input.numel() == batch * dim
+        assert output.numel() == batch * dim
+        E = n_experts or self._infer_experts(gate_up, dim, exp_dim, wtype)
+        ws = self.reserve(dim, exp_dim, E, n_active, batch)
+        experts(wtype, gate_up, down, ids, weights, scales, input, output, dim, exp_dim, E, n_active, batch, ws)
+
+    @staticmethod
+    def _infer_experts(gate_up, dim, exp_dim, wtype):
+        bb = 18 if wtype == MRML_Q4_0 else 34
+        per_expert = 2 * exp_dim * (dim // 32) * bb
+        assert gate_up.numel() % per_expert == 0, "gate_up size is not a whole number of experts"
+        return gate_up.numel() // per_expert

@@ -1,0 +1,381 @@
+"""Parity of the B200 library with the reference's CPU MoE path.
+
+Every case runs the CUDA path through the C ABI and the CPU oracle on the
+same seeded inputs.  Bars (from the task's north star):
+  * expert ids (and so the permutation) bit-exact, ties to the lower id;
+  * layer output: max-abs <= 1e-3 * max|ref| and rel-L2 <= 1e-4;
+  * GGUF quantisers byte-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS_FRAC = 1e-3
+REL_L2 = 1e-4
+
+
+def dev_tensor(a, device):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def assert_close(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = max(np.abs(ref).max(), 1e-30)
+    rel = np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
+    mx = np.abs(got - ref).max() / scale
+    assert mx <= MAX_ABS_FRAC, f"max-abs {mx:.3e} of max|ref|"
+    assert rel <= REL_L2, f"rel-L2 {rel:.3e}"
+    return rel, mx
+
+
+class Layer:
+    """Device copies of one MoE layer's inputs plus output buffers."""
+
+    def __init__(self, moe, device, wtype, gu, dn, W, H, I, E, K, T, down_scale=None):
+        import torch
+
+        self.moe, self.device = moe, device
+        self.wtype, self.H, self.I, self.E, self.K, self.T = wtype, H, I, E, K, T
+        self.gu, self.dn = dev_tensor(gu, device), dev_tensor(dn, device)
+        self.W = None if W is None else dev_tensor(W, device)
+        self.scale = None if down_scale is None else dev_tensor(down_scale, device)
+        self.logits = torch.empty(T, E, device=device)
+        self.ids = torch.empty(T, K, dtype=torch.int32, device=device)
+        self.probs = torch.empty(T, K, device=device)
+        self.out = torch.empty(T, H, device=device)
+        self.ws = moe.new_workspace(H, I, E, K, T, device)
+
+    def forward(self, x):
+        d_x = dev_tensor(x, self.device)
+        self.moe.forward(self.wtype, self.W, d_x, d_x, self.gu, self.dn, self.scale, self.logits, self.ids,
+                         self.probs, self.out, self.H, self.I, self.E, self.K, self.T, self.ws)
+        st, rec = self.moe.device_status(self.ws)
+        assert st == 0, f"device status {st}"
+        return self.ids.cpu().numpy(), self.probs.cpu().numpy(), self.out.cpu().numpy(), rec
+
+    def experts(self, x, ids, probs):
+        d_x = dev_tensor(x, self.device)
+        d_ids, d_probs = dev_tensor(ids, self.device), dev_tensor(probs, self.device)
+        self.moe.experts(self.wtype, self.gu, self.dn, d_ids, d_probs, self.scale, d_x, self.out, self.H, self.I,
+                         self.E, self.K, self.T, self.ws)
+        st, _ = self.moe.device_status(self.ws)
+        assert st == 0, f"device status {st}"
+        return self.out.cpu().numpy()
+
+
+# --------------------------------------------------------------- quantisers
+
+
+@pytest.mark.parametrize("wtype", [2, 8])
+def test_gguf_quantisers_byte_exact(cuda, moe, oracle, synth, wtype):
+    import torch
+
+    rng = np.random.default_rng(1)
+    parts = [
+        rng.standard_normal(32 * 4099).astype(np.float32),
+        (rng.standard_normal(32 * 64) * 1e-6).astype(np.float32),
+        np.zeros(64, np.float32),
+        np.tile(np.array([0.5, -0.5, 1.5, -2.5, 127.0, -127.0, 63.5, 0.25], np.float32), 8),
+        (rng.standard_normal(32 * 16) * 1e5).astype(np.float32),
+    ]
+    x = np.concatenate(parts)
+    bb = 18 if wtype == 2 else 34
+    dst = torch.zeros(x.size // 32 * bb, dtype=torch.uint8, device=cuda)
+    moe.quantize(wtype, dev_tensor(x, cuda), dst)
+    torch.cuda.synchronize()
+    assert np.array_equal(dst.cpu().numpy(), oracle.quantize(x, wtype))
+
+
+# ------------------------------------------------------------------ router
+
+
+def test_router_reference_fixture(cuda, moe, oracle):
+    """cuda.rs:3260-3323 restated: ids exact, probabilities within 2e-5."""
+    import importlib.util, os
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    spec = importlib.util.spec_from_file_location("mg", os.path.join(here, "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    x, w, H, E = mg.reference_router_fixture()
+    K, T = 8, 1
+    golden = np.load(os.path.join(here, "golden", "router_fixture.npz"))
+    import torch
+
+    logits = torch.empty(T, E, device=cuda)
+    ids = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    probs = torch.empty(T, K, device=cuda)
+    ws = moe.new_workspace(32, 32, E, K, T, cuda)
+    moe.router(dev_tensor(w, cuda), dev_tensor(x, cuda), logits, ids, probs, H, E, K, T, ws)
+    assert moe.device_status(ws)[0] == 0
+    assert np.array_equal(ids.cpu().numpy(), golden["ids"])
+    assert np.abs(probs.cpu().numpy() - golden["probs"]).max() < 2e-5
+    r_logits, r_ids, r_probs = oracle.router(w, x, H, E, K, T)
+    assert np.array_equal(r_ids, golden["ids"])
+
+
+@pytest.mark.parametrize("H,E,K,T", [(1024, 16, 2, 4), (2816, 128, 8, 1), (2816, 128, 8, 64), (1024, 16, 2, 2048),
+                                     (257, 128, 8, 33), (96, 256, 64, 7)])
+def test_router_ids_exact(cuda, moe, oracle, synth, H, E, K, T):
+    import torch
+
+    W = synth.normal(H * 31 + E, E * H, 0.02).reshape(E, H)
+    x = synth.normal(T * 17 + K, T * H).reshape(T, H)
+    logits = torch.empty(T, E, device=cuda)
+    ids = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    probs = torch.empty(T, K, device=cuda)
+    ws = moe.new_workspace(32, 32, E, K, T, cuda)
+    moe.router(dev_tensor(W, cuda), dev_tensor(x, cuda), logits, ids, probs, H, E, K, T, ws)
+    st, _ = moe.device_status(ws)
+    assert st == 0
+    r_logits, r_ids, r_probs = oracle.router(W, x, H, E, K, T)
+    assert np.array_equal(ids.cpu().numpy(), r_ids)
+    assert np.abs(probs.cpu().numpy() - r_probs).max() < 2e-5
+    assert np.abs(logits.cpu().numpy() - r_logits).max() < 1e-3
+
+
+def test_router_near_ties_take_the_exact_path(cuda, moe, oracle, synth):
+    """Experts whose logits differ by a few ulps: the certified fast path
+    cannot separate them, so the exact sequential chain decides."""
+    import torch
+
+    H, E, K, T = 2816, 128, 8, 16
+    base = synth.normal(91, H, 0.02)
+    W = np.stack([base + np.float32(1e-7) * synth.normal(92 + e, H) if e % 8 == 0 else synth.normal(200 + e, H, 0.02)
+                  for e in range(E)]).astype(np.float32)
+    x = synth.normal(93, T * H).reshape(T, H)
+    x[:, :] += 4.0 * base[None, :] / np.float32(np.linalg.norm(base))  # push the near-tied experts to the top
+    logits = torch.empty(T, E, device=cuda)
+    ids = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    probs = torch.empty(T, K, device=cuda)
+    ws = moe.new_workspace(32, 32, E, K, T, cuda)
+    moe.router(dev_tensor(W, cuda), dev_tensor(x, cuda), logits, ids, probs, H, E, K, T, ws)
+    st, recomputed = moe.device_status(ws)
+    assert st == 0
+    r_logits, r_ids, r_probs = oracle.router(W, x, H, E, K, T)
+    assert np.array_equal(ids.cpu().numpy(), r_ids)
+    assert recomputed > 0
+
+
+def test_router_exact_ties(cuda, moe, oracle):
+    import torch
+
+    H, E, K, T = 64, 16, 4, 2
+    W = np.zeros((E, H), np.float32)
+    W[[3, 7, 11, 12]] = 0.5
+    x = np.ones((T, H), np.float32)
+    logits = torch.empty(T, E, device=cuda)
+    ids = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    probs = torch.empty(T, K, device=cuda)
+    ws = moe.new_workspace(32, 32, E, K, T, cuda)
+    moe.router(dev_tensor(W, cuda), dev_tensor(x, cuda), logits, ids, probs, H, E, K, T, ws)
+    assert moe.device_status(ws)[0] == 0
+    assert ids.cpu().numpy().tolist() == [[3, 7, 11, 12]] * 2
+
+
+def test_route_from_logits_zipf(cuda, moe, oracle, synth):
+    """Config 3's routing: logits N(0,1) plus a Zipf(1.1) expert bias."""
+    import torch
+
+    E, K, T = 16, 2, 2048
+    logits = (synth.normal(5, T * E).reshape(T, E) + synth.zipf_bias(6, E)[None, :]).astype(np.float32)
+    logits[7, 3] = logits[7, 5]  # an exact tie
+    ids = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    probs = torch.empty(T, K, device=cuda)
+    moe.route_from_logits(dev_tensor(logits, cuda), ids, probs, E, K, T)
+    torch.cuda.synchronize()
+    r_ids, r_probs = oracle.route_from_logits(logits, E, K, T)
+    assert np.array_equal(ids.cpu().numpy(), r_ids)
+    assert np.abs(probs.cpu().numpy() - r_probs).max() < 2e-5
+
+
+# ----------------------------------------------------------------- experts
+
+
+def test_experts_reference_fixture(cuda, moe, oracle):
+    """ops_test.rs:453-541 inputs (Q4_0, H=64, I=32, E=2, K=2, scales 1.0/0.8)."""
+    import os
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    golden = np.load(os.path.join(here, "golden", "moe_fixture.npz"))
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("mg", os.path.join(here, "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    f = mg.reference_moe_fixture(oracle)
+    L = Layer(moe, cuda, 2, f["gate_up"], f["down"], None, f["H"], f["I"], f["E"], f["K"], 1, f["scales"])
+    got = L.experts(f["x"], f["ids"], f["probs"])
+    assert_close(got, golden["out"])
+    assert np.array_equal(got, golden["out"])  # this fixture has no tanh-sensitive rounding
+
+
+def test_config1_forward_matches_golden(cuda, moe, oracle, synth):
+    import importlib.util, os
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    spec = importlib.util.spec_from_file_location("mg", os.path.join(here, "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    c = mg.c1_inputs(synth)
+    golden = np.load(os.path.join(here, "golden", "c1_t4.npz"))
+    L = Layer(moe, cuda, c["wtype"], c["gate_up"], c["down"], c["W"], c["H"], c["I"], c["E"], c["K"], c["T"])
+    ids, probs, out, _ = L.forward(c["x"])
+    assert np.array_equal(ids, golden["ids"])
+    assert np.abs(probs - golden["probs"]).max() < 2e-5
+    assert_close(out, golden["out"])
+
+
+def make_layer_inputs(synth, wtype, H, I, E, T, seed):
+    gu, dn = synth.expert_weights(seed, wtype, H, I, E)
+    W = synth.normal(seed * 7919 + 11, E * H, 0.02).reshape(E, H)
+    x = synth.normal(seed * 7919 + 13 + T, T * H).reshape(T, H)
+    return gu, dn, W, x
+
+
+@pytest.fixture(scope="module")
+def c2_q4(cuda, moe, synth):
+    """Config-2 expert weights (128 experts, Q4_0), generated and quantised on
+    the GPU (the quantiser is checked byte-exact above); host copies."""
+    gu, dn = synth.expert_weights_device(2, 2, 2816, 704, 128, cuda, moe.quantize)
+    return gu.cpu().numpy(), dn.cpu().numpy()
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_config2_forward(cuda, moe, oracle, synth, c2_q4, T):
+    """Config 2: H=2816, E=128, K=8, I=704, Q4_0, T in {1, 8, 64}."""
+    H, I, E, K = 2816, 704, 128, 8
+    gu, dn = c2_q4
+    W = synth.normal(33, E * H, 0.02).reshape(E, H)
+    x = synth.normal(34 + T, T * H).reshape(T, H)
+    L = Layer(moe, cuda, 2, gu, dn, W, H, I, E, K, T)
+    ids, probs, out, _ = L.forward(x)
+    r_logits, r_ids, r_probs = oracle.router(W, x, H, E, K, T)
+    assert np.array_equal(ids, r_ids)
+    ref = oracle.experts(2, gu, dn, r_ids, r_probs, None, x, H, I, E, K, T, 8)
+    assert_close(out, ref)
+
+
+@pytest.mark.parametrize("wtype,H,I,E,K,T", [(8, 1024, 512, 16, 2, 64), (8, 2816, 704, 16, 8, 9), (2, 1024, 512, 16, 2, 33),
+                                             (2, 64, 32, 1, 1, 5), (8, 96, 64, 4, 4, 3)])
+def test_experts_shapes(cuda, moe, oracle, synth, wtype, H, I, E, K, T):
+    gu, dn, W, x = make_layer_inputs(synth, wtype, H, I, E, T, seed=H + I + E)
+    scale = (0.5 + synth.normal(77, E, 0.1)).astype(np.float32)
+    L = Layer(moe, cuda, wtype, gu, dn, W, H, I, E, K, T, scale)
+    _, r_ids, r_probs = oracle.router(W, x, H, E, K, T)
+    got = L.experts(x, r_ids, r_probs)
+    ref = oracle.experts(wtype, gu, dn, r_ids, r_probs, scale, x, H, I, E, K, T, 8)
+    assert_close(got, ref)
+
+
+def test_config3_prefill_zipf(cuda, moe, oracle, synth):
+    """Config 3: the config-1 layer (Q8_0) at T=2048 with Zipf-skewed routing."""
+    import torch
+
+    H, I, E, K, T = 1024, 512, 16, 2, 2048
+    gu, dn = synth.expert_weights(3, 8, H, I, E)
+    x = synth.normal(35, T * H).reshape(T, H)
+    logits = (synth.normal(36, T * E).reshape(T, E) + synth.zipf_bias(37, E)[None, :]).astype(np.float32)
+    r_ids, r_probs = oracle.route_from_logits(logits, E, K, T)
+    L = Layer(moe, cuda, 8, gu, dn, None, H, I, E, K, T)
+    got = L.experts(x, r_ids, r_probs)
+    ref = oracle.experts(8, gu, dn, r_ids, r_probs, None, x, H, I, E, K, T, 16)
+    assert_close(got, ref)
+    counts = np.bincount(r_ids.reshape(-1), minlength=E)
+    assert counts.max() > 3 * counts.min()  # the routing really is skewed
+
+
+def test_alpha_skip_and_zero_slots(cuda, moe, oracle, synth):
+    H, I, E, K, T = 256, 128, 8, 4, 6
+    gu, dn, W, x = make_layer_inputs(synth, 8, H, I, E, T, seed=4)
+    ids = np.array([[0, 1, 2, 3]] * T, np.int32)
+    probs = np.array([[0.7, 0.2999, 0.0001, 0.0]] * T, np.float32)
+    probs[3] = [1e-5, 1e-4, 5e-5, 0.0]  # a token with every slot skipped -> zeros
+    L = Layer(moe, cuda, 8, gu, dn, None, H, I, E, K, T)
+    got = L.experts(x, ids, probs)
+    ref = oracle.experts(8, gu, dn, ids, probs, None, x, H, I, E, K, T)
+    assert np.all(got[3] == 0.0)
+    assert_close(got, ref)
+
+
+def test_bad_expert_id_reported(cuda, moe, synth):
+    H, I, E, K, T = 64, 32, 4, 2, 2
+    gu, dn, W, x = make_layer_inputs(synth, 8, H, I, E, T, seed=9)
+    L = Layer(moe, cuda, 8, gu, dn, None, H, I, E, K, T)
+    d_x = dev_tensor(x, cuda)
+    ids = dev_tensor(np.array([[0, 9], [1, 2]], np.int32), cuda)
+    probs = dev_tensor(np.array([[0.5, 0.5], [0.5, 0.5]], np.float32), cuda)
+    moe.experts(8, L.gu, L.dn, ids, probs, None, d_x, L.out, H, I, E, K, T, L.ws)
+    st, _ = moe.device_status(L.ws)
+    assert st == -7
+    assert moe.device_status(L.ws)[0] == 0  # reading clears it
+
+
+def test_workspace_too_small(cuda, moe, synth):
+    import torch
+
+    H, I, E, K, T = 64, 32, 4, 2, 2
+    gu, dn, W, x = make_layer_inputs(synth, 8, H, I, E, T, seed=9)
+    L = Layer(moe, cuda, 8, gu, dn, None, H, I, E, K, T)
+    small = torch.zeros(512, dtype=torch.uint8, device=cuda)
+    with pytest.raises(moe.MoeError) as ei:
+        moe.experts(8, L.gu, L.dn, L.ids, L.probs, None, dev_tensor(x, cuda), L.out, H, I, E, K, T, small)
+    assert ei.value.status == -3
+
+
+def test_deterministic_and_token_permutation_equivariant(cuda, moe, synth, c2_q4):
+    """Size-independent properties at a prefill-size config-2 batch."""
+    H, I, E, K, T = 2816, 704, 128, 8, 512
+    gu, dn = c2_q4
+    W = synth.normal(40, E * H, 0.02).reshape(E, H)
+    x = synth.normal(41, T * H).reshape(T, H)
+    L = Layer(moe, cuda, 2, gu, dn, W, H, I, E, K, T)
+    ids1, probs1, out1, _ = L.forward(x)
+    ids2, probs2, out2, _ = L.forward(x)
+    assert np.array_equal(out1, out2) and np.array_equal(ids1, ids2)
+    perm = np.random.default_rng(3).permutation(T)
+    ids3, probs3, out3, _ = L.forward(x[perm])
+    assert np.array_equal(ids3, ids1[perm])
+    assert np.array_equal(out3, out1[perm])
+
+
+def test_reference_surface_mirror(cuda, moe, oracle, synth):
+    """The CudaDevice-style methods (cuda.rs:2772-2912) on a T=1 and a batch."""
+    import torch
+
+    H, I, E, K = 256, 128, 16, 8
+    gu, dn, W, x = make_layer_inputs(synth, 2, H, I, E, 3, seed=12)
+    dev = moe.MoeDevice(0)
+    d_W, d_x = dev_tensor(W, cuda), dev_tensor(x, cuda)
+    logits = torch.empty(E, device=cuda)
+    ids = torch.empty(K, dtype=torch.int32, device=cuda)
+    probs = torch.empty(K, device=cuda)
+    dev.moe_router(d_W, d_x[0], logits, ids, probs, H, E)
+    out = torch.empty(H, device=cuda)
+    act = torch.empty(K * I, device=cuda)
+    dev.moe_topk_q4_0(dev_tensor(gu, cuda), dev_tensor(dn, cuda), ids, probs, None, d_x[0], act, out, H, I, K)
+    torch.cuda.synchronize()
+    _, r_ids, r_probs = oracle.router(W, x[:1], H, E, K, 1)
+    assert np.array_equal(ids.cpu().numpy(), r_ids[0])
+    ref = oracle.experts(2, gu, dn, r_ids, r_probs, None, x[:1], H, I, E, K, 1)
+    assert_close(out.cpu().numpy()[None], ref)
+    # batch
+    T = 3
+    lb = torch.empty(T * E, device=cuda)
+    ib = torch.empty(T * K, dtype=torch.int32, device=cuda)
+    pb = torch.empty(T * K, device=cuda)
+    dev.moe_router_batch(d_W, d_x.reshape(-1), lb, ib, pb, H, E, T)
+    ob = torch.empty(T * H, device=cuda)
+    dev.moe_topk_batch_q4_0(dev_tensor(gu, cuda), dev_tensor(dn, cuda), ib, pb, None, d_x.reshape(-1),
+                            torch.empty(T * K * I, device=cuda), ob, H, I, K, T)
+    torch.cuda.synchronize()
+    _, r_ids, r_probs = oracle.router(W, x, H, E, K, T)
+    assert np.array_equal(ib.cpu().numpy().reshape(T, K), r_ids)
+    assert_close(ob.cpu().numpy().reshape(T, H), oracle.experts(2, gu, dn, r_ids, r_probs, None, x, H, I, E, K, T))
