@@ -69,8 +69,8 @@ WORKLOADS = {
     "c1_t4": (8, 1024, 512, 16, 2, 4, "router"),
 }
 KERNELS = {
-    "router": ["router_logits", "router_topk", "quantize", "dispatch", "gate_up", "down", "combine"],
-    "zipf_logits": ["route_from_logits", "quantize", "dispatch", "gate_up", "down", "combine"],
+    "router": ["router_logits", "router_topk", "dispatch", "quantize", "gate_up", "down", "combine"],
+    "zipf_logits": ["route_from_logits", "dispatch", "quantize", "gate_up", "down", "combine"],
 }
 
 
@@ -174,6 +174,32 @@ class LayerSet:
             m.experts(self.wtype, gu, dn, self.ids, self.probs, None, x, out, self.H, self.I, self.E, self.K, self.T,
                       self.ws)
 
+    def capture(self, i, profile_events=None):
+        """A CUDA graph of step i (the decode path replays per-layer graphs, as
+        the reference's capture_layer_ffn_graph does, model.rs:295-381).  With
+        profile_events, the library's hook records them around every launch."""
+        import ctypes
+
+        import torch
+
+        lib = self.moe.load_library()
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.step(i)  # warm the host-side caches outside capture
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=side):
+            if profile_events is not None:
+                handles = (ctypes.c_void_p * len(profile_events))(*[e.cuda_event for e in profile_events])
+                assert lib.mrml_moe_profile_events(handles, len(profile_events)) == 0
+            try:
+                self.step(i)
+            finally:
+                lib.mrml_moe_profile_events(None, 0)
+        return g
+
     def n_kernels(self):
         return len(KERNELS[self.routing])
 
@@ -223,85 +249,90 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-def time_steps(ls, steps, warmup, world, start_index=0):
-    """Device time (ms) of `steps` consecutive steps after `warmup` ones."""
+def time_steps(ls, steps, warmup, world, graphs):
+    """Device time (ms) of `steps` consecutive graph replays after `warmup`."""
     import torch
 
+    G = len(graphs)
     for i in range(warmup):
-        ls.step(start_index + i)
+        graphs[i % G].replay()
     barrier(world)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
     for i in range(steps):
-        ls.step(start_index + warmup + i)
+        graphs[(warmup + i) % G].replay()
     e1.record(s)
     torch.cuda.synchronize()
     barrier(world)
     return max_over_ranks(e0.elapsed_time(e1), world)
 
 
-def time_kernels(ls, steps, start_index=0):
-    """Per-kernel device times (ms, summed over steps) via the library's
-    profiling hook, which records events around every launch on the stream
-    the kernels run on."""
-    import ctypes
-
+def time_kernels(ls, steps):
+    """Per-kernel device times (ms, summed over steps): graphs captured with
+    the library's profiling hook, which records events around every launch on
+    the stream the kernels run on; one graph replay per step."""
     import torch
 
-    lib = ls.moe.load_library()
     nk = ls.n_kernels()
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * nk * steps)]
-    for e in evs:  # materialise the cudaEvent_t handles
-        e.record()
-    torch.cuda.synchronize()
-    handles = (ctypes.c_void_p * len(evs))(*[e.cuda_event for e in evs])
-    st = lib.mrml_moe_profile_events(handles, len(evs))
-    assert st == 0
-    try:
-        for i in range(steps):
-            ls.step(start_index + i)
-    finally:
-        lib.mrml_moe_profile_events(None, 0)
-    torch.cuda.synchronize()
     totals = [0.0] * nk
+    G = min(steps, 2 * ls.n_layers)
+    prof = []
+    for g in range(G):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * nk)]
+        for e in evs:
+            e.record()
+        torch.cuda.synchronize()
+        prof.append((ls.capture(g, evs), evs))
     for i in range(steps):
+        graph, evs = prof[i % G]
+        graph.replay()
+        torch.cuda.synchronize()
         for k in range(nk):
-            j = 2 * (i * nk + k)
-            totals[k] += evs[j].elapsed_time(evs[j + 1])
+            totals[k] += evs[2 * k].elapsed_time(evs[2 * k + 1])
     return dict(zip(KERNELS[ls.routing], totals))
 
 
 def time_e2e(ls, steps, warmup, world):
-    """Same steps through the public API with host buffers: H2D of x from
-    pinned memory and D2H of the output inside the timed region."""
+    """Same steps through the public API with host buffers: every step copies
+    its x from pinned host memory to the device, runs the layer and copies the
+    output back to pinned host memory.  Each step is a replayed CUDA graph of
+    those three stages (the reference's decode path captures its per-layer
+    FFN work the same way)."""
     import torch
 
     T, H = ls.T, ls.H
-    host_x = [ls.xs[i % len(ls.xs)].cpu().pin_memory() for i in range(max(steps, 1))]
-    host_out = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    G = 2 * ls.n_layers
+    host_x = [ls.xs[g % len(ls.xs)].cpu().pin_memory() for g in range(G)]
+    host_out = [torch.empty((T, H), dtype=torch.float32).pin_memory() for _ in range(G)]
     dx = torch.empty((T, H), device=ls.device)
-    s = torch.cuda.current_stream()
-
-    def one(i):
-        dx.copy_(host_x[i % len(host_x)], non_blocking=True)
-        ls.step(i, x=dx)
-        host_out.copy_(ls.out, non_blocking=True)
-
-    for i in range(warmup):
-        one(i)
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for i in range(steps):
-        one(warmup + i)
-    e1.record(s)
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    graphs = []
+    side = torch.cuda.Stream(device=ls.device)
+    for g in range(G):
+        with torch.cuda.stream(side):  # warm-up outside capture
+            dx.copy_(host_x[g], non_blocking=True)
+            ls.step(g, x=dx)
+            host_out[g].copy_(ls.out, non_blocking=True)
+        side.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            dx.copy_(host_x[g], non_blocking=True)
+            ls.step(g, x=dx)
+            host_out[g].copy_(ls.out, non_blocking=True)
+        graphs.append(graph)
+    ms = time_steps(ls, steps, warmup, world, graphs)
     return ms, T * H * 4, T * H * 4
+
+
+def router_recomputed(ls, steps):
+    """Tokens whose top-k needed the exact sequential logits, over `steps`
+    eager steps (read from the workspace's counter)."""
+    ls.moe.device_status(ls.ws)
+    for i in range(steps):
+        ls.step(i)
+    st, rec = ls.moe.device_status(ls.ws)
+    return {"tokens": rec, "of": steps * ls.T, "status": st}
 
 
 def algorithmic_bytes(ls, unique, pairs):
@@ -355,8 +386,11 @@ def run_ours(args):
 
     ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
     unique, pairs = ls.unique_experts(0)
+    graphs = [ls.capture(g) for g in range(2 * ls.n_layers)]
     with ClockSampler(local) as clk:
-        ms = time_steps(ls, steps, warmup, world)
+        ms = time_steps(ls, steps, warmup, world, graphs)
+    recomputed = router_recomputed(ls, steps)
+    del graphs
     kern = time_kernels(ls, steps)
     e2e_ms, h2d, d2h = time_e2e(ls, steps, warmup, world)
 
@@ -398,6 +432,7 @@ def run_ours(args):
         "e2e": {"value": round(world * T * steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": ls.n_kernels() * steps,
+        "router_exact_fallback_tokens": recomputed,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -413,7 +448,9 @@ def run_ours(args):
             ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank)
             u, p = ls.unique_experts(0)
             n = max(steps, 20)
-            m = time_steps(ls, n, max(warmup, 3), world)
+            gr = [ls.capture(g) for g in range(2 * ls.n_layers)]
+            m = time_steps(ls, n, max(warmup, 3), world, gr)
+            del gr
             k = time_kernels(ls, n)
             lb, gb = algorithmic_bytes(ls, u, p)
             also[name] = {"tokens_per_s": round(ls.T * n / (m / 1e3), 1), "ms_per_step": round(m / n, 5),

@@ -113,14 +113,21 @@ int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, co
 int mrml_moe_quantize_q8_0(const float *src, uint8_t *dst, size_t n, mrml_stream_t stream);
 int mrml_moe_quantize_q4_0(const float *src, uint8_t *dst, size_t n, mrml_stream_t stream);
 
+/* Process-wide options.  MRML_OPTION_EXPERT_PATH selects how the expert
+ * products run: 0 automatic (tensor cores once experts see several tokens),
+ * 1 CUDA-core dp4a kernels, 2 tcgen05 tensor-core kernels.  Both paths give
+ * bit-identical results; the option exists for tests and benchmarks. */
+enum { MRML_OPTION_EXPERT_PATH = 1 };
+int mrml_moe_set_option(int option, int value);
+
 /* Profiling hook for benchmarks.  With n_events > 0, the following calls on
  * this host thread record events[2i] (a cudaEvent_t) on their stream just
  * before their i-th kernel launch and events[2i+1] just after it, counting
  * launches across calls, until the list is used up or the hook is reset
  * with mrml_moe_profile_events(NULL, 0).  Per call: mrml_moe_router 2
- * launches, mrml_moe_route_from_logits 1, mrml_moe_experts 5,
- * mrml_moe_forward 7 (router_logits, router_topk, quantize, dispatch,
- * gate_up, down, combine). */
+ * launches (router_logits, router_topk), mrml_moe_route_from_logits 1,
+ * mrml_moe_experts 5 (dispatch, quantize, gate_up, down, combine), and
+ * mrml_moe_forward the 7 of both. */
 int mrml_moe_profile_events(void **events, int n_events);
 
 /* Synchronises `stream`, reads and clears the device status word of a

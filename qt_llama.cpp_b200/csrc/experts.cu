@@ -107,24 +107,32 @@ __global__ void quantize_q4_0_gguf_kernel(const float* __restrict__ x, uint8_t* 
 
 // ---------------------------------------------------------------------------
 // Dispatch: a stable counting sort of the (token, slot) pairs p = t*K + k by
-// expert id, skipping slots with alpha <= 1e-4 (model.rs:2119).  Produces
-// offsets[E+1], sorted[n] (pair ids, grouped by expert, ascending p within an
-// expert) and pos[T*K] (the sorted position of each pair, -1 if skipped).
+// expert id, skipping slots with alpha <= 1e-4 (model.rs:2119).  Each
+// expert's segment of the sorted order is padded to a multiple of 16
+// positions (tensor-core token tiles start on 8-position core-matrix
+// boundaries).  Produces cnt[E], poff[E+1] (padded segment starts),
+// pair_at[poff[E]] (the pair at each position, -1 for padding) and
+// pos[T*K] (each pair's position, -1 if skipped), and the work-unit tables
+// of the tensor-core products: units_gu / units_dn hold {e, first position,
+// valid positions, first weight row} per (expert, 128-row tile, NT-position
+// tile); n_units = {#gate/up units, #down units}.
 // One CTA of 1024 threads; pairs are ranked chunk by chunk with warp match.
 // ---------------------------------------------------------------------------
 constexpr int kDispatchThreads = 1024;
 
 __global__ void __launch_bounds__(kDispatchThreads)
     dispatch_kernel(const int32_t* __restrict__ ids, const float* __restrict__ probs, int n_pairs, int E,
-                    int32_t* __restrict__ offsets, int32_t* __restrict__ sorted, int32_t* __restrict__ pos,
-                    int* __restrict__ err) {
+                    int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
+                    int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
+                    int* __restrict__ n_units, int NT, int mt_gu, int mt_dn, int* __restrict__ err) {
   extern __shared__ int32_t dsm[];
-  int32_t* cnt = dsm;                  // [E] totals, then running bases
-  int32_t* wcnt = dsm + E;             // [32][E] per-warp counts of the current chunk
+  int32_t* cnt = dsm;            // [E] totals
+  int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
+  int32_t* ubase = dsm + 2 * E;  // [E] first unit of expert e (per product: times mt)
+  int32_t* wcnt = dsm + 3 * E;   // [32][E] per-warp counts of the current chunk
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < E * 33; i += blockDim.x) dsm[i] = 0;
+  for (int i = tid; i < E * 35; i += blockDim.x) dsm[i] = 0;
   __syncthreads();
-  // Pass 1: totals per expert.
   for (int p = tid; p < n_pairs; p += blockDim.x) {
     const int e = ids[p];
     if (probs[p] > 0.0001f) {
@@ -135,21 +143,38 @@ __global__ void __launch_bounds__(kDispatchThreads)
     }
   }
   __syncthreads();
-  // Exclusive scan of the totals (E is small; one thread).
   if (tid == 0) {
-    int run = 0;
+    int run = 0, units = 0;
     for (int e = 0; e < E; ++e) {
       const int c = cnt[e];
-      offsets[e] = run;
-      cnt[e] = run;
-      run += c;
+      poff[e] = run;
+      base[e] = run;
+      ubase[e] = units;
+      cnt_out[e] = c;
+      run += (c + 15) & ~15;
+      units += (c + NT - 1) / NT;
     }
-    offsets[E] = run;
+    poff[E] = run;
+    n_units[0] = units * mt_gu;
+    n_units[1] = units * mt_dn;
   }
   __syncthreads();
-  // Pass 2: stable scatter, 1024 pairs at a time.
-  for (int base = 0; base < n_pairs; base += blockDim.x) {
-    const int p = base + tid;
+  const int npos = poff[E];
+  for (int i = tid; i < npos; i += blockDim.x) pair_at[i] = -1;
+  // Work units, one thread per expert: (row tile m, position tile j), j fastest.
+  for (int e = tid; e < E; e += blockDim.x) {
+    const int c = cnt[e], nt = (c + NT - 1) / NT;
+    for (int m = 0; m < mt_gu; ++m)
+      for (int j = 0; j < nt; ++j)
+        units_gu[ubase[e] * mt_gu + m * nt + j] = make_int4(e, poff[e] + j * NT, min(NT, c - j * NT), m * 128);
+    for (int m = 0; m < mt_dn; ++m)
+      for (int j = 0; j < nt; ++j)
+        units_dn[ubase[e] * mt_dn + m * nt + j] = make_int4(e, poff[e] + j * NT, min(NT, c - j * NT), m * 128);
+  }
+  __syncthreads();
+  // Stable scatter, 1024 pairs at a time.
+  for (int b0 = 0; b0 < n_pairs; b0 += blockDim.x) {
+    const int p = b0 + tid;
     int e = -1;
     if (p < n_pairs) {
       const int id = ids[p];
@@ -160,25 +185,65 @@ __global__ void __launch_bounds__(kDispatchThreads)
     const int rank = __popc(peers & ((1u << lane) - 1u));
     if (e >= 0 && rank == 0) wcnt[warp * E + e] = __popc(peers);
     __syncthreads();
-    // Per expert: exclusive prefix over warps, in place.
     for (int x = tid; x < E; x += blockDim.x) {
-      int run = cnt[x];
+      int run = base[x];
       for (int w = 0; w < 32; ++w) {
         const int c = wcnt[w * E + x];
         wcnt[w * E + x] = run;
         run += c;
       }
-      cnt[x] = run;
+      base[x] = run;
     }
     __syncthreads();
     if (e >= 0) {
       const int dst = wcnt[warp * E + e] + rank;
-      sorted[dst] = p;
+      pair_at[dst] = p;
       pos[p] = dst;
     }
     __syncthreads();
     for (int i = tid; i < 32 * E; i += blockDim.x) wcnt[i] = 0;
     __syncthreads();
+  }
+}
+
+// Q8_0 quantisation of the layer input scattered straight into the tensor-
+// core B operand: for every position a token was routed to, its 32 int8
+// values of block b go to bq[b][pos/8] in the canonical K-major layout (two
+// 16-byte halves, core matrices of 8 positions), and {d, correction} to
+// bsc[b][pos].  One warp per (token, block), lane = element.
+template <int WQ4>
+__global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32_t* __restrict__ pos, int T, int H,
+                                        int K, int npad, int8_t* __restrict__ bq, int2* __restrict__ bsc) {
+  const int nb = H / 32;
+  const long long total = (long long)T * nb;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31;
+  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+    const int t = (int)(w / nb), b = (int)(w % nb);
+    const float v = x[(size_t)t * H + b * 32 + lane];
+    float amax = fabsf(v);
+    if (!(amax > 0.f)) amax = 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = __fdiv_rn(amax, 127.0f);
+    const uint32_t d16 = f32_to_f16_trunc(scale);
+    const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+    float r = round_half_away(__fmul_rn(v, id));
+    if (r != r) r = 0.f;
+    r = fminf(fmaxf(r, -128.f), 127.f);
+    const int q = (int)r;
+    int qsum = q;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+    const int2 sc = make_int2(__float_as_int(f16_bits_to_f32(d16)), WQ4 ? kMagicI - 8 * qsum : kMagicI);
+    for (int k = 0; k < K; ++k) {
+      const int p = pos[t * K + k];
+      if (p < 0) continue;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + ((size_t)b * (npad / 8) + (p >> 3)) * 256 + (lane >> 4) * 128 +
+                     (p & 7) * 16 + (lane & 15);
+      *dst = (uint8_t)(int8_t)q;
+      if (lane == 0) bsc[(size_t)b * npad + p] = sc;
+    }
   }
 }
 
@@ -267,12 +332,12 @@ __host__ __device__ inline GateUpSmem gate_up_smem_layout(int wtype, int H, int 
 
 template <int WT>
 __global__ void __launch_bounds__(kGateUpThreads)
-    gate_up_kernel(const uint8_t* __restrict__ gate_up, const int32_t* __restrict__ offsets,
-                   const int32_t* __restrict__ sorted, const int8_t* __restrict__ xq, const float* __restrict__ xd,
-                   const int32_t* __restrict__ xsum, float* __restrict__ act, int H, int I, int K, int tok_chunk,
-                   int* __restrict__ err) {
+    gate_up_kernel(const uint8_t* __restrict__ gate_up, const int32_t* __restrict__ cnt,
+                   const int32_t* __restrict__ poff, const int32_t* __restrict__ sorted,
+                   const int8_t* __restrict__ xq, const float* __restrict__ xd, const int32_t* __restrict__ xsum,
+                   float* __restrict__ act, int H, int I, int K, int tok_chunk, int* __restrict__ err) {
   const int e = blockIdx.y, tile = blockIdx.x;
-  const int beg = offsets[e], n_e = offsets[e + 1] - beg;
+  const int beg = poff[e], n_e = cnt[e];
   if (n_e <= 0) return;
   extern __shared__ __align__(128) uint8_t smem[];
   const GateUpSmem L = gate_up_smem_layout(WT, H, tok_chunk);
@@ -371,10 +436,11 @@ __host__ __device__ inline DownSmem down_smem_layout(int wtype, int I, int tok_c
 
 template <int WT>
 __global__ void __launch_bounds__(kDownThreads)
-    down_kernel(const uint8_t* __restrict__ down, const int32_t* __restrict__ offsets, const float* __restrict__ act,
-                float* __restrict__ ydown, int H, int I, int tok_chunk, int* __restrict__ err) {
+    down_kernel(const uint8_t* __restrict__ down, const int32_t* __restrict__ cnt, const int32_t* __restrict__ poff,
+                const float* __restrict__ act, float* __restrict__ ydown, int H, int I, int tok_chunk,
+                int* __restrict__ err) {
   const int e = blockIdx.y, tile = blockIdx.x;
-  const int beg = offsets[e], n_e = offsets[e + 1] - beg;
+  const int beg = poff[e], n_e = cnt[e];
   if (n_e <= 0) return;
   extern __shared__ __align__(128) uint8_t smem[];
   const DownSmem L = down_smem_layout(WT, I, tok_chunk);
@@ -469,14 +535,26 @@ cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long l
   return cudaPeekAtLastError();
 }
 
-cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* offsets,
-                            int32_t* sorted, int32_t* pos, int* err, cudaStream_t s) {
-  const size_t smem = (size_t)33 * E * sizeof(int32_t);
+cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* cnt, int32_t* poff,
+                            int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
+                            int mt_gu, int mt_dn, int* err, cudaStream_t s) {
+  const size_t smem = (size_t)35 * E * sizeof(int32_t);
   if (smem > 48 * 1024) {
     cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
   }
-  dispatch_kernel<<<1, kDispatchThreads, smem, s>>>(ids, probs, n_pairs, E, offsets, sorted, pos, err);
+  dispatch_kernel<<<1, kDispatchThreads, smem, s>>>(ids, probs, n_pairs, E, cnt, poff, pair_at, pos, units_gu,
+                                                     units_dn, n_units, NT, mt_gu, mt_dn, err);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,
+                                    int8_t* bq, int2* bsc, cudaStream_t s) {
+  const long long warps = (long long)T * (H / 32);
+  if (wtype == kQ4_0)
+    quantize_scatter_kernel<1><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, bq, bsc);
+  else
+    quantize_scatter_kernel<0><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, bq, bsc);
   return cudaPeekAtLastError();
 }
 
@@ -494,39 +572,39 @@ int down_tok_chunk(int wtype, int I) {
   return 0;
 }
 
-cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* offsets, const int32_t* sorted,
-                           const int8_t* xq, const float* xd, const int32_t* xsum, float* act, int H, int I, int E,
-                           int K, int* err, cudaStream_t s) {
+cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* cnt, const int32_t* poff,
+                           const int32_t* sorted, const int8_t* xq, const float* xd, const int32_t* xsum, float* act,
+                           int H, int I, int E, int K, int* err, cudaStream_t s) {
   const int chunk = gate_up_tok_chunk(wtype, H);
   const size_t smem = gate_up_smem_layout(wtype, H, chunk).total;
   const dim3 grid(I / kTileRows, E);
   if (wtype == kQ4_0) {
     cudaError_t st = cudaFuncSetAttribute(gate_up_kernel<kQ4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
-    gate_up_kernel<kQ4_0><<<grid, kGateUpThreads, smem, s>>>(gate_up, offsets, sorted, xq, xd, xsum, act, H, I, K,
+    gate_up_kernel<kQ4_0><<<grid, kGateUpThreads, smem, s>>>(gate_up, cnt, poff, sorted, xq, xd, xsum, act, H, I, K,
                                                              chunk, err);
   } else {
     cudaError_t st = cudaFuncSetAttribute(gate_up_kernel<kQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
-    gate_up_kernel<kQ8_0><<<grid, kGateUpThreads, smem, s>>>(gate_up, offsets, sorted, xq, xd, xsum, act, H, I, K,
+    gate_up_kernel<kQ8_0><<<grid, kGateUpThreads, smem, s>>>(gate_up, cnt, poff, sorted, xq, xd, xsum, act, H, I, K,
                                                              chunk, err);
   }
   return cudaPeekAtLastError();
 }
 
-cudaError_t launch_down(int wtype, const uint8_t* down, const int32_t* offsets, const float* act, float* ydown, int H,
-                        int I, int E, int* err, cudaStream_t s) {
+cudaError_t launch_down(int wtype, const uint8_t* down, const int32_t* cnt, const int32_t* poff, const float* act,
+                        float* ydown, int H, int I, int E, int* err, cudaStream_t s) {
   const int chunk = down_tok_chunk(wtype, I);
   const size_t smem = down_smem_layout(wtype, I, chunk).total;
   const dim3 grid(H / kTileRows, E);
   if (wtype == kQ4_0) {
     cudaError_t st = cudaFuncSetAttribute(down_kernel<kQ4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
-    down_kernel<kQ4_0><<<grid, kDownThreads, smem, s>>>(down, offsets, act, ydown, H, I, chunk, err);
+    down_kernel<kQ4_0><<<grid, kDownThreads, smem, s>>>(down, cnt, poff, act, ydown, H, I, chunk, err);
   } else {
     cudaError_t st = cudaFuncSetAttribute(down_kernel<kQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
-    down_kernel<kQ8_0><<<grid, kDownThreads, smem, s>>>(down, offsets, act, ydown, H, I, chunk, err);
+    down_kernel<kQ8_0><<<grid, kDownThreads, smem, s>>>(down, cnt, poff, act, ydown, H, I, chunk, err);
   }
   return cudaPeekAtLastError();
 }

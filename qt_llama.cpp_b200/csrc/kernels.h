@@ -12,13 +12,21 @@ cudaError_t launch_router_topk(const float* W, const float* x, float* logits, co
 cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
                                  cudaStream_t s);
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s);
-cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* offsets,
-                            int32_t* sorted, int32_t* pos, int* err, cudaStream_t s);
-cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* offsets, const int32_t* sorted,
-                           const int8_t* xq, const float* xd, const int32_t* xsum, float* act, int H, int I, int E,
-                           int K, int* err, cudaStream_t s);
-cudaError_t launch_down(int wtype, const uint8_t* down, const int32_t* offsets, const float* act, float* ydown, int H,
-                        int I, int E, int* err, cudaStream_t s);
+cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* cnt, int32_t* poff,
+                            int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
+                            int mt_gu, int mt_dn, int* err, cudaStream_t s);
+cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,
+                                    int8_t* bq, int2* bsc, cudaStream_t s);
+cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* cnt, const int32_t* poff,
+                           const int32_t* sorted, const int8_t* xq, const float* xd, const int32_t* xsum, float* act,
+                           int H, int I, int E, int K, int* err, cudaStream_t s);
+cudaError_t launch_down(int wtype, const uint8_t* down, const int32_t* cnt, const int32_t* poff, const float* act,
+                        float* ydown, int H, int I, int E, int* err, cudaStream_t s);
+// Tensor-core grouped products (gemm_tc.cu).  mode 0 = gate/up, 1 = down.
+bool tc_supported(int wtype, int H, int I, int NT);
+cudaError_t launch_gemm_tc(int mode, int wtype, int NT, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
+                           const int2* bsc, const int4* units, const int* n_units, int max_units, int npad,
+                           int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s);
 cudaError_t launch_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,
                            const float* down_scale, float* out, int H, int K, int T, cudaStream_t s);
 int gate_up_tok_chunk(int wtype, int H);

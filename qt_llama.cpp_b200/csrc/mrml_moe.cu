@@ -23,14 +23,25 @@ thread_local cudaEvent_t* t_events = nullptr;
 thread_local int t_n_events = 0;
 thread_local int t_next_event = 0;
 
+// Records an event on `s`; under stream capture it becomes an event-record
+// node of the graph (cudaEventRecordExternal), so it can be timed on replay.
+void record_event(cudaEvent_t e, cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(s, &cs);
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+  else
+    cudaEventRecord(e, s);
+}
+
 struct LaunchMark {
   cudaStream_t s;
   explicit LaunchMark(cudaStream_t st) : s(st) {
-    if (t_events && t_next_event + 1 < t_n_events) cudaEventRecord(t_events[t_next_event], s);
+    if (t_events && t_next_event + 1 < t_n_events) record_event(t_events[t_next_event], s);
   }
   ~LaunchMark() {
     if (t_events && t_next_event + 1 < t_n_events) {
-      cudaEventRecord(t_events[t_next_event + 1], s);
+      record_event(t_events[t_next_event + 1], s);
       t_next_event += 2;
     }
   }
@@ -38,18 +49,38 @@ struct LaunchMark {
 
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// Workspace regions (each 256-byte aligned), in order.
+// Largest token tile of the tensor-core path; position buffers carry this
+// much slack so that a tile starting at the last position stays in bounds.
+constexpr int kMaxNT = 64;
+
+// Positions after padding every expert's segment to a multiple of 16.
+int npad_alloc(int E, int K, int T) { return (((T * K + 16 * E) + 15) & ~15) + kMaxNT; }
+
+int units_bound(int E, int K, int T, int NT, int rows) {
+  return ((T * K + NT - 1) / NT + E) * ((rows + 127) / 128);
+}
+
+// Workspace regions (each 256-byte aligned), in order.  Positions are the
+// padded, expert-grouped order produced by the dispatch kernel.
 struct Workspace {
-  int* status;     // [0] device status word, [1] router recompute counter
-  int8_t* xq;      // [T][H]        Q8_0 values of the layer input
-  float* xd;       // [T][H/32]     decoded Q8_0 scales
-  int32_t* xsum;   // [T][H/32]     sums of the Q8_0 values per block
-  float* bounds;   // [T][E]        router error bounds
-  int32_t* offsets;  // [E+1]       per-expert start in the sorted pair list
-  int32_t* sorted;   // [T*K]       pair ids grouped by expert
-  int32_t* pos;      // [T*K]       sorted position of each pair (-1 skipped)
-  float* act;        // [T*K][I]    geglu output per sorted pair
-  float* ydown;      // [T*K][H]    down output per sorted pair (unscaled)
+  int* status;       // [0] device status word, [1] router recompute counter, [2..3] unit counts
+  int8_t* xq;        // [T][H]        Q8_0 values of the layer input (CUDA-core path)
+  float* xd;         // [T][H/32]     decoded Q8_0 scales
+  int32_t* xsum;     // [T][H/32]     sums of the Q8_0 values per block
+  float* bounds;     // [T][E]        router error bounds
+  int32_t* cnt;      // [E]           pairs per expert
+  int32_t* poff;     // [E+1]         padded segment start per expert
+  int32_t* pair_at;  // [npad]        pair at each position (-1 padding)
+  int32_t* pos;      // [T*K]         position of each pair (-1 skipped)
+  int4* units_gu;    // tensor-core work units, gate/up
+  int4* units_dn;    // tensor-core work units, down
+  int8_t* xb;        // [H/32][npad/8][256]  tensor-core B operand of gate/up
+  int2* xs;          // [H/32][npad]         its scales
+  int8_t* ab;        // [I/32][npad/8][256]  B operand of down (re-quantised act)
+  int2* as;          // [I/32][npad]         its scales
+  float* act;        // [npad][I]     geglu output per position (CUDA-core path)
+  float* ydown;      // [npad][H]     down output per position (unscaled)
+  int npad, max_units_gu, max_units_dn;
   size_t bytes;
 };
 
@@ -62,20 +93,34 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
     off += align256(n);
     return r;
   };
-  const size_t nb = (size_t)H / 32, tk = (size_t)T * K;
+  const size_t nb = (size_t)H / 32, nbi = (size_t)I / 32, tk = (size_t)T * K;
+  const int npad = npad_alloc(E, K, T);
+  w.npad = npad;
+  w.max_units_gu = units_bound(E, K, T, 16, I);
+  w.max_units_dn = units_bound(E, K, T, 16, H);
   w.status = reinterpret_cast<int*>(take(256));
   w.xq = reinterpret_cast<int8_t*>(take((size_t)T * H));
   w.xd = reinterpret_cast<float*>(take((size_t)T * nb * 4));
   w.xsum = reinterpret_cast<int32_t*>(take((size_t)T * nb * 4));
   w.bounds = reinterpret_cast<float*>(take((size_t)T * E * 4));
-  w.offsets = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
-  w.sorted = reinterpret_cast<int32_t*>(take(tk * 4));
+  w.cnt = reinterpret_cast<int32_t*>(take((size_t)E * 4));
+  w.poff = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
+  w.pair_at = reinterpret_cast<int32_t*>(take((size_t)npad * 4));
   w.pos = reinterpret_cast<int32_t*>(take(tk * 4));
-  w.act = reinterpret_cast<float*>(take(tk * I * 4));
-  w.ydown = reinterpret_cast<float*>(take(tk * H * 4));
+  w.units_gu = reinterpret_cast<int4*>(take((size_t)w.max_units_gu * 16));
+  w.units_dn = reinterpret_cast<int4*>(take((size_t)w.max_units_dn * 16));
+  w.xb = reinterpret_cast<int8_t*>(take(nb * npad * 32));
+  w.xs = reinterpret_cast<int2*>(take(nb * npad * 8));
+  w.ab = reinterpret_cast<int8_t*>(take(nbi * npad * 32));
+  w.as = reinterpret_cast<int2*>(take(nbi * npad * 8));
+  w.act = reinterpret_cast<float*>(take((size_t)npad * I * 4));
+  w.ydown = reinterpret_cast<float*>(take((size_t)npad * H * 4));
   w.bytes = off;
   return w;
 }
+
+// Expert-product path: 0 = automatic, 1 = CUDA-core dp4a, 2 = tensor cores.
+int g_path = 0;
 
 // Once per device: is it an sm_100 part?
 int check_device() {
@@ -143,14 +188,37 @@ int run_router(const Workspace& w, const float* W, const float* x, float* logits
   return MRML_OK;
 }
 
+// Tensor cores pay off once experts see several tokens; a single decode
+// token per expert is served better by the finer-grained CUDA-core kernels.
+bool use_tensor_cores(int wtype, int H, int I, int E, int K, int T, int NT) {
+  if (g_path == 1) return false;
+  const bool ok = mrml::tc_supported(wtype, H, I, NT);
+  if (g_path == 2) return ok;
+  return ok && (long long)T * K >= 2ll * E;
+}
+
 int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids,
                 const float* probs, const float* down_scale, const float* x, float* out, int H, int I, int E, int K,
                 int T, cudaStream_t s) {
-  MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
-  MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, w.offsets, w.sorted, w.pos, w.status, s));
-  MRML_LAUNCH(
-      mrml::launch_gate_up(wtype, gate_up, w.offsets, w.sorted, w.xq, w.xd, w.xsum, w.act, H, I, E, K, w.status, s));
-  MRML_LAUNCH(mrml::launch_down(wtype, down, w.offsets, w.act, w.ydown, H, I, E, w.status, s));
+  const int NT = (long long)T * K > 12ll * E ? 64 : 16;
+  const bool tc = use_tensor_cores(wtype, H, I, E, K, T, NT);
+  const int mt_gu = (I + 127) / 128, mt_dn = (H + 127) / 128;
+  int* n_units = w.status + 2;
+  MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
+                                    n_units, NT, mt_gu, mt_dn, w.status, s));
+  if (tc) {
+    const int mu_gu = units_bound(E, K, T, NT, I), mu_dn = units_bound(E, K, T, NT, H);
+    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, w.xb, w.xs, s));
+    MRML_LAUNCH(mrml::launch_gemm_tc(0, wtype, NT, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad,
+                                     w.ab, w.as, nullptr, w.status, s));
+    MRML_LAUNCH(mrml::launch_gemm_tc(1, wtype, NT, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
+                                     nullptr, nullptr, w.ydown, w.status, s));
+  } else {
+    MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
+    MRML_LAUNCH(mrml::launch_gate_up(wtype, gate_up, w.cnt, w.poff, w.pair_at, w.xq, w.xd, w.xsum, w.act, H, I, E, K,
+                                     w.status, s));
+    MRML_LAUNCH(mrml::launch_down(wtype, down, w.cnt, w.poff, w.act, w.ydown, H, I, E, w.status, s));
+  }
   MRML_LAUNCH(mrml::launch_combine(w.ydown, w.pos, ids, probs, down_scale, out, H, K, T, s));
   return MRML_OK;
 }
@@ -245,6 +313,15 @@ int mrml_moe_quantize_q4_0(const float* src, uint8_t* dst, size_t n, mrml_stream
   if (!src || !dst) return MRML_ERR_INVALID_ARGUMENT;
   MRML_TRY(check_device());
   return cuda_status(mrml::launch_quantize_gguf(kQ4_0, src, dst, (long long)(n / 32), (cudaStream_t)stream));
+}
+
+int mrml_moe_set_option(int option, int value) {
+  if (option == MRML_OPTION_EXPERT_PATH) {
+    if (value < 0 || value > 2) return MRML_ERR_INVALID_ARGUMENT;
+    g_path = value;
+    return MRML_OK;
+  }
+  return MRML_ERR_INVALID_ARGUMENT;
 }
 
 int mrml_moe_profile_events(void** events, int n_events) {

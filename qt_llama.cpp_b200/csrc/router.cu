@@ -7,11 +7,11 @@
 //
 // A sequential 2816-term f32 chain per (token, expert) is latency bound
 // (~6 us), so the GPU computes every logit in parallel and, with it, a
-// rigorous bound B on |CPU value - our value|.  The top-K choice and order
-// are accepted only when every comparison that decides them is separated by
-// more than the two bounds.  The few experts whose intervals overlap are then
-// recomputed with the exact sequential chain, so the chosen ids and their
-// order always equal the CPU's.
+// rigorous bound B on |reference value - our value|.  The top-K choice and
+// order are accepted only when every comparison that decides them is
+// separated by more than the two bounds.  The few experts whose intervals
+// overlap are then recomputed with the exact sequential chain, so the chosen
+// ids and their order always equal the reference's.
 //
 // Error bound.  For the sequential sum s^_n of the rounded products the
 // first-order bound is |s^_n - s_n| <= u*(sum_i |p_i| + sum_k |s^_k|), u =
@@ -27,42 +27,75 @@ namespace mrml {
 
 constexpr int kRouterWarps = 8;
 constexpr int kMaxCandidates = 64;  // also the largest supported K
+constexpr int kTopkWarps = 8;       // tokens per top-k CTA
+constexpr int kExactRows = 4;       // flagged expert rows staged per pass
 
-// grid (E, ceil(T / tokens_per_cta)), block 32*kRouterWarps.
-// Writes logits[t*E + e] (our estimate) and bounds[t*E + e] (B >= 0).
+// Row pitch (floats) of the chunked layout: lane l owns elements
+// [l*C, l*C + C) of a row, stored at l*pitch; an odd pitch keeps the 32
+// lanes' reads of one chunk offset on 32 different banks.
+__host__ __device__ inline int chunk_len(int H) { return (H + 31) / 32; }
+__host__ __device__ inline int chunk_pitch(int H) { return chunk_len(H) | 1; }
+
+// Copies `rows` rows of length H (row stride H) into the chunked layout.
+// The chunk index and offset of element i advance incrementally.
+__device__ __forceinline__ void stage_chunked(float* dst, const float* __restrict__ src, int rows, int H) {
+  const int C = chunk_len(H), pitch = chunk_pitch(H), row_floats = 32 * pitch;
+  const int step = blockDim.x, dq = step / C, dr = step % C;
+  for (int r = 0; r < rows; ++r) {
+    const float* s = src + (size_t)r * H;
+    float* d = dst + r * row_floats;
+    int q = threadIdx.x / C, rem = threadIdx.x % C;
+    for (int i = threadIdx.x; i < H; i += step) {
+      d[q * pitch + rem] = s[i];
+      q += dq;
+      rem += dr;
+      if (rem >= C) {
+        rem -= C;
+        ++q;
+      }
+    }
+  }
+}
+
+// grid (ceil(E / epc), ceil(T / tpc)), block 32*kRouterWarps.  The CTA
+// stages tpc token rows of x and epc expert rows of W in shared memory
+// (coalesced global reads), then one warp per (token, expert) pair computes
+// the logit and its error bound.  Writes logits[t*E + e] and bounds[t*E + e].
 __global__ void __launch_bounds__(32 * kRouterWarps)
     router_logits_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
-                         float* __restrict__ bounds, int H, int E, int T, int tokens_per_cta) {
-  extern __shared__ float wsm[];  // 32 chunks of C floats, each padded by 1
-  const int e = blockIdx.x;
-  const int C = (H + 31) / 32;
-  const int pitch = C + 1;
-  const float* wrow = W + (size_t)e * H;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) wsm[(i / C) * pitch + (i % C)] = wrow[i];
+                         float* __restrict__ bounds, int H, int E, int T, int epc, int tpc) {
+  extern __shared__ float rsm[];
+  const int C = chunk_len(H), pitch = chunk_pitch(H);
+  const int row_floats = 32 * pitch;
+  const int e0 = blockIdx.x * epc, t0 = blockIdx.y * tpc;
+  const int ne = min(epc, E - e0), nt = min(tpc, T - t0);
+  float* xs = rsm;                     // [tpc][row_floats]
+  float* ws = rsm + tpc * row_floats;  // [epc][row_floats]
+  stage_chunked(xs, x + (size_t)t0 * H, nt, H);
+  stage_chunked(ws, W + (size_t)e0 * H, ne, H);
   __syncthreads();
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t0 = blockIdx.y * tokens_per_cta;
-  const int t1 = min(T, t0 + tokens_per_cta);
   const int start = lane * C;
   const int len = max(0, min(C, H - start));
-  const float* wl = wsm + lane * pitch;
   const float u = 5.9604644775390625e-8f;  // 2^-24
-
-  for (int t = t0 + warp; t < t1; t += kRouterWarps) {
-    const float* xl = x + (size_t)t * H + start;
+  for (int p = warp; p < ne * nt; p += kRouterWarps) {
+    const int el = p % ne, tl = p / ne;
+    const float* xl = xs + tl * row_floats + lane * pitch;
+    const float* wl = ws + el * row_floats + lane * pitch;
     float r = 0.f, A = 0.f, P = 0.f;
+#pragma unroll 4
     for (int j = 0; j < len; ++j) {
-      float p = __fmul_rn(xl[j], wl[j]);
-      r = __fadd_rn(r, p);
+      const float prod = __fmul_rn(xl[j], wl[j]);
+      r = __fadd_rn(r, prod);
       A += fabsf(r);
-      P += fabsf(p);
+      P += fabsf(prod);
     }
     // Exclusive prefix of the chunk sums, in double.
     double incl = (double)r;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      double v = __shfl_up_sync(0xffffffffu, incl, o);
+      const double v = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += v;
     }
     const double excl = incl - (double)r;
@@ -84,18 +117,10 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
       // Slack for rounding the center to f32 and for the f32 comparisons of
       // c - B against c' + B' made by the top-k kernel.
       B += 4.f * fabsf(center) * u + fabsf((float)(total - (double)center)) + 1e-30f;
-      logits[(size_t)t * E + e] = center;
-      bounds[(size_t)t * E + e] = B;
+      logits[(size_t)(t0 + tl) * E + e0 + el] = center;
+      bounds[(size_t)(t0 + tl) * E + e0 + el] = B;
     }
   }
-}
-
-// The reference's exact value of one logit: sequential f32, mul then add.
-__device__ float exact_logit(const float* __restrict__ x, const float* __restrict__ w, int H) {
-  float dot = 0.f;
-#pragma unroll 8
-  for (int i = 0; i < H; ++i) dot = __fadd_rn(dot, __fmul_rn(x[i], w[i]));
-  return dot;
 }
 
 // (value desc, id asc) ordering used by the reference's GPU top-8
@@ -140,170 +165,269 @@ __device__ __forceinline__ void warp_topk(const float (&val)[PL], int E, int K, 
   __syncwarp();
 }
 
-// One warp per token.  bounds == nullptr means the logits are exact inputs
-// (route-from-logits): no certification is needed.  When bounds is given,
-// W and x must be the router weights and inputs the logits came from.
-// stats[0] counts tokens that needed an exact recomputation.
+// The reference's exact value of one logit: sequential f32, mul then add,
+// over rows staged in shared memory (vector loads when H % 4 == 0; the order
+// of the additions is the reference's either way).
+__device__ __forceinline__ float exact_logit_smem(const float* __restrict__ xs, const float* __restrict__ ws, int H) {
+  float dot = 0.f;
+  int i = 0;
+  if ((H & 3) == 0) {
+    for (; i < H; i += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(xs + i);
+      const float4 b = *reinterpret_cast<const float4*>(ws + i);
+      dot = __fadd_rn(dot, __fmul_rn(a.x, b.x));
+      dot = __fadd_rn(dot, __fmul_rn(a.y, b.y));
+      dot = __fadd_rn(dot, __fmul_rn(a.z, b.z));
+      dot = __fadd_rn(dot, __fmul_rn(a.w, b.w));
+    }
+  }
+  for (; i < H; ++i) dot = __fadd_rn(dot, __fmul_rn(xs[i], ws[i]));
+  return dot;
+}
+
+struct TopkShared {
+  int cand[kTopkWarps][kMaxCandidates];
+  float cval[kTopkWarps][kMaxCandidates];
+  float cbnd[kTopkWarps][kMaxCandidates];
+  int flag[kTopkWarps][kMaxCandidates];
+  int count[kTopkWarps];
+  int pending[kTopkWarps];  // warps of this CTA whose token needs exact values
+  int n_pending;
+};
+
+// Per-token selection tail: order Z (count candidates) by (value desc, id
+// asc), then the reference's softmax over the first K.
+__device__ void finish_token(int* cand, float* cval, int count, int K, int t, int32_t* ids, float* probs) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) {
+    for (int i = 1; i < count; ++i) {
+      const float v = cval[i];
+      const int c = cand[i];
+      int j = i - 1;
+      while (j >= 0 && better(v, c, cval[j], cand[j])) {
+        cval[j + 1] = cval[j];
+        cand[j + 1] = cand[j];
+        --j;
+      }
+      cval[j + 1] = v;
+      cand[j + 1] = c;
+    }
+  }
+  __syncwarp();
+  // model.rs:1819-1829: p_k = expf(l_k - l_0), summed in k order, then
+  // divided by max(sum, 1e-6).  Lanes compute the exponentials in parallel;
+  // lane 0 adds them in k order.
+  const float max_l = cval[0];
+  __syncwarp();
+  for (int k = lane; k < K; k += 32) cval[k] = exp_f32(__fsub_rn(cval[k], max_l));
+  __syncwarp();
+  float sum = 0.f;
+  if (lane == 0)
+    for (int k = 0; k < K; ++k) sum = __fadd_rn(sum, cval[k]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  const float denom = sum > 1e-6f ? sum : 1e-6f;
+  for (int k = lane; k < K; k += 32) {
+    ids[(size_t)t * K + k] = cand[k];
+    probs[(size_t)t * K + k] = __fdiv_rn(cval[k], denom);
+  }
+  __syncwarp();
+}
+
+// grid ceil(T / kTopkWarps), block 32*kTopkWarps; one warp per token.
+// bounds == nullptr: the logits are exact inputs (route-from-logits).
+// Otherwise W and x are the router weights and inputs the logits came from,
+// and the dynamic shared memory (router_exact_smem(H) bytes) stages the rows
+// of the exact fallback.  stats[0] counts tokens that needed it.
 template <int PL>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(32 * kTopkWarps)
     router_topk_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
                        const float* __restrict__ bounds, int32_t* __restrict__ ids, float* __restrict__ probs, int H,
                        int E, int K, int T, int* __restrict__ stats) {
-  const int lane = threadIdx.x & 31;
-  const int wl = threadIdx.x >> 5;
-  const int t = blockIdx.x * (blockDim.x >> 5) + wl;
-  if (t >= T) return;
-  __shared__ int s_cand[4][kMaxCandidates];
-  __shared__ float s_val[4][kMaxCandidates];
-  __shared__ int s_flag[4][kMaxCandidates];
-  int* cand = s_cand[wl];
-  float* cval = s_val[wl];
-  int* flag = s_flag[wl];
+  __shared__ TopkShared S;
+  extern __shared__ __align__(16) float stage[];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int t = blockIdx.x * kTopkWarps + wl;
+  if (threadIdx.x == 0) S.n_pending = 0;
+  __syncthreads();
+  int* cand = S.cand[wl];
+  float* cval = S.cval[wl];
+  float* cbnd = S.cbnd[wl];
+  int* flag = S.flag[wl];
+  bool mine_pending = false;
 
-  float* lrow = logits + (size_t)t * E;
-  const float* brow = bounds ? bounds + (size_t)t * E : nullptr;
-  float val[PL];
-  float bnd[PL];
-#pragma unroll
-  for (int m = 0; m < PL; ++m) {
-    const int e = lane + 32 * m;
-    val[m] = e < E ? lrow[e] : -INFINITY;
-    bnd[m] = (e < E && brow) ? brow[e] : 0.f;
-  }
-  uint32_t taken;
-  warp_topk<PL>(val, E, K, cand, cval, taken);
-  int count = K;
-
-  if (brow) {
-    // Lowest lower bound among the chosen experts.
-    float lowest_lo = INFINITY;
-#pragma unroll
-    for (int m = 0; m < PL; ++m)
-      if (taken >> m & 1u) lowest_lo = fminf(lowest_lo, val[m] - bnd[m]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lowest_lo = fminf(lowest_lo, __shfl_xor_sync(0xffffffffu, lowest_lo, o));
-
-    // Candidate set Z = chosen experts plus every expert whose upper bound
-    // reaches lowest_lo: every other expert is below all K chosen ones in the
-    // reference too, so the reference's top-K lies in Z.
-    count = K;
+  if (t < T) {
+    float* lrow = logits + (size_t)t * E;
+    const float* brow = bounds ? bounds + (size_t)t * E : nullptr;
+    float val[PL];
+    float bnd[PL];
 #pragma unroll
     for (int m = 0; m < PL; ++m) {
       const int e = lane + 32 * m;
-      const bool extra = e < E && !(taken >> m & 1u) && val[m] + bnd[m] >= lowest_lo;
-      const uint32_t mask = __ballot_sync(0xffffffffu, extra);
-      if (extra) {
-        const int slot = count + __popc(mask & ((1u << lane) - 1u));
-        if (slot < kMaxCandidates) {
-          cand[slot] = e;
-          cval[slot] = val[m];
-        }
-      }
-      count += __popc(mask);
+      val[m] = e < E ? lrow[e] : -INFINITY;
+      bnd[m] = (e < E && brow) ? brow[e] : 0.f;
     }
-    __syncwarp();
-
-    bool recomputed = false;
-    if (count <= kMaxCandidates) {
-      // Exact values for every candidate whose interval meets another's.
-      for (int i = lane; i < count; i += 32) {
-        const int ei = cand[i];
-        const float ci = cval[i], bi_ = brow[ei];
-        bool overlap = false;
-        for (int j = 0; j < count; ++j) {
-          if (j == i) continue;
-          const float cj = cval[j], bj = brow[cand[j]];
-          if (!(ci - bi_ > cj + bj || cj - bj > ci + bi_)) overlap = true;
-        }
-        flag[i] = overlap;
-      }
-      __syncwarp();
-      for (int i = lane; i < count; i += 32) {
-        if (flag[i]) {
-          const int e = cand[i];
-          const float v = exact_logit(x + (size_t)t * H, W + (size_t)e * H, H);
-          cval[i] = v;
-          lrow[e] = v;
-          recomputed = true;
-        }
-      }
-      __syncwarp();
-      // Order Z by (value desc, id asc).  Every pair is either separated by
-      // its bounds or compared on exact values: this is the reference order.
-      if (lane == 0) {
-        for (int i = 1; i < count; ++i) {
-          const float v = cval[i];
-          const int c = cand[i];
-          int j = i - 1;
-          while (j >= 0 && better(v, c, cval[j], cand[j])) {
-            cval[j + 1] = cval[j];
-            cand[j + 1] = cand[j];
-            --j;
-          }
-          cval[j + 1] = v;
-          cand[j + 1] = c;
-        }
-      }
-    } else {
-      // Bounds too wide to certify anything: exact values for all experts.
-      recomputed = true;
+    uint32_t taken;
+    warp_topk<PL>(val, E, K, cand, cval, taken);
+    int count = K;
+    if (brow) {
+      float lowest_lo = INFINITY;
+#pragma unroll
+      for (int m = 0; m < PL; ++m)
+        if (taken >> m & 1u) lowest_lo = fminf(lowest_lo, val[m] - bnd[m]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lowest_lo = fminf(lowest_lo, __shfl_xor_sync(0xffffffffu, lowest_lo, o));
+      // Bounds of the chosen experts, in the order of cand[].
+      for (int k = lane; k < K; k += 32) cbnd[k] = brow[cand[k]];
+      // Candidate set Z = chosen experts plus every expert whose upper bound
+      // reaches lowest_lo: every other expert is below all K chosen ones in
+      // the reference too, so the reference's top-K lies in Z.
 #pragma unroll
       for (int m = 0; m < PL; ++m) {
         const int e = lane + 32 * m;
-        if (e < E) {
-          val[m] = exact_logit(x + (size_t)t * H, W + (size_t)e * H, H);
-          lrow[e] = val[m];
+        const bool extra = e < E && !(taken >> m & 1u) && val[m] + bnd[m] >= lowest_lo;
+        const uint32_t mask = __ballot_sync(0xffffffffu, extra);
+        if (extra) {
+          const int slot = count + __popc(mask & ((1u << lane) - 1u));
+          if (slot < kMaxCandidates) {
+            cand[slot] = e;
+            cval[slot] = val[m];
+            cbnd[slot] = bnd[m];
+          }
+        }
+        count += __popc(mask);
+      }
+      __syncwarp();
+      bool any = false;
+      if (count <= kMaxCandidates) {
+        for (int i = lane; i < count; i += 32) {
+          const float ci = cval[i], bi_ = cbnd[i];
+          bool overlap = false;
+          for (int j = 0; j < count; ++j) {
+            if (j == i) continue;
+            const float cj = cval[j], bj = cbnd[j];
+            if (!(ci - bi_ > cj + bj || cj - bj > ci + bi_)) overlap = true;
+          }
+          flag[i] = overlap;
+          any |= overlap;
+        }
+      } else {
+        any = true;  // bounds too wide to certify: exact values for all
+      }
+      mine_pending = __any_sync(0xffffffffu, any);
+    }
+    if (lane == 0) S.count[wl] = count;
+    if (!mine_pending) finish_token(cand, cval, min(count, kMaxCandidates), K, t, ids, probs);
+  }
+  if (lane == 0 && mine_pending) S.pending[atomicAdd(&S.n_pending, 1)] = wl;
+  __syncthreads();
+  const int n_pending = S.n_pending;
+  if (n_pending == 0) return;
+  if (threadIdx.x == 0 && stats) atomicAdd(stats, n_pending);
+
+  // Exact fallback, one pending token at a time: the whole CTA stages the
+  // token's x row and up to kExactRows flagged W rows, and one thread per
+  // row runs the reference's sequential chain.
+  const int pitch = (H + 3) & ~3;
+  float* xs = stage;
+  float* wsr = stage + pitch;
+  for (int q = 0; q < n_pending; ++q) {
+    const int w = S.pending[q];
+    const int tq = blockIdx.x * kTopkWarps + w;
+    float* lrow = logits + (size_t)tq * E;
+    int count = S.count[w];
+    const bool all = count > kMaxCandidates;
+    int* qc = S.cand[w];
+    float* qv = S.cval[w];
+    int* qf = S.flag[w];
+    const int n_items = all ? E : count;
+    __syncthreads();
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[(size_t)tq * H + i];
+    for (int base = 0; base < n_items; base += kExactRows) {
+      __syncthreads();
+      for (int r = 0; r < kExactRows; ++r) {
+        const int item = base + r;
+        if (item >= n_items || !(all || qf[item])) continue;
+        const float* wrow = W + (size_t)(all ? item : qc[item]) * H;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) wsr[r * pitch + i] = wrow[i];
+      }
+      __syncthreads();
+      if (threadIdx.x < kExactRows) {
+        const int item = base + threadIdx.x;
+        if (item < n_items && (all || qf[item])) {
+          const int e = all ? item : qc[item];
+          const float v = exact_logit_smem(xs, wsr + threadIdx.x * pitch, H);
+          lrow[e] = v;
+          if (!all) qv[item] = v;
         }
       }
-      warp_topk<PL>(val, E, K, cand, cval, taken);
     }
-    recomputed = __any_sync(0xffffffffu, recomputed);
-    if (recomputed && lane == 0 && stats) atomicAdd(stats, 1);
-    __syncwarp();
-  }
-
-  // model.rs:1819-1829: p_k = expf(l_k - l_0), summed in k order, then
-  // divided by max(sum, 1e-6).
-  if (lane == 0) {
-    const float max_l = cval[0];
-    float sum = 0.f;
-    for (int k = 0; k < K; ++k) sum = __fadd_rn(sum, exp_f32(__fsub_rn(cval[k], max_l)));
-    const float denom = sum > 1e-6f ? sum : 1e-6f;
-    for (int k = 0; k < K; ++k) {
-      ids[(size_t)t * K + k] = cand[k];
-      probs[(size_t)t * K + k] = __fdiv_rn(exp_f32(__fsub_rn(cval[k], max_l)), denom);
+    __syncthreads();
+    if (wl == w) {
+      if (all) {
+        float val[PL];
+#pragma unroll
+        for (int m = 0; m < PL; ++m) {
+          const int e = lane + 32 * m;
+          val[m] = e < E ? lrow[e] : -INFINITY;
+        }
+        uint32_t taken;
+        warp_topk<PL>(val, E, K, qc, qv, taken);
+        count = K;
+      }
+      finish_token(qc, qv, count, K, tq, ids, probs);
     }
   }
 }
 
-
-}  // namespace mrml
-
 // ------------------------------------------------------------ launchers ---
-namespace mrml {
+
+// cudaFuncSetAttribute once per (kernel, device, size): it is host-side
+// state and not a stream operation, but calling it on every launch costs
+// host time on the decode path.
+template <typename Kern>
+cudaError_t ensure_smem(Kern k, size_t bytes, int* cache) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  if (dev >= 0 && dev < 16 && cache[dev] >= (int)bytes) return cudaSuccess;
+  st = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (st == cudaSuccess && dev >= 0 && dev < 16) cache[dev] = (int)bytes;
+  return st;
+}
 
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, float* bounds, int H, int E, int T,
                                  cudaStream_t s) {
-  const int tpc = T < 64 ? T : 64;
-  const dim3 grid(E, (T + tpc - 1) / tpc);
-  const size_t smem = (size_t)32 * ((H + 31) / 32 + 1) * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t st = cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (st != cudaSuccess) return st;
-  }
-  router_logits_kernel<<<grid, 32 * kRouterWarps, smem, s>>>(W, x, logits, bounds, H, E, T, tpc);
+  static int cache[16] = {0};
+  const int epc = T <= 4 ? 1 : 4;
+  const int tpc = T <= 4 ? T : 8;
+  const dim3 grid((E + epc - 1) / epc, (T + tpc - 1) / tpc);
+  const size_t smem = (size_t)(epc + tpc) * 32 * chunk_pitch(H) * sizeof(float);
+  cudaError_t st = ensure_smem(router_logits_kernel, smem, cache);
+  if (st != cudaSuccess) return st;
+  router_logits_kernel<<<grid, 32 * kRouterWarps, smem, s>>>(W, x, logits, bounds, H, E, T, epc, tpc);
   return cudaPeekAtLastError();
 }
 
+size_t router_exact_smem(int H) { return (size_t)((H + 3) & ~3) * (1 + kExactRows) * sizeof(float); }
+
 cudaError_t launch_router_topk(const float* W, const float* x, float* logits, const float* bounds, int32_t* ids,
                                float* probs, int H, int E, int K, int T, int* stats, cudaStream_t s) {
-  const dim3 grid((T + 3) / 4);
-  if (E <= 32)
-    router_topk_kernel<1><<<grid, 128, 0, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
-  else if (E <= 128)
-    router_topk_kernel<4><<<grid, 128, 0, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
-  else
-    router_topk_kernel<8><<<grid, 128, 0, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
+  static int cache[3][16] = {{0}};
+  const dim3 grid((T + kTopkWarps - 1) / kTopkWarps);
+  const int block = 32 * kTopkWarps;
+  const size_t smem = bounds ? router_exact_smem(H) : 0;
+  cudaError_t st;
+  if (E <= 32) {
+    if ((st = ensure_smem(router_topk_kernel<1>, smem, cache[0])) != cudaSuccess) return st;
+    router_topk_kernel<1><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
+  } else if (E <= 128) {
+    if ((st = ensure_smem(router_topk_kernel<4>, smem, cache[1])) != cudaSuccess) return st;
+    router_topk_kernel<4><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
+  } else {
+    if ((st = ensure_smem(router_topk_kernel<8>, smem, cache[2])) != cudaSuccess) return st;
+    router_topk_kernel<8><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
+  }
   return cudaPeekAtLastError();
 }
 

@@ -52,6 +52,7 @@ SIGNATURES = {
     "mrml_moe_quantize_q4_0": (_i, [_vp, _vp, _sz, _vp]),
     "mrml_moe_device_status": (_i, [_vp, _vp, _c.POINTER(_c.c_int)]),
     "mrml_moe_profile_events": (_i, [_c.POINTER(_vp), _i]),
+    "mrml_moe_set_option": (_i, [_i, _i]),
 }
 
 
@@ -154,6 +155,15 @@ def quantize(wtype, src, dst, stream=None):
     lib = load_library()
     fn = lib.mrml_moe_quantize_q4_0 if wtype == MRML_Q4_0 else lib.mrml_moe_quantize_q8_0
     _check("mrml_moe_quantize", fn(_ptr(src), _ptr(dst), src.numel(), _stream_ptr(stream)))
+
+
+OPTION_EXPERT_PATH = 1
+PATH_AUTO, PATH_DP4A, PATH_TENSOR = 0, 1, 2
+
+
+def set_expert_path(path: int) -> None:
+    """0 automatic, 1 CUDA-core dp4a, 2 tcgen05 tensor cores (process-wide)."""
+    _check("mrml_moe_set_option", load_library().mrml_moe_set_option(OPTION_EXPERT_PATH, path))
 
 
 def device_status(ws, stream=None):

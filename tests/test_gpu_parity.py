@@ -17,6 +17,17 @@ pytestmark = pytest.mark.gpu
 MAX_ABS_FRAC = 1e-3
 REL_L2 = 1e-4
 
+PATHS = {"dp4a": 1, "tensor": 2}
+
+
+@pytest.fixture(params=sorted(PATHS))
+def expert_path(request, cuda, moe):
+    """Run the test once on each expert-product path (CUDA-core dp4a and the
+    tcgen05 tensor-core kernels); restores automatic selection after."""
+    moe.set_expert_path(PATHS[request.param])
+    yield request.param
+    moe.set_expert_path(0)
+
 
 def dev_tensor(a, device):
     import torch
@@ -199,7 +210,7 @@ def test_route_from_logits_zipf(cuda, moe, oracle, synth):
 # ----------------------------------------------------------------- experts
 
 
-def test_experts_reference_fixture(cuda, moe, oracle):
+def test_experts_reference_fixture(cuda, moe, oracle, expert_path):
     """ops_test.rs:453-541 inputs (Q4_0, H=64, I=32, E=2, K=2, scales 1.0/0.8)."""
     import os
 
@@ -217,7 +228,7 @@ def test_experts_reference_fixture(cuda, moe, oracle):
     assert np.array_equal(got, golden["out"])  # this fixture has no tanh-sensitive rounding
 
 
-def test_config1_forward_matches_golden(cuda, moe, oracle, synth):
+def test_config1_forward_matches_golden(cuda, moe, oracle, synth, expert_path):
     import importlib.util, os
 
     here = os.path.dirname(os.path.abspath(__file__))
@@ -249,7 +260,7 @@ def c2_q4(cuda, moe, synth):
 
 
 @pytest.mark.parametrize("T", [1, 8, 64])
-def test_config2_forward(cuda, moe, oracle, synth, c2_q4, T):
+def test_config2_forward(cuda, moe, oracle, synth, c2_q4, T, expert_path):
     """Config 2: H=2816, E=128, K=8, I=704, Q4_0, T in {1, 8, 64}."""
     H, I, E, K = 2816, 704, 128, 8
     gu, dn = c2_q4
@@ -264,8 +275,9 @@ def test_config2_forward(cuda, moe, oracle, synth, c2_q4, T):
 
 
 @pytest.mark.parametrize("wtype,H,I,E,K,T", [(8, 1024, 512, 16, 2, 64), (8, 2816, 704, 16, 8, 9), (2, 1024, 512, 16, 2, 33),
-                                             (2, 64, 32, 1, 1, 5), (8, 96, 64, 4, 4, 3)])
-def test_experts_shapes(cuda, moe, oracle, synth, wtype, H, I, E, K, T):
+                                             (2, 64, 32, 1, 1, 5), (8, 96, 64, 4, 4, 3), (2, 256, 32, 3, 2, 40),
+                                             (8, 512, 160, 8, 8, 100), (2, 2816, 704, 32, 8, 300)])
+def test_experts_shapes(cuda, moe, oracle, synth, wtype, H, I, E, K, T, expert_path):
     gu, dn, W, x = make_layer_inputs(synth, wtype, H, I, E, T, seed=H + I + E)
     scale = (0.5 + synth.normal(77, E, 0.1)).astype(np.float32)
     L = Layer(moe, cuda, wtype, gu, dn, W, H, I, E, K, T, scale)
@@ -275,7 +287,7 @@ def test_experts_shapes(cuda, moe, oracle, synth, wtype, H, I, E, K, T):
     assert_close(got, ref)
 
 
-def test_config3_prefill_zipf(cuda, moe, oracle, synth):
+def test_config3_prefill_zipf(cuda, moe, oracle, synth, expert_path):
     """Config 3: the config-1 layer (Q8_0) at T=2048 with Zipf-skewed routing."""
     import torch
 
@@ -292,7 +304,7 @@ def test_config3_prefill_zipf(cuda, moe, oracle, synth):
     assert counts.max() > 3 * counts.min()  # the routing really is skewed
 
 
-def test_alpha_skip_and_zero_slots(cuda, moe, oracle, synth):
+def test_alpha_skip_and_zero_slots(cuda, moe, oracle, synth, expert_path):
     H, I, E, K, T = 256, 128, 8, 4, 6
     gu, dn, W, x = make_layer_inputs(synth, 8, H, I, E, T, seed=4)
     ids = np.array([[0, 1, 2, 3]] * T, np.int32)
@@ -330,7 +342,7 @@ def test_workspace_too_small(cuda, moe, synth):
     assert ei.value.status == -3
 
 
-def test_deterministic_and_token_permutation_equivariant(cuda, moe, synth, c2_q4):
+def test_deterministic_and_token_permutation_equivariant(cuda, moe, synth, c2_q4, expert_path):
     """Size-independent properties at a prefill-size config-2 batch."""
     H, I, E, K, T = 2816, 704, 128, 8, 512
     gu, dn = c2_q4
@@ -379,3 +391,26 @@ def test_reference_surface_mirror(cuda, moe, oracle, synth):
     _, r_ids, r_probs = oracle.router(W, x, H, E, K, T)
     assert np.array_equal(ib.cpu().numpy().reshape(T, K), r_ids)
     assert_close(ob.cpu().numpy().reshape(T, H), oracle.experts(2, gu, dn, r_ids, r_probs, None, x, H, I, E, K, T))
+
+
+@pytest.mark.parametrize("wtype,T", [(2, 64), (8, 200), (2, 1)])
+def test_paths_bit_identical(cuda, moe, synth, c2_q4, wtype, T):
+    """The tensor-core and CUDA-core paths keep the same per-block order of
+    f32 operations, so their outputs agree bit for bit."""
+    H, I, E, K = 2816, 704, 128, 8
+    if wtype == 2:
+        gu, dn = c2_q4
+    else:
+        g, d = synth.expert_weights_device(4, 8, H, I, E, cuda, moe.quantize)
+        gu, dn = g.cpu().numpy(), d.cpu().numpy()
+    W = synth.normal(50, E * H, 0.02).reshape(E, H)
+    x = synth.normal(51 + T, T * H).reshape(T, H)
+    L = Layer(moe, cuda, wtype, gu, dn, W, H, I, E, K, T)
+    try:
+        moe.set_expert_path(1)
+        _, _, a, _ = L.forward(x)
+        moe.set_expert_path(2)
+        _, _, b, _ = L.forward(x)
+    finally:
+        moe.set_expert_path(0)
+    assert np.array_equal(a, b)
