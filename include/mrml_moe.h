@@ -114,9 +114,12 @@ int mrml_moe_quantize_q8_0(const float *src, uint8_t *dst, size_t n, mrml_stream
 int mrml_moe_quantize_q4_0(const float *src, uint8_t *dst, size_t n, mrml_stream_t stream);
 
 /* Process-wide options.  MRML_OPTION_EXPERT_PATH selects how the expert
- * products run: 0 automatic (tensor cores once experts see several tokens),
- * 1 CUDA-core dp4a kernels, 2 tcgen05 tensor-core kernels.  Both paths give
- * bit-identical results; the option exists for tests and benchmarks. */
+ * products run: 0 automatic (tcgen05 tensor cores once experts see more than
+ * 16 tokens on average, else the pipelined CUDA-core dp4a kernels),
+ * 1 pipelined CUDA-core kernels, 2 tensor cores, 3 the general CUDA-core
+ * kernels (any H, I multiple of 32; used automatically when H is not a
+ * multiple of 256).  All paths give bit-identical results; the option exists
+ * for tests and benchmarks. */
 enum { MRML_OPTION_EXPERT_PATH = 1 };
 int mrml_moe_set_option(int option, int value);
 

@@ -115,7 +115,8 @@ __global__ void quantize_q4_0_gguf_kernel(const float* __restrict__ x, uint8_t* 
 // pos[T*K] (each pair's position, -1 if skipped), and the work-unit tables
 // of the tensor-core products: units_gu / units_dn hold {e, first position,
 // valid positions, first weight row} per (expert, 128-row tile, NT-position
-// tile); n_units = {#gate/up units, #down units}.
+// tile; gate/up tiles have rows_gu rows, down tiles 128); n_units =
+// {#gate/up units, #down units}.
 // One CTA of 1024 threads; pairs are ranked chunk by chunk with warp match.
 // ---------------------------------------------------------------------------
 constexpr int kDispatchThreads = 1024;
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(kDispatchThreads)
     dispatch_kernel(const int32_t* __restrict__ ids, const float* __restrict__ probs, int n_pairs, int E,
                     int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
                     int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
-                    int* __restrict__ n_units, int NT, int mt_gu, int mt_dn, int* __restrict__ err) {
+                    int* __restrict__ n_units, int NT, int mt_gu, int rows_gu, int mt_dn, int* __restrict__ err) {
   extern __shared__ int32_t dsm[];
   int32_t* cnt = dsm;            // [E] totals
   int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
@@ -166,7 +167,7 @@ __global__ void __launch_bounds__(kDispatchThreads)
     const int c = cnt[e], nt = (c + NT - 1) / NT;
     for (int m = 0; m < mt_gu; ++m)
       for (int j = 0; j < nt; ++j)
-        units_gu[ubase[e] * mt_gu + m * nt + j] = make_int4(e, poff[e] + j * NT, min(NT, c - j * NT), m * 128);
+        units_gu[ubase[e] * mt_gu + m * nt + j] = make_int4(e, poff[e] + j * NT, min(NT, c - j * NT), m * rows_gu);
     for (int m = 0; m < mt_dn; ++m)
       for (int j = 0; j < nt; ++j)
         units_dn[ubase[e] * mt_dn + m * nt + j] = make_int4(e, poff[e] + j * NT, min(NT, c - j * NT), m * 128);
@@ -537,14 +538,14 @@ cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long l
 
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
-                            int mt_gu, int mt_dn, int* err, cudaStream_t s) {
+                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s) {
   const size_t smem = (size_t)35 * E * sizeof(int32_t);
   if (smem > 48 * 1024) {
     cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
   }
   dispatch_kernel<<<1, kDispatchThreads, smem, s>>>(ids, probs, n_pairs, E, cnt, poff, pair_at, pos, units_gu,
-                                                     units_dn, n_units, NT, mt_gu, mt_dn, err);
+                                                     units_dn, n_units, NT, mt_gu, rows_gu, mt_dn, err);
   return cudaPeekAtLastError();
 }
 

@@ -11,178 +11,28 @@
 // scale-and-accumulate runs in the epilogue warps in the reference's order.
 //
 // Warp roles (one CTA per SM, persistent over units):
-//   warp 0       TMA producer: raw GGUF weight chunks (tensor-map tiles, or
-//                1-D bulk copies of whole rows), activation B tiles, scales
+//   warp 0       weight producer: raw GGUF weight chunks (TMA tensor-map
+//                tiles, or 1-D bulk copies of whole rows)
 //   warp 1       TMEM allocation; lane 0 issues the MMAs
-//   warps 2..5   converters: raw Q4_0/Q8_0 bytes -> int8 A tiles in the
+//   warp 2       activation producer: B tiles and their scales (bulk copies)
+//   warps 3..6   converters: raw Q4_0/Q8_0 bytes -> int8 A tiles in the
 //                canonical no-swizzle K-major layout, f16 scales -> f32
-//   warps 6..    epilogue: tcgen05.ld, block scaling, GeGLU, re-quantisation
+//   warps 7..    epilogue: tcgen05.ld, block scaling, GeGLU, re-quantisation
 //                of act (gate/up) or the f32 down rows (down)
+// The two producers run independently, so the HBM weight stream can run as
+// far ahead as its ring allows, whatever the activation ring's depth.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
 // drops out of its loops, frees its TMEM and returns.
 #include <cuda.h>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "pipe.cuh"
 
 namespace mrml {
 namespace tc {
 
-constexpr int kM = 128;        // weight rows per tile (MMA M)
-constexpr int kKC = 8;         // quant blocks per gate/up K chunk (8*18 and 8*34 bytes are 16-byte multiples)
-constexpr int kConvWarps = 4;
-constexpr int kEpiWarp0 = 6;
-constexpr int kMaxRing = 16;
-
-enum Mode : int { kGateUp = 0, kDown = 1 };
-
-struct Params {
-  const uint8_t* w_raw;  // down: raw weights [E][rows][row_bytes]
-  const int8_t* bq;      // B operand [nb][npad_alloc/8][2][8][16]
-  const int2* bsc;       // B scales [nb][npad_alloc] {f32 bits of d_a, int32 correction}
-  const int4* units;     // {e, p0, nvalid, m0}
-  const int* n_units;
-  int nb;                // quant blocks along K
-  int rows;              // weight rows per expert part (I for gate/up, H for down)
-  int row_bytes;         // raw bytes per weight row
-  int npad;              // position stride of bq/bsc/out (npad_alloc)
-  int w_q4;              // 1: weights Q4_0 (unsigned nibbles), 0: Q8_0
-  // gate/up outputs: act as the down product's B operand and its scales
-  int8_t* out_q;
-  int2* out_s;
-  int down_q4;           // the down weights' type (selects the act correction)
-  // down output
-  float* y;              // [npad_alloc][H]
-  int* err;
-  // ring sizes
-  int rs, as, bs, tb;
-  int raw_bytes;         // bytes per raw stage
-  int kcb;               // blocks per B stage (kKC for gate/up, nb for down)
-};
-
-struct __align__(8) Bars {
-  uint64_t raw_full[2], raw_empty[2];
-  uint64_t conv_full[kMaxRing], conv_empty[kMaxRing];
-  uint64_t bs_full[2], bs_empty[2];
-  uint64_t tmem_full[kMaxRing], tmem_empty[kMaxRing];
-  uint32_t tmem_base;
-  int abort;
-};
-
-__device__ __forceinline__ bool aborted(const Bars* B) { return *(const volatile int*)&B->abort != 0; }
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Bounded wait that also watches the CTA's abort flag.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* B, int* err) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 255 && aborted(B)) return false;
-    if (i > 128) __nanosleep(64);
-  }
-  set_error(err, kDevTimeout);
-  *(volatile int*)&B->abort = 1;
-  return false;
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Shared-memory matrix descriptor, canonical K-major layout without swizzle:
-// 8-row x 16-byte core matrices stored contiguously; LBO = distance between
-// the two core matrices along K (128 B), SBO = distance between 8-row groups
-// (256 B).  Bits 46-47 hold the descriptor version (1) for sm_100.
-__device__ __forceinline__ uint64_t smem_desc(const void* p) {
-  const uint32_t a = smem_u32(p);
-  uint64_t d = (uint64_t)((a >> 4) & 0x3FFF);
-  d |= (uint64_t)(128 >> 4) << 16;
-  d |= (uint64_t)(256 >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  return d;
-}
-
-// Instruction descriptor of tcgen05.mma kind::i8: D s32, A u8 or s8,
-// B s8, both K-major, N and M encoded as N>>3 and M>>4.
-__host__ __device__ constexpr uint32_t idesc_i8(bool a_unsigned, int N, int M) {
-  return (2u << 4) | ((a_unsigned ? 0u : 1u) << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
-         ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, 0, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 8 consecutive TMEM columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// ---------------------------------------------------------------- convert
-// Writes one row's 32 int8 values (two 16-byte halves) into an A tile in the
-// canonical layout: core (g, c) at (2g + c)*128, row rr at +16*rr.
-__device__ __forceinline__ void store_a_row(int8_t* tile, int r, uint4 lo, uint4 hi) {
-  uint8_t* base = reinterpret_cast<uint8_t*>(tile) + (r >> 3) * 256 + (r & 7) * 16;
-  *reinterpret_cast<uint4*>(base) = lo;
-  *reinterpret_cast<uint4*>(base + 128) = hi;
-}
-
-// Q4_0 block -> unsigned nibble bytes: low nibbles are elements 0..15,
-// high nibbles elements 16..31 (quant.rs:119-163).
-__device__ __forceinline__ void q4_to_a(const uint32_t (&qs)[4], uint4& lo, uint4& hi) {
-  lo = make_uint4(qs[0] & 0x0f0f0f0fu, qs[1] & 0x0f0f0f0fu, qs[2] & 0x0f0f0f0fu, qs[3] & 0x0f0f0f0fu);
-  hi = make_uint4((qs[0] >> 4) & 0x0f0f0f0fu, (qs[1] >> 4) & 0x0f0f0f0fu, (qs[2] >> 4) & 0x0f0f0f0fu,
-                  (qs[3] >> 4) & 0x0f0f0f0fu);
-}
-
-// Reads the 16-byte-aligned window around block `bl` of a gate/up chunk row
-// (row pitch 8*BB bytes, a 16-byte multiple) and extracts the block.
-template <int BB, int BL>
-__device__ __forceinline__ void chunk_block(const uint8_t* row, uint32_t& d16, uint32_t (&qs)[BB == 18 ? 4 : 8]) {
-  constexpr int start = BB * BL;
-  constexpr int w0 = (start & ~15);
-  constexpr int nvec = ((start + BB - w0) + 15) / 16;
-  uint32_t w[4 * nvec];
-#pragma unroll
-  for (int v = 0; v < nvec; ++v) {
-    const uint4 t = *reinterpret_cast<const uint4*>(row + w0 + 16 * v);
-    w[4 * v] = t.x;
-    w[4 * v + 1] = t.y;
-    w[4 * v + 2] = t.z;
-    w[4 * v + 3] = t.w;
-  }
-  constexpr int off = start - w0;  // even, 0..14
-  constexpr int wi = off / 4;
-  if constexpr ((off & 3) == 0) {  // scale in the low half of w[wi]
-    d16 = w[wi] & 0xffffu;
-#pragma unroll
-    for (int i = 0; i < (BB == 18 ? 4 : 8); ++i) qs[i] = __funnelshift_r(w[wi + i], w[wi + i + 1], 16);
-  } else {  // scale in the high half, values word-aligned
-    d16 = w[wi] >> 16;
-#pragma unroll
-    for (int i = 0; i < (BB == 18 ? 4 : 8); ++i) qs[i] = w[wi + 1 + i];
-  }
-}
+// Pipeline helpers (Bars, bounded waits, TMA, descriptors) live in pipe.cuh.
 
 // ------------------------------------------------------------------ kernel
 template <int WQ4, int MODE, int NT>
@@ -195,14 +45,17 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
   constexpr int EW = 4 * ((NT + 31) / 32);         // epilogue warps
   constexpr uint32_t IDESC = idesc_i8(WQ4 != 0, NT, kM);
   constexpr int A_BYTES = kM * 32;                 // one A tile
-  constexpr int SLOT_BYTES = NA * (A_BYTES + kM * 4);
+  constexpr int SLOT_BYTES = NA * A_BYTES;
+  constexpr int DW_BYTES = NA * kM * 4;
+  constexpr int kG = NT <= 16 ? 4 : 1;             // blocks per epilogue round (decode tiles)
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   Bars* B = reinterpret_cast<Bars*>(smem);
   uint8_t* raw = smem + 1024;
-  uint8_t* conv = raw + P.rs * P.raw_bytes;                       // 1024-aligned (raw_bytes multiple of 1024)
-  uint8_t* bsb = conv + P.as * SLOT_BYTES;                        // B tiles + scales
+  uint8_t* conv = raw + P.rs * P.raw_bytes;   // A tiles, 1024-aligned (raw_bytes multiple of 1024)
+  float* dwr = reinterpret_cast<float*>(conv + P.as * SLOT_BYTES);  // weight scales, P.tb slots
+  uint8_t* bsb = reinterpret_cast<uint8_t*>(dwr) + P.tb * DW_BYTES;  // B tiles + scales
   const int bs_stage = P.kcb * NT * (32 + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -213,7 +66,11 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
     }
     for (int i = 0; i < P.as; ++i) {
       mbar_init(&B->conv_full[i], kConvWarps);
-      mbar_init(&B->conv_empty[i], EW);
+      mbar_init(&B->conv_empty[i], 1);
+    }
+    for (int i = 0; i < P.tb; ++i) {
+      mbar_init(&B->dw_full[i], kConvWarps);
+      mbar_init(&B->dw_empty[i], EW);
     }
     for (int i = 0; i < P.bs; ++i) {
       mbar_init(&B->bs_full[i], 1);
@@ -238,13 +95,13 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
   const int nkc = MODE == kGateUp ? P.nb / kKC : 1;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ----------------------------------------------------- weight producer
     if (lane == 0) {
-      int rs = 0, bsi = 0;
-      uint32_t rph = 0, bph = 0;
+      int rs = 0;
+      uint32_t rph = 0;
       for (int u = blockIdx.x; u < n_units && !aborted(B); u += gridDim.x) {
         const int4 U = P.units[u];
-        const int e = U.x, p0 = U.y, m0 = U.w;
+        const int e = U.x, m0 = U.w;
         for (int kc = 0; kc < nkc; ++kc) {
           if (!wait_bar(&B->raw_empty[rs], rph ^ 1, B, P.err)) break;
           uint8_t* dst = raw + rs * P.raw_bytes;
@@ -263,6 +120,17 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
             rs = 0;
             rph ^= 1;
           }
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------- activation producer
+    if (lane == 0) {
+      int bsi = 0;
+      uint32_t bph = 0;
+      for (int u = blockIdx.x; u < n_units && !aborted(B); u += gridDim.x) {
+        const int p0 = P.units[u].y;
+        for (int kc = 0; kc < nkc; ++kc) {
           if (!wait_bar(&B->bs_empty[bsi], bph ^ 1, B, P.err)) break;
           uint8_t* bdst = bsb + bsi * bs_stage;
           const int b0 = kc * P.kcb;
@@ -299,6 +167,7 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
             const uint64_t bdesc = smem_desc(bt + bl * NT * 32);
             mma_i8(tmem + ts * CPB, smem_desc(slot), bdesc, IDESC);
             if constexpr (NA == 2) mma_i8(tmem + ts * CPB + NT, smem_desc(slot + A_BYTES), bdesc, IDESC);
+            mma_commit(&B->conv_empty[as]);  // A slot reusable once these MMAs have read it
             mma_commit(&B->tmem_full[ts]);
             if (++as == P.as) {
               as = 0;
@@ -319,9 +188,9 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
     }
   } else if (warp < kEpiWarp0) {
     // ---------------------------------------------------------- converters
-    const int r = threadIdx.x - 64;  // weight row within the tile
-    int rs = 0, as = 0;
-    uint32_t rph = 0, aph = 0;
+    const int r = threadIdx.x - 32 * kConvWarp0;  // weight row within the tile
+    int rs = 0, as = 0, ts = 0;
+    uint32_t rph = 0, aph = 0, tph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok && !aborted(B); u += gridDim.x) {
       for (int kc = 0; kc < nkc && ok; ++kc) {
@@ -332,9 +201,11 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
           const uint8_t* urow = src + kM * kKC * BB + r * (kKC * BB);
 #define MRML_CONV_BLOCK(BL)                                                                   \
   {                                                                                           \
-    if (ok && (ok = wait_bar(&B->conv_empty[as], aph ^ 1, B, P.err))) {                       \
+    if (ok) ok = wait_bar(&B->conv_empty[as], aph ^ 1, B, P.err);                             \
+    if (ok) ok = wait_bar(&B->dw_empty[ts], tph ^ 1, B, P.err);                               \
+    if (ok) {                                                                                 \
       uint8_t* slot = conv + as * SLOT_BYTES;                                                 \
-      float* dws = reinterpret_cast<float*>(slot + NA * A_BYTES);                             \
+      float* dws = dwr + ts * (NA * kM);                                                      \
       uint32_t d16;                                                                           \
       uint32_t qs[BB == 18 ? 4 : 8];                                                          \
       uint4 lo, hi;                                                                           \
@@ -350,8 +221,12 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
       dws[kM + r] = f16_bits_to_f32(d16);                                                     \
       fence_proxy_async();                                                                    \
       __syncwarp();                                                                           \
-      if (lane == 0) mbar_arrive(&B->conv_full[as]);                                          \
+      if (lane == 0) {                                                                        \
+        mbar_arrive(&B->conv_full[as]);                                                       \
+        mbar_arrive(&B->dw_full[ts]);                                                         \
+      }                                                                                       \
       if (++as == P.as) { as = 0; aph ^= 1; }                                                 \
+      if (++ts == P.tb) { ts = 0; tph ^= 1; }                                                 \
     }                                                                                         \
   }
           MRML_CONV_BLOCK(0) MRML_CONV_BLOCK(1) MRML_CONV_BLOCK(2) MRML_CONV_BLOCK(3)
@@ -361,8 +236,9 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
           const uint8_t* row = src + (size_t)r * P.row_bytes;
           for (int b = 0; b < P.nb && ok; ++b) {
             if (!(ok = wait_bar(&B->conv_empty[as], aph ^ 1, B, P.err))) break;
+            if (!(ok = wait_bar(&B->dw_empty[ts], tph ^ 1, B, P.err))) break;
             uint8_t* slot = conv + as * SLOT_BYTES;
-            float* dws = reinterpret_cast<float*>(slot + A_BYTES);
+            float* dws = dwr + ts * (NA * kM);
             uint4 lo, hi;
             uint32_t d16;
             if constexpr (BB == 18) {
@@ -379,10 +255,17 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
             dws[r] = f16_bits_to_f32(d16);
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&B->conv_full[as]);
+            if (lane == 0) {
+              mbar_arrive(&B->conv_full[as]);
+              mbar_arrive(&B->dw_full[ts]);
+            }
             if (++as == P.as) {
               as = 0;
               aph ^= 1;
+            }
+            if (++ts == P.tb) {
+              ts = 0;
+              tph ^= 1;
             }
           }
         }
@@ -399,8 +282,8 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
     const int ew = warp - kEpiWarp0;
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int j0 = (ew >> 2) * TPW;  // first token column of this warp
-    int as = 0, ts = 0, bsi = 0;
-    uint32_t aph = 0, tph = 0, bph = 0;
+    int ts = 0, bsi = 0;
+    uint32_t tph = 0, bph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok && !aborted(B); u += gridDim.x) {
       const int4 U = P.units[u];
@@ -416,30 +299,74 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
         if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
         const int2* sc = reinterpret_cast<const int2*>(bsb + bsi * bs_stage + P.kcb * NT * 32);
         const int nblk = min(P.kcb, P.nb - kc * P.kcb);
-        for (int bl = 0; bl < nblk; ++bl) {
-          if (!(ok = wait_bar(&B->tmem_full[ts], tph, B, P.err))) break;
-          // The converters' scale writes are ordered before this read by the
-          // slot's full barrier (its phase cannot advance before we release it).
-          if (!(ok = wait_bar(&B->conv_full[as], aph, B, P.err))) break;
+        for (int bl = 0; bl < nblk && ok;) {
+          // Up to kG blocks per round when every token fits in the first 8
+          // columns: their TMEM loads are all issued before one wait.
+          const int g = nj <= 8 ? min(kG, nblk - bl) : 1;
+          int tsi[kG];
+          uint32_t phi[kG];
+#pragma unroll
+          for (int i = 0; i < kG; ++i) {
+            tsi[i] = ts + i;
+            phi[i] = tph;
+            if (tsi[i] >= P.tb) {
+              tsi[i] -= P.tb;
+              phi[i] ^= 1;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < kG; ++i) {
+            if (i < g && ok) ok = wait_bar(&B->tmem_full[tsi[i]], phi[i], B, P.err);
+            if (i < g && ok) ok = wait_bar(&B->dw_full[tsi[i]], phi[i], B, P.err);
+          }
+          if (!ok) break;
           fence_after();
-          const float* dws = reinterpret_cast<const float*>(conv + as * SLOT_BYTES + NA * A_BYTES);
-          const int2* scb = sc + bl * NT + j0;
+          if (nj <= 8) {
+            uint32_t v[kG][NA][8];
 #pragma unroll
-          for (int a = 0; a < NA; ++a) {
-            const float dw = dws[a * kM + 32 * q + lane];
+            for (int i = 0; i < kG; ++i)
 #pragma unroll
-            for (int c8 = 0; c8 < TPW; c8 += 8) {
-              if (c8 < nj) {
-                uint32_t v[8];
-                tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + ts * CPB + a * NT + j0 + c8, v);
-                tmem_wait_ld();
+              for (int a = 0; a < NA; ++a)
+                if (i < g) tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + tsi[i] * CPB + a * NT + j0, v[i][a]);
+            tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  if (c8 + i < nj) {
-                    const int2 s = scb[c8 + i];
-                    const float isum = __fsub_rn(__int_as_float((int)v[i] + s.y), kMagicF);
-                    const float scale = __fmul_rn(dw, __int_as_float(s.x));
-                    acc[a][c8 + i] = __fadd_rn(acc[a][c8 + i], __fmul_rn(isum, scale));
+            for (int i = 0; i < kG; ++i) {
+              if (i < g) {
+                const int2* scb = sc + (bl + i) * NT + j0;
+#pragma unroll
+                for (int a = 0; a < NA; ++a) {
+                  const float dw = dwr[tsi[i] * (NA * kM) + a * kM + 32 * q + lane];
+#pragma unroll
+                  for (int t = 0; t < 8; ++t) {
+                    if (t < nj) {
+                      const int2 s2 = scb[t];
+                      const float isum = __fsub_rn(__int_as_float((int)v[i][a][t] + s2.y), kMagicF);
+                      const float scale = __fmul_rn(dw, __int_as_float(s2.x));
+                      acc[a][t] = __fadd_rn(acc[a][t], __fmul_rn(isum, scale));
+                    }
+                  }
+                }
+              }
+            }
+          } else {
+            const int2* scb = sc + bl * NT + j0;
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              const float dw = dwr[ts * (NA * kM) + a * kM + 32 * q + lane];
+#pragma unroll
+              for (int c8 = 0; c8 < TPW; c8 += 8) {
+                if (c8 < nj) {
+                  uint32_t v[8];
+                  tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + ts * CPB + a * NT + j0 + c8, v);
+                  tmem_wait_ld();
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) {
+                    if (c8 + i < nj) {
+                      const int2 s2 = scb[c8 + i];
+                      const float isum = __fsub_rn(__int_as_float((int)v[i] + s2.y), kMagicF);
+                      const float scale = __fmul_rn(dw, __int_as_float(s2.x));
+                      acc[a][c8 + i] = __fadd_rn(acc[a][c8 + i], __fmul_rn(isum, scale));
+                    }
                   }
                 }
               }
@@ -448,17 +375,20 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
           fence_before();
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive(&B->tmem_empty[ts]);
-            mbar_arrive(&B->conv_empty[as]);
+#pragma unroll
+            for (int i = 0; i < kG; ++i) {
+              if (i < g) {
+                mbar_arrive(&B->tmem_empty[tsi[i]]);
+                mbar_arrive(&B->dw_empty[tsi[i]]);
+              }
+            }
           }
-          if (++as == P.as) {
-            as = 0;
-            aph ^= 1;
-          }
-          if (++ts == P.tb) {
-            ts = 0;
+          ts += g;
+          if (ts >= P.tb) {
+            ts -= P.tb;
             tph ^= 1;
           }
+          bl += g;
         }
         __syncwarp();
         if (ok && lane == 0) mbar_arrive(&B->bs_empty[bsi]);
@@ -547,15 +477,15 @@ EncodeTiledFn encode_fn() {
 }
 
 // 3-D map over the gate/up weights viewed as 16-bit elements:
-// {row_bytes/2, I rows, 2E parts} with a box of {8 blocks, 128 rows, 1}.
-bool make_gate_up_map(CUtensorMap* m, const uint8_t* w, int wtype, int H, int I, int E) {
+// {row_bytes/2, I rows, 2E parts} with a box of {8 blocks, box_rows rows, 1}.
+bool make_gate_up_map(CUtensorMap* m, const uint8_t* w, int wtype, int H, int I, int E, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const int bb = block_bytes(wtype);
   const cuuint64_t row_bytes = (cuuint64_t)(H / 32) * bb;
   cuuint64_t dims[3] = {row_bytes / 2, (cuuint64_t)I, (cuuint64_t)2 * E};
   cuuint64_t strides[2] = {row_bytes, row_bytes * I};
-  cuuint32_t box[3] = {(cuuint32_t)(tc::kKC * bb / 2), (cuuint32_t)tc::kM, 1};
+  cuuint32_t box[3] = {(cuuint32_t)(tc::kKC * bb / 2), (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t*>(w), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -583,16 +513,18 @@ Plan plan_for(int mode, int wtype, int NT, int nb, int rows_other, int row_bytes
   Plan p{};
   const int bb = block_bytes(wtype);
   const int na = mode == tc::kGateUp ? 2 : 1;
-  const int slot = na * (tc::kM * 32 + tc::kM * 4);
+  const int slot = na * tc::kM * 32;
   p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
   const int raw1 = mode == tc::kGateUp ? 2 * tc::kM * tc::kKC * bb : tc::kM * row_bytes;
   p.raw_bytes = (raw1 + 1023) & ~1023;
   p.tb = std::min(tc::kMaxRing, 512 / (na * NT));
+  const int dw = p.tb * na * tc::kM * 4;
   const int bs_stage = p.kcb * NT * 40;
-  for (int rs = 2; rs >= 1; --rs)
-    for (int bs = 2; bs >= 1; --bs)
-      for (int as = tc::kMaxRing; as >= 2; as /= 2) {
-        const size_t total = 2048 + (size_t)rs * p.raw_bytes + (size_t)as * slot + (size_t)bs * bs_stage;
+  // Prefer a deep raw (HBM) ring, then A-tile and B-stage depth.
+  for (int rs = tc::kMaxRaw; rs >= 1; --rs)
+    for (int bs = 4; bs >= 1; --bs)
+      for (int as = 8; as >= 2; as /= 2) {
+        const size_t total = 2048 + (size_t)rs * p.raw_bytes + (size_t)as * slot + dw + (size_t)bs * bs_stage;
         if (total <= (size_t)kSmemLimit) {
           p.rs = rs;
           p.bs = bs;
@@ -623,6 +555,14 @@ cudaError_t launch_one(const CUtensorMap& map, const tc::Params& P, size_t smem,
 }
 
 }  // namespace
+
+bool tc_map_available() { return encode_fn() != nullptr; }
+
+bool tc_make_gate_up_map(CUtensorMap* m, const uint8_t* w, int wtype, int H, int I, int E, int box_rows) {
+  return make_gate_up_map(m, w, wtype, H, I, E, box_rows);
+}
+
+int tc_num_sms() { return num_sms(); }
 
 bool tc_supported(int wtype, int H, int I, int NT) {
   const int bbw = block_bytes(wtype);
@@ -657,7 +597,7 @@ cudaError_t launch_gemm_tc(int mode, int wtype, int NT, const uint8_t* weights, 
     P.out_q = out_q;
     P.out_s = out_s;
     P.down_q4 = wtype == kQ4_0;
-    if (!make_gate_up_map(&map, weights, wtype, H, I, E)) return cudaErrorInvalidValue;
+    if (!make_gate_up_map(&map, weights, wtype, H, I, E, tc::kM)) return cudaErrorInvalidValue;
     pl = plan_for(mode, wtype, NT, P.nb, 0, P.row_bytes);
   } else {
     P.nb = I / 32;

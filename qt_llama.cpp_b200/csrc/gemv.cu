@@ -1,0 +1,422 @@
+// gemv.cu — grouped expert products on the CUDA cores for decode-size work.
+//
+// When an expert sees only a few tokens, one tcgen05.mma per 32-element
+// quant block keeps the tensor pipe busy ~160 cycles whatever the token
+// count, which caps a Q4_0 layer well below the HBM rate.  This kernel keeps
+// the same warp-specialised TMA pipeline as gemm_tc.cu but computes the
+// integer block dots with dp4a:
+//   warp 0       weight producer (TMA tensor-map tiles / 1-D bulk rows)
+//   warp 1       activation producer (B tiles and scales, bulk copies)
+//   warps 2..5   compute: thread = weight row, the unit's (up to 4) tokens in
+//                registers; gate/up units hold 64 gate rows and the matching
+//                up rows, whose sums meet in shared memory for the GeGLU
+// The per-row f32 chain sum += (float)isum_b * (d_w * d_a) runs in block
+// order, as in the reference (quant.rs:335-369 / 564-577), so the results
+// are bit-identical to the tensor-core kernel and to the reference.
+#include "common.cuh"
+#include "kernels.h"
+#include "pipe.cuh"
+
+namespace mrml {
+namespace gv {
+
+using tc::Bars;
+using tc::kDown;
+using tc::kGateUp;
+using tc::kKC;
+using tc::kM;
+using tc::Params;
+using tc::wait_bar;
+
+constexpr int kComp0 = 2;     // first compute warp
+constexpr int kCompWarps = 4;
+
+// Integer dot of one weight block (8 words of bytes: Q4_0 nibbles or Q8_0
+// values) with a token's 32 activation bytes, plus the token's correction
+// (the float-conversion magic, and -8*sum(q) for Q4_0).  Two partial chains
+// keep the dp4a dependency depth at 4.
+template <int WQ4>
+__device__ __forceinline__ float block_isum(const uint32_t (&w)[8], const uint4& alo, const uint4& ahi, int corr) {
+  int s0 = corr, s1 = 0;
+  if constexpr (WQ4) {
+    s0 = dp4a_us(w[0], alo.x, s0);
+    s1 = dp4a_us(w[1], alo.y, s1);
+    s0 = dp4a_us(w[2], alo.z, s0);
+    s1 = dp4a_us(w[3], alo.w, s1);
+    s0 = dp4a_us(w[4], ahi.x, s0);
+    s1 = dp4a_us(w[5], ahi.y, s1);
+    s0 = dp4a_us(w[6], ahi.z, s0);
+    s1 = dp4a_us(w[7], ahi.w, s1);
+  } else {
+    s0 = dp4a_ss(w[0], alo.x, s0);
+    s1 = dp4a_ss(w[1], alo.y, s1);
+    s0 = dp4a_ss(w[2], alo.z, s0);
+    s1 = dp4a_ss(w[3], alo.w, s1);
+    s0 = dp4a_ss(w[4], ahi.x, s0);
+    s1 = dp4a_ss(w[5], ahi.y, s1);
+    s0 = dp4a_ss(w[6], ahi.z, s0);
+    s1 = dp4a_ss(w[7], ahi.w, s1);
+  }
+  return __fsub_rn(__int_as_float(s0 + s1), kMagicF);  // exact: |isum| < 2^22
+}
+
+// Raw block -> 8 words in element order: Q4_0 low nibbles (elements 0..15)
+// then high nibbles (16..31); Q8_0 values as stored.
+template <int WQ4>
+__device__ __forceinline__ void block_words(const uint32_t* qs, uint32_t (&w)[8]) {
+  if constexpr (WQ4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      w[i] = qs[i] & 0x0f0f0f0fu;
+      w[4 + i] = (qs[i] >> 4) & 0x0f0f0f0fu;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = qs[i];
+  }
+}
+
+// One weight block against the unit's tokens: acc[t] += isum(t) * (dw * da(t)).
+// btile is the block's 8-position activation group (tokens start at row t0).
+template <int WQ4, int TT>
+__device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, int t0,
+                                             const int2* sc, int nj, float (&acc)[TT]) {
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
+    if (t < nj) {
+      const uint8_t* a = btile + (t0 + t) * 16;
+      const uint4 alo = *reinterpret_cast<const uint4*>(a);
+      const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
+      const int2 s2 = sc[t];
+      const float isum = block_isum<WQ4>(w, alo, ahi, s2.y);
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(isum, __fmul_rn(dw, __int_as_float(s2.x))));
+    }
+  }
+}
+
+// Unit: kGvTokens positions and, for gate/up, kGvRowsGateUp gate rows plus
+// the matching up rows (compute thread r < 64: gate row r, r >= 64: up row
+// r - 64); for down, 128 rows.  The B stage holds, per block, the 256-byte
+// group of 8 positions that contains the unit's tokens, then the tokens'
+// scales.
+template <int WQ4, int MODE>
+__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
+    moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
+  constexpr int BB = WQ4 ? 18 : 34;
+  constexpr int TT = kGvTokens;
+  constexpr int RG = kGvRowsGateUp;               // gate rows per gate/up unit
+  constexpr int GB = 256;                         // bytes of one block's activation group
+  constexpr int SB = TT * 8;                      // bytes of one block's scales
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  Bars* B = reinterpret_cast<Bars*>(smem);
+  uint8_t* raw = smem + 1024;
+  uint8_t* bsb = raw + P.rs * P.raw_bytes;
+  const int bs_stage = P.kcb * (GB + SB);
+  float* xch = reinterpret_cast<float*>(bsb + P.bs * bs_stage);  // up-row results [TT][RG]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P.rs; ++i) {
+      mbar_init(&B->raw_full[i], 1);
+      mbar_init(&B->raw_empty[i], kCompWarps);
+    }
+    for (int i = 0; i < P.bs; ++i) {
+      mbar_init(&B->bs_full[i], 1);
+      mbar_init(&B->bs_empty[i], kCompWarps);
+    }
+    B->abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int n_units = *P.n_units;
+  const int nkc = MODE == kGateUp ? P.nb / kKC : 1;
+
+  if (warp == 0) {
+    // ----------------------------------------------------- weight producer
+    if (lane == 0) {
+      int rs = 0;
+      uint32_t rph = 0;
+      for (int u = blockIdx.x; u < n_units && !tc::aborted(B); u += gridDim.x) {
+        const int4 U = P.units[u];
+        const int e = U.x, m0 = U.w;
+        for (int kc = 0; kc < nkc; ++kc) {
+          if (!wait_bar(&B->raw_empty[rs], rph ^ 1, B, P.err)) break;
+          uint8_t* dst = raw + rs * P.raw_bytes;
+          if constexpr (MODE == kGateUp) {
+            mbar_arrive_expect_tx(&B->raw_full[rs], 2 * RG * kKC * BB);
+            const int c0 = kc * kKC * BB / 2;
+            tc::tma_load_3d(dst, &tmap, c0, m0, 2 * e, &B->raw_full[rs]);
+            tc::tma_load_3d(dst + RG * kKC * BB, &tmap, c0, m0, 2 * e + 1, &B->raw_full[rs]);
+          } else {
+            const int nrows = min(kM, P.rows - m0);
+            const uint32_t bytes = (uint32_t)(nrows * P.row_bytes);
+            mbar_arrive_expect_tx(&B->raw_full[rs], bytes);
+            bulk_g2s(dst, P.w_raw + ((size_t)e * P.rows + m0) * P.row_bytes, bytes, &B->raw_full[rs]);
+          }
+          if (++rs == P.rs) {
+            rs = 0;
+            rph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------- activation producer
+    if (lane == 0) {
+      int bsi = 0;
+      uint32_t bph = 0;
+      for (int u = blockIdx.x; u < n_units && !tc::aborted(B); u += gridDim.x) {
+        const int p0 = P.units[u].y;
+        for (int kc = 0; kc < nkc; ++kc) {
+          if (!wait_bar(&B->bs_empty[bsi], bph ^ 1, B, P.err)) break;
+          uint8_t* bdst = bsb + bsi * bs_stage;
+          const int b0 = kc * P.kcb;
+          const int nblk = min(P.kcb, P.nb - b0);
+          mbar_arrive_expect_tx(&B->bs_full[bsi], (uint32_t)(nblk * (GB + SB)));
+          for (int bl = 0; bl < nblk; ++bl) {
+            const int b = b0 + bl;
+            bulk_g2s(bdst + bl * GB, P.bq + ((size_t)b * (P.npad / 8) + p0 / 8) * 256, GB, &B->bs_full[bsi]);
+            bulk_g2s(bdst + P.kcb * GB + bl * SB, P.bsc + (size_t)b * P.npad + p0, SB, &B->bs_full[bsi]);
+          }
+          if (++bsi == P.bs) {
+            bsi = 0;
+            bph ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ compute
+    const int r = threadIdx.x - 32 * kComp0;  // weight row within the tile
+    int rs = 0, bsi = 0;
+    uint32_t rph = 0, bph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < n_units && ok && !tc::aborted(B); u += gridDim.x) {
+      const int4 U = P.units[u];
+      const int p0 = U.y, nvalid = U.z, m0 = U.w;
+      const int nj = min(TT, nvalid);
+      const int t0 = p0 & 7;  // first token's row in its 8-position group
+      float acc[TT];
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+      for (int kc = 0; kc < nkc && ok; ++kc) {
+        if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
+        if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
+        const uint8_t* src = raw + rs * P.raw_bytes;
+        const uint8_t* bt = bsb + bsi * bs_stage;
+        const int2* sc = reinterpret_cast<const int2*>(bt + P.kcb * GB);
+        if constexpr (MODE == kGateUp) {
+          const uint8_t* row = src + r * (kKC * BB);  // rows 0..63 gate, 64..127 up
+#define MRML_GV_BLOCK(BL)                                                                  \
+  {                                                                                        \
+    uint32_t d16, qs[BB == 18 ? 4 : 8], w[8];                                              \
+    tc::chunk_block<BB, BL>(row, d16, qs);                                                 \
+    block_words<WQ4>(qs, w);                                                               \
+    block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + (BL) * GB, t0, sc + (BL) * TT, nj, acc); \
+  }
+          MRML_GV_BLOCK(0) MRML_GV_BLOCK(1) MRML_GV_BLOCK(2) MRML_GV_BLOCK(3)
+          MRML_GV_BLOCK(4) MRML_GV_BLOCK(5) MRML_GV_BLOCK(6) MRML_GV_BLOCK(7)
+#undef MRML_GV_BLOCK
+        } else {
+          const uint8_t* row = src + (size_t)r * P.row_bytes;
+          for (int b = 0; b < P.nb; ++b) {
+            uint32_t w[8];
+            uint32_t d16;
+            if constexpr (WQ4) {
+              const Q4Block blk = load_q4_block(row + b * 18);
+              d16 = blk.d16;
+              block_words<1>(blk.qs, w);
+            } else {
+              const Q8Block blk = load_q8_block(row + b * 34);
+              d16 = blk.d16;
+              block_words<0>(blk.qs, w);
+            }
+            block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + b * GB, t0, sc + b * TT, nj, acc);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&B->raw_empty[rs]);
+          tc::mbar_arrive(&B->bs_empty[bsi]);
+        }
+        if (++rs == P.rs) {
+          rs = 0;
+          rph ^= 1;
+        }
+        if (++bsi == P.bs) {
+          bsi = 0;
+          bph ^= 1;
+        }
+      }
+      if (!ok) break;
+      if constexpr (MODE == kGateUp) {
+        // Up rows hand their sums to the gate rows through shared memory;
+        // then act = gelu(gate) * up (ops.rs:99-114) and the down product's
+        // Q8_0 re-quantisation (quant.rs:193-228), one act block per warp.
+        const bool up = r >= RG;
+        if (up) {
+#pragma unroll
+          for (int t = 0; t < TT; ++t) xch[t * RG + (r - RG)] = acc[t];
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kCompWarps));
+        if (!up && m0 + r - lane < P.rows) {
+          const int blk = (m0 + r - lane) >> 5;
+#pragma unroll
+          for (int t = 0; t < TT; ++t) {
+            if (t < nj) {
+              const float v = __fmul_rn(gelu_approx(acc[t]), xch[t * RG + r]);
+              float amax = fabsf(v);
+              if (!(amax > 0.f)) amax = 0.f;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+              const float scale = __fdiv_rn(amax, 127.0f);
+              const uint32_t d16 = f32_to_f16_trunc(scale);
+              const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+              float rq = round_half_away(__fmul_rn(v, id));
+              if (rq != rq) rq = 0.f;
+              rq = fminf(fmaxf(rq, -128.f), 127.f);
+              const int qv = (int)rq;
+              int qsum = qv;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+              const int pos = p0 + t;
+              uint8_t* dst = reinterpret_cast<uint8_t*>(P.out_q) +
+                             ((size_t)blk * (P.npad / 8) + (pos >> 3)) * 256 + (lane >> 4) * 128 + (pos & 7) * 16 +
+                             (lane & 15);
+              *dst = (uint8_t)(int8_t)qv;
+              if (lane == 0) {
+                const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
+                P.out_s[(size_t)blk * P.npad + pos] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
+              }
+            }
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kCompWarps));
+      } else {
+        const int row = m0 + r;
+        if (row < P.rows) {
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+            if (t < nj) P.y[(size_t)(p0 + t) * P.rows + row] = acc[t];
+        }
+      }
+    }
+  }
+}
+
+}  // namespace gv
+
+// ---------------------------------------------------------------- host side
+
+namespace {
+
+constexpr int kSmemLimit = 227 * 1024;
+
+struct GvPlan {
+  int rs, bs, raw_bytes, kcb;
+  size_t smem;
+};
+
+// Two CTAs per SM when there are enough units to share the SMs, otherwise
+// one CTA with as deep a weight ring as fits (few units: each SM must keep
+// many bytes in flight on its own).
+GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
+  GvPlan p{};
+  const int bb = block_bytes(wtype);
+  p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
+  const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb : tc::kM * row_bytes;
+  p.raw_bytes = (raw1 + 1023) & ~1023;
+  const int bs_stage = p.kcb * (256 + kGvTokens * 8);
+  const int xch = kGvTokens * kGvRowsGateUp * 4;
+  const size_t budget = many_units ? (kSmemLimit / 2 - 1024) : kSmemLimit;
+  for (int rs = tc::kMaxRaw; rs >= 1; --rs)
+    for (int bs = 4; bs >= 1; --bs) {
+      if (bs > rs + 1) continue;
+      const size_t total = 2048 + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage + xch;
+      if (total <= budget) {
+        p.rs = rs;
+        p.bs = bs;
+        p.smem = total;
+        return p;
+      }
+    }
+  p.smem = 0;
+  return p;
+}
+
+template <int WQ4, int MODE>
+cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, int grid, cudaStream_t s) {
+  auto kern = gv::moe_gemv_kernel<WQ4, MODE>;
+  static int cache[16] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 16 || cache[dev] < (int)smem) {
+    cudaError_t st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (st != cudaSuccess) return st;
+    if (dev >= 0 && dev < 16) cache[dev] = (int)smem;
+  }
+  kern<<<grid, 32 * (gv::kComp0 + gv::kCompWarps), smem, s>>>(map, P);
+  return cudaPeekAtLastError();
+}
+
+}  // namespace
+
+bool gv_supported(int wtype, int H, int I) {
+  if (H % 256 != 0 || I % 32 != 0) return false;
+  const int down_row = (I / 32) * block_bytes(wtype);
+  if (I % kGvRowsGateUp != 0) return false;
+  if (gv_plan(tc::kGateUp, wtype, H / 32, 0, false).smem == 0) return false;
+  if (gv_plan(tc::kDown, wtype, I / 32, down_row, false).smem == 0) return false;
+  return tc_map_available();
+}
+
+cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
+                        const int2* bsc, const int4* units, const int* n_units, int max_units, int npad, int8_t* out_q,
+                        int2* out_s, float* y, int* err, cudaStream_t s) {
+  tc::Params P{};
+  const int bb = block_bytes(wtype);
+  P.bq = bq;
+  P.bsc = bsc;
+  P.units = units;
+  P.n_units = n_units;
+  P.npad = npad;
+  P.w_q4 = wtype == kQ4_0;
+  P.err = err;
+  CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  const int sms = tc_num_sms();
+  const bool many = max_units >= 2 * sms;
+  GvPlan pl;
+  if (mode == tc::kGateUp) {
+    P.nb = H / 32;
+    P.rows = I;
+    P.row_bytes = (H / 32) * bb;
+    P.out_q = out_q;
+    P.out_s = out_s;
+    P.down_q4 = wtype == kQ4_0;
+    if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp)) return cudaErrorInvalidValue;
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many);
+  } else {
+    P.nb = I / 32;
+    P.rows = H;
+    P.row_bytes = (I / 32) * bb;
+    P.w_raw = weights;
+    P.y = y;
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many);
+  }
+  if (pl.smem == 0) return cudaErrorInvalidValue;
+  P.rs = pl.rs;
+  P.bs = pl.bs;
+  P.raw_bytes = pl.raw_bytes;
+  P.kcb = pl.kcb;
+  const int per_sm = pl.smem <= (size_t)(kSmemLimit / 2 - 1024) ? 2 : 1;
+  const int grid = std::max(1, std::min(per_sm * sms, max_units));
+  const bool q4 = wtype == kQ4_0;
+  if (mode == tc::kGateUp)
+    return q4 ? gv_launch<1, tc::kGateUp>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kGateUp>(map, P, pl.smem, grid, s);
+  return q4 ? gv_launch<1, tc::kDown>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kDown>(map, P, pl.smem, grid, s);
+}
+
+}  // namespace mrml

@@ -1,5 +1,6 @@
 // kernels.h — host launchers of the MRML MoE kernels (internal).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -14,7 +15,7 @@ cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t*
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s);
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
-                            int mt_gu, int mt_dn, int* err, cudaStream_t s);
+                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s);
 cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,
                                     int8_t* bq, int2* bsc, cudaStream_t s);
 cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* cnt, const int32_t* poff,
@@ -23,6 +24,18 @@ cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* cnt
 cudaError_t launch_down(int wtype, const uint8_t* down, const int32_t* cnt, const int32_t* poff, const float* act,
                         float* ydown, int H, int I, int E, int* err, cudaStream_t s);
 // Tensor-core grouped products (gemm_tc.cu).  mode 0 = gate/up, 1 = down.
+bool tc_map_available();
+bool tc_make_gate_up_map(CUtensorMap* m, const uint8_t* w, int wtype, int H, int I, int E, int box_rows);
+int tc_num_sms();
+// CUDA-core pipelined products for decode-size tiles (gemv.cu): units of
+// kGvTokens positions and kGvRowsGateUp gate (and as many up) rows, or 128
+// down rows; otherwise the same arguments as launch_gemm_tc.
+constexpr int kGvTokens = 4;
+constexpr int kGvRowsGateUp = 64;
+bool gv_supported(int wtype, int H, int I);
+cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
+                        const int2* bsc, const int4* units, const int* n_units, int max_units, int npad, int8_t* out_q,
+                        int2* out_s, float* y, int* err, cudaStream_t s);
 bool tc_supported(int wtype, int H, int I, int NT);
 cudaError_t launch_gemm_tc(int mode, int wtype, int NT, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
                            const int2* bsc, const int4* units, const int* n_units, int max_units, int npad,

@@ -56,8 +56,8 @@ constexpr int kMaxNT = 64;
 // Positions after padding every expert's segment to a multiple of 16.
 int npad_alloc(int E, int K, int T) { return (((T * K + 16 * E) + 15) & ~15) + kMaxNT; }
 
-int units_bound(int E, int K, int T, int NT, int rows) {
-  return ((T * K + NT - 1) / NT + E) * ((rows + 127) / 128);
+int units_bound(int E, int K, int T, int NT, int rows, int rows_per_unit) {
+  return ((T * K + NT - 1) / NT + E) * ((rows + rows_per_unit - 1) / rows_per_unit);
 }
 
 // Workspace regions (each 256-byte aligned), in order.  Positions are the
@@ -96,8 +96,8 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
   const size_t nb = (size_t)H / 32, nbi = (size_t)I / 32, tk = (size_t)T * K;
   const int npad = npad_alloc(E, K, T);
   w.npad = npad;
-  w.max_units_gu = units_bound(E, K, T, 16, I);
-  w.max_units_dn = units_bound(E, K, T, 16, H);
+  w.max_units_gu = units_bound(E, K, T, mrml::kGvTokens, I, mrml::kGvRowsGateUp);
+  w.max_units_dn = units_bound(E, K, T, mrml::kGvTokens, H, 128);
   w.status = reinterpret_cast<int*>(take(256));
   w.xq = reinterpret_cast<int8_t*>(take((size_t)T * H));
   w.xd = reinterpret_cast<float*>(take((size_t)T * nb * 4));
@@ -188,36 +188,54 @@ int run_router(const Workspace& w, const float* W, const float* x, float* logits
   return MRML_OK;
 }
 
-// Tensor cores pay off once experts see several tokens; a single decode
-// token per expert is served better by the finer-grained CUDA-core kernels.
-bool use_tensor_cores(int wtype, int H, int I, int E, int K, int T, int NT) {
-  if (g_path == 1) return false;
-  const bool ok = mrml::tc_supported(wtype, H, I, NT);
-  if (g_path == 2) return ok;
-  return ok && (long long)T * K >= 2ll * E;
+// Expert-product kernels.  The tensor cores pay off once experts see many
+// tokens (prefill); at decode sizes one MMA per quant block wastes most of
+// each MMA, and the pipelined dp4a kernel is faster.  Shapes outside both
+// kernels' limits (H not a multiple of 256) use the general dp4a kernels.
+enum Route { kRouteGeneral = 0, kRouteGemv = 1, kRouteTensor = 2 };
+
+Route pick_route(int wtype, int H, int I, int E, int K, int T) {
+  const bool tc = mrml::tc_supported(wtype, H, I, 64) && mrml::tc_supported(wtype, H, I, 16);
+  const bool gv = mrml::gv_supported(wtype, H, I);
+  switch (g_path) {
+    case 1: return gv ? kRouteGemv : kRouteGeneral;
+    case 2: return tc ? kRouteTensor : (gv ? kRouteGemv : kRouteGeneral);
+    case 3: return kRouteGeneral;
+    default: break;
+  }
+  if (tc && (long long)T * K > 16ll * E) return kRouteTensor;
+  return gv ? kRouteGemv : kRouteGeneral;
 }
 
 int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids,
                 const float* probs, const float* down_scale, const float* x, float* out, int H, int I, int E, int K,
                 int T, cudaStream_t s) {
-  const int NT = (long long)T * K > 12ll * E ? 64 : 16;
-  const bool tc = use_tensor_cores(wtype, H, I, E, K, T, NT);
-  const int mt_gu = (I + 127) / 128, mt_dn = (H + 127) / 128;
+  const Route route = pick_route(wtype, H, I, E, K, T);
+  const int NT = route == kRouteGemv ? mrml::kGvTokens : ((long long)T * K > 12ll * E ? 64 : 16);
+  const int rows_gu = route == kRouteGemv ? mrml::kGvRowsGateUp : 128;
+  const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;
   int* n_units = w.status + 2;
   MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
-                                    n_units, NT, mt_gu, mt_dn, w.status, s));
-  if (tc) {
-    const int mu_gu = units_bound(E, K, T, NT, I), mu_dn = units_bound(E, K, T, NT, H);
-    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, w.xb, w.xs, s));
-    MRML_LAUNCH(mrml::launch_gemm_tc(0, wtype, NT, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad,
-                                     w.ab, w.as, nullptr, w.status, s));
-    MRML_LAUNCH(mrml::launch_gemm_tc(1, wtype, NT, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
-                                     nullptr, nullptr, w.ydown, w.status, s));
-  } else {
+                                    n_units, NT, mt_gu, rows_gu, mt_dn, w.status, s));
+  if (route == kRouteGeneral) {
     MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
     MRML_LAUNCH(mrml::launch_gate_up(wtype, gate_up, w.cnt, w.poff, w.pair_at, w.xq, w.xd, w.xsum, w.act, H, I, E, K,
                                      w.status, s));
     MRML_LAUNCH(mrml::launch_down(wtype, down, w.cnt, w.poff, w.act, w.ydown, H, I, E, w.status, s));
+  } else {
+    const int mu_gu = units_bound(E, K, T, NT, I, rows_gu), mu_dn = units_bound(E, K, T, NT, H, 128);
+    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, w.xb, w.xs, s));
+    if (route == kRouteTensor) {
+      MRML_LAUNCH(mrml::launch_gemm_tc(0, wtype, NT, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu,
+                                       w.npad, w.ab, w.as, nullptr, w.status, s));
+      MRML_LAUNCH(mrml::launch_gemm_tc(1, wtype, NT, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn,
+                                       w.npad, nullptr, nullptr, w.ydown, w.status, s));
+    } else {
+      MRML_LAUNCH(mrml::launch_gemv(0, wtype, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad, w.ab,
+                                    w.as, nullptr, w.status, s));
+      MRML_LAUNCH(mrml::launch_gemv(1, wtype, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
+                                    nullptr, nullptr, w.ydown, w.status, s));
+    }
   }
   MRML_LAUNCH(mrml::launch_combine(w.ydown, w.pos, ids, probs, down_scale, out, H, K, T, s));
   return MRML_OK;
@@ -317,7 +335,7 @@ int mrml_moe_quantize_q4_0(const float* src, uint8_t* dst, size_t n, mrml_stream
 
 int mrml_moe_set_option(int option, int value) {
   if (option == MRML_OPTION_EXPERT_PATH) {
-    if (value < 0 || value > 2) return MRML_ERR_INVALID_ARGUMENT;
+    if (value < 0 || value > 3) return MRML_ERR_INVALID_ARGUMENT;
     g_path = value;
     return MRML_OK;
   }

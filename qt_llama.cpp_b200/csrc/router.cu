@@ -37,21 +37,33 @@ __host__ __device__ inline int chunk_len(int H) { return (H + 31) / 32; }
 __host__ __device__ inline int chunk_pitch(int H) { return chunk_len(H) | 1; }
 
 // Copies `rows` rows of length H (row stride H) into the chunked layout.
-// The chunk index and offset of element i advance incrementally.
+// Each thread loads a batch of elements into registers before storing them,
+// so that the global loads of a batch are in flight together; the chunk
+// index and offset of element i advance incrementally.
 __device__ __forceinline__ void stage_chunked(float* dst, const float* __restrict__ src, int rows, int H) {
+  constexpr int kBatch = 16;
   const int C = chunk_len(H), pitch = chunk_pitch(H), row_floats = 32 * pitch;
   const int step = blockDim.x, dq = step / C, dr = step % C;
   for (int r = 0; r < rows; ++r) {
     const float* s = src + (size_t)r * H;
     float* d = dst + r * row_floats;
     int q = threadIdx.x / C, rem = threadIdx.x % C;
-    for (int i = threadIdx.x; i < H; i += step) {
-      d[q * pitch + rem] = s[i];
-      q += dq;
-      rem += dr;
-      if (rem >= C) {
-        rem -= C;
-        ++q;
+    for (int i0 = threadIdx.x; i0 < H; i0 += step * kBatch) {
+      float v[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int i = i0 + k * step;
+        v[k] = i < H ? s[i] : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        if (i0 + k * step < H) d[q * pitch + rem] = v[k];
+        q += dq;
+        rem += dr;
+        if (rem >= C) {
+          rem -= C;
+          ++q;
+        }
       }
     }
   }

@@ -158,11 +158,12 @@ def quantize(wtype, src, dst, stream=None):
 
 
 OPTION_EXPERT_PATH = 1
-PATH_AUTO, PATH_DP4A, PATH_TENSOR = 0, 1, 2
+PATH_AUTO, PATH_GEMV, PATH_TENSOR, PATH_GENERAL = 0, 1, 2, 3
 
 
 def set_expert_path(path: int) -> None:
-    """0 automatic, 1 CUDA-core dp4a, 2 tcgen05 tensor cores (process-wide)."""
+    """0 automatic, 1 pipelined CUDA-core kernels, 2 tcgen05 tensor cores,
+    3 general CUDA-core kernels (process-wide)."""
     _check("mrml_moe_set_option", load_library().mrml_moe_set_option(OPTION_EXPERT_PATH, path))
 
 

@@ -17,13 +17,14 @@ pytestmark = pytest.mark.gpu
 MAX_ABS_FRAC = 1e-3
 REL_L2 = 1e-4
 
-PATHS = {"dp4a": 1, "tensor": 2}
+PATHS = {"general": 3, "gemv": 1, "tensor": 2}
 
 
 @pytest.fixture(params=sorted(PATHS))
 def expert_path(request, cuda, moe):
-    """Run the test once on each expert-product path (CUDA-core dp4a and the
-    tcgen05 tensor-core kernels); restores automatic selection after."""
+    """Run the test once on each expert-product path (the general CUDA-core
+    kernels, the pipelined CUDA-core kernels and the tcgen05 tensor-core
+    kernels); restores automatic selection after."""
     moe.set_expert_path(PATHS[request.param])
     yield request.param
     moe.set_expert_path(0)
@@ -395,8 +396,8 @@ def test_reference_surface_mirror(cuda, moe, oracle, synth):
 
 @pytest.mark.parametrize("wtype,T", [(2, 64), (8, 200), (2, 1)])
 def test_paths_bit_identical(cuda, moe, synth, c2_q4, wtype, T):
-    """The tensor-core and CUDA-core paths keep the same per-block order of
-    f32 operations, so their outputs agree bit for bit."""
+    """The three expert-product paths keep the same per-block order of f32
+    operations, so their outputs agree bit for bit."""
     H, I, E, K = 2816, 704, 128, 8
     if wtype == 2:
         gu, dn = c2_q4
@@ -406,11 +407,11 @@ def test_paths_bit_identical(cuda, moe, synth, c2_q4, wtype, T):
     W = synth.normal(50, E * H, 0.02).reshape(E, H)
     x = synth.normal(51 + T, T * H).reshape(T, H)
     L = Layer(moe, cuda, wtype, gu, dn, W, H, I, E, K, T)
+    outs = []
     try:
-        moe.set_expert_path(1)
-        _, _, a, _ = L.forward(x)
-        moe.set_expert_path(2)
-        _, _, b, _ = L.forward(x)
+        for path in (3, 1, 2):
+            moe.set_expert_path(path)
+            outs.append(L.forward(x)[2])
     finally:
         moe.set_expert_path(0)
-    assert np.array_equal(a, b)
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
