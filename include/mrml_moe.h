@@ -84,6 +84,25 @@ int mrml_moe_workspace_init(void *workspace, size_t workspace_bytes, mrml_stream
 int mrml_moe_router(const float *W, const float *x, float *logits, int32_t *ids, float *probs, int H, int E, int K,
                     int T, void *workspace, size_t workspace_bytes, mrml_stream_t stream);
 
+/* mrml_moe_router for callers that cannot allocate device memory.  No
+ * counterpart in the reference (its router always had a device buffer set
+ * up by the caller).  Some callers can only use buffers they were given:
+ * a sandboxed or mediated GPU client that may launch work but not create
+ * allocations, code that must not allocate on its latency path, or code
+ * recording into a CUDA graph, where cudaMalloc cannot be captured.  This
+ * entry point keeps the router's scratch (its per-token, per-expert error
+ * bounds) in a fixed device array inside the library, so it allocates
+ * nothing and needs no workspace argument; results equal mrml_moe_router's.
+ * Limit: T * E <= 65536, otherwise MRML_ERR_UNSUPPORTED.  The array (about
+ * 256 KiB) is held on every GPU that loads the library until the process
+ * exits.  The first call on a device looks up the array's device address;
+ * make that first call before any stream capture.  All calls on a device
+ * share the array (each call clears its counters first), so calls whose
+ * kernels can overlap on the GPU, such as calls on unordered streams, race;
+ * calls ordered on one stream are fine. */
+int mrml_moe_router_noalloc(const float *W, const float *x, float *logits, int32_t *ids, float *probs, int H, int E,
+                            int K, int T, mrml_stream_t stream);
+
 /* Top-K and softmax from caller-supplied logits[T][E] (model.rs:1816-1829).
  * Needs no workspace. */
 int mrml_moe_route_from_logits(const float *logits, int32_t *ids, float *probs, int E, int K, int T,

@@ -40,6 +40,7 @@ SIGNATURES = {
     "mrml_moe_workspace_init": (_i, [_vp, _sz, _vp]),
     "mrml_moe_router": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "mrml_moe_route_from_logits": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "mrml_moe_router_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mrml_moe_experts": (
         _i,
         [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp],
@@ -120,6 +121,17 @@ def router(W, x, logits, ids, probs, H, E, K, T, ws, stream=None):
         "mrml_moe_router",
         lib.mrml_moe_router(_ptr(W), _ptr(x), _ptr(logits), _ptr(ids), _ptr(probs), H, E, K, T, _ptr(ws),
                             ws.numel(), _stream_ptr(stream)),
+    )
+
+
+def router_noalloc(W, x, logits, ids, probs, H, E, K, T, stream=None):
+    """The router without a workspace (scratch kept inside the library); for
+    callers that cannot allocate device memory.  T * E must be <= 65536."""
+    lib = load_library()
+    _check(
+        "mrml_moe_router_noalloc",
+        lib.mrml_moe_router_noalloc(_ptr(W), _ptr(x), _ptr(logits), _ptr(ids), _ptr(probs), H, E, K, T,
+                                    _stream_ptr(stream)),
     )
 
 
