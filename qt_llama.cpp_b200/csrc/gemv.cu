@@ -7,9 +7,9 @@
 // integer block dots with dp4a:
 //   warp 0       weight producer (TMA tensor-map tiles / 1-D bulk rows)
 //   warp 1       activation producer (B tiles and scales, bulk copies)
-//   warps 2..5   compute: thread = weight row, the unit's (up to 4) tokens in
-//                registers; gate/up units hold 64 gate rows and the matching
-//                up rows, whose sums meet in shared memory for the GeGLU
+//   warps 2..3   compute: thread = two weight rows that share activations
+//                (a gate row and its up row, or two down rows), the unit's
+//                (up to 8) tokens in registers
 // The per-row f32 chain sum += (float)isum_b * (d_w * d_a) runs in block
 // order, as in the reference (quant.rs:335-369 / 564-577), so the results
 // are bit-identical to the tensor-core kernel and to the reference.
@@ -29,14 +29,14 @@ using tc::Params;
 using tc::wait_bar;
 
 constexpr int kComp0 = 2;     // first compute warp
-constexpr int kCompWarps = 4;
+constexpr int kCompWarps = 2;  // 64 threads, two weight rows each
 
-// Integer dot of one weight block (8 words of bytes: Q4_0 nibbles or Q8_0
-// values) with a token's 32 activation bytes, plus the token's correction
-// (the float-conversion magic, and -8*sum(q) for Q4_0).  Two partial chains
-// keep the dp4a dependency depth at 4.
+// Integer dot of one weight block (8 words: Q4_0 nibbles or Q8_0 values in
+// element order) with a token's 32 activation bytes, as the bits of the float
+// 1.5*2^23 + isum: the correction word carries the magic (and, for Q4_0, the
+// -8 * sum(q) nibble offset).  Two partial chains halve the dp4a depth.
 template <int WQ4>
-__device__ __forceinline__ float block_isum(const uint32_t (&w)[8], const uint4& alo, const uint4& ahi, int corr) {
+__device__ __forceinline__ int block_isum_bits(const uint32_t (&w)[8], const uint4& alo, const uint4& ahi, int corr) {
   int s0 = corr, s1 = 0;
   if constexpr (WQ4) {
     s0 = dp4a_us(w[0], alo.x, s0);
@@ -57,7 +57,7 @@ __device__ __forceinline__ float block_isum(const uint32_t (&w)[8], const uint4&
     s0 = dp4a_ss(w[6], ahi.z, s0);
     s1 = dp4a_ss(w[7], ahi.w, s1);
   }
-  return __fsub_rn(__int_as_float(s0 + s1), kMagicF);  // exact: |isum| < 2^22
+  return s0 + s1;
 }
 
 // Raw block -> 8 words in element order: Q4_0 low nibbles (elements 0..15)
@@ -76,37 +76,44 @@ __device__ __forceinline__ void block_words(const uint32_t* qs, uint32_t (&w)[8]
   }
 }
 
-// One weight block against the unit's tokens: acc[t] += isum(t) * (dw * da(t)).
-// btile is the block's 8-position activation group (tokens start at row t0).
+// One quant block of two weight rows (A, B) against the unit's tokens:
+//   acc_X[t] += isum_X(t) * (d_X * d_a(t))     for X in {A, B}
+// in the reference's rounding order (scalar round-to-nearest operations; a
+// packed f32x2 version of this sequence did not reproduce the scalar bits).
+// btile: the block's 8-position activation group; sc: the tokens'
+// {d_a, correction}.
 template <int WQ4, int TT>
-__device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, int t0,
-                                             const int2* sc, int nj, float (&acc)[TT]) {
+__device__ __forceinline__ void block_pair_tokens(const uint32_t (&wa)[8], const uint32_t (&wb)[8], float dwa,
+                                                  float dwb, const uint8_t* btile, const int2* sc, int nj,
+                                                  float (&acc_a)[TT], float (&acc_b)[TT]) {
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
     if (t < nj) {
-      const uint8_t* a = btile + (t0 + t) * 16;
+      const uint8_t* a = btile + t * 16;
       const uint4 alo = *reinterpret_cast<const uint4*>(a);
       const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
       const int2 s2 = sc[t];
-      const float isum = block_isum<WQ4>(w, alo, ahi, s2.y);
-      acc[t] = __fadd_rn(acc[t], __fmul_rn(isum, __fmul_rn(dw, __int_as_float(s2.x))));
+      const float da = __int_as_float(s2.x);
+      const float fa = __fsub_rn(__int_as_float(block_isum_bits<WQ4>(wa, alo, ahi, s2.y)), kMagicF);  // exact
+      const float fb = __fsub_rn(__int_as_float(block_isum_bits<WQ4>(wb, alo, ahi, s2.y)), kMagicF);
+      acc_a[t] = __fadd_rn(acc_a[t], __fmul_rn(fa, __fmul_rn(dwa, da)));
+      acc_b[t] = __fadd_rn(acc_b[t], __fmul_rn(fb, __fmul_rn(dwb, da)));
     }
   }
 }
 
-// Unit: kGvTokens positions and, for gate/up, kGvRowsGateUp gate rows plus
-// the matching up rows (compute thread r < 64: gate row r, r >= 64: up row
-// r - 64); for down, 128 rows.  The B stage holds, per block, the 256-byte
-// group of 8 positions that contains the unit's tokens, then the tokens'
-// scales.
+// Unit: kGvTokens (8) positions and 64 row pairs: for gate/up, gate row r and
+// up row r (r < 64); for down, rows r and r + 64 of a 128-row tile.  Thread r
+// of the compute group owns pair r.  The B stage holds, per block, the
+// 256-byte group of the unit's 8 positions, then the tokens' scales.
 template <int WQ4, int MODE>
-__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
+__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 4)
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   constexpr int BB = WQ4 ? 18 : 34;
   constexpr int TT = kGvTokens;
-  constexpr int RG = kGvRowsGateUp;               // gate rows per gate/up unit
-  constexpr int GB = 256;                         // bytes of one block's activation group
-  constexpr int SB = TT * 8;                      // bytes of one block's scales
+  constexpr int RG = kGvRowsGateUp;  // row pairs per unit
+  constexpr int GB = 256;            // bytes of one block's activation group
+  constexpr int SB = TT * 8;         // bytes of one block's scales
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -114,7 +121,6 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
   uint8_t* raw = smem + 1024;
   uint8_t* bsb = raw + P.rs * P.raw_bytes;
   const int bs_stage = P.kcb * (GB + SB);
-  float* xch = reinterpret_cast<float*>(bsb + P.bs * bs_stage);  // up-row results [TT][RG]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -150,7 +156,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
             tc::tma_load_3d(dst, &tmap, c0, m0, 2 * e, &B->raw_full[rs]);
             tc::tma_load_3d(dst + RG * kKC * BB, &tmap, c0, m0, 2 * e + 1, &B->raw_full[rs]);
           } else {
-            const int nrows = min(kM, P.rows - m0);
+            const int nrows = min(2 * RG, P.rows - m0);
             const uint32_t bytes = (uint32_t)(nrows * P.row_bytes);
             mbar_arrive_expect_tx(&B->raw_full[rs], bytes);
             bulk_g2s(dst, P.w_raw + ((size_t)e * P.rows + m0) * P.row_bytes, bytes, &B->raw_full[rs]);
@@ -189,7 +195,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
     }
   } else {
     // ------------------------------------------------------------ compute
-    const int r = threadIdx.x - 32 * kComp0;  // weight row within the tile
+    const int r = threadIdx.x - 32 * kComp0;  // row pair within the tile
     int rs = 0, bsi = 0;
     uint32_t rph = 0, bph = 0;
     bool ok = true;
@@ -197,10 +203,9 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
       const int4 U = P.units[u];
       const int p0 = U.y, nvalid = U.z, m0 = U.w;
       const int nj = min(TT, nvalid);
-      const int t0 = p0 & 7;  // first token's row in its 8-position group
-      float acc[TT];
+      float acc_a[TT], acc_b[TT];
 #pragma unroll
-      for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+      for (int t = 0; t < TT; ++t) acc_a[t] = acc_b[t] = 0.f;
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
         if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
@@ -208,32 +213,44 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
         const uint8_t* bt = bsb + bsi * bs_stage;
         const int2* sc = reinterpret_cast<const int2*>(bt + P.kcb * GB);
         if constexpr (MODE == kGateUp) {
-          const uint8_t* row = src + r * (kKC * BB);  // rows 0..63 gate, 64..127 up
-#define MRML_GV_BLOCK(BL)                                                                  \
-  {                                                                                        \
-    uint32_t d16, qs[BB == 18 ? 4 : 8], w[8];                                              \
-    tc::chunk_block<BB, BL>(row, d16, qs);                                                 \
-    block_words<WQ4>(qs, w);                                                               \
-    block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + (BL) * GB, t0, sc + (BL) * TT, nj, acc); \
+          const uint8_t* rowa = src + r * (kKC * BB);                 // gate row r
+          const uint8_t* rowb = src + (RG + r) * (kKC * BB);          // up row r
+#define MRML_GV_BLOCK(BL)                                                                        \
+  {                                                                                              \
+    uint32_t da16, db16, qa[BB == 18 ? 4 : 8], qb[BB == 18 ? 4 : 8], wa[8], wb[8];               \
+    tc::chunk_block<BB, BL>(rowa, da16, qa);                                                     \
+    tc::chunk_block<BB, BL>(rowb, db16, qb);                                                     \
+    block_words<WQ4>(qa, wa);                                                                    \
+    block_words<WQ4>(qb, wb);                                                                    \
+    block_pair_tokens<WQ4, TT>(wa, wb, f16_bits_to_f32(da16), f16_bits_to_f32(db16),             \
+                               bt + (BL) * GB, sc + (BL) * TT, nj, acc_a, acc_b);                \
   }
           MRML_GV_BLOCK(0) MRML_GV_BLOCK(1) MRML_GV_BLOCK(2) MRML_GV_BLOCK(3)
           MRML_GV_BLOCK(4) MRML_GV_BLOCK(5) MRML_GV_BLOCK(6) MRML_GV_BLOCK(7)
 #undef MRML_GV_BLOCK
         } else {
-          const uint8_t* row = src + (size_t)r * P.row_bytes;
+          const uint8_t* rowa = src + (size_t)r * P.row_bytes;
+          const uint8_t* rowb = src + (size_t)(RG + r) * P.row_bytes;
           for (int b = 0; b < P.nb; ++b) {
-            uint32_t w[8];
-            uint32_t d16;
+            uint32_t wa[8], wb[8];
+            uint32_t da16, db16;
             if constexpr (WQ4) {
-              const Q4Block blk = load_q4_block(row + b * 18);
-              d16 = blk.d16;
-              block_words<1>(blk.qs, w);
+              const Q4Block qa = load_q4_block(rowa + b * 18);
+              const Q4Block qb = load_q4_block(rowb + b * 18);
+              da16 = qa.d16;
+              db16 = qb.d16;
+              block_words<1>(qa.qs, wa);
+              block_words<1>(qb.qs, wb);
             } else {
-              const Q8Block blk = load_q8_block(row + b * 34);
-              d16 = blk.d16;
-              block_words<0>(blk.qs, w);
+              const Q8Block qa = load_q8_block(rowa + b * 34);
+              const Q8Block qb = load_q8_block(rowb + b * 34);
+              da16 = qa.d16;
+              db16 = qb.d16;
+              block_words<0>(qa.qs, wa);
+              block_words<0>(qb.qs, wb);
             }
-            block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + b * GB, t0, sc + b * TT, nj, acc);
+            block_pair_tokens<WQ4, TT>(wa, wb, f16_bits_to_f32(da16), f16_bits_to_f32(db16), bt + b * GB,
+                                       sc + b * TT, nj, acc_a, acc_b);
           }
         }
         __syncwarp();
@@ -252,21 +269,15 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
       }
       if (!ok) break;
       if constexpr (MODE == kGateUp) {
-        // Up rows hand their sums to the gate rows through shared memory;
-        // then act = gelu(gate) * up (ops.rs:99-114) and the down product's
-        // Q8_0 re-quantisation (quant.rs:193-228), one act block per warp.
-        const bool up = r >= RG;
-        if (up) {
-#pragma unroll
-          for (int t = 0; t < TT; ++t) xch[t * RG + (r - RG)] = acc[t];
-        }
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * kCompWarps));
-        if (!up && m0 + r - lane < P.rows) {
+        // act = gelu(gate) * up (ops.rs:99-114), then the down product's
+        // Q8_0 re-quantisation (quant.rs:193-228): a warp's 32 lanes hold the
+        // 32 elements of one act block.
+        if (m0 + r - lane < P.rows) {
           const int blk = (m0 + r - lane) >> 5;
 #pragma unroll
           for (int t = 0; t < TT; ++t) {
             if (t < nj) {
-              const float v = __fmul_rn(gelu_approx(acc[t]), xch[t * RG + r]);
+              const float v = __fmul_rn(gelu_approx(acc_a[t]), acc_b[t]);
               float amax = fabsf(v);
               if (!(amax > 0.f)) amax = 0.f;
 #pragma unroll
@@ -293,13 +304,14 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps))
             }
           }
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * kCompWarps));
       } else {
-        const int row = m0 + r;
-        if (row < P.rows) {
+        const int ra = m0 + r, rb = m0 + RG + r;
 #pragma unroll
-          for (int t = 0; t < TT; ++t)
-            if (t < nj) P.y[(size_t)(p0 + t) * P.rows + row] = acc[t];
+        for (int t = 0; t < TT; ++t) {
+          if (t < nj) {
+            if (ra < P.rows) P.y[(size_t)(p0 + t) * P.rows + ra] = acc_a[t];
+            if (rb < P.rows) P.y[(size_t)(p0 + t) * P.rows + rb] = acc_b[t];
+          }
         }
       }
     }
@@ -315,7 +327,7 @@ namespace {
 constexpr int kSmemLimit = 227 * 1024;
 
 struct GvPlan {
-  int rs, bs, raw_bytes, kcb;
+  int rs, bs, raw_bytes, kcb, per_sm;
   size_t smem;
 };
 
@@ -326,22 +338,27 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
   GvPlan p{};
   const int bb = block_bytes(wtype);
   p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
-  const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb : tc::kM * row_bytes;
+  const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb : 2 * kGvRowsGateUp * row_bytes;
   p.raw_bytes = (raw1 + 1023) & ~1023;
   const int bs_stage = p.kcb * (256 + kGvTokens * 8);
-  const int xch = kGvTokens * kGvRowsGateUp * 4;
-  const size_t budget = many_units ? (kSmemLimit / 2 - 1024) : kSmemLimit;
-  for (int rs = tc::kMaxRaw; rs >= 1; --rs)
-    for (int bs = 4; bs >= 1; --bs) {
-      if (bs > rs + 1) continue;
-      const size_t total = 2048 + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage + xch;
-      if (total <= budget) {
-        p.rs = rs;
-        p.bs = bs;
-        p.smem = total;
-        return p;
+  // With many units, as many CTAs per SM as fit with a double-buffered weight
+  // ring (4 at most); with few units, one CTA and the deepest ring that fits.
+  const int per_sm_max = many_units ? 4 : 1;
+  for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
+    const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
+    const int rs_min = per_sm > 1 ? 2 : 1;
+    for (int rs = tc::kMaxRaw; rs >= rs_min; --rs)
+      for (int bs = 2; bs >= 1; --bs) {
+        const size_t total = 2048 + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage;
+        if (total <= budget) {
+          p.rs = rs;
+          p.bs = bs;
+          p.smem = total;
+          p.per_sm = per_sm;
+          return p;
+        }
       }
-    }
+  }
   p.smem = 0;
   return p;
 }
@@ -411,8 +428,7 @@ cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int 
   P.bs = pl.bs;
   P.raw_bytes = pl.raw_bytes;
   P.kcb = pl.kcb;
-  const int per_sm = pl.smem <= (size_t)(kSmemLimit / 2 - 1024) ? 2 : 1;
-  const int grid = std::max(1, std::min(per_sm * sms, max_units));
+  const int grid = std::max(1, std::min(pl.per_sm * sms, max_units));
   const bool q4 = wtype == kQ4_0;
   if (mode == tc::kGateUp)
     return q4 ? gv_launch<1, tc::kGateUp>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kGateUp>(map, P, pl.smem, grid, s);

@@ -7,7 +7,7 @@
 namespace mrml {
 
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, float* bounds, int H, int E, int T,
-                                 cudaStream_t s);
+                                 int* err, cudaStream_t s);
 cudaError_t launch_router_topk(const float* W, const float* x, float* logits, const float* bounds, int32_t* ids,
                                float* probs, int H, int E, int K, int T, int* stats, cudaStream_t s);
 cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
@@ -28,9 +28,10 @@ bool tc_map_available();
 bool tc_make_gate_up_map(CUtensorMap* m, const uint8_t* w, int wtype, int H, int I, int E, int box_rows);
 int tc_num_sms();
 // CUDA-core pipelined products for decode-size tiles (gemv.cu): units of
-// kGvTokens positions and kGvRowsGateUp gate (and as many up) rows, or 128
-// down rows; otherwise the same arguments as launch_gemm_tc.
-constexpr int kGvTokens = 4;
+// kGvTokens positions and kGvRowsGateUp gate (and as many up) rows, or
+// 2 * kGvRowsGateUp down rows; otherwise the same arguments as
+// launch_gemm_tc.
+constexpr int kGvTokens = 8;
 constexpr int kGvRowsGateUp = 64;
 bool gv_supported(int wtype, int H, int I);
 cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int I, int E, const int8_t* bq,

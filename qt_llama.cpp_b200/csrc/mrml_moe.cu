@@ -183,7 +183,7 @@ int check_workspace(void* ws, size_t ws_bytes, int H, int I, int E, int K, int T
 
 int run_router(const Workspace& w, const float* W, const float* x, float* logits, int32_t* ids, float* probs, int H,
                int E, int K, int T, cudaStream_t s) {
-  MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, w.bounds, H, E, T, s));
+  MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, w.bounds, H, E, T, w.status, s));
   MRML_LAUNCH(mrml::launch_router_topk(W, x, logits, w.bounds, ids, probs, H, E, K, T, w.status + 1, s));
   return MRML_OK;
 }
@@ -213,7 +213,7 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
   const Route route = pick_route(wtype, H, I, E, K, T);
   const int NT = route == kRouteGemv ? mrml::kGvTokens : ((long long)T * K > 12ll * E ? 64 : 16);
   const int rows_gu = route == kRouteGemv ? mrml::kGvRowsGateUp : 128;
-  const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;
+  const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;  // down tiles: 128 rows on both paths
   int* n_units = w.status + 2;
   MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
                                     n_units, NT, mt_gu, rows_gu, mt_dn, w.status, s));

@@ -69,25 +69,58 @@ __device__ __forceinline__ void stage_chunked(float* dst, const float* __restric
   }
 }
 
+// Bulk-copy layout: when H % 128 == 0 (chunks of C = H/32 floats, a multiple
+// of 4) each lane's chunk is copied by the TMA engine to a pitch of
+// P4 = C rounded up to 4 (mod 32): 16-byte aligned, and the 8 lanes of a
+// quarter-warp reading float4s at the same chunk offset hit 8 different
+// 16-byte bank groups.
+__host__ __device__ inline int chunk_pitch4(int H) {
+  const int C = chunk_len(H);
+  int p = (C + 3) & ~3;
+  while ((p & 31) != 4) p += 4;
+  return p;
+}
+
 // grid (ceil(E / epc), ceil(T / tpc)), block 32*kRouterWarps.  The CTA
-// stages tpc token rows of x and epc expert rows of W in shared memory
-// (coalesced global reads), then one warp per (token, expert) pair computes
-// the logit and its error bound.  Writes logits[t*E + e] and bounds[t*E + e].
+// stages tpc token rows of x and epc expert rows of W in shared memory (bulk
+// copies when `bulk`, else coalesced loads), then one warp per (token,
+// expert) pair computes the logit and its error bound.  Writes
+// logits[t*E + e] and bounds[t*E + e].
 __global__ void __launch_bounds__(32 * kRouterWarps)
     router_logits_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
-                         float* __restrict__ bounds, int H, int E, int T, int epc, int tpc) {
-  extern __shared__ float rsm[];
-  const int C = chunk_len(H), pitch = chunk_pitch(H);
+                         float* __restrict__ bounds, int H, int E, int T, int epc, int tpc, int bulk,
+                         int* __restrict__ err) {
+  extern __shared__ __align__(16) float rsm[];
+  __shared__ __align__(8) uint64_t bar;
+  const int C = chunk_len(H);
+  const int pitch = bulk ? chunk_pitch4(H) : chunk_pitch(H);
   const int row_floats = 32 * pitch;
   const int e0 = blockIdx.x * epc, t0 = blockIdx.y * tpc;
   const int ne = min(epc, E - e0), nt = min(tpc, T - t0);
   float* xs = rsm;                     // [tpc][row_floats]
   float* ws = rsm + tpc * row_floats;  // [epc][row_floats]
-  stage_chunked(xs, x + (size_t)t0 * H, nt, H);
-  stage_chunked(ws, W + (size_t)e0 * H, ne, H);
-  __syncthreads();
-
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    if (warp == 0) {
+      if (lane == 0) mbar_arrive_expect_tx(&bar, (uint32_t)((nt + ne) * H * 4));
+      __syncwarp();
+      for (int r = 0; r < nt; ++r)
+        bulk_g2s(xs + r * row_floats + lane * pitch, x + (size_t)(t0 + r) * H + lane * C, C * 4, &bar);
+      for (int r = 0; r < ne; ++r)
+        bulk_g2s(ws + r * row_floats + lane * pitch, W + (size_t)(e0 + r) * H + lane * C, C * 4, &bar);
+    }
+    if (!mbar_wait_bounded(&bar, 0, err)) return;
+  } else {
+    stage_chunked(xs, x + (size_t)t0 * H, nt, H);
+    stage_chunked(ws, W + (size_t)e0 * H, ne, H);
+    __syncthreads();
+  }
+
   const int start = lane * C;
   const int len = max(0, min(C, H - start));
   const float u = 5.9604644775390625e-8f;  // 2^-24
@@ -96,12 +129,30 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
     const float* xl = xs + tl * row_floats + lane * pitch;
     const float* wl = ws + el * row_floats + lane * pitch;
     float r = 0.f, A = 0.f, P = 0.f;
+    if (bulk) {
+      for (int j = 0; j < len; j += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(xl + j);
+        const float4 b = *reinterpret_cast<const float4*>(wl + j);
+        const float p0 = __fmul_rn(a.x, b.x), p1 = __fmul_rn(a.y, b.y);
+        const float p2 = __fmul_rn(a.z, b.z), p3 = __fmul_rn(a.w, b.w);
+        r = __fadd_rn(r, p0);
+        A += fabsf(r);
+        r = __fadd_rn(r, p1);
+        A += fabsf(r);
+        r = __fadd_rn(r, p2);
+        A += fabsf(r);
+        r = __fadd_rn(r, p3);
+        A += fabsf(r);
+        P += (fabsf(p0) + fabsf(p1)) + (fabsf(p2) + fabsf(p3));
+      }
+    } else {
 #pragma unroll 4
-    for (int j = 0; j < len; ++j) {
-      const float prod = __fmul_rn(xl[j], wl[j]);
-      r = __fadd_rn(r, prod);
-      A += fabsf(r);
-      P += fabsf(prod);
+      for (int j = 0; j < len; ++j) {
+        const float prod = __fmul_rn(xl[j], wl[j]);
+        r = __fadd_rn(r, prod);
+        A += fabsf(r);
+        P += fabsf(prod);
+      }
     }
     // Exclusive prefix of the chunk sums, in double.
     double incl = (double)r;
@@ -125,6 +176,8 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
       const float center = (float)total;
       const float n = (float)H;
       const float gamma = n * u / (1.f - n * u);
+      // The bound's own f32 sums carry relative errors of at most n*u; the
+      // 1.01 factors cover them.
       float B = u * (2.f * p_part + s_part + a_part) * 1.01f + n * gamma * u * p_part * 1.01f;
       // Slack for rounding the center to f32 and for the f32 comparisons of
       // c - B against c' + B' made by the top-k kernel.
@@ -409,15 +462,17 @@ cudaError_t ensure_smem(Kern k, size_t bytes, int* cache) {
 }
 
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, float* bounds, int H, int E, int T,
-                                 cudaStream_t s) {
+                                 int* err, cudaStream_t s) {
   static int cache[16] = {0};
   const int epc = T <= 4 ? 1 : 4;
   const int tpc = T <= 4 ? T : 8;
   const dim3 grid((E + epc - 1) / epc, (T + tpc - 1) / tpc);
-  const size_t smem = (size_t)(epc + tpc) * 32 * chunk_pitch(H) * sizeof(float);
+  const bool bulk = H % 128 == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
+  const size_t smem = (size_t)(epc + tpc) * 32 * (bulk ? chunk_pitch4(H) : chunk_pitch(H)) * sizeof(float);
   cudaError_t st = ensure_smem(router_logits_kernel, smem, cache);
   if (st != cudaSuccess) return st;
-  router_logits_kernel<<<grid, 32 * kRouterWarps, smem, s>>>(W, x, logits, bounds, H, E, T, epc, tpc);
+  router_logits_kernel<<<grid, 32 * kRouterWarps, smem, s>>>(W, x, logits, bounds, H, E, T, epc, tpc, bulk ? 1 : 0,
+                                                             err);
   return cudaPeekAtLastError();
 }
 
