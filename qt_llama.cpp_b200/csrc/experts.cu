@@ -144,20 +144,53 @@ __global__ void __launch_bounds__(kDispatchThreads)
     }
   }
   __syncthreads();
-  if (tid == 0) {
-    int run = 0, units = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = cnt[e];
-      poff[e] = run;
-      base[e] = run;
-      ubase[e] = units;
-      cnt_out[e] = c;
-      run += (c + 15) & ~15;
-      units += (c + NT - 1) / NT;
+  // Exclusive scans of the padded counts and of the unit counts, one warp
+  // per 32 experts, then across warps (E <= 1024).
+  {
+    __shared__ int wsum_pos[32], wsum_units[32];
+    const int e = tid;
+    const int c = e < E ? cnt[e] : 0;
+    const int pad = (c + 15) & ~15, nun = (c + NT - 1) / NT;
+    int ip = pad, iu = nun;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int vp = __shfl_up_sync(0xffffffffu, ip, o), vu = __shfl_up_sync(0xffffffffu, iu, o);
+      if (lane >= o) {
+        ip += vp;
+        iu += vu;
+      }
     }
-    poff[E] = run;
-    n_units[0] = units * mt_gu;
-    n_units[1] = units * mt_dn;
+    if (lane == 31) {
+      wsum_pos[warp] = ip;
+      wsum_units[warp] = iu;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int vp = wsum_pos[lane], vu = wsum_units[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, vp, o), b = __shfl_up_sync(0xffffffffu, vu, o);
+        if (lane >= o) {
+          vp += a;
+          vu += b;
+        }
+      }
+      wsum_pos[lane] = vp;  // inclusive per warp
+      wsum_units[lane] = vu;
+    }
+    __syncthreads();
+    const int bp = warp ? wsum_pos[warp - 1] : 0, bu = warp ? wsum_units[warp - 1] : 0;
+    if (e < E) {
+      poff[e] = bp + ip - pad;
+      base[e] = bp + ip - pad;
+      ubase[e] = bu + iu - nun;
+      cnt_out[e] = c;
+    }
+    if (e == E - 1) {
+      poff[E] = bp + ip;
+      n_units[0] = (bu + iu) * mt_gu;
+      n_units[1] = (bu + iu) * mt_dn;
+    }
   }
   __syncthreads();
   const int npos = poff[E];

@@ -184,7 +184,7 @@ int check_workspace(void* ws, size_t ws_bytes, int H, int I, int E, int K, int T
 int run_router(const Workspace& w, const float* W, const float* x, float* logits, int32_t* ids, float* probs, int H,
                int E, int K, int T, cudaStream_t s) {
   MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, w.bounds, H, E, T, w.status, s));
-  MRML_LAUNCH(mrml::launch_router_topk(W, x, logits, w.bounds, ids, probs, H, E, K, T, w.status + 1, s));
+  MRML_LAUNCH(mrml::launch_router_topk(W, x, logits, w.bounds, ids, probs, H, E, K, T, w.status, s));
   return MRML_OK;
 }
 

@@ -69,23 +69,15 @@ __device__ __forceinline__ void stage_chunked(float* dst, const float* __restric
   }
 }
 
-// Bulk-copy layout: when H % 128 == 0 (chunks of C = H/32 floats, a multiple
-// of 4) each lane's chunk is copied by the TMA engine to a pitch of
-// P4 = C rounded up to 4 (mod 32): 16-byte aligned, and the 8 lanes of a
-// quarter-warp reading float4s at the same chunk offset hit 8 different
-// 16-byte bank groups.
-__host__ __device__ inline int chunk_pitch4(int H) {
-  const int C = chunk_len(H);
-  int p = (C + 3) & ~3;
-  while ((p & 31) != 4) p += 4;
-  return p;
-}
-
 // grid (ceil(E / epc), ceil(T / tpc)), block 32*kRouterWarps.  The CTA
-// stages tpc token rows of x and epc expert rows of W in shared memory (bulk
-// copies when `bulk`, else coalesced loads), then one warp per (token,
-// expert) pair computes the logit and its error bound.  Writes
-// logits[t*E + e] and bounds[t*E + e].
+// stages tpc token rows of x and epc expert rows of W in shared memory,
+// then one warp per (token, expert) pair computes the logit and its error
+// bound; lane l owns the contiguous chunk [l*C, l*C + C) of the row.
+// With `bulk` (H % 128 == 0, 16-byte aligned rows) each row arrives by one
+// bulk copy into a dense layout (row pitch H) and lanes read float4s: the
+// 8 lanes of a quarter-warp then hit at most 2 requests per bank group.
+// Otherwise rows are staged by coalesced loads into a padded chunk layout.
+// Writes logits[t*E + e] and bounds[t*E + e].
 __global__ void __launch_bounds__(32 * kRouterWarps)
     router_logits_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
                          float* __restrict__ bounds, int H, int E, int T, int epc, int tpc, int bulk,
@@ -93,8 +85,8 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
   extern __shared__ __align__(16) float rsm[];
   __shared__ __align__(8) uint64_t bar;
   const int C = chunk_len(H);
-  const int pitch = bulk ? chunk_pitch4(H) : chunk_pitch(H);
-  const int row_floats = 32 * pitch;
+  const int pitch = bulk ? C : chunk_pitch(H);  // lane chunk stride
+  const int row_floats = bulk ? H : 32 * pitch;
   const int e0 = blockIdx.x * epc, t0 = blockIdx.y * tpc;
   const int ne = min(epc, E - e0), nt = min(tpc, T - t0);
   float* xs = rsm;                     // [tpc][row_floats]
@@ -106,13 +98,10 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
       fence_barrier_init();
     }
     __syncthreads();
-    if (warp == 0) {
-      if (lane == 0) mbar_arrive_expect_tx(&bar, (uint32_t)((nt + ne) * H * 4));
-      __syncwarp();
-      for (int r = 0; r < nt; ++r)
-        bulk_g2s(xs + r * row_floats + lane * pitch, x + (size_t)(t0 + r) * H + lane * C, C * 4, &bar);
-      for (int r = 0; r < ne; ++r)
-        bulk_g2s(ws + r * row_floats + lane * pitch, W + (size_t)(e0 + r) * H + lane * C, C * 4, &bar);
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&bar, (uint32_t)((nt + ne) * H * 4));
+      for (int r = 0; r < nt; ++r) bulk_g2s(xs + r * row_floats, x + (size_t)(t0 + r) * H, H * 4, &bar);
+      for (int r = 0; r < ne; ++r) bulk_g2s(ws + r * row_floats, W + (size_t)(e0 + r) * H, H * 4, &bar);
     }
     if (!mbar_wait_bounded(&bar, 0, err)) return;
   } else {
@@ -302,13 +291,15 @@ __device__ void finish_token(int* cand, float* cval, int count, int K, int t, in
 // bounds == nullptr: the logits are exact inputs (route-from-logits).
 // Otherwise W and x are the router weights and inputs the logits came from,
 // and the dynamic shared memory (router_exact_smem(H) bytes) stages the rows
-// of the exact fallback.  stats[0] counts tokens that needed it.
+// of the exact fallback.  status[0] is the device status word, status[1]
+// counts tokens that needed the fallback (status may be null without bounds).
 template <int PL>
 __global__ void __launch_bounds__(32 * kTopkWarps)
     router_topk_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
                        const float* __restrict__ bounds, int32_t* __restrict__ ids, float* __restrict__ probs, int H,
-                       int E, int K, int T, int* __restrict__ stats) {
+                       int E, int K, int T, int* __restrict__ status) {
   __shared__ TopkShared S;
+  int* stats = status ? status + 1 : nullptr;
   extern __shared__ __align__(16) float stage[];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int t = blockIdx.x * kTopkWarps + wl;
@@ -389,12 +380,21 @@ __global__ void __launch_bounds__(32 * kTopkWarps)
   if (n_pending == 0) return;
   if (threadIdx.x == 0 && stats) atomicAdd(stats, n_pending);
 
-  // Exact fallback, one pending token at a time: the whole CTA stages the
-  // token's x row and up to kExactRows flagged W rows, and one thread per
-  // row runs the reference's sequential chain.
+  // Exact fallback, one pending token at a time: the CTA stages the token's
+  // x row and up to kExactRows flagged W rows (bulk copies when rows are
+  // 16-byte multiples, else coalesced loads), and one thread per row runs
+  // the reference's sequential chain.
   const int pitch = (H + 3) & ~3;
   float* xs = stage;
   float* wsr = stage + pitch;
+  __shared__ __align__(8) uint64_t xbar;
+  const bool bulk = (H & 3) == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
+  uint32_t xph = 0;
+  if (threadIdx.x == 0) {
+    mbar_init(&xbar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
   for (int q = 0; q < n_pending; ++q) {
     const int w = S.pending[q];
     const int tq = blockIdx.x * kTopkWarps + w;
@@ -405,17 +405,36 @@ __global__ void __launch_bounds__(32 * kTopkWarps)
     float* qv = S.cval[w];
     int* qf = S.flag[w];
     const int n_items = all ? E : count;
-    __syncthreads();
-    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[(size_t)tq * H + i];
     for (int base = 0; base < n_items; base += kExactRows) {
       __syncthreads();
-      for (int r = 0; r < kExactRows; ++r) {
-        const int item = base + r;
-        if (item >= n_items || !(all || qf[item])) continue;
-        const float* wrow = W + (size_t)(all ? item : qc[item]) * H;
-        for (int i = threadIdx.x; i < H; i += blockDim.x) wsr[r * pitch + i] = wrow[i];
+      if (bulk) {
+        if (threadIdx.x == 0) {
+          int nrows = 0;
+          for (int r = 0; r < kExactRows; ++r) {
+            const int item = base + r;
+            if (item < n_items && (all || qf[item])) ++nrows;
+          }
+          mbar_arrive_expect_tx(&xbar, (uint32_t)((base == 0 ? 1 + nrows : nrows) * H * 4));
+          if (base == 0) bulk_g2s(xs, x + (size_t)tq * H, H * 4, &xbar);
+          for (int r = 0; r < kExactRows; ++r) {
+            const int item = base + r;
+            if (item >= n_items || !(all || qf[item])) continue;
+            bulk_g2s(wsr + r * pitch, W + (size_t)(all ? item : qc[item]) * H, H * 4, &xbar);
+          }
+        }
+        if (!mbar_wait_bounded(&xbar, xph, status)) return;
+        xph ^= 1;
+      } else {
+        if (base == 0)
+          for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[(size_t)tq * H + i];
+        for (int r = 0; r < kExactRows; ++r) {
+          const int item = base + r;
+          if (item >= n_items || !(all || qf[item])) continue;
+          const float* wrow = W + (size_t)(all ? item : qc[item]) * H;
+          for (int i = threadIdx.x; i < H; i += blockDim.x) wsr[r * pitch + i] = wrow[i];
+        }
+        __syncthreads();
       }
-      __syncthreads();
       if (threadIdx.x < kExactRows) {
         const int item = base + threadIdx.x;
         if (item < n_items && (all || qf[item])) {
@@ -465,10 +484,10 @@ cudaError_t launch_router_logits(const float* W, const float* x, float* logits, 
                                  int* err, cudaStream_t s) {
   static int cache[16] = {0};
   const int epc = T <= 4 ? 1 : 4;
-  const int tpc = T <= 4 ? T : 8;
+  const int tpc = T <= 4 ? T : 4;
   const dim3 grid((E + epc - 1) / epc, (T + tpc - 1) / tpc);
   const bool bulk = H % 128 == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
-  const size_t smem = (size_t)(epc + tpc) * 32 * (bulk ? chunk_pitch4(H) : chunk_pitch(H)) * sizeof(float);
+  const size_t smem = (size_t)(epc + tpc) * (bulk ? (size_t)H : (size_t)32 * chunk_pitch(H)) * sizeof(float);
   cudaError_t st = ensure_smem(router_logits_kernel, smem, cache);
   if (st != cudaSuccess) return st;
   router_logits_kernel<<<grid, 32 * kRouterWarps, smem, s>>>(W, x, logits, bounds, H, E, T, epc, tpc, bulk ? 1 : 0,
@@ -479,7 +498,7 @@ cudaError_t launch_router_logits(const float* W, const float* x, float* logits, 
 size_t router_exact_smem(int H) { return (size_t)((H + 3) & ~3) * (1 + kExactRows) * sizeof(float); }
 
 cudaError_t launch_router_topk(const float* W, const float* x, float* logits, const float* bounds, int32_t* ids,
-                               float* probs, int H, int E, int K, int T, int* stats, cudaStream_t s) {
+                               float* probs, int H, int E, int K, int T, int* status, cudaStream_t s) {
   static int cache[3][16] = {{0}};
   const dim3 grid((T + kTopkWarps - 1) / kTopkWarps);
   const int block = 32 * kTopkWarps;
@@ -487,13 +506,13 @@ cudaError_t launch_router_topk(const float* W, const float* x, float* logits, co
   cudaError_t st;
   if (E <= 32) {
     if ((st = ensure_smem(router_topk_kernel<1>, smem, cache[0])) != cudaSuccess) return st;
-    router_topk_kernel<1><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
+    router_topk_kernel<1><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, status);
   } else if (E <= 128) {
     if ((st = ensure_smem(router_topk_kernel<4>, smem, cache[1])) != cudaSuccess) return st;
-    router_topk_kernel<4><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
+    router_topk_kernel<4><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, status);
   } else {
     if ((st = ensure_smem(router_topk_kernel<8>, smem, cache[2])) != cudaSuccess) return st;
-    router_topk_kernel<8><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, stats);
+    router_topk_kernel<8><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, status);
   }
   return cudaPeekAtLastError();
 }

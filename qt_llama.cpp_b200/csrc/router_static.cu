@@ -70,7 +70,7 @@ extern "C" int mrml_moe_router_noalloc(const float* W, const float* x, float* lo
   // The counter words keep the previous call's values: clear them.
   if (cudaMemsetAsync(status, 0, kStatusFloats * sizeof(float), s) != cudaSuccess) return MRML_ERR_CUDA;
   if (mrml::launch_router_logits(W, x, logits, bounds, H, E, T, status, s) != cudaSuccess) return MRML_ERR_CUDA;
-  if (mrml::launch_router_topk(W, x, logits, bounds, ids, probs, H, E, K, T, status + 1, s) != cudaSuccess)
+  if (mrml::launch_router_topk(W, x, logits, bounds, ids, probs, H, E, K, T, status, s) != cudaSuccess)
     return MRML_ERR_CUDA;
   return MRML_OK;
 }
