@@ -140,6 +140,9 @@ int mrml_moe_quantize_q4_0(const float *src, uint8_t *dst, size_t n, mrml_stream
  * multiple of 256).  All paths give bit-identical results; the option exists
  * for tests and benchmarks. */
 enum { MRML_OPTION_EXPERT_PATH = 1 };
+/* Tuning of the decode (CUDA-core) expert kernel: CTAs per SM (1..8) and
+ * the depth of its weight ring (1..8); 0 restores the automatic choice. */
+enum { MRML_OPTION_DECODE_CTAS_PER_SM = 2, MRML_OPTION_DECODE_RING = 3 };
 int mrml_moe_set_option(int option, int value);
 
 /* Profiling hook for benchmarks.  With n_events > 0, the following calls on

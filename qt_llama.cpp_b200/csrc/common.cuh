@@ -203,4 +203,19 @@ __device__ __forceinline__ Q8Block load_q8_block(const uint8_t* p) {
 
 __host__ __device__ constexpr int block_bytes(int wtype) { return wtype == kQ4_0 ? 18 : 34; }
 
+// Activation operand layouts (quantised Q8_0 rows by position).  Positions
+// come in groups of 8; a group's block b is 256 bytes: two 16-byte halves
+// (elements 0..15 at +0, 16..31 at +128) of 8 positions (16 bytes apart),
+// the canonical no-swizzle K-major core matrices of a tcgen05 B operand.
+//  - block-major (tensor cores): group g of block b at (b * npad/8 + g) * 256,
+//    so a block's token tile is contiguous; scales at [b * npad + pos].
+//  - group-major (decode kernel): at (g * nb + b) * 256, so a group's
+//    consecutive blocks are contiguous; scales at [(g * nb + b) * 8 + pos % 8].
+__host__ __device__ inline size_t act_group_offset(bool group_major, int b, int g, int nb, int npad) {
+  return group_major ? ((size_t)g * nb + b) * 256 : ((size_t)b * (npad / 8) + g) * 256;
+}
+__host__ __device__ inline size_t act_scale_index(bool group_major, int b, int pos, int nb, int npad) {
+  return group_major ? ((size_t)(pos >> 3) * nb + b) * 8 + (pos & 7) : (size_t)b * npad + pos;
+}
+
 }  // namespace mrml

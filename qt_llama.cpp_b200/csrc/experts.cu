@@ -247,7 +247,8 @@ __global__ void __launch_bounds__(kDispatchThreads)
 // bsc[b][pos].  One warp per (token, block), lane = element.
 template <int WQ4>
 __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32_t* __restrict__ pos, int T, int H,
-                                        int K, int npad, int8_t* __restrict__ bq, int2* __restrict__ bsc) {
+                                        int K, int npad, int group_major, int8_t* __restrict__ bq,
+                                        int2* __restrict__ bsc) {
   const int nb = H / 32;
   const long long total = (long long)T * nb;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
@@ -273,10 +274,10 @@ __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32
     for (int k = 0; k < K; ++k) {
       const int p = pos[t * K + k];
       if (p < 0) continue;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + ((size_t)b * (npad / 8) + (p >> 3)) * 256 + (lane >> 4) * 128 +
-                     (p & 7) * 16 + (lane & 15);
+      uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + act_group_offset(group_major, b, p >> 3, nb, npad) +
+                     (lane >> 4) * 128 + (p & 7) * 16 + (lane & 15);
       *dst = (uint8_t)(int8_t)q;
-      if (lane == 0) bsc[(size_t)b * npad + p] = sc;
+      if (lane == 0) bsc[act_scale_index(group_major, b, p, nb, npad)] = sc;
     }
   }
 }
@@ -583,12 +584,13 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
 }
 
 cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,
-                                    int8_t* bq, int2* bsc, cudaStream_t s) {
+                                    bool group_major, int8_t* bq, int2* bsc, cudaStream_t s) {
   const long long warps = (long long)T * (H / 32);
+  const int gm = group_major ? 1 : 0;
   if (wtype == kQ4_0)
-    quantize_scatter_kernel<1><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, bq, bsc);
+    quantize_scatter_kernel<1><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, gm, bq, bsc);
   else
-    quantize_scatter_kernel<0><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, bq, bsc);
+    quantize_scatter_kernel<0><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, gm, bq, bsc);
   return cudaPeekAtLastError();
 }
 

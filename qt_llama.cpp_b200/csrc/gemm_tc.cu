@@ -425,12 +425,12 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
               for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
               const int pos = p0 + j0 + j;
               uint8_t* dst = reinterpret_cast<uint8_t*>(P.out_q) +
-                             ((size_t)blk * (P.npad / 8) + (pos >> 3)) * 256 + (lane >> 4) * 128 + (pos & 7) * 16 +
+                             act_group_offset(false, blk, pos >> 3, 0, P.npad) + (lane >> 4) * 128 + (pos & 7) * 16 +
                              (lane & 15);
               *dst = (uint8_t)(int8_t)qv;
               if (lane == 0) {
                 const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
-                P.out_s[(size_t)blk * P.npad + pos] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
+                P.out_s[act_scale_index(false, blk, pos, 0, P.npad)] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
               }
             }
           }

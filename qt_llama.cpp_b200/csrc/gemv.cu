@@ -104,10 +104,11 @@ __device__ __forceinline__ void block_pair_tokens(const uint32_t (&wa)[8], const
 
 // Unit: kGvTokens (8) positions and 64 row pairs: for gate/up, gate row r and
 // up row r (r < 64); for down, rows r and r + 64 of a 128-row tile.  Thread r
-// of the compute group owns pair r.  The B stage holds, per block, the
-// 256-byte group of the unit's 8 positions, then the tokens' scales.
+// of the compute group owns pair r.  Activations use the group-major layout
+// (common.cuh): a B stage is the unit's position group for the chunk's
+// blocks (256 bytes each, contiguous), then their scales (64 bytes each).
 template <int WQ4, int MODE>
-__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 4)
+__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   constexpr int BB = WQ4 ? 18 : 34;
   constexpr int TT = kGvTokens;
@@ -181,11 +182,12 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 4)
           const int b0 = kc * P.kcb;
           const int nblk = min(P.kcb, P.nb - b0);
           mbar_arrive_expect_tx(&B->bs_full[bsi], (uint32_t)(nblk * (GB + SB)));
-          for (int bl = 0; bl < nblk; ++bl) {
-            const int b = b0 + bl;
-            bulk_g2s(bdst + bl * GB, P.bq + ((size_t)b * (P.npad / 8) + p0 / 8) * 256, GB, &B->bs_full[bsi]);
-            bulk_g2s(bdst + P.kcb * GB + bl * SB, P.bsc + (size_t)b * P.npad + p0, SB, &B->bs_full[bsi]);
-          }
+          // Group-major layout: the unit's blocks b0 .. b0+nblk-1 are
+          // contiguous, for the activations and for their scales.
+          const int g = p0 >> 3;
+          bulk_g2s(bdst, P.bq + act_group_offset(true, b0, g, P.nb, P.npad), nblk * GB, &B->bs_full[bsi]);
+          bulk_g2s(bdst + P.kcb * GB, P.bsc + act_scale_index(true, b0, p0, P.nb, P.npad), nblk * SB,
+                   &B->bs_full[bsi]);
           if (++bsi == P.bs) {
             bsi = 0;
             bph ^= 1;
@@ -294,12 +296,12 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 4)
               for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
               const int pos = p0 + t;
               uint8_t* dst = reinterpret_cast<uint8_t*>(P.out_q) +
-                             ((size_t)blk * (P.npad / 8) + (pos >> 3)) * 256 + (lane >> 4) * 128 + (pos & 7) * 16 +
+                             act_group_offset(true, blk, pos >> 3, P.out_nb, P.npad) + (lane >> 4) * 128 + (pos & 7) * 16 +
                              (lane & 15);
               *dst = (uint8_t)(int8_t)qv;
               if (lane == 0) {
                 const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
-                P.out_s[(size_t)blk * P.npad + pos] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
+                P.out_s[act_scale_index(true, blk, pos, P.out_nb, P.npad)] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
               }
             }
           }
@@ -334,6 +336,10 @@ struct GvPlan {
 // Two CTAs per SM when there are enough units to share the SMs, otherwise
 // one CTA with as deep a weight ring as fits (few units: each SM must keep
 // many bytes in flight on its own).
+// Tuning overrides (mrml_moe_set_option): CTAs per SM and weight-ring depth
+// of the decode kernel; 0 = automatic.
+int g_gv_per_sm = 0, g_gv_ring = 0;
+
 GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
   GvPlan p{};
   const int bb = block_bytes(wtype);
@@ -343,11 +349,14 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
   const int bs_stage = p.kcb * (256 + kGvTokens * 8);
   // With many units, as many CTAs per SM as fit with a double-buffered weight
   // ring (4 at most); with few units, one CTA and the deepest ring that fits.
-  const int per_sm_max = many_units ? 4 : 1;
+  const int per_sm_max = g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? 5 : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
     const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
-    const int rs_min = per_sm > 1 ? 2 : 1;
-    for (int rs = tc::kMaxRaw; rs >= rs_min; --rs)
+    // Down tiles hold a whole K (one stage per unit); several CTAs per SM
+    // overlap one another's loads, so a single stage each is allowed there.
+    const int rs_min = (per_sm > 1 && mode == tc::kGateUp) ? 2 : 1;
+    const int rs_max = g_gv_ring > 0 ? g_gv_ring : tc::kMaxRaw;
+    for (int rs = rs_max; rs >= rs_min; --rs)
       for (int bs = 2; bs >= 1; --bs) {
         const size_t total = 2048 + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage;
         if (total <= budget) {
@@ -379,6 +388,11 @@ cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, 
 }
 
 }  // namespace
+
+void gv_set_tuning(int per_sm, int ring) {
+  g_gv_per_sm = per_sm;
+  g_gv_ring = ring;
+}
 
 bool gv_supported(int wtype, int H, int I) {
   if (H % 256 != 0 || I % 32 != 0) return false;
@@ -412,6 +426,7 @@ cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int 
     P.row_bytes = (H / 32) * bb;
     P.out_q = out_q;
     P.out_s = out_s;
+    P.out_nb = I / 32;
     P.down_q4 = wtype == kQ4_0;
     if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp)) return cudaErrorInvalidValue;
     pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many);

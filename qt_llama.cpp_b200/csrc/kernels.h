@@ -17,7 +17,7 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
                             int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s);
 cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,
-                                    int8_t* bq, int2* bsc, cudaStream_t s);
+                                    bool group_major, int8_t* bq, int2* bsc, cudaStream_t s);
 cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* cnt, const int32_t* poff,
                            const int32_t* sorted, const int8_t* xq, const float* xd, const int32_t* xsum, float* act,
                            int H, int I, int E, int K, int* err, cudaStream_t s);
@@ -34,6 +34,7 @@ int tc_num_sms();
 constexpr int kGvTokens = 8;
 constexpr int kGvRowsGateUp = 64;
 bool gv_supported(int wtype, int H, int I);
+void gv_set_tuning(int per_sm, int ring);
 cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
                         const int2* bsc, const int4* units, const int* n_units, int max_units, int npad, int8_t* out_q,
                         int2* out_s, float* y, int* err, cudaStream_t s);

@@ -224,7 +224,7 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
     MRML_LAUNCH(mrml::launch_down(wtype, down, w.cnt, w.poff, w.act, w.ydown, H, I, E, w.status, s));
   } else {
     const int mu_gu = units_bound(E, K, T, NT, I, rows_gu), mu_dn = units_bound(E, K, T, NT, H, 128);
-    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, w.xb, w.xs, s));
+    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, route == kRouteGemv, w.xb, w.xs, s));
     if (route == kRouteTensor) {
       MRML_LAUNCH(mrml::launch_gemm_tc(0, wtype, NT, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu,
                                        w.npad, w.ab, w.as, nullptr, w.status, s));
@@ -334,12 +334,25 @@ int mrml_moe_quantize_q4_0(const float* src, uint8_t* dst, size_t n, mrml_stream
 }
 
 int mrml_moe_set_option(int option, int value) {
-  if (option == MRML_OPTION_EXPERT_PATH) {
-    if (value < 0 || value > 3) return MRML_ERR_INVALID_ARGUMENT;
-    g_path = value;
-    return MRML_OK;
+  static int gv_per_sm = 0, gv_ring = 0;
+  switch (option) {
+    case MRML_OPTION_EXPERT_PATH:
+      if (value < 0 || value > 3) return MRML_ERR_INVALID_ARGUMENT;
+      g_path = value;
+      return MRML_OK;
+    case MRML_OPTION_DECODE_CTAS_PER_SM:
+      if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
+      gv_per_sm = value;
+      mrml::gv_set_tuning(gv_per_sm, gv_ring);
+      return MRML_OK;
+    case MRML_OPTION_DECODE_RING:
+      if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
+      gv_ring = value;
+      mrml::gv_set_tuning(gv_per_sm, gv_ring);
+      return MRML_OK;
+    default:
+      return MRML_ERR_INVALID_ARGUMENT;
   }
-  return MRML_ERR_INVALID_ARGUMENT;
 }
 
 int mrml_moe_profile_events(void** events, int n_events) {

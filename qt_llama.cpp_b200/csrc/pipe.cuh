@@ -35,6 +35,7 @@ struct Params {
   int8_t* out_q;
   int2* out_s;
   int down_q4;           // the down weights' type (selects the act correction)
+  int out_nb;            // quant blocks per act row (I / 32), group-major act layout
   // down output
   float* y;              // [npad_alloc][H]
   int* err;
