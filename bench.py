@@ -19,8 +19,12 @@ experts from HBM.  `value` is tokens/s with inputs resident in HBM; `e2e`
 adds, every step, the host->device copy of x from pinned memory and the
 device->host copy of the layer output.
 
-With --gpus N > 1 every rank runs its own replica of the layer on its own
-tokens (weak scaling; no collective on the data path).
+With --gpus N > 1 (torchrun, one rank per GPU, NCCL) the layer runs expert-
+parallel: rank r holds experts [r*E/N, (r+1)*E/N) and 64 home tokens (weak
+scaling: N*64 tokens per step); a step routes the home tokens, all-gathers
+them, runs the rank's experts on every rank's tokens and reduce-scatters the
+partial outputs (qt_llama.cpp_b200/ep.py).  Workload "c4" is config 4:
+8192 tokens per step in total (strong scaling).
 
 --impl reference times the reference's CPU algorithm (the C restatement
 under oracle/, the reference's Rust cannot be built here) on the host cores.
@@ -61,13 +65,18 @@ def package():
 
 
 WORKLOADS = {
-    # name: (wtype, H, I, E, K, T, routing)
+    # name: (wtype, H, I, E, K, T, routing); T is per rank, except for the
+    # STRONG workloads, whose T is the whole job's (T / N home tokens per rank).
     "c2_t64": (2, 2816, 704, 128, 8, 64, "router"),
     "c2_t8": (2, 2816, 704, 128, 8, 8, "router"),
     "c2_t1": (2, 2816, 704, 128, 8, 1, "router"),
     "c3_prefill": (8, 1024, 512, 16, 2, 2048, "zipf_logits"),
     "c1_t4": (8, 1024, 512, 16, 2, 4, "router"),
+    "c4": (2, 2816, 704, 128, 8, 8192, "router"),
+    "c4_q8": (8, 2816, 704, 128, 8, 8192, "router"),
 }
+STRONG = {"c4", "c4_q8"}
+METRIC = "MoE-layer tokens/sec at decode batch 1/64 and 2048-token prefill; % of roofline"
 KERNELS = {
     "router": ["router_logits", "router_topk", "dispatch", "quantize", "gate_up", "down", "combine"],
     "zipf_logits": ["route_from_logits", "dispatch", "quantize", "gate_up", "down", "combine"],
@@ -85,27 +94,58 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    every few milliseconds (the timed regions are short), else nvidia-smi."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits, in the order of FIELDS[2:].
+    NVML_BITS = (0x8, 0x40, 0x20, 0x4)
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.samples = []
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(gpu_index).uuid)
+                h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            self._nvml = (pynvml, h)
+        except Exception:
+            self._nvml = None
+
+    def _sample_nvml(self):
+        nv, h = self._nvml
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        try:
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        except Exception:
+            bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+        return [str(sm), str(mx)] + ["Active" if bits & b else "Not Active" for b in self.NVML_BITS]
 
     def _run(self):
         while not self._stop.is_set():
             try:
+                if self._nvml is not None:
+                    self.samples.append(self._sample_nvml())
+                    self._stop.wait(0.005)
+                    continue
                 out = subprocess.run(
                     ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.gpu)],
                     capture_output=True, text=True, timeout=5).stdout.strip()
                 if out:
                     self.samples.append([v.strip() for v in out.split(",")])
             except Exception:
-                pass
+                self._nvml = None
             self._stop.wait(0.1)
 
     def __enter__(self):
@@ -125,7 +165,8 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 2 + i and s[2 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+                "reasons": reasons, "samples": len(self.samples),
+                "source": "nvml" if self._nvml is not None else "nvidia-smi"}
 
 
 class LayerSet:
@@ -203,6 +244,10 @@ class LayerSet:
     def n_kernels(self):
         return len(KERNELS[self.routing])
 
+    @property
+    def router_ws(self):
+        return self.ws
+
     def unique_experts(self, i):
         """Experts hit (with alpha > 1e-4) by step i's routing, and the pair count."""
         self.step(i)
@@ -210,6 +255,81 @@ class LayerSet:
         probs = self.probs.cpu().numpy()
         hit = ids[probs > 1e-4]
         return len(np.unique(hit)), int(hit.size)
+
+
+class EPLayerSet:
+    """The expert-parallel layer on this rank: every layer copy holds the
+    rank's E/N experts and the replicated router; a step routes the rank's
+    home tokens, all-gathers them, runs the rank's experts on every rank's
+    tokens and reduce-scatters the partial outputs (qt_llama.cpp_b200/ep.py).
+    Same interface as LayerSet."""
+
+    def __init__(self, moe, synth, device, name, n_inputs, rank, world, seed=0):
+        import torch
+
+        ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
+        wtype, H, I, E, K, T, routing = WORKLOADS[name]
+        assert routing == "router", "expert parallelism runs the router workloads"
+        if name in STRONG:
+            T //= world
+        self.moe, self.device, self.name = moe, device, name
+        self.wtype, self.H, self.I, self.E, self.K, self.T, self.routing = wtype, H, I, E, K, T, routing
+        self.world, self.rank = world, rank
+        self.ep = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, device)
+        first, count = self.ep.first, self.ep.count
+        bb = 18 if wtype == 2 else 34
+        layer_bytes = count * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
+        self.n_layers = max(2, -(-4 * L2_BYTES // layer_bytes))
+        self.layers = []
+        for l in range(self.n_layers):
+            # Every rank generates the whole layer with the same seed and keeps
+            # its experts, so that the job computes one well-defined layer.
+            gu, dn = synth.expert_weights_device(seed * 100 + l + 1, wtype, H, I, E, device, moe.quantize)
+            gu, dn = gu[first:first + count].clone(), dn[first:first + count].clone()
+            torch.cuda.empty_cache()
+            g = torch.Generator(device=device)
+            g.manual_seed(seed * 100 + l + 1000)
+            W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
+            self.layers.append((gu, dn, W))
+        g = torch.Generator(device=device)
+        g.manual_seed(seed + 77 + 1000 * rank)
+        self.xs = [torch.randn((T, H), generator=g, device=device) for _ in range(n_inputs)]
+        self.out = torch.empty(T, H, device=device)
+        self.ids, self.probs = self.ep.ids, self.ep.probs
+        self.ws = self.ep.ws
+        self.layer_bytes = layer_bytes
+
+    @property
+    def router_ws(self):
+        return self.ep.router_ws
+
+    def step(self, i, x=None, out=None):
+        gu, dn, W = self.layers[i % self.n_layers]
+        x = self.xs[i % len(self.xs)] if x is None else x
+        out = self.out if out is None else out
+        self.ep.forward(W, x, gu, dn, out)
+
+    capture = LayerSet.capture
+
+    def n_kernels(self):
+        return len(KERNELS[self.routing])
+
+    def unique_experts(self, i):
+        """This rank's experts hit by step i (every rank's tokens) and its
+        pair count."""
+        self.step(i)
+        ids = self.ep.bufs.ids_all.cpu().numpy()
+        probs = self.ep.bufs.probs_all.cpu().numpy()
+        first, count = self.ep.first, self.ep.count
+        hit = ids[(probs > 1e-4) & (ids >= first) & (ids < first + count)]
+        return len(np.unique(hit)), int(hit.size)
+
+    def nvlink_bytes(self):
+        """Bytes each rank receives per step: the all-gather brings (N-1)
+        home batches of rows, ids and weights; the reduce-scatter (ring or
+        in-switch) moves (N-1)/N of the [N*T, H] partials."""
+        n, T, H, K = self.world, self.T, self.H, self.K
+        return (n - 1) * T * (H * 4 + K * 8) + (n - 1) * T * H * 4
 
 
 def dist_setup(n_gpus):
@@ -328,10 +448,10 @@ def time_e2e(ls, steps, warmup, world):
 def router_recomputed(ls, steps):
     """Tokens whose top-k needed the exact sequential logits, over `steps`
     eager steps (read from the workspace's counter)."""
-    ls.moe.device_status(ls.ws)
+    ls.moe.device_status(ls.router_ws)
     for i in range(steps):
         ls.step(i)
-    st, rec = ls.moe.device_status(ls.ws)
+    st, rec = ls.moe.device_status(ls.router_ws)
     return {"tokens": rec, "of": steps * ls.T, "status": st}
 
 
@@ -348,30 +468,31 @@ def algorithmic_bytes(ls, unique, pairs):
     return layer, gate_up
 
 
-def cpu_baseline(oracle, ls, budget_s=12.0):
+def cpu_baseline(oracle, ls, budget_s=10.0):
     """The reference's CPU algorithm (oracle port) on a bounded sample of the
-    workload's tokens, all host threads, per-token like forward_token."""
-    import torch
-
+    workload: the tokens of the bench's inputs in order, one token at a time
+    like forward_token, all host threads, for about `budget_s` seconds."""
     wtype, H, I, E, K, T = ls.wtype, ls.H, ls.I, ls.E, ls.K, ls.T
     gu, dn, W = ls.layers[0]
     gu_h, dn_h, W_h = gu.cpu().numpy(), dn.cpu().numpy(), W.cpu().numpy()
-    x = ls.xs[0].cpu().numpy()
+    xs = [x.cpu().numpy() for x in ls.xs]
+    lgs = [l.cpu().numpy() for l in ls.logit_in] if ls.routing != "router" else None
     threads = os.cpu_count() or 1
     done = 0
     t0 = time.perf_counter()
-    while done < T and time.perf_counter() - t0 < budget_s:
-        xt = x[done:done + 1]
+    while time.perf_counter() - t0 < budget_s:
+        j, t = divmod(done % (len(xs) * T), T)
+        xt = xs[j][t:t + 1]
         if ls.routing == "router":
             _, ids, probs = oracle.router(W_h, xt, H, E, K, 1)
         else:
-            ids, probs = oracle.route_from_logits(ls.logit_in[0][done:done + 1].cpu().numpy(), E, K, 1)
+            ids, probs = oracle.route_from_logits(lgs[j][t:t + 1], E, K, 1)
         oracle.experts(wtype, gu_h, dn_h, ids, probs, None, xt, H, I, E, K, 1, threads)
         done += 1
     dt = time.perf_counter() - t0
     return {"value": done / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{done} of the {T} tokens of step 0, one token at a time (model.rs forward_token order), "
-                      f"{dt:.1f} s"}
+            "sample": f"{done} tokens, cycling over the bench's {len(xs)} input batches of {T}, one token at a time "
+                      f"(model.rs forward_token order), {dt:.1f} s"}
 
 
 def run_ours(args):
@@ -384,7 +505,10 @@ def run_ours(args):
     steps, warmup = args.steps, args.warmup
     hbm_peak, peak_kind = peaks()
 
-    ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
+    if world > 1:
+        ls = EPLayerSet(moe, synth, device, args.workload, 8, rank, world)
+    else:
+        ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
     unique, pairs = ls.unique_experts(0)
     graphs = [ls.capture(g) for g in range(2 * ls.n_layers)]
     with ClockSampler(local) as clk:
@@ -396,12 +520,13 @@ def run_ours(args):
 
     T = ls.T
     value = world * T * steps / (ms / 1e3)
+    strong = args.workload in STRONG
     layer_bytes, gate_up_bytes = algorithmic_bytes(ls, unique, pairs)
     gu_ms = kern["gate_up"] / steps
     top = max(kern, key=kern.get)
     total_kern = sum(kern.values())
     line = {
-        "metric": "MoE-layer tokens/sec (decode batch 64, Gemma-4-26B-A4B MoE shape); % of HBM roofline",
+        "metric": METRIC,
         "value": round(value, 2),
         "unit": "tokens/s",
         "n_gpus": world,
@@ -409,13 +534,15 @@ def run_ours(args):
         "warmup": warmup,
         "ms_per_step": round(ms / steps, 5),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         "dtype": "q4_0 weights x q8_0 activations, int32 block dots, f32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights quantised with the reference's Q4_0 rules, N(0,1) x)",
         "config": {"workload": args.workload, "hidden": ls.H, "experts": ls.E, "top_k": ls.K, "expert_ffn": ls.I,
-                   "tokens_per_step": T, "weights": "Q4_0" if ls.wtype == 2 else "Q8_0",
-                   "parallelism": "replicas" if world > 1 else "single",
+                   "tokens_per_step": world * T, "home_tokens_per_rank": T,
+                   "weights": "Q4_0" if ls.wtype == 2 else "Q8_0",
+                   "parallelism": f"ep{world} (experts sharded, NCCL all-gather + reduce-scatter)" if world > 1
+                   else "single GPU",
                    "l2": f"inputs larger than L2: steps rotate over {ls.n_layers} layer copies "
                          f"({ls.n_layers * ls.layer_bytes / 1e6:.0f} MB of weights)",
                    "unique_experts_step0": unique},
@@ -435,6 +562,13 @@ def run_ours(args):
         "router_exact_fallback_tokens": recomputed,
         "clocks": clk.summary(),
     }
+    if world > 1:
+        nv = ls.nvlink_bytes()
+        comm_ms = ms / steps - total_kern / steps
+        line["nvlink"] = {"bytes_received_per_rank_per_step": nv,
+                          "ms_outside_library_kernels_per_step": round(comm_ms, 5),
+                          "peer_copy_peak_GBs": 770.0,
+                          "roofline_ms_per_step": round(nv / 770e9 * 1e3, 5)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
         line["cpu_baseline"] = cpu_baseline(oracle, ls)
@@ -467,14 +601,23 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def traffic_from_profile(workload):
-    """DRAM bytes per gate_up launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "traffic.json")
+def traffic_from_profile(workload, kernel="gate_up"):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
+    summaries under profiles/ (a line "traffic: <workload> <kernel> <bytes>"),
+    or None."""
+    d = os.path.join(ROOT, "profiles")
     try:
-        with open(path) as f:
-            return json.load(f).get(workload, {}).get("gate_up")
-    except Exception:
-        return None
+        for name in sorted(os.listdir(d)):
+            if not name.endswith(".md"):
+                continue
+            with open(os.path.join(d, name)) as f:
+                for line in f:
+                    parts = line.split()
+                    if len(parts) == 4 and parts[0] == "traffic:" and parts[1] == workload and parts[2] == kernel:
+                        return int(parts[3])
+    except OSError:
+        pass
+    return None
 
 
 def run_reference(args):
@@ -521,7 +664,7 @@ def run_reference(args):
     v = tokens / dt
     line = {
         "impl": "reference",
-        "metric": "MoE-layer tokens/sec (decode batch 64, Gemma-4-26B-A4B MoE shape); % of HBM roofline",
+        "metric": METRIC,
         "value": round(v, 3), "unit": "tokens/s", "higher_is_better": True, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "config": {"workload": args.workload, "hidden": H, "experts": E, "top_k": K, "expert_ffn": I,
@@ -537,7 +680,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS))

@@ -119,12 +119,36 @@ int mrml_moe_experts(int wtype, const uint8_t *gate_up, const uint8_t *down, con
                      const float *down_scale, const float *x, float *out, int H, int I, int E, int K, int T,
                      void *workspace, size_t workspace_bytes, mrml_stream_t stream);
 
+/* One expert-parallel shard of mrml_moe_experts.  No counterpart in the
+ * reference, which keeps all experts on one device.  gate_up and down hold
+ * only experts [e_first, e_first + e_count) of the layer's E (same per-expert
+ * layout as above, expert e_first first); ids are global in [0, E).  Pairs
+ * routed to experts outside the shard are skipped like pairs with
+ * alpha <= 1e-4, and out[t] is the slot-ordered sum over this shard's pairs,
+ * (alpha * down) * down_scale[id] (down_scale indexed by the global id), or 0
+ * for a token with none.  Summing the shards' outputs gives the layer output
+ * within rounding of the single-device result (the sum order differs).
+ * Workspace: mrml_moe_workspace_bytes(H, I, e_count, K, T).  Used by the
+ * expert-parallel layer across GPUs, where T covers every rank's tokens. */
+int mrml_moe_experts_shard(int wtype, const uint8_t *gate_up, const uint8_t *down, const int32_t *ids,
+                           const float *probs, const float *down_scale, const float *x, float *out, int H, int I,
+                           int E, int e_first, int e_count, int K, int T, void *workspace, size_t workspace_bytes,
+                           mrml_stream_t stream);
+
 /* The whole layer: mrml_moe_router on (router_w, router_x) followed by
  * mrml_moe_experts on x.  router_x and x may be the same pointer. */
 int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, const float *x, const uint8_t *gate_up,
                      const uint8_t *down, const float *down_scale, float *logits, int32_t *ids, float *probs,
                      float *out, int H, int I, int E, int K, int T, void *workspace, size_t workspace_bytes,
                      mrml_stream_t stream);
+
+/* The weighted combine alone (model.rs:2163-2165): out[t][i] = sum over
+ * k ascending of (probs[t,k] * ydown[pos[t,k]][i]) * down_scale[ids[t,k]],
+ * starting from 0; pairs with pos < 0 are skipped.  ydown holds unscaled
+ * down-projection rows, one per (token, slot).  Used by the expert-parallel
+ * path, where those rows come back from the ranks that own the experts. */
+int mrml_moe_combine(const float *ydown, const int32_t *pos, const int32_t *ids, const float *probs,
+                     const float *down_scale, float *out, int H, int K, int T, mrml_stream_t stream);
 
 /* GGUF block quantisers on the device, byte-identical to the reference's
  * host quantisers: Q8_0 quant.rs:193-228, Q4_0 quant.rs:372-389.

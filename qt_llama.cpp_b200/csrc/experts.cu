@@ -123,7 +123,7 @@ constexpr int kDispatchThreads = 1024;
 
 __global__ void __launch_bounds__(kDispatchThreads)
     dispatch_kernel(const int32_t* __restrict__ ids, const float* __restrict__ probs, int n_pairs, int E,
-                    int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
+                    int e_first, int e_total, int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
                     int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
                     int* __restrict__ n_units, int NT, int mt_gu, int rows_gu, int mt_dn, int* __restrict__ err) {
   extern __shared__ int32_t dsm[];
@@ -134,13 +134,16 @@ __global__ void __launch_bounds__(kDispatchThreads)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < E * 35; i += blockDim.x) dsm[i] = 0;
   __syncthreads();
+  // Experts [e_first, e_first + E) of e_total are this call's; pairs routed
+  // to the others are skipped like pairs with alpha <= 1e-4 (an expert-
+  // parallel shard), ids outside [0, e_total) are errors.
   for (int p = tid; p < n_pairs; p += blockDim.x) {
-    const int e = ids[p];
+    const int id = ids[p];
     if (probs[p] > 0.0001f) {
-      if (e >= 0 && e < E)
-        atomicAdd(&cnt[e], 1);
-      else
+      if (id < 0 || id >= e_total)
         set_error(err, kDevBadExpert);
+      else if (id - e_first >= 0 && id - e_first < E)
+        atomicAdd(&cnt[id - e_first], 1);
     }
   }
   __syncthreads();
@@ -211,8 +214,8 @@ __global__ void __launch_bounds__(kDispatchThreads)
     const int p = b0 + tid;
     int e = -1;
     if (p < n_pairs) {
-      const int id = ids[p];
-      if (probs[p] > 0.0001f && id >= 0 && id < E) e = id;
+      const int id = ids[p] - e_first;
+      if (probs[p] > 0.0001f && id >= 0 && id < E && id + e_first < e_total) e = id;
       if (e < 0) pos[p] = -1;
     }
     const uint32_t peers = __match_any_sync(0xffffffffu, e);
@@ -570,7 +573,8 @@ cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long l
   return cudaPeekAtLastError();
 }
 
-cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int32_t* cnt, int32_t* poff,
+cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
+                            int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
                             int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s) {
   const size_t smem = (size_t)35 * E * sizeof(int32_t);
@@ -578,7 +582,8 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
     cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
   }
-  dispatch_kernel<<<1, kDispatchThreads, smem, s>>>(ids, probs, n_pairs, E, cnt, poff, pair_at, pos, units_gu,
+  dispatch_kernel<<<1, kDispatchThreads, smem, s>>>(ids, probs, n_pairs, E, e_first, e_total, cnt, poff, pair_at, pos,
+                                                     units_gu,
                                                      units_dn, n_units, NT, mt_gu, rows_gu, mt_dn, err);
   return cudaPeekAtLastError();
 }

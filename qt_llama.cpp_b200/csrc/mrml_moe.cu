@@ -1,6 +1,7 @@
 // mrml_moe.cu — the C ABI of libmrml_moe_b200.so (declared in
 // include/mrml_moe.h): argument checks, the workspace layout and the order
 // of kernel launches on the caller's stream.
+#include <algorithm>
 #include <stdint.h>
 #include <stdio.h>
 
@@ -194,7 +195,9 @@ int run_router(const Workspace& w, const float* W, const float* x, float* logits
 // kernels' limits (H not a multiple of 256) use the general dp4a kernels.
 enum Route { kRouteGeneral = 0, kRouteGemv = 1, kRouteTensor = 2 };
 
-Route pick_route(int wtype, int H, int I, int E, int K, int T) {
+// `pairs` is the expected number of (token, slot) pairs this call computes:
+// T * K on one device, about T * K * E / e_total for an expert shard.
+Route pick_route(int wtype, int H, int I, int E, long long pairs) {
   const bool tc = mrml::tc_supported(wtype, H, I, 64) && mrml::tc_supported(wtype, H, I, 16);
   const bool gv = mrml::gv_supported(wtype, H, I);
   switch (g_path) {
@@ -203,19 +206,21 @@ Route pick_route(int wtype, int H, int I, int E, int K, int T) {
     case 3: return kRouteGeneral;
     default: break;
   }
-  if (tc && (long long)T * K > 16ll * E) return kRouteTensor;
+  if (tc && pairs > 16ll * E) return kRouteTensor;
   return gv ? kRouteGemv : kRouteGeneral;
 }
 
 int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids,
                 const float* probs, const float* down_scale, const float* x, float* out, int H, int I, int E, int K,
-                int T, cudaStream_t s) {
-  const Route route = pick_route(wtype, H, I, E, K, T);
-  const int NT = route == kRouteGemv ? mrml::kGvTokens : ((long long)T * K > 12ll * E ? 64 : 16);
+                int T, cudaStream_t s, int e_first = 0, int e_total = 0) {
+  if (e_total == 0) e_total = E;
+  const long long pairs = (long long)T * K * E / e_total;
+  const Route route = pick_route(wtype, H, I, E, pairs);
+  const int NT = route == kRouteGemv ? mrml::kGvTokens : (pairs > 12ll * E ? 64 : 16);
   const int rows_gu = route == kRouteGemv ? mrml::kGvRowsGateUp : 128;
   const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;  // down tiles: 128 rows on both paths
   int* n_units = w.status + 2;
-  MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
+  MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, e_first, e_total, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
                                     n_units, NT, mt_gu, rows_gu, mt_dn, w.status, s));
   if (route == kRouteGeneral) {
     MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
@@ -302,6 +307,21 @@ int mrml_moe_experts(int wtype, const uint8_t* gate_up, const uint8_t* down, con
   return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, (cudaStream_t)stream);
 }
 
+int mrml_moe_experts_shard(int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids,
+                           const float* probs, const float* down_scale, const float* x, float* out, int H, int I,
+                           int E, int e_first, int e_count, int K, int T, void* workspace, size_t workspace_bytes,
+                           mrml_stream_t stream) {
+  if (E <= 0 || e_first < 0 || e_count <= 0 || e_first + e_count > E || E > kMaxE) return MRML_ERR_INVALID_ARGUMENT;
+  if (K > E) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_expert_args(wtype, gate_up, down, ids, probs, x, out, H, I, e_count, std::min(K, e_count), T));
+  if (T == 0) return MRML_OK;
+  MRML_TRY(check_device());
+  MRML_TRY(check_workspace(workspace, workspace_bytes, H, I, e_count, K, T));
+  const Workspace w = carve(workspace, H, I, e_count, K, T);
+  return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, e_count, K, T,
+                     (cudaStream_t)stream, e_first, E);
+}
+
 int mrml_moe_forward(int wtype, const float* router_w, const float* router_x, const float* x, const uint8_t* gate_up,
                      const uint8_t* down, const float* down_scale, float* logits, int32_t* ids, float* probs,
                      float* out, int H, int I, int E, int K, int T, void* workspace, size_t workspace_bytes,
@@ -315,6 +335,17 @@ int mrml_moe_forward(int wtype, const float* router_w, const float* router_x, co
   const cudaStream_t s = (cudaStream_t)stream;
   MRML_TRY(run_router(w, router_w, router_x, logits, ids, probs, H, E, K, T, s));
   return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s);
+}
+
+int mrml_moe_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,
+                     const float* down_scale, float* out, int H, int K, int T, mrml_stream_t stream) {
+  if (H <= 0 || K <= 0 || T < 0 || K > kMaxK) return MRML_ERR_INVALID_ARGUMENT;
+  if (T == 0) return MRML_OK;
+  if (!ydown || !pos || !ids || !probs || !out) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_combine(ydown, pos, ids, probs, down_scale, out, H, K, T, s));
+  return MRML_OK;
 }
 
 int mrml_moe_quantize_q8_0(const float* src, uint8_t* dst, size_t n, mrml_stream_t stream) {

@@ -49,6 +49,9 @@ SIGNATURES = {
         _i,
         [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp],
     ),
+    "mrml_moe_experts_shard": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz,
+                                    _vp]),
+    "mrml_moe_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mrml_moe_quantize_q8_0": (_i, [_vp, _vp, _sz, _vp]),
     "mrml_moe_quantize_q4_0": (_i, [_vp, _vp, _sz, _vp]),
     "mrml_moe_device_status": (_i, [_vp, _vp, _c.POINTER(_c.c_int)]),
@@ -160,6 +163,26 @@ def forward(wtype, router_w, router_x, x, gate_up, down, down_scale, logits, ids
         lib.mrml_moe_forward(wtype, _ptr(router_w), _ptr(router_x), _ptr(x), _ptr(gate_up), _ptr(down),
                              _ptr(down_scale), _ptr(logits), _ptr(ids), _ptr(probs), _ptr(out), H, I, E, K, T,
                              _ptr(ws), ws.numel(), _stream_ptr(stream)),
+    )
+
+
+def experts_shard(wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, e_first, e_count, K, T, ws,
+                  stream=None):
+    lib = load_library()
+    _check(
+        "mrml_moe_experts_shard",
+        lib.mrml_moe_experts_shard(wtype, _ptr(gate_up), _ptr(down), _ptr(ids), _ptr(probs), _ptr(down_scale), _ptr(x),
+                                   _ptr(out), H, I, E, e_first, e_count, K, T, _ptr(ws), ws.numel(),
+                                   _stream_ptr(stream)),
+    )
+
+
+def combine(ydown, pos, ids, probs, down_scale, out, H, K, T, stream=None):
+    lib = load_library()
+    _check(
+        "mrml_moe_combine",
+        lib.mrml_moe_combine(_ptr(ydown), _ptr(pos), _ptr(ids), _ptr(probs), _ptr(down_scale), _ptr(out), H, K, T,
+                             _stream_ptr(stream)),
     )
 
 

@@ -74,9 +74,19 @@ def test_invalid_arguments_rejected_without_a_gpu(moe):
     # Null pointers with work to do.
     assert lib.mrml_moe_experts(2, None, P, P, P, None, P, P, 64, 64, 8, 2, 1, P, 1 << 20, None) == -1
     assert lib.mrml_moe_quantize_q8_0(P, P, 33, None) == -1
+    # Expert shards: the range must lie inside [0, E).
+    shard = lib.mrml_moe_experts_shard
+    assert shard(2, P, P, P, P, None, P, P, 64, 64, 8, 6, 4, 2, 1, P, 1 << 20, None) == -1
+    assert shard(2, P, P, P, P, None, P, P, 64, 64, 8, -1, 4, 2, 1, P, 1 << 20, None) == -1
+    assert shard(2, P, P, P, P, None, P, P, 64, 64, 8, 0, 0, 2, 1, P, 1 << 20, None) == -1
+    assert shard(2, P, P, P, P, None, P, P, 64, 64, 512, 0, 4, 2, 1, P, 1 << 20, None) == -1
+    assert lib.mrml_moe_combine(P, P, P, P, None, P, 64, 65, 1, None) == -1
 
 
 def test_zero_tokens_is_a_no_op(moe):
     lib = moe.load_library()
     assert lib.mrml_moe_experts(2, None, None, None, None, None, None, None, 64, 64, 8, 2, 0, None, 0, None) == 0
     assert lib.mrml_moe_router(None, None, None, None, None, 64, 8, 2, 0, None, 0, None) == 0
+    assert lib.mrml_moe_experts_shard(2, None, None, None, None, None, None, None, 64, 64, 8, 4, 4, 2, 0, None, 0,
+                                      None) == 0
+    assert lib.mrml_moe_combine(None, None, None, None, None, None, 64, 2, 0, None) == 0

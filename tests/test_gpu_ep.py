@@ -1,0 +1,203 @@
+"""Expert-parallel shards on the GPU.
+
+* mrml_moe_experts_shard on one GPU, on each expert-product path: every
+  shard's partial equals, bit for bit, the single-device mrml_moe_experts
+  call with the other shards' pairs given weight 0, and matches the oracle's
+  partial within tolerance; the partials add up to the layer within
+  tolerance.  (The library matches the oracle bit for bit except where the
+  f32 tanh of the GeGLU rounds differently by one ulp and that changes a
+  Q8_0 rounding of the activation; hence tolerance against the oracle.)
+* The expert-parallel layer on 2 GPUs (NCCL all-gather / reduce-scatter),
+  when the box has them: equal to the sum of the two shards' partials bit
+  for bit, and to the reference within tolerance.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+from test_ep import _case, oracle_shard, synth_range
+from test_gpu_parity import PATHS, assert_close, dev_tensor
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(params=sorted(PATHS))
+def expert_path(request, cuda, moe):
+    moe.set_expert_path(PATHS[request.param])
+    yield request.param
+    moe.set_expert_path(0)
+
+
+def _gpu_case(synth, oracle, moe, device, wtype, H, I, E, K, T, seed):
+    """Like test_ep._case, with the expert weights generated and quantised on
+    the GPU (the quantiser is byte-exact to the reference's)."""
+    gu, dn = synth.expert_weights_device(seed, wtype, H, I, E, device, moe.quantize)
+    W = synth.normal(seed + 1000, E * H, 0.02).reshape(E, H)
+    x = synth.normal(seed + 77, T * H).reshape(T, H)
+    _, ids, probs = oracle.router(W, x, H, E, K, T)
+    return gu.cpu().numpy(), dn.cpu().numpy(), ids, probs, x
+
+
+def _shard_on_gpu(moe, device, wtype, gu, dn, ids, probs, scale, x, H, I, E, first, count, K):
+    import torch
+
+    T = x.shape[0]
+    gu_e = gu.reshape(E, -1)[first:first + count]
+    dn_e = dn.reshape(E, -1)[first:first + count]
+    out = torch.full((T, H), float("nan"), device=device)
+    ws = moe.new_workspace(H, I, count, K, T, device)
+    moe.experts_shard(wtype, dev_tensor(gu_e, device), dev_tensor(dn_e, device), dev_tensor(ids, device),
+                      dev_tensor(probs, device), None if scale is None else dev_tensor(scale, device),
+                      dev_tensor(x, device), out, H, I, E, first, count, K, T, ws)
+    st, _ = moe.device_status(ws)
+    assert st == 0, f"device status {st}"
+    return out.cpu().numpy()
+
+
+_ORACLE = {}
+
+
+@pytest.mark.parametrize("wtype,H,I,E,K,T", [(2, 2816, 704, 128, 8, 64), (8, 1024, 512, 16, 2, 300),
+                                              (2, 256, 128, 8, 3, 7)])
+def _masked_on_gpu(moe, device, wtype, gu, dn, ids, probs, x, H, I, E, first, count, K):
+    """The single-device layer with the pairs outside [first, first+count)
+    given weight 0."""
+    import torch
+
+    T = x.shape[0]
+    loc = (ids >= first) & (ids < first + count)
+    out = torch.full((T, H), float("nan"), device=device)
+    ws = moe.new_workspace(H, I, E, K, T, device)
+    moe.experts(wtype, dev_tensor(gu, device), dev_tensor(dn, device), dev_tensor(ids, device),
+                dev_tensor(np.where(loc, probs, 0).astype(np.float32), device), None, dev_tensor(x, device), out, H,
+                I, E, K, T, ws)
+    st, _ = moe.device_status(ws)
+    assert st == 0, f"device status {st}"
+    return out.cpu().numpy()
+
+
+def test_experts_shard_bit_exact(cuda, moe, oracle, synth, expert_path, wtype, H, I, E, K, T):
+    key = (wtype, H, I, E, K, T)
+    if key not in _ORACLE:  # the oracle's answers are shared by the three paths
+        gu, dn, ids, probs, x = _gpu_case(synth, oracle, moe, cuda, wtype, H, I, E, K, T, 21)
+        ref = oracle.experts(wtype, gu, dn, ids, probs, None, x, H, I, E, K, T, os.cpu_count() or 1)
+        parts = {}
+        for world in (2, 8):
+            for r in range(world):
+                first, count = synth_range(r, world, E)
+                parts[world, r] = oracle_shard(oracle, wtype, gu, dn, first, count, H, I, E, K)(x, ids, probs)
+        _ORACLE[key] = (gu, dn, ids, probs, x, ref, parts)
+    gu, dn, ids, probs, x, ref, parts = _ORACLE[key]
+    for world in (2, 8):
+        total = np.zeros_like(ref)
+        for r in range(world):
+            first, count = synth_range(r, world, E)
+            got = _shard_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, None, x, H, I, E, first, count, K)
+            same = _masked_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, x, H, I, E, first, count, K)
+            assert np.array_equal(got, same), f"shard {r}/{world}: {np.count_nonzero(got != same)} elements differ"
+            if np.abs(parts[world, r]).max() > 0:
+                assert_close(got, parts[world, r])
+            total += got
+        assert_close(total, ref)
+
+
+def test_experts_shard_scale_uses_global_ids(cuda, moe, oracle, synth):
+    wtype, H, I, E, K, T = 8, 256, 128, 8, 2, 9
+    gu, dn, ids, probs, x = _case(synth, oracle, wtype, H, I, E, K, T, 3)
+    scale = (0.5 + np.arange(E, dtype=np.float32) / 4).astype(np.float32)
+    ref = oracle.experts(wtype, gu, dn, ids, probs, scale, x, H, I, E, K, T)
+    a = _shard_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, scale, x, H, I, E, 0, 4, K)
+    b = _shard_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, scale, x, H, I, E, 4, 4, K)
+    assert np.isfinite(a).all() and np.isfinite(b).all()
+    assert_close(a + b, ref)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ep_worker(rank, world, port, args, results):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from tests.conftest import _load
+
+    moe = _load("mrml_moe_b200", os.path.join(ROOT, "qt_llama.cpp_b200", "mrml_moe.py"))
+    synth = _load("mrml_moe_b200_synth", os.path.join(ROOT, "qt_llama.cpp_b200", "synth.py"))
+    ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
+    wtype, H, I, E, K, T, seed = args
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        gu, dn = synth.expert_weights_device(seed, wtype, H, I, E, dev, moe.quantize)
+        W = synth.normal(seed + 1000, E * H, 0.02).reshape(E, H)
+        x = synth.normal(seed + 77, world * T * H).reshape(world * T, H)
+        layer = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, dev)
+        f, c = layer.first, layer.count
+        gu_l = gu[f:f + c].contiguous()
+        dn_l = dn[f:f + c].contiguous()
+        del gu, dn
+        out = torch.empty((T, H), device=dev)
+        layer.forward(dev_tensor(W, dev), dev_tensor(x[rank * T:(rank + 1) * T], dev), gu_l, dn_l, out)
+        torch.cuda.synchronize()
+        st, _ = moe.device_status(layer.ws)
+        results.put((rank, out.cpu().numpy(), layer.ids.cpu().numpy(), st))
+    except Exception as exc:
+        results.put((rank, repr(exc), None, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_layer_two_gpus(cuda, moe, oracle, synth):
+    import multiprocessing as mp
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    args = (2, 2816, 704, 128, 8, 32, 9)
+    wtype, H, I, E, K, T, seed = args
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, args, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(world):
+            r, out, ids, st = q.get(timeout=300)
+            assert not isinstance(out, str), f"rank {r}: {out}"
+            assert st == 0
+            got[r] = (out, ids)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    gu, dn, ids, probs, x = _gpu_case(synth, oracle, moe, cuda, wtype, H, I, E, K, world * T, seed)
+    ref = oracle.experts(wtype, gu, dn, ids, probs, None, x, H, I, E, K, world * T, os.cpu_count() or 1)
+    parts = [_shard_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, None, x, H, I, E, *synth_range(r, world, E), K)
+             for r in range(world)]
+    for r in range(world):
+        out, ids_home = got[r]
+        home = slice(r * T, (r + 1) * T)
+        np.testing.assert_array_equal(ids_home, ids[home])
+        np.testing.assert_array_equal(out, parts[0][home] + parts[1][home])
+        assert_close(out, ref[home])
