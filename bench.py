@@ -548,7 +548,8 @@ def run_ours(args):
                    "unique_experts_step0": unique},
         "roofline": {"bound": "hbm", "kernel": "gate_up", "achieved": round(gate_up_bytes / (gu_ms / 1e3) / 1e9, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(gate_up_bytes / (gu_ms / 1e3) / 1e9 / hbm_peak, 4),
-                     "traffic": traffic_from_profile(args.workload), "peak_source": peak_kind,
+                     "traffic": traffic_from_profile(args.workload) if world == 1 else None,
+                     "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": gate_up_bytes, "ms_per_launch": round(gu_ms, 5)},
         "layer_roofline": {"achieved": round(layer_bytes / (ms / steps / 1e3) / 1e9, 1), "peak": hbm_peak,
                            "unit": "GB/s", "frac": round(layer_bytes / (ms / steps / 1e3) / 1e9 / hbm_peak, 4),

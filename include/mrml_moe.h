@@ -150,6 +150,12 @@ int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, co
 int mrml_moe_combine(const float *ydown, const int32_t *pos, const int32_t *ids, const float *probs,
                      const float *down_scale, float *out, int H, int K, int T, mrml_stream_t stream);
 
+/* GeGLU, elementwise: out[i] = gelu_tanh(gate[i]) * up[i] with the
+ * reference's formula and rounding (ops.rs:99-114; tanh as glibc's tanhf),
+ * the expert epilogue applied on its own.  Replaces CudaDevice::geglu
+ * (crates/mrml-tensor/src/cuda.rs:2215), the launch of rust_cuda_geglu_f32. */
+int mrml_moe_geglu(const float *gate, const float *up, float *out, size_t n, mrml_stream_t stream);
+
 /* GGUF block quantisers on the device, byte-identical to the reference's
  * host quantisers: Q8_0 quant.rs:193-228, Q4_0 quant.rs:372-389.
  * n is a multiple of 32; dst holds n/32*34 (Q8_0) or n/32*18 (Q4_0) bytes. */

@@ -102,6 +102,13 @@ def mat_vec_f32(wtype, w, x, n_rows, n_cols):
     return y
 
 
+def geglu(gate, up):
+    gate, up = _c(gate, np.float32), _c(up, np.float32)
+    out = np.zeros_like(gate)
+    lib().oracle_geglu(_p(gate), _p(up), _p(out), gate.size)
+    return out
+
+
 def router(W, x, H, E, K, T):
     W, x = _c(W, np.float32), _c(x, np.float32)
     logits = np.zeros((T, E), np.float32)

@@ -66,11 +66,97 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
-// tanh for the GeGLU epilogue: the double-precision libdevice tanh rounded
-// once to f32.  It equals the correctly rounded f32 tanh except in rare
-// double-rounding cases; glibc's tanhf (the reference) is within about one
-// ulp of that.
-__device__ __forceinline__ float tanh_f32(float x) { return (float)tanh((double)x); }
+// tanh for the GeGLU epilogue, bit-identical to the reference's: the Rust
+// reference's f32::tanh is the C library's tanhf, which in glibc 2.39 is the
+// fdlibm single-precision algorithm (sysdeps/ieee754/flt-32/s_tanhf.c and
+// s_expm1f.c).  That algorithm is restated here step for step in f32 with
+// round-to-nearest operations and no contraction:
+//   tanh(x) = sign(x) * (|x| >= 1 ? 1 - 2 / (expm1(2|x|) + 2)
+//                                 : -m / (m + 2), m = expm1(-2|x|)),
+//   x for |x| < 2^-55 (as x * (1 + x)), 1 for |x| >= 22;
+//   expm1(x): x = k ln2 + r (ln2 split hi/lo, compensation c), then
+//   r - (r*e - r^2/2) with e from the Remez rational approximation
+//   R1 = 1 + hxs*(Q1 + hxs*(Q2 + ... Q5)), hxs = r^2/2, and reconstruction
+//   by the exponent k.
+// The steps are evaluated for every input and the case is chosen by
+// selects (the case split depends on the data, and branches would diverge
+// inside a warp); every case computes exactly glibc's operations.  This
+// form was checked equal to glibc's tanhf on all 2^32 - 2^24 + 2 non-NaN
+// f32 inputs.
+namespace tanh_glibc {
+constexpr float kLn2Hi = 6.9313812256e-01f, kLn2Lo = 9.0580006145e-06f, kInvLn2 = 1.4426950216e+00f;
+constexpr float kQ1 = -3.3333335072e-02f, kQ2 = 1.5873016091e-03f, kQ3 = -7.9365076090e-05f,
+                kQ4 = 4.0082177293e-06f, kQ5 = -2.0109921195e-07f;
+
+// expm1 for finite |x| < 44 (other inputs give unused garbage).
+__device__ __forceinline__ float expm1(float x) {
+  const uint32_t ax = __float_as_uint(x) & 0x7fffffffu;
+  const bool neg = (__float_as_uint(x) >> 31) != 0;
+  // Reduction x = k ln2 + (hi - lo); k = 0 (no reduction) for |x| <= ln2/2,
+  // +-1 up to 1.5 ln2, else round(x / ln2).  k = 0 and k = +-1 give the
+  // same values as glibc's special-cased forms.
+  int k = 0;
+  if (ax > 0x3eb17218u) {
+    const int kg = __float2int_rz(__fadd_rn(__fmul_rn(kInvLn2, x), neg ? -0.5f : 0.5f));
+    k = ax < 0x3f851592u ? (neg ? -1 : 1) : kg;
+  }
+  const float tk = (float)k;
+  const float hi = __fsub_rn(x, __fmul_rn(tk, kLn2Hi));
+  const float lo = __fmul_rn(tk, kLn2Lo);
+  const float xr = __fsub_rn(hi, lo);
+  const float c = __fsub_rn(__fsub_rn(hi, xr), lo);
+  const float hfx = __fmul_rn(0.5f, xr);
+  const float hxs = __fmul_rn(xr, hfx);
+  float r1 = __fadd_rn(kQ4, __fmul_rn(hxs, kQ5));
+  r1 = __fadd_rn(kQ3, __fmul_rn(hxs, r1));
+  r1 = __fadd_rn(kQ2, __fmul_rn(hxs, r1));
+  r1 = __fadd_rn(kQ1, __fmul_rn(hxs, r1));
+  r1 = __fadd_rn(1.0f, __fmul_rn(hxs, r1));
+  const float t = __fsub_rn(3.0f, __fmul_rn(r1, hfx));
+  float e = __fmul_rn(hxs, __fdiv_rn(__fsub_rn(r1, t), __fsub_rn(6.0f, __fmul_rn(xr, t))));
+  const float res0 = __fsub_rn(xr, __fsub_rn(__fmul_rn(xr, e), hxs));  // k == 0
+  e = __fsub_rn(__fsub_rn(__fmul_rn(xr, __fsub_rn(e, c)), c), hxs);
+  const float resm1 = __fsub_rn(__fmul_rn(0.5f, __fsub_rn(xr, e)), 0.5f);  // k == -1
+  const float res1 = xr < -0.25f ? __fmul_rn(-2.0f, __fsub_rn(e, __fadd_rn(xr, 0.5f)))
+                                 : __fadd_rn(1.0f, __fmul_rn(2.0f, __fsub_rn(xr, e)));  // k == 1
+  const uint32_t kb = (uint32_t)k << 23;
+  // k <= -2 or k > 56: 2^k * (1 - (e - x)) - 1
+  const float resA = __fsub_rn(__uint_as_float(__float_as_uint(__fsub_rn(1.0f, __fsub_rn(e, xr))) + kb), 1.0f);
+  // 2 <= k < 23: 2^k * ((1 - 2^-k) - (e - x))
+  const int ks = min(max(k, 2), 22);
+  const float resB = __uint_as_float(
+      __float_as_uint(__fsub_rn(__uint_as_float(0x3f800000u - (0x1000000u >> ks)), __fsub_rn(e, xr))) + kb);
+  // 23 <= k <= 56: 2^k * ((x - (e + 2^-k)) + 1)
+  const int kc = min(max(k, 23), 56);
+  const float resC = __uint_as_float(
+      __float_as_uint(__fadd_rn(__fsub_rn(xr, __fadd_rn(e, __uint_as_float((uint32_t)(0x7f - kc) << 23))), 1.0f)) +
+      kb);
+  float r = k == 0    ? res0
+            : k == -1 ? resm1
+            : k == 1  ? res1
+            : (k <= -2 || k > 56) ? resA
+            : k < 23  ? resB
+                      : resC;
+  if (ax < 0x33000000u) r = x;                                        // |x| < 2^-25
+  if (ax >= 0x4195b844u && neg) r = __fsub_rn(1.0e-30f, 1.0f);        // x < -27 ln2
+  return r;
+}
+}  // namespace tanh_glibc
+
+__device__ __forceinline__ float tanh_f32(float x) {
+  const uint32_t ax = __float_as_uint(x) & 0x7fffffffu;
+  const bool big = ax >= 0x3f800000u;  // |x| >= 1
+  const float a = fabsf(x);
+  const float m = tanh_glibc::expm1(big ? __fmul_rn(2.0f, a) : __fmul_rn(-2.0f, a));
+  // |x| >= 1: 1 - 2 / (m + 2);  |x| < 1: -m / (m + 2)
+  const float q = __fdiv_rn(big ? 2.0f : -m, __fadd_rn(m, 2.0f));
+  float z = big ? __fsub_rn(1.0f, q) : q;
+  if (ax >= 0x41b00000u) z = 1.0f;  // |x| >= 22: 1 - 1e-30 rounded
+  z = (__float_as_uint(x) >> 31) ? -z : z;
+  if (ax < 0x24000000u) z = __fmul_rn(x, __fadd_rn(1.0f, x));  // |x| < 2^-55 (and +-0)
+  if (ax > 0x7f800000u) z = x;                                 // NaN
+  return z;
+}
 
 // ops.rs:101-104, evaluated left to right without contraction:
 // 0.5*x*(1 + tanh(0.7978845608*(x + 0.044715*x*x*x))).
@@ -80,9 +166,54 @@ __device__ __forceinline__ float gelu_approx(float x) {
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanh_f32(inner)));
 }
 
-// expf for the router softmax: double exp rounded once to f32 (equal to the
-// correctly rounded expf except in rare double-rounding cases).
-__device__ __forceinline__ float exp_f32(float x) { return (float)exp((double)x); }
+// expf for the router softmax, bit-identical to the reference's f32::exp,
+// i.e. glibc 2.39's expf (sysdeps/ieee754/flt-32/e_expf.c, the table-driven
+// algorithm published in ARM's optimized-routines): in double precision,
+//   z = x * 32/ln2 = k + r  (k by the 1.5*2^52 shift trick, r in [-1/2, 1/2]),
+//   2^(k/32) = s from a 32-entry table of 2^(i/32) (bits minus i*2^52/32)
+//   with the exponent k>>5 added to the bits,
+//   exp(x) ~= s * (C0 r^3 + C1 r^2 + C2 r + 1), rounded once to f32.
+// glibc's x86-64 build contracts the multiply-adds into FMAs (the variant
+// picked on FMA hardware, as on the B200 hosts); the steps below use the same
+// fused operations.  Checked equal to glibc's expf on every f32 input in
+// (-103.97, 88.72); outside it the result is 0 or +inf as in glibc.
+namespace exp_glibc {
+__device__ __constant__ const uint64_t kTab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
+};
+constexpr double kInvLn2N = 0x1.71547652b82fep+0 * 32, kShift = 0x1.8p+52;
+constexpr double kC0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32, kC1 = 0x1.ebfce50fac4f3p-3 / 32 / 32,
+                 kC2 = 0x1.62e42ff0c52d6p-1 / 32;
+}  // namespace exp_glibc
+
+__device__ __forceinline__ float exp_f32(float x) {
+  using namespace exp_glibc;
+  const uint32_t ux = __float_as_uint(x);
+  if (((ux >> 20) & 0x7ffu) >= 0x42bu) {  // |x| >= 88 or not finite
+    if (ux == 0xff800000u) return 0.0f;
+    if (((ux >> 20) & 0x7ffu) >= 0x7f8u) return x + x;
+    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
+    if (x < -0x1.9fe368p6f) return 0.0f;
+  }
+  const double xd = (double)x;
+  double kd = __fma_rn(kInvLn2N, xd, kShift);
+  const uint64_t ki = (uint64_t)__double_as_longlong(kd);
+  kd = __dsub_rn(kd, kShift);
+  const double r = __fma_rn(kInvLn2N, xd, -kd);
+  const double s = __longlong_as_double((long long)(kTab[ki % 32] + (ki << 47)));
+  const double z = __fma_rn(kC0, r, kC1);
+  const double r2 = __dmul_rn(r, r);
+  double y = __fma_rn(kC2, r, 1.0);
+  y = __fma_rn(z, r2, y);
+  return __double2float_rn(__dmul_rn(y, s));
+}
 
 // C roundf: nearest integer, halfway cases away from zero (CUDA's roundf has
 // these semantics).

@@ -548,6 +548,12 @@ __global__ void combine_kernel(const float* __restrict__ ydown, const int32_t* _
   out[(size_t)t * H + i] = o;
 }
 
+__global__ void geglu_kernel(const float* __restrict__ gate, const float* __restrict__ up, float* __restrict__ out,
+                             long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = __fmul_rn(gelu_approx(gate[i]), up[i]);
+}
+
 }  // namespace mrml
 
 // ------------------------------------------------------------ launchers ---
@@ -562,6 +568,13 @@ static int grid_for_blocks(long long warps_needed) {
 cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
                                  cudaStream_t s) {
   quantize_rows_kernel<<<grid_for_blocks(n_blocks), 256, 0, s>>>(x, xq, xd, xsum, n_blocks);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_geglu(const float* gate, const float* up, float* out, long long n, cudaStream_t s) {
+  long long g = (n + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  geglu_kernel<<<(int)(g < 1 ? 1 : g), 256, 0, s>>>(gate, up, out, n);
   return cudaPeekAtLastError();
 }
 

@@ -348,6 +348,15 @@ int mrml_moe_combine(const float* ydown, const int32_t* pos, const int32_t* ids,
   return MRML_OK;
 }
 
+int mrml_moe_geglu(const float* gate, const float* up, float* out, size_t n, mrml_stream_t stream) {
+  if (n == 0) return MRML_OK;
+  if (!gate || !up || !out || n > ((size_t)1 << 40)) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_geglu(gate, up, out, (long long)n, s));
+  return MRML_OK;
+}
+
 int mrml_moe_quantize_q8_0(const float* src, uint8_t* dst, size_t n, mrml_stream_t stream) {
   if (n % 32 != 0) return MRML_ERR_INVALID_ARGUMENT;
   if (n == 0) return MRML_OK;

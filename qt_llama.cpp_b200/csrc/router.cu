@@ -226,6 +226,9 @@ __device__ __forceinline__ float exact_logit_smem(const float* __restrict__ xs, 
   float dot = 0.f;
   int i = 0;
   if ((H & 3) == 0) {
+    // The chain is a dependent sequence of adds; unrolling lets the shared-
+    // memory loads run ahead of it.
+#pragma unroll 8
     for (; i < H; i += 4) {
       const float4 a = *reinterpret_cast<const float4*>(xs + i);
       const float4 b = *reinterpret_cast<const float4*>(ws + i);
@@ -294,7 +297,7 @@ __device__ void finish_token(int* cand, float* cval, int count, int K, int t, in
 // of the exact fallback.  status[0] is the device status word, status[1]
 // counts tokens that needed the fallback (status may be null without bounds).
 template <int PL>
-__global__ void __launch_bounds__(32 * kTopkWarps)
+__global__ void __launch_bounds__(32 * kTopkWarps, 1)
     router_topk_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
                        const float* __restrict__ bounds, int32_t* __restrict__ ids, float* __restrict__ probs, int H,
                        int E, int K, int T, int* __restrict__ status) {

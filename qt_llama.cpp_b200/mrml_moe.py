@@ -52,6 +52,7 @@ SIGNATURES = {
     "mrml_moe_experts_shard": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz,
                                     _vp]),
     "mrml_moe_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "mrml_moe_geglu": (_i, [_vp, _vp, _vp, _sz, _vp]),
     "mrml_moe_quantize_q8_0": (_i, [_vp, _vp, _sz, _vp]),
     "mrml_moe_quantize_q4_0": (_i, [_vp, _vp, _sz, _vp]),
     "mrml_moe_device_status": (_i, [_vp, _vp, _c.POINTER(_c.c_int)]),
@@ -184,6 +185,11 @@ def combine(ydown, pos, ids, probs, down_scale, out, H, K, T, stream=None):
         lib.mrml_moe_combine(_ptr(ydown), _ptr(pos), _ptr(ids), _ptr(probs), _ptr(down_scale), _ptr(out), H, K, T,
                              _stream_ptr(stream)),
     )
+
+
+def geglu(gate, up, out, stream=None):
+    lib = load_library()
+    _check("mrml_moe_geglu", lib.mrml_moe_geglu(_ptr(gate), _ptr(up), _ptr(out), gate.numel(), _stream_ptr(stream)))
 
 
 def quantize(wtype, src, dst, stream=None):

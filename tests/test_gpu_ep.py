@@ -1,12 +1,9 @@
 """Expert-parallel shards on the GPU.
 
 * mrml_moe_experts_shard on one GPU, on each expert-product path: every
-  shard's partial equals, bit for bit, the single-device mrml_moe_experts
-  call with the other shards' pairs given weight 0, and matches the oracle's
-  partial within tolerance; the partials add up to the layer within
-  tolerance.  (The library matches the oracle bit for bit except where the
-  f32 tanh of the GeGLU rounds differently by one ulp and that changes a
-  Q8_0 rounding of the activation; hence tolerance against the oracle.)
+  shard's partial equals, bit for bit, both the single-device
+  mrml_moe_experts call and the oracle with the other shards' pairs given
+  weight 0; the partials add up to the layer within tolerance.
 * The expert-parallel layer on 2 GPUs (NCCL all-gather / reduce-scatter),
   when the box has them: equal to the sum of the two shards' partials bit
   for bit, and to the reference within tolerance.
@@ -22,7 +19,7 @@ import numpy as np
 import pytest
 
 from test_ep import _case, oracle_shard, synth_range
-from test_gpu_parity import PATHS, assert_close, dev_tensor
+from test_gpu_parity import PATHS, assert_close, assert_exact, dev_tensor
 
 pytestmark = pytest.mark.gpu
 
@@ -65,8 +62,6 @@ def _shard_on_gpu(moe, device, wtype, gu, dn, ids, probs, scale, x, H, I, E, fir
 _ORACLE = {}
 
 
-@pytest.mark.parametrize("wtype,H,I,E,K,T", [(2, 2816, 704, 128, 8, 64), (8, 1024, 512, 16, 2, 300),
-                                              (2, 256, 128, 8, 3, 7)])
 def _masked_on_gpu(moe, device, wtype, gu, dn, ids, probs, x, H, I, E, first, count, K):
     """The single-device layer with the pairs outside [first, first+count)
     given weight 0."""
@@ -84,6 +79,8 @@ def _masked_on_gpu(moe, device, wtype, gu, dn, ids, probs, x, H, I, E, first, co
     return out.cpu().numpy()
 
 
+@pytest.mark.parametrize("wtype,H,I,E,K,T", [(2, 2816, 704, 128, 8, 64), (8, 1024, 512, 16, 2, 300),
+                                              (2, 256, 128, 8, 3, 7)])
 def test_experts_shard_bit_exact(cuda, moe, oracle, synth, expert_path, wtype, H, I, E, K, T):
     key = (wtype, H, I, E, K, T)
     if key not in _ORACLE:  # the oracle's answers are shared by the three paths
@@ -103,8 +100,7 @@ def test_experts_shard_bit_exact(cuda, moe, oracle, synth, expert_path, wtype, H
             got = _shard_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, None, x, H, I, E, first, count, K)
             same = _masked_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, x, H, I, E, first, count, K)
             assert np.array_equal(got, same), f"shard {r}/{world}: {np.count_nonzero(got != same)} elements differ"
-            if np.abs(parts[world, r]).max() > 0:
-                assert_close(got, parts[world, r])
+            assert_exact(got, parts[world, r])
             total += got
         assert_close(total, ref)
 

@@ -36,6 +36,15 @@ def dev_tensor(a, device):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device)
 
 
+def assert_exact(got, ref):
+    """Bit-identical to the oracle (the library restates the reference's f32
+    operation order, glibc's tanhf and expf included)."""
+    got, ref = np.asarray(got, np.float32), np.asarray(ref, np.float32)
+    assert got.shape == ref.shape
+    diff = got.view(np.uint32) != ref.view(np.uint32)
+    assert not diff.any(), f"{np.count_nonzero(diff)} of {diff.size} elements differ (max {np.abs(got - ref).max():.3e})"
+
+
 def assert_close(got, ref):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
@@ -106,6 +115,27 @@ def test_gguf_quantisers_byte_exact(cuda, moe, oracle, synth, wtype):
 
 
 # ------------------------------------------------------------------ router
+
+
+def test_geglu_bit_exact(cuda, moe, oracle):
+    """The device GeGLU (the expert epilogue's gelu_tanh(gate) * up) equals
+    the reference's f32 evaluation with glibc's tanhf bit for bit, over
+    gates at every scale and arbitrary finite bit patterns."""
+    import torch
+
+    rng = np.random.default_rng(7)
+    parts = [rng.standard_normal(1 << 20).astype(np.float32) * s for s in (1e-6, 1e-3, 0.05, 0.5, 2.0, 8.0, 40.0)]
+    bits = rng.integers(0, 1 << 32, size=1 << 21, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    parts.append(bits[np.isfinite(bits)])
+    parts.append(np.array([0.0, -0.0, 1e-40, -1e-40, 22.0, -22.0, 9.0, -9.0, 1.0, -1.0], np.float32))
+    gate = np.concatenate(parts).astype(np.float32)
+    up = rng.standard_normal(gate.size).astype(np.float32)
+    want = oracle.geglu(gate, up)
+    out = torch.empty(gate.size, device=cuda)
+    moe.geglu(dev_tensor(gate, cuda), dev_tensor(up, cuda), out)
+    got = out.cpu().numpy()
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    assert same.all(), f"{np.count_nonzero(~same)} of {gate.size} differ, first gate {gate[~same][:4]}"
 
 
 def test_router_reference_fixture(cuda, moe, oracle):
@@ -205,7 +235,24 @@ def test_route_from_logits_zipf(cuda, moe, oracle, synth):
     torch.cuda.synchronize()
     r_ids, r_probs = oracle.route_from_logits(logits, E, K, T)
     assert np.array_equal(ids.cpu().numpy(), r_ids)
-    assert np.abs(probs.cpu().numpy() - r_probs).max() < 2e-5
+    assert_exact(probs.cpu().numpy(), r_probs)
+
+
+@pytest.mark.parametrize("spread", [1e-3, 0.1, 1.0, 10.0, 60.0])
+def test_route_from_logits_probs_bit_exact(cuda, moe, oracle, spread):
+    """Softmax weights from given logits equal the reference's bit for bit
+    (glibc's expf restated on the device), at every logit spread."""
+    import torch
+
+    E, K, T = 128, 8, 4096
+    rng = np.random.default_rng(int(spread * 1000))
+    logits = (rng.standard_normal((T, E)) * spread).astype(np.float32)
+    ids = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    probs = torch.empty(T, K, device=cuda)
+    moe.route_from_logits(dev_tensor(logits, cuda), ids, probs, E, K, T)
+    r_ids, r_probs = oracle.route_from_logits(logits, E, K, T)
+    assert np.array_equal(ids.cpu().numpy(), r_ids)
+    assert_exact(probs.cpu().numpy(), r_probs)
 
 
 # ----------------------------------------------------------------- experts
@@ -225,8 +272,7 @@ def test_experts_reference_fixture(cuda, moe, oracle, expert_path):
     f = mg.reference_moe_fixture(oracle)
     L = Layer(moe, cuda, 2, f["gate_up"], f["down"], None, f["H"], f["I"], f["E"], f["K"], 1, f["scales"])
     got = L.experts(f["x"], f["ids"], f["probs"])
-    assert_close(got, golden["out"])
-    assert np.array_equal(got, golden["out"])  # this fixture has no tanh-sensitive rounding
+    assert_exact(got, golden["out"])
 
 
 def test_config1_forward_matches_golden(cuda, moe, oracle, synth, expert_path):
@@ -243,6 +289,8 @@ def test_config1_forward_matches_golden(cuda, moe, oracle, synth, expert_path):
     assert np.array_equal(ids, golden["ids"])
     assert np.abs(probs - golden["probs"]).max() < 2e-5
     assert_close(out, golden["out"])
+    # Given the same routing weights, the experts are exact.
+    assert_exact(L.experts(c["x"], golden["ids"], golden["probs"]), golden["out"])
 
 
 def make_layer_inputs(synth, wtype, H, I, E, T, seed):
@@ -273,6 +321,9 @@ def test_config2_forward(cuda, moe, oracle, synth, c2_q4, T, expert_path):
     assert np.array_equal(ids, r_ids)
     ref = oracle.experts(2, gu, dn, r_ids, r_probs, None, x, H, I, E, K, T, 8)
     assert_close(out, ref)
+    # The router's weights come from its parallel logits (within the
+    # reference's rounding); with the same weights the layer is exact.
+    assert_exact(out, oracle.experts(2, gu, dn, r_ids, probs, None, x, H, I, E, K, T, 8))
 
 
 @pytest.mark.parametrize("wtype,H,I,E,K,T", [(8, 1024, 512, 16, 2, 64), (8, 2816, 704, 16, 8, 9), (2, 1024, 512, 16, 2, 33),
@@ -285,7 +336,7 @@ def test_experts_shapes(cuda, moe, oracle, synth, wtype, H, I, E, K, T, expert_p
     _, r_ids, r_probs = oracle.router(W, x, H, E, K, T)
     got = L.experts(x, r_ids, r_probs)
     ref = oracle.experts(wtype, gu, dn, r_ids, r_probs, scale, x, H, I, E, K, T, 8)
-    assert_close(got, ref)
+    assert_exact(got, ref)
 
 
 def test_config3_prefill_zipf(cuda, moe, oracle, synth, expert_path):
@@ -300,7 +351,7 @@ def test_config3_prefill_zipf(cuda, moe, oracle, synth, expert_path):
     L = Layer(moe, cuda, 8, gu, dn, None, H, I, E, K, T)
     got = L.experts(x, r_ids, r_probs)
     ref = oracle.experts(8, gu, dn, r_ids, r_probs, None, x, H, I, E, K, T, 16)
-    assert_close(got, ref)
+    assert_exact(got, ref)
     counts = np.bincount(r_ids.reshape(-1), minlength=E)
     assert counts.max() > 3 * counts.min()  # the routing really is skewed
 
@@ -315,7 +366,7 @@ def test_alpha_skip_and_zero_slots(cuda, moe, oracle, synth, expert_path):
     got = L.experts(x, ids, probs)
     ref = oracle.experts(8, gu, dn, ids, probs, None, x, H, I, E, K, T)
     assert np.all(got[3] == 0.0)
-    assert_close(got, ref)
+    assert_exact(got, ref)
 
 
 def test_bad_expert_id_reported(cuda, moe, synth):
