@@ -7,9 +7,11 @@
 // integer block dots with dp4a:
 //   warp 0       weight producer (TMA tensor-map tiles / 1-D bulk rows)
 //   warp 1       activation producer (B tiles and scales, bulk copies)
-//   warps 2..3   compute: thread = two weight rows that share activations
-//                (a gate row and its up row, or two down rows), the unit's
-//                (up to 8) tokens in registers
+//   warps 2..5   compute: thread = one weight row, the unit's (up to 8)
+//                tokens in registers.  For gate/up, warps 2-3 hold the 64
+//                gate rows and warps 4-5 the matching up rows; at the end of
+//                a unit the up rows' sums pass to the gate threads through
+//                shared memory, which apply GeGLU and the Q8_0 quantisation.
 // The per-row f32 chain sum += (float)isum_b * (d_w * d_a) runs in block
 // order, as in the reference (quant.rs:335-369 / 564-577), so the results
 // are bit-identical to the tensor-core kernel and to the reference.
@@ -28,8 +30,8 @@ using tc::kM;
 using tc::Params;
 using tc::wait_bar;
 
-constexpr int kComp0 = 2;     // first compute warp
-constexpr int kCompWarps = 2;  // 64 threads, two weight rows each
+constexpr int kComp0 = 2;      // first compute warp
+constexpr int kCompWarps = 4;  // 128 threads, one weight row each
 
 // Integer dot of one weight block (8 words: Q4_0 nibbles or Q8_0 values in
 // element order) with a token's 32 activation bytes, as the bits of the float
@@ -76,16 +78,15 @@ __device__ __forceinline__ void block_words(const uint32_t* qs, uint32_t (&w)[8]
   }
 }
 
-// One quant block of two weight rows (A, B) against the unit's tokens:
-//   acc_X[t] += isum_X(t) * (d_X * d_a(t))     for X in {A, B}
+// One quant block of a weight row against the unit's tokens:
+//   acc[t] += isum(t) * (d_w * d_a(t))
 // in the reference's rounding order (scalar round-to-nearest operations; a
 // packed f32x2 version of this sequence did not reproduce the scalar bits).
 // btile: the block's 8-position activation group; sc: the tokens'
 // {d_a, correction}.
 template <int WQ4, int TT>
-__device__ __forceinline__ void block_pair_tokens(const uint32_t (&wa)[8], const uint32_t (&wb)[8], float dwa,
-                                                  float dwb, const uint8_t* btile, const int2* sc, int nj,
-                                                  float (&acc_a)[TT], float (&acc_b)[TT]) {
+__device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, const int2* sc,
+                                             int nj, float (&acc)[TT]) {
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
     if (t < nj) {
@@ -94,17 +95,15 @@ __device__ __forceinline__ void block_pair_tokens(const uint32_t (&wa)[8], const
       const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
       const int2 s2 = sc[t];
       const float da = __int_as_float(s2.x);
-      const float fa = __fsub_rn(__int_as_float(block_isum_bits<WQ4>(wa, alo, ahi, s2.y)), kMagicF);  // exact
-      const float fb = __fsub_rn(__int_as_float(block_isum_bits<WQ4>(wb, alo, ahi, s2.y)), kMagicF);
-      acc_a[t] = __fadd_rn(acc_a[t], __fmul_rn(fa, __fmul_rn(dwa, da)));
-      acc_b[t] = __fadd_rn(acc_b[t], __fmul_rn(fb, __fmul_rn(dwb, da)));
+      const float f = __fsub_rn(__int_as_float(block_isum_bits<WQ4>(w, alo, ahi, s2.y)), kMagicF);  // exact
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(f, __fmul_rn(dw, da)));
     }
   }
 }
 
-// Unit: kGvTokens (8) positions and 64 row pairs: for gate/up, gate row r and
-// up row r (r < 64); for down, rows r and r + 64 of a 128-row tile.  Thread r
-// of the compute group owns pair r.  Activations use the group-major layout
+// Unit: kGvTokens (8) positions and 128 weight rows: for gate/up, gate rows
+// m0..m0+63 and the same up rows; for down, rows m0..m0+127.  Compute thread
+// c owns raw-tile row c.  Activations use the group-major layout
 // (common.cuh): a B stage is the unit's position group for the chunk's
 // blocks (256 bytes each, contiguous), then their scales (64 bytes each).
 template <int WQ4, int MODE>
@@ -116,12 +115,15 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
   constexpr int GB = 256;            // bytes of one block's activation group
   constexpr int SB = TT * 8;         // bytes of one block's scales
 
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  // 128-byte alignment is what the (unswizzled) tensor copies need; the
+  // barrier block takes the first KiB.
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
   Bars* B = reinterpret_cast<Bars*>(smem);
   uint8_t* raw = smem + 1024;
   uint8_t* bsb = raw + P.rs * P.raw_bytes;
   const int bs_stage = P.kcb * (GB + SB);
+  float* xch = reinterpret_cast<float*>(bsb + P.bs * bs_stage);  // [TT][RG] up-row sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -133,6 +135,8 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
       mbar_init(&B->bs_full[i], 1);
       mbar_init(&B->bs_empty[i], kCompWarps);
     }
+    mbar_init(&B->xch_full, kCompWarps / 2);
+    mbar_init(&B->xch_empty, kCompWarps / 2);
     B->abort = 0;
     fence_barrier_init();
   }
@@ -197,17 +201,18 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
     }
   } else {
     // ------------------------------------------------------------ compute
-    const int r = threadIdx.x - 32 * kComp0;  // row pair within the tile
+    const int c = threadIdx.x - 32 * kComp0;  // raw-tile row of this thread
+    const bool up_row = MODE == kGateUp && c >= RG;
     int rs = 0, bsi = 0;
-    uint32_t rph = 0, bph = 0;
+    uint32_t rph = 0, bph = 0, xph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok && !tc::aborted(B); u += gridDim.x) {
       const int4 U = P.units[u];
       const int p0 = U.y, nvalid = U.z, m0 = U.w;
       const int nj = min(TT, nvalid);
-      float acc_a[TT], acc_b[TT];
+      float acc[TT];
 #pragma unroll
-      for (int t = 0; t < TT; ++t) acc_a[t] = acc_b[t] = 0.f;
+      for (int t = 0; t < TT; ++t) acc[t] = 0.f;
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
         if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
@@ -215,44 +220,32 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
         const uint8_t* bt = bsb + bsi * bs_stage;
         const int2* sc = reinterpret_cast<const int2*>(bt + P.kcb * GB);
         if constexpr (MODE == kGateUp) {
-          const uint8_t* rowa = src + r * (kKC * BB);                 // gate row r
-          const uint8_t* rowb = src + (RG + r) * (kKC * BB);          // up row r
-#define MRML_GV_BLOCK(BL)                                                                        \
-  {                                                                                              \
-    uint32_t da16, db16, qa[BB == 18 ? 4 : 8], qb[BB == 18 ? 4 : 8], wa[8], wb[8];               \
-    tc::chunk_block<BB, BL>(rowa, da16, qa);                                                     \
-    tc::chunk_block<BB, BL>(rowb, db16, qb);                                                     \
-    block_words<WQ4>(qa, wa);                                                                    \
-    block_words<WQ4>(qb, wb);                                                                    \
-    block_pair_tokens<WQ4, TT>(wa, wb, f16_bits_to_f32(da16), f16_bits_to_f32(db16),             \
-                               bt + (BL) * GB, sc + (BL) * TT, nj, acc_a, acc_b);                \
+          const uint8_t* row = src + c * (kKC * BB);  // gate rows 0..63, then up rows
+#define MRML_GV_BLOCK(BL)                                                                     \
+  {                                                                                           \
+    uint32_t d16, q[BB == 18 ? 4 : 8], w[8];                                                  \
+    tc::chunk_block<BB, BL>(row, d16, q);                                                     \
+    block_words<WQ4>(q, w);                                                                   \
+    block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + (BL) * GB, sc + (BL) * TT, nj, acc); \
   }
           MRML_GV_BLOCK(0) MRML_GV_BLOCK(1) MRML_GV_BLOCK(2) MRML_GV_BLOCK(3)
           MRML_GV_BLOCK(4) MRML_GV_BLOCK(5) MRML_GV_BLOCK(6) MRML_GV_BLOCK(7)
 #undef MRML_GV_BLOCK
         } else {
-          const uint8_t* rowa = src + (size_t)r * P.row_bytes;
-          const uint8_t* rowb = src + (size_t)(RG + r) * P.row_bytes;
+          const uint8_t* row = src + (size_t)c * P.row_bytes;
           for (int b = 0; b < P.nb; ++b) {
-            uint32_t wa[8], wb[8];
-            uint32_t da16, db16;
+            uint32_t w[8];
+            uint32_t d16;
             if constexpr (WQ4) {
-              const Q4Block qa = load_q4_block(rowa + b * 18);
-              const Q4Block qb = load_q4_block(rowb + b * 18);
-              da16 = qa.d16;
-              db16 = qb.d16;
-              block_words<1>(qa.qs, wa);
-              block_words<1>(qb.qs, wb);
+              const Q4Block q = load_q4_block(row + b * 18);
+              d16 = q.d16;
+              block_words<1>(q.qs, w);
             } else {
-              const Q8Block qa = load_q8_block(rowa + b * 34);
-              const Q8Block qb = load_q8_block(rowb + b * 34);
-              da16 = qa.d16;
-              db16 = qb.d16;
-              block_words<0>(qa.qs, wa);
-              block_words<0>(qb.qs, wb);
+              const Q8Block q = load_q8_block(row + b * 34);
+              d16 = q.d16;
+              block_words<0>(q.qs, w);
             }
-            block_pair_tokens<WQ4, TT>(wa, wb, f16_bits_to_f32(da16), f16_bits_to_f32(db16), bt + b * GB,
-                                       sc + b * TT, nj, acc_a, acc_b);
+            block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + b * GB, sc + b * TT, nj, acc);
           }
         }
         __syncwarp();
@@ -271,6 +264,26 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
       }
       if (!ok) break;
       if constexpr (MODE == kGateUp) {
+        const int r = c & (RG - 1);
+        if (up_row) {
+          // Hand the up sums to the gate threads (bounded waits: a wait
+          // that gives up raises the CTA's abort flag).
+          if (!(ok = wait_bar(&B->xch_empty, xph ^ 1, B, P.err))) break;
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+            if (t < nj) xch[t * RG + r] = acc[t];
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&B->xch_full);
+          xph ^= 1;
+          continue;
+        }
+        if (!(ok = wait_bar(&B->xch_full, xph, B, P.err))) break;
+        float upv[TT];
+#pragma unroll
+        for (int t = 0; t < TT; ++t) upv[t] = t < nj ? xch[t * RG + r] : 0.f;
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&B->xch_empty);
+        xph ^= 1;
         // act = gelu(gate) * up (ops.rs:99-114), then the down product's
         // Q8_0 re-quantisation (quant.rs:193-228): a warp's 32 lanes hold the
         // 32 elements of one act block.
@@ -279,7 +292,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
 #pragma unroll
           for (int t = 0; t < TT; ++t) {
             if (t < nj) {
-              const float v = __fmul_rn(gelu_approx(acc_a[t]), acc_b[t]);
+              const float v = __fmul_rn(gelu_approx(acc[t]), upv[t]);
               float amax = fabsf(v);
               if (!(amax > 0.f)) amax = 0.f;
 #pragma unroll
@@ -307,13 +320,11 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
           }
         }
       } else {
-        const int ra = m0 + r, rb = m0 + RG + r;
+        const int ra = m0 + c;
+        if (ra < P.rows) {
 #pragma unroll
-        for (int t = 0; t < TT; ++t) {
-          if (t < nj) {
-            if (ra < P.rows) P.y[(size_t)(p0 + t) * P.rows + ra] = acc_a[t];
-            if (rb < P.rows) P.y[(size_t)(p0 + t) * P.rows + rb] = acc_b[t];
-          }
+          for (int t = 0; t < TT; ++t)
+            if (t < nj) P.y[(size_t)(p0 + t) * P.rows + ra] = acc[t];
         }
       }
     }
@@ -347,6 +358,7 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
   const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb : 2 * kGvRowsGateUp * row_bytes;
   p.raw_bytes = (raw1 + 1023) & ~1023;
   const int bs_stage = p.kcb * (256 + kGvTokens * 8);
+  const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * kGvRowsGateUp * 4 : 0;
   // With many units, as many CTAs per SM as fit with a double-buffered weight
   // ring (4 at most); with few units, one CTA and the deepest ring that fits.
   const int per_sm_max = g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? 5 : 1);
@@ -358,7 +370,7 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
     const int rs_max = g_gv_ring > 0 ? g_gv_ring : tc::kMaxRaw;
     for (int rs = rs_max; rs >= rs_min; --rs)
       for (int bs = 2; bs >= 1; --bs) {
-        const size_t total = 2048 + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage;
+        const size_t total = 128 + 1024 + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage + xch_bytes;
         if (total <= budget) {
           p.rs = rs;
           p.bs = bs;

@@ -53,6 +53,7 @@ struct __align__(8) Bars {
   uint64_t dw_full[kMaxRing], dw_empty[kMaxRing];       // weight-scale ring, one slot per TMEM slot
   uint64_t bs_full[4], bs_empty[4];
   uint64_t tmem_full[kMaxRing], tmem_empty[kMaxRing];
+  uint64_t xch_full, xch_empty;  // gate/up row exchange of the CUDA-core kernel
   uint32_t tmem_base;
   int abort;
 };
