@@ -164,11 +164,13 @@ int mrml_moe_quantize_q4_0(const float *src, uint8_t *dst, size_t n, mrml_stream
 
 /* Process-wide options.  MRML_OPTION_EXPERT_PATH selects how the expert
  * products run: 0 automatic (tcgen05 tensor cores once experts see more than
- * 16 tokens on average, else the pipelined CUDA-core dp4a kernels),
- * 1 pipelined CUDA-core kernels, 2 tensor cores, 3 the general CUDA-core
- * kernels (any H, I multiple of 32; used automatically when H is not a
- * multiple of 256).  All paths give bit-identical results; the option exists
- * for tests and benchmarks. */
+ * 16 tokens on average, the pipelined decode kernel with warp-level MMA from
+ * 2 tokens per expert, else the same kernel with dp4a dots),
+ * 1 pipelined decode kernel with dp4a, 2 tensor cores, 3 the general
+ * CUDA-core kernels (any H, I multiple of 32; used automatically when H is
+ * not a multiple of 256), 4 pipelined decode kernel with warp-level MMA.
+ * All paths give bit-identical results; the option exists for tests and
+ * benchmarks. */
 enum { MRML_OPTION_EXPERT_PATH = 1 };
 /* Tuning of the decode (CUDA-core) expert kernel: CTAs per SM (1..8) and
  * the depth of its weight ring (1..8); 0 restores the automatic choice. */

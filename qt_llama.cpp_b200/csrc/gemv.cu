@@ -101,12 +101,95 @@ __device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, c
   }
 }
 
+// ---------------------------------------------------- warp-level MMA path
+// For units with several tokens, the integer block dots run on the tensor
+// cores through mma.sync m16n8k32 (A = 16 weight rows x one 32-element
+// quant block, B = the block's activations of the unit's 8 positions),
+// which replaces 8 dp4a per (row, token, block) by one instruction per
+// 16 rows x 8 tokens.  The accumulator is seeded with the same correction
+// word as the dp4a chain (magic, and -8*sum(a) for Q4_0's unsigned
+// nibbles), so D holds the bits of 1.5*2^23 + isum exactly, and the f32
+// chain that follows is the reference's, element by element.
+//
+// Fragment layouts (PTX ISA, mma.m16n8k32 with 8-bit operands), lane =
+// 4*g + t: a0/a2 = row g, elements 4t..4t+3 / 16+4t..; a1/a3 = row g+8;
+// b0/b1 = position g, elements 4t.. / 16+4t..; d0,d1 = row g, positions
+// 2t, 2t+1; d2,d3 = row g+8.
+template <int WQ4>
+__device__ __forceinline__ void mma_block(uint32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                          uint32_t c0, uint32_t c1) {
+  if constexpr (WQ4)
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+  else
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+
+// A 32-bit word of shared memory at an address that is 4-byte aligned
+// (ODD) or 2 bytes past a 4-byte boundary.
+template <bool ALIGNED>
+__device__ __forceinline__ uint32_t lds_word(const uint8_t* p) {
+  if constexpr (ALIGNED) {
+    return *reinterpret_cast<const uint32_t*>(p);
+  } else {
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p - 2);
+    return __funnelshift_r(q[0], q[1], 16);
+  }
+}
+
+// Row fragment of one quant block for lane t: the low (elements 4t..) and
+// high (16+4t..) words as unsigned nibbles (Q4_0) or signed bytes (Q8_0).
+// A block's values start 2 bytes after its (2-byte aligned) start; blocks
+// with an odd index within a 4-byte aligned row have them 4-byte aligned.
+template <int WQ4, bool ODD>
+__device__ __forceinline__ void block_frag(const uint8_t* blk, int t, uint32_t& lo, uint32_t& hi) {
+  if constexpr (WQ4) {
+    const uint32_t w = lds_word<ODD>(blk + 2 + 4 * t);
+    lo = w & 0x0f0f0f0fu;
+    hi = (w >> 4) & 0x0f0f0f0fu;
+  } else {
+    lo = lds_word<ODD>(blk + 2 + 4 * t);
+    hi = lds_word<ODD>(blk + 18 + 4 * t);
+  }
+}
+
+// One quant block for the warp's two 16-row tiles (rows r0+16i+g, +8):
+//   acc[4i + 2h + k] += isum * (d_w(row) * d_a(2t + k))
+// grp: the block's activation group, s4: {d_a, corr} of positions 2t, 2t+1.
+template <int WQ4, bool ODD>
+__device__ __forceinline__ void mma_block_rows(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
+                                               const int4 s4, int g, int t, float (&acc)[8]) {
+  const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + g * 16 + 4 * t);
+  const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + 128 + g * 16 + 4 * t);
+  const float da0 = __int_as_float(s4.x), da1 = __int_as_float(s4.z);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint8_t* ra = row0 + (16 * i + g) * pitch + boff;
+    const uint8_t* rb = ra + 8 * pitch;
+    uint32_t a[4], d[4];
+    block_frag<WQ4, ODD>(ra, t, a[0], a[2]);
+    block_frag<WQ4, ODD>(rb, t, a[1], a[3]);
+    mma_block<WQ4>(d, a, b0, b1, (uint32_t)s4.y, (uint32_t)s4.w);
+    const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
+    const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
+    const float f0 = __fsub_rn(__uint_as_float(d[0]), kMagicF), f1 = __fsub_rn(__uint_as_float(d[1]), kMagicF);
+    const float f2 = __fsub_rn(__uint_as_float(d[2]), kMagicF), f3 = __fsub_rn(__uint_as_float(d[3]), kMagicF);
+    acc[4 * i + 0] = __fadd_rn(acc[4 * i + 0], __fmul_rn(f0, __fmul_rn(dwa, da0)));
+    acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], __fmul_rn(f1, __fmul_rn(dwa, da1)));
+    acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], __fmul_rn(f2, __fmul_rn(dwb, da0)));
+    acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], __fmul_rn(f3, __fmul_rn(dwb, da1)));
+  }
+}
+
 // Unit: kGvTokens (8) positions and 128 weight rows: for gate/up, gate rows
 // m0..m0+63 and the same up rows; for down, rows m0..m0+127.  Compute thread
 // c owns raw-tile row c.  Activations use the group-major layout
 // (common.cuh): a B stage is the unit's position group for the chunk's
 // blocks (256 bytes each, contiguous), then their scales (64 bytes each).
-template <int WQ4, int MODE>
+template <int WQ4, int MODE, int MMA>
 __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   constexpr int BB = WQ4 ? 18 : 34;
@@ -196,6 +279,141 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
             bsi = 0;
             bph ^= 1;
           }
+        }
+      }
+    }
+  } else if constexpr (MMA) {
+    // -------------------------------------------------- compute (mma.sync)
+    // Compute warp cw owns tile rows 32cw .. 32cw+31 (gate/up: warps 0-1 the
+    // gate rows, 2-3 the same up rows, lane for lane).
+    const int cw = warp - kComp0;
+    const int g = lane >> 2, t = lane & 3;
+    const bool up_warp = MODE == kGateUp && cw >= kCompWarps / 2;
+    int rs = 0, bsi = 0;
+    uint32_t rph = 0, bph = 0, xph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < n_units && ok && !tc::aborted(B); u += gridDim.x) {
+      const int4 U = P.units[u];
+      const int p0 = U.y, nvalid = U.z, m0 = U.w;
+      const int nj = min(TT, nvalid);
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int kc = 0; kc < nkc && ok; ++kc) {
+        if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
+        if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
+        const uint8_t* src = raw + rs * P.raw_bytes;
+        const uint8_t* bt = bsb + bsi * bs_stage;
+        const int4* sc4 = reinterpret_cast<const int4*>(bt + P.kcb * GB);  // [block][4] position pairs
+        if constexpr (MODE == kGateUp) {
+          const uint8_t* row0 = src + 32 * cw * (kKC * BB);
+#pragma unroll
+          for (int bl = 0; bl < kKC; bl += 2) {
+            mma_block_rows<WQ4, false>(row0, kKC * BB, bl * BB, bt + bl * GB, sc4[bl * 4 + t], g, t, acc);
+            mma_block_rows<WQ4, true>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, sc4[(bl + 1) * 4 + t], g,
+                                      t, acc);
+          }
+        } else {
+          const uint8_t* row0 = src + (size_t)(32 * cw) * P.row_bytes;
+#pragma unroll 1
+          for (int b = 0; b < P.nb; b += 2) {
+            mma_block_rows<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + t], g, t, acc);
+            mma_block_rows<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc4[(b + 1) * 4 + t], g,
+                                      t, acc);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&B->raw_empty[rs]);
+          tc::mbar_arrive(&B->bs_empty[bsi]);
+        }
+        if (++rs == P.rs) {
+          rs = 0;
+          rph ^= 1;
+        }
+        if (++bsi == P.bs) {
+          bsi = 0;
+          bph ^= 1;
+        }
+      }
+      if (!ok) break;
+      // acc[4i + 2h + k]: tile row 32cw + 16i + 8h + g, position p0 + 2t + k.
+      if constexpr (MODE == kGateUp) {
+        float* xw = xch + (cw & 1) * 8 * 32;  // [8][32 lanes] per gate/up warp pair
+        if (up_warp) {
+          if (!(ok = wait_bar(&B->xch_empty, xph ^ 1, B, P.err))) break;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xw[j * 32 + lane] = acc[j];
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&B->xch_full);
+          xph ^= 1;
+          continue;
+        }
+        if (!(ok = wait_bar(&B->xch_full, xph, B, P.err))) break;
+        float upv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) upv[j] = xw[j * 32 + lane];
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&B->xch_empty);
+        xph ^= 1;
+        // act = gelu(gate) * up (ops.rs:99-114) and the down product's Q8_0
+        // re-quantisation (quant.rs:193-228).  The warp's 32 rows are one act
+        // block; the 8 lanes with the same t hold its 32 values for
+        // positions 2t and 2t+1.
+        const int rbase = m0 + 32 * cw;
+        if (rbase < P.rows) {
+          const int blk = rbase >> 5;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int pj = 2 * t + k;
+            float v[4];
+            float amax = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              v[q] = __fmul_rn(gelu_approx(acc[2 * q + k]), upv[2 * q + k]);
+              float a = fabsf(v[q]);
+              if (!(a > 0.f)) a = 0.f;
+              amax = fmaxf(amax, a);
+            }
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float scale = __fdiv_rn(amax, 127.0f);
+            const uint32_t d16 = f32_to_f16_trunc(scale);
+            const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+            int qv[4], qsum = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float rq = round_half_away(__fmul_rn(v[q], id));
+              if (rq != rq) rq = 0.f;
+              rq = fminf(fmaxf(rq, -128.f), 127.f);
+              qv[q] = (int)rq;
+              qsum += qv[q];
+            }
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+            if (pj < nj) {
+              const int pos = p0 + pj;
+              uint8_t* dst = reinterpret_cast<uint8_t*>(P.out_q) + act_group_offset(true, blk, pos >> 3, P.out_nb, P.npad) +
+                             (pos & 7) * 16;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {  // element 16i + 8h + g of the block, q = 2i + h
+                const int e = 8 * q + g;
+                dst[(e >> 4) * 128 + (e & 15)] = (uint8_t)(int8_t)qv[q];
+              }
+              if (g == 0) {
+                const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
+                P.out_s[act_scale_index(true, blk, pos, P.out_nb, P.npad)] =
+                    make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int row = m0 + 32 * cw + 8 * (j >> 1) + g;  // 16i + 8h = 8 * (2i + h)
+          const int pj = 2 * t + (j & 1);
+          if (row < P.rows && pj < nj) P.y[(size_t)(p0 + pj) * P.rows + row] = acc[j];
         }
       }
     }
@@ -384,9 +602,9 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
   return p;
 }
 
-template <int WQ4, int MODE>
+template <int WQ4, int MODE, int MMA>
 cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, int grid, cudaStream_t s) {
-  auto kern = gv::moe_gemv_kernel<WQ4, MODE>;
+  auto kern = gv::moe_gemv_kernel<WQ4, MODE, MMA>;
   static int cache[16] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -415,7 +633,7 @@ bool gv_supported(int wtype, int H, int I) {
   return tc_map_available();
 }
 
-cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
+cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
                         const int2* bsc, const int4* units, const int* n_units, int max_units, int npad, int8_t* out_q,
                         int2* out_s, float* y, int* err, cudaStream_t s) {
   tc::Params P{};
@@ -457,9 +675,16 @@ cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int 
   P.kcb = pl.kcb;
   const int grid = std::max(1, std::min(pl.per_sm * sms, max_units));
   const bool q4 = wtype == kQ4_0;
+  if (mma) {
+    if (mode == tc::kGateUp)
+      return q4 ? gv_launch<1, tc::kGateUp, 1>(map, P, pl.smem, grid, s)
+                : gv_launch<0, tc::kGateUp, 1>(map, P, pl.smem, grid, s);
+    return q4 ? gv_launch<1, tc::kDown, 1>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kDown, 1>(map, P, pl.smem, grid, s);
+  }
   if (mode == tc::kGateUp)
-    return q4 ? gv_launch<1, tc::kGateUp>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kGateUp>(map, P, pl.smem, grid, s);
-  return q4 ? gv_launch<1, tc::kDown>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kDown>(map, P, pl.smem, grid, s);
+    return q4 ? gv_launch<1, tc::kGateUp, 0>(map, P, pl.smem, grid, s)
+              : gv_launch<0, tc::kGateUp, 0>(map, P, pl.smem, grid, s);
+  return q4 ? gv_launch<1, tc::kDown, 0>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kDown, 0>(map, P, pl.smem, grid, s);
 }
 
 }  // namespace mrml

@@ -37,7 +37,7 @@ constexpr int kGvTokens = 8;
 constexpr int kGvRowsGateUp = 64;
 bool gv_supported(int wtype, int H, int I);
 void gv_set_tuning(int per_sm, int ring);
-cudaError_t launch_gemv(int mode, int wtype, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
+cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
                         const int2* bsc, const int4* units, const int* n_units, int max_units, int npad, int8_t* out_q,
                         int2* out_s, float* y, int* err, cudaStream_t s);
 bool tc_supported(int wtype, int H, int I, int NT);

@@ -193,7 +193,7 @@ int run_router(const Workspace& w, const float* W, const float* x, float* logits
 // tokens (prefill); at decode sizes one MMA per quant block wastes most of
 // each MMA, and the pipelined dp4a kernel is faster.  Shapes outside both
 // kernels' limits (H not a multiple of 256) use the general dp4a kernels.
-enum Route { kRouteGeneral = 0, kRouteGemv = 1, kRouteTensor = 2 };
+enum Route { kRouteGeneral = 0, kRouteGemv = 1, kRouteTensor = 2, kRouteGemvMma = 3 };
 
 // `pairs` is the expected number of (token, slot) pairs this call computes:
 // T * K on one device, about T * K * E / e_total for an expert shard.
@@ -204,10 +204,14 @@ Route pick_route(int wtype, int H, int I, int E, long long pairs) {
     case 1: return gv ? kRouteGemv : kRouteGeneral;
     case 2: return tc ? kRouteTensor : (gv ? kRouteGemv : kRouteGeneral);
     case 3: return kRouteGeneral;
+    case 4: return gv ? kRouteGemvMma : kRouteGeneral;
     default: break;
   }
   if (tc && pairs > 16ll * E) return kRouteTensor;
-  return gv ? kRouteGemv : kRouteGeneral;
+  if (!gv) return kRouteGeneral;
+  // A warp-level MMA covers 8 positions whatever the count: worth it once
+  // experts see about two tokens or more.
+  return pairs >= 2ll * E ? kRouteGemvMma : kRouteGemv;
 }
 
 int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids,
@@ -216,8 +220,9 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
   if (e_total == 0) e_total = E;
   const long long pairs = (long long)T * K * E / e_total;
   const Route route = pick_route(wtype, H, I, E, pairs);
-  const int NT = route == kRouteGemv ? mrml::kGvTokens : (pairs > 12ll * E ? 64 : 16);
-  const int rows_gu = route == kRouteGemv ? mrml::kGvRowsGateUp : 128;
+  const bool gv = route == kRouteGemv || route == kRouteGemvMma;
+  const int NT = gv ? mrml::kGvTokens : (pairs > 12ll * E ? 64 : 16);
+  const int rows_gu = gv ? mrml::kGvRowsGateUp : 128;
   const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;  // down tiles: 128 rows on both paths
   int* n_units = w.status + 2;
   MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, e_first, e_total, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
@@ -229,16 +234,16 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
     MRML_LAUNCH(mrml::launch_down(wtype, down, w.cnt, w.poff, w.act, w.ydown, H, I, E, w.status, s));
   } else {
     const int mu_gu = units_bound(E, K, T, NT, I, rows_gu), mu_dn = units_bound(E, K, T, NT, H, 128);
-    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, route == kRouteGemv, w.xb, w.xs, s));
+    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, gv, w.xb, w.xs, s));
     if (route == kRouteTensor) {
       MRML_LAUNCH(mrml::launch_gemm_tc(0, wtype, NT, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu,
                                        w.npad, w.ab, w.as, nullptr, w.status, s));
       MRML_LAUNCH(mrml::launch_gemm_tc(1, wtype, NT, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn,
                                        w.npad, nullptr, nullptr, w.ydown, w.status, s));
     } else {
-      MRML_LAUNCH(mrml::launch_gemv(0, wtype, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad, w.ab,
+      MRML_LAUNCH(mrml::launch_gemv(0, wtype, route == kRouteGemvMma, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad, w.ab,
                                     w.as, nullptr, w.status, s));
-      MRML_LAUNCH(mrml::launch_gemv(1, wtype, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
+      MRML_LAUNCH(mrml::launch_gemv(1, wtype, route == kRouteGemvMma, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
                                     nullptr, nullptr, w.ydown, w.status, s));
     }
   }
@@ -377,7 +382,7 @@ int mrml_moe_set_option(int option, int value) {
   static int gv_per_sm = 0, gv_ring = 0;
   switch (option) {
     case MRML_OPTION_EXPERT_PATH:
-      if (value < 0 || value > 3) return MRML_ERR_INVALID_ARGUMENT;
+      if (value < 0 || value > 4) return MRML_ERR_INVALID_ARGUMENT;
       g_path = value;
       return MRML_OK;
     case MRML_OPTION_DECODE_CTAS_PER_SM:
