@@ -156,15 +156,41 @@ __device__ __forceinline__ void block_frag(const uint8_t* blk, int t, uint32_t& 
   }
 }
 
+// Packed f32x2 arithmetic (sm_100): two independent IEEE round-to-nearest
+// operations per instruction, lane for lane the scalar results.  Measured
+// on B200 with CUDA 12.9: a packed multiply whose result feeds a packed add
+// is contracted into a fused multiply-add despite the .rn modifiers, which
+// changes the rounding; a packed multiply followed by scalar add.rn is not.
+// So products are packed and the chain's additions stay scalar.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // One quant block for the warp's two 16-row tiles (rows r0+16i+g, +8):
 //   acc[4i + 2h + k] += isum * (d_w(row) * d_a(2t + k))
 // grp: the block's activation group, s4: {d_a, corr} of positions 2t, 2t+1.
 template <int WQ4, bool ODD>
-__device__ __forceinline__ void mma_block_rows(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
-                                               const int4 s4, int g, int t, float (&acc)[8]) {
+__device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
+                                                const int4 s4, int g, int t, float (&acc)[8]) {
   const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + g * 16 + 4 * t);
   const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + 128 + g * 16 + 4 * t);
-  const float da0 = __int_as_float(s4.x), da1 = __int_as_float(s4.z);
+  const uint64_t da = f2_pack(__int_as_float(s4.x), __int_as_float(s4.z));
+  const uint64_t magic = f2_pack(kMagicF, kMagicF);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const uint8_t* ra = row0 + (16 * i + g) * pitch + boff;
@@ -175,12 +201,15 @@ __device__ __forceinline__ void mma_block_rows(const uint8_t* row0, int pitch, i
     mma_block<WQ4>(d, a, b0, b1, (uint32_t)s4.y, (uint32_t)s4.w);
     const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
     const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
-    const float f0 = __fsub_rn(__uint_as_float(d[0]), kMagicF), f1 = __fsub_rn(__uint_as_float(d[1]), kMagicF);
-    const float f2 = __fsub_rn(__uint_as_float(d[2]), kMagicF), f3 = __fsub_rn(__uint_as_float(d[3]), kMagicF);
-    acc[4 * i + 0] = __fadd_rn(acc[4 * i + 0], __fmul_rn(f0, __fmul_rn(dwa, da0)));
-    acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], __fmul_rn(f1, __fmul_rn(dwa, da1)));
-    acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], __fmul_rn(f2, __fmul_rn(dwb, da0)));
-    acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], __fmul_rn(f3, __fmul_rn(dwb, da1)));
+    const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
+    const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
+    float p0, p1, p2, p3;
+    f2_unpack(f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), p0, p1);
+    f2_unpack(f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), p2, p3);
+    acc[4 * i + 0] = __fadd_rn(acc[4 * i + 0], p0);
+    acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], p1);
+    acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], p2);
+    acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], p3);
   }
 }
 
@@ -309,17 +338,17 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
           const uint8_t* row0 = src + 32 * cw * (kKC * BB);
 #pragma unroll
           for (int bl = 0; bl < kKC; bl += 2) {
-            mma_block_rows<WQ4, false>(row0, kKC * BB, bl * BB, bt + bl * GB, sc4[bl * 4 + t], g, t, acc);
-            mma_block_rows<WQ4, true>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, sc4[(bl + 1) * 4 + t], g,
-                                      t, acc);
+            mma_block_rows2<WQ4, false>(row0, kKC * BB, bl * BB, bt + bl * GB, sc4[bl * 4 + t], g, t, acc);
+            mma_block_rows2<WQ4, true>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, sc4[(bl + 1) * 4 + t], g,
+                                       t, acc);
           }
         } else {
           const uint8_t* row0 = src + (size_t)(32 * cw) * P.row_bytes;
 #pragma unroll 1
           for (int b = 0; b < P.nb; b += 2) {
-            mma_block_rows<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + t], g, t, acc);
-            mma_block_rows<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc4[(b + 1) * 4 + t], g,
-                                      t, acc);
+            mma_block_rows2<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + t], g, t, acc);
+            mma_block_rows2<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc4[(b + 1) * 4 + t], g,
+                                       t, acc);
           }
         }
         __syncwarp();
