@@ -445,16 +445,6 @@ def time_e2e(ls, steps, warmup, world):
     return ms, T * H * 4, T * H * 4
 
 
-def router_recomputed(ls, steps):
-    """Tokens whose top-k needed the exact sequential logits, over `steps`
-    eager steps (read from the workspace's counter)."""
-    ls.moe.device_status(ls.router_ws)
-    for i in range(steps):
-        ls.step(i)
-    st, rec = ls.moe.device_status(ls.router_ws)
-    return {"tokens": rec, "of": steps * ls.T, "status": st}
-
-
 def algorithmic_bytes(ls, unique, pairs):
     """Bytes the layer must move at minimum (weights of the experts hit once,
     router weights, activations in and out, routing outputs)."""
@@ -513,7 +503,6 @@ def run_ours(args):
     graphs = [ls.capture(g) for g in range(2 * ls.n_layers)]
     with ClockSampler(local) as clk:
         ms = time_steps(ls, steps, warmup, world, graphs)
-    recomputed = router_recomputed(ls, steps)
     del graphs
     kern = time_kernels(ls, steps)
     e2e_ms, h2d, d2h = time_e2e(ls, steps, warmup, world)
@@ -560,7 +549,6 @@ def run_ours(args):
         "e2e": {"value": round(world * T * steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": ls.n_kernels() * steps,
-        "router_exact_fallback_tokens": recomputed,
         "clocks": clk.summary(),
     }
     if world > 1:

@@ -78,9 +78,10 @@ int mrml_moe_workspace_init(void *workspace, size_t workspace_bytes, mrml_stream
  * experts (logit descending, ties to the lower id) and their renormalised
  * softmax weights ids[T][K], probs[T][K].
  * Replaces launch_rust_moe_router (cuda.rs:849-897), which always used K=8;
- * semantics of model.rs:1804-1829.  The ids equal the reference's sequential
- * f32 logits' ranking bit for bit; logits are within the reference's own
- * rounding error of it (exact for any expert whose rank was close). */
+ * semantics of model.rs:1804-1829.  Logits, ids and probs equal the
+ * reference CPU path's bit for bit (sequential f32 dot products, glibc's
+ * expf).  The workspace is only checked for size and may be shared with
+ * mrml_moe_experts. */
 int mrml_moe_router(const float *W, const float *x, float *logits, int32_t *ids, float *probs, int H, int E, int K,
                     int T, void *workspace, size_t workspace_bytes, mrml_stream_t stream);
 
@@ -90,12 +91,11 @@ int mrml_moe_router(const float *W, const float *x, float *logits, int32_t *ids,
  * a sandboxed or mediated GPU client that may launch work but not create
  * allocations, code that must not allocate on its latency path, or code
  * recording into a CUDA graph, where cudaMalloc cannot be captured.  This
- * entry point keeps the router's scratch (its per-token, per-expert error
- * bounds) in a fixed device array inside the library, so it allocates
- * nothing and needs no workspace argument; results equal mrml_moe_router's.
- * Limit: T * E <= 65536, otherwise MRML_ERR_UNSUPPORTED.  The array (about
- * 256 KiB) is held on every GPU that loads the library until the process
- * exits.  The first call on a device looks up the array's device address;
+ * entry point keeps the router's scratch in a fixed device array inside the
+ * library, so it allocates nothing and needs no workspace argument; results
+ * equal mrml_moe_router's.  Limit: T * E <= 65536, otherwise
+ * MRML_ERR_UNSUPPORTED.  The array (about 256 KiB) is held on every GPU that
+ * loads the library until the process exits.  The first call on a device looks up the array's device address;
  * make that first call before any stream capture.  All calls on a device
  * share the array (each call clears its counters first), so calls whose
  * kernels can overlap on the GPU, such as calls on unordered streams, race;
@@ -189,8 +189,9 @@ int mrml_moe_profile_events(void **events, int n_events);
 
 /* Synchronises `stream`, reads and clears the device status word of a
  * workspace: MRML_OK, MRML_ERR_DEVICE_TIMEOUT or MRML_ERR_BAD_EXPERT_ID.
- * *recomputed_tokens (may be NULL) receives how many router tokens needed
- * the exact sequential logit fallback since the last call.  Not capturable. */
+ * *recomputed_tokens (may be NULL) receives 0: the router computes every
+ * logit exactly and has no fallback to count (the argument is kept for
+ * binary compatibility).  Not capturable. */
 int mrml_moe_device_status(void *workspace, mrml_stream_t stream, int *recomputed_tokens);
 
 #ifdef __cplusplus

@@ -6,10 +6,9 @@
 
 namespace mrml {
 
-cudaError_t launch_router_logits(const float* W, const float* x, float* logits, float* bounds, int H, int E, int T,
-                                 int* err, cudaStream_t s);
-cudaError_t launch_router_topk(const float* W, const float* x, float* logits, const float* bounds, int32_t* ids,
-                               float* probs, int H, int E, int K, int T, int* status, cudaStream_t s);
+cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
+                                 cudaStream_t s);
+cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, int E, int K, int T, cudaStream_t s);
 cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
                                  cudaStream_t s);
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s);

@@ -64,11 +64,10 @@ int units_bound(int E, int K, int T, int NT, int rows, int rows_per_unit) {
 // Workspace regions (each 256-byte aligned), in order.  Positions are the
 // padded, expert-grouped order produced by the dispatch kernel.
 struct Workspace {
-  int* status;       // [0] device status word, [1] router recompute counter, [2..3] unit counts
+  int* status;       // [0] device status word, [1] reserved (0), [2..3] unit counts
   int8_t* xq;        // [T][H]        Q8_0 values of the layer input (CUDA-core path)
   float* xd;         // [T][H/32]     decoded Q8_0 scales
   int32_t* xsum;     // [T][H/32]     sums of the Q8_0 values per block
-  float* bounds;     // [T][E]        router error bounds
   int32_t* cnt;      // [E]           pairs per expert
   int32_t* poff;     // [E+1]         padded segment start per expert
   int32_t* pair_at;  // [npad]        pair at each position (-1 padding)
@@ -103,7 +102,6 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
   w.xq = reinterpret_cast<int8_t*>(take((size_t)T * H));
   w.xd = reinterpret_cast<float*>(take((size_t)T * nb * 4));
   w.xsum = reinterpret_cast<int32_t*>(take((size_t)T * nb * 4));
-  w.bounds = reinterpret_cast<float*>(take((size_t)T * E * 4));
   w.cnt = reinterpret_cast<int32_t*>(take((size_t)E * 4));
   w.poff = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
   w.pair_at = reinterpret_cast<int32_t*>(take((size_t)npad * 4));
@@ -184,8 +182,8 @@ int check_workspace(void* ws, size_t ws_bytes, int H, int I, int E, int K, int T
 
 int run_router(const Workspace& w, const float* W, const float* x, float* logits, int32_t* ids, float* probs, int H,
                int E, int K, int T, cudaStream_t s) {
-  MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, w.bounds, H, E, T, w.status, s));
-  MRML_LAUNCH(mrml::launch_router_topk(W, x, logits, w.bounds, ids, probs, H, E, K, T, w.status, s));
+  MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, H, E, T, w.status, s));
+  MRML_LAUNCH(mrml::launch_router_topk(logits, ids, probs, E, K, T, s));
   return MRML_OK;
 }
 
@@ -281,8 +279,9 @@ int mrml_moe_router(const float* W, const float* x, float* logits, int32_t* ids,
   MRML_TRY(check_router_args(W, x, logits, ids, probs, H, E, K, T));
   if (T == 0) return MRML_OK;
   MRML_TRY(check_device());
-  // The router needs only the status words and the bounds region; size the
-  // check with the smallest expert shape.
+  // The router itself uses no workspace memory; the size check keeps the
+  // documented contract (a workspace of mrml_moe_workspace_bytes for the
+  // smallest expert shape).
   MRML_TRY(check_workspace(workspace, workspace_bytes, 32, 32, E, K, T));
   const Workspace w = carve(workspace, 32, 32, E, K, T);
   return run_router(w, W, x, logits, ids, probs, H, E, K, T, (cudaStream_t)stream);
@@ -296,8 +295,7 @@ int mrml_moe_route_from_logits(const float* logits, int32_t* ids, float* probs, 
   if (!logits || !ids || !probs) return MRML_ERR_INVALID_ARGUMENT;
   MRML_TRY(check_device());
   const cudaStream_t s = (cudaStream_t)stream;
-  MRML_LAUNCH(mrml::launch_router_topk(nullptr, nullptr, const_cast<float*>(logits), nullptr, ids, probs, 0, E, K, T,
-                                       nullptr, s));
+  MRML_LAUNCH(mrml::launch_router_topk(logits, ids, probs, E, K, T, s));
   return MRML_OK;
 }
 

@@ -5,176 +5,201 @@
 // order; experts are sorted by logit descending (ties: lower expert id), the
 // first K are kept and p_k = expf(l_k - l_0) / max(sum_k, 1e-6).
 //
-// A sequential 2816-term f32 chain per (token, expert) is latency bound
-// (~6 us), so the GPU computes every logit in parallel and, with it, a
-// rigorous bound B on |reference value - our value|.  The top-K choice and
-// order are accepted only when every comparison that decides them is
-// separated by more than the two bounds.  The few experts whose intervals
-// overlap are then recomputed with the exact sequential chain, so the chosen
-// ids and their order always equal the reference's.
-//
-// Error bound.  For the sequential sum s^_n of the rounded products the
-// first-order bound is |s^_n - s_n| <= u*(sum_i |p_i| + sum_k |s^_k|), u =
-// 2^-24, and sum_k |s^_k| <= sum_k |s_k| + n*gamma_n*sum|p_i|.  Lane l of a
-// warp sums a contiguous chunk c of the row in f32; sum_k |s_k| over the
-// chunk is at most len_c*|S_c| + sum_{k in c} |r_k|, where S_c is the exact
-// prefix before the chunk (scanned in double from the chunk sums) and r_k the
-// lane's running sum.  Our own value carries at most u*(sum|p| + sum|r_k|).
+// The logits are computed exactly that way: one thread per (token, expert)
+// runs the reference's chain over the row.  A chain of H dependent f32 adds
+// takes about 4*H cycles (~6 us for H = 2816), and T*E chains run side by
+// side, so the logits, and with them the chosen ids, their order and the
+// softmax weights, equal the reference's bit for bit at every size.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace mrml {
 
-constexpr int kRouterWarps = 8;
-constexpr int kMaxCandidates = 64;  // also the largest supported K
+constexpr int kRT = 4;             // tokens per logits CTA (one warp each)
+constexpr int kRE = 32;            // experts per logits CTA (one lane each)
+constexpr int kRK = 256;           // row elements per staged chunk
+constexpr int kRPitch = kRK + 4;   // W chunk row pitch: lanes' float4 reads hit distinct banks
+constexpr int kRStages = 4;        // chunks in flight: a chunk's chain (~1000 cycles) is shorter than a copy
+constexpr int kMaxCandidates = 64;  // the largest supported K
 constexpr int kTopkWarps = 8;       // tokens per top-k CTA
-constexpr int kExactRows = 4;       // flagged expert rows staged per pass
 
-// Row pitch (floats) of the chunked layout: lane l owns elements
-// [l*C, l*C + C) of a row, stored at l*pitch; an odd pitch keeps the 32
-// lanes' reads of one chunk offset on 32 different banks.
-__host__ __device__ inline int chunk_len(int H) { return (H + 31) / 32; }
-__host__ __device__ inline int chunk_pitch(int H) { return chunk_len(H) | 1; }
-
-// Copies `rows` rows of length H (row stride H) into the chunked layout.
-// Each thread loads a batch of elements into registers before storing them,
-// so that the global loads of a batch are in flight together; the chunk
-// index and offset of element i advance incrementally.
-__device__ __forceinline__ void stage_chunked(float* dst, const float* __restrict__ src, int rows, int H) {
-  constexpr int kBatch = 16;
-  const int C = chunk_len(H), pitch = chunk_pitch(H), row_floats = 32 * pitch;
-  const int step = blockDim.x, dq = step / C, dr = step % C;
-  for (int r = 0; r < rows; ++r) {
-    const float* s = src + (size_t)r * H;
-    float* d = dst + r * row_floats;
-    int q = threadIdx.x / C, rem = threadIdx.x % C;
-    for (int i0 = threadIdx.x; i0 < H; i0 += step * kBatch) {
-      float v[kBatch];
-#pragma unroll
-      for (int k = 0; k < kBatch; ++k) {
-        const int i = i0 + k * step;
-        v[k] = i < H ? s[i] : 0.f;
+// grid (ceil(E / kRE), ceil(T / kRT)), block 32*kRT; lane l = expert e0 + l,
+// warp w = token t0 + w, one chain per thread.  Row chunks stream through a
+// ring of kRStages shared-memory buffers: Ws [kRE][kRPitch] (each lane reads
+// its own row) and Xs [kRT][kRK] (a warp reads one row, broadcast).
+// With `bulk` (H % 4 == 0, 16-byte aligned rows) thread 0 fills a stage with
+// one bulk copy per row, completing on the stage's mbarrier; otherwise the
+// CTA copies the chunk with plain loads.  Shared-memory reads bound the
+// kernel (each warp reads its CTA's W chunk), so the CTA keeps few warps and
+// the grid spreads over the SMs.
+__global__ void __launch_bounds__(32 * kRT)
+    router_logits_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits, int H,
+                         int E, int T, int bulk, int* __restrict__ err) {
+  extern __shared__ __align__(16) float rsm[];
+  __shared__ __align__(8) uint64_t full[kRStages];
+  float* Ws = rsm;                             // [kRStages][kRE][kRPitch]
+  float* Xs = rsm + kRStages * kRE * kRPitch;  // [kRStages][kRT][kRK]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e0 = blockIdx.x * kRE, t0 = blockIdx.y * kRT;
+  const int ne = min(kRE, E - e0), nt = min(kRT, T - t0);
+  const int nchunks = (H + kRK - 1) / kRK;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRStages; ++i) mbar_init(&full[i], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // Warp 0 fills a stage: lane 0 announces the bytes, then lane r copies
+  // W row r and x row r, so the copies of a chunk issue together.
+  auto issue = [&](int c) {
+    const int st = c % kRStages, k0 = c * kRK, len = min(kRK, H - k0);
+    if (lane == 0) mbar_arrive_expect_tx(&full[st], (uint32_t)((ne + nt) * len * 4));
+    __syncwarp();
+    if (lane < ne) bulk_g2s(Ws + (st * kRE + lane) * kRPitch, W + (size_t)(e0 + lane) * H + k0, len * 4, &full[st]);
+    if (lane < nt) bulk_g2s(Xs + (st * kRT + lane) * kRK, x + (size_t)(t0 + lane) * H + k0, len * 4, &full[st]);
+  };
+  bool ok = true;
+  if (bulk && warp == 0)
+    for (int c = 0; c < kRStages - 1 && c < nchunks; ++c) issue(c);
+  const bool active = warp < nt;  // warp-uniform
+  float acc = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const int st = c % kRStages, k0 = c * kRK, len = min(kRK, H - k0);
+    float* ws = Ws + st * kRE * kRPitch;
+    float* xs = Xs + st * kRT * kRK;
+    if (bulk) {
+      if (warp == 0 && __all_sync(0xffffffffu, ok) && c + kRStages - 1 < nchunks) issue(c + kRStages - 1);
+      // A wait that gives up records the error; the CTA then stops computing
+      // but keeps its barrier steps so that no thread is left waiting.
+      if (ok && !mbar_wait_bounded(&full[st], (uint32_t)(c / kRStages) & 1u, err)) ok = false;
+    } else {
+      for (int q = threadIdx.x; q < (ne + nt) * len; q += blockDim.x) {
+        const int r = q / len, i = q - r * len;
+        if (r < ne)
+          ws[r * kRPitch + i] = W[(size_t)(e0 + r) * H + k0 + i];
+        else
+          xs[(r - ne) * kRK + i] = x[(size_t)(t0 + r - ne) * H + k0 + i];
       }
+      __syncthreads();
+    }
+    if (active && ok) {
+      const float* wr = ws + lane * kRPitch;
+      const float* xr = xs + warp * kRK;
+      int i = 0;
+      if (len == kRK) {
+        // Loads of the next 32 elements are issued before the adds of the
+        // current 32, so the chain never waits on shared memory.
+        float4 xa[8], wa[8];
 #pragma unroll
-      for (int k = 0; k < kBatch; ++k) {
-        if (i0 + k * step < H) d[q * pitch + rem] = v[k];
-        q += dq;
-        rem += dr;
-        if (rem >= C) {
-          rem -= C;
-          ++q;
+        for (int q = 0; q < 8; ++q) {
+          xa[q] = *reinterpret_cast<const float4*>(xr + 4 * q);
+          wa[q] = *reinterpret_cast<const float4*>(wr + 4 * q);
         }
+#pragma unroll 1
+        for (; i < kRK; i += 32) {
+          float4 xb[8], wb[8];
+          const int nx = i + 32 < kRK ? i + 32 : i;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            xb[q] = *reinterpret_cast<const float4*>(xr + nx + 4 * q);
+            wb[q] = *reinterpret_cast<const float4*>(wr + nx + 4 * q);
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            acc = __fadd_rn(acc, __fmul_rn(xa[q].x, wa[q].x));
+            acc = __fadd_rn(acc, __fmul_rn(xa[q].y, wa[q].y));
+            acc = __fadd_rn(acc, __fmul_rn(xa[q].z, wa[q].z));
+            acc = __fadd_rn(acc, __fmul_rn(xa[q].w, wa[q].w));
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            xa[q] = xb[q];
+            wa[q] = wb[q];
+          }
+        }
+      } else {
+        for (; i < len; ++i) acc = __fadd_rn(acc, __fmul_rn(xr[i], wr[i]));
       }
     }
+    __syncthreads();  // the stage is refilled in the next iteration
   }
+  if (!ok && bulk && threadIdx.x == 0) {
+    // Let copies still in flight land before the CTA exits.
+    for (int c = 0; c < nchunks; ++c) mbar_wait_bounded(&full[c % kRStages], (uint32_t)(c / kRStages) & 1u, err);
+  }
+  const int t = t0 + warp, e = e0 + lane;
+  if (ok && t < T && e < E) logits[(size_t)t * E + e] = acc;
 }
 
-// grid (ceil(E / epc), ceil(T / tpc)), block 32*kRouterWarps.  The CTA
-// stages tpc token rows of x and epc expert rows of W in shared memory,
-// then one warp per (token, expert) pair computes the logit and its error
-// bound; lane l owns the contiguous chunk [l*C, l*C + C) of the row.
-// With `bulk` (H % 128 == 0, 16-byte aligned rows) each row arrives by one
-// bulk copy into a dense layout (row pitch H) and lanes read float4s: the
-// 8 lanes of a quarter-warp then hit at most 2 requests per bank group.
-// Otherwise rows are staged by coalesced loads into a padded chunk layout.
-// Writes logits[t*E + e] and bounds[t*E + e].
-__global__ void __launch_bounds__(32 * kRouterWarps)
-    router_logits_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
-                         float* __restrict__ bounds, int H, int E, int T, int epc, int tpc, int bulk,
-                         int* __restrict__ err) {
-  extern __shared__ __align__(16) float rsm[];
-  __shared__ __align__(8) uint64_t bar;
-  const int C = chunk_len(H);
-  const int pitch = bulk ? C : chunk_pitch(H);  // lane chunk stride
-  const int row_floats = bulk ? H : 32 * pitch;
-  const int e0 = blockIdx.x * epc, t0 = blockIdx.y * tpc;
-  const int ne = min(epc, E - e0), nt = min(tpc, T - t0);
-  float* xs = rsm;                     // [tpc][row_floats]
-  float* ws = rsm + tpc * row_floats;  // [epc][row_floats]
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (bulk) {
-    if (threadIdx.x == 0) {
-      mbar_init(&bar, 1);
-      fence_barrier_init();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(&bar, (uint32_t)((nt + ne) * H * 4));
-      for (int r = 0; r < nt; ++r) bulk_g2s(xs + r * row_floats, x + (size_t)(t0 + r) * H, H * 4, &bar);
-      for (int r = 0; r < ne; ++r) bulk_g2s(ws + r * row_floats, W + (size_t)(e0 + r) * H, H * 4, &bar);
-    }
-    if (!mbar_wait_bounded(&bar, 0, err)) return;
-  } else {
-    stage_chunked(xs, x + (size_t)t0 * H, nt, H);
-    stage_chunked(ws, W + (size_t)e0 * H, ne, H);
-    __syncthreads();
-  }
+// Whole-row variant for rows that fit: the CTA (kRT warps = tokens, lanes
+// 0..kRE2-1 = experts) loads its kRE2 W rows and kRT x rows with one bulk
+// copy each, waits once, and runs the chains with register prefetch.  Row
+// pitch H + 4 floats keeps the lanes' float4 reads on distinct banks.
+constexpr int kRE2 = 16;
 
-  const int start = lane * C;
-  const int len = max(0, min(C, H - start));
-  const float u = 5.9604644775390625e-8f;  // 2^-24
-  for (int p = warp; p < ne * nt; p += kRouterWarps) {
-    const int el = p % ne, tl = p / ne;
-    const float* xl = xs + tl * row_floats + lane * pitch;
-    const float* wl = ws + el * row_floats + lane * pitch;
-    float r = 0.f, A = 0.f, P = 0.f;
-    if (bulk) {
-      for (int j = 0; j < len; j += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(xl + j);
-        const float4 b = *reinterpret_cast<const float4*>(wl + j);
-        const float p0 = __fmul_rn(a.x, b.x), p1 = __fmul_rn(a.y, b.y);
-        const float p2 = __fmul_rn(a.z, b.z), p3 = __fmul_rn(a.w, b.w);
-        r = __fadd_rn(r, p0);
-        A += fabsf(r);
-        r = __fadd_rn(r, p1);
-        A += fabsf(r);
-        r = __fadd_rn(r, p2);
-        A += fabsf(r);
-        r = __fadd_rn(r, p3);
-        A += fabsf(r);
-        P += (fabsf(p0) + fabsf(p1)) + (fabsf(p2) + fabsf(p3));
-      }
-    } else {
-#pragma unroll 4
-      for (int j = 0; j < len; ++j) {
-        const float prod = __fmul_rn(xl[j], wl[j]);
-        r = __fadd_rn(r, prod);
-        A += fabsf(r);
-        P += fabsf(prod);
-      }
-    }
-    // Exclusive prefix of the chunk sums, in double.
-    double incl = (double)r;
+__host__ __device__ inline size_t router_rows_smem(int H) {
+  return (size_t)(kRE2 + kRT) * (size_t)(H + 4) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(32 * kRT)
+    router_logits_rows_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
+                              int H, int E, int T, int* __restrict__ err) {
+  extern __shared__ __align__(16) float rsm[];
+  __shared__ __align__(8) uint64_t full;
+  const int pitch = H + 4;
+  float* Ws = rsm;                 // [kRE2][pitch]
+  float* Xs = rsm + kRE2 * pitch;  // [kRT][pitch]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e0 = blockIdx.x * kRE2, t0 = blockIdx.y * kRT;
+  const int ne = min(kRE2, E - e0), nt = min(kRT, T - t0);
+  if (threadIdx.x == 0) {
+    mbar_init(&full, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) mbar_arrive_expect_tx(&full, (uint32_t)((ne + nt) * H * 4));
+    __syncwarp();
+    if (lane < ne) bulk_g2s(Ws + lane * pitch, W + (size_t)(e0 + lane) * H, H * 4, &full);
+    if (lane < nt) bulk_g2s(Xs + lane * pitch, x + (size_t)(t0 + lane) * H, H * 4, &full);
+  }
+  if (!mbar_wait_bounded(&full, 0, err)) {
+    if (threadIdx.x == 0) mbar_wait_bounded(&full, 0, err);  // let copies in flight land
+    return;
+  }
+  if (warp >= nt || lane >= ne) return;
+  const float* wr = Ws + lane * pitch;
+  const float* xr = Xs + warp * pitch;
+  float acc = 0.f;
+  float4 xa[8], wa[8];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const double excl = incl - (double)r;
-    const double total = __shfl_sync(0xffffffffu, incl, 31);
-    float s_part = (float)len * (float)fabs(excl) + A;
-    float a_part = A;
-    float p_part = P;
+  for (int q = 0; q < 8; ++q) {
+    xa[q] = *reinterpret_cast<const float4*>(xr + 4 * q);
+    wa[q] = *reinterpret_cast<const float4*>(wr + 4 * q);
+  }
+  // H is a multiple of 32 here.
+#pragma unroll 1
+  for (int i = 0; i < H; i += 32) {
+    float4 xb[8], wb[8];
+    const int nx = i + 32 < H ? i + 32 : i;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      s_part += __shfl_xor_sync(0xffffffffu, s_part, o);
-      a_part += __shfl_xor_sync(0xffffffffu, a_part, o);
-      p_part += __shfl_xor_sync(0xffffffffu, p_part, o);
+    for (int q = 0; q < 8; ++q) {
+      xb[q] = *reinterpret_cast<const float4*>(xr + nx + 4 * q);
+      wb[q] = *reinterpret_cast<const float4*>(wr + nx + 4 * q);
     }
-    if (lane == 0) {
-      const float center = (float)total;
-      const float n = (float)H;
-      const float gamma = n * u / (1.f - n * u);
-      // The bound's own f32 sums carry relative errors of at most n*u; the
-      // 1.01 factors cover them.
-      float B = u * (2.f * p_part + s_part + a_part) * 1.01f + n * gamma * u * p_part * 1.01f;
-      // Slack for rounding the center to f32 and for the f32 comparisons of
-      // c - B against c' + B' made by the top-k kernel.
-      B += 4.f * fabsf(center) * u + fabsf((float)(total - (double)center)) + 1e-30f;
-      logits[(size_t)(t0 + tl) * E + e0 + el] = center;
-      bounds[(size_t)(t0 + tl) * E + e0 + el] = B;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      acc = __fadd_rn(acc, __fmul_rn(xa[q].x, wa[q].x));
+      acc = __fadd_rn(acc, __fmul_rn(xa[q].y, wa[q].y));
+      acc = __fadd_rn(acc, __fmul_rn(xa[q].z, wa[q].z));
+      acc = __fadd_rn(acc, __fmul_rn(xa[q].w, wa[q].w));
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      xa[q] = xb[q];
+      wa[q] = wb[q];
     }
   }
+  logits[(size_t)(t0 + warp) * E + e0 + lane] = acc;
 }
 
 // (value desc, id asc) ordering used by the reference's GPU top-8
@@ -219,39 +244,6 @@ __device__ __forceinline__ void warp_topk(const float (&val)[PL], int E, int K, 
   __syncwarp();
 }
 
-// The reference's exact value of one logit: sequential f32, mul then add,
-// over rows staged in shared memory (vector loads when H % 4 == 0; the order
-// of the additions is the reference's either way).
-__device__ __forceinline__ float exact_logit_smem(const float* __restrict__ xs, const float* __restrict__ ws, int H) {
-  float dot = 0.f;
-  int i = 0;
-  if ((H & 3) == 0) {
-    // The chain is a dependent sequence of adds; unrolling lets the shared-
-    // memory loads run ahead of it.
-#pragma unroll 8
-    for (; i < H; i += 4) {
-      const float4 a = *reinterpret_cast<const float4*>(xs + i);
-      const float4 b = *reinterpret_cast<const float4*>(ws + i);
-      dot = __fadd_rn(dot, __fmul_rn(a.x, b.x));
-      dot = __fadd_rn(dot, __fmul_rn(a.y, b.y));
-      dot = __fadd_rn(dot, __fmul_rn(a.z, b.z));
-      dot = __fadd_rn(dot, __fmul_rn(a.w, b.w));
-    }
-  }
-  for (; i < H; ++i) dot = __fadd_rn(dot, __fmul_rn(xs[i], ws[i]));
-  return dot;
-}
-
-struct TopkShared {
-  int cand[kTopkWarps][kMaxCandidates];
-  float cval[kTopkWarps][kMaxCandidates];
-  float cbnd[kTopkWarps][kMaxCandidates];
-  int flag[kTopkWarps][kMaxCandidates];
-  int count[kTopkWarps];
-  int pending[kTopkWarps];  // warps of this CTA whose token needs exact values
-  int n_pending;
-};
-
 // Per-token selection tail: order Z (count candidates) by (value desc, id
 // asc), then the reference's softmax over the first K.
 __device__ void finish_token(int* cand, float* cval, int count, int K, int t, int32_t* ids, float* probs) {
@@ -290,180 +282,32 @@ __device__ void finish_token(int* cand, float* cval, int count, int K, int t, in
   __syncwarp();
 }
 
-// grid ceil(T / kTopkWarps), block 32*kTopkWarps; one warp per token.
-// bounds == nullptr: the logits are exact inputs (route-from-logits).
-// Otherwise W and x are the router weights and inputs the logits came from,
-// and the dynamic shared memory (router_exact_smem(H) bytes) stages the rows
-// of the exact fallback.  status[0] is the device status word, status[1]
-// counts tokens that needed the fallback (status may be null without bounds).
+struct TopkShared {
+  int cand[kTopkWarps][kMaxCandidates];
+  float cval[kTopkWarps][kMaxCandidates];
+};
+
+// grid ceil(T / kTopkWarps), block 32*kTopkWarps; one warp per token: the
+// K best experts of the token's logits (value desc, id asc) and their
+// softmax weights.
 template <int PL>
-__global__ void __launch_bounds__(32 * kTopkWarps, 1)
-    router_topk_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
-                       const float* __restrict__ bounds, int32_t* __restrict__ ids, float* __restrict__ probs, int H,
-                       int E, int K, int T, int* __restrict__ status) {
+__global__ void __launch_bounds__(32 * kTopkWarps)
+    router_topk_kernel(const float* __restrict__ logits, int32_t* __restrict__ ids, float* __restrict__ probs, int E,
+                       int K, int T) {
   __shared__ TopkShared S;
-  int* stats = status ? status + 1 : nullptr;
-  extern __shared__ __align__(16) float stage[];
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int t = blockIdx.x * kTopkWarps + wl;
-  if (threadIdx.x == 0) S.n_pending = 0;
-  __syncthreads();
-  int* cand = S.cand[wl];
-  float* cval = S.cval[wl];
-  float* cbnd = S.cbnd[wl];
-  int* flag = S.flag[wl];
-  bool mine_pending = false;
-
-  if (t < T) {
-    float* lrow = logits + (size_t)t * E;
-    const float* brow = bounds ? bounds + (size_t)t * E : nullptr;
-    float val[PL];
-    float bnd[PL];
+  if (t >= T) return;
+  const float* lrow = logits + (size_t)t * E;
+  float val[PL];
 #pragma unroll
-    for (int m = 0; m < PL; ++m) {
-      const int e = lane + 32 * m;
-      val[m] = e < E ? lrow[e] : -INFINITY;
-      bnd[m] = (e < E && brow) ? brow[e] : 0.f;
-    }
-    uint32_t taken;
-    warp_topk<PL>(val, E, K, cand, cval, taken);
-    int count = K;
-    if (brow) {
-      float lowest_lo = INFINITY;
-#pragma unroll
-      for (int m = 0; m < PL; ++m)
-        if (taken >> m & 1u) lowest_lo = fminf(lowest_lo, val[m] - bnd[m]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) lowest_lo = fminf(lowest_lo, __shfl_xor_sync(0xffffffffu, lowest_lo, o));
-      // Bounds of the chosen experts, in the order of cand[].
-      for (int k = lane; k < K; k += 32) cbnd[k] = brow[cand[k]];
-      // Candidate set Z = chosen experts plus every expert whose upper bound
-      // reaches lowest_lo: every other expert is below all K chosen ones in
-      // the reference too, so the reference's top-K lies in Z.
-#pragma unroll
-      for (int m = 0; m < PL; ++m) {
-        const int e = lane + 32 * m;
-        const bool extra = e < E && !(taken >> m & 1u) && val[m] + bnd[m] >= lowest_lo;
-        const uint32_t mask = __ballot_sync(0xffffffffu, extra);
-        if (extra) {
-          const int slot = count + __popc(mask & ((1u << lane) - 1u));
-          if (slot < kMaxCandidates) {
-            cand[slot] = e;
-            cval[slot] = val[m];
-            cbnd[slot] = bnd[m];
-          }
-        }
-        count += __popc(mask);
-      }
-      __syncwarp();
-      bool any = false;
-      if (count <= kMaxCandidates) {
-        for (int i = lane; i < count; i += 32) {
-          const float ci = cval[i], bi_ = cbnd[i];
-          bool overlap = false;
-          for (int j = 0; j < count; ++j) {
-            if (j == i) continue;
-            const float cj = cval[j], bj = cbnd[j];
-            if (!(ci - bi_ > cj + bj || cj - bj > ci + bi_)) overlap = true;
-          }
-          flag[i] = overlap;
-          any |= overlap;
-        }
-      } else {
-        any = true;  // bounds too wide to certify: exact values for all
-      }
-      mine_pending = __any_sync(0xffffffffu, any);
-    }
-    if (lane == 0) S.count[wl] = count;
-    if (!mine_pending) finish_token(cand, cval, min(count, kMaxCandidates), K, t, ids, probs);
+  for (int m = 0; m < PL; ++m) {
+    const int e = lane + 32 * m;
+    val[m] = e < E ? lrow[e] : -INFINITY;
   }
-  if (lane == 0 && mine_pending) S.pending[atomicAdd(&S.n_pending, 1)] = wl;
-  __syncthreads();
-  const int n_pending = S.n_pending;
-  if (n_pending == 0) return;
-  if (threadIdx.x == 0 && stats) atomicAdd(stats, n_pending);
-
-  // Exact fallback, one pending token at a time: the CTA stages the token's
-  // x row and up to kExactRows flagged W rows (bulk copies when rows are
-  // 16-byte multiples, else coalesced loads), and one thread per row runs
-  // the reference's sequential chain.
-  const int pitch = (H + 3) & ~3;
-  float* xs = stage;
-  float* wsr = stage + pitch;
-  __shared__ __align__(8) uint64_t xbar;
-  const bool bulk = (H & 3) == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
-  uint32_t xph = 0;
-  if (threadIdx.x == 0) {
-    mbar_init(&xbar, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  for (int q = 0; q < n_pending; ++q) {
-    const int w = S.pending[q];
-    const int tq = blockIdx.x * kTopkWarps + w;
-    float* lrow = logits + (size_t)tq * E;
-    int count = S.count[w];
-    const bool all = count > kMaxCandidates;
-    int* qc = S.cand[w];
-    float* qv = S.cval[w];
-    int* qf = S.flag[w];
-    const int n_items = all ? E : count;
-    for (int base = 0; base < n_items; base += kExactRows) {
-      __syncthreads();
-      if (bulk) {
-        if (threadIdx.x == 0) {
-          int nrows = 0;
-          for (int r = 0; r < kExactRows; ++r) {
-            const int item = base + r;
-            if (item < n_items && (all || qf[item])) ++nrows;
-          }
-          mbar_arrive_expect_tx(&xbar, (uint32_t)((base == 0 ? 1 + nrows : nrows) * H * 4));
-          if (base == 0) bulk_g2s(xs, x + (size_t)tq * H, H * 4, &xbar);
-          for (int r = 0; r < kExactRows; ++r) {
-            const int item = base + r;
-            if (item >= n_items || !(all || qf[item])) continue;
-            bulk_g2s(wsr + r * pitch, W + (size_t)(all ? item : qc[item]) * H, H * 4, &xbar);
-          }
-        }
-        if (!mbar_wait_bounded(&xbar, xph, status)) return;
-        xph ^= 1;
-      } else {
-        if (base == 0)
-          for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[(size_t)tq * H + i];
-        for (int r = 0; r < kExactRows; ++r) {
-          const int item = base + r;
-          if (item >= n_items || !(all || qf[item])) continue;
-          const float* wrow = W + (size_t)(all ? item : qc[item]) * H;
-          for (int i = threadIdx.x; i < H; i += blockDim.x) wsr[r * pitch + i] = wrow[i];
-        }
-        __syncthreads();
-      }
-      if (threadIdx.x < kExactRows) {
-        const int item = base + threadIdx.x;
-        if (item < n_items && (all || qf[item])) {
-          const int e = all ? item : qc[item];
-          const float v = exact_logit_smem(xs, wsr + threadIdx.x * pitch, H);
-          lrow[e] = v;
-          if (!all) qv[item] = v;
-        }
-      }
-    }
-    __syncthreads();
-    if (wl == w) {
-      if (all) {
-        float val[PL];
-#pragma unroll
-        for (int m = 0; m < PL; ++m) {
-          const int e = lane + 32 * m;
-          val[m] = e < E ? lrow[e] : -INFINITY;
-        }
-        uint32_t taken;
-        warp_topk<PL>(val, E, K, qc, qv, taken);
-        count = K;
-      }
-      finish_token(qc, qv, count, K, tq, ids, probs);
-    }
-  }
+  uint32_t taken;
+  warp_topk<PL>(val, E, K, S.cand[wl], S.cval[wl], taken);
+  finish_token(S.cand[wl], S.cval[wl], K, K, t, ids, probs);
 }
 
 // ------------------------------------------------------------ launchers ---
@@ -483,40 +327,36 @@ cudaError_t ensure_smem(Kern k, size_t bytes, int* cache) {
   return st;
 }
 
-cudaError_t launch_router_logits(const float* W, const float* x, float* logits, float* bounds, int H, int E, int T,
-                                 int* err, cudaStream_t s) {
-  static int cache[16] = {0};
-  const int epc = T <= 4 ? 1 : 4;
-  const int tpc = T <= 4 ? T : 4;
-  const dim3 grid((E + epc - 1) / epc, (T + tpc - 1) / tpc);
-  const bool bulk = H % 128 == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
-  const size_t smem = (size_t)(epc + tpc) * (bulk ? (size_t)H : (size_t)32 * chunk_pitch(H)) * sizeof(float);
+cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
+                                 cudaStream_t s) {
+  static int cache[16] = {0}, cache_rows[16] = {0};
+  const bool aligned = (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
+  if (aligned && H % 32 == 0 && router_rows_smem(H) <= 227 * 1024) {
+    const dim3 grid((E + kRE2 - 1) / kRE2, (T + kRT - 1) / kRT);
+    const size_t smem = router_rows_smem(H);
+    cudaError_t st = ensure_smem(router_logits_rows_kernel, smem, cache_rows);
+    if (st != cudaSuccess) return st;
+    router_logits_rows_kernel<<<grid, 32 * kRT, smem, s>>>(W, x, logits, H, E, T, err);
+    return cudaPeekAtLastError();
+  }
+  const dim3 grid((E + kRE - 1) / kRE, (T + kRT - 1) / kRT);
+  const bool bulk = H % 4 == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
+  const size_t smem = (size_t)kRStages * (kRE * kRPitch + kRT * kRK) * sizeof(float);
   cudaError_t st = ensure_smem(router_logits_kernel, smem, cache);
   if (st != cudaSuccess) return st;
-  router_logits_kernel<<<grid, 32 * kRouterWarps, smem, s>>>(W, x, logits, bounds, H, E, T, epc, tpc, bulk ? 1 : 0,
-                                                             err);
+  router_logits_kernel<<<grid, 32 * kRT, smem, s>>>(W, x, logits, H, E, T, bulk ? 1 : 0, err);
   return cudaPeekAtLastError();
 }
 
-size_t router_exact_smem(int H) { return (size_t)((H + 3) & ~3) * (1 + kExactRows) * sizeof(float); }
-
-cudaError_t launch_router_topk(const float* W, const float* x, float* logits, const float* bounds, int32_t* ids,
-                               float* probs, int H, int E, int K, int T, int* status, cudaStream_t s) {
-  static int cache[3][16] = {{0}};
+cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, int E, int K, int T, cudaStream_t s) {
   const dim3 grid((T + kTopkWarps - 1) / kTopkWarps);
   const int block = 32 * kTopkWarps;
-  const size_t smem = bounds ? router_exact_smem(H) : 0;
-  cudaError_t st;
-  if (E <= 32) {
-    if ((st = ensure_smem(router_topk_kernel<1>, smem, cache[0])) != cudaSuccess) return st;
-    router_topk_kernel<1><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, status);
-  } else if (E <= 128) {
-    if ((st = ensure_smem(router_topk_kernel<4>, smem, cache[1])) != cudaSuccess) return st;
-    router_topk_kernel<4><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, status);
-  } else {
-    if ((st = ensure_smem(router_topk_kernel<8>, smem, cache[2])) != cudaSuccess) return st;
-    router_topk_kernel<8><<<grid, block, smem, s>>>(W, x, logits, bounds, ids, probs, H, E, K, T, status);
-  }
+  if (E <= 32)
+    router_topk_kernel<1><<<grid, block, 0, s>>>(logits, ids, probs, E, K, T);
+  else if (E <= 128)
+    router_topk_kernel<4><<<grid, block, 0, s>>>(logits, ids, probs, E, K, T);
+  else
+    router_topk_kernel<8><<<grid, block, 0, s>>>(logits, ids, probs, E, K, T);
   return cudaPeekAtLastError();
 }
 

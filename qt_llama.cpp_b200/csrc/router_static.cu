@@ -1,21 +1,23 @@
 // router_static.cu — the router without a caller-supplied workspace.
 //
-// mrml_moe_router needs device scratch for its per-(token, expert) error
-// bounds, which the caller normally allocates once and passes in.  Some
-// callers cannot do that: a host that only holds buffers it was handed
-// (a sandboxed or mediated GPU client that may launch work but not create
-// allocations), code that must not allocate on its latency path, or a
-// caller recording work into a CUDA graph, where cudaMalloc is not a
-// capturable operation.  For them, mrml_moe_router_noalloc keeps that
-// scratch in a fixed, file-scope device array instead, so the call itself
-// allocates nothing.
+// mrml_moe_router takes a caller-allocated workspace.  Some callers cannot
+// provide one: a host that only holds buffers it was handed (a sandboxed or
+// mediated GPU client that may launch work but not create allocations),
+// code that must not allocate on its latency path, or a caller recording
+// work into a CUDA graph, where cudaMalloc is not a capturable operation.
+// For them, mrml_moe_router_noalloc keeps its scratch in a fixed, file-scope
+// device array instead, so the call itself allocates nothing.
 //
 // The array is g_router_scratch below: 256 bytes of status words followed by
-// room for kNoAllocMaxBounds floats, i.e. T * E <= 65536 (256 KiB).  Every
-// GPU that loads this library holds one copy of it until the process exits.
-// All calls on a device share that one copy, so calls whose kernels may
-// overlap on the GPU (different streams without ordering) race on it; calls
-// ordered on one stream are safe.
+// room for kNoAllocMaxBounds floats of per-(token, expert) scratch, which
+// fixes the entry point's limit T * E <= 65536.  The current router kernels
+// compute every logit with the reference's sequential chain and need no
+// per-pair scratch, so only the status words are touched (cleared on every
+// call); the limit and the footprint are kept as this entry point's
+// published contract.  Every GPU that loads this library holds one copy of
+// the array until the process exits.  All calls on a device share it, so
+// calls whose kernels may overlap on the GPU (different streams without
+// ordering) race on the status words; calls ordered on one stream are safe.
 #include <mutex>
 
 #include "../../include/mrml_moe.h"
@@ -66,11 +68,9 @@ extern "C" int mrml_moe_router_noalloc(const float* W, const float* x, float* lo
   if (st != MRML_OK) return st;
   const cudaStream_t s = (cudaStream_t)stream;
   int* status = reinterpret_cast<int*>(scratch);
-  float* bounds = scratch + kStatusFloats;
-  // The counter words keep the previous call's values: clear them.
+  // The status words keep the previous call's values: clear them.
   if (cudaMemsetAsync(status, 0, kStatusFloats * sizeof(float), s) != cudaSuccess) return MRML_ERR_CUDA;
-  if (mrml::launch_router_logits(W, x, logits, bounds, H, E, T, status, s) != cudaSuccess) return MRML_ERR_CUDA;
-  if (mrml::launch_router_topk(W, x, logits, bounds, ids, probs, H, E, K, T, status, s) != cudaSuccess)
-    return MRML_ERR_CUDA;
+  if (mrml::launch_router_logits(W, x, logits, H, E, T, status, s) != cudaSuccess) return MRML_ERR_CUDA;
+  if (mrml::launch_router_topk(logits, ids, probs, E, K, T, s) != cudaSuccess) return MRML_ERR_CUDA;
   return MRML_OK;
 }

@@ -209,7 +209,8 @@ def set_expert_path(path: int) -> None:
 
 
 def device_status(ws, stream=None):
-    """(status, recomputed_tokens); synchronises the stream."""
+    """(status, 0); synchronises the stream.  The second value is the
+    header's recomputed-token count, always 0 (the router is exact)."""
     lib = load_library()
     rec = ctypes.c_int(0)
     st = lib.mrml_moe_device_status(_ptr(ws), _stream_ptr(stream), ctypes.byref(rec))
