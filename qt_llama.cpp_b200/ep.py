@@ -68,6 +68,21 @@ class ExchangeBuffers:
         self.partial = torch.empty((n, H), dtype=torch.float32, device=device)
 
 
+def _all_gather_3(bufs: ExchangeBuffers, x, ids, probs, group) -> None:
+    """The three dispatch all-gathers, issued as one NCCL group (one launch)
+    where the backend supports coalescing, else one after another."""
+    cm = getattr(dist, "_coalescing_manager", None)
+    if cm is not None and x.is_cuda:
+        with cm(group=group, device=x.device):
+            dist.all_gather_into_tensor(bufs.x_all, x, group=group)
+            dist.all_gather_into_tensor(bufs.ids_all, ids, group=group)
+            dist.all_gather_into_tensor(bufs.probs_all, probs, group=group)
+        return
+    dist.all_gather_into_tensor(bufs.x_all, x, group=group)
+    dist.all_gather_into_tensor(bufs.ids_all, ids, group=group)
+    dist.all_gather_into_tensor(bufs.probs_all, probs, group=group)
+
+
 def ep_exchange(bufs: ExchangeBuffers, x_home: torch.Tensor, ids_home: torch.Tensor, probs_home: torch.Tensor,
                 shard_fn: ShardFn, out_home: torch.Tensor, group=None) -> torch.Tensor:
     """Steps 2-4 for this rank's routed home tokens; writes and returns
@@ -79,9 +94,7 @@ def ep_exchange(bufs: ExchangeBuffers, x_home: torch.Tensor, ids_home: torch.Ten
     if bufs.world == 1:
         shard_fn(x_home, ids_home, probs_home, out_home)
         return out_home
-    dist.all_gather_into_tensor(bufs.x_all, x_home.contiguous(), group=group)
-    dist.all_gather_into_tensor(bufs.ids_all, ids_home.contiguous(), group=group)
-    dist.all_gather_into_tensor(bufs.probs_all, probs_home.contiguous(), group=group)
+    _all_gather_3(bufs, x_home.contiguous(), ids_home.contiguous(), probs_home.contiguous(), group)
     shard_fn(bufs.x_all, bufs.ids_all, bufs.probs_all, bufs.partial)
     dist.reduce_scatter_tensor(out_home, bufs.partial, op=dist.ReduceOp.SUM, group=group)
     return out_home
