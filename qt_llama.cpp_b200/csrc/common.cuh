@@ -30,6 +30,12 @@ constexpr uint32_t kSpinLimit = 1u << 24;
 constexpr int32_t kMagicI = 0x4B400000;
 constexpr float kMagicF = 12582912.0f;
 
+// Programmatic dependent launch (launch_pdl): wait for the previous grid on
+// the stream (a no-op when launched without the attribute), and let the
+// next grid start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

@@ -57,6 +57,8 @@ __device__ __forceinline__ void quantize_block_warp(float v, int8_t* q_out, floa
 
 __global__ void quantize_rows_kernel(const float* __restrict__ x, int8_t* __restrict__ xq, float* __restrict__ xd,
                                      int32_t* __restrict__ xsum, long long n_blocks) {
+  pdl_trigger();
+  pdl_wait();
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps) {
     const float v = x[b * 32 + (threadIdx.x & 31)];
@@ -126,6 +128,8 @@ __global__ void __launch_bounds__(kDispatchThreads)
                     int e_first, int e_total, int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
                     int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
                     int* __restrict__ n_units, int NT, int mt_gu, int rows_gu, int mt_dn, int* __restrict__ err) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ int32_t dsm[];
   int32_t* cnt = dsm;            // [E] totals
   int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
@@ -252,6 +256,8 @@ template <int WQ4>
 __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32_t* __restrict__ pos, int T, int H,
                                         int K, int npad, int group_major, int8_t* __restrict__ bq,
                                         int2* __restrict__ bsc) {
+  pdl_trigger();
+  pdl_wait();
   const int nb = H / 32;
   const long long total = (long long)T * nb;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
@@ -374,6 +380,8 @@ __global__ void __launch_bounds__(kGateUpThreads)
                    const int32_t* __restrict__ poff, const int32_t* __restrict__ sorted,
                    const int8_t* __restrict__ xq, const float* __restrict__ xd, const int32_t* __restrict__ xsum,
                    float* __restrict__ act, int H, int I, int K, int tok_chunk, int* __restrict__ err) {
+  pdl_trigger();
+  pdl_wait();
   const int e = blockIdx.y, tile = blockIdx.x;
   const int beg = poff[e], n_e = cnt[e];
   if (n_e <= 0) return;
@@ -477,6 +485,8 @@ __global__ void __launch_bounds__(kDownThreads)
     down_kernel(const uint8_t* __restrict__ down, const int32_t* __restrict__ cnt, const int32_t* __restrict__ poff,
                 const float* __restrict__ act, float* __restrict__ ydown, int H, int I, int tok_chunk,
                 int* __restrict__ err) {
+  pdl_trigger();
+  pdl_wait();
   const int e = blockIdx.y, tile = blockIdx.x;
   const int beg = poff[e], n_e = cnt[e];
   if (n_e <= 0) return;
@@ -534,6 +544,8 @@ __global__ void __launch_bounds__(kDownThreads)
 __global__ void combine_kernel(const float* __restrict__ ydown, const int32_t* __restrict__ pos,
                                const int32_t* __restrict__ ids, const float* __restrict__ probs,
                                const float* __restrict__ down_scale, float* __restrict__ out, int H, int K, int T) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.y;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T || i >= H) return;
@@ -567,8 +579,7 @@ static int grid_for_blocks(long long warps_needed) {
 
 cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
                                  cudaStream_t s) {
-  quantize_rows_kernel<<<grid_for_blocks(n_blocks), 256, 0, s>>>(x, xq, xd, xsum, n_blocks);
-  return cudaPeekAtLastError();
+  return launch_pdl(quantize_rows_kernel, dim3(grid_for_blocks(n_blocks)), dim3(256), 0, s, x, xq, xd, xsum, n_blocks);
 }
 
 cudaError_t launch_geglu(const float* gate, const float* up, float* out, long long n, cudaStream_t s) {
@@ -595,9 +606,10 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
     cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
   }
-  dispatch_kernel<<<1, kDispatchThreads, smem, s>>>(ids, probs, n_pairs, E, e_first, e_total, cnt, poff, pair_at, pos,
-                                                     units_gu,
-                                                     units_dn, n_units, NT, mt_gu, rows_gu, mt_dn, err);
+  cudaError_t st = launch_pdl(dispatch_kernel, dim3(1), dim3(kDispatchThreads), smem, s, ids, probs, n_pairs, E, e_first,
+                              e_total, cnt, poff, pair_at, pos, units_gu, units_dn, n_units, NT, mt_gu, rows_gu, mt_dn,
+                              err);
+  if (st != cudaSuccess) return st;
   return cudaPeekAtLastError();
 }
 
@@ -606,10 +618,10 @@ cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* po
   const long long warps = (long long)T * (H / 32);
   const int gm = group_major ? 1 : 0;
   if (wtype == kQ4_0)
-    quantize_scatter_kernel<1><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, gm, bq, bsc);
-  else
-    quantize_scatter_kernel<0><<<grid_for_blocks(warps), 256, 0, s>>>(x, pos, T, H, K, npad, gm, bq, bsc);
-  return cudaPeekAtLastError();
+    return launch_pdl(quantize_scatter_kernel<1>, dim3(grid_for_blocks(warps)), dim3(256), 0, s, x, pos, T, H, K, npad,
+                      gm, bq, bsc);
+  return launch_pdl(quantize_scatter_kernel<0>, dim3(grid_for_blocks(warps)), dim3(256), 0, s, x, pos, T, H, K, npad, gm,
+                    bq, bsc);
 }
 
 constexpr size_t kMaxSmem = 227 * 1024;
@@ -666,8 +678,7 @@ cudaError_t launch_down(int wtype, const uint8_t* down, const int32_t* cnt, cons
 cudaError_t launch_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,
                            const float* down_scale, float* out, int H, int K, int T, cudaStream_t s) {
   const dim3 grid((H + 255) / 256, T);
-  combine_kernel<<<grid, 256, 0, s>>>(ydown, pos, ids, probs, down_scale, out, H, K, T);
-  return cudaPeekAtLastError();
+  return launch_pdl(combine_kernel, grid, dim3(256), 0, s, ydown, pos, ids, probs, down_scale, out, H, K, T);
 }
 
 }  // namespace mrml

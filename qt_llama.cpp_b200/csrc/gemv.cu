@@ -252,7 +252,9 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
     B->abort = 0;
     fence_barrier_init();
   }
+  pdl_trigger();
   __syncthreads();
+  pdl_wait();
   const int n_units = *P.n_units;
   const int nkc = MODE == kGateUp ? P.nb / kKC : 1;
 
@@ -642,8 +644,7 @@ cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, 
     if (st != cudaSuccess) return st;
     if (dev >= 0 && dev < 16) cache[dev] = (int)smem;
   }
-  kern<<<grid, 32 * (gv::kComp0 + gv::kCompWarps), smem, s>>>(map, P);
-  return cudaPeekAtLastError();
+  return launch_pdl(kern, dim3(grid), dim3(32 * (gv::kComp0 + gv::kCompWarps)), smem, s, map, P);
 }
 
 }  // namespace

@@ -6,6 +6,28 @@
 
 namespace mrml {
 
+// Launches `kern` with programmatic dependent launch: the grid may start
+// while the previous kernel on the stream finishes (its CTAs run their
+// prologue, then wait in pdl_wait() for the previous grid to complete and
+// its writes to be visible).  Every kernel of the library calls pdl_wait()
+// before its first read of anything an earlier kernel wrote, and
+// pdl_trigger() once its own CTAs are running.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
                                  cudaStream_t s);
 cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, int E, int K, int T, cudaStream_t s);

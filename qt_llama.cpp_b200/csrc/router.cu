@@ -43,11 +43,13 @@ __global__ void __launch_bounds__(32 * kRT)
   const int e0 = blockIdx.x * kRE, t0 = blockIdx.y * kRT;
   const int ne = min(kRE, E - e0), nt = min(kRT, T - t0);
   const int nchunks = (H + kRK - 1) / kRK;
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRStages; ++i) mbar_init(&full[i], 1);
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_wait();
   // Warp 0 fills a stage: lane 0 announces the bytes, then lane r copies
   // W row r and x row r, so the copies of a chunk issue together.
   auto issue = [&](int c) {
@@ -151,11 +153,13 @@ __global__ void __launch_bounds__(32 * kRT)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e0 = blockIdx.x * kRE2, t0 = blockIdx.y * kRT;
   const int ne = min(kRE2, E - e0), nt = min(kRT, T - t0);
+  pdl_trigger();
   if (threadIdx.x == 0) {
     mbar_init(&full, 1);
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_wait();
   if (warp == 0) {
     if (lane == 0) mbar_arrive_expect_tx(&full, (uint32_t)((ne + nt) * H * 4));
     __syncwarp();
@@ -295,6 +299,8 @@ __global__ void __launch_bounds__(32 * kTopkWarps)
     router_topk_kernel(const float* __restrict__ logits, int32_t* __restrict__ ids, float* __restrict__ probs, int E,
                        int K, int T) {
   __shared__ TopkShared S;
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   const int t = blockIdx.x * kTopkWarps + wl;
   if (t >= T) return;
@@ -336,28 +342,22 @@ cudaError_t launch_router_logits(const float* W, const float* x, float* logits, 
     const size_t smem = router_rows_smem(H);
     cudaError_t st = ensure_smem(router_logits_rows_kernel, smem, cache_rows);
     if (st != cudaSuccess) return st;
-    router_logits_rows_kernel<<<grid, 32 * kRT, smem, s>>>(W, x, logits, H, E, T, err);
-    return cudaPeekAtLastError();
+    return launch_pdl(router_logits_rows_kernel, grid, dim3(32 * kRT), smem, s, W, x, logits, H, E, T, err);
   }
   const dim3 grid((E + kRE - 1) / kRE, (T + kRT - 1) / kRT);
   const bool bulk = H % 4 == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
   const size_t smem = (size_t)kRStages * (kRE * kRPitch + kRT * kRK) * sizeof(float);
   cudaError_t st = ensure_smem(router_logits_kernel, smem, cache);
   if (st != cudaSuccess) return st;
-  router_logits_kernel<<<grid, 32 * kRT, smem, s>>>(W, x, logits, H, E, T, bulk ? 1 : 0, err);
-  return cudaPeekAtLastError();
+  return launch_pdl(router_logits_kernel, grid, dim3(32 * kRT), smem, s, W, x, logits, H, E, T, bulk ? 1 : 0, err);
 }
 
 cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, int E, int K, int T, cudaStream_t s) {
   const dim3 grid((T + kTopkWarps - 1) / kTopkWarps);
   const int block = 32 * kTopkWarps;
-  if (E <= 32)
-    router_topk_kernel<1><<<grid, block, 0, s>>>(logits, ids, probs, E, K, T);
-  else if (E <= 128)
-    router_topk_kernel<4><<<grid, block, 0, s>>>(logits, ids, probs, E, K, T);
-  else
-    router_topk_kernel<8><<<grid, block, 0, s>>>(logits, ids, probs, E, K, T);
-  return cudaPeekAtLastError();
+  if (E <= 32) return launch_pdl(router_topk_kernel<1>, grid, dim3(block), 0, s, logits, ids, probs, E, K, T);
+  if (E <= 128) return launch_pdl(router_topk_kernel<4>, grid, dim3(block), 0, s, logits, ids, probs, E, K, T);
+  return launch_pdl(router_topk_kernel<8>, grid, dim3(block), 0, s, logits, ids, probs, E, K, T);
 }
 
 }  // namespace mrml
