@@ -72,6 +72,8 @@ WORKLOADS = {
     "c2_t1": (2, 2816, 704, 128, 8, 1, "router"),
     "c3_prefill": (8, 1024, 512, 16, 2, 2048, "zipf_logits"),
     "c1_t4": (8, 1024, 512, 16, 2, 4, "router"),
+    "c2_t512": (2, 2816, 704, 128, 8, 512, "router"),
+    "c3_c2q8": (8, 2816, 704, 128, 8, 2048, "zipf_logits"),
     "c4": (2, 2816, 704, 128, 8, 8192, "router"),
     "c4_q8": (8, 2816, 704, 128, 8, 8192, "router"),
 }
@@ -492,6 +494,8 @@ def run_ours(args):
     moe, synth = package()
     device = torch.device("cuda", local)
     moe.load_library()
+    if args.expert_path:
+        moe.set_expert_path(args.expert_path)
     steps, warmup = args.steps, args.warmup
     hbm_peak, peak_kind = peaks()
 
@@ -675,6 +679,8 @@ def main():
     ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-also", action="store_true")
+    ap.add_argument("--expert-path", type=int, default=0,
+                    help="MRML_OPTION_EXPERT_PATH: 0 automatic, 1 decode dp4a, 2 tcgen05, 3 general, 4 decode MMA")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

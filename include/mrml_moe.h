@@ -163,9 +163,10 @@ int mrml_moe_quantize_q8_0(const float *src, uint8_t *dst, size_t n, mrml_stream
 int mrml_moe_quantize_q4_0(const float *src, uint8_t *dst, size_t n, mrml_stream_t stream);
 
 /* Process-wide options.  MRML_OPTION_EXPERT_PATH selects how the expert
- * products run: 0 automatic (tcgen05 tensor cores once experts see more than
- * 16 tokens on average, the pipelined decode kernel with warp-level MMA from
- * 2 tokens per expert, else the same kernel with dp4a dots),
+ * products run: 0 automatic (the pipelined kernel with warp-level MMA from 2
+ * tokens per expert, else the same kernel with dp4a dots; when that
+ * kernel's shape limits are not met (H a multiple of 256, I of 64), the
+ * general kernels, or tcgen05 above 16 tokens per expert),
  * 1 pipelined decode kernel with dp4a, 2 tensor cores, 3 the general
  * CUDA-core kernels (any H, I multiple of 32; used automatically when H is
  * not a multiple of 256), 4 pipelined decode kernel with warp-level MMA.

@@ -202,15 +202,30 @@ __global__ void __launch_bounds__(kDispatchThreads)
   __syncthreads();
   const int npos = poff[E];
   for (int i = tid; i < npos; i += blockDim.x) pair_at[i] = -1;
-  // Work units, one thread per expert: (row tile m, position tile j), j fastest.
-  for (int e = tid; e < E; e += blockDim.x) {
-    const int c = cnt[e], nt = (c + NT - 1) / NT;
-    for (int m = 0; m < mt_gu; ++m)
-      for (int j = 0; j < nt; ++j)
-        units_gu[ubase[e] * mt_gu + m * nt + j] = make_int4(e, poff[e] + j * NT, min(NT, c - j * NT), m * rows_gu);
-    for (int m = 0; m < mt_dn; ++m)
-      for (int j = 0; j < nt; ++j)
-        units_dn[ubase[e] * mt_dn + m * nt + j] = make_int4(e, poff[e] + j * NT, min(NT, c - j * NT), m * 128);
+  // Work units: expert e owns units [ubase[e]*mt, (ubase[e] + nt_e)*mt) of
+  // each product, ordered (row tile m, position tile j), j fastest.  One
+  // thread per unit; the unit's expert is the last e with ubase[e]*mt <= u
+  // (experts without pairs share their successor's base and come first).
+  // base[] still holds the segment starts here.
+  {
+    const int nu = ubase[E - 1] + (cnt[E - 1] + NT - 1) / NT;
+    for (int prod = 0; prod < 2; ++prod) {
+      const int mt = prod == 0 ? mt_gu : mt_dn, rows = prod == 0 ? rows_gu : 128;
+      int4* units = prod == 0 ? units_gu : units_dn;
+      for (int u = tid; u < nu * mt; u += blockDim.x) {
+        int lo = 0, hi = E - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (ubase[mid] * mt <= u)
+            lo = mid;
+          else
+            hi = mid - 1;
+        }
+        const int e = lo, c = cnt[e], nt = (c + NT - 1) / NT;
+        const int local = u - ubase[e] * mt, m = local / nt, j = local - m * nt;
+        units[u] = make_int4(e, base[e] + j * NT, min(NT, c - j * NT), m * rows);
+      }
+    }
   }
   __syncthreads();
   // Stable scatter, 1024 pairs at a time.
