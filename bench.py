@@ -266,7 +266,7 @@ class EPLayerSet:
     tokens and reduce-scatters the partial outputs (qt_llama.cpp_b200/ep.py).
     Same interface as LayerSet."""
 
-    def __init__(self, moe, synth, device, name, n_inputs, rank, world, seed=0):
+    def __init__(self, moe, synth, device, name, n_inputs, rank, world, seed=0, exchange="p2p"):
         import torch
 
         ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
@@ -277,7 +277,7 @@ class EPLayerSet:
         self.moe, self.device, self.name = moe, device, name
         self.wtype, self.H, self.I, self.E, self.K, self.T, self.routing = wtype, H, I, E, K, T, routing
         self.world, self.rank = world, rank
-        self.ep = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, device)
+        self.ep = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, device, exchange=exchange)
         first, count = self.ep.first, self.ep.count
         bb = 18 if wtype == 2 else 34
         layer_bytes = count * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
@@ -500,7 +500,7 @@ def run_ours(args):
     hbm_peak, peak_kind = peaks()
 
     if world > 1:
-        ls = EPLayerSet(moe, synth, device, args.workload, 8, rank, world)
+        ls = EPLayerSet(moe, synth, device, args.workload, 8, rank, world, exchange=args.ep_exchange)
     else:
         ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
     unique, pairs = ls.unique_experts(0)
@@ -534,7 +534,9 @@ def run_ours(args):
         "config": {"workload": args.workload, "hidden": ls.H, "experts": ls.E, "top_k": ls.K, "expert_ffn": ls.I,
                    "tokens_per_step": world * T, "home_tokens_per_rank": T,
                    "weights": "Q4_0" if ls.wtype == 2 else "Q8_0",
-                   "parallelism": f"ep{world} (experts sharded, NCCL all-gather + reduce-scatter)" if world > 1
+                   "parallelism": (f"ep{world} (experts sharded; " + ("peer-memory push over NVLink, library kernels"
+                                   if args.ep_exchange == "p2p" else "NCCL all-gather + reduce-scatter") + ")")
+                   if world > 1
                    else "single GPU",
                    "l2": f"inputs larger than L2: steps rotate over {ls.n_layers} layer copies "
                          f"({ls.n_layers * ls.layer_bytes / 1e6:.0f} MB of weights)",
@@ -589,8 +591,13 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        import gc
+
         import torch.distributed as dist
 
+        gc.collect()  # graphs first: they hold the exchange's launches
+        torch.cuda.synchronize()
+        ls.ep.close()
         dist.destroy_process_group()
 
 
@@ -679,6 +686,8 @@ def main():
     ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-also", action="store_true")
+    ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel exchange for --gpus N > 1")
     ap.add_argument("--expert-path", type=int, default=0,
                     help="MRML_OPTION_EXPERT_PATH: 0 automatic, 1 decode dp4a, 2 tcgen05, 3 general, 4 decode MMA")
     args = ap.parse_args()

@@ -135,6 +135,39 @@ int mrml_moe_experts_shard(int wtype, const uint8_t *gate_up, const uint8_t *dow
                            int E, int e_first, int e_count, int K, int T, void *workspace, size_t workspace_bytes,
                            mrml_stream_t stream);
 
+/* Expert-parallel exchange over NVLink peer memory (no counterpart in the
+ * reference, which runs on one device).  Each of the N ranks (one process
+ * per GPU) allocates one slab of mrml_moe_ep_slab_bytes(N, T, H, K) bytes
+ * with mrml_moe_ep_slab_alloc (set-up time; zeroed), shares its IPC handle
+ * (mrml_moe_ipc_get_handle, 64 bytes) with the other ranks, opens theirs
+ * (mrml_moe_ipc_open_handle) and keeps a device array `slabs` of the N slab
+ * pointers in rank order (its own allocation at its own index).  Per layer
+ * step, every rank calls, in this order on one stream:
+ *   mrml_moe_ep_dispatch: stores its T home rows x[T][H], ids and probs
+ *     [T][K] into every rank's slab and, once all ranks' rows of this step
+ *     have arrived, copies them to x_all [N*T][H], ids_all / probs_all
+ *     [N*T][K] (rank order);
+ *   (its experts, e.g. mrml_moe_experts_shard on those buffers, writing
+ *     partial [N*T][H]);
+ *   mrml_moe_ep_combine: stores the partial rows of each rank's tokens into
+ *     that rank's slab and, once all N partials of its own tokens have
+ *     arrived, writes out[T][H] = their sum in rank order.
+ * Waits are bounded; a wait that gives up writes MRML_ERR_DEVICE_TIMEOUT's
+ * device code into *status (a workspace's status word, read with
+ * mrml_moe_device_status) and leaves the outputs untouched.  All ranks must
+ * make the same calls with the same shapes; H % 4 == 0, N <= 16. */
+size_t mrml_moe_ep_slab_bytes(int N, int T, int H, int K);
+int mrml_moe_ep_slab_alloc(size_t bytes, void **slab);
+int mrml_moe_ep_slab_free(void *slab);
+int mrml_moe_ipc_get_handle(const void *slab, void *handle);
+int mrml_moe_ipc_open_handle(const void *handle, void **slab);
+int mrml_moe_ipc_close_handle(void *slab);
+int mrml_moe_ep_dispatch(void *const *slabs, int rank, int N, int T, int H, int K, const float *x, const int32_t *ids,
+                         const float *probs, float *x_all, int32_t *ids_all, float *probs_all, int *status,
+                         mrml_stream_t stream);
+int mrml_moe_ep_combine(void *const *slabs, int rank, int N, int T, int H, int K, const float *partial, float *out,
+                        int *status, mrml_stream_t stream);
+
 /* The whole layer: mrml_moe_router on (router_w, router_x) followed by
  * mrml_moe_experts on x.  router_x and x may be the same pointer. */
 int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, const float *x, const uint8_t *gate_up,

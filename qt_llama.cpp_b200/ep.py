@@ -15,13 +15,20 @@ One layer step on every rank:
 4. combine: reduce-scatter (sum) of the [P*T, H] partials, so that each rank
    receives the sum of the P partials of its own home tokens.
 
-Dispatch and combine are NCCL collectives through torch.distributed (gloo in
-the CPU tests).  Without a host round trip for per-peer counts, an
-all-to-all has to move fixed-capacity buffers, and a capacity of T rows per
-peer is exactly what the all-gather moves; the all-gather / reduce-scatter
-pair is also NCCL's best-tuned form of that exchange (NVLink SHARP in the
-switch when NCCL enables it) and needs no host synchronisation, so a whole
-step can be captured into one CUDA graph.
+Two implementations of steps 2 and 4 share the compute step:
+
+* "p2p" (default on GPUs, `PeerExchange`): the library's own kernels write
+  the home rows and the partials straight into the other GPUs' memory over
+  NVLink (CUDA IPC mappings of each rank's exchange slab) and signal with
+  system-scope counters (mrml_moe_ep_dispatch / mrml_moe_ep_combine); the
+  home rank sums the N partials of its tokens in rank order;
+* "nccl" (`ep_exchange`): all-gathers and a reduce-scatter through
+  torch.distributed (gloo in the CPU tests).  Without a host round trip for
+  per-peer counts, an all-to-all has to move fixed-capacity buffers, and a
+  capacity of T rows per peer is exactly what the all-gather moves.
+
+Neither needs host synchronisation, so a whole step can be captured into
+one CUDA graph.
 
 Numerics: each shard's partial is computed bit for bit as the single-device
 path computes it with the other experts' weights set to zero (the Q8_0
@@ -100,6 +107,52 @@ def ep_exchange(bufs: ExchangeBuffers, x_home: torch.Tensor, ids_home: torch.Ten
     return out_home
 
 
+class PeerExchange:
+    """This rank's exchange slab, the other ranks' slabs mapped over CUDA IPC,
+    and the contiguous buffers the experts read (mrml_moe_ep_dispatch /
+    mrml_moe_ep_combine).  Set-up is collective: every rank of `group`
+    constructs it with the same shapes.  close() is collective too."""
+
+    def __init__(self, moe, rank: int, world: int, T: int, H: int, K: int, device, status, group=None):
+        self.moe, self.rank, self.world, self.group = moe, rank, world, group
+        self.T, self.H, self.K = T, H, K
+        self.status = status  # int32 device word(s) that receive a timeout code
+        self.bufs = ExchangeBuffers(world, T, H, K, device)
+        self.own = moe.ep_slab_alloc(world, T, H, K)
+        handles = [None] * world
+        dist.all_gather_object(handles, moe.ipc_get_handle(self.own), group=group)
+        self.opened = []
+        ptrs = []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self.own)
+            else:
+                p = moe.ipc_open_handle(handles[r])
+                self.opened.append(p)
+                ptrs.append(p)
+        self.slabs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        dist.barrier(group=group)
+
+    def exchange(self, x_home, ids_home, probs_home, shard_fn: ShardFn, out_home):
+        m, b = self.moe, self.bufs
+        args = (self.slabs, self.rank, self.world, self.T, self.H, self.K)
+        m.ep_dispatch(*args, x_home, ids_home, probs_home, b.x_all, b.ids_all, b.probs_all, self.status)
+        shard_fn(b.x_all, b.ids_all, b.probs_all, b.partial)
+        m.ep_combine(*args, b.partial, out_home, self.status)
+        return out_home
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            self.moe.ipc_close_handle(p)
+        self.opened = []
+        dist.barrier(group=self.group)
+        if self.own:
+            self.moe.ep_slab_free(self.own)
+            self.own = 0
+
+
 class ExpertParallelLayer:
     """One MoE layer (router replicated, experts sharded) on this rank's GPU,
     through the library's C ABI.
@@ -108,16 +161,29 @@ class ExpertParallelLayer:
     layout of mrml_moe_experts; router_w is the full [E, H] router."""
 
     def __init__(self, moe, rank: int, world: int, wtype: int, H: int, I: int, E: int, K: int, T: int, device,
-                 group=None):
+                 group=None, exchange: str = "p2p"):
         self.moe, self.rank, self.world, self.group = moe, rank, world, group
         self.wtype, self.H, self.I, self.E, self.K, self.T = wtype, H, I, E, K, T
         self.first, self.count = shard_range(rank, world, E)
-        self.bufs = ExchangeBuffers(world, T, H, K, device)
         self.logits = torch.empty((T, E), dtype=torch.float32, device=device)
         self.ids = torch.empty((T, K), dtype=torch.int32, device=device)
         self.probs = torch.empty((T, K), dtype=torch.float32, device=device)
         self.router_ws = moe.new_workspace(H, I, E, K, T, device)
         self.ws = moe.new_workspace(H, I, self.count, K, world * T, device)
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.exchange = exchange if world > 1 else "nccl"
+        if self.exchange == "p2p":
+            self.peer = PeerExchange(moe, rank, world, T, H, K, device, self.ws, group)
+            self.bufs = self.peer.bufs
+        else:
+            self.peer = None
+            self.bufs = ExchangeBuffers(world, T, H, K, device)
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def forward(self, router_w, x_home, gate_up, down, out_home, down_scale: Optional[torch.Tensor] = None):
         m = self.moe
@@ -127,4 +193,6 @@ class ExpertParallelLayer:
             m.experts_shard(self.wtype, gate_up, down, ids, probs, down_scale, x, out, self.H, self.I, self.E,
                             self.first, self.count, self.K, x.shape[0], self.ws)
 
+        if self.peer is not None:
+            return self.peer.exchange(x_home, self.ids, self.probs, shard_fn, out_home)
         return ep_exchange(self.bufs, x_home, self.ids, self.probs, shard_fn, out_home, self.group)

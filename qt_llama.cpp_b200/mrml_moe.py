@@ -27,6 +27,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmrml_moe_b200.so")
 
 MRML_OK = 0
+MRML_ERR_INVALID_ARGUMENT = -1
 MRML_Q4_0 = 2
 MRML_Q8_0 = 8
 
@@ -51,6 +52,14 @@ SIGNATURES = {
     ),
     "mrml_moe_experts_shard": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz,
                                     _vp]),
+    "mrml_moe_ep_slab_bytes": (_sz, [_i, _i, _i, _i]),
+    "mrml_moe_ep_slab_alloc": (_i, [_sz, ctypes.POINTER(ctypes.c_void_p)]),
+    "mrml_moe_ep_slab_free": (_i, [_vp]),
+    "mrml_moe_ipc_get_handle": (_i, [_vp, _vp]),
+    "mrml_moe_ipc_open_handle": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "mrml_moe_ipc_close_handle": (_i, [_vp]),
+    "mrml_moe_ep_dispatch": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "mrml_moe_ep_combine": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "mrml_moe_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mrml_moe_geglu": (_i, [_vp, _vp, _vp, _sz, _vp]),
     "mrml_moe_quantize_q8_0": (_i, [_vp, _vp, _sz, _vp]),
@@ -176,6 +185,52 @@ def experts_shard(wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E,
                                    _ptr(out), H, I, E, e_first, e_count, K, T, _ptr(ws), ws.numel(),
                                    _stream_ptr(stream)),
     )
+
+
+def ep_slab_alloc(N: int, T: int, H: int, K: int) -> int:
+    """Allocates (set-up time) this rank's expert-parallel exchange slab."""
+    lib = load_library()
+    nbytes = lib.mrml_moe_ep_slab_bytes(N, T, H, K)
+    if nbytes == 0:
+        raise MoeError("mrml_moe_ep_slab_bytes", MRML_ERR_INVALID_ARGUMENT, "invalid argument")
+    p = ctypes.c_void_p()
+    _check("mrml_moe_ep_slab_alloc", lib.mrml_moe_ep_slab_alloc(nbytes, ctypes.byref(p)))
+    return p.value
+
+
+def ep_slab_free(ptr: int) -> None:
+    _check("mrml_moe_ep_slab_free", load_library().mrml_moe_ep_slab_free(ptr))
+
+
+def ipc_get_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(64)
+    _check("mrml_moe_ipc_get_handle", load_library().mrml_moe_ipc_get_handle(ptr, buf))
+    return bytes(buf.raw)
+
+
+def ipc_open_handle(handle: bytes) -> int:
+    p = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(handle, 64)
+    _check("mrml_moe_ipc_open_handle", load_library().mrml_moe_ipc_open_handle(buf, ctypes.byref(p)))
+    return p.value
+
+
+def ipc_close_handle(ptr: int) -> None:
+    _check("mrml_moe_ipc_close_handle", load_library().mrml_moe_ipc_close_handle(ptr))
+
+
+def ep_dispatch(slabs, rank, N, T, H, K, x, ids, probs, x_all, ids_all, probs_all, status, stream=None):
+    lib = load_library()
+    _check("mrml_moe_ep_dispatch",
+           lib.mrml_moe_ep_dispatch(_ptr(slabs), rank, N, T, H, K, _ptr(x), _ptr(ids), _ptr(probs), _ptr(x_all),
+                                    _ptr(ids_all), _ptr(probs_all), _ptr(status), _stream_ptr(stream)))
+
+
+def ep_combine(slabs, rank, N, T, H, K, partial, out, status, stream=None):
+    lib = load_library()
+    _check("mrml_moe_ep_combine",
+           lib.mrml_moe_ep_combine(_ptr(slabs), rank, N, T, H, K, _ptr(partial), _ptr(out), _ptr(status),
+                                   _stream_ptr(stream)))
 
 
 def combine(ydown, pos, ids, probs, down_scale, out, H, K, T, stream=None):

@@ -122,7 +122,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _ep_worker(rank, world, port, args, results):
+def _ep_worker(rank, world, port, args, exchange, results):
     import datetime
 
     import torch
@@ -134,66 +134,101 @@ def _ep_worker(rank, world, port, args, results):
     moe = _load("mrml_moe_b200", os.path.join(ROOT, "qt_llama.cpp_b200", "mrml_moe.py"))
     synth = _load("mrml_moe_b200_synth", os.path.join(ROOT, "qt_llama.cpp_b200", "synth.py"))
     ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
-    wtype, H, I, E, K, T, seed = args
+    wtype, H, I, E, K, T, seed, steps = args
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
+    layer = None
     try:
         gu, dn = synth.expert_weights_device(seed, wtype, H, I, E, dev, moe.quantize)
-        W = synth.normal(seed + 1000, E * H, 0.02).reshape(E, H)
-        x = synth.normal(seed + 77, world * T * H).reshape(world * T, H)
-        layer = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, dev)
+        W = dev_tensor(synth.normal(seed + 1000, E * H, 0.02).reshape(E, H), dev)
+        layer = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, dev, exchange=exchange)
         f, c = layer.first, layer.count
         gu_l = gu[f:f + c].contiguous()
         dn_l = dn[f:f + c].contiguous()
         del gu, dn
+        x_in = torch.empty((T, H), device=dev)
         out = torch.empty((T, H), device=dev)
-        layer.forward(dev_tensor(W, dev), dev_tensor(x[rank * T:(rank + 1) * T], dev), gu_l, dn_l, out)
-        torch.cuda.synchronize()
+        outs, idss = [], []
+        # The first half of the steps eager, the rest replayed from one CUDA
+        # graph with new inputs copied into its input buffer.
+        graph = None
+        for s in range(steps):
+            x = synth.normal(seed + 77 + s, world * T * H).reshape(world * T, H)
+            x_in.copy_(torch.from_numpy(x[rank * T:(rank + 1) * T]))
+            if s < steps // 2:
+                layer.forward(W, x_in, gu_l, dn_l, out)
+            else:
+                if graph is None:
+                    graph = torch.cuda.CUDAGraph()
+                    side = torch.cuda.Stream(device=dev)
+                    side.wait_stream(torch.cuda.current_stream())
+                    torch.cuda.synchronize()
+                    with torch.cuda.graph(graph, stream=side):
+                        layer.forward(W, x_in, gu_l, dn_l, out)
+                graph.replay()
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy().copy())
+            idss.append(layer.ids.cpu().numpy().copy())
+        del graph
         st, _ = moe.device_status(layer.ws)
-        results.put((rank, out.cpu().numpy(), layer.ids.cpu().numpy(), st))
+        results.put((rank, outs, idss, st))
     except Exception as exc:
         results.put((rank, repr(exc), None, None))
     finally:
+        if layer is not None:
+            try:
+                layer.close()
+            except Exception:
+                pass
         dist.destroy_process_group()
 
 
-def test_ep_layer_two_gpus(cuda, moe, oracle, synth):
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_ep_layer_two_gpus(cuda, moe, oracle, synth, exchange):
+    """Four consecutive layer steps (two eager, two replayed from a CUDA
+    graph) on 2 GPUs: every output equals the sum of the two shards'
+    partials bit for bit, and the reference within tolerance."""
     import multiprocessing as mp
 
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    world = 2
-    args = (2, 2816, 704, 128, 8, 32, 9)
-    wtype, H, I, E, K, T, seed = args
+    world, steps = 2, 4
+    args = (2, 2816, 704, 128, 8, 32, 9, steps)
+    wtype, H, I, E, K, T, seed, _ = args
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, args, q)) for r in range(world)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, args, exchange, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
     try:
         for _ in range(world):
-            r, out, ids, st = q.get(timeout=300)
-            assert not isinstance(out, str), f"rank {r}: {out}"
+            r, outs, idss, st = q.get(timeout=300)
+            assert not isinstance(outs, str), f"rank {r}: {outs}"
             assert st == 0
-            got[r] = (out, ids)
+            got[r] = (outs, idss)
     finally:
         for p in procs:
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    gu, dn, ids, probs, x = _gpu_case(synth, oracle, moe, cuda, wtype, H, I, E, K, world * T, seed)
-    ref = oracle.experts(wtype, gu, dn, ids, probs, None, x, H, I, E, K, world * T, os.cpu_count() or 1)
-    parts = [_shard_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, None, x, H, I, E, *synth_range(r, world, E), K)
-             for r in range(world)]
-    for r in range(world):
-        out, ids_home = got[r]
-        home = slice(r * T, (r + 1) * T)
-        np.testing.assert_array_equal(ids_home, ids[home])
-        np.testing.assert_array_equal(out, parts[0][home] + parts[1][home])
-        assert_close(out, ref[home])
+    gu_d, dn_d = synth.expert_weights_device(seed, wtype, H, I, E, cuda, moe.quantize)
+    gu, dn = gu_d.cpu().numpy(), dn_d.cpu().numpy()
+    W = synth.normal(seed + 1000, E * H, 0.02).reshape(E, H)
+    for s in range(steps):
+        x = synth.normal(seed + 77 + s, world * T * H).reshape(world * T, H)
+        _, ids, probs = oracle.router(W, x, H, E, K, world * T)
+        parts = [_shard_on_gpu(moe, cuda, wtype, gu, dn, ids, probs, None, x, H, I, E, *synth_range(r, world, E), K)
+                 for r in range(world)]
+        ref = oracle.experts(wtype, gu, dn, ids, probs, None, x, H, I, E, K, world * T, os.cpu_count() or 1)
+        for r in range(world):
+            outs, idss = got[r]
+            home = slice(r * T, (r + 1) * T)
+            np.testing.assert_array_equal(idss[s], ids[home])
+            np.testing.assert_array_equal(outs[s], parts[0][home] + parts[1][home])
+            assert_close(outs[s], ref[home])
