@@ -271,8 +271,11 @@ template <int WQ4>
 __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32_t* __restrict__ pos, int T, int H,
                                         int K, int npad, int group_major, int8_t* __restrict__ bq,
                                         int2* __restrict__ bsc) {
-  pdl_trigger();
+  // Waiting before triggering means that when the expert kernel that
+  // follows starts, the dispatch kernel before this one has completed, so
+  // that kernel may read its work units and stream weights right away.
   pdl_wait();
+  pdl_trigger();
   const int nb = H / 32;
   const long long total = (long long)T * nb;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);

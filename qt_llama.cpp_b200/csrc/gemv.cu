@@ -252,9 +252,14 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
     B->abort = 0;
     fence_barrier_init();
   }
+  // Programmatic dependent launch: the work units and the weights were
+  // complete before this grid started (the kernel before it waits for the
+  // dispatch before triggering this launch, and weights are never written),
+  // so the weight producer streams right away; only the activation producer
+  // waits for the previous kernel (whose output it reads), and the compute
+  // warps consume nothing that has not passed through it.
   pdl_trigger();
   __syncthreads();
-  pdl_wait();
   const int n_units = *P.n_units;
   const int nkc = MODE == kGateUp ? P.nb / kKC : 1;
 
@@ -290,6 +295,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
   } else if (warp == 1) {
     // ------------------------------------------------- activation producer
     if (lane == 0) {
+      pdl_wait();  // in every CTA, so the grid completes after its predecessor
       int bsi = 0;
       uint32_t bph = 0;
       for (int u = blockIdx.x; u < n_units && !tc::aborted(B); u += gridDim.x) {

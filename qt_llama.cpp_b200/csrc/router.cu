@@ -159,11 +159,13 @@ __global__ void __launch_bounds__(32 * kRT)
     fence_barrier_init();
   }
   __syncthreads();
-  pdl_wait();
   if (warp == 0) {
+    // The router weights are not written by earlier kernels: their copies
+    // start while the previous kernel finishes; the inputs wait for it.
     if (lane == 0) mbar_arrive_expect_tx(&full, (uint32_t)((ne + nt) * H * 4));
     __syncwarp();
     if (lane < ne) bulk_g2s(Ws + lane * pitch, W + (size_t)(e0 + lane) * H, H * 4, &full);
+    pdl_wait();
     if (lane < nt) bulk_g2s(Xs + lane * pitch, x + (size_t)(t0 + lane) * H, H * 4, &full);
   }
   if (!mbar_wait_bounded(&full, 0, err)) {
