@@ -334,6 +334,137 @@ class EPLayerSet:
         return (n - 1) * T * (H * 4 + K * 8) + (n - 1) * T * H * 4
 
 
+class StackSet:
+    """Config 5: a stack of 30 independent MoE layers of the config-2 shape
+    (Q4_0) with x_{l+1} = rms_norm(moe_l(x_l)) (weight 1, eps 1e-6; the norm
+    model.rs:2176-2196 applies after the MoE output), decode batch of 32
+    tokens in total.  With N > 1 every layer runs expert-parallel (T = 32/N
+    home tokens per rank), one exchange object shared by the 30 layers.
+    A step runs the whole stack; inputs are fresh N(0,1) batches."""
+
+    N_LAYERS = 30
+
+    def __init__(self, moe, synth, device, n_inputs, rank, world, exchange="p2p", seed=0):
+        import torch
+
+        ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
+        wtype, H, I, E, K = 2, 2816, 704, 128, 8
+        T = 32 // world
+        self.moe, self.device, self.name = moe, device, "c5"
+        self.wtype, self.H, self.I, self.E, self.K, self.T, self.routing = wtype, H, I, E, K, T, "router"
+        self.world = world
+        self.n_layers = 1  # graphs per input: one graph holds the whole stack
+        if world > 1:
+            self.ep = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, device, exchange=exchange)
+            first, count = self.ep.first, self.ep.count
+        else:
+            self.ep = None
+            first, count = 0, E
+            self.ws = moe.new_workspace(H, I, E, K, T, device)
+            self.logits = torch.empty(T, E, device=device)
+            self.ids = torch.empty(T, K, dtype=torch.int32, device=device)
+            self.probs = torch.empty(T, K, device=device)
+        self.layers = []
+        for l in range(self.N_LAYERS):
+            gu, dn = synth.expert_weights_device(seed * 1000 + 500 + l, wtype, H, I, E, device, moe.quantize)
+            if world > 1:
+                gu, dn = gu[first:first + count].clone(), dn[first:first + count].clone()
+                torch.cuda.empty_cache()
+            g = torch.Generator(device=device)
+            g.manual_seed(seed * 1000 + 900 + l)
+            W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
+            self.layers.append((gu, dn, W))
+        bb = 18
+        self.layer_bytes = count * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
+        g = torch.Generator(device=device)
+        g.manual_seed(seed + 77 + 1000 * rank)
+        self.xs = [torch.randn((T, H), generator=g, device=device) for _ in range(n_inputs)]
+        self.h = [torch.empty((T, H), device=device) for _ in range(2)]
+        self.moe_out = torch.empty((T, H), device=device)
+        self.out = torch.empty((T, H), device=device)
+
+    def step(self, i, x=None, out=None):
+        m, H, T = self.moe, self.H, self.T
+        h = self.xs[i % len(self.xs)] if x is None else x
+        out = self.out if out is None else out
+        for l, (gu, dn, W) in enumerate(self.layers):
+            if self.ep is not None:
+                self.ep.forward(W, h, gu, dn, self.moe_out)
+            else:
+                m.forward(self.wtype, W, h, h, gu, dn, None, self.logits, self.ids, self.probs, self.moe_out, H,
+                          self.I, self.E, self.K, T, self.ws)
+            nxt = out if l == len(self.layers) - 1 else self.h[l & 1]
+            m.rms_norm(self.moe_out, None, nxt, H, T, 1e-6)
+            h = nxt
+
+    capture = LayerSet.capture
+
+    def n_kernels(self):
+        return 0
+
+
+def run_stack(args):
+    """Config 5 through the public API (see StackSet); prints the JSON line."""
+    import torch
+
+    rank, world, local = dist_setup(args.gpus)
+    moe, synth = package()
+    device = torch.device("cuda", local)
+    moe.load_library()
+    hbm_peak, peak_kind = peaks()
+    ss = StackSet(moe, synth, device, 4, rank, world, exchange=args.ep_exchange)
+    graphs = [ss.capture(g) for g in range(2)]
+    with ClockSampler(local) as clk:
+        ms = time_steps(ss, args.steps, args.warmup, world, graphs)
+    del graphs
+    e2e_ms, h2d, d2h = time_e2e(ss, args.steps, args.warmup, world)
+    total_tokens = world * ss.T
+    step_ms = ms / args.steps
+    nl = StackSet.N_LAYERS
+    # Per layer at 32 tokens about 200 of the 256 (token, slot) pairs hit
+    # distinct experts; the bytes counted are the rank's expert slabs touched
+    # (an upper bound of the algorithmic bytes) plus the router weights.
+    layer_bytes = ss.layer_bytes + ss.E * ss.H * 4
+    line = {
+        "metric": METRIC,
+        "value": round(total_tokens * args.steps / (ms / 1e3), 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 5),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "q4_0 weights x q8_0 activations, int32 block dots, f32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights quantised with the reference's Q4_0 rules, fresh N(0,1) x)",
+        "config": {"workload": "c5", "layers": nl, "hidden": ss.H, "experts": ss.E, "top_k": ss.K,
+                   "expert_ffn": ss.I, "tokens_per_step": total_tokens, "home_tokens_per_rank": ss.T,
+                   "norm": "rms_norm(w=1, eps=1e-6) after every layer",
+                   "parallelism": (f"ep{world} (" + args.ep_exchange + " exchange)") if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2: each step streams {nl} layers "
+                         f"({nl * ss.layer_bytes / 1e6:.0f} MB of this rank's expert weights)"},
+        "layer_roofline": {"achieved": round(nl * layer_bytes / (step_ms / 1e3) / 1e9, 1), "peak": hbm_peak,
+                           "unit": "GB/s", "frac": round(nl * layer_bytes / (step_ms / 1e3) / 1e9 / hbm_peak, 4),
+                           "bytes_per_step_upper_bound": nl * layer_bytes, "peak_source": peak_kind},
+        "e2e": {"value": round(total_tokens * args.steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps * nl * (8 if world == 1 else 11),
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import gc
+
+        import torch.distributed as dist
+
+        gc.collect()
+        torch.cuda.synchronize()
+        ss.ep.close()
+        dist.destroy_process_group()
+
+
 def dist_setup(n_gpus):
     import torch
 
@@ -628,7 +759,10 @@ def run_reference(args):
 
     moe, synth = package()
     oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
-    wtype, H, I, E, K, T, routing = WORKLOADS[args.workload]
+    stack = args.workload == "c5"  # one token through the 30-layer stack per step
+    wtype, H, I, E, K, T, routing = WORKLOADS["c2_t64" if stack else args.workload]
+    if stack:
+        T = 32
     # Inputs: the same generator as our arm (device-quantised with the
     # reference's rules when a GPU is present; host numpy otherwise).
     if torch.cuda.is_available():
@@ -641,9 +775,18 @@ def run_reference(args):
     x = synth.normal(77, T * H).reshape(T, H)
     bias = synth.zipf_bias(5, E)
     threads = os.cpu_count() or 1
-    per_step = max(1, min(T, 4))
+    per_step = 1 if stack else max(1, min(T, 4))
+
+    def one_stack(i):
+        h = x[i % T:i % T + 1]
+        for _ in range(StackSet.N_LAYERS):  # the sample reuses one layer's weights for all 30
+            _, ids, probs = oracle.router(W, h, H, E, K, 1)
+            h = oracle.rms_norm(oracle.experts(wtype, gu, dn, ids, probs, None, h, H, I, E, K, 1, threads), None, 1e-6)
+        return 1
 
     def one(i):
+        if stack:
+            return one_stack(i)
         t0 = (i * per_step) % T
         xt = x[t0:t0 + per_step]
         n = xt.shape[0]
@@ -670,7 +813,9 @@ def run_reference(args):
         "config": {"workload": args.workload, "hidden": H, "experts": E, "top_k": K, "expert_ffn": I,
                    "tokens_per_step": per_step},
         "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{per_step} tokens of the {T}-token batch per step, one token at a time"},
+                         "sample": (f"1 token through the {StackSet.N_LAYERS}-layer stack (one layer's weights "
+                                    "reused) per step" if stack else
+                                    f"{per_step} tokens of the {T}-token batch per step, one token at a time")},
         "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference is Rust (no toolchain here); the oracle/ C restatement of its CPU MoE path is timed",
     }
@@ -683,7 +828,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS) + ["c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-also", action="store_true")
     ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
@@ -695,6 +840,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c5":
+        run_stack(args)
     else:
         run_ours(args)
 

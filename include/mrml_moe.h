@@ -183,6 +183,16 @@ int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, co
 int mrml_moe_combine(const float *ydown, const int32_t *pos, const int32_t *ids, const float *probs,
                      const float *down_scale, float *out, int H, int K, int T, mrml_stream_t stream);
 
+/* RMS normalisation of `batch` rows of `dim` floats: out = x / sqrt(mean(x^2)
+ * + eps) * weight (weight may be NULL), with the reference's rounding: the
+ * sum of squares in index order, then 1 / sqrt(sum / dim + eps) (ops.rs:24-49;
+ * the norm applied after the MoE output, model.rs:2176-2196).  Replaces
+ * CudaDevice::rms_norm_batch (cuda.rs:2139) and rms_norm (cuda.rs:2102) with
+ * the same argument order.  x 16-byte aligned; dim <= 51200; out may not
+ * alias x. */
+int mrml_moe_rms_norm(const float *x, const float *weight, float *out, int dim, int batch, float eps,
+                      mrml_stream_t stream);
+
 /* GeGLU, elementwise: out[i] = gelu_tanh(gate[i]) * up[i] with the
  * reference's formula and rounding (ops.rs:99-114; tanh as glibc's tanhf),
  * the expert epilogue applied on its own.  Replaces CudaDevice::geglu

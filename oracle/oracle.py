@@ -102,6 +102,17 @@ def mat_vec_f32(wtype, w, x, n_rows, n_cols):
     return y
 
 
+def rms_norm(x, weight, eps):
+    """Row-wise over a [T, H] array (ops.rs:24-49 per row)."""
+    x = _c(x, np.float32)
+    T, H = x.shape
+    out = np.zeros_like(x)
+    w = None if weight is None else _c(weight, np.float32)
+    for t in range(T):
+        lib().oracle_rms_norm(_p(x[t]), None if w is None else _p(w), eps, _p(out[t]), H)
+    return out
+
+
 def geglu(gate, up):
     gate, up = _c(gate, np.float32), _c(up, np.float32)
     out = np.zeros_like(gate)

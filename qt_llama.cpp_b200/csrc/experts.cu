@@ -578,6 +578,50 @@ __global__ void combine_kernel(const float* __restrict__ ydown, const int32_t* _
   out[(size_t)t * H + i] = o;
 }
 
+// RMS normalisation of T rows of H (ops.rs:24-49): sum_sq accumulated in
+// index order in f32 (x*x rounded, then added), mean = sum_sq / H,
+// scale = 1 / sqrt(mean + eps), out = (x * scale) * w.  One warp per row:
+// the warp stages the row in shared memory, lane 0 runs the reference's
+// sequential sum over it (the order decides the rounding), and the warp
+// scales the row.  Dynamic shared memory: rows_per_cta * H floats.
+__global__ void rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
+                                int H, int T, float eps) {
+  extern __shared__ __align__(16) float rows_s[];
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const float* xr = x + (size_t)t * H;
+  float* row = rows_s + (size_t)warp * H;
+  for (int i = lane; i < H; i += 32) row[i] = xr[i];
+  __syncwarp();
+  float scale = 0.f;
+  if (lane == 0) {
+    float s = 0.f;
+    int i = 0;
+    if ((H & 3) == 0) {
+#pragma unroll 8
+      for (; i < H; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(row + i);
+        s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+        s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+        s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+        s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+      }
+    }
+    for (; i < H; ++i) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
+    const float mean = __fdiv_rn(s, (float)H);
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  }
+  scale = __shfl_sync(0xffffffffu, scale, 0);
+  float* orow = out + (size_t)t * H;
+  for (int i = lane; i < H; i += 32) {
+    const float v = __fmul_rn(row[i], scale);
+    orow[i] = w ? __fmul_rn(v, w[i]) : v;
+  }
+}
+
 __global__ void geglu_kernel(const float* __restrict__ gate, const float* __restrict__ up, float* __restrict__ out,
                              long long n) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
@@ -605,6 +649,26 @@ cudaError_t launch_geglu(const float* gate, const float* up, float* out, long lo
   if (g > 148 * 32) g = 148 * 32;
   geglu_kernel<<<(int)(g < 1 ? 1 : g), 256, 0, s>>>(gate, up, out, n);
   return cudaPeekAtLastError();
+}
+
+int rms_norm_rows_per_cta(int H) {
+  int r = 8;
+  while (r > 1 && (size_t)r * H * 4 > 200 * 1024) r >>= 1;
+  return (size_t)r * H * 4 <= 200 * 1024 ? r : 0;
+}
+
+cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, int T, float eps, cudaStream_t s) {
+  static int cache[16] = {0};
+  const int r = rms_norm_rows_per_cta(H);
+  const size_t smem = (size_t)r * H * 4;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && (dev < 0 || dev >= 16 || cache[dev] < (int)smem)) {
+    cudaError_t st = cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (st != cudaSuccess) return st;
+    if (dev >= 0 && dev < 16) cache[dev] = (int)smem;
+  }
+  return launch_pdl(rms_norm_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, x, w, out, H, T, eps);
 }
 
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s) {

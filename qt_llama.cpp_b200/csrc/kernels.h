@@ -34,6 +34,8 @@ cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, 
 cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
                                  cudaStream_t s);
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s);
+int rms_norm_rows_per_cta(int H);
+cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, int T, float eps, cudaStream_t s);
 cudaError_t launch_geglu(const float* gate, const float* up, float* out, long long n, cudaStream_t s);
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
                             int32_t* cnt, int32_t* poff,

@@ -354,6 +354,19 @@ int mrml_moe_combine(const float* ydown, const int32_t* pos, const int32_t* ids,
   return MRML_OK;
 }
 
+int mrml_moe_rms_norm(const float* x, const float* weight, float* out, int dim, int batch, float eps,
+                      mrml_stream_t stream) {
+  if (dim <= 0 || batch < 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return MRML_OK;
+  if (!x || !out) return MRML_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)x & 15) != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (mrml::rms_norm_rows_per_cta(dim) == 0) return MRML_ERR_UNSUPPORTED;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_rms_norm(x, weight, out, dim, batch, eps, s));
+  return MRML_OK;
+}
+
 int mrml_moe_geglu(const float* gate, const float* up, float* out, size_t n, mrml_stream_t stream) {
   if (n == 0) return MRML_OK;
   if (!gate || !up || !out || n > ((size_t)1 << 40)) return MRML_ERR_INVALID_ARGUMENT;

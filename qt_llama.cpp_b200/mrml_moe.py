@@ -62,6 +62,7 @@ SIGNATURES = {
     "mrml_moe_ep_combine": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "mrml_moe_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mrml_moe_geglu": (_i, [_vp, _vp, _vp, _sz, _vp]),
+    "mrml_moe_rms_norm": (_i, [_vp, _vp, _vp, _i, _i, _f, _vp]),
     "mrml_moe_quantize_q8_0": (_i, [_vp, _vp, _sz, _vp]),
     "mrml_moe_quantize_q4_0": (_i, [_vp, _vp, _sz, _vp]),
     "mrml_moe_device_status": (_i, [_vp, _vp, _c.POINTER(_c.c_int)]),
@@ -240,6 +241,12 @@ def combine(ydown, pos, ids, probs, down_scale, out, H, K, T, stream=None):
         lib.mrml_moe_combine(_ptr(ydown), _ptr(pos), _ptr(ids), _ptr(probs), _ptr(down_scale), _ptr(out), H, K, T,
                              _stream_ptr(stream)),
     )
+
+
+def rms_norm(x, weight, out, dim, batch, eps, stream=None):
+    lib = load_library()
+    _check("mrml_moe_rms_norm",
+           lib.mrml_moe_rms_norm(_ptr(x), _ptr(weight), _ptr(out), dim, batch, eps, _stream_ptr(stream)))
 
 
 def geglu(gate, up, out, stream=None):

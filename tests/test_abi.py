@@ -81,6 +81,15 @@ def test_invalid_arguments_rejected_without_a_gpu(moe):
     assert shard(2, P, P, P, P, None, P, P, 64, 64, 8, 0, 0, 2, 1, P, 1 << 20, None) == -1
     assert shard(2, P, P, P, P, None, P, P, 64, 64, 512, 0, 4, 2, 1, P, 1 << 20, None) == -1
     assert lib.mrml_moe_combine(P, P, P, P, None, P, 64, 65, 1, None) == -1
+    assert lib.mrml_moe_rms_norm(P, None, P, 0, 1, ctypes.c_float(1e-6), None) == -1
+    assert lib.mrml_moe_rms_norm(ctypes.c_void_p(0x1004), None, P, 64, 1, ctypes.c_float(1e-6), None) == -1
+    assert lib.mrml_moe_rms_norm(P, None, P, 1 << 20, 1, ctypes.c_float(1e-6), None) == -2
+    # Expert-parallel exchange: ranks and shapes are checked first.
+    assert lib.mrml_moe_ep_slab_bytes(0, 64, 2816, 8) == 0
+    assert lib.mrml_moe_ep_slab_bytes(2, 64, 2818, 8) == 0
+    assert lib.mrml_moe_ep_slab_bytes(8, 64, 2816, 8) > 8 * 64 * 2816 * 4
+    assert lib.mrml_moe_ep_dispatch(P, 2, 2, 64, 2816, 8, P, P, P, P, P, P, P, None) == -1
+    assert lib.mrml_moe_ep_combine(None, 0, 2, 64, 2816, 8, P, P, P, None) == -1
 
 
 def test_zero_tokens_is_a_no_op(moe):

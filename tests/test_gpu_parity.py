@@ -138,6 +138,19 @@ def test_geglu_bit_exact(cuda, moe, oracle):
     assert same.all(), f"{np.count_nonzero(~same)} of {gate.size} differ, first gate {gate[~same][:4]}"
 
 
+@pytest.mark.parametrize("H,T,weighted", [(2816, 32, False), (2816, 9, True), (1024, 17, True), (257, 3, False)])
+def test_rms_norm_bit_exact(cuda, moe, oracle, synth, H, T, weighted):
+    """The norm that follows the MoE output (config 5's layer stack) equals
+    the reference's f32 evaluation bit for bit."""
+    import torch
+
+    x = (synth.normal(H + T, T * H) * 3.0).reshape(T, H).astype(np.float32)
+    w = (1.0 + synth.normal(H + 1, H, 0.1)).astype(np.float32) if weighted else None
+    out = torch.empty((T, H), device=cuda)
+    moe.rms_norm(dev_tensor(x, cuda), None if w is None else dev_tensor(w, cuda), out, H, T, 1e-6)
+    assert_exact(out.cpu().numpy(), oracle.rms_norm(x, w, 1e-6))
+
+
 def test_router_reference_fixture(cuda, moe, oracle):
     """cuda.rs:3260-3323 restated: ids exact, probabilities within 2e-5."""
     import importlib.util, os
