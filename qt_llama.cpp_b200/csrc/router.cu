@@ -208,6 +208,98 @@ __global__ void __launch_bounds__(32 * kRT)
   logits[(size_t)(t0 + warp) * E + e0 + lane] = acc;
 }
 
+// Large-batch variant (many tokens): throughput rather than latency.  CTA =
+// 32 experts (lanes) × 32 tokens (8 warps × 4 tokens per thread), so a W
+// value read from shared memory serves 4 chains and an x value (broadcast
+// in the warp) 32.  Rows stream in chunks of kTK elements through a
+// kTStages ring filled with 16-byte asynchronous copies (4 per thread per
+// chunk); W rows are padded so that the lanes' float4 reads hit distinct
+// banks.  Needs H % 4 == 0 and 16-byte aligned rows.
+constexpr int kTE = 32, kTWarps = 8, kTB = 4, kTT = kTWarps * kTB;
+constexpr int kTK = 64, kTPitch = kTK + 4, kTStages = 3;
+constexpr size_t kTStageFloats = (size_t)kTE * kTPitch + (size_t)kTT * kTK;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_stages() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kTStages - 1) : "memory");
+}
+
+__device__ __forceinline__ void tiled_stage(float* st, const float* __restrict__ W, const float* __restrict__ x, int H,
+                                            int e0, int ne, int t0, int nt, int k0, int len) {
+  float* Ws = st;
+  float* Xs = st + kTE * kTPitch;
+  const int pieces = len >> 2;  // float4 pieces per row
+  for (int q = threadIdx.x; q < (kTE + kTT) * pieces; q += blockDim.x) {
+    const int r = q / pieces, c = (q - r * pieces) << 2;
+    if (r < kTE) {
+      if (r < ne) cp_async16(Ws + r * kTPitch + c, W + (size_t)(e0 + r) * H + k0 + c);
+    } else if (r - kTE < nt) {
+      cp_async16(Xs + (r - kTE) * kTK + c, x + (size_t)(t0 + r - kTE) * H + k0 + c);
+    }
+  }
+  cp_async_commit();  // one group per chunk, possibly empty
+}
+
+__global__ void __launch_bounds__(32 * kTWarps)
+    router_logits_tiled_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
+                               int H, int E, int T) {
+  extern __shared__ __align__(16) float tsm[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e0 = blockIdx.x * kTE, t0 = blockIdx.y * kTT;
+  const int ne = min(kTE, E - e0), nt = min(kTT, T - t0);
+  const int nchunks = (H + kTK - 1) / kTK;
+  pdl_trigger();
+  pdl_wait();
+  for (int c = 0; c < kTStages - 1; ++c) {
+    if (c < nchunks)
+      tiled_stage(tsm + c * kTStageFloats, W, x, H, e0, ne, t0, nt, c * kTK, min(kTK, H - c * kTK));
+    else
+      cp_async_commit();
+  }
+  float acc[kTB];
+#pragma unroll
+  for (int j = 0; j < kTB; ++j) acc[j] = 0.f;
+  const bool active = kTB * warp < nt;  // warp-uniform
+  for (int c = 0; c < nchunks; ++c) {
+    const int cn = c + kTStages - 1;
+    if (cn < nchunks)
+      tiled_stage(tsm + (cn % kTStages) * kTStageFloats, W, x, H, e0, ne, t0, nt, cn * kTK, min(kTK, H - cn * kTK));
+    else
+      cp_async_commit();
+    cp_async_wait_stages();
+    __syncthreads();
+    const float* st = tsm + (c % kTStages) * kTStageFloats;
+    const float* wr = st + lane * kTPitch;
+    const float* xr = st + kTE * kTPitch + kTB * warp * kTK;
+    const int len = min(kTK, H - c * kTK);
+    if (active) {
+#pragma unroll 4
+      for (int i = 0; i < len; i += 4) {
+        const float4 b = *reinterpret_cast<const float4*>(wr + i);
+#pragma unroll
+        for (int j = 0; j < kTB; ++j) {
+          const float4 a = *reinterpret_cast<const float4*>(xr + j * kTK + i);
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(a.x, b.x));
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(a.y, b.y));
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(a.z, b.z));
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(a.w, b.w));
+        }
+      }
+    }
+    __syncthreads();  // the stage is refilled in the next iteration
+  }
+  if (lane < ne) {
+#pragma unroll
+    for (int j = 0; j < kTB; ++j) {
+      const int t = t0 + kTB * warp + j;
+      if (t < T) logits[(size_t)t * E + e0 + lane] = acc[j];
+    }
+  }
+}
+
 // (value desc, id asc) ordering used by the reference's GPU top-8
 // (kernels.rs:944-968) and by the north star for exact ties.
 __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
@@ -337,8 +429,17 @@ cudaError_t ensure_smem(Kern k, size_t bytes, int* cache) {
 
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
                                  cudaStream_t s) {
-  static int cache[16] = {0}, cache_rows[16] = {0};
+  static int cache[16] = {0}, cache_rows[16] = {0}, cache_tiled[16] = {0};
   const bool aligned = (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
+  // Large batches: the tiled kernel (throughput); decode batches: whole rows
+  // per CTA (latency).  Measured crossover on B200 at H = 2816: ~256 tokens.
+  if (aligned && H % 4 == 0 && T > 256) {
+    const dim3 grid((E + kTE - 1) / kTE, (T + kTT - 1) / kTT);
+    const size_t smem = kTStages * kTStageFloats * sizeof(float);
+    cudaError_t st = ensure_smem(router_logits_tiled_kernel, smem, cache_tiled);
+    if (st != cudaSuccess) return st;
+    return launch_pdl(router_logits_tiled_kernel, grid, dim3(32 * kTWarps), smem, s, W, x, logits, H, E, T);
+  }
   if (aligned && H % 32 == 0 && router_rows_smem(H) <= 227 * 1024) {
     const dim3 grid((E + kRE2 - 1) / kRE2, (T + kRT - 1) / kRT);
     const size_t smem = router_rows_smem(H);

@@ -179,6 +179,7 @@ def test_router_reference_fixture(cuda, moe, oracle):
 
 
 @pytest.mark.parametrize("H,E,K,T", [(1024, 16, 2, 4), (2816, 128, 8, 1), (2816, 128, 8, 64), (1024, 16, 2, 2048),
+                                     (2816, 128, 8, 1000), (260, 40, 4, 300),
                                      (257, 128, 8, 33), (96, 256, 64, 7)])
 def test_router_ids_exact(cuda, moe, oracle, synth, H, E, K, T):
     import torch
