@@ -449,7 +449,7 @@ def run_stack(args):
                            "bytes_per_step_upper_bound": nl * layer_bytes, "peak_source": peak_kind},
         "e2e": {"value": round(total_tokens * args.steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * nl * (8 if world == 1 else 11),
+        "gpu_launches": args.steps * nl * (8 if world == 1 else (12 if args.ep_exchange == "p2p" else 8)),
         "clocks": clk.summary(),
     }
     if rank == 0:
@@ -685,7 +685,9 @@ def run_ours(args):
         "top_kernel": top,
         "e2e": {"value": round(world * T * steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": ls.n_kernels() * steps,
+        # The library's kernels per step, plus the peer exchange's four
+        # (push, gather, push, reduce) when the layer runs expert-parallel.
+        "gpu_launches": (ls.n_kernels() + (4 if world > 1 and args.ep_exchange == "p2p" else 0)) * steps,
         "clocks": clk.summary(),
     }
     if world > 1:
