@@ -19,12 +19,15 @@ experts from HBM.  `value` is tokens/s with inputs resident in HBM; `e2e`
 adds, every step, the host->device copy of x from pinned memory and the
 device->host copy of the layer output.
 
-With --gpus N > 1 (torchrun, one rank per GPU, NCCL) the layer runs expert-
+With --gpus N > 1 (torchrun, one rank per GPU) the layer runs expert-
 parallel: rank r holds experts [r*E/N, (r+1)*E/N) and 64 home tokens (weak
-scaling: N*64 tokens per step); a step routes the home tokens, all-gathers
-them, runs the rank's experts on every rank's tokens and reduce-scatters the
-partial outputs (qt_llama.cpp_b200/ep.py).  Workload "c4" is config 4:
-8192 tokens per step in total (strong scaling).
+scaling: N*64 tokens per step); a step routes the home tokens, sends them to
+every rank, runs the rank's experts on every rank's tokens and returns the
+partial outputs to their home ranks (qt_llama.cpp_b200/ep.py): by default
+with the library's peer-memory kernels over NVLink (--ep-exchange p2p), or
+with NCCL all-gathers and a reduce-scatter (--ep-exchange nccl).  Workload
+"c4" is config 4: 8192 tokens per step in total (strong scaling); "c5" is
+config 5: a 30-layer stack with an RMS norm between layers, 32 tokens.
 
 --impl reference times the reference's CPU algorithm (the C restatement
 under oracle/, the reference's Rust cannot be built here) on the host cores.
