@@ -213,13 +213,78 @@ __device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, 
   }
 }
 
+// The K chunks of one unit on the dp4a path, for compute thread row `c`:
+// NJ accumulators, of which the first nj hold tokens (NJ = 1 for the units
+// of a single token, the common case below two tokens per expert, so that
+// their blocks carry no predicated work for absent tokens).  Ring indices
+// and phases advance as the caller's.  Returns false when a wait gave up.
+template <int WQ4, int MODE, int NJ>
+__device__ __forceinline__ bool dp4a_chunks(const Params& P, Bars* B, const uint8_t* raw, const uint8_t* bsb,
+                                            int bs_stage, int nkc, int c, int nj, int& rs, int& bsi, uint32_t& rph,
+                                            uint32_t& bph, float (&acc)[NJ]) {
+  constexpr int BB = WQ4 ? 18 : 34;
+  constexpr int TT = kGvTokens;
+  constexpr int GB = 256;
+  const int lane = threadIdx.x & 31;
+  for (int kc = 0; kc < nkc; ++kc) {
+    if (!wait_bar(&B->raw_full[rs], rph, B, P.err)) return false;
+    if (!wait_bar(&B->bs_full[bsi], bph, B, P.err)) return false;
+    const uint8_t* src = raw + rs * P.raw_bytes;
+    const uint8_t* bt = bsb + bsi * bs_stage;
+    const int2* sc = reinterpret_cast<const int2*>(bt + P.kcb * GB);
+    if constexpr (MODE == kGateUp) {
+      const uint8_t* row = src + c * (kKC * BB);  // gate rows 0..63, then up rows
+#define MRML_GV_BLOCK(BL)                                                                     \
+  {                                                                                           \
+    uint32_t d16, q[BB == 18 ? 4 : 8], w[8];                                                  \
+    tc::chunk_block<BB, BL>(row, d16, q);                                                     \
+    block_words<WQ4>(q, w);                                                                   \
+    block_tokens<WQ4, NJ>(w, f16_bits_to_f32(d16), bt + (BL) * GB, sc + (BL) * TT, nj, acc); \
+  }
+      MRML_GV_BLOCK(0) MRML_GV_BLOCK(1) MRML_GV_BLOCK(2) MRML_GV_BLOCK(3)
+      MRML_GV_BLOCK(4) MRML_GV_BLOCK(5) MRML_GV_BLOCK(6) MRML_GV_BLOCK(7)
+#undef MRML_GV_BLOCK
+    } else {
+      const uint8_t* row = src + (size_t)c * P.row_bytes;
+      for (int b = 0; b < P.nb; ++b) {
+        uint32_t w[8];
+        uint32_t d16;
+        if constexpr (WQ4) {
+          const Q4Block q = load_q4_block(row + b * 18);
+          d16 = q.d16;
+          block_words<1>(q.qs, w);
+        } else {
+          const Q8Block q = load_q8_block(row + b * 34);
+          d16 = q.d16;
+          block_words<0>(q.qs, w);
+        }
+        block_tokens<WQ4, NJ>(w, f16_bits_to_f32(d16), bt + b * GB, sc + b * TT, nj, acc);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      tc::mbar_arrive(&B->raw_empty[rs]);
+      tc::mbar_arrive(&B->bs_empty[bsi]);
+    }
+    if (++rs == P.rs) {
+      rs = 0;
+      rph ^= 1;
+    }
+    if (++bsi == P.bs) {
+      bsi = 0;
+      bph ^= 1;
+    }
+  }
+  return true;
+}
+
 // Unit: kGvTokens (8) positions and 128 weight rows: for gate/up, gate rows
 // m0..m0+63 and the same up rows; for down, rows m0..m0+127.  Compute thread
 // c owns raw-tile row c.  Activations use the group-major layout
 // (common.cuh): a B stage is the unit's position group for the chunk's
 // blocks (256 bytes each, contiguous), then their scales (64 bytes each).
 template <int WQ4, int MODE, int MMA>
-__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
+__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), MMA ? 5 : 4)
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   constexpr int BB = WQ4 ? 18 : 34;
   constexpr int TT = kGvTokens;
@@ -468,54 +533,12 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), 5)
       float acc[TT];
 #pragma unroll
       for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-      for (int kc = 0; kc < nkc && ok; ++kc) {
-        if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
-        if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
-        const uint8_t* src = raw + rs * P.raw_bytes;
-        const uint8_t* bt = bsb + bsi * bs_stage;
-        const int2* sc = reinterpret_cast<const int2*>(bt + P.kcb * GB);
-        if constexpr (MODE == kGateUp) {
-          const uint8_t* row = src + c * (kKC * BB);  // gate rows 0..63, then up rows
-#define MRML_GV_BLOCK(BL)                                                                     \
-  {                                                                                           \
-    uint32_t d16, q[BB == 18 ? 4 : 8], w[8];                                                  \
-    tc::chunk_block<BB, BL>(row, d16, q);                                                     \
-    block_words<WQ4>(q, w);                                                                   \
-    block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + (BL) * GB, sc + (BL) * TT, nj, acc); \
-  }
-          MRML_GV_BLOCK(0) MRML_GV_BLOCK(1) MRML_GV_BLOCK(2) MRML_GV_BLOCK(3)
-          MRML_GV_BLOCK(4) MRML_GV_BLOCK(5) MRML_GV_BLOCK(6) MRML_GV_BLOCK(7)
-#undef MRML_GV_BLOCK
-        } else {
-          const uint8_t* row = src + (size_t)c * P.row_bytes;
-          for (int b = 0; b < P.nb; ++b) {
-            uint32_t w[8];
-            uint32_t d16;
-            if constexpr (WQ4) {
-              const Q4Block q = load_q4_block(row + b * 18);
-              d16 = q.d16;
-              block_words<1>(q.qs, w);
-            } else {
-              const Q8Block q = load_q8_block(row + b * 34);
-              d16 = q.d16;
-              block_words<0>(q.qs, w);
-            }
-            block_tokens<WQ4, TT>(w, f16_bits_to_f32(d16), bt + b * GB, sc + b * TT, nj, acc);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) {
-          tc::mbar_arrive(&B->raw_empty[rs]);
-          tc::mbar_arrive(&B->bs_empty[bsi]);
-        }
-        if (++rs == P.rs) {
-          rs = 0;
-          rph ^= 1;
-        }
-        if (++bsi == P.bs) {
-          bsi = 0;
-          bph ^= 1;
-        }
+      if (nj == 1) {
+        float acc1[1] = {0.f};
+        ok = dp4a_chunks<WQ4, MODE, 1>(P, B, raw, bsb, bs_stage, nkc, c, 1, rs, bsi, rph, bph, acc1);
+        acc[0] = acc1[0];
+      } else {
+        ok = dp4a_chunks<WQ4, MODE, TT>(P, B, raw, bsb, bs_stage, nkc, c, nj, rs, bsi, rph, bph, acc);
       }
       if (!ok) break;
       if constexpr (MODE == kGateUp) {
@@ -599,14 +622,14 @@ struct GvPlan {
   size_t smem;
 };
 
-// Two CTAs per SM when there are enough units to share the SMs, otherwise
-// one CTA with as deep a weight ring as fits (few units: each SM must keep
-// many bytes in flight on its own).
+// Several CTAs per SM when there are more units than SMs, otherwise one CTA
+// with as deep a weight ring as fits (few units: each SM must keep many bytes
+// in flight on its own).
 // Tuning overrides (mrml_moe_set_option): CTAs per SM and weight-ring depth
 // of the decode kernel; 0 = automatic.
 int g_gv_per_sm = 0, g_gv_ring = 0;
 
-GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
+GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma) {
   GvPlan p{};
   const int bb = block_bytes(wtype);
   p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
@@ -615,8 +638,9 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units) {
   const int bs_stage = p.kcb * (256 + kGvTokens * 8);
   const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * kGvRowsGateUp * 4 : 0;
   // With many units, as many CTAs per SM as fit with a double-buffered weight
-  // ring (4 at most); with few units, one CTA and the deepest ring that fits.
-  const int per_sm_max = g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? 5 : 1);
+  // ring (the kernel's launch bound: 5 on the MMA path, 4 on the dp4a path);
+  // with few units, one CTA and the deepest ring that fits.
+  const int per_sm_max = g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? (mma ? 5 : 4) : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
     const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
     // Down tiles hold a whole K (one stage per unit); several CTAs per SM
@@ -664,8 +688,8 @@ bool gv_supported(int wtype, int H, int I) {
   if (H % 256 != 0 || I % 32 != 0) return false;
   const int down_row = (I / 32) * block_bytes(wtype);
   if (I % kGvRowsGateUp != 0) return false;
-  if (gv_plan(tc::kGateUp, wtype, H / 32, 0, false).smem == 0) return false;
-  if (gv_plan(tc::kDown, wtype, I / 32, down_row, false).smem == 0) return false;
+  if (gv_plan(tc::kGateUp, wtype, H / 32, 0, false, false).smem == 0) return false;
+  if (gv_plan(tc::kDown, wtype, I / 32, down_row, false, false).smem == 0) return false;
   return tc_map_available();
 }
 
@@ -684,7 +708,7 @@ cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, i
   CUtensorMap map;
   memset(&map, 0, sizeof(map));
   const int sms = tc_num_sms();
-  const bool many = max_units >= 2 * sms;
+  const bool many = max_units > sms;
   GvPlan pl;
   if (mode == tc::kGateUp) {
     P.nb = H / 32;
@@ -695,14 +719,14 @@ cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, i
     P.out_nb = I / 32;
     P.down_q4 = wtype == kQ4_0;
     if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp)) return cudaErrorInvalidValue;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma);
   } else {
     P.nb = I / 32;
     P.rows = H;
     P.row_bytes = (I / 32) * bb;
     P.w_raw = weights;
     P.y = y;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma);
   }
   if (pl.smem == 0) return cudaErrorInvalidValue;
   P.rs = pl.rs;

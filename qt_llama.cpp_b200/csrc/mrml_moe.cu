@@ -57,8 +57,11 @@ constexpr int kMaxNT = 64;
 // Positions after padding every expert's segment to a multiple of 16.
 int npad_alloc(int E, int K, int T) { return (((T * K + 16 * E) + 15) & ~15) + kMaxNT; }
 
+// Work units of one product: sum over experts of ceil(c_e / NT) row-tile
+// columns, at most T*K/NT (rounded up) plus one partial tile per expert that
+// has pairs, of which there are at most min(E, T*K).
 int units_bound(int E, int K, int T, int NT, int rows, int rows_per_unit) {
-  return ((T * K + NT - 1) / NT + E) * ((rows + rows_per_unit - 1) / rows_per_unit);
+  return ((T * K + NT - 1) / NT + std::min(E, T * K)) * ((rows + rows_per_unit - 1) / rows_per_unit);
 }
 
 // Workspace regions (each 256-byte aligned), in order.  Positions are the
