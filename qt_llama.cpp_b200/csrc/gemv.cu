@@ -213,6 +213,48 @@ __device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, 
   }
 }
 
+// The same block for a down unit of at most 4 tokens.  The warp's two 16-row MMAs
+// see the positions in order (rows 0-15) and rotated by 4 (rows 16-31), so
+// the valid columns of the first land in lanes t = 0, 1 and those of the
+// second in lanes t = 2, 3; each lane runs the f32 chain for one of the two
+// (half the chain work of mma_block_rows2, which computes all 8 columns).
+// acc[2h + k]: tile row 16*(t >> 1) + 8h + g, position 2*(t & 1) + k;
+// s4: {d_a, corr} of positions 2*(t & 1) and 2*(t & 1) + 1.
+template <int WQ4, bool ODD>
+__device__ __forceinline__ void mma_block_rows2_half(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
+                                                     const int4 s4, int g, int t, float (&acc)[4]) {
+  const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + g * 16 + 4 * t);
+  const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + 128 + g * 16 + 4 * t);
+  const uint32_t r0 = *reinterpret_cast<const uint32_t*>(grp + (g ^ 4) * 16 + 4 * t);
+  const uint32_t r1 = *reinterpret_cast<const uint32_t*>(grp + 128 + (g ^ 4) * 16 + 4 * t);
+  uint32_t a[4], d0[4], d1[4];
+  block_frag<WQ4, ODD>(row0 + g * pitch + boff, t, a[0], a[2]);
+  block_frag<WQ4, ODD>(row0 + (g + 8) * pitch + boff, t, a[1], a[3]);
+  mma_block<WQ4>(d0, a, b0, b1, (uint32_t)s4.y, (uint32_t)s4.w);
+  block_frag<WQ4, ODD>(row0 + (g + 16) * pitch + boff, t, a[0], a[2]);
+  block_frag<WQ4, ODD>(row0 + (g + 24) * pitch + boff, t, a[1], a[3]);
+  mma_block<WQ4>(d1, a, r0, r1, (uint32_t)s4.y, (uint32_t)s4.w);
+  const bool hi = t >= 2;
+  uint32_t d[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) d[j] = hi ? d1[j] : d0[j];
+  const uint8_t* ra = row0 + ((hi ? 16 : 0) + g) * pitch + boff;
+  const uint8_t* rb = ra + 8 * pitch;
+  const uint64_t da = f2_pack(__int_as_float(s4.x), __int_as_float(s4.z));
+  const uint64_t magic = f2_pack(kMagicF, kMagicF);
+  const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
+  const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
+  const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
+  const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
+  float p0, p1, p2, p3;
+  f2_unpack(f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), p0, p1);
+  f2_unpack(f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), p2, p3);
+  acc[0] = __fadd_rn(acc[0], p0);
+  acc[1] = __fadd_rn(acc[1], p1);
+  acc[2] = __fadd_rn(acc[2], p2);
+  acc[3] = __fadd_rn(acc[3], p3);
+}
+
 // The K chunks of one unit on the dp4a path, for compute thread row `c`:
 // NJ accumulators, of which the first nj hold tokens (NJ = 1 for the units
 // of a single token, the common case below two tokens per expert, so that
@@ -284,7 +326,7 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, Bars* B, const uint
 // (common.cuh): a B stage is the unit's position group for the chunk's
 // blocks (256 bytes each, contiguous), then their scales (64 bytes each).
 template <int WQ4, int MODE, int MMA>
-__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), MMA ? 5 : 4)
+__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kGateUp) ? 5 : 4)
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   constexpr int BB = WQ4 ? 18 : 34;
   constexpr int TT = kGvTokens;
@@ -401,6 +443,12 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), MMA ? 5 : 4)
       float acc[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      // Q4_0 down units of at most 4 tokens run the half-chain form.  (For
+      // gate/up it measured slower: a second unrolled chunk body in a kernel
+      // held to 64 registers; for Q8_0 its registers spill.)
+      const bool half = MODE == kDown && WQ4 && nj <= 4;  // warp-uniform
+      float(&acch)[4] = *reinterpret_cast<float(*)[4]>(&acc[0]);  // the half layout's sums
+      const int th = t & 1;
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
         if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
@@ -417,11 +465,20 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), MMA ? 5 : 4)
           }
         } else {
           const uint8_t* row0 = src + (size_t)(32 * cw) * P.row_bytes;
+          if (WQ4 && half) {
 #pragma unroll 1
-          for (int b = 0; b < P.nb; b += 2) {
-            mma_block_rows2<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + t], g, t, acc);
-            mma_block_rows2<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc4[(b + 1) * 4 + t], g,
-                                       t, acc);
+            for (int b = 0; b < P.nb; b += 2) {
+              mma_block_rows2_half<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + th], g, t, acch);
+              mma_block_rows2_half<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB,
+                                              sc4[(b + 1) * 4 + th], g, t, acch);
+            }
+          } else {
+#pragma unroll 1
+            for (int b = 0; b < P.nb; b += 2) {
+              mma_block_rows2<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + t], g, t, acc);
+              mma_block_rows2<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc4[(b + 1) * 4 + t],
+                                         g, t, acc);
+            }
           }
         }
         __syncwarp();
@@ -439,6 +496,16 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), MMA ? 5 : 4)
         }
       }
       if (!ok) break;
+      if (half) {
+        // Back to the 8-position layout: lane (g, t < 2) keeps its rows
+        // 0-15 and takes rows 16-31 of the same positions from lane t ^ 2;
+        // lanes t >= 2 hold positions 4..7, absent in these units.
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float other = __shfl_xor_sync(0xffffffffu, acch[j], 2);
+          if (t < 2) acc[4 + j] = other;
+        }
+      }
       // acc[4i + 2h + k]: tile row 32cw + 16i + 8h + g, position p0 + 2t + k.
       if constexpr (MODE == kGateUp) {
         float* xw = xch + (cw & 1) * 8 * 32;  // [8][32 lanes] per gate/up warp pair
@@ -638,9 +705,10 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   const int bs_stage = p.kcb * (256 + kGvTokens * 8);
   const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * kGvRowsGateUp * 4 : 0;
   // With many units, as many CTAs per SM as fit with a double-buffered weight
-  // ring (the kernel's launch bound: 5 on the MMA path, 4 on the dp4a path);
-  // with few units, one CTA and the deepest ring that fits.
-  const int per_sm_max = g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? (mma ? 5 : 4) : 1);
+  // ring (the kernel's launch bound: 5 for the MMA gate/up product, 4 for the
+  // others); with few units, one CTA and the deepest ring that fits.
+  const int per_sm_max =
+      g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? ((mma && mode == tc::kGateUp) ? 5 : 4) : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
     const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
     // Down tiles hold a whole K (one stage per unit); several CTAs per SM
