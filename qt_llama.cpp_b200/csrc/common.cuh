@@ -347,12 +347,34 @@ __host__ __device__ constexpr int block_bytes(int wtype) { return wtype == kQ4_0
 //  - block-major (tensor cores): group g of block b at (b * npad/8 + g) * 256,
 //    so a block's token tile is contiguous; scales at [b * npad + pos].
 //  - group-major (decode kernel): at (g * nb + b) * 256, so a group's
-//    consecutive blocks are contiguous; scales at [(g * nb + b) * 8 + pos % 8].
+//    consecutive blocks are contiguous; scales in kActScaleBytes records at
+//    (g * nb + b) * kActScaleBytes (act_scale_offset_gm).
+// Block-major scales are int2 {d, correction} per position.
 __host__ __device__ inline size_t act_group_offset(bool group_major, int b, int g, int nb, int npad) {
   return group_major ? ((size_t)g * nb + b) * 256 : ((size_t)b * (npad / 8) + g) * 256;
 }
-__host__ __device__ inline size_t act_scale_index(bool group_major, int b, int pos, int nb, int npad) {
-  return group_major ? ((size_t)(pos >> 3) * nb + b) * 8 + (pos & 7) : (size_t)b * npad + pos;
+__host__ __device__ inline size_t act_scale_index(int b, int pos, int npad) { return (size_t)b * npad + pos; }
+
+// Group-major scale record of (position group, block): float d[8] in
+// position order, then int4 c[4] with c[j] = {corr(2j), corr(2j+1),
+// corr(2j), corr(2j+1)}: the decode kernel's m16n8k32 MMA takes lane t's
+// accumulator seeds (rows g and g+8, positions 2t and 2t+1) as one aligned
+// 16-byte load, and its d_a pair as one 8-byte load.  12 bytes per position.
+constexpr int kActScaleBytes = 96;
+__host__ __device__ inline size_t act_scale_offset_gm(int b, int pos, int nb) {
+  return ((size_t)(pos >> 3) * nb + b) * kActScaleBytes;
+}
+__device__ __forceinline__ void store_act_scale_gm(void* base, int b, int pos, int nb, float d, int corr) {
+  uint8_t* rec = static_cast<uint8_t*>(base) + act_scale_offset_gm(b, pos, nb);
+  const int j = pos & 7;
+  reinterpret_cast<float*>(rec)[j] = d;
+  int* c = reinterpret_cast<int*>(rec + 32) + (j >> 1) * 4 + (j & 1);
+  c[0] = corr;
+  c[2] = corr;
+}
+// Reads position j's {d, corr} from a group-major record.
+__device__ __forceinline__ int2 load_act_scale_gm(const uint8_t* rec, int j) {
+  return make_int2(reinterpret_cast<const int*>(rec)[j], reinterpret_cast<const int*>(rec + 32)[(j >> 1) * 4 + (j & 1)]);
 }
 
 }  // namespace mrml

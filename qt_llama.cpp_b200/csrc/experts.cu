@@ -266,7 +266,8 @@ __global__ void __launch_bounds__(kDispatchThreads)
 // core B operand: for every position a token was routed to, its 32 int8
 // values of block b go to bq[b][pos/8] in the canonical K-major layout (two
 // 16-byte halves, core matrices of 8 positions), and {d, correction} to
-// bsc[b][pos].  One warp per (token, block), lane = element.
+// bsc[b][pos] (block-major), or into the group-major scale records of the
+// decode kernel.  One warp per (token, block), lane = element.
 template <int WQ4>
 __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32_t* __restrict__ pos, int T, int H,
                                         int K, int npad, int group_major, int8_t* __restrict__ bq,
@@ -304,7 +305,12 @@ __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32
       uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + act_group_offset(group_major, b, p >> 3, nb, npad) +
                      (lane >> 4) * 128 + (p & 7) * 16 + (lane & 15);
       *dst = (uint8_t)(int8_t)q;
-      if (lane == 0) bsc[act_scale_index(group_major, b, p, nb, npad)] = sc;
+      if (lane == 0) {
+        if (group_major)
+          store_act_scale_gm(bsc, b, p, nb, __int_as_float(sc.x), sc.y);
+        else
+          bsc[act_scale_index(b, p, npad)] = sc;
+      }
     }
   }
 }

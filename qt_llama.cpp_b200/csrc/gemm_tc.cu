@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(32 * (kEpiWarp0 + 4 * ((NT + 31) / 32)), 1)
               *dst = (uint8_t)(int8_t)qv;
               if (lane == 0) {
                 const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
-                P.out_s[act_scale_index(false, blk, pos, 0, P.npad)] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
+                P.out_s[act_scale_index(blk, pos, P.npad)] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
               }
             }
           }

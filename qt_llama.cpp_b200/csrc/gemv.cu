@@ -22,7 +22,7 @@
 namespace mrml {
 namespace gv {
 
-using tc::Bars;
+using tc::GvBars;
 using tc::kDown;
 using tc::kGateUp;
 using tc::kKC;
@@ -82,10 +82,10 @@ __device__ __forceinline__ void block_words(const uint32_t* qs, uint32_t (&w)[8]
 //   acc[t] += isum(t) * (d_w * d_a(t))
 // in the reference's rounding order (scalar round-to-nearest operations; a
 // packed f32x2 version of this sequence did not reproduce the scalar bits).
-// btile: the block's 8-position activation group; sc: the tokens'
-// {d_a, correction}.
+// btile: the block's 8-position activation group; rec: its group-major
+// scale record ({d_a, correction} of the positions).
 template <int WQ4, int TT>
-__device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, const int2* sc,
+__device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, const uint8_t* rec,
                                              int nj, float (&acc)[TT]) {
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
@@ -93,7 +93,7 @@ __device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, c
       const uint8_t* a = btile + t * 16;
       const uint4 alo = *reinterpret_cast<const uint4*>(a);
       const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
-      const int2 s2 = sc[t];
+      const int2 s2 = load_act_scale_gm(rec, t);
       const float da = __int_as_float(s2.x);
       const float f = __fsub_rn(__int_as_float(block_isum_bits<WQ4>(w, alo, ahi, s2.y)), kMagicF);  // exact
       acc[t] = __fadd_rn(acc[t], __fmul_rn(f, __fmul_rn(dw, da)));
@@ -117,15 +117,15 @@ __device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, c
 // 2t, 2t+1; d2,d3 = row g+8.
 template <int WQ4>
 __device__ __forceinline__ void mma_block(uint32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
-                                          uint32_t c0, uint32_t c1) {
+                                          const uint4& c) {
   if constexpr (WQ4)
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c.x), "r"(c.y), "r"(c.z), "r"(c.w));
   else
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c.x), "r"(c.y), "r"(c.z), "r"(c.w));
 }
 
 // A 32-bit word of shared memory at an address that is 4-byte aligned
@@ -161,7 +161,10 @@ __device__ __forceinline__ void block_frag(const uint8_t* blk, int t, uint32_t& 
 // on B200 with CUDA 12.9: a packed multiply whose result feeds a packed add
 // is contracted into a fused multiply-add despite the .rn modifiers, which
 // changes the rounding; a packed multiply followed by scalar add.rn is not.
-// So products are packed and the chain's additions stay scalar.
+// So the chain's additions are packed fused multiply-adds acc + p * one,
+// with `one` = 1.0 passed in at run time: p * 1.0 is exact, so the single
+// rounding is that of the addition, and the compiler cannot fold the product
+// that feeds p into the FMA, as it would for a literal 1.0 or a plain add.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
@@ -180,16 +183,28 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// acc pair += p (one = {1.0, 1.0}, opaque): two round-to-nearest additions.
+__device__ __forceinline__ void f2_acc(float& a0, float& a1, uint64_t p, uint64_t one) {
+  f2_unpack(f2_fma(p, one, f2_pack(a0, a1)), a0, a1);
+}
 
 // One quant block for the warp's two 16-row tiles (rows r0+16i+g, +8):
 //   acc[4i + 2h + k] += isum * (d_w(row) * d_a(2t + k))
-// grp: the block's activation group, s4: {d_a, corr} of positions 2t, 2t+1.
+// grp: the block's activation group; rec: its group-major scale record, from
+// which lane t takes the d_a pair and the accumulator seeds of positions 2t,
+// 2t+1 with one load each.
 template <int WQ4, bool ODD>
 __device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
-                                                const int4 s4, int g, int t, float (&acc)[8]) {
+                                                const uint8_t* rec, uint64_t one, int g, int t, float (&acc)[8]) {
   const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + g * 16 + 4 * t);
   const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + 128 + g * 16 + 4 * t);
-  const uint64_t da = f2_pack(__int_as_float(s4.x), __int_as_float(s4.z));
+  const uint64_t da = *reinterpret_cast<const uint64_t*>(rec + 8 * t);
+  const uint4 seed = *reinterpret_cast<const uint4*>(rec + 32 + 16 * t);
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -198,18 +213,13 @@ __device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, 
     uint32_t a[4], d[4];
     block_frag<WQ4, ODD>(ra, t, a[0], a[2]);
     block_frag<WQ4, ODD>(rb, t, a[1], a[3]);
-    mma_block<WQ4>(d, a, b0, b1, (uint32_t)s4.y, (uint32_t)s4.w);
+    mma_block<WQ4>(d, a, b0, b1, seed);
     const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
     const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
     const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
     const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
-    float p0, p1, p2, p3;
-    f2_unpack(f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), p0, p1);
-    f2_unpack(f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), p2, p3);
-    acc[4 * i + 0] = __fadd_rn(acc[4 * i + 0], p0);
-    acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], p1);
-    acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], p2);
-    acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], p3);
+    f2_acc(acc[4 * i + 0], acc[4 * i + 1], f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), one);
+    f2_acc(acc[4 * i + 2], acc[4 * i + 3], f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), one);
   }
 }
 
@@ -218,11 +228,15 @@ __device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, 
 // the valid columns of the first land in lanes t = 0, 1 and those of the
 // second in lanes t = 2, 3; each lane runs the f32 chain for one of the two
 // (half the chain work of mma_block_rows2, which computes all 8 columns).
-// acc[2h + k]: tile row 16*(t >> 1) + 8h + g, position 2*(t & 1) + k;
-// s4: {d_a, corr} of positions 2*(t & 1) and 2*(t & 1) + 1.
+// acc[2h + k]: tile row 16*(t >> 1) + 8h + g, position 2*(t & 1) + k; the
+// d_a pair and seeds come from positions 2*(t & 1) and 2*(t & 1) + 1.
 template <int WQ4, bool ODD>
 __device__ __forceinline__ void mma_block_rows2_half(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
-                                                     const int4 s4, int g, int t, float (&acc)[4]) {
+                                                     const uint8_t* rec, uint64_t one, int g, int t,
+                                                     float (&acc)[4]) {
+  const int th = t & 1;
+  const uint64_t da = *reinterpret_cast<const uint64_t*>(rec + 8 * th);
+  const uint4 seed = *reinterpret_cast<const uint4*>(rec + 32 + 16 * th);
   const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + g * 16 + 4 * t);
   const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + 128 + g * 16 + 4 * t);
   const uint32_t r0 = *reinterpret_cast<const uint32_t*>(grp + (g ^ 4) * 16 + 4 * t);
@@ -230,29 +244,23 @@ __device__ __forceinline__ void mma_block_rows2_half(const uint8_t* row0, int pi
   uint32_t a[4], d0[4], d1[4];
   block_frag<WQ4, ODD>(row0 + g * pitch + boff, t, a[0], a[2]);
   block_frag<WQ4, ODD>(row0 + (g + 8) * pitch + boff, t, a[1], a[3]);
-  mma_block<WQ4>(d0, a, b0, b1, (uint32_t)s4.y, (uint32_t)s4.w);
+  mma_block<WQ4>(d0, a, b0, b1, seed);
   block_frag<WQ4, ODD>(row0 + (g + 16) * pitch + boff, t, a[0], a[2]);
   block_frag<WQ4, ODD>(row0 + (g + 24) * pitch + boff, t, a[1], a[3]);
-  mma_block<WQ4>(d1, a, r0, r1, (uint32_t)s4.y, (uint32_t)s4.w);
+  mma_block<WQ4>(d1, a, r0, r1, seed);
   const bool hi = t >= 2;
   uint32_t d[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) d[j] = hi ? d1[j] : d0[j];
   const uint8_t* ra = row0 + ((hi ? 16 : 0) + g) * pitch + boff;
   const uint8_t* rb = ra + 8 * pitch;
-  const uint64_t da = f2_pack(__int_as_float(s4.x), __int_as_float(s4.z));
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
   const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
   const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
   const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
   const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
-  float p0, p1, p2, p3;
-  f2_unpack(f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), p0, p1);
-  f2_unpack(f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), p2, p3);
-  acc[0] = __fadd_rn(acc[0], p0);
-  acc[1] = __fadd_rn(acc[1], p1);
-  acc[2] = __fadd_rn(acc[2], p2);
-  acc[3] = __fadd_rn(acc[3], p3);
+  f2_acc(acc[0], acc[1], f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), one);
+  f2_acc(acc[2], acc[3], f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), one);
 }
 
 // The K chunks of one unit on the dp4a path, for compute thread row `c`:
@@ -261,11 +269,10 @@ __device__ __forceinline__ void mma_block_rows2_half(const uint8_t* row0, int pi
 // their blocks carry no predicated work for absent tokens).  Ring indices
 // and phases advance as the caller's.  Returns false when a wait gave up.
 template <int WQ4, int MODE, int NJ>
-__device__ __forceinline__ bool dp4a_chunks(const Params& P, Bars* B, const uint8_t* raw, const uint8_t* bsb,
+__device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const uint8_t* raw, const uint8_t* bsb,
                                             int bs_stage, int nkc, int c, int nj, int& rs, int& bsi, uint32_t& rph,
                                             uint32_t& bph, float (&acc)[NJ]) {
   constexpr int BB = WQ4 ? 18 : 34;
-  constexpr int TT = kGvTokens;
   constexpr int GB = 256;
   const int lane = threadIdx.x & 31;
   for (int kc = 0; kc < nkc; ++kc) {
@@ -273,7 +280,7 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, Bars* B, const uint
     if (!wait_bar(&B->bs_full[bsi], bph, B, P.err)) return false;
     const uint8_t* src = raw + rs * P.raw_bytes;
     const uint8_t* bt = bsb + bsi * bs_stage;
-    const int2* sc = reinterpret_cast<const int2*>(bt + P.kcb * GB);
+    const uint8_t* sc = bt + P.kcb * GB;  // the blocks' group-major scale records
     if constexpr (MODE == kGateUp) {
       const uint8_t* row = src + c * (kKC * BB);  // gate rows 0..63, then up rows
 #define MRML_GV_BLOCK(BL)                                                                     \
@@ -281,7 +288,7 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, Bars* B, const uint
     uint32_t d16, q[BB == 18 ? 4 : 8], w[8];                                                  \
     tc::chunk_block<BB, BL>(row, d16, q);                                                     \
     block_words<WQ4>(q, w);                                                                   \
-    block_tokens<WQ4, NJ>(w, f16_bits_to_f32(d16), bt + (BL) * GB, sc + (BL) * TT, nj, acc); \
+    block_tokens<WQ4, NJ>(w, f16_bits_to_f32(d16), bt + (BL) * GB, sc + (BL) * kActScaleBytes, nj, acc); \
   }
       MRML_GV_BLOCK(0) MRML_GV_BLOCK(1) MRML_GV_BLOCK(2) MRML_GV_BLOCK(3)
       MRML_GV_BLOCK(4) MRML_GV_BLOCK(5) MRML_GV_BLOCK(6) MRML_GV_BLOCK(7)
@@ -300,7 +307,7 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, Bars* B, const uint
           d16 = q.d16;
           block_words<0>(q.qs, w);
         }
-        block_tokens<WQ4, NJ>(w, f16_bits_to_f32(d16), bt + b * GB, sc + b * TT, nj, acc);
+        block_tokens<WQ4, NJ>(w, f16_bits_to_f32(d16), bt + b * GB, sc + b * kActScaleBytes, nj, acc);
       }
     }
     __syncwarp();
@@ -332,14 +339,14 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
   constexpr int TT = kGvTokens;
   constexpr int RG = kGvRowsGateUp;  // row pairs per unit
   constexpr int GB = 256;            // bytes of one block's activation group
-  constexpr int SB = TT * 8;         // bytes of one block's scales
+  constexpr int SB = kActScaleBytes;  // bytes of one block's scale record
 
   // 128-byte alignment is what the (unswizzled) tensor copies need; the
-  // barrier block takes the first KiB.
+  // barrier block takes the first kGvBarBytes.
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
-  Bars* B = reinterpret_cast<Bars*>(smem);
-  uint8_t* raw = smem + 1024;
+  GvBars* B = reinterpret_cast<GvBars*>(smem);
+  uint8_t* raw = smem + tc::kGvBarBytes;
   uint8_t* bsb = raw + P.rs * P.raw_bytes;
   const int bs_stage = P.kcb * (GB + SB);
   float* xch = reinterpret_cast<float*>(bsb + P.bs * bs_stage);  // [TT][RG] up-row sums
@@ -417,7 +424,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
           // contiguous, for the activations and for their scales.
           const int g = p0 >> 3;
           bulk_g2s(bdst, P.bq + act_group_offset(true, b0, g, P.nb, P.npad), nblk * GB, &B->bs_full[bsi]);
-          bulk_g2s(bdst + P.kcb * GB, P.bsc + act_scale_index(true, b0, p0, P.nb, P.npad), nblk * SB,
+          bulk_g2s(bdst + P.kcb * GB, reinterpret_cast<const uint8_t*>(P.bsc) + act_scale_offset_gm(b0, p0, P.nb), nblk * SB,
                    &B->bs_full[bsi]);
           if (++bsi == P.bs) {
             bsi = 0;
@@ -433,6 +440,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
     const int cw = warp - kComp0;
     const int g = lane >> 2, t = lane & 3;
     const bool up_warp = MODE == kGateUp && cw >= kCompWarps / 2;
+    const uint64_t one = f2_pack(P.one, P.one);
     int rs = 0, bsi = 0;
     uint32_t rph = 0, bph = 0, xph = 0;
     bool ok = true;
@@ -448,35 +456,34 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
       // held to 64 registers; for Q8_0 its registers spill.)
       const bool half = MODE == kDown && WQ4 && nj <= 4;  // warp-uniform
       float(&acch)[4] = *reinterpret_cast<float(*)[4]>(&acc[0]);  // the half layout's sums
-      const int th = t & 1;
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
         if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
         const uint8_t* src = raw + rs * P.raw_bytes;
         const uint8_t* bt = bsb + bsi * bs_stage;
-        const int4* sc4 = reinterpret_cast<const int4*>(bt + P.kcb * GB);  // [block][4] position pairs
+        const uint8_t* sc = bt + P.kcb * GB;  // the blocks' group-major scale records
         if constexpr (MODE == kGateUp) {
           const uint8_t* row0 = src + 32 * cw * (kKC * BB);
 #pragma unroll
           for (int bl = 0; bl < kKC; bl += 2) {
-            mma_block_rows2<WQ4, false>(row0, kKC * BB, bl * BB, bt + bl * GB, sc4[bl * 4 + t], g, t, acc);
-            mma_block_rows2<WQ4, true>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, sc4[(bl + 1) * 4 + t], g,
-                                       t, acc);
+            mma_block_rows2<WQ4, false>(row0, kKC * BB, bl * BB, bt + bl * GB, sc + bl * SB, one, g, t, acc);
+            mma_block_rows2<WQ4, true>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, sc + (bl + 1) * SB, one,
+                                       g, t, acc);
           }
         } else {
           const uint8_t* row0 = src + (size_t)(32 * cw) * P.row_bytes;
           if (WQ4 && half) {
 #pragma unroll 1
             for (int b = 0; b < P.nb; b += 2) {
-              mma_block_rows2_half<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + th], g, t, acch);
-              mma_block_rows2_half<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB,
-                                              sc4[(b + 1) * 4 + th], g, t, acch);
+              mma_block_rows2_half<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc + b * SB, one, g, t, acch);
+              mma_block_rows2_half<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc + (b + 1) * SB,
+                                              one, g, t, acch);
             }
           } else {
 #pragma unroll 1
             for (int b = 0; b < P.nb; b += 2) {
-              mma_block_rows2<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc4[b * 4 + t], g, t, acc);
-              mma_block_rows2<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc4[(b + 1) * 4 + t],
+              mma_block_rows2<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc + b * SB, one, g, t, acc);
+              mma_block_rows2<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc + (b + 1) * SB, one,
                                          g, t, acc);
             }
           }
@@ -571,8 +578,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
               }
               if (g == 0) {
                 const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
-                P.out_s[act_scale_index(true, blk, pos, P.out_nb, P.npad)] =
-                    make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
+                store_act_scale_gm(P.out_s, blk, pos, P.out_nb, f16_bits_to_f32(d16), corr);
               }
             }
           }
@@ -659,7 +665,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
               *dst = (uint8_t)(int8_t)qv;
               if (lane == 0) {
                 const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
-                P.out_s[act_scale_index(true, blk, pos, P.out_nb, P.npad)] = make_int2(__float_as_int(f16_bits_to_f32(d16)), corr);
+                store_act_scale_gm(P.out_s, blk, pos, P.out_nb, f16_bits_to_f32(d16), corr);
               }
             }
           }
@@ -702,7 +708,7 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
   const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb : 2 * kGvRowsGateUp * row_bytes;
   p.raw_bytes = (raw1 + 1023) & ~1023;
-  const int bs_stage = p.kcb * (256 + kGvTokens * 8);
+  const int bs_stage = p.kcb * (256 + kActScaleBytes);
   const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * kGvRowsGateUp * 4 : 0;
   // With many units, as many CTAs per SM as fit with a double-buffered weight
   // ring (the kernel's launch bound: 5 for the MMA gate/up product, 4 for the
@@ -717,7 +723,7 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
     const int rs_max = g_gv_ring > 0 ? g_gv_ring : tc::kMaxRaw;
     for (int rs = rs_max; rs >= rs_min; --rs)
       for (int bs = 2; bs >= 1; --bs) {
-        const size_t total = 128 + 1024 + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage + xch_bytes;
+        const size_t total = 128 + tc::kGvBarBytes + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage + xch_bytes;
         if (total <= budget) {
           p.rs = rs;
           p.bs = bs;
@@ -801,6 +807,7 @@ cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, i
   P.bs = pl.bs;
   P.raw_bytes = pl.raw_bytes;
   P.kcb = pl.kcb;
+  P.one = 1.0f;
   const int grid = std::max(1, std::min(pl.per_sm * sms, max_units));
   const bool q4 = wtype == kQ4_0;
   if (mma) {

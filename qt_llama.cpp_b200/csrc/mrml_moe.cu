@@ -78,9 +78,9 @@ struct Workspace {
   int4* units_gu;    // tensor-core work units, gate/up
   int4* units_dn;    // tensor-core work units, down
   int8_t* xb;        // [H/32][npad/8][256]  tensor-core B operand of gate/up
-  int2* xs;          // [H/32][npad]         its scales
+  int2* xs;          // its scales: [H/32][npad] int2, or group-major 12-byte records (decode kernel)
   int8_t* ab;        // [I/32][npad/8][256]  B operand of down (re-quantised act)
-  int2* as;          // [I/32][npad]         its scales
+  int2* as;          // its scales, laid out as xs
   float* act;        // [npad][I]     geglu output per position (CUDA-core path)
   float* ydown;      // [npad][H]     down output per position (unscaled)
   int npad, max_units_gu, max_units_dn;
@@ -112,9 +112,9 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
   w.units_gu = reinterpret_cast<int4*>(take((size_t)w.max_units_gu * 16));
   w.units_dn = reinterpret_cast<int4*>(take((size_t)w.max_units_dn * 16));
   w.xb = reinterpret_cast<int8_t*>(take(nb * npad * 32));
-  w.xs = reinterpret_cast<int2*>(take(nb * npad * 8));
+  w.xs = reinterpret_cast<int2*>(take(nb * npad * 12));  // int2 per position, or 12-byte group-major records
   w.ab = reinterpret_cast<int8_t*>(take(nbi * npad * 32));
-  w.as = reinterpret_cast<int2*>(take(nbi * npad * 8));
+  w.as = reinterpret_cast<int2*>(take(nbi * npad * 12));
   w.act = reinterpret_cast<float*>(take((size_t)npad * I * 4));
   w.ydown = reinterpret_cast<float*>(take((size_t)npad * H * 4));
   w.bytes = off;

@@ -23,7 +23,8 @@ enum Mode : int { kGateUp = 0, kDown = 1 };
 struct Params {
   const uint8_t* w_raw;  // down: raw weights [E][rows][row_bytes]
   const int8_t* bq;      // B operand [nb][npad_alloc/8][2][8][16]
-  const int2* bsc;       // B scales [nb][npad_alloc] {f32 bits of d_a, int32 correction}
+  const int2* bsc;       // B scales: [nb][npad_alloc] {f32 bits of d_a, int32 correction}
+                         // (tensor cores), group-major records (decode kernel)
   const int4* units;     // {e, p0, nvalid, m0}
   const int* n_units;
   int nb;                // quant blocks along K
@@ -43,6 +44,7 @@ struct Params {
   int rs, as, bs, tb;
   int raw_bytes;         // bytes per raw stage
   int kcb;               // blocks per B stage (kKC for gate/up, nb for down)
+  float one;             // 1.0f, opaque to the compiler (decode kernel's chain adds)
 };
 
 constexpr int kMaxRaw = 8;
@@ -60,14 +62,27 @@ struct __align__(8) Bars {
 
 static_assert(sizeof(Bars) <= 1024, "the barrier block must fit the first KiB of shared memory");
 
-__device__ __forceinline__ bool aborted(const Bars* B) { return *(const volatile int*)&B->abort != 0; }
+// The decode kernel's barrier block: only the rings it uses, so that five
+// of its CTAs fit an SM's shared memory with both activation stages.
+struct __align__(8) GvBars {
+  uint64_t raw_full[kMaxRaw], raw_empty[kMaxRaw];
+  uint64_t bs_full[4], bs_empty[4];
+  uint64_t xch_full, xch_empty;
+  int abort;
+};
+constexpr int kGvBarBytes = 256;
+static_assert(sizeof(GvBars) <= kGvBarBytes, "the decode barrier block must fit its 256 bytes");
+
+template <class BarsT>
+__device__ __forceinline__ bool aborted(const BarsT* B) { return *(const volatile int*)&B->abort != 0; }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Bounded wait that also watches the CTA's abort flag.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Bars* B, int* err) {
+template <class BarsT>
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, BarsT* B, int* err) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255) == 255 && aborted(B)) return false;
