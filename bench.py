@@ -84,8 +84,16 @@ STRONG = {"c4", "c4_q8"}
 METRIC = "MoE-layer tokens/sec at decode batch 1/64 and 2048-token prefill; % of roofline"
 KERNELS = {
     "router": ["router_logits", "router_topk", "dispatch", "quantize", "gate_up", "down", "combine"],
+    # mrml_moe_forward at most 32 tokens (E <= 256, K <= 64): the dispatch
+    # kernel selects the experts itself (the library's dispatch_topk_supported)
+    "router_small": ["router_logits", "topk_dispatch", "quantize", "gate_up", "down", "combine"],
     "zipf_logits": ["route_from_logits", "dispatch", "quantize", "gate_up", "down", "combine"],
 }
+
+
+def forward_kernels(T, E, K):
+    """Launch list of one mrml_moe_forward call."""
+    return KERNELS["router_small" if T <= 32 and E <= 256 and K <= 64 else "router"]
 
 
 def peaks():
@@ -206,6 +214,7 @@ class LayerSet:
         self.out = torch.empty(T, H, device=device)
         self.ws = moe.new_workspace(H, I, E, K, T, device)
         self.layer_bytes = layer_bytes
+        self.kernels = forward_kernels(T, E, K) if routing == "router" else KERNELS[routing]
 
     def step(self, i, x=None, out=None):
         gu, dn, W = self.layers[i % self.n_layers]
@@ -247,7 +256,7 @@ class LayerSet:
         return g
 
     def n_kernels(self):
-        return len(KERNELS[self.routing])
+        return len(self.kernels)
 
     @property
     def router_ws(self):
@@ -303,6 +312,7 @@ class EPLayerSet:
         self.ids, self.probs = self.ep.ids, self.ep.probs
         self.ws = self.ep.ws
         self.layer_bytes = layer_bytes
+        self.kernels = KERNELS[routing]  # mrml_moe_router, then the expert shard
 
     @property
     def router_ws(self):
@@ -317,7 +327,7 @@ class EPLayerSet:
     capture = LayerSet.capture
 
     def n_kernels(self):
-        return len(KERNELS[self.routing])
+        return len(self.kernels)
 
     def unique_experts(self, i):
         """This rank's experts hit by step i (every rank's tokens) and its
@@ -452,7 +462,10 @@ def run_stack(args):
                            "bytes_per_step_upper_bound": nl * layer_bytes, "peak_source": peak_kind},
         "e2e": {"value": round(total_tokens * args.steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * nl * (8 if world == 1 else (12 if args.ep_exchange == "p2p" else 8)),
+        # per layer: the MoE launches (forward at world 1; router, expert
+        # shard and the exchange kernels under expert parallelism) + rms_norm
+        "gpu_launches": args.steps * nl * (1 + (len(forward_kernels(ss.T, ss.E, ss.K)) if world == 1 else
+                                               (11 if args.ep_exchange == "p2p" else 7))),
         "clocks": clk.summary(),
     }
     if rank == 0:
@@ -547,7 +560,7 @@ def time_kernels(ls, steps):
         torch.cuda.synchronize()
         for k in range(nk):
             totals[k] += evs[2 * k].elapsed_time(evs[2 * k + 1])
-    return dict(zip(KERNELS[ls.routing], totals))
+    return dict(zip(ls.kernels, totals))
 
 
 def time_e2e(ls, steps, warmup, world):

@@ -169,7 +169,10 @@ int mrml_moe_ep_combine(void *const *slabs, int rank, int N, int T, int H, int K
                         int *status, mrml_stream_t stream);
 
 /* The whole layer: mrml_moe_router on (router_w, router_x) followed by
- * mrml_moe_experts on x.  router_x and x may be the same pointer. */
+ * mrml_moe_experts on x.  router_x and x may be the same pointer.  Up to 32
+ * tokens (E <= 256, K <= 64) the experts' dispatch kernel selects the
+ * experts itself from the logits (the same selection code, one launch
+ * fewer); logits, ids and probs are written either way. */
 int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, const float *x, const uint8_t *gate_up,
                      const uint8_t *down, const float *down_scale, float *logits, int32_t *ids, float *probs,
                      float *out, int H, int I, int E, int K, int T, void *workspace, size_t workspace_bytes,
@@ -228,7 +231,8 @@ int mrml_moe_set_option(int option, int value);
  * with mrml_moe_profile_events(NULL, 0).  Per call: mrml_moe_router 2
  * launches (router_logits, router_topk), mrml_moe_route_from_logits 1,
  * mrml_moe_experts 5 (dispatch, quantize, gate_up, down, combine), and
- * mrml_moe_forward the 7 of both. */
+ * mrml_moe_forward the 7 of both, or 6 up to 32 tokens (router_logits, then
+ * the dispatch kernel with the selection, then the other four). */
 int mrml_moe_profile_events(void **events, int n_events);
 
 /* Synchronises `stream`, reads and clears the device status word of a

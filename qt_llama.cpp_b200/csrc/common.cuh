@@ -372,9 +372,5 @@ __device__ __forceinline__ void store_act_scale_gm(void* base, int b, int pos, i
   c[0] = corr;
   c[2] = corr;
 }
-// Reads position j's {d, corr} from a group-major record.
-__device__ __forceinline__ int2 load_act_scale_gm(const uint8_t* rec, int j) {
-  return make_int2(reinterpret_cast<const int*>(rec)[j], reinterpret_cast<const int*>(rec + 32)[(j >> 1) * 4 + (j & 1)]);
-}
 
 }  // namespace mrml

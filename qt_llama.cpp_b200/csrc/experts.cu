@@ -21,6 +21,7 @@
 // int32 block sum becomes an f32 through the 1.5*2^23 bit trick.
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 namespace mrml {
 
@@ -123,13 +124,37 @@ __global__ void quantize_q4_0_gguf_kernel(const float* __restrict__ x, uint8_t* 
 // ---------------------------------------------------------------------------
 constexpr int kDispatchThreads = 1024;
 
+//
+// With `logits` (small batches: T = n_pairs / K <= 32 tokens, E <= 256) the
+// kernel first selects each token's experts itself, one warp per token, as
+// router_topk_kernel does, and writes ids and probs; the rest of the kernel
+// reads them back (global writes of the CTA are visible to it after the
+// barrier).  That saves the top-k launch on the decode path.
 __global__ void __launch_bounds__(kDispatchThreads)
-    dispatch_kernel(const int32_t* __restrict__ ids, const float* __restrict__ probs, int n_pairs, int E,
-                    int e_first, int e_total, int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
+    dispatch_kernel(int32_t* ids, float* probs, int n_pairs, int E, int e_first, int e_total,
+                    int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
                     int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
-                    int* __restrict__ n_units, int NT, int mt_gu, int rows_gu, int mt_dn, int* __restrict__ err) {
+                    int* __restrict__ n_units, int NT, int mt_gu, int rows_gu, int mt_dn, int* __restrict__ err,
+                    const float* __restrict__ logits, int K) {
   pdl_trigger();
   pdl_wait();
+  if (logits != nullptr) {
+    __shared__ int tk_cand[kDispatchThreads / 32][kMaxCandidates];
+    __shared__ float tk_cval[kDispatchThreads / 32][kMaxCandidates];
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, T = n_pairs / K;
+    if (w < T) {
+      float val[8];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int e = l + 32 * m;
+        val[m] = e < E ? logits[(size_t)w * E + e] : -INFINITY;
+      }
+      uint32_t taken;
+      warp_topk<8>(val, E, K, tk_cand[w], tk_cval[w], taken);
+      finish_token(tk_cand[w], tk_cval[w], K, K, w, ids, probs);
+    }
+    __syncthreads();
+  }
   extern __shared__ int32_t dsm[];
   int32_t* cnt = dsm;            // [E] totals
   int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
@@ -685,18 +710,30 @@ cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long l
   return cudaPeekAtLastError();
 }
 
+bool dispatch_topk_supported(int E, int K, int T) {
+  return E >= 1 && E <= 256 && K >= 1 && K <= kMaxCandidates && K <= E && T >= 1 && T <= kDispatchThreads / 32;
+}
+
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
                             int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
-                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s) {
+                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s, const float* logits, int K,
+                            int32_t* ids_out, float* probs_out) {
+  if (logits && (!dispatch_topk_supported(E, K, n_pairs / (K > 0 ? K : 1)) || n_pairs % K != 0 || !ids_out ||
+                 !probs_out))
+    return cudaErrorInvalidValue;
+  // The kernel reads ids and probs through the same pointers it writes them
+  // with in the fused mode; otherwise it only reads them.
+  int32_t* idp = logits ? ids_out : const_cast<int32_t*>(ids);
+  float* prp = logits ? probs_out : const_cast<float*>(probs);
   const size_t smem = (size_t)35 * E * sizeof(int32_t);
   if (smem > 48 * 1024) {
     cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
   }
-  cudaError_t st = launch_pdl(dispatch_kernel, dim3(1), dim3(kDispatchThreads), smem, s, ids, probs, n_pairs, E, e_first,
+  cudaError_t st = launch_pdl(dispatch_kernel, dim3(1), dim3(kDispatchThreads), smem, s, idp, prp, n_pairs, E, e_first,
                               e_total, cnt, poff, pair_at, pos, units_gu, units_dn, n_units, NT, mt_gu, rows_gu, mt_dn,
-                              err);
+                              err, logits, K);
   if (st != cudaSuccess) return st;
   return cudaPeekAtLastError();
 }

@@ -87,16 +87,25 @@ __device__ __forceinline__ void block_words(const uint32_t* qs, uint32_t (&w)[8]
 template <int WQ4, int TT>
 __device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, const uint8_t* rec,
                                              int nj, float (&acc)[TT]) {
+  // Tokens in pairs: the record holds d(t), d(t+1) and corr(t), corr(t+1)
+  // (even t) as adjacent words, one 8-byte load each.
 #pragma unroll
-  for (int t = 0; t < TT; ++t) {
+  for (int t = 0; t < TT; t += 2) {
     if (t < nj) {
-      const uint8_t* a = btile + t * 16;
-      const uint4 alo = *reinterpret_cast<const uint4*>(a);
-      const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
-      const int2 s2 = load_act_scale_gm(rec, t);
-      const float da = __int_as_float(s2.x);
-      const float f = __fsub_rn(__int_as_float(block_isum_bits<WQ4>(w, alo, ahi, s2.y)), kMagicF);  // exact
-      acc[t] = __fadd_rn(acc[t], __fmul_rn(f, __fmul_rn(dw, da)));
+      const int2 dd = *reinterpret_cast<const int2*>(rec + 4 * t);
+      const int2 cc = *reinterpret_cast<const int2*>(rec + 32 + 8 * t);
+#pragma unroll
+      for (int k = 0; k < 2 && t + k < TT; ++k) {
+        if (k == 0 || t + 1 < nj) {
+          const uint8_t* a = btile + (t + k) * 16;
+          const uint4 alo = *reinterpret_cast<const uint4*>(a);
+          const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
+          const float da = __int_as_float(k ? dd.y : dd.x);
+          const float f =
+              __fsub_rn(__int_as_float(block_isum_bits<WQ4>(w, alo, ahi, k ? cc.y : cc.x)), kMagicF);  // exact
+          acc[t + k] = __fadd_rn(acc[t + k], __fmul_rn(f, __fmul_rn(dw, da)));
+        }
+      }
     }
   }
 }

@@ -40,7 +40,12 @@ cudaError_t launch_geglu(const float* gate, const float* up, float* out, long lo
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
                             int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
-                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s);
+                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s,
+                            const float* logits = nullptr, int K = 0, int32_t* ids_out = nullptr,
+                            float* probs_out = nullptr);
+// Whether launch_dispatch can select the experts itself (from `logits`) for
+// T tokens: the top-k of up to 256 experts, one warp per token.
+bool dispatch_topk_supported(int E, int K, int T);
 cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,
                                     bool group_major, int8_t* bq, int2* bsc, cudaStream_t s);
 cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* cnt, const int32_t* poff,

@@ -218,9 +218,13 @@ Route pick_route(int wtype, int H, int I, int E, long long pairs) {
   return pairs >= 2ll * E ? kRouteGemvMma : kRouteGemv;
 }
 
+// With topk_logits, the dispatch kernel first selects the experts from the
+// router logits and writes ids/probs (ids_out/probs_out, the buffers that
+// ids/probs point to), replacing the top-k launch (small batches).
 int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids,
                 const float* probs, const float* down_scale, const float* x, float* out, int H, int I, int E, int K,
-                int T, cudaStream_t s, int e_first = 0, int e_total = 0) {
+                int T, cudaStream_t s, int e_first = 0, int e_total = 0, const float* topk_logits = nullptr,
+                int32_t* ids_out = nullptr, float* probs_out = nullptr) {
   if (e_total == 0) e_total = E;
   const long long pairs = (long long)T * K * E / e_total;
   const Route route = pick_route(wtype, H, I, E, pairs);
@@ -230,7 +234,8 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
   const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;  // down tiles: 128 rows on both paths
   int* n_units = w.status + 2;
   MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, e_first, e_total, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
-                                    n_units, NT, mt_gu, rows_gu, mt_dn, w.status, s));
+                                    n_units, NT, mt_gu, rows_gu, mt_dn, w.status, s, topk_logits, K, ids_out,
+                                    probs_out));
   if (route == kRouteGeneral) {
     MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
     MRML_LAUNCH(mrml::launch_gate_up(wtype, gate_up, w.cnt, w.poff, w.pair_at, w.xq, w.xd, w.xsum, w.act, H, I, E, K,
@@ -342,6 +347,13 @@ int mrml_moe_forward(int wtype, const float* router_w, const float* router_x, co
   MRML_TRY(check_workspace(workspace, workspace_bytes, H, I, E, K, T));
   const Workspace w = carve(workspace, H, I, E, K, T);
   const cudaStream_t s = (cudaStream_t)stream;
+  // Up to 32 tokens the dispatch kernel selects the experts itself (one
+  // launch fewer on the decode path); the selection is the same code.
+  if (mrml::dispatch_topk_supported(E, K, T)) {
+    MRML_LAUNCH(mrml::launch_router_logits(router_w, router_x, logits, H, E, T, w.status, s));
+    return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s, 0, 0, logits, ids,
+                       probs);
+  }
   MRML_TRY(run_router(w, router_w, router_x, logits, ids, probs, H, E, K, T, s));
   return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s);
 }
