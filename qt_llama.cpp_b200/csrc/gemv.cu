@@ -1,17 +1,19 @@
-// gemv.cu — grouped expert products on the CUDA cores for decode-size work.
+// gemv.cu — grouped expert products for decode-size work (and prefill).
 //
 // When an expert sees only a few tokens, one tcgen05.mma per 32-element
 // quant block keeps the tensor pipe busy ~160 cycles whatever the token
 // count, which caps a Q4_0 layer well below the HBM rate.  This kernel keeps
-// the same warp-specialised TMA pipeline as gemm_tc.cu but computes the
-// integer block dots with dp4a:
+// the same warp-specialised TMA pipeline as gemm_tc.cu:
 //   warp 0       weight producer (TMA tensor-map tiles / 1-D bulk rows)
-//   warp 1       activation producer (B tiles and scales, bulk copies)
-//   warps 2..5   compute: thread = one weight row, the unit's (up to 8)
-//                tokens in registers.  For gate/up, warps 2-3 hold the 64
-//                gate rows and warps 4-5 the matching up rows; at the end of
-//                a unit the up rows' sums pass to the gate threads through
-//                shared memory, which apply GeGLU and the Q8_0 quantisation.
+//   warp 1       activation producer (B tiles and scale records, bulk copies)
+//   warps 2..5   compute, 128 weight rows x one unit of up to 8 positions.
+//                For gate/up, warps 2-3 hold the 64 gate rows and warps 4-5
+//                the matching up rows; at the end of a unit the up rows' sums
+//                pass to the gate warps through shared memory, which apply
+//                GeGLU and the Q8_0 quantisation of the down product's input.
+// Two compute forms: MMA = 1, warp-level mma.sync m16n8k32 block dots (the
+// automatic choice from two tokens per expert), and MMA = 0, dp4a with one
+// weight row per thread (single tokens).
 // The per-row f32 chain sum += (float)isum_b * (d_w * d_a) runs in block
 // order, as in the reference (quant.rs:335-369 / 564-577), so the results
 // are bit-identical to the tensor-core kernel and to the reference.
