@@ -137,6 +137,15 @@ __global__ void __launch_bounds__(kDispatchThreads)
                     int* __restrict__ n_units, int NT, int mt_gu, int rows_gu, int mt_dn, int* __restrict__ err,
                     const float* __restrict__ logits, int K) {
   pdl_trigger();
+  extern __shared__ int32_t dsm[];
+  int32_t* cnt = dsm;            // [E] totals
+  int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
+  int32_t* ubase = dsm + 2 * E;  // [E] first unit of expert e (per product: times mt)
+  int32_t* wcnt = dsm + 3 * E;   // [32][E] per-warp counts of the current chunk
+  __shared__ int s_npos;         // positions in use (padded segments)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // Shared memory is this CTA's own: cleared while the previous kernel ends.
+  for (int i = tid; i < E * 35; i += blockDim.x) dsm[i] = 0;
   pdl_wait();
   if (logits != nullptr) {
     __shared__ int tk_cand[kDispatchThreads / 32][kMaxCandidates];
@@ -153,22 +162,21 @@ __global__ void __launch_bounds__(kDispatchThreads)
       warp_topk<8>(val, E, K, tk_cand[w], tk_cval[w], taken);
       finish_token(tk_cand[w], tk_cval[w], K, K, w, ids, probs);
     }
-    __syncthreads();
   }
-  extern __shared__ int32_t dsm[];
-  int32_t* cnt = dsm;            // [E] totals
-  int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
-  int32_t* ubase = dsm + 2 * E;  // [E] first unit of expert e (per product: times mt)
-  int32_t* wcnt = dsm + 3 * E;   // [32][E] per-warp counts of the current chunk
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < E * 35; i += blockDim.x) dsm[i] = 0;
   __syncthreads();
+  // The thread's first pair, read once for the count and the scatter.
+  int id0 = 0;
+  float p0 = 0.f;
+  if (tid < n_pairs) {
+    id0 = ids[tid];
+    p0 = probs[tid];
+  }
   // Experts [e_first, e_first + E) of e_total are this call's; pairs routed
   // to the others are skipped like pairs with alpha <= 1e-4 (an expert-
   // parallel shard), ids outside [0, e_total) are errors.
   for (int p = tid; p < n_pairs; p += blockDim.x) {
-    const int id = ids[p];
-    if (probs[p] > 0.0001f) {
+    const int id = p == tid ? id0 : ids[p];
+    if ((p == tid ? p0 : probs[p]) > 0.0001f) {
       if (id < 0 || id >= e_total)
         set_error(err, kDevBadExpert);
       else if (id - e_first >= 0 && id - e_first < E)
@@ -220,12 +228,13 @@ __global__ void __launch_bounds__(kDispatchThreads)
     }
     if (e == E - 1) {
       poff[E] = bp + ip;
+      s_npos = bp + ip;
       n_units[0] = (bu + iu) * mt_gu;
       n_units[1] = (bu + iu) * mt_dn;
     }
   }
   __syncthreads();
-  const int npos = poff[E];
+  const int npos = s_npos;
   for (int i = tid; i < npos; i += blockDim.x) pair_at[i] = -1;
   // Work units: expert e owns units [ubase[e]*mt, (ubase[e] + nt_e)*mt) of
   // each product, ordered (row tile m, position tile j), j fastest.  One
@@ -258,8 +267,8 @@ __global__ void __launch_bounds__(kDispatchThreads)
     const int p = b0 + tid;
     int e = -1;
     if (p < n_pairs) {
-      const int id = ids[p] - e_first;
-      if (probs[p] > 0.0001f && id >= 0 && id < E && id + e_first < e_total) e = id;
+      const int id = (b0 == 0 ? id0 : ids[p]) - e_first;
+      if ((b0 == 0 ? p0 : probs[p]) > 0.0001f && id >= 0 && id < E && id + e_first < e_total) e = id;
       if (e < 0) pos[p] = -1;
     }
     const uint32_t peers = __match_any_sync(0xffffffffu, e);
