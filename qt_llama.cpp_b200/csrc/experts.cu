@@ -134,18 +134,19 @@ __global__ void __launch_bounds__(kDispatchThreads)
     dispatch_kernel(int32_t* ids, float* probs, int n_pairs, int E, int e_first, int e_total,
                     int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
                     int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
-                    int* __restrict__ n_units, int NT, int mt_gu, int rows_gu, int mt_dn, int* __restrict__ err,
-                    const float* __restrict__ logits, int K) {
+                    int* __restrict__ n_units, int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn,
+                    int* __restrict__ err, const float* __restrict__ logits, int K) {
   pdl_trigger();
   extern __shared__ int32_t dsm[];
   int32_t* cnt = dsm;            // [E] totals
   int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
-  int32_t* ubase = dsm + 2 * E;  // [E] first unit of expert e (per product: times mt)
+  int32_t* ubase = dsm + 2 * E;  // [E] first gate/up unit of expert e (times mt)
   int32_t* wcnt = dsm + 3 * E;   // [32][E] per-warp counts of the current chunk
+  int32_t* ubase_dn = dsm + 35 * E;  // [E] first down unit of expert e (times mt)
   __shared__ int s_npos;         // positions in use (padded segments)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // Shared memory is this CTA's own: cleared while the previous kernel ends.
-  for (int i = tid; i < E * 35; i += blockDim.x) dsm[i] = 0;
+  for (int i = tid; i < E * 36; i += blockDim.x) dsm[i] = 0;
   pdl_wait();
   if (logits != nullptr) {
     __shared__ int tk_cand[kDispatchThreads / 32][kMaxCandidates];
@@ -184,53 +185,61 @@ __global__ void __launch_bounds__(kDispatchThreads)
     }
   }
   __syncthreads();
-  // Exclusive scans of the padded counts and of the unit counts, one warp
-  // per 32 experts, then across warps (E <= 1024).
+  // Exclusive scans of the padded counts and of the two products' unit
+  // counts, one warp per 32 experts, then across warps (E <= 1024).
   {
-    __shared__ int wsum_pos[32], wsum_units[32];
+    __shared__ int wsum_pos[32], wsum_units[32], wsum_dn[32];
     const int e = tid;
     const int c = e < E ? cnt[e] : 0;
-    const int pad = (c + 15) & ~15, nun = (c + NT - 1) / NT;
-    int ip = pad, iu = nun;
+    const int pad = (c + 15) & ~15, nun = (c + NT_gu - 1) / NT_gu, nud = (c + NT_dn - 1) / NT_dn;
+    int ip = pad, iu = nun, id = nud;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int vp = __shfl_up_sync(0xffffffffu, ip, o), vu = __shfl_up_sync(0xffffffffu, iu, o);
+      const int vd = __shfl_up_sync(0xffffffffu, id, o);
       if (lane >= o) {
         ip += vp;
         iu += vu;
+        id += vd;
       }
     }
     if (lane == 31) {
       wsum_pos[warp] = ip;
       wsum_units[warp] = iu;
+      wsum_dn[warp] = id;
     }
     __syncthreads();
     if (warp == 0) {
-      int vp = wsum_pos[lane], vu = wsum_units[lane];
+      int vp = wsum_pos[lane], vu = wsum_units[lane], vd = wsum_dn[lane];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int a = __shfl_up_sync(0xffffffffu, vp, o), b = __shfl_up_sync(0xffffffffu, vu, o);
+        const int d = __shfl_up_sync(0xffffffffu, vd, o);
         if (lane >= o) {
           vp += a;
           vu += b;
+          vd += d;
         }
       }
       wsum_pos[lane] = vp;  // inclusive per warp
       wsum_units[lane] = vu;
+      wsum_dn[lane] = vd;
     }
     __syncthreads();
     const int bp = warp ? wsum_pos[warp - 1] : 0, bu = warp ? wsum_units[warp - 1] : 0;
+    const int bd = warp ? wsum_dn[warp - 1] : 0;
     if (e < E) {
       poff[e] = bp + ip - pad;
       base[e] = bp + ip - pad;
       ubase[e] = bu + iu - nun;
+      ubase_dn[e] = bd + id - nud;
       cnt_out[e] = c;
     }
     if (e == E - 1) {
       poff[E] = bp + ip;
       s_npos = bp + ip;
       n_units[0] = (bu + iu) * mt_gu;
-      n_units[1] = (bu + iu) * mt_dn;
+      n_units[1] = (bd + id) * mt_dn;
     }
   }
   __syncthreads();
@@ -242,21 +251,23 @@ __global__ void __launch_bounds__(kDispatchThreads)
   // (experts without pairs share their successor's base and come first).
   // base[] still holds the segment starts here.
   {
-    const int nu = ubase[E - 1] + (cnt[E - 1] + NT - 1) / NT;
     for (int prod = 0; prod < 2; ++prod) {
       const int mt = prod == 0 ? mt_gu : mt_dn, rows = prod == 0 ? rows_gu : 128;
+      const int NT = prod == 0 ? NT_gu : NT_dn;
+      const int32_t* ub = prod == 0 ? ubase : ubase_dn;
+      const int nu = ub[E - 1] + (cnt[E - 1] + NT - 1) / NT;
       int4* units = prod == 0 ? units_gu : units_dn;
       for (int u = tid; u < nu * mt; u += blockDim.x) {
         int lo = 0, hi = E - 1;
         while (lo < hi) {
           const int mid = (lo + hi + 1) >> 1;
-          if (ubase[mid] * mt <= u)
+          if (ub[mid] * mt <= u)
             lo = mid;
           else
             hi = mid - 1;
         }
         const int e = lo, c = cnt[e], nt = (c + NT - 1) / NT;
-        const int local = u - ubase[e] * mt, m = local / nt, j = local - m * nt;
+        const int local = u - ub[e] * mt, m = local / nt, j = local - m * nt;
         units[u] = make_int4(e, base[e] + j * NT, min(NT, c - j * NT), m * rows);
       }
     }
@@ -725,9 +736,9 @@ bool dispatch_topk_supported(int E, int K, int T) {
 
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
                             int32_t* cnt, int32_t* poff,
-                            int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
-                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s, const float* logits, int K,
-                            int32_t* ids_out, float* probs_out) {
+                            int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units,
+                            int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s,
+                            const float* logits, int K, int32_t* ids_out, float* probs_out) {
   if (logits && (!dispatch_topk_supported(E, K, n_pairs / (K > 0 ? K : 1)) || n_pairs % K != 0 || !ids_out ||
                  !probs_out))
     return cudaErrorInvalidValue;
@@ -735,14 +746,14 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
   // with in the fused mode; otherwise it only reads them.
   int32_t* idp = logits ? ids_out : const_cast<int32_t*>(ids);
   float* prp = logits ? probs_out : const_cast<float*>(probs);
-  const size_t smem = (size_t)35 * E * sizeof(int32_t);
+  const size_t smem = (size_t)36 * E * sizeof(int32_t);
   if (smem > 48 * 1024) {
     cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (st != cudaSuccess) return st;
   }
   cudaError_t st = launch_pdl(dispatch_kernel, dim3(1), dim3(kDispatchThreads), smem, s, idp, prp, n_pairs, E, e_first,
-                              e_total, cnt, poff, pair_at, pos, units_gu, units_dn, n_units, NT, mt_gu, rows_gu, mt_dn,
-                              err, logits, K);
+                              e_total, cnt, poff, pair_at, pos, units_gu, units_dn, n_units, NT_gu, NT_dn, mt_gu,
+                              rows_gu, mt_dn, err, logits, K);
   if (st != cudaSuccess) return st;
   return cudaPeekAtLastError();
 }

@@ -204,33 +204,48 @@ __device__ __forceinline__ void f2_acc(float& a0, float& a1, uint64_t p, uint64_
   f2_unpack(f2_fma(p, one, f2_pack(a0, a1)), a0, a1);
 }
 
-// One quant block for the warp's two 16-row tiles (rows r0+16i+g, +8):
-//   acc[4i + 2h + k] += isum * (d_w(row) * d_a(2t + k))
-// grp: the block's activation group; rec: its group-major scale record, from
+// One quant block for the warp's two 16-row tiles (rows r0+16i+g, +8) and
+// the unit's NG position groups of 8:
+//   acc[8q + 4i + 2h + k] += isum * (d_w(row) * d_a(8q + 2t + k))
+// grp: group 0's activations of the block, the next group gstride bytes on;
+// rec: group 0's group-major scale record (rstride bytes to the next), from
 // which lane t takes the d_a pair and the accumulator seeds of positions 2t,
-// 2t+1 with one load each.
-template <int WQ4, bool ODD>
+// 2t+1 with one load each.  A row fragment is loaded and unpacked once for
+// all NG groups.
+template <int WQ4, bool ODD, int NG>
 __device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
-                                                const uint8_t* rec, uint64_t one, int g, int t, float (&acc)[8]) {
-  const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + g * 16 + 4 * t);
-  const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + 128 + g * 16 + 4 * t);
-  const uint64_t da = *reinterpret_cast<const uint64_t*>(rec + 8 * t);
-  const uint4 seed = *reinterpret_cast<const uint4*>(rec + 32 + 16 * t);
+                                                int gstride, const uint8_t* rec, int rstride, uint64_t one, int g,
+                                                int t, float (&acc)[8 * NG]) {
+  uint32_t b0[NG], b1[NG];
+  uint64_t da[NG];
+  uint4 seed[NG];
+#pragma unroll
+  for (int q = 0; q < NG; ++q) {
+    b0[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + g * 16 + 4 * t);
+    b1[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + 128 + g * 16 + 4 * t);
+    da[q] = *reinterpret_cast<const uint64_t*>(rec + q * rstride + 8 * t);
+    seed[q] = *reinterpret_cast<const uint4*>(rec + q * rstride + 32 + 16 * t);
+  }
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const uint8_t* ra = row0 + (16 * i + g) * pitch + boff;
     const uint8_t* rb = ra + 8 * pitch;
-    uint32_t a[4], d[4];
+    uint32_t a[4];
     block_frag<WQ4, ODD>(ra, t, a[0], a[2]);
     block_frag<WQ4, ODD>(rb, t, a[1], a[3]);
-    mma_block<WQ4>(d, a, b0, b1, seed);
     const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
     const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
-    const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
-    const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
-    f2_acc(acc[4 * i + 0], acc[4 * i + 1], f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), one);
-    f2_acc(acc[4 * i + 2], acc[4 * i + 3], f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), one);
+#pragma unroll
+    for (int q = 0; q < NG; ++q) {
+      uint32_t d[4];
+      mma_block<WQ4>(d, a, b0[q], b1[q], seed[q]);
+      const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
+      const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
+      float* aq = acc + 8 * q + 4 * i;
+      f2_acc(aq[0], aq[1], f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da[q])), one);
+      f2_acc(aq[2], aq[3], f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da[q])), one);
+    }
   }
 }
 
@@ -338,16 +353,22 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const ui
   return true;
 }
 
-// Unit: kGvTokens (8) positions and 128 weight rows: for gate/up, gate rows
-// m0..m0+63 and the same up rows; for down, rows m0..m0+127.  Compute thread
-// c owns raw-tile row c.  Activations use the group-major layout
-// (common.cuh): a B stage is the unit's position group for the chunk's
-// blocks (256 bytes each, contiguous), then their scales (64 bytes each).
-template <int WQ4, int MODE, int MMA>
-__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kGateUp) ? 5 : 4)
+// Unit: NG groups of kGvTokens (8) positions and 128 weight rows: for
+// gate/up, gate rows m0..m0+63 and the same up rows; for down, rows
+// m0..m0+127.  NG = 2 (the MMA form only) when experts see about 12 tokens
+// or more: a weight stage then serves 16 positions, each row fragment is
+// unpacked once for two MMAs, and the weights stream half as often.
+// Activations use the group-major layout (common.cuh): a B stage holds, for
+// each of the unit's groups, the chunk's blocks (256 bytes each, contiguous),
+// then each group's scale records.
+template <int WQ4, int MODE, int MMA, int NG>
+__global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
+                                  (MMA && MODE == kGateUp && NG == 1) ? 5 : ((NG == 2 && !WQ4) ? 3 : 4))
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
+  static_assert(NG == 1 || (NG == 2 && MMA), "two position groups per unit on the MMA form only");
   constexpr int BB = WQ4 ? 18 : 34;
   constexpr int TT = kGvTokens;
+  constexpr int NP = TT * NG;  // positions per unit
   constexpr int RG = kGvRowsGateUp;  // row pairs per unit
   constexpr int GB = 256;            // bytes of one block's activation group
   constexpr int SB = kActScaleBytes;  // bytes of one block's scale record
@@ -359,8 +380,8 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
   GvBars* B = reinterpret_cast<GvBars*>(smem);
   uint8_t* raw = smem + tc::kGvBarBytes;
   uint8_t* bsb = raw + P.rs * P.raw_bytes;
-  const int bs_stage = P.kcb * (GB + SB);
-  float* xch = reinterpret_cast<float*>(bsb + P.bs * bs_stage);  // [TT][RG] up-row sums
+  const int bs_stage = P.kcb * NG * (GB + SB);
+  float* xch = reinterpret_cast<float*>(bsb + P.bs * bs_stage);  // [NP][RG] up-row sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -430,13 +451,18 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
           uint8_t* bdst = bsb + bsi * bs_stage;
           const int b0 = kc * P.kcb;
           const int nblk = min(P.kcb, P.nb - b0);
-          mbar_arrive_expect_tx(&B->bs_full[bsi], (uint32_t)(nblk * (GB + SB)));
-          // Group-major layout: the unit's blocks b0 .. b0+nblk-1 are
-          // contiguous, for the activations and for their scales.
-          const int g = p0 >> 3;
-          bulk_g2s(bdst, P.bq + act_group_offset(true, b0, g, P.nb, P.npad), nblk * GB, &B->bs_full[bsi]);
-          bulk_g2s(bdst + P.kcb * GB, reinterpret_cast<const uint8_t*>(P.bsc) + act_scale_offset_gm(b0, p0, P.nb), nblk * SB,
-                   &B->bs_full[bsi]);
+          mbar_arrive_expect_tx(&B->bs_full[bsi], (uint32_t)(nblk * NG * (GB + SB)));
+          // Group-major layout: a group's blocks b0 .. b0+nblk-1 are
+          // contiguous, for the activations and for their scale records.
+#pragma unroll
+          for (int q = 0; q < NG; ++q) {
+            const int g = (p0 >> 3) + q;
+            bulk_g2s(bdst + q * P.kcb * GB, P.bq + act_group_offset(true, b0, g, P.nb, P.npad), nblk * GB,
+                     &B->bs_full[bsi]);
+            bulk_g2s(bdst + NG * P.kcb * GB + q * P.kcb * SB,
+                     reinterpret_cast<const uint8_t*>(P.bsc) + act_scale_offset_gm(b0, 8 * g, P.nb), nblk * SB,
+                     &B->bs_full[bsi]);
+          }
           if (++bsi == P.bs) {
             bsi = 0;
             bph ^= 1;
@@ -458,32 +484,34 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
     for (int u = blockIdx.x; u < n_units && ok && !tc::aborted(B); u += gridDim.x) {
       const int4 U = P.units[u];
       const int p0 = U.y, nvalid = U.z, m0 = U.w;
-      const int nj = min(TT, nvalid);
-      float acc[8];
+      const int nj = min(NP, nvalid);
+      float acc[8 * NG];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int j = 0; j < 8 * NG; ++j) acc[j] = 0.f;
       // Q4_0 down units of at most 4 tokens run the half-chain form.  (For
       // gate/up it measured slower: a second unrolled chunk body in a kernel
       // held to 64 registers; for Q8_0 its registers spill.)
-      const bool half = MODE == kDown && WQ4 && nj <= 4;  // warp-uniform
+      const bool half = MODE == kDown && WQ4 && NG == 1 && nj <= 4;  // warp-uniform
       float(&acch)[4] = *reinterpret_cast<float(*)[4]>(&acc[0]);  // the half layout's sums
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
         if (!(ok = wait_bar(&B->bs_full[bsi], bph, B, P.err))) break;
         const uint8_t* src = raw + rs * P.raw_bytes;
         const uint8_t* bt = bsb + bsi * bs_stage;
-        const uint8_t* sc = bt + P.kcb * GB;  // the blocks' group-major scale records
+        const uint8_t* sc = bt + NG * P.kcb * GB;  // the blocks' group-major scale records
+        const int gs = P.kcb * GB, ss = P.kcb * SB;  // strides between the unit's groups
         if constexpr (MODE == kGateUp) {
           const uint8_t* row0 = src + 32 * cw * (kKC * BB);
 #pragma unroll
           for (int bl = 0; bl < kKC; bl += 2) {
-            mma_block_rows2<WQ4, false>(row0, kKC * BB, bl * BB, bt + bl * GB, sc + bl * SB, one, g, t, acc);
-            mma_block_rows2<WQ4, true>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, sc + (bl + 1) * SB, one,
-                                       g, t, acc);
+            mma_block_rows2<WQ4, false, NG>(row0, kKC * BB, bl * BB, bt + bl * GB, gs, sc + bl * SB, ss, one, g, t,
+                                            acc);
+            mma_block_rows2<WQ4, true, NG>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, gs,
+                                           sc + (bl + 1) * SB, ss, one, g, t, acc);
           }
         } else {
           const uint8_t* row0 = src + (size_t)(32 * cw) * P.row_bytes;
-          if (WQ4 && half) {
+          if (WQ4 && NG == 1 && half) {
 #pragma unroll 1
             for (int b = 0; b < P.nb; b += 2) {
               mma_block_rows2_half<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc + b * SB, one, g, t, acch);
@@ -493,9 +521,10 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
           } else {
 #pragma unroll 1
             for (int b = 0; b < P.nb; b += 2) {
-              mma_block_rows2<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc + b * SB, one, g, t, acc);
-              mma_block_rows2<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc + (b + 1) * SB, one,
-                                         g, t, acc);
+              mma_block_rows2<WQ4, false, NG>(row0, P.row_bytes, b * BB, bt + b * GB, gs, sc + b * SB, ss, one, g,
+                                              t, acc);
+              mma_block_rows2<WQ4, true, NG>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, gs,
+                                             sc + (b + 1) * SB, ss, one, g, t, acc);
             }
           }
         }
@@ -524,22 +553,23 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
           if (t < 2) acc[4 + j] = other;
         }
       }
-      // acc[4i + 2h + k]: tile row 32cw + 16i + 8h + g, position p0 + 2t + k.
+      // acc[8q + 4i + 2h + k]: tile row 32cw + 16i + 8h + g, position
+      // p0 + 8q + 2t + k.
       if constexpr (MODE == kGateUp) {
-        float* xw = xch + (cw & 1) * 8 * 32;  // [8][32 lanes] per gate/up warp pair
+        float* xw = xch + (cw & 1) * 8 * NG * 32;  // [8 NG][32 lanes] per gate/up warp pair
         if (up_warp) {
           if (!(ok = wait_bar(&B->xch_empty, xph ^ 1, B, P.err))) break;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) xw[j * 32 + lane] = acc[j];
+          for (int j = 0; j < 8 * NG; ++j) xw[j * 32 + lane] = acc[j];
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(&B->xch_full);
           xph ^= 1;
           continue;
         }
         if (!(ok = wait_bar(&B->xch_full, xph, B, P.err))) break;
-        float upv[8];
+        float upv[8 * NG];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) upv[j] = xw[j * 32 + lane];
+        for (int j = 0; j < 8 * NG; ++j) upv[j] = xw[j * 32 + lane];
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&B->xch_empty);
         xph ^= 1;
@@ -551,13 +581,14 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
         if (rbase < P.rows) {
           const int blk = rbase >> 5;
 #pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int pj = 2 * t + k;
+          for (int kk = 0; kk < 2 * NG; ++kk) {
+            const int k = kk & 1, o8 = 8 * (kk >> 1);  // position 2t + k of group kk / 2
+            const int pj = o8 + 2 * t + k;
             float v[4];
             float amax = 0.f;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              v[q] = __fmul_rn(gelu_approx(acc[2 * q + k]), upv[2 * q + k]);
+              v[q] = __fmul_rn(gelu_approx(acc[o8 + 2 * q + k]), upv[o8 + 2 * q + k]);
               float a = fabsf(v[q]);
               if (!(a > 0.f)) a = 0.f;
               amax = fmaxf(amax, a);
@@ -596,9 +627,9 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps), (MMA && MODE == kG
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int row = m0 + 32 * cw + 8 * (j >> 1) + g;  // 16i + 8h = 8 * (2i + h)
-          const int pj = 2 * t + (j & 1);
+        for (int j = 0; j < 8 * NG; ++j) {
+          const int row = m0 + 32 * cw + 8 * ((j & 7) >> 1) + g;  // 16i + 8h = 8 * (2i + h)
+          const int pj = 8 * (j >> 3) + 2 * t + (j & 1);
           if (row < P.rows && pj < nj) P.y[(size_t)(p0 + pj) * P.rows + row] = acc[j];
         }
       }
@@ -713,19 +744,20 @@ struct GvPlan {
 // of the decode kernel; 0 = automatic.
 int g_gv_per_sm = 0, g_gv_ring = 0;
 
-GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma) {
+GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma, int ng) {
   GvPlan p{};
   const int bb = block_bytes(wtype);
   p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
   const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb : 2 * kGvRowsGateUp * row_bytes;
   p.raw_bytes = (raw1 + 1023) & ~1023;
-  const int bs_stage = p.kcb * (256 + kActScaleBytes);
-  const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * kGvRowsGateUp * 4 : 0;
+  const int bs_stage = p.kcb * ng * (256 + kActScaleBytes);
+  const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * ng * kGvRowsGateUp * 4 : 0;
   // With many units, as many CTAs per SM as fit with a double-buffered weight
-  // ring (the kernel's launch bound: 5 for the MMA gate/up product, 4 for the
-  // others); with few units, one CTA and the deepest ring that fits.
-  const int per_sm_max =
-      g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? ((mma && mode == tc::kGateUp) ? 5 : 4) : 1);
+  // ring (the kernel's launch bound: 5 for the MMA gate/up product with one
+  // position group per unit, 3 for Q8_0 weights with two, 4 for the others);
+  // with few units, one CTA and the deepest ring that fits.
+  const int bound = (mma && mode == tc::kGateUp && ng == 1) ? 5 : ((ng == 2 && wtype != kQ4_0) ? 3 : 4);
+  const int per_sm_max = g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? bound : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
     const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
     // Down tiles hold a whole K (one stage per unit); several CTAs per SM
@@ -748,9 +780,9 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   return p;
 }
 
-template <int WQ4, int MODE, int MMA>
+template <int WQ4, int MODE, int MMA, int NG>
 cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, int grid, cudaStream_t s) {
-  auto kern = gv::moe_gemv_kernel<WQ4, MODE, MMA>;
+  auto kern = gv::moe_gemv_kernel<WQ4, MODE, MMA, NG>;
   static int cache[16] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -773,14 +805,21 @@ bool gv_supported(int wtype, int H, int I) {
   if (H % 256 != 0 || I % 32 != 0) return false;
   const int down_row = (I / 32) * block_bytes(wtype);
   if (I % kGvRowsGateUp != 0) return false;
-  if (gv_plan(tc::kGateUp, wtype, H / 32, 0, false, false).smem == 0) return false;
-  if (gv_plan(tc::kDown, wtype, I / 32, down_row, false, false).smem == 0) return false;
+  if (gv_plan(tc::kGateUp, wtype, H / 32, 0, false, false, 1).smem == 0) return false;
+  if (gv_plan(tc::kDown, wtype, I / 32, down_row, false, false, 1).smem == 0) return false;
   return tc_map_available();
 }
 
-cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
-                        const int2* bsc, const int4* units, const int* n_units, int max_units, int npad, int8_t* out_q,
-                        int2* out_s, float* y, int* err, cudaStream_t s) {
+bool gv_two_groups_supported(int wtype, int H, int I) {
+  const int down_row = (I / 32) * block_bytes(wtype);
+  return gv_plan(tc::kGateUp, wtype, H / 32, 0, true, true, 2).smem != 0 &&
+         gv_plan(tc::kDown, wtype, I / 32, down_row, true, true, 2).smem != 0;
+}
+
+cudaError_t launch_gemv(int mode, int wtype, bool mma, int ng, const uint8_t* weights, int H, int I, int E,
+                        const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
+                        int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s) {
+  if (ng != 1 && !(ng == 2 && mma)) return cudaErrorInvalidValue;
   tc::Params P{};
   const int bb = block_bytes(wtype);
   P.bq = bq;
@@ -804,14 +843,14 @@ cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, i
     P.out_nb = I / 32;
     P.down_q4 = wtype == kQ4_0;
     if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp)) return cudaErrorInvalidValue;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng);
   } else {
     P.nb = I / 32;
     P.rows = H;
     P.row_bytes = (I / 32) * bb;
     P.w_raw = weights;
     P.y = y;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng);
   }
   if (pl.smem == 0) return cudaErrorInvalidValue;
   P.rs = pl.rs;
@@ -821,16 +860,25 @@ cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, i
   P.one = 1.0f;
   const int grid = std::max(1, std::min(pl.per_sm * sms, max_units));
   const bool q4 = wtype == kQ4_0;
+  if (mma && ng == 2) {
+    if (mode == tc::kGateUp)
+      return q4 ? gv_launch<1, tc::kGateUp, 1, 2>(map, P, pl.smem, grid, s)
+                : gv_launch<0, tc::kGateUp, 1, 2>(map, P, pl.smem, grid, s);
+    return q4 ? gv_launch<1, tc::kDown, 1, 2>(map, P, pl.smem, grid, s)
+              : gv_launch<0, tc::kDown, 1, 2>(map, P, pl.smem, grid, s);
+  }
   if (mma) {
     if (mode == tc::kGateUp)
-      return q4 ? gv_launch<1, tc::kGateUp, 1>(map, P, pl.smem, grid, s)
-                : gv_launch<0, tc::kGateUp, 1>(map, P, pl.smem, grid, s);
-    return q4 ? gv_launch<1, tc::kDown, 1>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kDown, 1>(map, P, pl.smem, grid, s);
+      return q4 ? gv_launch<1, tc::kGateUp, 1, 1>(map, P, pl.smem, grid, s)
+                : gv_launch<0, tc::kGateUp, 1, 1>(map, P, pl.smem, grid, s);
+    return q4 ? gv_launch<1, tc::kDown, 1, 1>(map, P, pl.smem, grid, s)
+              : gv_launch<0, tc::kDown, 1, 1>(map, P, pl.smem, grid, s);
   }
   if (mode == tc::kGateUp)
-    return q4 ? gv_launch<1, tc::kGateUp, 0>(map, P, pl.smem, grid, s)
-              : gv_launch<0, tc::kGateUp, 0>(map, P, pl.smem, grid, s);
-  return q4 ? gv_launch<1, tc::kDown, 0>(map, P, pl.smem, grid, s) : gv_launch<0, tc::kDown, 0>(map, P, pl.smem, grid, s);
+    return q4 ? gv_launch<1, tc::kGateUp, 0, 1>(map, P, pl.smem, grid, s)
+              : gv_launch<0, tc::kGateUp, 0, 1>(map, P, pl.smem, grid, s);
+  return q4 ? gv_launch<1, tc::kDown, 0, 1>(map, P, pl.smem, grid, s)
+            : gv_launch<0, tc::kDown, 0, 1>(map, P, pl.smem, grid, s);
 }
 
 }  // namespace mrml

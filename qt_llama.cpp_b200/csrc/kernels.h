@@ -39,8 +39,8 @@ cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, i
 cudaError_t launch_geglu(const float* gate, const float* up, float* out, long long n, cudaStream_t s);
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
                             int32_t* cnt, int32_t* poff,
-                            int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units, int NT,
-                            int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s,
+                            int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units,
+                            int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s,
                             const float* logits = nullptr, int K = 0, int32_t* ids_out = nullptr,
                             float* probs_out = nullptr);
 // Whether launch_dispatch can select the experts itself (from `logits`) for
@@ -65,9 +65,12 @@ constexpr int kGvTokens = 8;
 constexpr int kGvRowsGateUp = 64;
 bool gv_supported(int wtype, int H, int I);
 void gv_set_tuning(int per_sm, int ring);
-cudaError_t launch_gemv(int mode, int wtype, bool mma, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
-                        const int2* bsc, const int4* units, const int* n_units, int max_units, int npad, int8_t* out_q,
-                        int2* out_s, float* y, int* err, cudaStream_t s);
+// ng: position groups of 8 per work unit (1, or 2 on the MMA form).
+cudaError_t launch_gemv(int mode, int wtype, bool mma, int ng, const uint8_t* weights, int H, int I, int E,
+                        const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
+                        int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s);
+// Whether the MMA form's 16-position units fit these shapes.
+bool gv_two_groups_supported(int wtype, int H, int I);
 bool tc_supported(int wtype, int H, int I, int NT);
 cudaError_t launch_gemm_tc(int mode, int wtype, int NT, const uint8_t* weights, int H, int I, int E, const int8_t* bq,
                            const int2* bsc, const int4* units, const int* n_units, int max_units, int npad,

@@ -229,12 +229,21 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
   const long long pairs = (long long)T * K * E / e_total;
   const Route route = pick_route(wtype, H, I, E, pairs);
   const bool gv = route == kRouteGemv || route == kRouteGemvMma;
-  const int NT = gv ? mrml::kGvTokens : (pairs > 12ll * E ? 64 : 16);
+  // Work units of 16 positions (two groups of 8) on the MMA form once
+  // experts see about 12 tokens or more: a weight stage and each unpacked
+  // row fragment then serve twice the positions.  Measured on B200: faster
+  // for both products with Q4_0 weights and for the Q8_0 down product; the
+  // Q8_0 gate/up kernel needs more registers for them (3 CTAs per SM instead
+  // of 5) and lost at config 3, so it keeps units of 8.
+  const bool two = route == kRouteGemvMma && pairs >= 12ll * E && mrml::gv_two_groups_supported(wtype, H, I);
+  const int ng_gu = two && wtype == MRML_Q4_0 ? 2 : 1, ng_dn = two ? 2 : 1;
+  const int NT = gv ? mrml::kGvTokens * ng_gu : (pairs > 12ll * E ? 64 : 16);
+  const int NT_dn = gv ? mrml::kGvTokens * ng_dn : NT;
   const int rows_gu = gv ? mrml::kGvRowsGateUp : 128;
   const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;  // down tiles: 128 rows on both paths
   int* n_units = w.status + 2;
   MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, e_first, e_total, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
-                                    n_units, NT, mt_gu, rows_gu, mt_dn, w.status, s, topk_logits, K, ids_out,
+                                    n_units, NT, NT_dn, mt_gu, rows_gu, mt_dn, w.status, s, topk_logits, K, ids_out,
                                     probs_out));
   if (route == kRouteGeneral) {
     MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
@@ -242,7 +251,7 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
                                      w.status, s));
     MRML_LAUNCH(mrml::launch_down(wtype, down, w.cnt, w.poff, w.act, w.ydown, H, I, E, w.status, s));
   } else {
-    const int mu_gu = units_bound(E, K, T, NT, I, rows_gu), mu_dn = units_bound(E, K, T, NT, H, 128);
+    const int mu_gu = units_bound(E, K, T, NT, I, rows_gu), mu_dn = units_bound(E, K, T, NT_dn, H, 128);
     MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, gv, w.xb, w.xs, s));
     if (route == kRouteTensor) {
       MRML_LAUNCH(mrml::launch_gemm_tc(0, wtype, NT, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu,
@@ -250,9 +259,9 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
       MRML_LAUNCH(mrml::launch_gemm_tc(1, wtype, NT, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn,
                                        w.npad, nullptr, nullptr, w.ydown, w.status, s));
     } else {
-      MRML_LAUNCH(mrml::launch_gemv(0, wtype, route == kRouteGemvMma, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad, w.ab,
+      MRML_LAUNCH(mrml::launch_gemv(0, wtype, route == kRouteGemvMma, ng_gu, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad, w.ab,
                                     w.as, nullptr, w.status, s));
-      MRML_LAUNCH(mrml::launch_gemv(1, wtype, route == kRouteGemvMma, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
+      MRML_LAUNCH(mrml::launch_gemv(1, wtype, route == kRouteGemvMma, ng_dn, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
                                     nullptr, nullptr, w.ydown, w.status, s));
     }
   }
