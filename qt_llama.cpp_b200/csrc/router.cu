@@ -7,9 +7,11 @@
 //
 // The logits are computed exactly that way: one thread per (token, expert)
 // runs the reference's chain over the row.  A chain of H dependent f32 adds
-// takes about 4*H cycles (~6 us for H = 2816), and T*E chains run side by
-// side, so the logits, and with them the chosen ids, their order and the
-// softmax weights, equal the reference's bit for bit at every size.
+// is latency-bound (measured on B200: ~9.8 us for H = 2816, about 7 cycles
+// per addition, with the products computed ahead or not), and T*E chains
+// run side by side, so the logits, and with them the chosen ids, their
+// order and the softmax weights, equal the reference's bit for bit at every
+// size.
 #include "common.cuh"
 #include "kernels.h"
 #include "topk.cuh"
