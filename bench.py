@@ -91,9 +91,20 @@ KERNELS = {
 }
 
 
+def expert_kernels(T):
+    """Launch list of the expert products for T tokens on the decode kernels:
+    from 256 tokens the input is quantised per token, then gathered per
+    position group after the dispatch (the library's kGatherMinTokens)."""
+    if T >= 256:
+        return ["quantize_rows", "dispatch", "gather", "gate_up", "down", "combine"]
+    return ["dispatch", "quantize", "gate_up", "down", "combine"]
+
+
 def forward_kernels(T, E, K):
     """Launch list of one mrml_moe_forward call."""
-    return KERNELS["router_small" if T <= 32 and E <= 256 and K <= 64 else "router"]
+    if T <= 32 and E <= 256 and K <= 64:
+        return KERNELS["router_small"]
+    return ["router_logits", "router_topk"] + expert_kernels(T)
 
 
 def peaks():
@@ -214,7 +225,7 @@ class LayerSet:
         self.out = torch.empty(T, H, device=device)
         self.ws = moe.new_workspace(H, I, E, K, T, device)
         self.layer_bytes = layer_bytes
-        self.kernels = forward_kernels(T, E, K) if routing == "router" else KERNELS[routing]
+        self.kernels = forward_kernels(T, E, K) if routing == "router" else ["route_from_logits"] + expert_kernels(T)
 
     def step(self, i, x=None, out=None):
         gu, dn, W = self.layers[i % self.n_layers]
@@ -312,7 +323,8 @@ class EPLayerSet:
         self.ids, self.probs = self.ep.ids, self.ep.probs
         self.ws = self.ep.ws
         self.layer_bytes = layer_bytes
-        self.kernels = KERNELS[routing]  # mrml_moe_router, then the expert shard
+        # mrml_moe_router on the home tokens, then the expert shard on all ranks' tokens
+        self.kernels = ["router_logits", "router_topk"] + expert_kernels(T * world)
 
     @property
     def router_ws(self):

@@ -230,9 +230,11 @@ int mrml_moe_set_option(int option, int value);
  * launches across calls, until the list is used up or the hook is reset
  * with mrml_moe_profile_events(NULL, 0).  Per call: mrml_moe_router 2
  * launches (router_logits, router_topk), mrml_moe_route_from_logits 1,
- * mrml_moe_experts 5 (dispatch, quantize, gate_up, down, combine), and
- * mrml_moe_forward the 7 of both, or 6 up to 32 tokens (router_logits, then
- * the dispatch kernel with the selection, then the other four). */
+ * mrml_moe_experts 5 (dispatch, quantize, gate_up, down, combine) — 6 from
+ * 256 tokens on the decode kernels (quantize_rows, dispatch, gather, gate_up,
+ * down, combine) — and mrml_moe_forward the router's 2 plus those, or 6 up to
+ * 32 tokens (router_logits, then the dispatch kernel with the selection, then
+ * the other four). */
 int mrml_moe_profile_events(void **events, int n_events);
 
 /* Synchronises `stream`, reads and clears the device status word of a

@@ -360,6 +360,48 @@ __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32
   }
 }
 
+// Large batches: the layer input is quantised once per token
+// (quantize_rows_kernel, the same quantiser), then this kernel builds the
+// decode kernel's group-major operand one (position group, block) per warp:
+// lane (j = lane / 4, part = lane % 4) copies 8 bytes of position j's row
+// from its token, so the warp writes the group's whole 256-byte block and
+// 96-byte scale record at once (the per-token scatter writes 16-byte
+// pieces of blocks that other tokens complete later).  Padding positions
+// get zero values and a zero scale.  Positions in use: poff[E].
+__global__ void gather_groups_kernel(const int8_t* __restrict__ xq, const float* __restrict__ xd,
+                                     const int32_t* __restrict__ xsum, const int32_t* __restrict__ pair_at,
+                                     const int32_t* __restrict__ poff_end, int H, int K, int wq4, int npad,
+                                     int8_t* __restrict__ bq, int2* __restrict__ bsc) {
+  // As quantize_scatter_kernel: wait, then trigger, so the expert kernel
+  // that follows may read the dispatch kernel's work units right away.
+  pdl_wait();
+  pdl_trigger();
+  const int nb = H / 32;
+  const long long total = (long long)(*poff_end / 8) * nb;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31, j = lane >> 2, part = lane & 3;
+  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+    const int g = (int)(w / nb), b = (int)(w % nb);
+    const int pos = 8 * g + j;
+    const int pair = pair_at[pos];
+    const int t = pair >= 0 ? pair / K : -1;
+    uint2 v = make_uint2(0u, 0u);
+    if (t >= 0) v = *reinterpret_cast<const uint2*>(xq + (size_t)t * H + 32 * b + 8 * part);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + act_group_offset(true, b, g, nb, npad) + (part >> 1) * 128 +
+                   j * 16 + 8 * (part & 1);
+    *reinterpret_cast<uint2*>(dst) = v;
+    if (part == 0) {
+      float d = 0.f;
+      int corr = kMagicI;
+      if (t >= 0) {
+        d = xd[(size_t)t * nb + b];
+        if (wq4) corr = kMagicI - 8 * xsum[(size_t)t * nb + b];
+      }
+      store_act_scale_gm(bsc, b, pos, nb, d, corr);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // One row-block product for `ntok` tokens is not done here; each thread runs
 // one (row, token) chain over the row's blocks in order, as the reference
@@ -756,6 +798,14 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
                               rows_gu, mt_dn, err, logits, K);
   if (st != cudaSuccess) return st;
   return cudaPeekAtLastError();
+}
+
+cudaError_t launch_gather_groups(int wtype, const int8_t* xq, const float* xd, const int32_t* xsum,
+                                 const int32_t* pair_at, const int32_t* poff_end, int H, int K, int npad, int8_t* bq,
+                                 int2* bsc, cudaStream_t s) {
+  const long long warps = (long long)(npad / 8) * (H / 32);  // upper bound; the kernel reads the count
+  return launch_pdl(gather_groups_kernel, dim3(grid_for_blocks(warps)), dim3(256), 0, s, xq, xd, xsum, pair_at,
+                    poff_end, H, K, wtype == kQ4_0 ? 1 : 0, npad, bq, bsc);
 }
 
 cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,

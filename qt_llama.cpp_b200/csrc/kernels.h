@@ -46,6 +46,12 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
 // Whether launch_dispatch can select the experts itself (from `logits`) for
 // T tokens: the top-k of up to 256 experts, one warp per token.
 bool dispatch_topk_supported(int E, int K, int T);
+// The decode kernel's group-major operand from the per-token quantisation
+// (xq/xd/xsum of launch_quantize_rows) and the dispatch's pair_at; poff_end
+// is the device count of positions in use.
+cudaError_t launch_gather_groups(int wtype, const int8_t* xq, const float* xd, const int32_t* xsum,
+                                 const int32_t* pair_at, const int32_t* poff_end, int H, int K, int npad, int8_t* bq,
+                                 int2* bsc, cudaStream_t s);
 cudaError_t launch_quantize_scatter(int wtype, const float* x, const int32_t* pos, int T, int H, int K, int npad,
                                     bool group_major, int8_t* bq, int2* bsc, cudaStream_t s);
 cudaError_t launch_gate_up(int wtype, const uint8_t* gate_up, const int32_t* cnt, const int32_t* poff,

@@ -53,6 +53,9 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 // Largest token tile of the tensor-core path; position buffers carry this
 // much slack so that a tile starting at the last position stays in bounds.
 constexpr int kMaxNT = 64;
+// Batches from which the decode kernel's operand is quantised per token and
+// then gathered per position group (see run_experts).
+constexpr int kGatherMinTokens = 256;
 
 // Positions after padding every expert's segment to a multiple of 16.
 int npad_alloc(int E, int K, int T) { return (((T * K + 16 * E) + 15) & ~15) + kMaxNT; }
@@ -242,6 +245,11 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
   const int rows_gu = gv ? mrml::kGvRowsGateUp : 128;
   const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;  // down tiles: 128 rows on both paths
   int* n_units = w.status + 2;
+  // From kGatherMinTokens tokens the decode kernel's operand is built in two
+  // steps: the input quantised once per token (before the dispatch, which it
+  // does not depend on), then gathered per position group after it.
+  const bool gather = gv && T >= kGatherMinTokens;
+  if (gather) MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
   MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, e_first, e_total, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
                                     n_units, NT, NT_dn, mt_gu, rows_gu, mt_dn, w.status, s, topk_logits, K, ids_out,
                                     probs_out));
@@ -252,7 +260,11 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
     MRML_LAUNCH(mrml::launch_down(wtype, down, w.cnt, w.poff, w.act, w.ydown, H, I, E, w.status, s));
   } else {
     const int mu_gu = units_bound(E, K, T, NT, I, rows_gu), mu_dn = units_bound(E, K, T, NT_dn, H, 128);
-    MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, gv, w.xb, w.xs, s));
+    if (gather)
+      MRML_LAUNCH(mrml::launch_gather_groups(wtype, w.xq, w.xd, w.xsum, w.pair_at, w.poff + E, H, K, w.npad, w.xb,
+                                             w.xs, s));
+    else
+      MRML_LAUNCH(mrml::launch_quantize_scatter(wtype, x, w.pos, T, H, K, w.npad, gv, w.xb, w.xs, s));
     if (route == kRouteTensor) {
       MRML_LAUNCH(mrml::launch_gemm_tc(0, wtype, NT, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu,
                                        w.npad, w.ab, w.as, nullptr, w.status, s));
