@@ -79,8 +79,11 @@ def _masked_on_gpu(moe, device, wtype, gu, dn, ids, probs, x, H, I, E, first, co
     return out.cpu().numpy()
 
 
+# (2, 2816, 704, 128, 8, 256): the expert-parallel decode shape at N = 4..8
+# (256+ tokens per shard call: the per-token quantisation and group gather,
+# and 16-position units from 12 pairs per expert).
 @pytest.mark.parametrize("wtype,H,I,E,K,T", [(2, 2816, 704, 128, 8, 64), (8, 1024, 512, 16, 2, 300),
-                                              (2, 256, 128, 8, 3, 7)])
+                                              (2, 256, 128, 8, 3, 7), (2, 2816, 704, 128, 8, 256)])
 def test_experts_shard_bit_exact(cuda, moe, oracle, synth, expert_path, wtype, H, I, E, K, T):
     key = (wtype, H, I, E, K, T)
     if key not in _ORACLE:  # the oracle's answers are shared by the three paths
