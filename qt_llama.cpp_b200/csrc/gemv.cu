@@ -578,7 +578,68 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
         // block; the 8 lanes with the same t hold its 32 values for
         // positions 2t and 2t+1.
         const int rbase = m0 + 32 * cw;
-        if (rbase < P.rows) {
+        if (rbase < P.rows && NG == 1 && nj <= 4) {
+          // Units of at most 4 positions: lanes t < 2 hold them, so each
+          // lane pair (t, t ^ 2) splits the work — lane t keeps rows 0-15
+          // of positions 2(t & 1) + k, lane t ^ 2 takes rows 16-31 — and a
+          // lane evaluates 4 GeGLUs instead of 8.  Maxima and sums then
+          // also reduce across the pair; both are order-independent, so the
+          // results are those of the 8-position form.
+          const int blk = rbase >> 5, th = t & 1, ih = t >> 1;
+          float a4[4], u4[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float ra = __shfl_xor_sync(0xffffffffu, acc[4 + j], 2);
+            const float ru = __shfl_xor_sync(0xffffffffu, upv[4 + j], 2);
+            a4[j] = ih ? ra : acc[j];  // a4[2h + k]: row 16 ih + 8h + g, position 2 th + k
+            u4[j] = ih ? ru : upv[j];
+          }
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int pj = 2 * th + k;
+            float v[2];
+            float amax = 0.f;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              v[h] = __fmul_rn(gelu_approx(a4[2 * h + k]), u4[2 * h + k]);
+              float a = fabsf(v[h]);
+              if (!(a > 0.f)) a = 0.f;
+              amax = fmaxf(amax, a);
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float scale = __fdiv_rn(amax, 127.0f);
+            const uint32_t d16 = f32_to_f16_trunc(scale);
+            const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+            int qv[2], qsum = 0;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float rq = round_half_away(__fmul_rn(v[h], id));
+              if (rq != rq) rq = 0.f;
+              rq = fminf(fmaxf(rq, -128.f), 127.f);
+              qv[h] = (int)rq;
+              qsum += qv[h];
+            }
+            qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+            if (pj < nj) {
+              const int pos = p0 + pj;
+              uint8_t* dst = reinterpret_cast<uint8_t*>(P.out_q) + act_group_offset(true, blk, pos >> 3, P.out_nb, P.npad) +
+                             (pos & 7) * 16;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {  // element 16 ih + 8h + g of the block
+                const int e = 16 * ih + 8 * h + g;
+                dst[(e >> 4) * 128 + (e & 15)] = (uint8_t)(int8_t)qv[h];
+              }
+              if (g == 0 && ih == 0) {
+                const int corr = P.down_q4 ? kMagicI - 8 * qsum : kMagicI;
+                store_act_scale_gm(P.out_s, blk, pos, P.out_nb, f16_bits_to_f32(d16), corr);
+              }
+            }
+          }
+        } else if (rbase < P.rows) {
           const int blk = rbase >> 5;
 #pragma unroll
           for (int kk = 0; kk < 2 * NG; ++kk) {
