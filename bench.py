@@ -117,6 +117,24 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def int8_peak_tops():
+    """Dense int8 tensor peak used for the prefill roofline.  MEASURED_PEAKS
+    holds the measured dense bf16 GEMM rate; B200's dense int8 rate is twice
+    its bf16 rate (4.5 vs 2.25 POPS nominal), so the peak is derived as 2x the
+    measured bf16 burst figure (fallback: 2 x 1590 TFLOP/s)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return 2.0 * float(json.load(f)["bf16_tflops"]), "derived: 2 x measured dense bf16 (MEASURED_PEAKS.json)"
+    except Exception:
+        return 2.0 * 1590.0, "derived: 2 x fallback dense bf16 1590 TFLOP/s"
+
+
+def int8_ops(ls, pairs):
+    """int8 multiply-add operations (2 per MAC) of the expert products for
+    `pairs` (token, slot) pairs: gate/up 2I x H and down H x I per pair."""
+    return 2 * pairs * (2 * ls.I * ls.H + ls.H * ls.I), 2 * pairs * (2 * ls.I * ls.H)
+
+
 class ClockSampler:
     """SM clocks and throttle reasons sampled during the timed region: NVML
     every few milliseconds (the timed regions are short), else nvidia-smi."""
@@ -439,8 +457,9 @@ def run_stack(args):
     hbm_peak, peak_kind = peaks()
     ss = StackSet(moe, synth, device, 4, rank, world, exchange=args.ep_exchange)
     graphs = [ss.capture(g) for g in range(2)]
+    reps = repeats_for(ss, args.steps, args.warmup, world, graphs, target_s=1.0, cap=20)
     with ClockSampler(local) as clk:
-        ms = time_steps(ss, args.steps, args.warmup, world, graphs)
+        ms = time_steps(ss, args.steps, args.warmup, world, graphs, reps)
     del graphs
     e2e_ms, h2d, d2h = time_e2e(ss, args.steps, args.warmup, world)
     total_tokens = world * ss.T
@@ -530,24 +549,42 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-def time_steps(ls, steps, warmup, world, graphs):
-    """Device time (ms) of `steps` consecutive graph replays after `warmup`."""
+def time_steps(ls, steps, warmup, world, graphs, repeats=1, stats=None):
+    """Device time (ms) of `steps` consecutive graph replays after `warmup`.
+
+    The K-step region (bracketed by a barrier and a synchronize on both sides,
+    CUDA events on the replay stream, max over ranks) is measured `repeats`
+    times back to back and the median is returned, so that a short region is
+    seen by many clock samples; `stats` (a dict) receives every repeat."""
     import torch
 
     G = len(graphs)
     for i in range(warmup):
         graphs[i % G].replay()
-    barrier(world)
-    torch.cuda.synchronize()
     s = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for i in range(steps):
-        graphs[(warmup + i) % G].replay()
-    e1.record(s)
-    torch.cuda.synchronize()
-    barrier(world)
-    return max_over_ranks(e0.elapsed_time(e1), world)
+    times = []
+    for r in range(repeats):
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(steps):
+            graphs[(warmup + i) % G].replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+        barrier(world)
+        times.append(max_over_ranks(e0.elapsed_time(e1), world))
+    if stats is not None:
+        stats["repeats"] = repeats
+        stats["ms_min"], stats["ms_max"] = round(min(times), 5), round(max(times), 5)
+    return statistics.median(times)
+
+
+def repeats_for(ls, steps, warmup, world, graphs, target_s=0.3, cap=200):
+    """Repeats of the K-step region that fill about `target_s` seconds (at
+    least 5; same count on every rank)."""
+    one = time_steps(ls, steps, warmup, world, graphs)
+    return int(min(cap, max(5, target_s * 1e3 / max(one, 1e-3))))
 
 
 def time_kernels(ls, steps):
@@ -602,7 +639,7 @@ def time_e2e(ls, steps, warmup, world):
             ls.step(g, x=dx)
             host_out[g].copy_(ls.out, non_blocking=True)
         graphs.append(graph)
-    ms = time_steps(ls, steps, warmup, world, graphs)
+    ms = time_steps(ls, steps, warmup, world, graphs, repeats=5)
     return ms, T * H * 4, T * H * 4
 
 
@@ -617,6 +654,23 @@ def algorithmic_bytes(ls, unique, pairs):
     layer = unique * (gu_e + dn_e) + router + T * H * 4 * 2 + T * E * 4 + T * K * 8
     gate_up = unique * gu_e + T * H + T * (H // 32) * 8 + pairs * I * 4
     return layer, gate_up
+
+
+def tensor_roofline(ls, pairs, step_ms, kern, n):
+    """Prefill against the dense int8 tensor peak: the expert products' int8
+    operations per step (and gate/up's per launch) over their time."""
+    peak, src = int8_peak_tops()
+    ops, gu_ops = int8_ops(ls, pairs)
+    prod_ms = (kern["gate_up"] + kern["down"]) / n
+    gu_ms = kern["gate_up"] / n
+    return {"bound": "tensor", "unit": "TOPS", "peak": round(peak, 1), "peak_source": src,
+            "int8_ops_per_step": ops,
+            "layer_achieved": round(ops / (step_ms / 1e3) / 1e12, 2),
+            "layer_frac": round(ops / (step_ms / 1e3) / 1e12 / peak, 4),
+            "products_achieved": round(ops / (prod_ms / 1e3) / 1e12, 2),
+            "products_frac": round(ops / (prod_ms / 1e3) / 1e12 / peak, 4),
+            "gate_up_frac": round(gu_ops / (gu_ms / 1e3) / 1e12 / peak, 4),
+            "instruction": "mma.sync m16n8k32 (warp-level; the legacy tensor path, not tcgen05)"}
 
 
 def cpu_baseline(oracle, ls, budget_s=10.0):
@@ -664,8 +718,10 @@ def run_ours(args):
         ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
     unique, pairs = ls.unique_experts(0)
     graphs = [ls.capture(g) for g in range(2 * ls.n_layers)]
+    reps = repeats_for(ls, steps, warmup, world, graphs)
+    rep_stats = {}
     with ClockSampler(local) as clk:
-        ms = time_steps(ls, steps, warmup, world, graphs)
+        ms = time_steps(ls, steps, warmup, world, graphs, reps, rep_stats)
     del graphs
     kern = time_kernels(ls, steps)
     e2e_ms, h2d, d2h = time_e2e(ls, steps, warmup, world)
@@ -685,6 +741,8 @@ def run_ours(args):
         "steps": steps,
         "warmup": warmup,
         "ms_per_step": round(ms / steps, 5),
+        "timing": {"region": f"{steps} steps", "repeats": rep_stats["repeats"], "reported": "median",
+                   "region_ms_min": rep_stats["ms_min"], "region_ms_max": rep_stats["ms_max"]},
         "higher_is_better": True,
         "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
@@ -718,6 +776,8 @@ def run_ours(args):
         "gpu_launches": (ls.n_kernels() + (4 if world > 1 and args.ep_exchange == "p2p" else 0)) * steps,
         "clocks": clk.summary(),
     }
+    if T >= 2048 and world == 1:
+        line["tensor_roofline"] = tensor_roofline(ls, pairs, ms / steps, kern, steps)
     if world > 1:
         nv = ls.nvlink_bytes()
         comm_ms = ms / steps - total_kern / steps
@@ -748,6 +808,8 @@ def run_ours(args):
                           "gate_up_hbm_frac": round(gb / (k["gate_up"] / n / 1e3) / 1e9 / hbm_peak, 4),
                           "kernel_ms_per_step": {kk: round(v / n, 5) for kk, v in k.items()},
                           "unique_experts_step0": u}
+            if ls.T >= 2048:
+                also[name]["tensor_roofline"] = tensor_roofline(ls, p, m / n, k, n)
         line["also"] = also
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -782,34 +844,37 @@ def traffic_from_profile(workload, kernel="gate_up"):
 
 
 def run_reference(args):
+    """The reference's CPU MoE path (the C restatement under oracle/; the
+    reference's Rust cannot be built here) on the host cores, for the same
+    workload as our arm.  Nothing here touches the GPU or this library: inputs
+    are generated on the host (numpy streams; expert weights quantised with
+    the oracle's C quantisers, the reference's rules).  A step is the whole
+    T-token batch: the router over the batch, then the experts one token at a
+    time as forward_token runs them (model.rs:2111-2165), row-parallel GEMVs
+    on every host thread.  For config 5 a step is one token through the
+    30-layer stack (one layer's weights reused), a bounded sample."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import torch
-
-    moe, synth = package()
+    synth = _load("mrml_moe_b200_synth", os.path.join(ROOT, "qt_llama.cpp_b200", "synth.py"))
     oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
-    stack = args.workload == "c5"  # one token through the 30-layer stack per step
+    stack = args.workload == "c5"
     wtype, H, I, E, K, T, routing = WORKLOADS["c2_t64" if stack else args.workload]
-    if stack:
-        T = 32
-    # Inputs: the same generator as our arm (device-quantised with the
-    # reference's rules when a GPU is present; host numpy otherwise).
-    if torch.cuda.is_available():
-        dev = torch.device("cuda", 0)
-        gu, dn = synth.expert_weights_device(1, wtype, H, I, E, dev, moe.quantize)
-        gu, dn = gu.cpu().numpy(), dn.cpu().numpy()
-    else:
-        gu, dn = synth.expert_weights(1, wtype, H, I, E)
+    if args.workload in STRONG:
+        T = 64  # config 4's 8192-token step is sampled as 64-token batches on the host
+    t_setup = time.perf_counter()
+    gu, dn = synth.expert_weights(1, wtype, H, I, E, quantize_fn=oracle.quantize)
     W = synth.normal(1000, E * H, 0.02).reshape(E, H)
-    x = synth.normal(77, T * H).reshape(T, H)
+    n_batches = 4
+    xs = [synth.normal(77 + j, T * H).reshape(T, H) for j in range(n_batches)]
     bias = synth.zipf_bias(5, E)
+    lgs = [(synth.normal(900 + j, T * E).reshape(T, E) + bias[None, :]).astype(np.float32) for j in range(n_batches)]
+    setup_s = time.perf_counter() - t_setup
     threads = os.cpu_count() or 1
-    per_step = 1 if stack else max(1, min(T, 4))
 
     def one_stack(i):
-        h = x[i % T:i % T + 1]
-        for _ in range(StackSet.N_LAYERS):  # the sample reuses one layer's weights for all 30
+        h = xs[0][i % 32:i % 32 + 1]
+        for _ in range(StackSet.N_LAYERS):
             _, ids, probs = oracle.router(W, h, H, E, K, 1)
             h = oracle.rms_norm(oracle.experts(wtype, gu, dn, ids, probs, None, h, H, I, E, K, 1, threads), None, 1e-6)
         return 1
@@ -817,17 +882,14 @@ def run_reference(args):
     def one(i):
         if stack:
             return one_stack(i)
-        t0 = (i * per_step) % T
-        xt = x[t0:t0 + per_step]
-        n = xt.shape[0]
+        x = xs[i % n_batches]
         if routing == "router":
-            _, ids, probs = oracle.router(W, xt, H, E, K, n)
+            _, ids, probs = oracle.router(W, x, H, E, K, T)
         else:
-            lg = (synth.normal(900 + i, n * E).reshape(n, E) + bias[None, :]).astype(np.float32)
-            ids, probs = oracle.route_from_logits(lg, E, K, n)
-        for t in range(n):  # forward_token processes one token at a time
-            oracle.experts(wtype, gu, dn, ids[t:t + 1], probs[t:t + 1], None, xt[t:t + 1], H, I, E, K, 1, threads)
-        return n
+            ids, probs = oracle.route_from_logits(lgs[i % n_batches], E, K, T)
+        for t in range(T):  # forward_token processes one token at a time
+            oracle.experts(wtype, gu, dn, ids[t:t + 1], probs[t:t + 1], None, x[t:t + 1], H, I, E, K, 1, threads)
+        return T
 
     for i in range(args.warmup):
         one(i)
@@ -835,18 +897,26 @@ def run_reference(args):
     tokens = sum(one(args.warmup + i) for i in range(args.steps))
     dt = time.perf_counter() - t0
     v = tokens / dt
+    per_step = 1 if stack else T
+    sample = (f"1 token through the {StackSet.N_LAYERS}-layer stack (one layer's weights reused) per step" if stack
+              else f"the whole {T}-token batch per step ({args.steps} steps, {tokens} tokens, {dt:.1f} s), "
+                   "one token at a time through the experts")
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": round(v, 3), "unit": "tokens/s", "higher_is_better": True, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "scaling": "strong" if args.workload in STRONG else "weak", "vs_baseline": None,
+        "dtype": "q4_0 weights x q8_0 activations, int32 block dots, f32 accumulate" if wtype == 2 else
+                 "q8_0 weights x q8_0 activations, int32 block dots, f32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights quantised with the reference's rules, N(0,1) x), host-generated",
         "config": {"workload": args.workload, "hidden": H, "experts": E, "top_k": K, "expert_ffn": I,
-                   "tokens_per_step": per_step},
+                   "tokens_per_step": per_step, "weights": "Q4_0" if wtype == 2 else "Q8_0",
+                   "parallelism": "host CPU, row-parallel GEMVs"},
         "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": (f"1 token through the {StackSet.N_LAYERS}-layer stack (one layer's weights "
-                                    "reused) per step" if stack else
-                                    f"{per_step} tokens of the {T}-token batch per step, one token at a time")},
+                         "sample": sample},
         "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_s": round(setup_s, 1),
         "note": "reference is Rust (no toolchain here); the oracle/ C restatement of its CPU MoE path is timed",
     }
     print(json.dumps(line), flush=True)

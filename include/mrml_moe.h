@@ -31,6 +31,10 @@
  *    (rows [0,I) gate, [I,2I) up) and down is [E][H][I/32] blocks.
  *    H and I must be multiples of 32; weight pointers 16-byte aligned.
  *  - Limits: 1 <= K <= 64, K <= E <= 256.
+ *  - Threads: calls may come from any host thread (the reference submits
+ *    from one).  The options of mrml_moe_set_option are process-wide; the
+ *    profiling hook is per thread; the per-device caches are thread-safe.
+ *    Calls that share a workspace must be ordered on one stream.
  */
 #ifndef MRML_MOE_H
 #define MRML_MOE_H
@@ -95,13 +99,27 @@ int mrml_moe_router(const float *W, const float *x, float *logits, int32_t *ids,
  * library, so it allocates nothing and needs no workspace argument; results
  * equal mrml_moe_router's.  Limit: T * E <= 65536, otherwise
  * MRML_ERR_UNSUPPORTED.  The array (about 256 KiB) is held on every GPU that
- * loads the library until the process exits.  The first call on a device looks up the array's device address;
- * make that first call before any stream capture.  All calls on a device
- * share the array (each call clears its counters first), so calls whose
- * kernels can overlap on the GPU, such as calls on unordered streams, race;
- * calls ordered on one stream are fine. */
+ * loads the library until the process exits.  The first call on a device
+ * looks up the array's device address; make that first call before any
+ * stream capture (calls on a stream that is
+ * not capturing look the address up again, so a cudaDeviceReset between
+ * calls is safe).  All calls on a device share the array (each call clears
+ * its status words first), so calls whose kernels can overlap on the GPU,
+ * such as calls on unordered streams, race; calls ordered on one stream are
+ * fine.  A device-side failure (a bounded wait that gave up) is read with
+ * mrml_moe_router_noalloc_status, not mrml_moe_device_status. */
 int mrml_moe_router_noalloc(const float *W, const float *x, float *logits, int32_t *ids, float *probs, int H, int E,
                             int K, int T, mrml_stream_t stream);
+
+/* Synchronises `stream`, then reads and clears the device status word of
+ * mrml_moe_router_noalloc's array on the current device: MRML_OK or
+ * MRML_ERR_DEVICE_TIMEOUT (the router's staging wait gave up; the logits of
+ * the affected tokens were not written).  The word is shared by every
+ * noalloc call on the device and holds the first failure since it was last
+ * cleared (each mrml_moe_router_noalloc call clears it too).  No counterpart
+ * in the reference.  Not capturable: returns MRML_ERR_INVALID_ARGUMENT if
+ * `stream` is being captured. */
+int mrml_moe_router_noalloc_status(mrml_stream_t stream);
 
 /* Top-K and softmax from caller-supplied logits[T][E] (model.rs:1816-1829).
  * Needs no workspace. */
@@ -239,9 +257,10 @@ int mrml_moe_profile_events(void **events, int n_events);
 
 /* Synchronises `stream`, reads and clears the device status word of a
  * workspace: MRML_OK, MRML_ERR_DEVICE_TIMEOUT or MRML_ERR_BAD_EXPERT_ID.
- * *recomputed_tokens (may be NULL) receives 0: the router computes every
- * logit exactly and has no fallback to count (the argument is kept for
- * binary compatibility).  Not capturable. */
+ * recomputed_tokens is deprecated: it may be NULL, and otherwise always
+ * receives 0 (the router computes every logit exactly and has no fallback
+ * to count; the argument stays for binary compatibility and will be removed
+ * at the next major version).  Not capturable. */
 int mrml_moe_device_status(void *workspace, mrml_stream_t stream, int *recomputed_tokens);
 
 #ifdef __cplusplus

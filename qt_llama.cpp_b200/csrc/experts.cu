@@ -751,16 +751,11 @@ int rms_norm_rows_per_cta(int H) {
 }
 
 cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, int T, float eps, cudaStream_t s) {
-  static int cache[16] = {0};
+  static SmemOptIn cache;
   const int r = rms_norm_rows_per_cta(H);
   const size_t smem = (size_t)r * H * 4;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (smem > 48 * 1024 && (dev < 0 || dev >= 16 || cache[dev] < (int)smem)) {
-    cudaError_t st = cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (st != cudaSuccess) return st;
-    if (dev >= 0 && dev < 16) cache[dev] = (int)smem;
-  }
+  const cudaError_t st = ensure_smem(rms_norm_kernel, smem, cache);
+  if (st != cudaSuccess) return st;
   return launch_pdl(rms_norm_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, x, w, out, H, T, eps);
 }
 

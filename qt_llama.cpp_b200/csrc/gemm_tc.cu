@@ -493,12 +493,13 @@ bool make_gate_up_map(CUtensorMap* m, const uint8_t* w, int wtype, int H, int I,
 }
 
 int num_sms() {
-  static int n[16] = {0};
-  int dev = 0;
+  static std::atomic<int> n[kMaxDevices];
+  int dev = 0, v = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 16) return 148;
-  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
-  return n[dev] > 0 ? n[dev] : 148;
+  if (dev >= 0 && dev < kMaxDevices && (v = n[dev].load(std::memory_order_relaxed)) > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) return 148;
+  if (dev >= 0 && dev < kMaxDevices) n[dev].store(v, std::memory_order_relaxed);
+  return v;
 }
 
 constexpr int kSmemLimit = 227 * 1024;
@@ -541,14 +542,9 @@ Plan plan_for(int mode, int wtype, int NT, int nb, int rows_other, int row_bytes
 template <int WQ4, int MODE, int NT>
 cudaError_t launch_one(const CUtensorMap& map, const tc::Params& P, size_t smem, int grid, cudaStream_t s) {
   auto kern = tc::moe_gemm_tc_kernel<WQ4, MODE, NT>;
-  static int cache[16] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 16 || cache[dev] < (int)smem) {
-    cudaError_t st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (st != cudaSuccess) return st;
-    if (dev >= 0 && dev < 16) cache[dev] = (int)smem;
-  }
+  static SmemOptIn cache;
+  const cudaError_t st = ensure_smem(kern, smem, cache);
+  if (st != cudaSuccess) return st;
   constexpr int threads = 32 * (tc::kEpiWarp0 + 4 * ((NT + 31) / 32));
   kern<<<grid, threads, smem, s>>>(map, P);
   return cudaPeekAtLastError();

@@ -803,7 +803,7 @@ struct GvPlan {
 // in flight on its own).
 // Tuning overrides (mrml_moe_set_option): CTAs per SM and weight-ring depth
 // of the decode kernel; 0 = automatic.
-int g_gv_per_sm = 0, g_gv_ring = 0;
+std::atomic<int> g_gv_per_sm{0}, g_gv_ring{0};
 
 GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma, int ng) {
   GvPlan p{};
@@ -818,13 +818,14 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   // position group per unit, 3 for Q8_0 weights with two, 4 for the others);
   // with few units, one CTA and the deepest ring that fits.
   const int bound = (mma && mode == tc::kGateUp && ng == 1) ? 5 : ((ng == 2 && wtype != kQ4_0) ? 3 : 4);
-  const int per_sm_max = g_gv_per_sm > 0 ? g_gv_per_sm : (many_units ? bound : 1);
+  const int per_sm_set = g_gv_per_sm.load(), ring_set = g_gv_ring.load();
+  const int per_sm_max = per_sm_set > 0 ? per_sm_set : (many_units ? bound : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
     const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
     // Down tiles hold a whole K (one stage per unit); several CTAs per SM
     // overlap one another's loads, so a single stage each is allowed there.
     const int rs_min = (per_sm > 1 && mode == tc::kGateUp) ? 2 : 1;
-    const int rs_max = g_gv_ring > 0 ? g_gv_ring : tc::kMaxRaw;
+    const int rs_max = ring_set > 0 ? ring_set : tc::kMaxRaw;
     for (int rs = rs_max; rs >= rs_min; --rs)
       for (int bs = 2; bs >= 1; --bs) {
         const size_t total = 128 + tc::kGvBarBytes + (size_t)rs * p.raw_bytes + (size_t)bs * bs_stage + xch_bytes;
@@ -844,14 +845,9 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
 template <int WQ4, int MODE, int MMA, int NG>
 cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, int grid, cudaStream_t s) {
   auto kern = gv::moe_gemv_kernel<WQ4, MODE, MMA, NG>;
-  static int cache[16] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 16 || cache[dev] < (int)smem) {
-    cudaError_t st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (st != cudaSuccess) return st;
-    if (dev >= 0 && dev < 16) cache[dev] = (int)smem;
-  }
+  static SmemOptIn cache;
+  const cudaError_t st = ensure_smem(kern, smem, cache);
+  if (st != cudaSuccess) return st;
   return launch_pdl(kern, dim3(grid), dim3(32 * (gv::kComp0 + gv::kCompWarps)), smem, s, map, P);
 }
 

@@ -4,7 +4,47 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
 namespace mrml {
+
+// Shape limits shared by every entry point (the top-k keeps up to 256
+// experts in a warp's registers and up to 64 candidates in shared memory).
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 64;
+// Devices whose per-device host caches are kept (higher ordinals work, but
+// repeat the cached lookups on every call).
+constexpr int kMaxDevices = 64;
+
+// The dynamic shared memory a kernel has been opened up to on each device.
+// cudaFuncSetAttribute is host-side state, not a stream operation; calling
+// it once per (kernel, device, size) keeps it off the decode path's host
+// time.  Safe to call from several host threads: the fast path reads an
+// atomic, and the attribute only ever grows (under a lock), so a thread
+// cannot lower the limit another thread is about to launch with.
+struct SmemOptIn {
+  std::atomic<int> bytes[kMaxDevices];
+};
+inline std::mutex& smem_opt_in_lock() {
+  static std::mutex m;
+  return m;
+}
+template <typename Kern>
+inline cudaError_t ensure_smem(Kern k, size_t bytes, SmemOptIn& c) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  const bool cached = dev >= 0 && dev < kMaxDevices;
+  if (cached && c.bytes[dev].load(std::memory_order_acquire) >= (int)bytes) return cudaSuccess;
+  std::lock_guard<std::mutex> lock(smem_opt_in_lock());
+  const int target = cached ? std::max((int)bytes, c.bytes[dev].load(std::memory_order_relaxed)) : (int)bytes;
+  st = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, target);
+  if (st == cudaSuccess && cached) c.bytes[dev].store(target, std::memory_order_release);
+  return st;
+}
 
 // Launches `kern` with programmatic dependent launch: the grid may start
 // while the previous kernel on the stream finishes (its CTAs run their

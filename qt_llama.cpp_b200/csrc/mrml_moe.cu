@@ -6,6 +6,7 @@
 #include <stdio.h>
 
 #include "../../include/mrml_moe.h"
+#include "checks.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -14,8 +15,9 @@ namespace {
 using mrml::kQ4_0;
 using mrml::kQ8_0;
 
-constexpr int kMaxE = 256;
-constexpr int kMaxK = 64;
+using mrml::check_router_args;
+constexpr int kMaxE = mrml::kMaxExperts;
+constexpr int kMaxK = mrml::kMaxTopK;
 
 // Optional per-launch profiling events (thread-local; see
 // mrml_moe_profile_events).  Slot 2i is recorded before launch i of a call,
@@ -124,21 +126,23 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
   return w;
 }
 
-// Expert-product path: 0 = automatic, 1 = CUDA-core dp4a, 2 = tensor cores.
-int g_path = 0;
+// Expert-product path (MRML_OPTION_EXPERT_PATH): 0 = automatic, else the
+// forced path; process-wide, set from any host thread.
+std::atomic<int> g_path{0};
 
 // Once per device: is it an sm_100 part?
 int check_device() {
-  static int verdict[64] = {0};  // 0 unknown, 1 ok, -1 wrong arch
+  static std::atomic<int> verdict[mrml::kMaxDevices];  // 0 unknown, 1 ok, -1 wrong arch
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MRML_ERR_CUDA;
-  if (dev < 0 || dev >= 64) return MRML_ERR_DEVICE;
-  if (verdict[dev] == 0) {
+  int v = dev >= 0 && dev < mrml::kMaxDevices ? verdict[dev].load(std::memory_order_relaxed) : 0;
+  if (v == 0) {
     int major = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return MRML_ERR_CUDA;
-    verdict[dev] = major == 10 ? 1 : -1;
+    v = major == 10 ? 1 : -1;
+    if (dev >= 0 && dev < mrml::kMaxDevices) verdict[dev].store(v, std::memory_order_relaxed);
   }
-  return verdict[dev] == 1 ? MRML_OK : MRML_ERR_DEVICE;
+  return v == 1 ? MRML_OK : MRML_ERR_DEVICE;
 }
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
@@ -150,15 +154,6 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? MRML_OK : MRML_ERR_CU
     const int _st = (expr);            \
     if (_st != MRML_OK) return _st;    \
   } while (0)
-
-int check_router_args(const float* W, const float* x, const float* logits, const int32_t* ids, const float* probs,
-                      int H, int E, int K, int T) {
-  if (H <= 0 || E <= 0 || K <= 0 || T < 0) return MRML_ERR_INVALID_ARGUMENT;
-  if (K > E) return MRML_ERR_INVALID_ARGUMENT;
-  if (E > kMaxE || K > kMaxK) return MRML_ERR_UNSUPPORTED;
-  if (T > 0 && (!W || !x || !logits || !ids || !probs)) return MRML_ERR_INVALID_ARGUMENT;
-  return MRML_OK;
-}
 
 int check_expert_args(int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids, const float* probs,
                       const float* x, const float* out, int H, int I, int E, int K, int T) {
@@ -204,7 +199,7 @@ enum Route { kRouteGeneral = 0, kRouteGemv = 1, kRouteTensor = 2, kRouteGemvMma 
 Route pick_route(int wtype, int H, int I, int E, long long pairs) {
   const bool tc = mrml::tc_supported(wtype, H, I, 64) && mrml::tc_supported(wtype, H, I, 16);
   const bool gv = mrml::gv_supported(wtype, H, I);
-  switch (g_path) {
+  switch (g_path.load(std::memory_order_relaxed)) {
     case 1: return gv ? kRouteGemv : kRouteGeneral;
     case 2: return tc ? kRouteTensor : (gv ? kRouteGemv : kRouteGeneral);
     case 3: return kRouteGeneral;
@@ -429,21 +424,21 @@ int mrml_moe_quantize_q4_0(const float* src, uint8_t* dst, size_t n, mrml_stream
 }
 
 int mrml_moe_set_option(int option, int value) {
-  static int gv_per_sm = 0, gv_ring = 0;
+  static std::atomic<int> gv_per_sm{0}, gv_ring{0};
   switch (option) {
     case MRML_OPTION_EXPERT_PATH:
       if (value < 0 || value > 4) return MRML_ERR_INVALID_ARGUMENT;
-      g_path = value;
+      g_path.store(value, std::memory_order_relaxed);
       return MRML_OK;
     case MRML_OPTION_DECODE_CTAS_PER_SM:
       if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
-      gv_per_sm = value;
-      mrml::gv_set_tuning(gv_per_sm, gv_ring);
+      gv_per_sm.store(value);
+      mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load());
       return MRML_OK;
     case MRML_OPTION_DECODE_RING:
       if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
-      gv_ring = value;
-      mrml::gv_set_tuning(gv_per_sm, gv_ring);
+      gv_ring.store(value);
+      mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load());
       return MRML_OK;
     default:
       return MRML_ERR_INVALID_ARGUMENT;

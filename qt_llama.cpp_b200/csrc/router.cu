@@ -334,24 +334,9 @@ __global__ void __launch_bounds__(32 * kTopkWarps)
 
 // ------------------------------------------------------------ launchers ---
 
-// cudaFuncSetAttribute once per (kernel, device, size): it is host-side
-// state and not a stream operation, but calling it on every launch costs
-// host time on the decode path.
-template <typename Kern>
-cudaError_t ensure_smem(Kern k, size_t bytes, int* cache) {
-  if (bytes <= 48 * 1024) return cudaSuccess;
-  int dev = 0;
-  cudaError_t st = cudaGetDevice(&dev);
-  if (st != cudaSuccess) return st;
-  if (dev >= 0 && dev < 16 && cache[dev] >= (int)bytes) return cudaSuccess;
-  st = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  if (st == cudaSuccess && dev >= 0 && dev < 16) cache[dev] = (int)bytes;
-  return st;
-}
-
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
                                  cudaStream_t s) {
-  static int cache[16] = {0}, cache_rows[16] = {0}, cache_tiled[16] = {0};
+  static SmemOptIn cache, cache_rows, cache_tiled;
   const bool aligned = (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
   // Large batches: the tiled kernel (throughput); decode batches: whole rows
   // per CTA (latency).  Measured crossover on B200 at H = 2816: ~256 tokens.

@@ -42,6 +42,7 @@ SIGNATURES = {
     "mrml_moe_router": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "mrml_moe_route_from_logits": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "mrml_moe_router_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "mrml_moe_router_noalloc_status": (_i, [_vp]),
     "mrml_moe_experts": (
         _i,
         [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp],

@@ -135,16 +135,20 @@ def quantize(x: np.ndarray, wtype: int) -> np.ndarray:
     raise ValueError(f"unsupported weight type {wtype}")
 
 
-def expert_weights(seed: int, wtype: int, H: int, I: int, E: int, std: float = 0.02):
+def expert_weights(seed: int, wtype: int, H: int, I: int, E: int, std: float = 0.02, quantize_fn=None):
     """GGUF-layout expert slabs: gate_up [E][2I][H/32 blocks], down [E][H][I/32 blocks].
 
-    Generated and quantised one expert at a time to bound host memory."""
+    Generated and quantised one expert at a time to bound host memory.
+    quantize_fn(rows, wtype) -> bytes may replace the numpy quantisers (for
+    instance a compiled one with the same rules, for large layers)."""
     bb = BLOCK_BYTES[wtype]
+    q = quantize if quantize_fn is None else quantize_fn
     gu = np.empty((E, 2 * I, H // 32 * bb), dtype=np.uint8)
     dn = np.empty((E, H, I // 32 * bb), dtype=np.uint8)
     for e in range(E):
-        gu[e] = quantize(normal(seed * 1000003 + 2 * e + 1, 2 * I * H, std).reshape(2 * I, H), wtype)
-        dn[e] = quantize(normal(seed * 1000003 + 2 * e + 2, H * I, std).reshape(H, I), wtype)
+        gu[e] = np.asarray(q(normal(seed * 1000003 + 2 * e + 1, 2 * I * H, std).reshape(2 * I, H), wtype)).reshape(
+            2 * I, -1)
+        dn[e] = np.asarray(q(normal(seed * 1000003 + 2 * e + 2, H * I, std).reshape(H, I), wtype)).reshape(H, -1)
     return gu, dn
 
 

@@ -482,3 +482,79 @@ def test_paths_bit_identical(cuda, moe, synth, c2_q4, wtype, T):
         moe.set_expert_path(0)
     for o in outs[1:]:
         assert_exact(o, outs[0])
+
+
+# ------------------------------------------------- large configs, sampled
+# Tokens are independent in the MoE layer, so a large batch is checked by
+# running the oracle on a seeded sample of its tokens: the GPU computes the
+# whole batch (every expert sees its full load, the large-batch kernels run),
+# the oracle recomputes the sampled tokens alone.
+
+
+def sample_tokens(T, n, seed):
+    return np.sort(np.random.default_rng(seed).choice(T, size=min(n, T), replace=False))
+
+
+@pytest.fixture(scope="module")
+def c2_q8(cuda, moe, synth):
+    """The config-2 layer with Q8_0 expert weights (host copies)."""
+    gu, dn = synth.expert_weights_device(6, 8, 2816, 704, 128, cuda, moe.quantize)
+    return gu.cpu().numpy(), dn.cpu().numpy()
+
+
+def test_config4_q4_forward_sampled(cuda, moe, oracle, synth, c2_q4):
+    """Config 4's per-step batch on one GPU: the C2 layer (Q4_0) at T = 8192
+    through mrml_moe_forward (router included); every token's ids and a
+    sample of 256 tokens' outputs against the oracle."""
+    H, I, E, K, T = 2816, 704, 128, 8, 8192
+    gu, dn = c2_q4
+    W = synth.normal(60, E * H, 0.02).reshape(E, H)
+    x = synth.normal(61, T * H).reshape(T, H)
+    L = Layer(moe, cuda, 2, gu, dn, W, H, I, E, K, T)
+    ids, probs, out, _ = L.forward(x)
+    idx = sample_tokens(T, 256, 62)
+    _, r_ids, r_probs = oracle.router(W, x[idx], H, E, K, len(idx))
+    assert np.array_equal(ids[idx], r_ids)
+    assert_exact(probs[idx], r_probs)
+    ref = oracle.experts(2, gu, dn, r_ids, r_probs, None, x[idx], H, I, E, K, len(idx), 16)
+    assert_exact(out[idx], ref)
+    # the tokens outside the sample were computed too: no zero rows
+    assert np.all(np.abs(out).max(axis=1) > 0)
+
+
+def test_config4_q8_zipf_sampled(cuda, moe, oracle, synth, c2_q8):
+    """Config 4's Q8_0 variant with uniform-plus-Zipf routing (logits N(0,1)
+    plus the per-expert Zipf(1.1) bias): T = 8192, all ids checked, 256
+    sampled tokens' outputs checked."""
+    H, I, E, K, T = 2816, 704, 128, 8, 8192
+    gu, dn = c2_q8
+    x = synth.normal(63, T * H).reshape(T, H)
+    logits = (synth.normal(64, T * E).reshape(T, E) + synth.zipf_bias(65, E)[None, :]).astype(np.float32)
+    L = Layer(moe, cuda, 8, gu, dn, None, H, I, E, K, T)
+    d_logits = dev_tensor(logits, cuda)
+    moe.route_from_logits(d_logits, L.ids, L.probs, E, K, T)
+    ids, probs = L.ids.cpu().numpy(), L.probs.cpu().numpy()
+    r_ids, r_probs = oracle.route_from_logits(logits, E, K, T)
+    assert np.array_equal(ids, r_ids)
+    assert_exact(probs, r_probs)
+    out = L.experts(x, r_ids, r_probs)
+    idx = sample_tokens(T, 256, 66)
+    ref = oracle.experts(8, gu, dn, r_ids[idx], r_probs[idx], None, x[idx], H, I, E, K, len(idx), 16)
+    assert_exact(out[idx], ref)
+    counts = np.bincount(r_ids.reshape(-1), minlength=E)
+    assert counts.max() > 3 * counts.min()
+
+
+def test_c2_q8_prefill_2048_sampled(cuda, moe, oracle, synth, c2_q8):
+    """The larger prefill probe: the C2 layer in Q8_0 at T = 2048 with Zipf
+    routing; 512 sampled tokens against the oracle."""
+    H, I, E, K, T = 2816, 704, 128, 8, 2048
+    gu, dn = c2_q8
+    x = synth.normal(67, T * H).reshape(T, H)
+    logits = (synth.normal(68, T * E).reshape(T, E) + synth.zipf_bias(69, E)[None, :]).astype(np.float32)
+    r_ids, r_probs = oracle.route_from_logits(logits, E, K, T)
+    L = Layer(moe, cuda, 8, gu, dn, None, H, I, E, K, T)
+    out = L.experts(x, r_ids, r_probs)
+    idx = sample_tokens(T, 512, 70)
+    ref = oracle.experts(8, gu, dn, r_ids[idx], r_probs[idx], None, x[idx], H, I, E, K, len(idx), 16)
+    assert_exact(out[idx], ref)

@@ -55,6 +55,25 @@ def test_noalloc_router_matches_workspace_router_on_consecutive_calls(cuda, moe,
         assert np.array_equal(got[2], ref[2]) and np.array_equal(got[0], ref[0])
 
 
+def test_noalloc_router_at_the_size_limit(cuda, moe, synth):
+    """T * E exactly at the fixed limit (512 x 128 = 65536): accepted, runs the
+    large-batch (tiled) logits kernel, and matches the workspace router bit
+    for bit; the status reader then reports no device-side failure."""
+    import torch
+
+    H, E, K, T = 2816, 128, 8, 512
+    W = torch.from_numpy(synth.normal(302, E * H, 0.02).reshape(E, H)).to(cuda)
+    x = torch.from_numpy(synth.normal(402, T * H).reshape(T, H)).to(cuda)
+    ws = moe.new_workspace(32, 32, E, K, T, cuda)
+    ref = _route(moe, moe.router, W, x, H, E, K, T, cuda, ws)
+    got = _route(moe, moe.router_noalloc, W, x, H, E, K, T, cuda)
+    assert np.array_equal(got[1], ref[1])
+    assert np.array_equal(got[2], ref[2]) and np.array_equal(got[0], ref[0])
+    lib = moe.load_library()
+    assert lib.mrml_moe_router_noalloc_status(None) == 0
+    assert lib.mrml_moe_router_noalloc_status(None) == 0  # reading clears; still clean
+
+
 def test_noalloc_router_rejects_oversized_batches(cuda, moe):
     lib = moe.load_library()
     P = ctypes.c_void_p(0x1000)
