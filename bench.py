@@ -718,7 +718,7 @@ def run_ours(args):
         ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
     unique, pairs = ls.unique_experts(0)
     graphs = [ls.capture(g) for g in range(2 * ls.n_layers)]
-    reps = repeats_for(ls, steps, warmup, world, graphs)
+    reps = args.repeats if args.repeats > 0 else repeats_for(ls, steps, warmup, world, graphs)
     rep_stats = {}
     with ClockSampler(local) as clk:
         ms = time_steps(ls, steps, warmup, world, graphs, reps, rep_stats)
@@ -931,6 +931,8 @@ def main():
     ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS) + ["c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-also", action="store_true")
+    ap.add_argument("--repeats", type=int, default=0,
+                    help="repeats of the timed K-step region (median reported); 0 = enough for ~0.3 s")
     ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel exchange for --gpus N > 1")
     ap.add_argument("--expert-path", type=int, default=0,
