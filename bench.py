@@ -215,18 +215,23 @@ class LayerSet:
     """Independent copies of one MoE layer on the device (weights + router),
     enough of them that their weights exceed L2, plus per-step inputs."""
 
-    def __init__(self, moe, synth, device, name, n_inputs, seed=0):
+    def __init__(self, moe, synth, device, name, n_inputs, seed=0, packed=False):
         import torch
 
         wtype, H, I, E, K, T, routing = WORKLOADS[name]
         self.moe, self.device, self.name = moe, device, name
         self.wtype, self.H, self.I, self.E, self.K, self.T, self.routing = wtype, H, I, E, K, T, routing
+        # the weight type passed to the library: packed weights carry the flag
+        self.wcall = wtype | (moe.MRML_PACKED if packed else 0)
         bb = 18 if wtype == 2 else 34
         layer_bytes = E * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
         self.n_layers = max(2, -(-4 * L2_BYTES // layer_bytes))
         self.layers = []
         for l in range(self.n_layers):
             gu, dn = synth.expert_weights_device(seed * 100 + l + 1, wtype, H, I, E, device, moe.quantize)
+            if packed:  # the load-time repack (mrml_moe_prepare_weights), outside the timed steps
+                gu, dn = moe.prepare_weights(wtype, gu, dn)
+                torch.cuda.synchronize()
             g = torch.Generator(device=device)
             g.manual_seed(seed * 100 + l + 1000)
             W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
@@ -251,11 +256,11 @@ class LayerSet:
         out = self.out if out is None else out
         m = self.moe
         if self.routing == "router":
-            m.forward(self.wtype, W, x, x, gu, dn, None, self.logits, self.ids, self.probs, out, self.H, self.I,
+            m.forward(self.wcall, W, x, x, gu, dn, None, self.logits, self.ids, self.probs, out, self.H, self.I,
                       self.E, self.K, self.T, self.ws)
         else:
             m.route_from_logits(self.logit_in[i % len(self.logit_in)], self.ids, self.probs, self.E, self.K, self.T)
-            m.experts(self.wtype, gu, dn, self.ids, self.probs, None, x, out, self.H, self.I, self.E, self.K, self.T,
+            m.experts(self.wcall, gu, dn, self.ids, self.probs, None, x, out, self.H, self.I, self.E, self.K, self.T,
                       self.ws)
 
     def capture(self, i, profile_events=None):
@@ -715,7 +720,7 @@ def run_ours(args):
     if world > 1:
         ls = EPLayerSet(moe, synth, device, args.workload, 8, rank, world, exchange=args.ep_exchange)
     else:
-        ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank)
+        ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank, packed=args.weights == "packed")
     unique, pairs = ls.unique_experts(0)
     graphs = [ls.capture(g) for g in range(2 * ls.n_layers)]
     reps = args.repeats if args.repeats > 0 else repeats_for(ls, steps, warmup, world, graphs)
@@ -795,7 +800,7 @@ def run_ours(args):
                 continue
             del ls
             torch.cuda.empty_cache()
-            ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank)
+            ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank, packed=args.weights == "packed")
             u, p = ls.unique_experts(0)
             n = max(steps, 20)
             gr = [ls.capture(g) for g in range(2 * ls.n_layers)]
@@ -931,6 +936,9 @@ def main():
     ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS) + ["c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-also", action="store_true")
+    ap.add_argument("--weights", default="gguf", choices=["gguf", "packed"],
+                    help="expert weights as the GGUF slabs (the reference's layout) or repacked at load time by "
+                         "mrml_moe_prepare_weights")
     ap.add_argument("--repeats", type=int, default=0,
                     help="repeats of the timed K-step region (median reported); 0 = enough for ~0.3 s")
     ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],

@@ -59,8 +59,11 @@ typedef enum {
   MRML_ERR_BAD_EXPERT_ID = -7,     /* reported by mrml_moe_device_status */
 } mrml_status;
 
-/* GGML type ids (crates/mrml-tensor/src/types.rs:7-27). */
-enum { MRML_Q4_0 = 2, MRML_Q8_0 = 8 };
+/* GGML type ids (crates/mrml-tensor/src/types.rs:7-27).  MRML_PACKED or'ed
+ * into a weight type marks expert weights repacked by
+ * mrml_moe_prepare_weights (no counterpart in the reference). */
+enum { MRML_Q4_0 = 2, MRML_Q8_0 = 8, MRML_PACKED = 0x100 };
+enum { MRML_Q4_0_PACKED = MRML_Q4_0 | MRML_PACKED, MRML_Q8_0_PACKED = MRML_Q8_0 | MRML_PACKED };
 
 /* Library version (major*10000 + minor*100 + patch). */
 int mrml_moe_version(void);
@@ -195,6 +198,25 @@ int mrml_moe_forward(int wtype, const float *router_w, const float *router_x, co
                      const uint8_t *down, const float *down_scale, float *logits, int32_t *ids, float *probs,
                      float *out, int H, int I, int E, int K, int T, void *workspace, size_t workspace_bytes,
                      mrml_stream_t stream);
+
+/* Bytes of one layer's expert weights: which = 0 gate_up ([E][2I][H/32]
+ * blocks), 1 down ([E][H][I/32] blocks); the same for the GGUF layout and
+ * the packed one.  0 for an invalid shape. */
+size_t mrml_moe_weights_bytes(int wtype, int H, int I, int E, int which);
+
+/* Load-time repack of one layer's GGUF expert weights (the slabs the
+ * reference uploads unchanged, model.rs:726-741, read from the GGUF file at
+ * model.rs:630-755) into the layout the decode expert kernel reads fastest:
+ * the same bytes (same size), reordered so that every lane of the warp-level
+ * MMA reads its weight fragment and both rows' f16 scales with aligned vector
+ * loads.  Pass the packed buffers to mrml_moe_experts / _forward / _shard
+ * with wtype | MRML_PACKED; results are bit-identical to the GGUF layout's.
+ * No counterpart in the reference (its GPU path reads the raw blocks).
+ * wtype MRML_Q4_0 or MRML_Q8_0; outputs mrml_moe_weights_bytes each, 16-byte
+ * aligned, not overlapping the inputs.  Needs H a multiple of 256 and I of
+ * 64 (MRML_ERR_UNSUPPORTED otherwise).  Enqueued on `stream`; capturable. */
+int mrml_moe_prepare_weights(int wtype, const uint8_t *gate_up, const uint8_t *down, uint8_t *gate_up_packed,
+                             uint8_t *down_packed, int H, int I, int E, mrml_stream_t stream);
 
 /* The weighted combine alone (model.rs:2163-2165): out[t][i] = sum over
  * k ascending of (probs[t,k] * ydown[pos[t,k]][i]) * down_scale[ids[t,k]],

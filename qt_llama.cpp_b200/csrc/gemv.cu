@@ -32,6 +32,13 @@ using tc::kM;
 using tc::Params;
 using tc::wait_bar;
 
+// CTAs per SM of the warp-MMA gate/up kernel with one position group per
+// unit (its launch bound: 5 leaves 64 registers per thread).
+#ifndef MRML_GV_GATE_UP_CTAS
+#define MRML_GV_GATE_UP_CTAS 5
+#endif
+constexpr int kGateUpCtas = MRML_GV_GATE_UP_CTAS;
+
 constexpr int kComp0 = 2;      // first compute warp
 constexpr int kCompWarps = 4;  // 128 threads, one weight row each
 
@@ -89,20 +96,20 @@ __device__ __forceinline__ void block_words(const uint32_t* qs, uint32_t (&w)[8]
 template <int WQ4, int TT>
 __device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, const uint8_t* rec,
                                              int nj, float (&acc)[TT]) {
-  // Tokens in pairs: the record holds d(t), d(t+1) and corr(t), corr(t+1)
-  // (even t) as adjacent words, one 8-byte load each.
+  // Tokens in pairs: for even t the record holds {d(t), d(t), d(t+1),
+  // d(t+1)} and {corr(t), corr(t+1), ...} as 16-byte groups, one load each.
 #pragma unroll
   for (int t = 0; t < TT; t += 2) {
     if (t < nj) {
-      const int2 dd = *reinterpret_cast<const int2*>(rec + 4 * t);
-      const int2 cc = *reinterpret_cast<const int2*>(rec + 32 + 8 * t);
+      const int4 dd = *reinterpret_cast<const int4*>(rec + 8 * t);
+      const int2 cc = *reinterpret_cast<const int2*>(rec + 64 + 8 * t);
 #pragma unroll
       for (int k = 0; k < 2 && t + k < TT; ++k) {
         if (k == 0 || t + 1 < nj) {
           const uint8_t* a = btile + (t + k) * 16;
           const uint4 alo = *reinterpret_cast<const uint4*>(a);
           const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
-          const float da = __int_as_float(k ? dd.y : dd.x);
+          const float da = __int_as_float(k ? dd.z : dd.x);
           const float f =
               __fsub_rn(__int_as_float(block_isum_bits<WQ4>(w, alo, ahi, k ? cc.y : cc.x)), kMagicF);  // exact
           acc[t + k] = __fadd_rn(acc[t + k], __fmul_rn(f, __fmul_rn(dw, da)));
@@ -204,47 +211,93 @@ __device__ __forceinline__ void f2_acc(float& a0, float& a1, uint64_t p, uint64_
   f2_unpack(f2_fma(p, one, f2_pack(a0, a1)), a0, a1);
 }
 
-// One quant block for the warp's two 16-row tiles (rows r0+16i+g, +8) and
+// Fragment loaders of the MMA path: lane (g, t)'s A fragment of one 16-row
+// tile and one quant block (a0/a2 = row g, elements 4t.. / 16+4t..; a1/a3 =
+// row g+8) and the two rows' scales {d_w(g), d_w(g+8)} as an f32 pair.
+//
+// Raw GGUF rows staged in shared memory: row g of the tile at `ra`, the block
+// `boff` bytes into the row; blocks of odd index in a 4-byte aligned row have
+// their values 4-byte aligned (ODD), even ones 2 bytes past.
+template <int WQ4, bool ODD>
+struct RawFrag {
+  const uint8_t* row0;
+  int pitch, boff;
+  __device__ __forceinline__ void operator()(int i, int g, int t, uint32_t (&a)[4], uint64_t& dw) const {
+    const uint8_t* ra = row0 + (16 * i + g) * pitch + boff;
+    const uint8_t* rb = ra + 8 * pitch;
+    block_frag<WQ4, ODD>(ra, t, a[0], a[2]);
+    block_frag<WQ4, ODD>(rb, t, a[1], a[3]);
+    dw = f2_pack(f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra)),
+                 f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb)));
+  }
+};
+
+// Packed weights (mrml_moe_prepare_weights): one record per (16-row tile,
+// block) in MMA fragment order, 16 * block_bytes long.  Q4_0: lane l = 4g+t
+// owns bytes [8l, 8l+8) = the raw nibble bytes [4t, 4t+4) of rows g and g+8;
+// Q8_0: bytes [16l, 16l+16) = rows g, g+8 values [4t, 4t+4), then rows g,
+// g+8 values [16+4t, 16+4t+4).  The 16 f16 scales follow the values as
+// pairs {d(g), d(g+8)}.  `rec` is tile 0's record; tile i's is rstep bytes on.
+template <int WQ4>
+struct PackedFrag {
+  const uint8_t* rec;
+  int rstep;
+  __device__ __forceinline__ void operator()(int i, int g, int t, uint32_t (&a)[4], uint64_t& dw) const {
+    const uint8_t* r = rec + i * rstep;
+    const int lane = 4 * g + t;
+    uint32_t s;
+    if constexpr (WQ4) {
+      const uint2 w = *reinterpret_cast<const uint2*>(r + 8 * lane);
+      a[0] = w.x & 0x0f0f0f0fu;
+      a[2] = (w.x >> 4) & 0x0f0f0f0fu;
+      a[1] = w.y & 0x0f0f0f0fu;
+      a[3] = (w.y >> 4) & 0x0f0f0f0fu;
+      s = *reinterpret_cast<const uint32_t*>(r + 256 + 4 * g);
+    } else {
+      const uint4 w = *reinterpret_cast<const uint4*>(r + 16 * lane);
+      a[0] = w.x;
+      a[1] = w.y;
+      a[2] = w.z;
+      a[3] = w.w;
+      s = *reinterpret_cast<const uint32_t*>(r + 512 + 4 * g);
+    }
+    dw = f2_pack(f16_bits_to_f32(s & 0xffffu), f16_bits_to_f32(s >> 16));
+  }
+};
+
+// One quant block for the warp's two 16-row tiles (rows 16i+g, 16i+g+8) and
 // the unit's NG position groups of 8:
-//   acc[8q + 4i + 2h + k] += isum * (d_w(row) * d_a(8q + 2t + k))
+//   acc[8q + 4i + 2h + k] += isum * (d_w(row 16i + 8h + g) * d_a(8q + 2t + k))
 // grp: group 0's activations of the block, the next group gstride bytes on;
 // rec: group 0's group-major scale record (rstride bytes to the next), from
-// which lane t takes the d_a pair and the accumulator seeds of positions 2t,
-// 2t+1 with one load each.  A row fragment is loaded and unpacked once for
+// which lane t takes the duplicated d_a of columns 2t, 2t+1 and the
+// accumulator seeds with one 16-byte load each.  The chain runs on packed
+// (row g, row g+8) pairs of one column: the pair's d_w is the two rows'
+// scales side by side and the column's d_a comes duplicated, so no operand
+// is rearranged in registers.  A row fragment is loaded and unpacked once for
 // all NG groups.
-template <int WQ4, bool ODD, int NG>
-__device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
-                                                int gstride, const uint8_t* rec, int rstride, uint64_t one, int g,
-                                                int t, float (&acc)[8 * NG]) {
-  uint32_t b0[NG], b1[NG];
-  uint64_t da[NG];
-  uint4 seed[NG];
-#pragma unroll
-  for (int q = 0; q < NG; ++q) {
-    b0[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + g * 16 + 4 * t);
-    b1[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + 128 + g * 16 + 4 * t);
-    da[q] = *reinterpret_cast<const uint64_t*>(rec + q * rstride + 8 * t);
-    seed[q] = *reinterpret_cast<const uint4*>(rec + q * rstride + 32 + 16 * t);
-  }
+template <int WQ4, int NG, class Frag>
+__device__ __forceinline__ void mma_block_rows2(const Frag& frag, const uint8_t* grp, int gstride, const uint8_t* rec,
+                                                int rstride, uint64_t one, int g, int t, float (&acc)[8 * NG]) {
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const uint8_t* ra = row0 + (16 * i + g) * pitch + boff;
-    const uint8_t* rb = ra + 8 * pitch;
     uint32_t a[4];
-    block_frag<WQ4, ODD>(ra, t, a[0], a[2]);
-    block_frag<WQ4, ODD>(rb, t, a[1], a[3]);
-    const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
-    const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
+    uint64_t dw;
+    frag(i, g, t, a, dw);
 #pragma unroll
     for (int q = 0; q < NG; ++q) {
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + q * gstride + g * 16 + 4 * t);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + q * gstride + 128 + g * 16 + 4 * t);
+      const uint4 seed = *reinterpret_cast<const uint4*>(rec + q * rstride + 64 + 16 * t);
       uint32_t d[4];
-      mma_block<WQ4>(d, a, b0[q], b1[q], seed[q]);
-      const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
-      const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
+      mma_block<WQ4>(d, a, b0, b1, seed);
+      const ulonglong2 da = *reinterpret_cast<const ulonglong2*>(rec + q * rstride + 16 * t);
+      const uint64_t f0 = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[2])), magic);  // exact
+      const uint64_t f1 = f2_sub(f2_pack(__uint_as_float(d[1]), __uint_as_float(d[3])), magic);
       float* aq = acc + 8 * q + 4 * i;
-      f2_acc(aq[0], aq[1], f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da[q])), one);
-      f2_acc(aq[2], aq[3], f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da[q])), one);
+      f2_acc(aq[0], aq[2], f2_mul(f0, f2_mul(dw, da.x)), one);
+      f2_acc(aq[1], aq[3], f2_mul(f1, f2_mul(dw, da.y)), one);
     }
   }
 }
@@ -255,38 +308,33 @@ __device__ __forceinline__ void mma_block_rows2(const uint8_t* row0, int pitch, 
 // second in lanes t = 2, 3; each lane runs the f32 chain for one of the two
 // (half the chain work of mma_block_rows2, which computes all 8 columns).
 // acc[2h + k]: tile row 16*(t >> 1) + 8h + g, position 2*(t & 1) + k; the
-// d_a pair and seeds come from positions 2*(t & 1) and 2*(t & 1) + 1.
-template <int WQ4, bool ODD>
-__device__ __forceinline__ void mma_block_rows2_half(const uint8_t* row0, int pitch, int boff, const uint8_t* grp,
-                                                     const uint8_t* rec, uint64_t one, int g, int t,
-                                                     float (&acc)[4]) {
+// d_a pairs and seeds come from positions 2*(t & 1) and 2*(t & 1) + 1.
+template <int WQ4, class Frag>
+__device__ __forceinline__ void mma_block_rows2_half(const Frag& frag, const uint8_t* grp, const uint8_t* rec,
+                                                     uint64_t one, int g, int t, float (&acc)[4]) {
   const int th = t & 1;
-  const uint64_t da = *reinterpret_cast<const uint64_t*>(rec + 8 * th);
-  const uint4 seed = *reinterpret_cast<const uint4*>(rec + 32 + 16 * th);
+  const uint4 seed = *reinterpret_cast<const uint4*>(rec + 64 + 16 * th);
   const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + g * 16 + 4 * t);
   const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + 128 + g * 16 + 4 * t);
   const uint32_t r0 = *reinterpret_cast<const uint32_t*>(grp + (g ^ 4) * 16 + 4 * t);
   const uint32_t r1 = *reinterpret_cast<const uint32_t*>(grp + 128 + (g ^ 4) * 16 + 4 * t);
   uint32_t a[4], d0[4], d1[4];
-  block_frag<WQ4, ODD>(row0 + g * pitch + boff, t, a[0], a[2]);
-  block_frag<WQ4, ODD>(row0 + (g + 8) * pitch + boff, t, a[1], a[3]);
+  uint64_t dw0, dw1;
+  frag(0, g, t, a, dw0);
   mma_block<WQ4>(d0, a, b0, b1, seed);
-  block_frag<WQ4, ODD>(row0 + (g + 16) * pitch + boff, t, a[0], a[2]);
-  block_frag<WQ4, ODD>(row0 + (g + 24) * pitch + boff, t, a[1], a[3]);
+  frag(1, g, t, a, dw1);
   mma_block<WQ4>(d1, a, r0, r1, seed);
   const bool hi = t >= 2;
   uint32_t d[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) d[j] = hi ? d1[j] : d0[j];
-  const uint8_t* ra = row0 + ((hi ? 16 : 0) + g) * pitch + boff;
-  const uint8_t* rb = ra + 8 * pitch;
+  const uint64_t dw = hi ? dw1 : dw0;
+  const ulonglong2 dd = *reinterpret_cast<const ulonglong2*>(rec + 16 * th);
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
-  const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ra));
-  const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rb));
-  const uint64_t fa = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
-  const uint64_t fb = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
-  f2_acc(acc[0], acc[1], f2_mul(fa, f2_mul(f2_pack(dwa, dwa), da)), one);
-  f2_acc(acc[2], acc[3], f2_mul(fb, f2_mul(f2_pack(dwb, dwb), da)), one);
+  const uint64_t f0 = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[2])), magic);  // exact
+  const uint64_t f1 = f2_sub(f2_pack(__uint_as_float(d[1]), __uint_as_float(d[3])), magic);
+  f2_acc(acc[0], acc[2], f2_mul(f0, f2_mul(dw, dd.x)), one);
+  f2_acc(acc[1], acc[3], f2_mul(f1, f2_mul(dw, dd.y)), one);
 }
 
 // The K chunks of one unit on the dp4a path, for compute thread row `c`:
@@ -294,12 +342,33 @@ __device__ __forceinline__ void mma_block_rows2_half(const uint8_t* row0, int pi
 // of a single token, the common case below two tokens per expert, so that
 // their blocks carry no predicated work for absent tokens).  Ring indices
 // and phases advance as the caller's.  Returns false when a wait gave up.
-template <int WQ4, int MODE, int NJ>
+// Row `r` (0..15) of a packed record (PackedFrag's layout) as the raw
+// block's values in element order's storage words and its f16 scale.
+template <int WQ4>
+__device__ __forceinline__ void packed_row(const uint8_t* rec, int r, uint32_t& d16,
+                                           uint32_t (&qs)[WQ4 ? 4 : 8]) {
+  const int g = r & 7, h = r >> 3;
+  if constexpr (WQ4) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) qs[t] = *reinterpret_cast<const uint32_t*>(rec + 8 * (4 * g + t) + 4 * h);
+    d16 = *reinterpret_cast<const uint16_t*>(rec + 256 + 4 * g + 2 * h);
+  } else {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      qs[t] = *reinterpret_cast<const uint32_t*>(rec + 16 * (4 * g + t) + 4 * h);
+      qs[4 + t] = *reinterpret_cast<const uint32_t*>(rec + 16 * (4 * g + t) + 8 + 4 * h);
+    }
+    d16 = *reinterpret_cast<const uint16_t*>(rec + 512 + 4 * g + 2 * h);
+  }
+}
+
+template <int WQ4, int MODE, int NJ, int PK>
 __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const uint8_t* raw, const uint8_t* bsb,
                                             int bs_stage, int nkc, int c, int nj, int& rs, int& bsi, uint32_t& rph,
                                             uint32_t& bph, float (&acc)[NJ]) {
   constexpr int BB = WQ4 ? 18 : 34;
   constexpr int GB = 256;
+  constexpr int RB = 16 * BB;  // packed record bytes
   const int lane = threadIdx.x & 31;
   for (int kc = 0; kc < nkc; ++kc) {
     if (!wait_bar(&B->raw_full[rs], rph, B, P.err)) return false;
@@ -307,7 +376,18 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const ui
     const uint8_t* src = raw + rs * P.raw_bytes;
     const uint8_t* bt = bsb + bsi * bs_stage;
     const uint8_t* sc = bt + P.kcb * GB;  // the blocks' group-major scale records
-    if constexpr (MODE == kGateUp) {
+    if constexpr (PK) {
+      // Stage: gate/up [part][tile 4][block kKC][RB] (thread c = part * 64 +
+      // 16 * tile + row); down [tile 8][block nb][RB].
+      const int nbs = MODE == kGateUp ? kKC : P.nb;
+      const uint8_t* tile = src + (size_t)(c >> 4) * nbs * RB;
+      for (int b = 0; b < nbs; ++b) {
+        uint32_t d16, q[WQ4 ? 4 : 8], w[8];
+        packed_row<WQ4>(tile + b * RB, c & 15, d16, q);
+        block_words<WQ4>(q, w);
+        block_tokens<WQ4, NJ>(w, f16_bits_to_f32(d16), bt + b * GB, sc + b * kActScaleBytes, nj, acc);
+      }
+    } else if constexpr (MODE == kGateUp) {
       const uint8_t* row = src + c * (kKC * BB);  // gate rows 0..63, then up rows
 #define MRML_GV_BLOCK(BL)                                                                     \
   {                                                                                           \
@@ -361,12 +441,18 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const ui
 // Activations use the group-major layout (common.cuh): a B stage holds, for
 // each of the unit's groups, the chunk's blocks (256 bytes each, contiguous),
 // then each group's scale records.
-template <int WQ4, int MODE, int MMA, int NG>
+//
+// PK = 1: the weights are in the packed layout of mrml_moe_prepare_weights
+// (PackedFrag's records; per unit and K chunk contiguous), streamed with 1-D
+// bulk copies: gate/up [E][part][64-row group][K chunk][tile 4][block
+// kKC][record], down [E][128-row group][tile 8][block][record].
+template <int WQ4, int MODE, int MMA, int NG, int PK>
 __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
-                                  (MMA && MODE == kGateUp && NG == 1) ? 5 : ((NG == 2 && !WQ4) ? 3 : 4))
+                                  (MMA && MODE == kGateUp && NG == 1) ? kGateUpCtas : ((NG == 2 && !WQ4) ? 3 : 4))
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   static_assert(NG == 1 || (NG == 2 && MMA), "two position groups per unit on the MMA form only");
   constexpr int BB = WQ4 ? 18 : 34;
+  constexpr int RB = 16 * BB;  // packed record bytes
   constexpr int TT = kGvTokens;
   constexpr int NP = TT * NG;  // positions per unit
   constexpr int RG = kGvRowsGateUp;  // row pairs per unit
@@ -420,7 +506,19 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
         for (int kc = 0; kc < nkc; ++kc) {
           if (!wait_bar(&B->raw_empty[rs], rph ^ 1, B, P.err)) break;
           uint8_t* dst = raw + rs * P.raw_bytes;
-          if constexpr (MODE == kGateUp) {
+          if constexpr (PK && MODE == kGateUp) {
+            // gate part, then up part: 4 tiles x kKC blocks each
+            const uint32_t part = 4 * kKC * RB;
+            const int ng = P.rows / RG, nc = P.nb / kKC;
+            mbar_arrive_expect_tx(&B->raw_full[rs], 2 * part);
+            const uint8_t* gsrc = P.w_raw + ((((size_t)e * 2) * ng + m0 / RG) * nc + kc) * part;
+            bulk_g2s(dst, gsrc, part, &B->raw_full[rs]);
+            bulk_g2s(dst + part, gsrc + (size_t)ng * nc * part, part, &B->raw_full[rs]);
+          } else if constexpr (PK) {
+            const uint32_t bytes = (uint32_t)(8 * P.nb * RB);
+            mbar_arrive_expect_tx(&B->raw_full[rs], bytes);
+            bulk_g2s(dst, P.w_raw + ((size_t)e * (P.rows / 128) + m0 / 128) * bytes, bytes, &B->raw_full[rs]);
+          } else if constexpr (MODE == kGateUp) {
             mbar_arrive_expect_tx(&B->raw_full[rs], 2 * RG * kKC * BB);
             const int c0 = kc * kKC * BB / 2;
             tc::tma_load_3d(dst, &tmap, c0, m0, 2 * e, &B->raw_full[rs]);
@@ -491,7 +589,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
       // Q4_0 down units of at most 4 tokens run the half-chain form.  (For
       // gate/up it measured slower: a second unrolled chunk body in a kernel
       // held to 64 registers; for Q8_0 its registers spill.)
-      const bool half = MODE == kDown && WQ4 && NG == 1 && nj <= 4;  // warp-uniform
+      const bool half = MODE == kDown && (WQ4 || PK) && NG == 1 && nj <= 4;  // warp-uniform
       float(&acch)[4] = *reinterpret_cast<float(*)[4]>(&acc[0]);  // the half layout's sums
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
@@ -500,31 +598,52 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
         const uint8_t* bt = bsb + bsi * bs_stage;
         const uint8_t* sc = bt + NG * P.kcb * GB;  // the blocks' group-major scale records
         const int gs = P.kcb * GB, ss = P.kcb * SB;  // strides between the unit's groups
-        if constexpr (MODE == kGateUp) {
+        if constexpr (PK && MODE == kGateUp) {
+          // warp cw: part cw / 2, tiles 2 (cw & 1) and 2 (cw & 1) + 1
+          const uint8_t* t0 = src + (size_t)((cw >> 1) * 4 + 2 * (cw & 1)) * kKC * RB;
+#pragma unroll
+          for (int bl = 0; bl < kKC; ++bl)
+            mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, gs, sc + bl * SB, ss, one,
+                                     g, t, acc);
+        } else if constexpr (PK) {
+          const uint8_t* t0 = src + (size_t)(2 * cw) * P.nb * RB;
+          if (NG == 1 && half) {
+#pragma unroll 2
+            for (int b = 0; b < P.nb; ++b)
+              mma_block_rows2_half<WQ4>(PackedFrag<WQ4>{t0 + b * RB, P.nb * RB}, bt + b * GB, sc + b * SB, one, g,
+                                        t, acch);
+          } else {
+#pragma unroll 2
+            for (int b = 0; b < P.nb; ++b)
+              mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + b * RB, P.nb * RB}, bt + b * GB, gs, sc + b * SB, ss,
+                                       one, g, t, acc);
+          }
+        } else if constexpr (MODE == kGateUp) {
           const uint8_t* row0 = src + 32 * cw * (kKC * BB);
 #pragma unroll
           for (int bl = 0; bl < kKC; bl += 2) {
-            mma_block_rows2<WQ4, false, NG>(row0, kKC * BB, bl * BB, bt + bl * GB, gs, sc + bl * SB, ss, one, g, t,
-                                            acc);
-            mma_block_rows2<WQ4, true, NG>(row0, kKC * BB, (bl + 1) * BB, bt + (bl + 1) * GB, gs,
-                                           sc + (bl + 1) * SB, ss, one, g, t, acc);
+            mma_block_rows2<WQ4, NG>(RawFrag<WQ4, false>{row0, kKC * BB, bl * BB}, bt + bl * GB, gs, sc + bl * SB,
+                                     ss, one, g, t, acc);
+            mma_block_rows2<WQ4, NG>(RawFrag<WQ4, true>{row0, kKC * BB, (bl + 1) * BB}, bt + (bl + 1) * GB, gs,
+                                     sc + (bl + 1) * SB, ss, one, g, t, acc);
           }
         } else {
           const uint8_t* row0 = src + (size_t)(32 * cw) * P.row_bytes;
           if (WQ4 && NG == 1 && half) {
 #pragma unroll 1
             for (int b = 0; b < P.nb; b += 2) {
-              mma_block_rows2_half<WQ4, false>(row0, P.row_bytes, b * BB, bt + b * GB, sc + b * SB, one, g, t, acch);
-              mma_block_rows2_half<WQ4, true>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, sc + (b + 1) * SB,
-                                              one, g, t, acch);
+              mma_block_rows2_half<WQ4>(RawFrag<WQ4, false>{row0, P.row_bytes, b * BB}, bt + b * GB, sc + b * SB, one,
+                                        g, t, acch);
+              mma_block_rows2_half<WQ4>(RawFrag<WQ4, true>{row0, P.row_bytes, (b + 1) * BB}, bt + (b + 1) * GB,
+                                        sc + (b + 1) * SB, one, g, t, acch);
             }
           } else {
 #pragma unroll 1
             for (int b = 0; b < P.nb; b += 2) {
-              mma_block_rows2<WQ4, false, NG>(row0, P.row_bytes, b * BB, bt + b * GB, gs, sc + b * SB, ss, one, g,
-                                              t, acc);
-              mma_block_rows2<WQ4, true, NG>(row0, P.row_bytes, (b + 1) * BB, bt + (b + 1) * GB, gs,
-                                             sc + (b + 1) * SB, ss, one, g, t, acc);
+              mma_block_rows2<WQ4, NG>(RawFrag<WQ4, false>{row0, P.row_bytes, b * BB}, bt + b * GB, gs, sc + b * SB,
+                                       ss, one, g, t, acc);
+              mma_block_rows2<WQ4, NG>(RawFrag<WQ4, true>{row0, P.row_bytes, (b + 1) * BB}, bt + (b + 1) * GB, gs,
+                                       sc + (b + 1) * SB, ss, one, g, t, acc);
             }
           }
         }
@@ -711,10 +830,10 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
       for (int t = 0; t < TT; ++t) acc[t] = 0.f;
       if (nj == 1) {
         float acc1[1] = {0.f};
-        ok = dp4a_chunks<WQ4, MODE, 1>(P, B, raw, bsb, bs_stage, nkc, c, 1, rs, bsi, rph, bph, acc1);
+        ok = dp4a_chunks<WQ4, MODE, 1, PK>(P, B, raw, bsb, bs_stage, nkc, c, 1, rs, bsi, rph, bph, acc1);
         acc[0] = acc1[0];
       } else {
-        ok = dp4a_chunks<WQ4, MODE, TT>(P, B, raw, bsb, bs_stage, nkc, c, nj, rs, bsi, rph, bph, acc);
+        ok = dp4a_chunks<WQ4, MODE, TT, PK>(P, B, raw, bsb, bs_stage, nkc, c, nj, rs, bsi, rph, bph, acc);
       }
       if (!ok) break;
       if constexpr (MODE == kGateUp) {
@@ -817,7 +936,7 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   // ring (the kernel's launch bound: 5 for the MMA gate/up product with one
   // position group per unit, 3 for Q8_0 weights with two, 4 for the others);
   // with few units, one CTA and the deepest ring that fits.
-  const int bound = (mma && mode == tc::kGateUp && ng == 1) ? 5 : ((ng == 2 && wtype != kQ4_0) ? 3 : 4);
+  const int bound = (mma && mode == tc::kGateUp && ng == 1) ? gv::kGateUpCtas : ((ng == 2 && wtype != kQ4_0) ? 3 : 4);
   const int per_sm_set = g_gv_per_sm.load(), ring_set = g_gv_ring.load();
   const int per_sm_max = per_sm_set > 0 ? per_sm_set : (many_units ? bound : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
@@ -842,9 +961,9 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   return p;
 }
 
-template <int WQ4, int MODE, int MMA, int NG>
+template <int WQ4, int MODE, int MMA, int NG, int PK>
 cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, int grid, cudaStream_t s) {
-  auto kern = gv::moe_gemv_kernel<WQ4, MODE, MMA, NG>;
+  auto kern = gv::moe_gemv_kernel<WQ4, MODE, MMA, NG, PK>;
   static SmemOptIn cache;
   const cudaError_t st = ensure_smem(kern, smem, cache);
   if (st != cudaSuccess) return st;
@@ -867,16 +986,46 @@ bool gv_supported(int wtype, int H, int I) {
   return tc_map_available();
 }
 
+bool gv_packed_supported(int wtype, int H, int I) {
+  // gate/up groups of 64 rows and K chunks of kKC blocks; down groups of 128
+  return gv_supported(wtype, H, I) && H % 128 == 0 && (H / 32) % tc::kKC == 0 && I % kGvRowsGateUp == 0;
+}
+
 bool gv_two_groups_supported(int wtype, int H, int I) {
   const int down_row = (I / 32) * block_bytes(wtype);
   return gv_plan(tc::kGateUp, wtype, H / 32, 0, true, true, 2).smem != 0 &&
          gv_plan(tc::kDown, wtype, I / 32, down_row, true, true, 2).smem != 0;
 }
 
-cudaError_t launch_gemv(int mode, int wtype, bool mma, int ng, const uint8_t* weights, int H, int I, int E,
-                        const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
+template <int PK>
+cudaError_t gv_dispatch(int mode, bool q4, bool mma, int ng, const CUtensorMap& map, const tc::Params& P, size_t smem,
+                        int grid, cudaStream_t s) {
+  if (mma && ng == 2) {
+    if (mode == tc::kGateUp)
+      return q4 ? gv_launch<1, tc::kGateUp, 1, 2, PK>(map, P, smem, grid, s)
+                : gv_launch<0, tc::kGateUp, 1, 2, PK>(map, P, smem, grid, s);
+    return q4 ? gv_launch<1, tc::kDown, 1, 2, PK>(map, P, smem, grid, s)
+              : gv_launch<0, tc::kDown, 1, 2, PK>(map, P, smem, grid, s);
+  }
+  if (mma) {
+    if (mode == tc::kGateUp)
+      return q4 ? gv_launch<1, tc::kGateUp, 1, 1, PK>(map, P, smem, grid, s)
+                : gv_launch<0, tc::kGateUp, 1, 1, PK>(map, P, smem, grid, s);
+    return q4 ? gv_launch<1, tc::kDown, 1, 1, PK>(map, P, smem, grid, s)
+              : gv_launch<0, tc::kDown, 1, 1, PK>(map, P, smem, grid, s);
+  }
+  if (mode == tc::kGateUp)
+    return q4 ? gv_launch<1, tc::kGateUp, 0, 1, PK>(map, P, smem, grid, s)
+              : gv_launch<0, tc::kGateUp, 0, 1, PK>(map, P, smem, grid, s);
+  return q4 ? gv_launch<1, tc::kDown, 0, 1, PK>(map, P, smem, grid, s)
+            : gv_launch<0, tc::kDown, 0, 1, PK>(map, P, smem, grid, s);
+}
+
+cudaError_t launch_gemv(int mode, int wtype, bool packed, bool mma, int ng, const uint8_t* weights, int H, int I,
+                        int E, const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
                         int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s) {
   if (ng != 1 && !(ng == 2 && mma)) return cudaErrorInvalidValue;
+  if (packed && !gv_packed_supported(wtype, H, I)) return cudaErrorInvalidValue;
   tc::Params P{};
   const int bb = block_bytes(wtype);
   P.bq = bq;
@@ -899,7 +1048,10 @@ cudaError_t launch_gemv(int mode, int wtype, bool mma, int ng, const uint8_t* we
     P.out_s = out_s;
     P.out_nb = I / 32;
     P.down_q4 = wtype == kQ4_0;
-    if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp)) return cudaErrorInvalidValue;
+    if (packed)
+      P.w_raw = weights;
+    else if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp))
+      return cudaErrorInvalidValue;
     pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng);
   } else {
     P.nb = I / 32;
@@ -917,25 +1069,8 @@ cudaError_t launch_gemv(int mode, int wtype, bool mma, int ng, const uint8_t* we
   P.one = 1.0f;
   const int grid = std::max(1, std::min(pl.per_sm * sms, max_units));
   const bool q4 = wtype == kQ4_0;
-  if (mma && ng == 2) {
-    if (mode == tc::kGateUp)
-      return q4 ? gv_launch<1, tc::kGateUp, 1, 2>(map, P, pl.smem, grid, s)
-                : gv_launch<0, tc::kGateUp, 1, 2>(map, P, pl.smem, grid, s);
-    return q4 ? gv_launch<1, tc::kDown, 1, 2>(map, P, pl.smem, grid, s)
-              : gv_launch<0, tc::kDown, 1, 2>(map, P, pl.smem, grid, s);
-  }
-  if (mma) {
-    if (mode == tc::kGateUp)
-      return q4 ? gv_launch<1, tc::kGateUp, 1, 1>(map, P, pl.smem, grid, s)
-                : gv_launch<0, tc::kGateUp, 1, 1>(map, P, pl.smem, grid, s);
-    return q4 ? gv_launch<1, tc::kDown, 1, 1>(map, P, pl.smem, grid, s)
-              : gv_launch<0, tc::kDown, 1, 1>(map, P, pl.smem, grid, s);
-  }
-  if (mode == tc::kGateUp)
-    return q4 ? gv_launch<1, tc::kGateUp, 0, 1>(map, P, pl.smem, grid, s)
-              : gv_launch<0, tc::kGateUp, 0, 1>(map, P, pl.smem, grid, s);
-  return q4 ? gv_launch<1, tc::kDown, 0, 1>(map, P, pl.smem, grid, s)
-            : gv_launch<0, tc::kDown, 0, 1>(map, P, pl.smem, grid, s);
+  return packed ? gv_dispatch<1>(mode, q4, mma, ng, map, P, pl.smem, grid, s)
+                : gv_dispatch<0>(mode, q4, mma, ng, map, P, pl.smem, grid, s);
 }
 
 }  // namespace mrml

@@ -111,10 +111,17 @@ constexpr int kGvTokens = 8;
 constexpr int kGvRowsGateUp = 64;
 bool gv_supported(int wtype, int H, int I);
 void gv_set_tuning(int per_sm, int ring);
-// ng: position groups of 8 per work unit (1, or 2 on the MMA form).
-cudaError_t launch_gemv(int mode, int wtype, bool mma, int ng, const uint8_t* weights, int H, int I, int E,
-                        const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
+// ng: position groups of 8 per work unit (1, or 2 on the MMA form);
+// packed: the weights are in mrml_moe_prepare_weights' layout.
+cudaError_t launch_gemv(int mode, int wtype, bool packed, bool mma, int ng, const uint8_t* weights, int H, int I,
+                        int E, const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
                         int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s);
+// Whether the packed layout (and the decode kernel on it) fits these shapes.
+bool gv_packed_supported(int wtype, int H, int I);
+// Repacks raw GGUF expert weights into the decode kernel's packed layout
+// (prepare.cu); which = 0 gate_up [E][2I][H/32 blocks], 1 down [E][H][I/32].
+cudaError_t launch_repack(int which, int wtype, const uint8_t* src, uint8_t* dst, int H, int I, int E,
+                          cudaStream_t s);
 // Whether the MMA form's 16-position units fit these shapes.
 bool gv_two_groups_supported(int wtype, int H, int I);
 bool tc_supported(int wtype, int H, int I, int NT);

@@ -83,7 +83,7 @@ struct Workspace {
   int4* units_gu;    // tensor-core work units, gate/up
   int4* units_dn;    // tensor-core work units, down
   int8_t* xb;        // [H/32][npad/8][256]  tensor-core B operand of gate/up
-  int2* xs;          // its scales: [H/32][npad] int2, or group-major 12-byte records (decode kernel)
+  int2* xs;          // its scales: [H/32][npad] int2, or group-major records (decode kernel)
   int8_t* ab;        // [I/32][npad/8][256]  B operand of down (re-quantised act)
   int2* as;          // its scales, laid out as xs
   float* act;        // [npad][I]     geglu output per position (CUDA-core path)
@@ -117,9 +117,12 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
   w.units_gu = reinterpret_cast<int4*>(take((size_t)w.max_units_gu * 16));
   w.units_dn = reinterpret_cast<int4*>(take((size_t)w.max_units_dn * 16));
   w.xb = reinterpret_cast<int8_t*>(take(nb * npad * 32));
-  w.xs = reinterpret_cast<int2*>(take(nb * npad * 12));  // int2 per position, or 12-byte group-major records
+  // int2 per position (tensor cores), or the decode kernel's group-major
+  // records (kActScaleBytes per 8 positions)
+  const size_t rec_pos = std::max<size_t>(8, mrml::kActScaleBytes / 8);
+  w.xs = reinterpret_cast<int2*>(take(nb * npad * rec_pos));
   w.ab = reinterpret_cast<int8_t*>(take(nbi * npad * 32));
-  w.as = reinterpret_cast<int2*>(take(nbi * npad * 12));
+  w.as = reinterpret_cast<int2*>(take(nbi * npad * rec_pos));
   w.act = reinterpret_cast<float*>(take((size_t)npad * I * 4));
   w.ydown = reinterpret_cast<float*>(take((size_t)npad * H * 4));
   w.bytes = off;
@@ -155,16 +158,24 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? MRML_OK : MRML_ERR_CU
     if (_st != MRML_OK) return _st;    \
   } while (0)
 
+// Weight type without the packed-layout flag, and the flag.
+int base_type(int wtype) { return wtype & ~MRML_PACKED; }
+bool is_packed(int wtype) { return (wtype & MRML_PACKED) != 0; }
+
 int check_expert_args(int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids, const float* probs,
                       const float* x, const float* out, int H, int I, int E, int K, int T) {
-  if (wtype != MRML_Q4_0 && wtype != MRML_Q8_0) return MRML_ERR_UNSUPPORTED;
+  const int wt = base_type(wtype);
+  if (wt != MRML_Q4_0 && wt != MRML_Q8_0) return MRML_ERR_UNSUPPORTED;
+  if ((wtype & ~(MRML_PACKED | 0xff)) != 0) return MRML_ERR_UNSUPPORTED;
+  if (is_packed(wtype) && (H <= 0 || I <= 0 || H % 32 != 0 || I % 32 != 0 || !mrml::gv_packed_supported(wt, H, I)))
+    return MRML_ERR_UNSUPPORTED;
   if (H <= 0 || I <= 0 || E <= 0 || K <= 0 || T < 0 || K > E) return MRML_ERR_INVALID_ARGUMENT;
   if (H % 32 != 0 || I % 32 != 0) return MRML_ERR_INVALID_ARGUMENT;
   if (E > kMaxE || K > kMaxK) return MRML_ERR_UNSUPPORTED;
   if ((long long)T * K > (1ll << 30)) return MRML_ERR_UNSUPPORTED;
   if (T > 0 && (!gate_up || !down || !ids || !probs || !x || !out)) return MRML_ERR_INVALID_ARGUMENT;
   if (T > 0 && (!aligned16(gate_up) || !aligned16(down) || !aligned16(x))) return MRML_ERR_INVALID_ARGUMENT;
-  if (mrml::gate_up_tok_chunk(wtype, H) == 0 || mrml::down_tok_chunk(wtype, I) == 0) return MRML_ERR_UNSUPPORTED;
+  if (mrml::gate_up_tok_chunk(wt, H) == 0 || mrml::down_tok_chunk(wt, I) == 0) return MRML_ERR_UNSUPPORTED;
   return MRML_OK;
 }
 
@@ -196,10 +207,13 @@ enum Route { kRouteGeneral = 0, kRouteGemv = 1, kRouteTensor = 2, kRouteGemvMma 
 
 // `pairs` is the expected number of (token, slot) pairs this call computes:
 // T * K on one device, about T * K * E / e_total for an expert shard.
-Route pick_route(int wtype, int H, int I, int E, long long pairs) {
+Route pick_route(int wtype, bool packed, int H, int I, int E, long long pairs) {
   const bool tc = mrml::tc_supported(wtype, H, I, 64) && mrml::tc_supported(wtype, H, I, 16);
   const bool gv = mrml::gv_supported(wtype, H, I);
-  switch (g_path.load(std::memory_order_relaxed)) {
+  const int forced = g_path.load(std::memory_order_relaxed);
+  // Packed weights run on the decode kernel only (its MMA or dp4a form).
+  if (packed) return forced == 1 ? kRouteGemv : forced == 4 || pairs >= 2ll * E ? kRouteGemvMma : kRouteGemv;
+  switch (forced) {
     case 1: return gv ? kRouteGemv : kRouteGeneral;
     case 2: return tc ? kRouteTensor : (gv ? kRouteGemv : kRouteGeneral);
     case 3: return kRouteGeneral;
@@ -224,8 +238,10 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
                 int T, cudaStream_t s, int e_first = 0, int e_total = 0, const float* topk_logits = nullptr,
                 int32_t* ids_out = nullptr, float* probs_out = nullptr) {
   if (e_total == 0) e_total = E;
+  const bool packed = is_packed(wtype);
+  wtype = base_type(wtype);
   const long long pairs = (long long)T * K * E / e_total;
-  const Route route = pick_route(wtype, H, I, E, pairs);
+  const Route route = pick_route(wtype, packed, H, I, E, pairs);
   const bool gv = route == kRouteGemv || route == kRouteGemvMma;
   // Work units of 16 positions (two groups of 8) on the MMA form once
   // experts see about 12 tokens or more: a weight stage and each unpacked
@@ -266,10 +282,11 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
       MRML_LAUNCH(mrml::launch_gemm_tc(1, wtype, NT, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn,
                                        w.npad, nullptr, nullptr, w.ydown, w.status, s));
     } else {
-      MRML_LAUNCH(mrml::launch_gemv(0, wtype, route == kRouteGemvMma, ng_gu, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units, mu_gu, w.npad, w.ab,
-                                    w.as, nullptr, w.status, s));
-      MRML_LAUNCH(mrml::launch_gemv(1, wtype, route == kRouteGemvMma, ng_dn, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1, mu_dn, w.npad,
-                                    nullptr, nullptr, w.ydown, w.status, s));
+      const bool mma = route == kRouteGemvMma;
+      MRML_LAUNCH(mrml::launch_gemv(0, wtype, packed, mma, ng_gu, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units,
+                                    mu_gu, w.npad, w.ab, w.as, nullptr, w.status, s));
+      MRML_LAUNCH(mrml::launch_gemv(1, wtype, packed, mma, ng_dn, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1,
+                                    mu_dn, w.npad, nullptr, nullptr, w.ydown, w.status, s));
     }
   }
   MRML_LAUNCH(mrml::launch_combine(w.ydown, w.pos, ids, probs, down_scale, out, H, K, T, s));
@@ -372,6 +389,39 @@ int mrml_moe_forward(int wtype, const float* router_w, const float* router_x, co
   }
   MRML_TRY(run_router(w, router_w, router_x, logits, ids, probs, H, E, K, T, s));
   return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s);
+}
+
+size_t mrml_moe_weights_bytes(int wtype, int H, int I, int E, int which) {
+  const int wt = base_type(wtype);
+  if ((wt != MRML_Q4_0 && wt != MRML_Q8_0) || H <= 0 || I <= 0 || E <= 0 || H % 32 != 0 || I % 32 != 0) return 0;
+  const size_t bb = mrml::block_bytes(wt);
+  if (which == 0) return (size_t)E * 2 * I * (H / 32) * bb;
+  if (which == 1) return (size_t)E * H * (I / 32) * bb;
+  return 0;
+}
+
+int mrml_moe_prepare_weights(int wtype, const uint8_t* gate_up, const uint8_t* down, uint8_t* gate_up_packed,
+                             uint8_t* down_packed, int H, int I, int E, mrml_stream_t stream) {
+  if (wtype != MRML_Q4_0 && wtype != MRML_Q8_0) return MRML_ERR_UNSUPPORTED;
+  if (H <= 0 || I <= 0 || E <= 0 || H % 32 != 0 || I % 32 != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (E > kMaxE) return MRML_ERR_UNSUPPORTED;
+  if (!gate_up || !down || !gate_up_packed || !down_packed) return MRML_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gate_up_packed) || !aligned16(down_packed) || ((uintptr_t)gate_up & 1) || ((uintptr_t)down & 1))
+    return MRML_ERR_INVALID_ARGUMENT;
+  const size_t gb = mrml_moe_weights_bytes(wtype, H, I, E, 0), db = mrml_moe_weights_bytes(wtype, H, I, E, 1);
+  auto overlap = [](const void* a, size_t na, const void* b, size_t nb) {
+    const uintptr_t x = (uintptr_t)a, y = (uintptr_t)b;
+    return x < y + nb && y < x + na;
+  };
+  if (overlap(gate_up, gb, gate_up_packed, gb) || overlap(down, db, down_packed, db) ||
+      overlap(gate_up_packed, gb, down_packed, db))
+    return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  if (!mrml::gv_packed_supported(wtype, H, I)) return MRML_ERR_UNSUPPORTED;
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_TRY(cuda_status(mrml::launch_repack(0, wtype, gate_up, gate_up_packed, H, I, E, s)));
+  MRML_TRY(cuda_status(mrml::launch_repack(1, wtype, down, down_packed, H, I, E, s)));
+  return MRML_OK;
 }
 
 int mrml_moe_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,

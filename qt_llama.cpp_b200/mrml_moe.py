@@ -30,6 +30,7 @@ MRML_OK = 0
 MRML_ERR_INVALID_ARGUMENT = -1
 MRML_Q4_0 = 2
 MRML_Q8_0 = 8
+MRML_PACKED = 0x100
 
 # Every symbol include/mrml_moe.h declares, with its ctypes signature.
 _c = ctypes
@@ -69,6 +70,8 @@ SIGNATURES = {
     "mrml_moe_device_status": (_i, [_vp, _vp, _c.POINTER(_c.c_int)]),
     "mrml_moe_profile_events": (_i, [_c.POINTER(_vp), _i]),
     "mrml_moe_set_option": (_i, [_i, _i]),
+    "mrml_moe_weights_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "mrml_moe_prepare_weights": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
 }
 
 
@@ -84,9 +87,11 @@ _lib = None
 
 
 def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
-    """Load libmrml_moe_b200.so (built in-tree by __graft_entry__.build)."""
+    """Load libmrml_moe_b200.so (built in-tree by __graft_entry__.build; the
+    environment variable MRML_MOE_LIB names another build of it)."""
     global _lib
     if _lib is None:
+        path = os.environ.get("MRML_MOE_LIB", path)
         if not os.path.exists(path):
             raise OSError(f"{path} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'`")
         lib = ctypes.CDLL(path)
@@ -263,6 +268,28 @@ def quantize(wtype, src, dst, stream=None):
 
 OPTION_EXPERT_PATH = 1
 PATH_AUTO, PATH_GEMV, PATH_TENSOR, PATH_GENERAL = 0, 1, 2, 3
+
+
+def prepare_weights(wtype, gate_up, down, stream=None):
+    """Repacks one layer's GGUF expert slabs into the decode kernel's layout
+    (mrml_moe_prepare_weights); returns (gate_up_packed, down_packed), device
+    tensors of the same sizes, to be passed with wtype | MRML_PACKED."""
+    import torch
+
+    lib = load_library()
+    gp = torch.empty_like(gate_up)
+    dp = torch.empty_like(down)
+    _check("mrml_moe_prepare_weights",
+           lib.mrml_moe_prepare_weights(wtype, _ptr(gate_up), _ptr(down), _ptr(gp), _ptr(dp), *_prep_shape(
+               wtype, gate_up, down), _stream_ptr(stream)))
+    return gp, dp
+
+
+def _prep_shape(wtype, gate_up, down):
+    """(H, I, E) of GGUF slabs shaped [E][2I][H/32*bb] and [E][H][I/32*bb]."""
+    bb = 18 if (wtype & 0xff) == MRML_Q4_0 else 34
+    E, two_i, row = gate_up.shape
+    return row // bb * 32, two_i // 2, E
 
 
 def set_expert_path(path: int) -> None:
