@@ -279,6 +279,16 @@ struct PackedFrag {
 template <int WQ4, int NG, class Frag>
 __device__ __forceinline__ void mma_block_rows2(const Frag& frag, const uint8_t* grp, int gstride, const uint8_t* rec,
                                                 int rstride, uint64_t one, int g, int t, float (&acc)[8 * NG]) {
+  uint32_t b0[NG], b1[NG];
+  uint4 seed[NG];
+  ulonglong2 da[NG];
+#pragma unroll
+  for (int q = 0; q < NG; ++q) {
+    b0[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + g * 16 + 4 * t);
+    b1[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + 128 + g * 16 + 4 * t);
+    seed[q] = *reinterpret_cast<const uint4*>(rec + q * rstride + 64 + 16 * t);
+    da[q] = *reinterpret_cast<const ulonglong2*>(rec + q * rstride + 16 * t);
+  }
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -287,17 +297,13 @@ __device__ __forceinline__ void mma_block_rows2(const Frag& frag, const uint8_t*
     frag(i, g, t, a, dw);
 #pragma unroll
     for (int q = 0; q < NG; ++q) {
-      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(grp + q * gstride + g * 16 + 4 * t);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(grp + q * gstride + 128 + g * 16 + 4 * t);
-      const uint4 seed = *reinterpret_cast<const uint4*>(rec + q * rstride + 64 + 16 * t);
       uint32_t d[4];
-      mma_block<WQ4>(d, a, b0, b1, seed);
-      const ulonglong2 da = *reinterpret_cast<const ulonglong2*>(rec + q * rstride + 16 * t);
+      mma_block<WQ4>(d, a, b0[q], b1[q], seed[q]);
       const uint64_t f0 = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[2])), magic);  // exact
       const uint64_t f1 = f2_sub(f2_pack(__uint_as_float(d[1]), __uint_as_float(d[3])), magic);
       float* aq = acc + 8 * q + 4 * i;
-      f2_acc(aq[0], aq[2], f2_mul(f0, f2_mul(dw, da.x)), one);
-      f2_acc(aq[1], aq[3], f2_mul(f1, f2_mul(dw, da.y)), one);
+      f2_acc(aq[0], aq[2], f2_mul(f0, f2_mul(dw, da[q].x)), one);
+      f2_acc(aq[1], aq[3], f2_mul(f1, f2_mul(dw, da[q].y)), one);
     }
   }
 }
@@ -589,7 +595,11 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
       // Q4_0 down units of at most 4 tokens run the half-chain form.  (For
       // gate/up it measured slower: a second unrolled chunk body in a kernel
       // held to 64 registers; for Q8_0 its registers spill.)
-      const bool half = MODE == kDown && (WQ4 || PK) && NG == 1 && nj <= 4;  // warp-uniform
+      // Units of at most 4 positions run the half-chain form: down with Q4_0
+      // weights, and every product on packed weights.  (For gate/up on GGUF
+      // rows it measured slower: a second unrolled chunk body in a kernel held
+      // to 64 registers; for Q8_0 down rows its registers spill.)
+      const bool half = (MODE == kDown ? (WQ4 || PK) : PK) && NG == 1 && nj <= 4;  // warp-uniform
       float(&acch)[4] = *reinterpret_cast<float(*)[4]>(&acc[0]);  // the half layout's sums
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
@@ -601,10 +611,17 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
         if constexpr (PK && MODE == kGateUp) {
           // warp cw: part cw / 2, tiles 2 (cw & 1) and 2 (cw & 1) + 1
           const uint8_t* t0 = src + (size_t)((cw >> 1) * 4 + 2 * (cw & 1)) * kKC * RB;
+          if (NG == 1 && half) {
 #pragma unroll
-          for (int bl = 0; bl < kKC; ++bl)
-            mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, gs, sc + bl * SB, ss, one,
-                                     g, t, acc);
+            for (int bl = 0; bl < kKC; ++bl)
+              mma_block_rows2_half<WQ4>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, sc + bl * SB, one, g,
+                                        t, acch);
+          } else {
+#pragma unroll
+            for (int bl = 0; bl < kKC; ++bl)
+              mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, gs, sc + bl * SB, ss,
+                                       one, g, t, acc);
+          }
         } else if constexpr (PK) {
           const uint8_t* t0 = src + (size_t)(2 * cw) * P.nb * RB;
           if (NG == 1 && half) {

@@ -130,15 +130,15 @@ def test_prepare_weights_rejects_bad_arguments(cuda, moe, synth):
     H, I, E = 256, 96, 2  # I not a multiple of 64: no packed layout
     gu = torch.zeros((E, 2 * I, H // 32 * 18), dtype=torch.uint8, device=cuda)
     dn = torch.zeros((E, H, I // 32 * 18), dtype=torch.uint8, device=cuda)
-    st = lib.mrml_moe_prepare_weights(2, gu.data_ptr(), dn.data_ptr(), torch.empty_like(gu).data_ptr(),
-                                      torch.empty_like(dn).data_ptr(), H, I, E, None)
+    gp, dp = torch.empty_like(gu), torch.empty_like(dn)  # held, so that the two outputs are distinct buffers
+    st = lib.mrml_moe_prepare_weights(2, gu.data_ptr(), dn.data_ptr(), gp.data_ptr(), dp.data_ptr(), H, I, E, None)
     assert st == -2
     H, I = 256, 128
     gu = torch.zeros((E, 2 * I, H // 32 * 18), dtype=torch.uint8, device=cuda)
     dn = torch.zeros((E, H, I // 32 * 18), dtype=torch.uint8, device=cuda)
     # in place (output overlapping the input) is refused
-    st = lib.mrml_moe_prepare_weights(2, gu.data_ptr(), dn.data_ptr(), gu.data_ptr(), torch.empty_like(dn).data_ptr(),
-                                      H, I, E, None)
+    dp = torch.empty_like(dn)
+    st = lib.mrml_moe_prepare_weights(2, gu.data_ptr(), dn.data_ptr(), gu.data_ptr(), dp.data_ptr(), H, I, E, None)
     assert st == -1
     assert lib.mrml_moe_weights_bytes(2, H, I, E, 0) == gu.numel()
     assert lib.mrml_moe_weights_bytes(2, H, I, E, 1) == dn.numel()
