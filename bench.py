@@ -36,6 +36,7 @@ under oracle/, the reference's Rust cannot be built here) on the host cores.
 from __future__ import annotations
 
 import argparse
+import gc
 import importlib.util
 import json
 import os
@@ -227,14 +228,17 @@ class LayerSet:
         layer_bytes = E * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
         self.n_layers = max(2, -(-4 * L2_BYTES // layer_bytes))
         self.layers = []
+        self.host_layer0 = None
         for l in range(self.n_layers):
             gu, dn = synth.expert_weights_device(seed * 100 + l + 1, wtype, H, I, E, device, moe.quantize)
-            if packed:  # the load-time repack (mrml_moe_prepare_weights), outside the timed steps
-                gu, dn = moe.prepare_weights(wtype, gu, dn)
-                torch.cuda.synchronize()
             g = torch.Generator(device=device)
             g.manual_seed(seed * 100 + l + 1000)
             W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
+            if l == 0:  # the parity check's reference weights (GGUF layout)
+                self.host_layer0 = (gu.cpu().numpy(), dn.cpu().numpy(), W.cpu().numpy())
+            if packed:  # the load-time repack (mrml_moe_prepare_weights), outside the timed steps
+                gu, dn = moe.prepare_weights(wtype, gu, dn)
+                torch.cuda.synchronize()
             self.layers.append((gu, dn, W))
         g = torch.Generator(device=device)
         g.manual_seed(seed + 77)
@@ -308,36 +312,44 @@ class LayerSet:
 class EPLayerSet:
     """The expert-parallel layer on this rank: every layer copy holds the
     rank's E/N experts and the replicated router; a step routes the rank's
-    home tokens, all-gathers them, runs the rank's experts on every rank's
-    tokens and reduce-scatters the partial outputs (qt_llama.cpp_b200/ep.py).
-    Same interface as LayerSet."""
+    home tokens, sends each row only to the ranks that own one of its experts,
+    runs the rank's experts on the rows it received and returns the partial
+    outputs to their home ranks (qt_llama.cpp_b200/ep.py).  Same interface as
+    LayerSet."""
 
-    def __init__(self, moe, synth, device, name, n_inputs, rank, world, seed=0, exchange="p2p"):
+    def __init__(self, moe, synth, device, name, n_inputs, rank, world, seed=0, exchange="p2p", packed=False):
         import torch
 
-        ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
+        self.epm = ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
         wtype, H, I, E, K, T, routing = WORKLOADS[name]
         assert routing == "router", "expert parallelism runs the router workloads"
         if name in STRONG:
             T //= world
         self.moe, self.device, self.name = moe, device, name
         self.wtype, self.H, self.I, self.E, self.K, self.T, self.routing = wtype, H, I, E, K, T, routing
-        self.world, self.rank = world, rank
-        self.ep = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, device, exchange=exchange)
+        self.world, self.rank, self.exchange = world, rank, exchange
+        wcall = wtype | (moe.MRML_PACKED if packed else 0)
+        self.ep = ep.ExpertParallelLayer(moe, rank, world, wcall, H, I, E, K, T, device, exchange=exchange)
         first, count = self.ep.first, self.ep.count
         bb = 18 if wtype == 2 else 34
         layer_bytes = count * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
         self.n_layers = max(2, -(-4 * L2_BYTES // layer_bytes))
         self.layers = []
+        self.host_layer0 = None
         for l in range(self.n_layers):
             # Every rank generates the whole layer with the same seed and keeps
             # its experts, so that the job computes one well-defined layer.
             gu, dn = synth.expert_weights_device(seed * 100 + l + 1, wtype, H, I, E, device, moe.quantize)
-            gu, dn = gu[first:first + count].clone(), dn[first:first + count].clone()
-            torch.cuda.empty_cache()
             g = torch.Generator(device=device)
             g.manual_seed(seed * 100 + l + 1000)
             W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
+            if l == 0 and rank == 0:  # the parity check's reference weights (GGUF layout)
+                self.host_layer0 = (gu.cpu().numpy(), dn.cpu().numpy(), W.cpu().numpy())
+            gu, dn = gu[first:first + count].clone(), dn[first:first + count].clone()
+            if packed:
+                gu, dn = moe.prepare_weights(wtype, gu, dn)
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
             self.layers.append((gu, dn, W))
         g = torch.Generator(device=device)
         g.manual_seed(seed + 77 + 1000 * rank)
@@ -346,8 +358,13 @@ class EPLayerSet:
         self.ids, self.probs = self.ep.ids, self.ep.probs
         self.ws = self.ep.ws
         self.layer_bytes = layer_bytes
-        # mrml_moe_router on the home tokens, then the expert shard on all ranks' tokens
-        self.kernels = ["router_logits", "router_topk"] + expert_kernels(T * world)
+        if self.ep.exchange == "p2p":
+            # router on the home tokens; push; then the expert step (receive,
+            # dispatch, gather, gate/up, down, partials pushed home); reduce
+            self.kernels = ["router_logits", "router_topk", "ep_push", "ep_recv", "dispatch", "gather", "gate_up",
+                            "down", "ep_combine_push", "ep_reduce"]
+        else:  # router, then the expert shard on all ranks' tokens (NCCL moves the data)
+            self.kernels = ["router_logits", "router_topk"] + expert_kernels(T * world)
 
     @property
     def router_ws(self):
@@ -364,22 +381,86 @@ class EPLayerSet:
     def n_kernels(self):
         return len(self.kernels)
 
+    def gather_routing(self):
+        """Every rank's home ids and weights of the last step, rank order."""
+        ids = all_gather_np(self.ids, self.world)
+        probs = all_gather_np(self.probs, self.world)
+        return ids, probs
+
     def unique_experts(self, i):
         """This rank's experts hit by step i (every rank's tokens) and its
-        pair count."""
+        pair count; also keeps step i's routing for nvlink_bytes."""
         self.step(i)
-        ids = self.ep.bufs.ids_all.cpu().numpy()
-        probs = self.ep.bufs.probs_all.cpu().numpy()
+        ids, probs = self.gather_routing()
+        self._routing = (ids, probs)
         first, count = self.ep.first, self.ep.count
         hit = ids[(probs > 1e-4) & (ids >= first) & (ids < first + count)]
         return len(np.unique(hit)), int(hit.size)
 
     def nvlink_bytes(self):
-        """Bytes each rank receives per step: the all-gather brings (N-1)
-        home batches of rows, ids and weights; the reduce-scatter (ring or
-        in-switch) moves (N-1)/N of the [N*T, H] partials."""
+        """Bytes this rank receives per step.  Peer exchange: the Q8_0 rows of
+        the tokens routed to its experts, every rank's ids and weights, and
+        the partials of its home tokens from the ranks that own their experts
+        (counted from the routing of the step unique_experts ran).  NCCL
+        baseline: the all-gathers bring (N-1) home batches of f32 rows, ids and
+        weights; the reduce-scatter moves (N-1)/N of the [N*T, H] partials."""
         n, T, H, K = self.world, self.T, self.H, self.K
+        if self.ep.exchange == "p2p":
+            ids, probs = self._routing
+            return self.epm.exchange_bytes(ids, probs, n, self.E, H, K, self.rank, T)["total"]
         return (n - 1) * T * (H * 4 + K * 8) + (n - 1) * T * H * 4
+
+    def close(self):
+        self.ep.close()
+
+
+def all_gather_np(t, world):
+    """A device tensor's values from every rank, concatenated in rank order
+    along the first axis (host numpy); the tensor itself at world 1."""
+    import torch
+
+    if world == 1:
+        return t.cpu().numpy()
+    import torch.distributed as dist
+
+    buf = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(buf, t.contiguous())
+    return buf.cpu().numpy()
+
+
+def parity_check(ls, world, rank, n_check=64, seed=123):
+    """One step outside the timed region, checked against the oracle (the
+    reference's CPU path) on a seeded sample of the job's tokens: their
+    expert ids must be identical, their outputs within the task's bars
+    (max-abs <= 1e-3 * max|ref|, rel-L2 <= 1e-4).  Every rank takes part (the
+    step and the gathers); rank 0 computes and returns the record."""
+    import torch
+
+    oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
+    x = ls.xs[0]
+    ls.step(0, x=x)
+    torch.cuda.synchronize()
+    xs = all_gather_np(x, world)
+    outs = all_gather_np(ls.out, world)
+    ids = all_gather_np(ls.ids, world)
+    if rank != 0:
+        return None
+    gu, dn, W = ls.host_layer0
+    H, I, E, K = ls.H, ls.I, ls.E, ls.K
+    idx = np.sort(np.random.default_rng(seed).choice(xs.shape[0], size=min(n_check, xs.shape[0]), replace=False))
+    n = len(idx)
+    if ls.routing == "router":
+        _, r_ids, r_probs = oracle.router(W, xs[idx], H, E, K, n)
+    else:
+        r_ids, r_probs = oracle.route_from_logits(ls.logit_in[0].cpu().numpy()[idx], E, K, n)
+    ref = oracle.experts(ls.wtype, gu, dn, r_ids, r_probs, None, xs[idx], H, I, E, K, n, os.cpu_count() or 1)
+    got = outs[idx].astype(np.float64)
+    rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+    mx = float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+    ids_ok = bool(np.array_equal(ids[idx], r_ids))
+    return {"ok": ids_ok and rel <= 1e-4 and mx <= 1e-3, "ids_exact": ids_ok, "max_rel_l2": rel,
+            "max_abs_frac": mx, "bit_exact": bool(np.array_equal(outs[idx], ref)), "tokens_checked": n,
+            "of_tokens": int(xs.shape[0]), "reference": "oracle/ (the reference's CPU MoE path restated)"}
 
 
 class StackSet:
@@ -661,6 +742,21 @@ def algorithmic_bytes(ls, unique, pairs):
     return layer, gate_up
 
 
+def nvlink_record(ls, step_ms, kern, n, world):
+    """The exchange's NVLink figures for one rank (the maximum over ranks of
+    the bytes received): bytes per step, the time the step spends outside
+    the library's expert kernels, and the peer-copy roofline of those bytes."""
+    nv = int(max_over_ranks(float(ls.nvlink_bytes()), world))
+    exch = [k for k in kern if k.startswith("ep_")]
+    rec = {"bytes_received_per_rank_per_step": nv, "peer_copy_peak_GBs": 770.0,
+           "roofline_ms_per_step": round(nv / 770e9 * 1e3, 5), "exchange": ls.ep.exchange}
+    if exch:
+        rec["exchange_kernels_ms_per_step"] = {k: round(kern[k] / n, 5) for k in exch}
+    else:
+        rec["ms_outside_library_kernels_per_step"] = round(step_ms - sum(kern.values()) / n, 5)
+    return rec
+
+
 def tensor_roofline(ls, pairs, step_ms, kern, n):
     """Prefill against the dense int8 tensor peak: the expert products' int8
     operations per step (and gate/up's per launch) over their time."""
@@ -717,8 +813,9 @@ def run_ours(args):
     steps, warmup = args.steps, args.warmup
     hbm_peak, peak_kind = peaks()
 
+    packed = args.weights == "packed"
     if world > 1:
-        ls = EPLayerSet(moe, synth, device, args.workload, 8, rank, world, exchange=args.ep_exchange)
+        ls = EPLayerSet(moe, synth, device, args.workload, 8, rank, world, exchange=args.ep_exchange, packed=packed)
     else:
         ls = LayerSet(moe, synth, device, args.workload, n_inputs=8, seed=rank, packed=args.weights == "packed")
     unique, pairs = ls.unique_experts(0)
@@ -730,6 +827,7 @@ def run_ours(args):
     del graphs
     kern = time_kernels(ls, steps)
     e2e_ms, h2d, d2h = time_e2e(ls, steps, warmup, world)
+    parity = parity_check(ls, world, rank)
 
     T = ls.T
     value = world * T * steps / (ms / 1e3)
@@ -755,9 +853,11 @@ def run_ours(args):
         "data": "synthetic (seeded N(0,0.02) weights quantised with the reference's Q4_0 rules, N(0,1) x)",
         "config": {"workload": args.workload, "hidden": ls.H, "experts": ls.E, "top_k": ls.K, "expert_ffn": ls.I,
                    "tokens_per_step": world * T, "home_tokens_per_rank": T,
-                   "weights": "Q4_0" if ls.wtype == 2 else "Q8_0",
-                   "parallelism": (f"ep{world} (experts sharded; " + ("peer-memory push over NVLink, library kernels"
-                                   if args.ep_exchange == "p2p" else "NCCL all-gather + reduce-scatter") + ")")
+                   "weights": ("Q4_0" if ls.wtype == 2 else "Q8_0") + (
+                       " (repacked at load by mrml_moe_prepare_weights)" if packed else " (GGUF layout)"),
+                   "parallelism": (f"ep{world} (experts sharded; " + (
+                       "sparse Q8_0 row push and partial return over NVLink peer memory, library kernels"
+                       if args.ep_exchange == "p2p" else "NCCL all-gather + reduce-scatter") + ")")
                    if world > 1
                    else "single GPU",
                    "l2": f"inputs larger than L2: steps rotate over {ls.n_layers} layer copies "
@@ -783,49 +883,62 @@ def run_ours(args):
     }
     if T >= 2048 and world == 1:
         line["tensor_roofline"] = tensor_roofline(ls, pairs, ms / steps, kern, steps)
+    if rank == 0:
+        line["parity"] = parity
     if world > 1:
-        nv = ls.nvlink_bytes()
-        comm_ms = ms / steps - total_kern / steps
-        line["nvlink"] = {"bytes_received_per_rank_per_step": nv,
-                          "ms_outside_library_kernels_per_step": round(comm_ms, 5),
-                          "peer_copy_peak_GBs": 770.0,
-                          "roofline_ms_per_step": round(nv / 770e9 * 1e3, 5)}
+        line["nvlink"] = nvlink_record(ls, ms / steps, kern, steps, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
         line["cpu_baseline"] = cpu_baseline(oracle, ls)
-    if not args.no_also and world == 1:
+    if not args.no_also:
         also = {}
-        for name in ("c2_t1", "c2_t8", "c3_prefill"):
+        names = (("c2_t1", "c2_t8", "c3_prefill") if world == 1 else ()) + ("c4", "c4_q8")
+        for name in names:
             if name == args.workload:
                 continue
+            if world > 1:
+                ls.close()
             del ls
+            gc.collect()
             torch.cuda.empty_cache()
-            ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank, packed=args.weights == "packed")
+            if world > 1:
+                ls = EPLayerSet(moe, synth, device, name, 8, rank, world, exchange=args.ep_exchange, packed=packed)
+            else:
+                ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank, packed=packed)
             u, p = ls.unique_experts(0)
             n = max(steps, 20)
             gr = [ls.capture(g) for g in range(2 * ls.n_layers)]
-            m = time_steps(ls, n, max(warmup, 3), world, gr)
+            m = time_steps(ls, n, max(warmup, 3), world, gr, repeats=3)
             del gr
             k = time_kernels(ls, n)
             lb, gb = algorithmic_bytes(ls, u, p)
-            also[name] = {"tokens_per_s": round(ls.T * n / (m / 1e3), 1), "ms_per_step": round(m / n, 5),
-                          "layer_hbm_frac": round(lb / (m / n / 1e3) / 1e9 / hbm_peak, 4),
-                          "gate_up_hbm_frac": round(gb / (k["gate_up"] / n / 1e3) / 1e9 / hbm_peak, 4),
-                          "kernel_ms_per_step": {kk: round(v / n, 5) for kk, v in k.items()},
-                          "unique_experts_step0": u}
-            if ls.T >= 2048:
-                also[name]["tensor_roofline"] = tensor_roofline(ls, p, m / n, k, n)
+            gb_max = max_over_ranks(gb / (k["gate_up"] / n / 1e3) / 1e9 / hbm_peak, world)
+            rec = {"tokens_per_s": round(world * ls.T * n / (m / 1e3), 1), "ms_per_step": round(m / n, 5),
+                   "tokens_per_step": world * ls.T,
+                   "scaling": "strong" if name in STRONG else "weak",
+                   "weights": "Q4_0" if ls.wtype == 2 else "Q8_0",
+                   "layer_hbm_frac": round(lb / (m / n / 1e3) / 1e9 / hbm_peak, 4),
+                   "gate_up_hbm_frac": round(gb_max, 4),
+                   "kernel_ms_per_step": {kk: round(v / n, 5) for kk, v in k.items()},
+                   "unique_experts_step0": u}
+            if ls.T * world >= 2048:
+                rec["tensor_roofline"] = tensor_roofline(ls, p, m / n, k, n)
+            if world > 1:
+                rec["nvlink"] = nvlink_record(ls, m / n, k, n, world)
+            if name in ("c4", "c4_q8"):
+                par = parity_check(ls, world, rank)
+                if rank == 0:
+                    rec["parity"] = par
+            also[name] = rec
         line["also"] = also
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        import gc
-
         import torch.distributed as dist
 
         gc.collect()  # graphs first: they hold the exchange's launches
         torch.cuda.synchronize()
-        ls.ep.close()
+        ls.close()
         dist.destroy_process_group()
 
 

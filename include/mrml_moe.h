@@ -156,38 +156,57 @@ int mrml_moe_experts_shard(int wtype, const uint8_t *gate_up, const uint8_t *dow
                            int E, int e_first, int e_count, int K, int T, void *workspace, size_t workspace_bytes,
                            mrml_stream_t stream);
 
-/* Expert-parallel exchange over NVLink peer memory (no counterpart in the
- * reference, which runs on one device).  Each of the N ranks (one process
- * per GPU) allocates one slab of mrml_moe_ep_slab_bytes(N, T, H, K) bytes
- * with mrml_moe_ep_slab_alloc (set-up time; zeroed), shares its IPC handle
- * (mrml_moe_ipc_get_handle, 64 bytes) with the other ranks, opens theirs
- * (mrml_moe_ipc_open_handle) and keeps a device array `slabs` of the N slab
- * pointers in rank order (its own allocation at its own index).  Per layer
- * step, every rank calls, in this order on one stream:
- *   mrml_moe_ep_dispatch: stores its T home rows x[T][H], ids and probs
- *     [T][K] into every rank's slab and, once all ranks' rows of this step
- *     have arrived, copies them to x_all [N*T][H], ids_all / probs_all
- *     [N*T][K] (rank order);
- *   (its experts, e.g. mrml_moe_experts_shard on those buffers, writing
- *     partial [N*T][H]);
- *   mrml_moe_ep_combine: stores the partial rows of each rank's tokens into
- *     that rank's slab and, once all N partials of its own tokens have
- *     arrived, writes out[T][H] = their sum in rank order.
- * Waits are bounded; a wait that gives up writes MRML_ERR_DEVICE_TIMEOUT's
- * device code into *status (a workspace's status word, read with
- * mrml_moe_device_status) and leaves the outputs untouched.  All ranks must
- * make the same calls with the same shapes; H % 4 == 0, N <= 16. */
+/* Expert parallelism across the GPUs of one node, over NVLink peer memory
+ * (no counterpart in the reference, which runs the layer on one device; its
+ * MoE call, cuda.rs:2840-2880, becomes the per-rank expert step here).
+ * Rank r of N (one process per GPU) holds experts [r*E/N, (r+1)*E/N) and T
+ * home tokens.  Set-up: every rank allocates one slab of
+ * mrml_moe_ep_slab_bytes(N, T, H, K) bytes with mrml_moe_ep_slab_alloc
+ * (zeroed), shares its IPC handle (mrml_moe_ipc_get_handle, 64 bytes), opens
+ * the others' (mrml_moe_ipc_open_handle) and keeps a device array `slabs` of
+ * the N slab pointers in rank order (its own at its own index).  Per layer
+ * step, after routing its home tokens (ids, probs [T][K]), every rank calls
+ * on one stream, in this order:
+ *   mrml_moe_ep_dispatch: quantises each home row x[t] to Q8_0 once (the
+ *     layer's activation quantiser) and stores it into the slabs of the ranks
+ *     that own one of t's experts (pairs with probs > 1e-4), with the ids and
+ *     weights of every home token into every rank;
+ *   mrml_moe_ep_experts: waits for all N ranks' dispatch, runs this rank's
+ *     experts (gate_up / down hold experts [r*E/N, (r+1)*E/N) only, in the
+ *     layout of mrml_moe_experts; down_scale, if given, is indexed by global
+ *     id) on the received rows, and stores into each token's home rank the
+ *     slot-ordered partial sum over this rank's pairs of it;
+ *   mrml_moe_ep_combine: waits for all N ranks' partials, then out[T][H] =
+ *     for each home token, its partials summed in rank order (0 for a token
+ *     with no pair).
+ * The output equals the single-device layer within rounding: each rank's
+ * partial is the single-device slot-ordered sum restricted to its pairs, and
+ * the partials are then added in rank order (bit-identical when one rank owns
+ * all of a token's experts).  Nothing synchronises with the host, so a whole
+ * step can be captured in a CUDA graph.  Waits are bounded (see
+ * MRML_OPTION_EXCHANGE_SPIN_LIMIT); a wait that gives up writes
+ * MRML_ERR_DEVICE_TIMEOUT's device code into the workspace's status word
+ * (read with mrml_moe_device_status) and leaves the data it would have
+ * produced untouched.  All ranks must make the same calls with the same
+ * shapes; H a multiple of 32, E a multiple of N, N <= 16; the experts need
+ * the decode kernel's shapes (H a multiple of 256, I of 64).  The workspace
+ * (mrml_moe_ep_workspace_bytes, 256-byte aligned, zeroed once with
+ * mrml_moe_workspace_init) serves mrml_moe_ep_experts and
+ * mrml_moe_ep_combine. */
 size_t mrml_moe_ep_slab_bytes(int N, int T, int H, int K);
+size_t mrml_moe_ep_workspace_bytes(int N, int T, int H, int I, int E, int K);
 int mrml_moe_ep_slab_alloc(size_t bytes, void **slab);
 int mrml_moe_ep_slab_free(void *slab);
 int mrml_moe_ipc_get_handle(const void *slab, void *handle);
 int mrml_moe_ipc_open_handle(const void *handle, void **slab);
 int mrml_moe_ipc_close_handle(void *slab);
-int mrml_moe_ep_dispatch(void *const *slabs, int rank, int N, int T, int H, int K, const float *x, const int32_t *ids,
-                         const float *probs, float *x_all, int32_t *ids_all, float *probs_all, int *status,
-                         mrml_stream_t stream);
-int mrml_moe_ep_combine(void *const *slabs, int rank, int N, int T, int H, int K, const float *partial, float *out,
-                        int *status, mrml_stream_t stream);
+int mrml_moe_ep_dispatch(void *const *slabs, int rank, int N, int T, int H, int E, int K, const float *x,
+                         const int32_t *ids, const float *probs, mrml_stream_t stream);
+int mrml_moe_ep_experts(int wtype, const uint8_t *gate_up, const uint8_t *down, const float *down_scale,
+                        void *const *slabs, int rank, int N, int T, int H, int I, int E, int K, void *workspace,
+                        size_t workspace_bytes, mrml_stream_t stream);
+int mrml_moe_ep_combine(void *const *slabs, int rank, int N, int T, int H, int E, int K, const int32_t *ids,
+                        const float *probs, float *out, void *workspace, mrml_stream_t stream);
 
 /* The whole layer: mrml_moe_router on (router_w, router_x) followed by
  * mrml_moe_experts on x.  router_x and x may be the same pointer.  Up to 32
@@ -262,6 +281,10 @@ enum { MRML_OPTION_EXPERT_PATH = 1 };
 /* Tuning of the decode (CUDA-core) expert kernel: CTAs per SM (1..8) and
  * the depth of its weight ring (1..8); 0 restores the automatic choice. */
 enum { MRML_OPTION_DECODE_CTAS_PER_SM = 2, MRML_OPTION_DECODE_RING = 3 };
+/* Poll limit of the expert-parallel exchange's bounded waits (about 2^24 by
+ * default, over a second; 0 restores the default).  Lets a test make a wait
+ * give up quickly. */
+enum { MRML_OPTION_EXCHANGE_SPIN_LIMIT = 4 };
 int mrml_moe_set_option(int option, int value);
 
 /* Profiling hook for benchmarks.  With n_events > 0, the following calls on

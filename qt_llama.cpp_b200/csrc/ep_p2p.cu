@@ -1,24 +1,26 @@
 // ep_p2p.cu — the expert-parallel exchange over NVLink peer memory.
 //
 // The expert-parallel layer (rank r of N holds experts [r*E/N, (r+1)*E/N)
-// and T home tokens) needs two exchanges per step: every rank must see all
-// N*T tokens (rows, expert ids, weights) before its experts run, and every
-// token's N partial outputs must come back to its home rank and be summed.
-// Here both are done by this library's kernels writing straight into the
+// and T home tokens) needs two exchanges per step.  Both are sparse: a token
+// goes only to the ranks that own one of its experts, and only those ranks
+// send a partial output back.  The library's kernels write straight into the
 // other GPUs' memory (CUDA IPC mappings of each rank's "slab"), without a
 // collective library:
 //
-//   dispatch:  push   — rank r stores its home rows, ids and weights into
-//                       slot r of every rank's receive area, then raises a
-//                       counter in every rank's slab (system-scope atomics);
-//              gather — a rank waits until all N counters show this step,
-//                       then copies the N slots into the contiguous
-//                       [N*T, ...] buffers its expert kernels read;
-//   combine:   push   — rank r stores the partial output rows of rank q's
-//                       tokens into slot r of q's partial area, then raises
-//                       q's combine counter;
-//              reduce — the home rank waits for all N partials and sums
-//                       them in rank order (out = ((p0 + p1) + p2) + ...).
+//   dispatch (home rank):   quantise each home row to Q8_0 once (the layer's
+//     own activation quantiser, quant.rs:193-228), store its values and f16
+//     scales into every rank that owns one of its experts, store the ids and
+//     weights of all home tokens into every rank, then raise a counter in
+//     every rank's slab (system-scope atomics);
+//   receive (expert rank):  wait until all N counters show this step, copy
+//     the N ranks' ids / weights into the workspace; the expert kernels then
+//     read the received Q8_0 rows straight from the slab;
+//   combine push (expert rank): per received token with a pair here, the
+//     slot-ordered partial sum over this rank's pairs (the single-device
+//     combine's arithmetic) is stored into the token's home rank, then a
+//     counter is raised in every rank's slab;
+//   reduce (home rank):     wait for all N combine pushes, then sum each home
+//     token's partials over the ranks that own its experts, in rank order.
 //
 // Slab layout (identical on every rank, offsets from slab_layout): control
 // counters written by peers, rank-local counters, and double-buffered
@@ -28,48 +30,57 @@
 // every kernel reads it, so a captured step replays correctly.  Double
 // buffering makes slot reuse safe: a rank writes parity p of a peer's areas
 // in step s + 2 only after it has waited, in step s + 1, for that peer's
-// step s + 1 combine push, which the peer issues after it finished reading
-// parity p in step s.
+// push of step s + 1, which the peer issues after it finished reading
+// parity p in step s (dispatch areas: the peer's combine push follows its
+// expert kernels; combine areas: the peer's dispatch push follows its
+// reduce).
 //
-// Every wait is bounded (kSpinLimit polls with back-off); a wait that gives
-// up records MRML_ERR_DEVICE_TIMEOUT in the caller's status word and the
-// kernel leaves without touching the data, so a rank that stops never
-// hangs the others' GPUs.
+// Every wait is bounded (a spin limit, kSpinLimit polls by default); a wait
+// that gives up records MRML_ERR_DEVICE_TIMEOUT in the caller's status word
+// and the kernel leaves without touching the data it would have produced, so
+// a rank that stops never hangs the others' GPUs.
 #include <string.h>
+
+#include <atomic>
 
 #include "../../include/mrml_moe.h"
 #include "common.cuh"
+#include "kernels.h"
 
 namespace mrml {
 namespace ep {
 
-constexpr int kMaxRanks = 16;
-
 struct Control {
-  unsigned int disp[kMaxRanks];  // dispatch pushes received from each rank
-  unsigned int comb[kMaxRanks];  // combine pushes received from each rank
-  unsigned int step;             // steps completed by this rank (rank-local)
-  unsigned int done_push;        // CTAs of the running push kernel that finished (rank-local)
-  unsigned int done_reduce;      // CTAs of the running reduce kernel that finished (rank-local)
+  unsigned int disp[kEpMaxRanks];  // dispatch pushes received from each rank
+  unsigned int comb[kEpMaxRanks];  // combine pushes received from each rank
+  unsigned int step;               // steps completed by this rank (rank-local)
+  unsigned int done_push;          // CTAs of the running push kernel that finished (rank-local)
+  unsigned int done_reduce;        // CTAs of the running reduce kernel that finished (rank-local)
 };
 
 struct Layout {
-  size_t xin, ids, probs, pin, bytes;  // byte offsets in the slab
+  size_t ids, probs, q, d, part, bytes;  // byte offsets in the slab
 };
 
 __host__ __device__ inline size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
+// Receive areas, each [parity][source rank][token]: ids / probs [K] of every
+// home token of the source; the Q8_0 values [H] and f16 scales [H/32] of
+// the source's tokens that have a pair here; the partial rows [H] of this
+// rank's home tokens computed by the source.
 __host__ __device__ inline Layout slab_layout(int N, int T, int H, int K) {
   Layout L;
   size_t off = align256(sizeof(Control));
-  const size_t rows = (size_t)2 * N * T;  // [parity][rank][token]
-  L.xin = off;
-  off += align256(rows * H * 4);
+  const size_t rows = (size_t)2 * N * T;
   L.ids = off;
   off += align256(rows * K * 4);
   L.probs = off;
   off += align256(rows * K * 4);
-  L.pin = off;
+  L.q = off;
+  off += align256(rows * H);
+  L.d = off;
+  off += align256(rows * (H / 32) * 2);
+  L.part = off;
   off += align256(rows * H * 4);
   L.bytes = off;
   return L;
@@ -82,12 +93,12 @@ __device__ __forceinline__ unsigned int load_acquire_sys(const unsigned int* p) 
 }
 
 // Thread 0 waits until every rank's counter in `cnt` reaches `target`;
-// false (and a recorded timeout) if one does not within the limit.
-__device__ bool wait_counts(const unsigned int* cnt, int N, unsigned int target, int* err) {
+// false (and a recorded timeout) if one does not within `limit` polls.
+__device__ bool wait_counts(const unsigned int* cnt, int N, unsigned int target, unsigned int limit, int* err) {
   for (int r = 0; r < N; ++r) {
     uint32_t i = 0;
     while (load_acquire_sys(cnt + r) < target) {
-      if (++i >= kSpinLimit) {
+      if (++i >= limit) {
         set_error(err, kDevTimeout);
         return false;
       }
@@ -115,100 +126,225 @@ __device__ void push_done(Control* mine, uint8_t* const* slabs, int rank, int N,
   }
 }
 
-// grid (blocks, N): y = destination rank q.  Rows of x [T][H] and the ids /
-// probs [T][K] go to slot `rank` of q's receive areas (parity of the step).
-__global__ void dispatch_push_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int K,
-                                     const float4* __restrict__ x, const int32_t* __restrict__ ids,
+// Ranks that own one of token t's experts (pairs with alpha > 1e-4 and an
+// id in [0, E); experts [q*E/N, (q+1)*E/N) on rank q), as a bit mask;
+// every lane of the warp gets it.
+__device__ __forceinline__ unsigned int owner_mask(const int32_t* __restrict__ ids, const float* __restrict__ probs,
+                                                   int t, int K, int E, int N) {
+  const int lane = threadIdx.x & 31, per = E / N;
+  unsigned int m = 0;
+  for (int k = lane; k < K; k += 32) {
+    const int id = ids[(size_t)t * K + k];
+    if (probs[(size_t)t * K + k] > 0.0001f && id >= 0 && id < E) m |= 1u << (id / per);
+  }
+  return __reduce_or_sync(0xffffffffu, m);
+}
+
+// Dispatch push.  One warp per (home token, 32-element block): the block is
+// quantised to Q8_0 (quant.rs:193-228, as quantize_rows_kernel does) and its
+// 32 values and f16 scale are stored into every rank that owns one of the
+// token's experts.  Threads [0, T*K) of the grid also store the ids and
+// weights of all home tokens into every rank.
+__global__ void dispatch_push_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int E, int K,
+                                     const float* __restrict__ x, const int32_t* __restrict__ ids,
                                      const float* __restrict__ probs) {
-  const int q = blockIdx.y;
   Control* mine = reinterpret_cast<Control*>(slabs[rank]);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int par = mine->step & 1u;
-  uint8_t* dst = slabs[q];
-  const size_t slot = ((size_t)par * N + rank) * T;  // first row of the slot
-  float4* xd = reinterpret_cast<float4*>(dst + L.xin) + slot * (H / 4);
-  const size_t n4 = (size_t)T * (H / 4);
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
-    xd[i] = x[i];
-  if (blockIdx.x == 0) {
-    int32_t* idd = reinterpret_cast<int32_t*>(dst + L.ids) + slot * K;
-    float* pd = reinterpret_cast<float*>(dst + L.probs) + slot * K;
-    for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
-      idd[i] = ids[i];
-      pd[i] = probs[i];
+  const int lane = threadIdx.x & 31, nb = H / 32;
+  const size_t slot = ((size_t)par * N + rank) * T;  // first row of this rank's slot
+  const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gtid < (long long)T * K) {
+    const int32_t id = ids[gtid];
+    const float p = probs[gtid];
+    for (int q = 0; q < N; ++q) {
+      reinterpret_cast<int32_t*>(slabs[q] + L.ids)[slot * K + gtid] = id;
+      reinterpret_cast<float*>(slabs[q] + L.probs)[slot * K + gtid] = p;
+    }
+  }
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < (long long)T * nb;
+       w += warps) {
+    const int t = (int)(w / nb), b = (int)(w % nb);
+    const unsigned int mask = owner_mask(ids, probs, t, K, E, N);
+    if (mask == 0) continue;  // warp-uniform
+    const float v = x[(size_t)t * H + 32 * b + lane];
+    float amax = fabsf(v);
+    if (!(amax > 0.f)) amax = 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = __fdiv_rn(amax, 127.0f);
+    const uint32_t d16 = f32_to_f16_trunc(scale);
+    const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+    float r = round_half_away(__fmul_rn(v, id));
+    if (r != r) r = 0.f;
+    r = fminf(fmaxf(r, -128.f), 127.f);
+    // four lanes' bytes into one word, held by the lane with (lane & 3) == 0
+    uint32_t word = ((uint32_t)(int)r & 0xffu) << (8 * (lane & 3));
+    word |= __shfl_xor_sync(0xffffffffu, word, 1);
+    word |= __shfl_xor_sync(0xffffffffu, word, 2);
+    for (int q = 0; q < N; ++q) {
+      if (!(mask >> q & 1u)) continue;
+      if ((lane & 3) == 0)
+        reinterpret_cast<uint32_t*>(slabs[q] + L.q + (slot + t) * H + 32 * b)[lane >> 2] = word;
+      if (lane == 0) reinterpret_cast<uint16_t*>(slabs[q] + L.d)[(slot + t) * nb + b] = (uint16_t)d16;
     }
   }
   push_done(mine, slabs, rank, N, 0);
 }
 
-// Waits for all N dispatch pushes of this step, then copies the receive
-// slots into the contiguous buffers x_all [N*T][H], ids_all / probs_all
-// [N*T][K] (rank order).
-__global__ void dispatch_gather_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int K,
-                                       float4* __restrict__ x_all, int32_t* __restrict__ ids_all,
-                                       float* __restrict__ probs_all, int* __restrict__ err) {
+// Receive: waits for all N dispatch pushes of this step, then copies the N
+// ranks' ids / weights into ids_all / probs_all [N*T][K] (rank order) and
+// (CTA 0) publishes the step's received Q8_0 rows: rows[0] = values
+// [N*T][H], rows[1] = f16 scales [N*T][H/32].  After a timeout the copies
+// are zero weights, so that the expert kernels that follow find no pairs.
+__global__ void recv_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int K,
+                            int32_t* __restrict__ ids_all, float* __restrict__ probs_all,
+                            const uint8_t** __restrict__ rows, unsigned int limit, int* __restrict__ err) {
   __shared__ int ok;
   uint8_t* mine_b = slabs[rank];
   Control* mine = reinterpret_cast<Control*>(mine_b);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int step = mine->step, par = step & 1u;
-  if (threadIdx.x == 0) ok = wait_counts(mine->disp, N, step + 1, err) ? 1 : 0;
+  if (threadIdx.x == 0) ok = wait_counts(mine->disp, N, step + 1, limit, err) ? 1 : 0;
   __syncthreads();
-  if (!ok) return;
   const size_t base = (size_t)par * N * T;
-  const float4* xs = reinterpret_cast<const float4*>(mine_b + L.xin) + base * (H / 4);
-  const size_t n4 = (size_t)N * T * (H / 4);
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
-    x_all[i] = xs[i];
   const int32_t* is = reinterpret_cast<const int32_t*>(mine_b + L.ids) + base * K;
   const float* ps = reinterpret_cast<const float*>(mine_b + L.probs) + base * K;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)N * T * K;
        i += (size_t)gridDim.x * blockDim.x) {
-    ids_all[i] = is[i];
-    probs_all[i] = ps[i];
+    ids_all[i] = ok ? is[i] : 0;
+    probs_all[i] = ok ? ps[i] : 0.f;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    rows[0] = mine_b + L.q + base * H;
+    rows[1] = mine_b + L.d + base * (H / 32) * 2;
+  }
+  pdl_trigger();
+}
+
+// The decode kernel's group-major operand from the received Q8_0 rows (as
+// gather_groups_kernel does from quantize_rows_kernel's output): one warp per
+// (position group, block); lane (j = lane / 4, part = lane % 4) copies 8
+// bytes of position j's row.  The block's value sum (the Q4_0 correction)
+// is summed over the row's 32 bytes.  Positions in use: *poff_end.
+__global__ void recv_gather_kernel(const uint8_t* const* __restrict__ rows, const int32_t* __restrict__ pair_at,
+                                   const int32_t* __restrict__ poff_end, int H, int K, int wq4, int npad,
+                                   int8_t* __restrict__ bq, int2* __restrict__ bsc) {
+  pdl_wait();
+  pdl_trigger();
+  const int nb = H / 32;
+  const int8_t* xq = reinterpret_cast<const int8_t*>(rows[0]);
+  const uint16_t* xd = reinterpret_cast<const uint16_t*>(rows[1]);
+  const long long total = (long long)(*poff_end / 8) * nb;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31, j = lane >> 2, part = lane & 3;
+  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+    const int g = (int)(w / nb), b = (int)(w % nb);
+    const int pos = 8 * g + j;
+    const int pair = pair_at[pos];
+    const int t = pair >= 0 ? pair / K : -1;
+    uint2 v = make_uint2(0u, 0u);
+    if (t >= 0) v = *reinterpret_cast<const uint2*>(xq + (size_t)t * H + 32 * b + 8 * part);
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s += (int)(int8_t)(v.x >> (8 * k)) + (int)(int8_t)(v.y >> (8 * k));
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + act_group_offset(true, b, g, nb, npad) + (part >> 1) * 128 +
+                   j * 16 + 8 * (part & 1);
+    *reinterpret_cast<uint2*>(dst) = v;
+    if (part == 0) {
+      float d = 0.f;
+      int corr = kMagicI;
+      if (t >= 0) {
+        d = f16_bits_to_f32(xd[(size_t)t * nb + b]);
+        if (wq4) corr = kMagicI - 8 * s;
+      }
+      store_act_scale_gm(bsc, b, pos, nb, d, corr);
+    }
   }
 }
 
-// grid (blocks, N): y = home rank q of the tokens.  Rows [q*T, (q+1)*T) of
-// partial [N*T][H] go to slot `rank` of q's partial area.
+// Combine push.  One warp per received token slot j = src * T + t: if this
+// rank computed any of its pairs, the warp forms the slot-ordered partial
+// (sum over k ascending of (alpha_k * ydown[pos]) * scale[id], from 0; the
+// single-device combine's arithmetic, model.rs:2163-2165) and stores it
+// into rank src's partial area.
 __global__ void combine_push_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int K,
-                                    const float4* __restrict__ partial) {
-  const int q = blockIdx.y;
+                                    const float* __restrict__ ydown, const int32_t* __restrict__ pos,
+                                    const int32_t* __restrict__ ids_all, const float* __restrict__ probs_all,
+                                    const float* __restrict__ down_scale) {
+  pdl_wait();
   Control* mine = reinterpret_cast<Control*>(slabs[rank]);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int par = mine->step & 1u;
-  float4* pd = reinterpret_cast<float4*>(slabs[q] + L.pin) + ((size_t)par * N + rank) * T * (H / 4);
-  const float4* ps = partial + (size_t)q * T * (H / 4);
-  const size_t n4 = (size_t)T * (H / 4);
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
-    pd[i] = ps[i];
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long j = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); j < (long long)N * T;
+       j += warps) {
+    bool any = false;
+    for (int k = lane; k < K; k += 32) any |= pos[j * K + k] >= 0;
+    if (!__any_sync(0xffffffffu, any)) continue;
+    const int src = (int)(j / T), t = (int)(j % T);
+    float4* dst = reinterpret_cast<float4*>(slabs[src] + L.part) + (((size_t)par * N + rank) * T + t) * (H / 4);
+    for (int i4 = lane; i4 < H / 4; i4 += 32) {
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < K; ++k) {
+        const int p = pos[j * K + k];
+        if (p < 0) continue;
+        const float alpha = probs_all[j * K + k];
+        const float sc = down_scale ? down_scale[ids_all[j * K + k]] : 1.0f;
+        const float4 y = reinterpret_cast<const float4*>(ydown + (size_t)p * H)[i4];
+        o.x = __fadd_rn(o.x, __fmul_rn(__fmul_rn(alpha, y.x), sc));
+        o.y = __fadd_rn(o.y, __fmul_rn(__fmul_rn(alpha, y.y), sc));
+        o.z = __fadd_rn(o.z, __fmul_rn(__fmul_rn(alpha, y.z), sc));
+        o.w = __fadd_rn(o.w, __fmul_rn(__fmul_rn(alpha, y.w), sc));
+      }
+      dst[i4] = o;
+    }
+  }
   push_done(mine, slabs, rank, N, 1);
 }
 
-// Waits for the N partials of this step's home tokens and sums them in
-// rank order; the last CTA to finish advances the step count.
-__global__ void combine_reduce_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int K,
-                                      float4* __restrict__ out, int* __restrict__ err) {
+// Reduce: waits for the N combine pushes of this step, then out[t] = the
+// partials of the ranks that own one of t's experts, summed in rank order
+// (0 for a token with no pair); the last CTA to finish advances the step.
+// One warp per home token.  After a timeout `out` is left untouched.
+__global__ void combine_reduce_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int E, int K,
+                                      const int32_t* __restrict__ ids, const float* __restrict__ probs,
+                                      float4* __restrict__ out, unsigned int limit, int* __restrict__ err) {
   __shared__ int ok;
   uint8_t* mine_b = slabs[rank];
   Control* mine = reinterpret_cast<Control*>(mine_b);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int step = mine->step, par = step & 1u;
-  if (threadIdx.x == 0) ok = wait_counts(mine->comb, N, step + 1, err) ? 1 : 0;
+  if (threadIdx.x == 0) ok = wait_counts(mine->comb, N, step + 1, limit, err) ? 1 : 0;
   __syncthreads();
   if (ok) {
-    const size_t n4 = (size_t)T * (H / 4);
-    const float4* pin = reinterpret_cast<const float4*>(mine_b + L.pin) + (size_t)par * N * n4;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-      float4 o = pin[i];
-      for (int r = 1; r < N; ++r) {
-        const float4 v = pin[(size_t)r * n4 + i];
-        o.x = __fadd_rn(o.x, v.x);
-        o.y = __fadd_rn(o.y, v.y);
-        o.z = __fadd_rn(o.z, v.z);
-        o.w = __fadd_rn(o.w, v.w);
+    const int lane = threadIdx.x & 31;
+    const float4* part = reinterpret_cast<const float4*>(mine_b + L.part) + (size_t)par * N * T * (H / 4);
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long t = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+      const unsigned int mask = owner_mask(ids, probs, (int)t, K, E, N);
+      for (int i4 = lane; i4 < H / 4; i4 += 32) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        bool first = true;
+        for (int q = 0; q < N; ++q) {
+          if (!(mask >> q & 1u)) continue;
+          const float4 v = part[((size_t)q * T + t) * (H / 4) + i4];
+          if (first) {
+            o = v;
+            first = false;
+          } else {
+            o.x = __fadd_rn(o.x, v.x);
+            o.y = __fadd_rn(o.y, v.y);
+            o.z = __fadd_rn(o.z, v.z);
+            o.w = __fadd_rn(o.w, v.w);
+          }
+        }
+        out[(size_t)t * (H / 4) + i4] = o;
       }
-      out[i] = o;
     }
   }
   // Every CTA has read the step count; the last one advances it.
@@ -224,33 +360,66 @@ __global__ void combine_reduce_kernel(uint8_t* const* __restrict__ slabs, int ra
   }
 }
 
-int grid_blocks(size_t n4) {
-  size_t g = (n4 + 255) / 256;
-  if (g > 148 * 4) g = 148 * 4;
+int grid_for(long long items, int per_cta) {
+  long long g = (items + per_cta - 1) / per_cta;
+  if (g > 148 * 8) g = 148 * 8;
   return (int)(g < 1 ? 1 : g);
 }
 
+std::atomic<unsigned int> g_spin_limit{kSpinLimit};
+
 }  // namespace ep
+
+size_t ep_slab_bytes(int N, int T, int H, int K) { return ep::slab_layout(N, T, H, K).bytes; }
+
+void ep_set_spin_limit(unsigned int limit) { ep::g_spin_limit.store(limit ? limit : kSpinLimit); }
+
+cudaError_t launch_ep_dispatch(uint8_t* const* slabs, int rank, int N, int T, int H, int E, int K, const float* x,
+                               const int32_t* ids, const float* probs, cudaStream_t s) {
+  const long long warps = (long long)T * (H / 32);
+  const int grid = std::max(ep::grid_for(warps, 8), ep::grid_for((long long)T * K, 256));
+  ep::dispatch_push_kernel<<<grid, 256, 0, s>>>(slabs, rank, N, T, H, E, K, x, ids, probs);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_ep_recv(uint8_t* const* slabs, int rank, int N, int T, int H, int K, int32_t* ids_all,
+                           float* probs_all, const uint8_t** rows, int* err, cudaStream_t s) {
+  const int grid = ep::grid_for((long long)N * T * K, 256 * 4);
+  ep::recv_kernel<<<grid, 256, 0, s>>>(slabs, rank, N, T, H, K, ids_all, probs_all, rows,
+                                       ep::g_spin_limit.load(), err);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_ep_gather(int wtype, const uint8_t* const* rows, const int32_t* pair_at, const int32_t* poff_end,
+                             int H, int K, int npad, int8_t* bq, int2* bsc, cudaStream_t s) {
+  const long long warps = (long long)(npad / 8) * (H / 32);  // upper bound; the kernel reads the count
+  return launch_pdl(ep::recv_gather_kernel, dim3(ep::grid_for(warps, 8)), dim3(256), 0, s, rows, pair_at, poff_end,
+                    H, K, wtype == kQ4_0 ? 1 : 0, npad, bq, bsc);
+}
+
+cudaError_t launch_ep_combine_push(uint8_t* const* slabs, int rank, int N, int T, int H, int K, const float* ydown,
+                                   const int32_t* pos, const int32_t* ids_all, const float* probs_all,
+                                   const float* down_scale, cudaStream_t s) {
+  return launch_pdl(ep::combine_push_kernel, dim3(ep::grid_for((long long)N * T, 8)), dim3(256), 0, s, slabs, rank,
+                    N, T, H, K, ydown, pos, ids_all, probs_all, down_scale);
+}
+
+cudaError_t launch_ep_reduce(uint8_t* const* slabs, int rank, int N, int T, int H, int E, int K, const int32_t* ids,
+                             const float* probs, float* out, int* err, cudaStream_t s) {
+  ep::combine_reduce_kernel<<<ep::grid_for(T, 8), 256, 0, s>>>(slabs, rank, N, T, H, E, K, ids, probs,
+                                                                 reinterpret_cast<float4*>(out),
+                                                                 ep::g_spin_limit.load(), err);
+  return cudaPeekAtLastError();
+}
+
 }  // namespace mrml
 
 using namespace mrml::ep;
 
-namespace {
-
-int ep_args_ok(void* const* slabs, int rank, int N, int T, int H, int K) {
-  if (!slabs || N < 1 || N > kMaxRanks || rank < 0 || rank >= N || T < 1 || H < 4 || H % 4 != 0 || K < 1 || K > 64)
-    return MRML_ERR_INVALID_ARGUMENT;
-  return MRML_OK;
-}
-
-int launched() { return cudaPeekAtLastError() == cudaSuccess ? MRML_OK : MRML_ERR_CUDA; }
-
-}  // namespace
-
 extern "C" {
 
 size_t mrml_moe_ep_slab_bytes(int N, int T, int H, int K) {
-  if (N < 1 || N > kMaxRanks || T < 1 || H < 4 || H % 4 != 0 || K < 1 || K > 64) return 0;
+  if (N < 1 || N > mrml::kEpMaxRanks || T < 1 || H < 32 || H % 32 != 0 || K < 1 || K > mrml::kMaxTopK) return 0;
   return slab_layout(N, T, H, K).bytes;
 }
 
@@ -292,40 +461,6 @@ int mrml_moe_ipc_open_handle(const void* handle, void** slab) {
 int mrml_moe_ipc_close_handle(void* slab) {
   if (!slab) return MRML_OK;
   return cudaIpcCloseMemHandle(slab) == cudaSuccess ? MRML_OK : MRML_ERR_CUDA;
-}
-
-int mrml_moe_ep_dispatch(void* const* slabs, int rank, int N, int T, int H, int K, const float* x, const int32_t* ids,
-                         const float* probs, float* x_all, int32_t* ids_all, float* probs_all, int* status,
-                         mrml_stream_t stream) {
-  int st = ep_args_ok(slabs, rank, N, T, H, K);
-  if (st != MRML_OK) return st;
-  if (!x || !ids || !probs || !x_all || !ids_all || !probs_all || !status) return MRML_ERR_INVALID_ARGUMENT;
-  if ((((uintptr_t)x | (uintptr_t)x_all) & 15) != 0) return MRML_ERR_INVALID_ARGUMENT;
-  const cudaStream_t s = (cudaStream_t)stream;
-  uint8_t* const* sl = reinterpret_cast<uint8_t* const*>(slabs);
-  const size_t n4 = (size_t)T * (H / 4);
-  dispatch_push_kernel<<<dim3(grid_blocks(n4), N), 256, 0, s>>>(sl, rank, N, T, H, K,
-                                                               reinterpret_cast<const float4*>(x), ids, probs);
-  if ((st = launched()) != MRML_OK) return st;
-  dispatch_gather_kernel<<<grid_blocks(n4 * N), 256, 0, s>>>(sl, rank, N, T, H, K, reinterpret_cast<float4*>(x_all),
-                                                             ids_all, probs_all, status);
-  return launched();
-}
-
-int mrml_moe_ep_combine(void* const* slabs, int rank, int N, int T, int H, int K, const float* partial, float* out,
-                        int* status, mrml_stream_t stream) {
-  int st = ep_args_ok(slabs, rank, N, T, H, K);
-  if (st != MRML_OK) return st;
-  if (!partial || !out || !status) return MRML_ERR_INVALID_ARGUMENT;
-  if ((((uintptr_t)partial | (uintptr_t)out) & 15) != 0) return MRML_ERR_INVALID_ARGUMENT;
-  const cudaStream_t s = (cudaStream_t)stream;
-  uint8_t* const* sl = reinterpret_cast<uint8_t* const*>(slabs);
-  const size_t n4 = (size_t)T * (H / 4);
-  combine_push_kernel<<<dim3(grid_blocks(n4), N), 256, 0, s>>>(sl, rank, N, T, H, K,
-                                                              reinterpret_cast<const float4*>(partial));
-  if ((st = launched()) != MRML_OK) return st;
-  combine_reduce_kernel<<<grid_blocks(n4), 256, 0, s>>>(sl, rank, N, T, H, K, reinterpret_cast<float4*>(out), status);
-  return launched();
 }
 
 }  // extern "C"

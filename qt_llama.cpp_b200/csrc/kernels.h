@@ -130,6 +130,23 @@ cudaError_t launch_gemm_tc(int mode, int wtype, int NT, const uint8_t* weights, 
                            int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s);
 cudaError_t launch_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,
                            const float* down_scale, float* out, int H, int K, int T, cudaStream_t s);
+
+// Expert-parallel exchange over peer memory (ep_p2p.cu).
+constexpr int kEpMaxRanks = 16;
+size_t ep_slab_bytes(int N, int T, int H, int K);
+// Poll limit of the exchange's bounded waits (0 restores the default).
+void ep_set_spin_limit(unsigned int limit);
+cudaError_t launch_ep_dispatch(uint8_t* const* slabs, int rank, int N, int T, int H, int E, int K, const float* x,
+                               const int32_t* ids, const float* probs, cudaStream_t s);
+cudaError_t launch_ep_recv(uint8_t* const* slabs, int rank, int N, int T, int H, int K, int32_t* ids_all,
+                           float* probs_all, const uint8_t** rows, int* err, cudaStream_t s);
+cudaError_t launch_ep_gather(int wtype, const uint8_t* const* rows, const int32_t* pair_at, const int32_t* poff_end,
+                             int H, int K, int npad, int8_t* bq, int2* bsc, cudaStream_t s);
+cudaError_t launch_ep_combine_push(uint8_t* const* slabs, int rank, int N, int T, int H, int K, const float* ydown,
+                                   const int32_t* pos, const int32_t* ids_all, const float* probs_all,
+                                   const float* down_scale, cudaStream_t s);
+cudaError_t launch_ep_reduce(uint8_t* const* slabs, int rank, int N, int T, int H, int E, int K, const int32_t* ids,
+                             const float* probs, float* out, int* err, cudaStream_t s);
 int gate_up_tok_chunk(int wtype, int H);
 int down_tok_chunk(int wtype, int I);
 

@@ -162,8 +162,8 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? MRML_OK : MRML_ERR_CU
 int base_type(int wtype) { return wtype & ~MRML_PACKED; }
 bool is_packed(int wtype) { return (wtype & MRML_PACKED) != 0; }
 
-int check_expert_args(int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids, const float* probs,
-                      const float* x, const float* out, int H, int I, int E, int K, int T) {
+// Weight type and the shapes it constrains (E experts' slabs).
+int check_weights(int wtype, int H, int I, int E, int K, int T) {
   const int wt = base_type(wtype);
   if (wt != MRML_Q4_0 && wt != MRML_Q8_0) return MRML_ERR_UNSUPPORTED;
   if ((wtype & ~(MRML_PACKED | 0xff)) != 0) return MRML_ERR_UNSUPPORTED;
@@ -173,9 +173,15 @@ int check_expert_args(int wtype, const uint8_t* gate_up, const uint8_t* down, co
   if (H % 32 != 0 || I % 32 != 0) return MRML_ERR_INVALID_ARGUMENT;
   if (E > kMaxE || K > kMaxK) return MRML_ERR_UNSUPPORTED;
   if ((long long)T * K > (1ll << 30)) return MRML_ERR_UNSUPPORTED;
+  if (mrml::gate_up_tok_chunk(wt, H) == 0 || mrml::down_tok_chunk(wt, I) == 0) return MRML_ERR_UNSUPPORTED;
+  return MRML_OK;
+}
+
+int check_expert_args(int wtype, const uint8_t* gate_up, const uint8_t* down, const int32_t* ids, const float* probs,
+                      const float* x, const float* out, int H, int I, int E, int K, int T) {
+  MRML_TRY(check_weights(wtype, H, I, E, K, T));
   if (T > 0 && (!gate_up || !down || !ids || !probs || !x || !out)) return MRML_ERR_INVALID_ARGUMENT;
   if (T > 0 && (!aligned16(gate_up) || !aligned16(down) || !aligned16(x))) return MRML_ERR_INVALID_ARGUMENT;
-  if (mrml::gate_up_tok_chunk(wt, H) == 0 || mrml::down_tok_chunk(wt, I) == 0) return MRML_ERR_UNSUPPORTED;
   return MRML_OK;
 }
 
@@ -290,6 +296,80 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
     }
   }
   MRML_LAUNCH(mrml::launch_combine(w.ydown, w.pos, ids, probs, down_scale, out, H, K, T, s));
+  return MRML_OK;
+}
+
+// The expert-parallel workspace: the shard's expert workspace for N*T
+// tokens and E/N experts, then the received ids / weights [N*T][K] and the
+// published row pointers of the step (values, f16 scales).
+struct EpExtras {
+  int32_t* ids_all;
+  float* probs_all;
+  const uint8_t** rows;
+  size_t bytes;
+};
+
+EpExtras carve_ep(void* base, int N, int T, int K) {
+  EpExtras x;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(n);
+    return r;
+  };
+  x.ids_all = reinterpret_cast<int32_t*>(take((size_t)N * T * K * 4));
+  x.probs_all = reinterpret_cast<float*>(take((size_t)N * T * K * 4));
+  x.rows = reinterpret_cast<const uint8_t**>(take(2 * sizeof(void*)));
+  x.bytes = off;
+  return x;
+}
+
+size_t ep_workspace_bytes(int N, int T, int H, int I, int E, int K) {
+  return carve(nullptr, H, I, E / N, K, N * T).bytes + carve_ep(nullptr, N, T, K).bytes;
+}
+
+int check_ep_args(void* const* slabs, int rank, int N, int T, int H, int E, int K) {
+  if (!slabs || N < 1 || N > mrml::kEpMaxRanks || rank < 0 || rank >= N || T < 1 || H < 32 || H % 32 != 0 || K < 1)
+    return MRML_ERR_INVALID_ARGUMENT;
+  if (E < N || E % N != 0 || K > E) return MRML_ERR_INVALID_ARGUMENT;
+  if (E > kMaxE || K > kMaxK) return MRML_ERR_UNSUPPORTED;
+  return MRML_OK;
+}
+
+// The experts of this rank on the tokens every rank sent it (see
+// mrml_moe_ep_experts): receive, dispatch over the N*T received tokens'
+// pairs on this rank's experts, the group-major operand gathered from the
+// received Q8_0 rows, gate/up, down, then the partials pushed home.
+int run_ep_experts(void* ws, int wtype, const uint8_t* gate_up, const uint8_t* down, const float* down_scale,
+                   uint8_t* const* slabs, int rank, int N, int T, int H, int I, int E, int K, cudaStream_t s) {
+  const int Ec = E / N, NT = N * T;
+  const Workspace w = carve(ws, H, I, Ec, K, NT);
+  const EpExtras x = carve_ep(static_cast<uint8_t*>(ws) + w.bytes, N, T, K);
+  const bool packed = is_packed(wtype);
+  wtype = base_type(wtype);
+  const long long pairs = (long long)T * K;  // expected pairs on this rank
+  const Route route = pick_route(wtype, packed, H, I, Ec, pairs);
+  if (route != kRouteGemv && route != kRouteGemvMma) return MRML_ERR_UNSUPPORTED;
+  const bool two = route == kRouteGemvMma && pairs >= 12ll * Ec && mrml::gv_two_groups_supported(wtype, H, I);
+  const int ng_gu = two && wtype == MRML_Q4_0 ? 2 : 1, ng_dn = two ? 2 : 1;
+  const int NT_gu = mrml::kGvTokens * ng_gu, NT_dn = mrml::kGvTokens * ng_dn;
+  const int rows_gu = mrml::kGvRowsGateUp;
+  const int mt_gu = (I + rows_gu - 1) / rows_gu, mt_dn = (H + 127) / 128;
+  int* n_units = w.status + 2;
+  MRML_LAUNCH(mrml::launch_ep_recv(slabs, rank, N, T, H, K, x.ids_all, x.probs_all, x.rows, w.status, s));
+  MRML_LAUNCH(mrml::launch_dispatch(x.ids_all, x.probs_all, NT * K, Ec, rank * Ec, E, w.cnt, w.poff, w.pair_at,
+                                    w.pos, w.units_gu, w.units_dn, n_units, NT_gu, NT_dn, mt_gu, rows_gu, mt_dn,
+                                    w.status, s));
+  MRML_LAUNCH(mrml::launch_ep_gather(wtype, x.rows, w.pair_at, w.poff + Ec, H, K, w.npad, w.xb, w.xs, s));
+  const int mu_gu = units_bound(Ec, K, NT, NT_gu, I, rows_gu), mu_dn = units_bound(Ec, K, NT, NT_dn, H, 128);
+  const bool mma = route == kRouteGemvMma;
+  MRML_LAUNCH(mrml::launch_gemv(0, wtype, packed, mma, ng_gu, gate_up, H, I, Ec, w.xb, w.xs, w.units_gu, n_units,
+                                mu_gu, w.npad, w.ab, w.as, nullptr, w.status, s));
+  MRML_LAUNCH(mrml::launch_gemv(1, wtype, packed, mma, ng_dn, down, H, I, Ec, w.ab, w.as, w.units_dn, n_units + 1,
+                                mu_dn, w.npad, nullptr, nullptr, w.ydown, w.status, s));
+  MRML_LAUNCH(mrml::launch_ep_combine_push(slabs, rank, N, T, H, K, w.ydown, w.pos, x.ids_all, x.probs_all,
+                                           down_scale, s));
   return MRML_OK;
 }
 
@@ -424,6 +504,48 @@ int mrml_moe_prepare_weights(int wtype, const uint8_t* gate_up, const uint8_t* d
   return MRML_OK;
 }
 
+size_t mrml_moe_ep_workspace_bytes(int N, int T, int H, int I, int E, int K) {
+  if (N < 1 || T < 1 || H <= 0 || I <= 0 || E < N || E % N != 0 || K <= 0) return 0;
+  return ep_workspace_bytes(N, T, H, I, E, K);
+}
+
+int mrml_moe_ep_dispatch(void* const* slabs, int rank, int N, int T, int H, int E, int K, const float* x,
+                         const int32_t* ids, const float* probs, mrml_stream_t stream) {
+  MRML_TRY(check_ep_args(slabs, rank, N, T, H, E, K));
+  if (!x || !ids || !probs) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_ep_dispatch(reinterpret_cast<uint8_t* const*>(slabs), rank, N, T, H, E, K, x, ids, probs,
+                                       s));
+  return MRML_OK;
+}
+
+int mrml_moe_ep_experts(int wtype, const uint8_t* gate_up, const uint8_t* down, const float* down_scale,
+                        void* const* slabs, int rank, int N, int T, int H, int I, int E, int K, void* workspace,
+                        size_t workspace_bytes, mrml_stream_t stream) {
+  MRML_TRY(check_ep_args(slabs, rank, N, T, H, E, K));
+  MRML_TRY(check_weights(wtype, H, I, E / N, std::min(K, E / N), N * T));
+  if (H % 256 != 0 || I % mrml::kGvRowsGateUp != 0) return MRML_ERR_UNSUPPORTED;  // the decode kernel's shapes
+  if (!gate_up || !down || !aligned16(gate_up) || !aligned16(down)) return MRML_ERR_INVALID_ARGUMENT;
+  if (!workspace || ((uintptr_t)workspace & 255u) != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < ep_workspace_bytes(N, T, H, I, E, K)) return MRML_ERR_WORKSPACE_TOO_SMALL;
+  MRML_TRY(check_device());
+  return run_ep_experts(workspace, wtype, gate_up, down, down_scale, reinterpret_cast<uint8_t* const*>(slabs), rank,
+                        N, T, H, I, E, K, (cudaStream_t)stream);
+}
+
+int mrml_moe_ep_combine(void* const* slabs, int rank, int N, int T, int H, int E, int K, const int32_t* ids,
+                        const float* probs, float* out, void* workspace, mrml_stream_t stream) {
+  MRML_TRY(check_ep_args(slabs, rank, N, T, H, E, K));
+  if (!ids || !probs || !out || !workspace || !aligned16(out) || ((uintptr_t)workspace & 255u) != 0)
+    return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_ep_reduce(reinterpret_cast<uint8_t* const*>(slabs), rank, N, T, H, E, K, ids, probs, out,
+                                     static_cast<int*>(workspace), s));
+  return MRML_OK;
+}
+
 int mrml_moe_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,
                      const float* down_scale, float* out, int H, int K, int T, mrml_stream_t stream) {
   if (H <= 0 || K <= 0 || T < 0 || K > kMaxK) return MRML_ERR_INVALID_ARGUMENT;
@@ -489,6 +611,10 @@ int mrml_moe_set_option(int option, int value) {
       if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
       gv_ring.store(value);
       mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load());
+      return MRML_OK;
+    case MRML_OPTION_EXCHANGE_SPIN_LIMIT:
+      if (value < 0) return MRML_ERR_INVALID_ARGUMENT;
+      mrml::ep_set_spin_limit((unsigned int)value);
       return MRML_OK;
     default:
       return MRML_ERR_INVALID_ARGUMENT;

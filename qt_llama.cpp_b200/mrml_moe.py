@@ -60,8 +60,10 @@ SIGNATURES = {
     "mrml_moe_ipc_get_handle": (_i, [_vp, _vp]),
     "mrml_moe_ipc_open_handle": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     "mrml_moe_ipc_close_handle": (_i, [_vp]),
-    "mrml_moe_ep_dispatch": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
-    "mrml_moe_ep_combine": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "mrml_moe_ep_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "mrml_moe_ep_dispatch": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "mrml_moe_ep_experts": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "mrml_moe_ep_combine": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "mrml_moe_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mrml_moe_geglu": (_i, [_vp, _vp, _vp, _sz, _vp]),
     "mrml_moe_rms_norm": (_i, [_vp, _vp, _vp, _i, _i, _f, _vp]),
@@ -226,18 +228,40 @@ def ipc_close_handle(ptr: int) -> None:
     _check("mrml_moe_ipc_close_handle", load_library().mrml_moe_ipc_close_handle(ptr))
 
 
-def ep_dispatch(slabs, rank, N, T, H, K, x, ids, probs, x_all, ids_all, probs_all, status, stream=None):
+def new_ep_workspace(N, T, H, I, E, K, device=None):
+    """A zeroed workspace for mrml_moe_ep_experts / mrml_moe_ep_combine."""
+    import torch
+
+    n = load_library().mrml_moe_ep_workspace_bytes(N, T, H, I, E, K)
+    if n == 0:
+        raise MoeError("mrml_moe_ep_workspace_bytes", MRML_ERR_INVALID_ARGUMENT, "invalid argument")
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def ep_dispatch(slabs, rank, N, T, H, E, K, x, ids, probs, stream=None):
     lib = load_library()
     _check("mrml_moe_ep_dispatch",
-           lib.mrml_moe_ep_dispatch(_ptr(slabs), rank, N, T, H, K, _ptr(x), _ptr(ids), _ptr(probs), _ptr(x_all),
-                                    _ptr(ids_all), _ptr(probs_all), _ptr(status), _stream_ptr(stream)))
+           lib.mrml_moe_ep_dispatch(_ptr(slabs), rank, N, T, H, E, K, _ptr(x), _ptr(ids), _ptr(probs),
+                                    _stream_ptr(stream)))
 
 
-def ep_combine(slabs, rank, N, T, H, K, partial, out, status, stream=None):
+def ep_experts(wtype, gate_up, down, down_scale, slabs, rank, N, T, H, I, E, K, ws, stream=None):
+    lib = load_library()
+    _check("mrml_moe_ep_experts",
+           lib.mrml_moe_ep_experts(wtype, _ptr(gate_up), _ptr(down), _ptr(down_scale), _ptr(slabs), rank, N, T, H, I,
+                                   E, K, _ptr(ws), ws.numel(), _stream_ptr(stream)))
+
+
+def ep_combine(slabs, rank, N, T, H, E, K, ids, probs, out, ws, stream=None):
     lib = load_library()
     _check("mrml_moe_ep_combine",
-           lib.mrml_moe_ep_combine(_ptr(slabs), rank, N, T, H, K, _ptr(partial), _ptr(out), _ptr(status),
+           lib.mrml_moe_ep_combine(_ptr(slabs), rank, N, T, H, E, K, _ptr(ids), _ptr(probs), _ptr(out), _ptr(ws),
                                    _stream_ptr(stream)))
+
+
+def set_exchange_spin_limit(limit: int) -> None:
+    """Poll limit of the exchange's bounded waits (0 = the default)."""
+    _check("mrml_moe_set_option", load_library().mrml_moe_set_option(4, limit))
 
 
 def combine(ydown, pos, ids, probs, down_scale, out, H, K, T, stream=None):

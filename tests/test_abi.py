@@ -88,8 +88,13 @@ def test_invalid_arguments_rejected_without_a_gpu(moe):
     assert lib.mrml_moe_ep_slab_bytes(0, 64, 2816, 8) == 0
     assert lib.mrml_moe_ep_slab_bytes(2, 64, 2818, 8) == 0
     assert lib.mrml_moe_ep_slab_bytes(8, 64, 2816, 8) > 8 * 64 * 2816 * 4
-    assert lib.mrml_moe_ep_dispatch(P, 2, 2, 64, 2816, 8, P, P, P, P, P, P, P, None) == -1
-    assert lib.mrml_moe_ep_combine(None, 0, 2, 64, 2816, 8, P, P, P, None) == -1
+    assert lib.mrml_moe_ep_dispatch(P, 2, 2, 64, 2816, 128, 8, P, P, P, None) == -1  # rank out of range
+    assert lib.mrml_moe_ep_dispatch(P, 0, 3, 64, 2816, 128, 8, P, P, P, None) == -1  # E not divisible by N
+    assert lib.mrml_moe_ep_combine(None, 0, 2, 64, 2816, 128, 8, P, P, P, P, None) == -1
+    assert lib.mrml_moe_ep_workspace_bytes(3, 64, 2816, 704, 128, 8) == 0
+    assert lib.mrml_moe_ep_workspace_bytes(8, 64, 2816, 704, 128, 8) > 0
+    # the experts step needs the decode kernel's shapes (I a multiple of 64)
+    assert lib.mrml_moe_ep_experts(2, P, P, None, P, 0, 2, 64, 2816, 96, 128, 8, P, 1 << 30, None) == -2
 
 
 def test_zero_tokens_is_a_no_op(moe):

@@ -153,3 +153,41 @@ def test_shard_range():
         ep.shard_range(0, 3, 128)
     with pytest.raises(ValueError):
         ep.shard_range(2, 2, 128)
+
+
+def _ep_module():
+    sys.path.insert(0, ROOT)
+    from tests.conftest import _load
+
+    return _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sparse_exchange_semantics(world, synth, oracle):
+    """The peer exchange's arithmetic, restated on the host: each rank's
+    partial is the oracle shard; the home rank adds the partials of the
+    ranks that own the token's experts in rank order.  Within the layer
+    tolerance of the reference, and equal to it bit for bit for tokens whose
+    experts all sit on one rank."""
+    ep = _ep_module()
+    wtype, H, I, E, K, T = 2, 256, 128, 16, 4, 24
+    gu, dn, ids, probs, x = _case(synth, oracle, wtype, H, I, E, K, T, 13)
+    probs[3, 1] = 0.0  # a skipped slot does not make its rank an owner
+    ref = oracle.experts(wtype, gu, dn, ids, probs, None, x, H, I, E, K, T)
+    parts = [oracle_shard(oracle, wtype, gu, dn, *synth_range(r, world, E), H, I, E, K)(x, ids, probs)
+             for r in range(world)]
+    masks = ep.owner_masks(ids, probs, world, E)
+    assert masks.shape == (T, world) and masks.any(axis=1).all()
+    if world > 1:
+        per = E // world
+        assert not masks[3, ids[3, 1] // per] or ((ids[3] // per == ids[3, 1] // per) & (probs[3] > 1e-4)).any()
+    out = ep.sparse_sum(parts, masks)
+    assert np.abs(out - ref).max() <= 1e-3 * np.abs(ref).max()
+    assert np.linalg.norm(out - ref) <= 1e-4 * np.linalg.norm(ref)
+    single = masks.sum(axis=1) == 1
+    np.testing.assert_array_equal(out[single], ref[single])
+    # bytes: every received row is counted once per (token, receiving rank)
+    b = ep.exchange_bytes(np.tile(ids, (world, 1)), np.tile(probs, (world, 1)), world, E, H, K, 0, T)
+    row = H + H // 32 * 2
+    assert b["dispatch"] == (world - 1) * (int(masks[:, 0].sum()) * row + T * K * 8)
+    assert b["combine"] == int(masks[:, 1:].sum()) * H * 4

@@ -235,3 +235,125 @@ def test_ep_layer_two_gpus(cuda, moe, oracle, synth, exchange):
             np.testing.assert_array_equal(idss[s], ids[home])
             np.testing.assert_array_equal(outs[s], parts[0][home] + parts[1][home])
             assert_close(outs[s], ref[home])
+
+
+# --------------------------------------------- the peer exchange, one GPU
+# The N ranks of the peer exchange are emulated on one GPU: N slabs in this
+# GPU's memory, and each rank's calls issued in an order in which every wait
+# is already satisfied by kernels that completed earlier on the same stream
+# (all dispatches, then all expert steps, then all combines), so no kernel
+# ever waits on a kernel that runs at the same time.
+
+
+def _ep_module():
+    from tests.conftest import _load
+
+    return _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
+
+
+class OneGpuRanks:
+    """N emulated ranks' slabs, workspaces and expert shards on cuda:0."""
+
+    def __init__(self, moe, device, N, wtype, gu, dn, H, I, E, K, T, packed=False):
+        import torch
+
+        self.moe, self.N, self.H, self.I, self.E, self.K, self.T = moe, N, H, I, E, K, T
+        self.wcall = wtype | (moe.MRML_PACKED if packed else 0)
+        self.own = [moe.ep_slab_alloc(N, T, H, K) for _ in range(N)]
+        self.slabs = torch.tensor(self.own, dtype=torch.int64, device=device)
+        self.ws = [moe.new_ep_workspace(N, T, H, I, E, K, device) for _ in range(N)]
+        per = E // N
+        self.w = []
+        for r in range(N):
+            g = dev_tensor(gu.reshape(E, -1)[r * per:(r + 1) * per], device)
+            d = dev_tensor(dn.reshape(E, -1)[r * per:(r + 1) * per], device)
+            if packed:
+                g, d = moe.prepare_weights(wtype, g.reshape(per, 2 * I, -1), d.reshape(per, H, -1))
+            self.w.append((g, d))
+
+    def step(self, x, ids, probs, out):
+        m, N, H, E, K, T = self.moe, self.N, self.H, self.E, self.K, self.T
+        for r in range(N):
+            m.ep_dispatch(self.slabs, r, N, T, H, E, K, x[r], ids[r], probs[r])
+        for r in range(N):
+            m.ep_experts(self.wcall, self.w[r][0], self.w[r][1], None, self.slabs, r, N, T, H, self.I, E, K,
+                         self.ws[r])
+        for r in range(N):
+            m.ep_combine(self.slabs, r, N, T, H, E, K, ids[r], probs[r], out[r], self.ws[r])
+
+    def close(self):
+        import torch
+
+        torch.cuda.synchronize()
+        for p in self.own:
+            self.moe.ep_slab_free(p)
+        self.own = []
+
+
+@pytest.mark.parametrize("N,wtype,H,I,E,K,T,packed", [(2, 2, 2816, 704, 128, 8, 16, False),
+                                                       (4, 8, 1024, 512, 16, 2, 40, False),
+                                                       (8, 2, 2816, 704, 128, 8, 8, True)])
+def test_peer_exchange_one_gpu(cuda, moe, oracle, synth, N, wtype, H, I, E, K, T, packed):
+    """Two consecutive steps of the sparse peer exchange with N ranks on one
+    GPU: every rank's output equals, bit for bit, the rank-ordered sum of
+    the oracle shards' partials over the ranks that own the token's experts,
+    and the reference within tolerance."""
+    import torch
+
+    ep = _ep_module()
+    gu_d, dn_d = synth.expert_weights_device(31 + N, wtype, H, I, E, cuda, moe.quantize)
+    gu, dn = gu_d.cpu().numpy(), dn_d.cpu().numpy()
+    del gu_d, dn_d
+    W = synth.normal(32 + N, E * H, 0.02).reshape(E, H)
+    R = OneGpuRanks(moe, cuda, N, wtype, gu, dn, H, I, E, K, T, packed)
+    try:
+        for step in range(2):
+            x = synth.normal(40 + 10 * N + step, N * T * H).reshape(N * T, H)
+            _, ids, probs = oracle.router(W, x, H, E, K, N * T)
+            xs = [dev_tensor(x[r * T:(r + 1) * T], cuda) for r in range(N)]
+            idd = [dev_tensor(ids[r * T:(r + 1) * T], cuda) for r in range(N)]
+            prd = [dev_tensor(probs[r * T:(r + 1) * T], cuda) for r in range(N)]
+            outs = [torch.full((T, H), float("nan"), device=cuda) for _ in range(N)]
+            R.step(xs, idd, prd, outs)
+            for r in range(N):
+                assert moe.device_status(R.ws[r])[0] == 0
+            parts = [oracle_shard(oracle, wtype, gu, dn, *synth_range(q, N, E), H, I, E, K)(x, ids, probs)
+                     for q in range(N)]
+            want = ep.sparse_sum(parts, ep.owner_masks(ids, probs, N, E))
+            ref = oracle.experts(wtype, gu, dn, ids, probs, None, x, H, I, E, K, N * T, os.cpu_count() or 1)
+            for r in range(N):
+                home = slice(r * T, (r + 1) * T)
+                got = outs[r].cpu().numpy()
+                assert_exact(got, want[home])
+                assert_close(got, ref[home])
+    finally:
+        R.close()
+
+
+def test_peer_exchange_wait_times_out(cuda, moe, synth):
+    """A rank whose peer never pushes: with a short spin limit the receive
+    wait and the combine wait give up, the device status reads
+    MRML_ERR_DEVICE_TIMEOUT, and the output is left untouched.  The wait is
+    bounded and returns; nothing hangs."""
+    import torch
+
+    N, wtype, H, I, E, K, T = 2, 2, 256, 128, 8, 2, 4
+    gu, dn = synth.expert_weights(51, wtype, H, I, E)
+    R = OneGpuRanks(moe, cuda, N, wtype, gu, dn, H, I, E, K, T)
+    moe.set_exchange_spin_limit(1 << 12)
+    try:
+        x = dev_tensor(synth.normal(52, T * H).reshape(T, H), cuda)
+        ids = dev_tensor(np.array([[0, 5], [1, 6], [2, 7], [3, 4]], np.int32), cuda)
+        probs = dev_tensor(np.full((T, K), 0.5, np.float32), cuda)
+        out = torch.full((T, H), 7.0, device=cuda)
+        # rank 0 alone: rank 1 never dispatches nor combines
+        moe.ep_dispatch(R.slabs, 0, N, T, H, E, K, x, ids, probs)
+        moe.ep_experts(R.wcall, R.w[0][0], R.w[0][1], None, R.slabs, 0, N, T, H, I, E, K, R.ws[0])
+        moe.ep_combine(R.slabs, 0, N, T, H, E, K, ids, probs, out, R.ws[0])
+        st, _ = moe.device_status(R.ws[0])
+        assert st == -6  # MRML_ERR_DEVICE_TIMEOUT
+        assert torch.all(out == 7.0)
+        assert moe.device_status(R.ws[0])[0] == 0  # reading clears it
+    finally:
+        moe.set_exchange_spin_limit(0)
+        R.close()
