@@ -82,7 +82,12 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units,
                             int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s,
                             const float* logits = nullptr, int K = 0, int32_t* ids_out = nullptr,
-                            float* probs_out = nullptr);
+                            float* probs_out = nullptr, int32_t* chunk_cnt = nullptr);
+// Above this many pairs (and with chunk_cnt, dispatch_chunk_ints(n_pairs, E)
+// ints of scratch) the dispatch runs as three launches over chunks of 1024
+// pairs instead of one CTA; same result.
+constexpr int kDispatchChunkedMin = 8192;
+inline size_t dispatch_chunk_ints(long long n_pairs, int E) { return (size_t)((n_pairs + 1023) / 1024) * E; }
 // Whether launch_dispatch can select the experts itself (from `logits`) for
 // T tokens: the top-k of up to 256 experts, one warp per token.
 bool dispatch_topk_supported(int E, int K, int T);

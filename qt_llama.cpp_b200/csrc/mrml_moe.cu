@@ -86,6 +86,7 @@ struct Workspace {
   int2* xs;          // its scales: [H/32][npad] int2, or group-major records (decode kernel)
   int8_t* ab;        // [I/32][npad/8][256]  B operand of down (re-quantised act)
   int2* as;          // its scales, laid out as xs
+  int32_t* chunk_cnt;  // [T*K/1024][E] per-chunk expert counts of the large-batch dispatch
   float* act;        // [npad][I]     geglu output per position (CUDA-core path)
   float* ydown;      // [npad][H]     down output per position (unscaled)
   int npad, max_units_gu, max_units_dn;
@@ -123,6 +124,7 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
   w.xs = reinterpret_cast<int2*>(take(nb * npad * rec_pos));
   w.ab = reinterpret_cast<int8_t*>(take(nbi * npad * 32));
   w.as = reinterpret_cast<int2*>(take(nbi * npad * rec_pos));
+  w.chunk_cnt = reinterpret_cast<int32_t*>(take(mrml::dispatch_chunk_ints(tk, E) * 4));
   w.act = reinterpret_cast<float*>(take((size_t)npad * I * 4));
   w.ydown = reinterpret_cast<float*>(take((size_t)npad * H * 4));
   w.bytes = off;
@@ -269,7 +271,7 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
   if (gather) MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
   MRML_LAUNCH(mrml::launch_dispatch(ids, probs, T * K, E, e_first, e_total, w.cnt, w.poff, w.pair_at, w.pos, w.units_gu, w.units_dn,
                                     n_units, NT, NT_dn, mt_gu, rows_gu, mt_dn, w.status, s, topk_logits, K, ids_out,
-                                    probs_out));
+                                    probs_out, w.chunk_cnt));
   if (route == kRouteGeneral) {
     MRML_LAUNCH(mrml::launch_quantize_rows(x, w.xq, w.xd, w.xsum, (long long)T * (H / 32), s));
     MRML_LAUNCH(mrml::launch_gate_up(wtype, gate_up, w.cnt, w.poff, w.pair_at, w.xq, w.xd, w.xsum, w.act, H, I, E, K,
@@ -360,7 +362,7 @@ int run_ep_experts(void* ws, int wtype, const uint8_t* gate_up, const uint8_t* d
   MRML_LAUNCH(mrml::launch_ep_recv(slabs, rank, N, T, H, K, x.ids_all, x.probs_all, x.rows, w.status, s));
   MRML_LAUNCH(mrml::launch_dispatch(x.ids_all, x.probs_all, NT * K, Ec, rank * Ec, E, w.cnt, w.poff, w.pair_at,
                                     w.pos, w.units_gu, w.units_dn, n_units, NT_gu, NT_dn, mt_gu, rows_gu, mt_dn,
-                                    w.status, s));
+                                    w.status, s, nullptr, 0, nullptr, nullptr, w.chunk_cnt));
   MRML_LAUNCH(mrml::launch_ep_gather(wtype, x.rows, w.pair_at, w.poff + Ec, H, K, w.npad, w.xb, w.xs, s));
   const int mu_gu = units_bound(Ec, K, NT, NT_gu, I, rows_gu), mu_dn = units_bound(Ec, K, NT, NT_dn, H, 128);
   const bool mma = route == kRouteGemvMma;
