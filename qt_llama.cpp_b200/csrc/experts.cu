@@ -355,6 +355,8 @@ __global__ void __launch_bounds__(kDispatchThreads)
   for (int i = threadIdx.x; i < E; i += blockDim.x) chunk_cnt[(size_t)blockIdx.x * E + i] = ccnt[i];
 }
 
+constexpr int kLayoutTile = 32;  // chunks per shared-memory tile of the layout step
+
 __global__ void __launch_bounds__(kDispatchThreads)
     dispatch_layout_kernel(int32_t* __restrict__ chunk_cnt, int nchunks, int E, int32_t* __restrict__ cnt_out,
                            int32_t* __restrict__ poff, int32_t* __restrict__ pair_at, int4* __restrict__ units_gu,
@@ -365,21 +367,34 @@ __global__ void __launch_bounds__(kDispatchThreads)
   int32_t* base = lsm + E;           // [E] segment start
   int32_t* ubase = lsm + 2 * E;      // [E] first gate/up unit (times mt)
   int32_t* ubase_dn = lsm + 3 * E;   // [E] first down unit (times mt)
+  int32_t* tile = lsm + 4 * E;       // [kLayoutTile][E] chunk counts being scanned
   __shared__ int s_npos;
   __shared__ int wsum_pos[32], wsum_units[32], wsum_dn[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();
   pdl_trigger();
   // Per expert: each chunk's offset within the expert's pairs (exclusive
-  // prefix over chunks, in place) and the expert's total.
-  for (int e = tid; e < E; e += blockDim.x) {
-    int run = 0;
-    for (int c = 0; c < nchunks; ++c) {
-      const int v = chunk_cnt[(size_t)c * E + e];
-      chunk_cnt[(size_t)c * E + e] = run;
-      run += v;
+  // prefix over chunks, written back in place) and the expert's total.  The
+  // counts move through shared memory kLayoutTile chunks at a time with
+  // coalesced loads and stores, so that no thread walks global memory in a
+  // dependent chain.
+  for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+  for (int c0 = 0; c0 < nchunks; c0 += kLayoutTile) {
+    const int nc = min(kLayoutTile, nchunks - c0);
+    __syncthreads();
+    for (int i = tid; i < nc * E; i += blockDim.x) tile[i] = chunk_cnt[(size_t)c0 * E + i];
+    __syncthreads();
+    for (int e = tid; e < E; e += blockDim.x) {
+      int run = cnt[e];
+      for (int c = 0; c < nc; ++c) {
+        const int v = tile[c * E + e];
+        tile[c * E + e] = run;
+        run += v;
+      }
+      cnt[e] = run;
     }
-    cnt[e] = run;
+    __syncthreads();
+    for (int i = tid; i < nc * E; i += blockDim.x) chunk_cnt[(size_t)c0 * E + i] = tile[i];
   }
   __syncthreads();
   {
@@ -984,7 +999,11 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
     cudaError_t st = launch_pdl(dispatch_count_kernel, dim3(nchunks), dim3(kDispatchThreads), (size_t)E * 4, s, ids,
                                 probs, n_pairs, E, e_first, e_total, chunk_cnt, err);
     if (st != cudaSuccess) return st;
-    st = launch_pdl(dispatch_layout_kernel, dim3(1), dim3(kDispatchThreads), (size_t)4 * E * 4, s, chunk_cnt,
+    const size_t lsmem = (size_t)(4 + kLayoutTile) * E * 4;
+    static SmemOptIn layout_cache;
+    st = ensure_smem(dispatch_layout_kernel, lsmem, layout_cache);
+    if (st != cudaSuccess) return st;
+    st = launch_pdl(dispatch_layout_kernel, dim3(1), dim3(kDispatchThreads), lsmem, s, chunk_cnt,
                     nchunks, E, cnt, poff, pair_at, units_gu, units_dn, n_units, NT_gu, NT_dn, mt_gu, rows_gu, mt_dn);
     if (st != cudaSuccess) return st;
     return launch_pdl(dispatch_scatter_kernel, dim3(nchunks), dim3(kDispatchThreads), (size_t)32 * E * 4, s, ids,

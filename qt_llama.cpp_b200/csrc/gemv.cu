@@ -595,11 +595,12 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
       // Q4_0 down units of at most 4 tokens run the half-chain form.  (For
       // gate/up it measured slower: a second unrolled chunk body in a kernel
       // held to 64 registers; for Q8_0 its registers spill.)
-      // Units of at most 4 positions run the half-chain form: down with Q4_0
-      // weights, and every product on packed weights.  (For gate/up on GGUF
-      // rows it measured slower: a second unrolled chunk body in a kernel held
-      // to 64 registers; for Q8_0 down rows its registers spill.)
-      const bool half = (MODE == kDown ? (WQ4 || PK) : PK) && NG == 1 && nj <= 4;  // warp-uniform
+      // Down units of at most 4 positions run the half-chain form (Q4_0 rows
+      // and packed weights).  For gate/up it measured slower (a second
+      // unrolled chunk body; on GGUF rows held to 64 registers, on packed
+      // weights 84.6 against 68.1 us at config 2, T = 64); for Q8_0 GGUF down
+      // rows its registers spill.
+      const bool half = MODE == kDown && (WQ4 || PK) && NG == 1 && nj <= 4;  // warp-uniform
       float(&acch)[4] = *reinterpret_cast<float(*)[4]>(&acc[0]);  // the half layout's sums
       for (int kc = 0; kc < nkc && ok; ++kc) {
         if (!(ok = wait_bar(&B->raw_full[rs], rph, B, P.err))) break;
@@ -611,17 +612,10 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
         if constexpr (PK && MODE == kGateUp) {
           // warp cw: part cw / 2, tiles 2 (cw & 1) and 2 (cw & 1) + 1
           const uint8_t* t0 = src + (size_t)((cw >> 1) * 4 + 2 * (cw & 1)) * kKC * RB;
-          if (NG == 1 && half) {
 #pragma unroll
-            for (int bl = 0; bl < kKC; ++bl)
-              mma_block_rows2_half<WQ4>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, sc + bl * SB, one, g,
-                                        t, acch);
-          } else {
-#pragma unroll
-            for (int bl = 0; bl < kKC; ++bl)
-              mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, gs, sc + bl * SB, ss,
-                                       one, g, t, acc);
-          }
+          for (int bl = 0; bl < kKC; ++bl)
+            mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, gs, sc + bl * SB, ss, one,
+                                     g, t, acc);
         } else if constexpr (PK) {
           const uint8_t* t0 = src + (size_t)(2 * cw) * P.nb * RB;
           if (NG == 1 && half) {
