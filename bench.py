@@ -473,18 +473,19 @@ class StackSet:
 
     N_LAYERS = 30
 
-    def __init__(self, moe, synth, device, n_inputs, rank, world, exchange="p2p", seed=0):
+    def __init__(self, moe, synth, device, n_inputs, rank, world, exchange="p2p", seed=0, packed=False):
         import torch
 
         ep = _load("mrml_moe_b200_ep", os.path.join(ROOT, "qt_llama.cpp_b200", "ep.py"))
         wtype, H, I, E, K = 2, 2816, 704, 128, 8
+        self.wcall = wtype | (moe.MRML_PACKED if packed else 0)
         T = 32 // world
         self.moe, self.device, self.name = moe, device, "c5"
         self.wtype, self.H, self.I, self.E, self.K, self.T, self.routing = wtype, H, I, E, K, T, "router"
         self.world = world
         self.n_layers = 1  # graphs per input: one graph holds the whole stack
         if world > 1:
-            self.ep = ep.ExpertParallelLayer(moe, rank, world, wtype, H, I, E, K, T, device, exchange=exchange)
+            self.ep = ep.ExpertParallelLayer(moe, rank, world, self.wcall, H, I, E, K, T, device, exchange=exchange)
             first, count = self.ep.first, self.ep.count
         else:
             self.ep = None
@@ -499,6 +500,9 @@ class StackSet:
             if world > 1:
                 gu, dn = gu[first:first + count].clone(), dn[first:first + count].clone()
                 torch.cuda.empty_cache()
+            if packed:
+                gu, dn = moe.prepare_weights(wtype, gu, dn)
+                torch.cuda.synchronize()
             g = torch.Generator(device=device)
             g.manual_seed(seed * 1000 + 900 + l)
             W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
@@ -520,7 +524,7 @@ class StackSet:
             if self.ep is not None:
                 self.ep.forward(W, h, gu, dn, self.moe_out)
             else:
-                m.forward(self.wtype, W, h, h, gu, dn, None, self.logits, self.ids, self.probs, self.moe_out, H,
+                m.forward(self.wcall, W, h, h, gu, dn, None, self.logits, self.ids, self.probs, self.moe_out, H,
                           self.I, self.E, self.K, T, self.ws)
             nxt = out if l == len(self.layers) - 1 else self.h[l & 1]
             m.rms_norm(self.moe_out, None, nxt, H, T, 1e-6)
@@ -541,7 +545,7 @@ def run_stack(args):
     device = torch.device("cuda", local)
     moe.load_library()
     hbm_peak, peak_kind = peaks()
-    ss = StackSet(moe, synth, device, 4, rank, world, exchange=args.ep_exchange)
+    ss = StackSet(moe, synth, device, 4, rank, world, exchange=args.ep_exchange, packed=args.weights == "packed")
     graphs = [ss.capture(g) for g in range(2)]
     reps = repeats_for(ss, args.steps, args.warmup, world, graphs, target_s=1.0, cap=20)
     with ClockSampler(local) as clk:
@@ -892,9 +896,13 @@ def run_ours(args):
         line["cpu_baseline"] = cpu_baseline(oracle, ls)
     if not args.no_also:
         also = {}
-        names = (("c2_t1", "c2_t8", "c3_prefill") if world == 1 else ()) + ("c4", "c4_q8")
-        for name in names:
-            if name == args.workload:
+        # (workload, weights packed?): the GGUF-layout headline shape is kept
+        # for comparison with the drop-in default layout
+        names = ((("c2_t1", packed), ("c2_t8", packed), ("c3_prefill", packed), ("c2_t64", not packed))
+                 if world == 1 else ()) + (("c4", packed), ("c4_q8", packed))
+        for name, pk in names:
+            key = name if pk == packed else name + ("_packed" if pk else "_gguf")
+            if name == args.workload and pk == packed:
                 continue
             if world > 1:
                 ls.close()
@@ -902,9 +910,9 @@ def run_ours(args):
             gc.collect()
             torch.cuda.empty_cache()
             if world > 1:
-                ls = EPLayerSet(moe, synth, device, name, 8, rank, world, exchange=args.ep_exchange, packed=packed)
+                ls = EPLayerSet(moe, synth, device, name, 8, rank, world, exchange=args.ep_exchange, packed=pk)
             else:
-                ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank, packed=packed)
+                ls = LayerSet(moe, synth, device, name, n_inputs=8, seed=rank, packed=pk)
             u, p = ls.unique_experts(0)
             n = max(steps, 20)
             gr = [ls.capture(g) for g in range(2 * ls.n_layers)]
@@ -916,7 +924,7 @@ def run_ours(args):
             rec = {"tokens_per_s": round(world * ls.T * n / (m / 1e3), 1), "ms_per_step": round(m / n, 5),
                    "tokens_per_step": world * ls.T,
                    "scaling": "strong" if name in STRONG else "weak",
-                   "weights": "Q4_0" if ls.wtype == 2 else "Q8_0",
+                   "weights": ("Q4_0" if ls.wtype == 2 else "Q8_0") + (" packed" if pk else " GGUF layout"),
                    "layer_hbm_frac": round(lb / (m / n / 1e3) / 1e9 / hbm_peak, 4),
                    "gate_up_hbm_frac": round(gb_max, 4),
                    "kernel_ms_per_step": {kk: round(v / n, 5) for kk, v in k.items()},
@@ -929,7 +937,7 @@ def run_ours(args):
                 par = parity_check(ls, world, rank)
                 if rank == 0:
                     rec["parity"] = par
-            also[name] = rec
+            also[key] = rec
         line["also"] = also
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -1049,7 +1057,7 @@ def main():
     ap.add_argument("--workload", default="c2_t64", choices=sorted(WORKLOADS) + ["c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-also", action="store_true")
-    ap.add_argument("--weights", default="gguf", choices=["gguf", "packed"],
+    ap.add_argument("--weights", default="packed", choices=["gguf", "packed"],
                     help="expert weights as the GGUF slabs (the reference's layout) or repacked at load time by "
                          "mrml_moe_prepare_weights")
     ap.add_argument("--repeats", type=int, default=0,

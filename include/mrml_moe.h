@@ -57,6 +57,7 @@ typedef enum {
   MRML_ERR_DEVICE = -5,            /* the device is not an sm_100 GPU */
   MRML_ERR_DEVICE_TIMEOUT = -6,    /* reported by mrml_moe_device_status */
   MRML_ERR_BAD_EXPERT_ID = -7,     /* reported by mrml_moe_device_status */
+  MRML_ERR_NOT_FOUND = -8,         /* a GGUF tensor or metadata key that the file does not have */
 } mrml_status;
 
 /* GGML type ids (crates/mrml-tensor/src/types.rs:7-27).  MRML_PACKED or'ed
@@ -236,6 +237,30 @@ size_t mrml_moe_weights_bytes(int wtype, int H, int I, int E, int which);
  * 64 (MRML_ERR_UNSUPPORTED otherwise).  Enqueued on `stream`; capturable. */
 int mrml_moe_prepare_weights(int wtype, const uint8_t *gate_up, const uint8_t *down, uint8_t *gate_up_packed,
                              uint8_t *down_packed, int H, int I, int E, mrml_stream_t stream);
+
+/* GGUF v2/v3 tensor table (host code), for loading the MoE layers' expert
+ * slabs as the reference's loader does: gguf.rs:80-181 parses the header,
+ * metadata and tensor infos (the data section starts at the next multiple of
+ * general.alignment, default 32), and model.rs:638-647 takes a tensor at
+ * data_offset + offset, e.g. "blk.{l}.ffn_gate_up_exps.weight" and
+ * "blk.{l}.ffn_down_exps.weight", whose bytes model.rs:726-741 uploads
+ * unchanged.  mrml_moe_gguf_open reads the header of the file at `path`
+ * (MRML_ERR_UNSUPPORTED for another version or a tensor type the reference
+ * does not read); mrml_moe_gguf_tensor gives a tensor's GGML type, dimensions
+ * (up to 4, innermost first), absolute file offset and size in bytes
+ * (elements / block elements * block bytes); mrml_moe_gguf_meta_u32 an
+ * integer metadata value; mrml_moe_gguf_read copies a tensor's bytes into a
+ * host buffer.  Missing names return MRML_ERR_NOT_FOUND.  The handle is
+ * read-only after opening and may be shared between threads. */
+int mrml_moe_gguf_open(const char *path, void **file);
+int mrml_moe_gguf_close(void *file);
+int mrml_moe_gguf_version(const void *file);
+int mrml_moe_gguf_tensor_count(const void *file);
+const char *mrml_moe_gguf_tensor_name(const void *file, int i);
+int mrml_moe_gguf_tensor(const void *file, const char *name, int *ggml_type, int *n_dims, int64_t *dims,
+                         uint64_t *file_offset, uint64_t *nbytes);
+int mrml_moe_gguf_meta_u32(const void *file, const char *key, uint32_t *value);
+int mrml_moe_gguf_read(const void *file, const char *name, void *dst, size_t dst_bytes);
 
 /* The weighted combine alone (model.rs:2163-2165): out[t][i] = sum over
  * k ascending of (probs[t,k] * ydown[pos[t,k]][i]) * down_scale[ids[t,k]],

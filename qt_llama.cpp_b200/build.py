@@ -13,7 +13,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libmrml_moe_b200.so")
-SOURCES = ["mrml_moe.cu", "router.cu", "experts.cu", "gemm_tc.cu", "gemv.cu", "router_static.cu", "ep_p2p.cu", "prepare.cu"]
+SOURCES = ["mrml_moe.cu", "router.cu", "experts.cu", "gemm_tc.cu", "gemv.cu", "router_static.cu", "ep_p2p.cu", "prepare.cu", "gguf.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -391,6 +391,7 @@ const char* mrml_moe_status_string(int status) {
     case MRML_ERR_DEVICE: return "device is not an sm_100 GPU";
     case MRML_ERR_DEVICE_TIMEOUT: return "a device-side wait timed out";
     case MRML_ERR_BAD_EXPERT_ID: return "expert id out of range";
+    case MRML_ERR_NOT_FOUND: return "not found";
     default: return "unknown status";
   }
 }

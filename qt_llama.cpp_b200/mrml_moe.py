@@ -74,6 +74,15 @@ SIGNATURES = {
     "mrml_moe_set_option": (_i, [_i, _i]),
     "mrml_moe_weights_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "mrml_moe_prepare_weights": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "mrml_moe_gguf_open": (_i, [_c.c_char_p, _c.POINTER(_vp)]),
+    "mrml_moe_gguf_close": (_i, [_vp]),
+    "mrml_moe_gguf_version": (_i, [_vp]),
+    "mrml_moe_gguf_tensor_count": (_i, [_vp]),
+    "mrml_moe_gguf_tensor_name": (_c.c_char_p, [_vp, _i]),
+    "mrml_moe_gguf_tensor": (_i, [_vp, _c.c_char_p, _c.POINTER(_i), _c.POINTER(_i), _c.POINTER(_c.c_int64),
+                                  _c.POINTER(_c.c_uint64), _c.POINTER(_c.c_uint64)]),
+    "mrml_moe_gguf_meta_u32": (_i, [_vp, _c.c_char_p, _c.POINTER(_c.c_uint32)]),
+    "mrml_moe_gguf_read": (_i, [_vp, _c.c_char_p, _vp, _sz]),
 }
 
 
@@ -329,6 +338,114 @@ def device_status(ws, stream=None):
     rec = ctypes.c_int(0)
     st = lib.mrml_moe_device_status(_ptr(ws), _stream_ptr(stream), ctypes.byref(rec))
     return st, rec.value
+
+
+class GgufFile:
+    """A GGUF file's tensor table through mrml_moe_gguf_* (the reference's
+    reader, crates/mrml-tensor/src/gguf.rs:80-181).  Host only."""
+
+    def __init__(self, path: str):
+        lib = load_library()
+        h = ctypes.c_void_p()
+        _check("mrml_moe_gguf_open", lib.mrml_moe_gguf_open(os.fsencode(path), ctypes.byref(h)))
+        self._h = h
+        self.version = lib.mrml_moe_gguf_version(h)
+
+    def close(self):
+        if self._h:
+            load_library().mrml_moe_gguf_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def names(self):
+        lib = load_library()
+        return [lib.mrml_moe_gguf_tensor_name(self._h, i).decode() for i in range(lib.mrml_moe_gguf_tensor_count(self._h))]
+
+    def tensor(self, name: str):
+        """{type, dims (innermost first), offset (absolute), nbytes} or None."""
+        t, nd = ctypes.c_int(), ctypes.c_int()
+        dims = (ctypes.c_int64 * 4)()
+        off, nb = ctypes.c_uint64(), ctypes.c_uint64()
+        st = load_library().mrml_moe_gguf_tensor(self._h, name.encode(), ctypes.byref(t), ctypes.byref(nd), dims,
+                                                 ctypes.byref(off), ctypes.byref(nb))
+        if st == -8:
+            return None
+        _check("mrml_moe_gguf_tensor", st)
+        return {"type": t.value, "dims": tuple(dims[:nd.value]), "offset": off.value, "nbytes": nb.value}
+
+    def meta_u32(self, key: str):
+        v = ctypes.c_uint32()
+        st = load_library().mrml_moe_gguf_meta_u32(self._h, key.encode(), ctypes.byref(v))
+        if st == -8:
+            return None
+        _check("mrml_moe_gguf_meta_u32", st)
+        return v.value
+
+    def read(self, name: str):
+        """The tensor's bytes (numpy uint8)."""
+        import numpy as np
+
+        info = self.tensor(name)
+        if info is None:
+            raise MoeError("mrml_moe_gguf_read", -8, f"no tensor {name}")
+        buf = np.empty(info["nbytes"], np.uint8)
+        _check("mrml_moe_gguf_read", load_library().mrml_moe_gguf_read(self._h, name.encode(),
+                                                                        buf.ctypes.data_as(ctypes.c_void_p),
+                                                                        buf.size))
+        return buf
+
+
+def load_moe_layer(gguf, layer: int, device, packed: bool = False, stream=None) -> dict:
+    """One MoE layer's tensors as the reference's loader takes them
+    (model.rs:630-755): the router `blk.{l}.ffn_gate_inp.weight` [E][H] f32,
+    its optional `.scale` [H], the expert slabs `blk.{l}.ffn_gate_up_exps.weight`
+    ([E][2I][H/32] blocks) and `ffn_down_exps.weight` ([E][H][I/32] blocks),
+    uploaded unchanged, and the optional `ffn_down_exps.scale` [E].  With
+    packed=True the slabs are repacked on the device (mrml_moe_prepare_weights)
+    and `wtype` carries MRML_PACKED.  `gguf` is a path or an open GgufFile."""
+    import numpy as np
+    import torch
+
+    own = isinstance(gguf, (str, bytes, os.PathLike))
+    g = GgufFile(gguf) if own else gguf
+    try:
+        pre = f"blk.{layer}."
+        gu_i, dn_i = g.tensor(pre + "ffn_gate_up_exps.weight"), g.tensor(pre + "ffn_down_exps.weight")
+        if gu_i is None or dn_i is None:
+            raise MoeError("load_moe_layer", -8, f"layer {layer} has no expert slabs")
+        wtype = gu_i["type"]
+        if wtype not in (MRML_Q4_0, MRML_Q8_0) or dn_i["type"] != wtype:
+            raise MoeError("load_moe_layer", -2, f"expert weight type {wtype}")
+        H, two_i, E = gu_i["dims"][:3]
+        I = two_i // 2
+        if tuple(dn_i["dims"][:3]) != (I, H, E):
+            raise MoeError("load_moe_layer", -1, "gate_up and down slabs disagree")
+        bb = 18 if wtype == MRML_Q4_0 else 34
+
+        def dev(a, shape=None, dtype=None):
+            t = torch.from_numpy(a if dtype is None else a.view(dtype))
+            return (t if shape is None else t.reshape(shape)).to(device)
+
+        out = {"wtype": wtype, "H": H, "I": I, "E": E,
+               "gate_up": dev(g.read(pre + "ffn_gate_up_exps.weight"), (E, 2 * I, H // 32 * bb)),
+               "down": dev(g.read(pre + "ffn_down_exps.weight"), (E, H, I // 32 * bb))}
+        for key, name, shape in (("router_w", "ffn_gate_inp.weight", (E, H)), ("gate_inp_scale", "ffn_gate_inp.scale",
+                                                                               (H,)),
+                                 ("down_scale", "ffn_down_exps.scale", (E,))):
+            info = g.tensor(pre + name)
+            out[key] = None if info is None or info["type"] != 0 else dev(g.read(pre + name), shape, np.float32)
+        if packed:
+            out["gate_up"], out["down"] = prepare_weights(wtype, out["gate_up"], out["down"], stream)
+            out["wtype"] = wtype | MRML_PACKED
+        return out
+    finally:
+        if own:
+            g.close()
 
 
 class MoeDevice:
