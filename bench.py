@@ -869,7 +869,7 @@ def run_ours(args):
                    "unique_experts_step0": unique},
         "roofline": {"bound": "hbm", "kernel": "gate_up", "achieved": round(gate_up_bytes / (gu_ms / 1e3) / 1e9, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(gate_up_bytes / (gu_ms / 1e3) / 1e9 / hbm_peak, 4),
-                     "traffic": traffic_from_profile(args.workload) if world == 1 else None,
+                     "traffic": traffic_from_profile(f"{args.workload}/{args.weights}") if world == 1 else None,
                      "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": gate_up_bytes, "ms_per_launch": round(gu_ms, 5)},
         "layer_roofline": {"achieved": round(layer_bytes / (ms / steps / 1e3) / 1e9, 1), "peak": hbm_peak,
@@ -952,8 +952,8 @@ def run_ours(args):
 
 def traffic_from_profile(workload, kernel="gate_up"):
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
-    summaries under profiles/ (a line "traffic: <workload> <kernel> <bytes>"),
-    or None."""
+    summaries under profiles/ (a line "traffic: <workload>/<weights layout>
+    <kernel> <bytes>"), or None."""
     d = os.path.join(ROOT, "profiles")
     try:
         for name in sorted(os.listdir(d)):

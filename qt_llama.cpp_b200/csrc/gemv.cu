@@ -39,6 +39,15 @@ using tc::wait_bar;
 #endif
 constexpr int kGateUpCtas = MRML_GV_GATE_UP_CTAS;
 
+// CTAs per SM of each form (its launch bound): the MMA gate/up product with
+// one position group per unit kGateUpCtas; 16-position units 3 (their
+// accumulators need the registers: at 4 CTAs the Q4_0 forms spilled, and the
+// packed Q4_0 gate/up at config 4 took 3.67 ms against 3.33 on GGUF rows);
+// the others 4.
+__host__ __device__ constexpr int ctas_per_sm(bool mma, int mode, int ng) {
+  return (mma && mode == kGateUp && ng == 1) ? kGateUpCtas : (ng == 2 ? 3 : 4);
+}
+
 constexpr int kComp0 = 2;      // first compute warp
 constexpr int kCompWarps = 4;  // 128 threads, one weight row each
 
@@ -454,7 +463,7 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const ui
 // kKC][record], down [E][128-row group][tile 8][block][record].
 template <int WQ4, int MODE, int MMA, int NG, int PK>
 __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
-                                  (MMA && MODE == kGateUp && NG == 1) ? kGateUpCtas : ((NG == 2 && !WQ4) ? 3 : 4))
+                                  ctas_per_sm(MMA, MODE, NG))
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   static_assert(NG == 1 || (NG == 2 && MMA), "two position groups per unit on the MMA form only");
   constexpr int BB = WQ4 ? 18 : 34;
@@ -944,10 +953,9 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   const int bs_stage = p.kcb * ng * (256 + kActScaleBytes);
   const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * ng * kGvRowsGateUp * 4 : 0;
   // With many units, as many CTAs per SM as fit with a double-buffered weight
-  // ring (the kernel's launch bound: 5 for the MMA gate/up product with one
-  // position group per unit, 3 for Q8_0 weights with two, 4 for the others);
+  // ring (the kernel's launch bound, ctas_per_sm);
   // with few units, one CTA and the deepest ring that fits.
-  const int bound = (mma && mode == tc::kGateUp && ng == 1) ? gv::kGateUpCtas : ((ng == 2 && wtype != kQ4_0) ? 3 : 4);
+  const int bound = gv::ctas_per_sm(mma, mode, ng);
   const int per_sm_set = g_gv_per_sm.load(), ring_set = g_gv_ring.load();
   const int per_sm_max = per_sm_set > 0 ? per_sm_set : (many_units ? bound : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
