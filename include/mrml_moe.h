@@ -270,6 +270,46 @@ int mrml_moe_gguf_read(const void *file, const char *name, void *dst, size_t dst
 int mrml_moe_combine(const float *ydown, const int32_t *pos, const int32_t *ids, const float *probs,
                      const float *down_scale, float *out, int H, int K, int T, mrml_stream_t stream);
 
+/* The FFN prologue of a Gemma-4 MoE layer, fused (model.rs:1743-1784; the
+ * reference's GPU form is rust_cuda_prepare_ffn_f32, cuda_ptx/kernels.rs:
+ * 987-1033).  From the residual h[T][H], with one sum of squares per row
+ * (s = 1 / sqrt(mean(h^2) + eps), ops.rs:24-49's order and rounding):
+ *   x_shared = (h * s) * ffn_norm            the shared dense MLP's input
+ *   x_moe    = (h * s) * pre_ffw_norm_2      the experts' input
+ *   router_x = ((h * s) * (1 / sqrt(H))) * gate_inp_scale   the router's input
+ * Bit-identical to the reference's three rms_norm calls and scaling.  Any
+ * output may be NULL (not written); a NULL weight means 1.  h 16-byte
+ * aligned; H <= 51200. */
+int mrml_moe_ffn_prologue(const float *h, const float *ffn_norm, const float *pre_ffw_norm_2,
+                          const float *gate_inp_scale, float *x_shared, float *x_moe, float *router_x, int H, int T,
+                          float eps, mrml_stream_t stream);
+
+/* The FFN epilogue, fused (model.rs:2176-2196; rust_cuda_finish_ffn_f32,
+ * cuda_ptx/kernels.rs:1036-1083):
+ *   hidden = (attn_res + rms_norm(rms_norm(mlp_raw, post_ffw_norm_1)
+ *                                 + rms_norm(moe_raw, post_ffw_norm_2), post_ffw_norm))
+ *            * layer_output_scale
+ * with the reference's roundings.  mlp_raw may be NULL (a layer without the
+ * shared MLP: zeros); a NULL weight means 1.  hidden may alias attn_res.
+ * H <= 25600. */
+int mrml_moe_ffn_epilogue(const float *attn_res, const float *mlp_raw, const float *moe_raw,
+                          const float *post_ffw_norm_1, const float *post_ffw_norm_2, const float *post_ffw_norm,
+                          float layer_output_scale, float *hidden, int H, int T, float eps, mrml_stream_t stream);
+
+/* The layer's shared dense GeGLU MLP (model.rs:2093-2109 on the CPU;
+ * gemv_q4_0_geglu + gemv_q4_0 on the reference's GPU, model.rs:1889-1890):
+ * out[T][H] = down(geglu(gate x, up x)) with x and act quantised to Q8_0 as
+ * the reference does, bit-identical to it.  It is the expert arithmetic of
+ * mrml_moe_experts for one expert with weight 1, so gate_up holds the
+ * ffn_gate rows then the ffn_up rows ([2I][H/32] blocks) and down [H][I/32]
+ * blocks; packed weights (mrml_moe_prepare_weights with E = 1) are taken
+ * too.  Run it on a second stream to overlap it with the MoE experts, as the
+ * reference's captured layer does.  Workspace:
+ * mrml_moe_dense_ffn_workspace_bytes. */
+size_t mrml_moe_dense_ffn_workspace_bytes(int H, int I, int T);
+int mrml_moe_dense_ffn(int wtype, const uint8_t *gate_up, const uint8_t *down, const float *x, float *out, int H,
+                       int I, int T, void *workspace, size_t workspace_bytes, mrml_stream_t stream);
+
 /* RMS normalisation of `batch` rows of `dim` floats: out = x / sqrt(mean(x^2)
  * + eps) * weight (weight may be NULL), with the reference's rounding: the
  * sum of squares in index order, then 1 / sqrt(sum / dim + eps) (ops.rs:24-49;

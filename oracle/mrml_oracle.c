@@ -315,6 +315,52 @@ void oracle_rms_norm(const float *x, const float *weight, float eps, float *out,
   for (int i = 0; i < n; i++) out[i] = weight ? x[i] * scale * weight[i] : x[i] * scale;
 }
 
+/* ------------------------------------------------------ FFN prologue --- */
+
+void oracle_ffn_prologue(const float *h, const float *ffn_norm, const float *pre_ffw_norm_2,
+                         const float *gate_inp_scale, float *x_shared, float *x_moe, float *router_x, int H, int T,
+                         float eps) {
+  float *tmp = (float *)malloc(sizeof(float) * (size_t)H);
+  float inv_sqrt_dim = 1.0f / sqrtf((float)H); /* model.rs:1776 */
+  for (int t = 0; t < T; t++) {
+    const float *row = h + (size_t)t * H;
+    size_t o = (size_t)t * H;
+    if (x_shared) oracle_rms_norm(row, ffn_norm, eps, x_shared + o, H); /* model.rs:1751-1753 */
+    if (x_moe) oracle_rms_norm(row, pre_ffw_norm_2, eps, x_moe + o, H); /* model.rs:1760-1767 */
+    if (router_x) {                                                       /* model.rs:1774-1784 */
+      oracle_rms_norm(row, NULL, eps, tmp, H);
+      for (int i = 0; i < H; i++) {
+        float scale = gate_inp_scale ? gate_inp_scale[i] : 1.0f;
+        router_x[o + i] = tmp[i] * inv_sqrt_dim * scale;
+      }
+    }
+  }
+  free(tmp);
+}
+
+void oracle_ffn_epilogue(const float *attn_res, const float *mlp_raw, const float *moe_raw,
+                         const float *post_ffw_norm_1, const float *post_ffw_norm_2, const float *post_ffw_norm,
+                         float out_scale, float *hidden, int H, int T, float eps) {
+  float *zeros = (float *)calloc((size_t)H, sizeof(float));
+  float *mlp_out = (float *)malloc(sizeof(float) * (size_t)H);
+  float *moe_out = (float *)malloc(sizeof(float) * (size_t)H);
+  float *comb = (float *)malloc(sizeof(float) * (size_t)H);
+  float *normed = (float *)malloc(sizeof(float) * (size_t)H);
+  for (int t = 0; t < T; t++) {
+    size_t o = (size_t)t * H;
+    oracle_rms_norm(mlp_raw ? mlp_raw + o : zeros, post_ffw_norm_1, eps, mlp_out, H); /* model.rs:2176-2177 */
+    oracle_rms_norm(moe_raw + o, post_ffw_norm_2, eps, moe_out, H);                  /* model.rs:2179-2180 */
+    for (int i = 0; i < H; i++) comb[i] = mlp_out[i] + moe_out[i];                   /* model.rs:2182-2185 */
+    oracle_rms_norm(comb, post_ffw_norm, eps, normed, H);                           /* model.rs:2187-2193 */
+    for (int i = 0; i < H; i++) hidden[o + i] = (attn_res[o + i] + normed[i]) * out_scale; /* model.rs:2194-2196 */
+  }
+  free(zeros);
+  free(mlp_out);
+  free(moe_out);
+  free(comb);
+  free(normed);
+}
+
 /* ----------------------------------------------------------- router --- */
 
 typedef struct {

@@ -66,6 +66,22 @@ void oracle_geglu(const float *gate, const float *up, float *out, int n);
 void oracle_rms_norm(const float *x, const float *weight, float eps, float *out,
                      int n);
 
+/* FFN prologue of a MoE layer, model.rs:1743-1784 for T rows of H:
+ * x_shared = rms_norm(h, ffn_norm), x_moe = rms_norm(h, pre_ffw_norm_2),
+ * router_x[i] = rms_norm(h, none)[i] * (1 / sqrtf(H)) * gate_inp_scale[i].
+ * A NULL output is skipped; a NULL weight means 1. */
+void oracle_ffn_prologue(const float *h, const float *ffn_norm, const float *pre_ffw_norm_2,
+                         const float *gate_inp_scale, float *x_shared, float *x_moe, float *router_x, int H, int T,
+                         float eps);
+
+/* FFN epilogue, model.rs:2176-2196 for T rows of H:
+ * hidden = (attn_res + rms_norm(rms_norm(mlp_raw, post_ffw_norm_1)
+ *          + rms_norm(moe_raw, post_ffw_norm_2), post_ffw_norm)) * out_scale.
+ * mlp_raw NULL reads as zeros; hidden may alias attn_res. */
+void oracle_ffn_epilogue(const float *attn_res, const float *mlp_raw, const float *moe_raw,
+                         const float *post_ffw_norm_1, const float *post_ffw_norm_2, const float *post_ffw_norm,
+                         float out_scale, float *hidden, int H, int T, float eps);
+
 /* Router, model.rs:1804-1829 generalised from (E=128, K=8) to (E, K):
  * logits[t,e] = sequential f32 sum of x[t,i]*W[e,i] (mul then add, i
  * ascending); experts sorted by logit descending, ties to the lower expert id;

@@ -49,6 +49,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_gelu_approx.argtypes = [f]
         L.oracle_geglu.argtypes = [vp, vp, vp, i]
         L.oracle_rms_norm.argtypes = [vp, vp, f, vp, i]
+        L.oracle_ffn_prologue.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, f]
+        L.oracle_ffn_epilogue.argtypes = [vp, vp, vp, vp, vp, vp, f, vp, i, i, f]
         L.oracle_moe_router.argtypes = [vp, vp, vp, vp, vp, i, i, i, i]
         L.oracle_moe_route_from_logits.argtypes = [vp, vp, vp, i, i, i]
         L.oracle_moe_experts.argtypes = [i, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, i, i]
@@ -110,6 +112,30 @@ def rms_norm(x, weight, eps):
     w = None if weight is None else _c(weight, np.float32)
     for t in range(T):
         lib().oracle_rms_norm(_p(x[t]), None if w is None else _p(w), eps, _p(out[t]), H)
+    return out
+
+
+def ffn_prologue(h, ffn_norm, pre_ffw_norm_2, gate_inp_scale, eps=1e-6):
+    """(x_shared, x_moe, router_x) of model.rs:1743-1784 for [T, H] rows."""
+    h = _c(h, np.float32)
+    T, H = h.shape
+    outs = [np.zeros_like(h) for _ in range(3)]
+    ws = [None if w is None else _c(w, np.float32) for w in (ffn_norm, pre_ffw_norm_2, gate_inp_scale)]
+    lib().oracle_ffn_prologue(_p(h), *[None if w is None else _p(w) for w in ws], *[_p(o) for o in outs], H, T,
+                              ctypes.c_float(eps))
+    return tuple(outs)
+
+
+def ffn_epilogue(attn_res, mlp_raw, moe_raw, post1, post2, post, out_scale, eps=1e-6):
+    """hidden of model.rs:2176-2196 for [T, H] rows (mlp_raw None = zeros)."""
+    attn_res, moe_raw = _c(attn_res, np.float32), _c(moe_raw, np.float32)
+    T, H = attn_res.shape
+    mlp = None if mlp_raw is None else _c(mlp_raw, np.float32)
+    ws = [None if w is None else _c(w, np.float32) for w in (post1, post2, post)]
+    out = np.zeros_like(attn_res)
+    lib().oracle_ffn_epilogue(_p(attn_res), None if mlp is None else _p(mlp), _p(moe_raw),
+                              *[None if w is None else _p(w) for w in ws], ctypes.c_float(out_scale), _p(out), H, T,
+                              ctypes.c_float(eps))
     return out
 
 

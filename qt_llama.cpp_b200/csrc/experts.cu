@@ -877,6 +877,109 @@ __global__ void combine_kernel(const float* __restrict__ ydown, const int32_t* _
   out[(size_t)t * H + i] = o;
 }
 
+// 1 / sqrt(mean(row^2) + eps) with the reference's rounding (ops.rs:29-34):
+// squares summed in index order in f32 by one thread, over a row staged in
+// shared memory (H a multiple of 4 takes float4 loads; the order is the same).
+__device__ __forceinline__ float rms_scale_seq(const float* row, int H, float eps) {
+  float s = 0.f;
+  int i = 0;
+  if ((H & 3) == 0) {
+#pragma unroll 8
+    for (; i < H; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(row + i);
+      s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+      s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+      s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+      s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+    }
+  }
+  for (; i < H; ++i) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), eps)));
+}
+
+// FFN prologue of a Gemma-4 MoE layer (model.rs:1743-1784; the reference's
+// GPU form is rust_cuda_prepare_ffn_f32, cuda_ptx/kernels.rs:987-1033).  From
+// the residual h, with one sum of squares (the three norms see the same row):
+//   x_shared = (h * s) * ffn_norm             (shared dense MLP input)
+//   x_moe    = (h * s) * pre_ffw_norm_2       (the experts' input)
+//   router_x = ((h * s) * (1/sqrt(H))) * gate_inp_scale   (router input)
+// each output optional, a missing weight meaning 1.  One warp per row.
+__global__ void ffn_prologue_kernel(const float* __restrict__ h, const float* __restrict__ ffn_norm,
+                                    const float* __restrict__ pre_norm2, const float* __restrict__ gis,
+                                    float* __restrict__ x_shared, float* __restrict__ x_moe,
+                                    float* __restrict__ router_x, int H, int T, float eps) {
+  extern __shared__ __align__(16) float rows_s[];
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const float* xr = h + (size_t)t * H;
+  float* row = rows_s + (size_t)warp * H;
+  for (int i = lane; i < H; i += 32) row[i] = xr[i];
+  __syncwarp();
+  float scale = 0.f;
+  if (lane == 0) scale = rms_scale_seq(row, H, eps);
+  scale = __shfl_sync(0xffffffffu, scale, 0);
+  const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)H));
+  const size_t o = (size_t)t * H;
+  for (int i = lane; i < H; i += 32) {
+    const float v = __fmul_rn(row[i], scale);
+    if (x_shared) x_shared[o + i] = ffn_norm ? __fmul_rn(v, ffn_norm[i]) : v;
+    if (x_moe) x_moe[o + i] = pre_norm2 ? __fmul_rn(v, pre_norm2[i]) : v;
+    if (router_x) {
+      const float r = __fmul_rn(v, inv_sqrt);
+      router_x[o + i] = gis ? __fmul_rn(r, gis[i]) : r;
+    }
+  }
+}
+
+// FFN epilogue (model.rs:2176-2196; rust_cuda_finish_ffn_f32,
+// cuda_ptx/kernels.rs:1036-1083):
+//   mlp_out = rms_norm(mlp_raw, post_ffw_norm_1)   (mlp_raw may be absent: 0)
+//   moe_out = rms_norm(moe_raw, post_ffw_norm_2)
+//   hidden  = (attn_res + rms_norm(mlp_out + moe_out, post_ffw_norm)) * out_scale
+// One warp per row; the two first sums of squares run in two lanes at once,
+// the third after them.  Shared memory: two rows per warp.
+__global__ void ffn_epilogue_kernel(const float* __restrict__ attn_res, const float* __restrict__ mlp_raw,
+                                    const float* __restrict__ moe_raw, const float* __restrict__ post1,
+                                    const float* __restrict__ post2, const float* __restrict__ post,
+                                    float out_scale, float* __restrict__ hidden, int H, int T, float eps) {
+  extern __shared__ __align__(16) float rows_s[];
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const size_t o = (size_t)t * H;
+  float* ma = rows_s + (size_t)warp * 2 * H;  // mlp row, then the combined row
+  float* mo = ma + H;                         // moe row
+  for (int i = lane; i < H; i += 32) {
+    ma[i] = mlp_raw ? mlp_raw[o + i] : 0.f;
+    mo[i] = moe_raw[o + i];
+  }
+  __syncwarp();
+  float s = 0.f;
+  if (lane < 2) s = rms_scale_seq(lane == 0 ? ma : mo, H, eps);
+  const float s1 = __shfl_sync(0xffffffffu, s, 0), s2 = __shfl_sync(0xffffffffu, s, 1);
+  for (int i = lane; i < H; i += 32) {
+    float a = __fmul_rn(ma[i], s1);
+    if (post1) a = __fmul_rn(a, post1[i]);
+    float b = __fmul_rn(mo[i], s2);
+    if (post2) b = __fmul_rn(b, post2[i]);
+    ma[i] = __fadd_rn(a, b);
+  }
+  __syncwarp();
+  float s3 = 0.f;
+  if (lane == 0) s3 = rms_scale_seq(ma, H, eps);
+  s3 = __shfl_sync(0xffffffffu, s3, 0);
+  for (int i = lane; i < H; i += 32) {
+    float v = __fmul_rn(ma[i], s3);
+    if (post) v = __fmul_rn(v, post[i]);
+    hidden[o + i] = __fmul_rn(__fadd_rn(attn_res[o + i], v), out_scale);
+  }
+}
+
 // RMS normalisation of T rows of H (ops.rs:24-49): sum_sq accumulated in
 // index order in f32 (x*x rounded, then added), mean = sum_sq / H,
 // scale = 1 / sqrt(mean + eps), out = (x * scale) * w.  One warp per row:
@@ -963,6 +1066,45 @@ cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, i
   const cudaError_t st = ensure_smem(rms_norm_kernel, smem, cache);
   if (st != cudaSuccess) return st;
   return launch_pdl(rms_norm_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, x, w, out, H, T, eps);
+}
+
+// The routing of a dense FFN run as one expert: every token's one slot goes
+// to expert 0 with weight 1 (so the combine's (1 * y) * 1 is y itself).
+__global__ void dense_routing_kernel(int32_t* __restrict__ ids, float* __restrict__ probs, int T) {
+  pdl_trigger();
+  pdl_wait();
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+    ids[t] = 0;
+    probs[t] = 1.0f;
+  }
+}
+
+cudaError_t launch_dense_routing(int32_t* ids, float* probs, int T, cudaStream_t s) {
+  return launch_pdl(dense_routing_kernel, dim3(std::min(148, (T + 255) / 256)), dim3(256), 0, s, ids, probs, T);
+}
+
+cudaError_t launch_ffn_prologue(const float* h, const float* ffn_norm, const float* pre_norm2, const float* gis,
+                                float* x_shared, float* x_moe, float* router_x, int H, int T, float eps,
+                                cudaStream_t s) {
+  static SmemOptIn cache;
+  const int r = rms_norm_rows_per_cta(H);
+  const size_t smem = (size_t)r * H * 4;
+  const cudaError_t st = ensure_smem(ffn_prologue_kernel, smem, cache);
+  if (st != cudaSuccess) return st;
+  return launch_pdl(ffn_prologue_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, h, ffn_norm, pre_norm2, gis,
+                    x_shared, x_moe, router_x, H, T, eps);
+}
+
+cudaError_t launch_ffn_epilogue(const float* attn_res, const float* mlp_raw, const float* moe_raw, const float* post1,
+                                const float* post2, const float* post, float out_scale, float* hidden, int H, int T,
+                                float eps, cudaStream_t s) {
+  static SmemOptIn cache;
+  const int r = rms_norm_rows_per_cta(2 * H);
+  const size_t smem = (size_t)r * 2 * H * 4;
+  const cudaError_t st = ensure_smem(ffn_epilogue_kernel, smem, cache);
+  if (st != cudaSuccess) return st;
+  return launch_pdl(ffn_epilogue_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, attn_res, mlp_raw, moe_raw,
+                    post1, post2, post, out_scale, hidden, H, T, eps);
 }
 
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s) {

@@ -40,12 +40,12 @@ using tc::wait_bar;
 constexpr int kGateUpCtas = MRML_GV_GATE_UP_CTAS;
 
 // CTAs per SM of each form (its launch bound): the MMA gate/up product with
-// one position group per unit kGateUpCtas; 16-position units 3 (their
-// accumulators need the registers: at 4 CTAs the Q4_0 forms spilled, and the
-// packed Q4_0 gate/up at config 4 took 3.67 ms against 3.33 on GGUF rows);
-// the others 4.
-__host__ __device__ constexpr int ctas_per_sm(bool mma, int mode, int ng) {
-  return (mma && mode == kGateUp && ng == 1) ? kGateUpCtas : (ng == 2 ? 3 : 4);
+// one position group per unit kGateUpCtas; 16-position units on packed
+// weights or Q8_0 rows 3 (their accumulators need the registers: at 4 the
+// packed Q4_0 gate/up spilled and took 3.67 ms at config 4 against 3.26 ms at
+// 3), on Q4_0 GGUF rows 4 (3.33 against 3.77 ms); the others 4.
+__host__ __device__ constexpr int ctas_per_sm(bool mma, int mode, int ng, bool q4, bool packed) {
+  return (mma && mode == kGateUp && ng == 1) ? kGateUpCtas : (ng == 2 && (packed || !q4) ? 3 : 4);
 }
 
 constexpr int kComp0 = 2;      // first compute warp
@@ -463,7 +463,7 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const ui
 // kKC][record], down [E][128-row group][tile 8][block][record].
 template <int WQ4, int MODE, int MMA, int NG, int PK>
 __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
-                                  ctas_per_sm(MMA, MODE, NG))
+                                  ctas_per_sm(MMA, MODE, NG, WQ4, PK))
     moe_gemv_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
   static_assert(NG == 1 || (NG == 2 && MMA), "two position groups per unit on the MMA form only");
   constexpr int BB = WQ4 ? 18 : 34;
@@ -944,7 +944,7 @@ struct GvPlan {
 // of the decode kernel; 0 = automatic.
 std::atomic<int> g_gv_per_sm{0}, g_gv_ring{0};
 
-GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma, int ng) {
+GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma, int ng, bool packed = false) {
   GvPlan p{};
   const int bb = block_bytes(wtype);
   p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
@@ -955,7 +955,7 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   // With many units, as many CTAs per SM as fit with a double-buffered weight
   // ring (the kernel's launch bound, ctas_per_sm);
   // with few units, one CTA and the deepest ring that fits.
-  const int bound = gv::ctas_per_sm(mma, mode, ng);
+  const int bound = gv::ctas_per_sm(mma, mode, ng, wtype == kQ4_0, packed);
   const int per_sm_set = g_gv_per_sm.load(), ring_set = g_gv_ring.load();
   const int per_sm_max = per_sm_set > 0 ? per_sm_set : (many_units ? bound : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
@@ -1071,14 +1071,14 @@ cudaError_t launch_gemv(int mode, int wtype, bool packed, bool mma, int ng, cons
       P.w_raw = weights;
     else if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp))
       return cudaErrorInvalidValue;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng, packed);
   } else {
     P.nb = I / 32;
     P.rows = H;
     P.row_bytes = (I / 32) * bb;
     P.w_raw = weights;
     P.y = y;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng, packed);
   }
   if (pl.smem == 0) return cudaErrorInvalidValue;
   P.rs = pl.rs;

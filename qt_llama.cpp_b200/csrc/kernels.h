@@ -76,7 +76,14 @@ cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t*
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s);
 int rms_norm_rows_per_cta(int H);
 cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, int T, float eps, cudaStream_t s);
+cudaError_t launch_ffn_prologue(const float* h, const float* ffn_norm, const float* pre_norm2, const float* gis,
+                                float* x_shared, float* x_moe, float* router_x, int H, int T, float eps,
+                                cudaStream_t s);
+cudaError_t launch_ffn_epilogue(const float* attn_res, const float* mlp_raw, const float* moe_raw, const float* post1,
+                                const float* post2, const float* post, float out_scale, float* hidden, int H, int T,
+                                float eps, cudaStream_t s);
 cudaError_t launch_geglu(const float* gate, const float* up, float* out, long long n, cudaStream_t s);
+cudaError_t launch_dense_routing(int32_t* ids, float* probs, int T, cudaStream_t s);
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
                             int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units,

@@ -560,6 +560,56 @@ int mrml_moe_combine(const float* ydown, const int32_t* pos, const int32_t* ids,
   return MRML_OK;
 }
 
+int mrml_moe_ffn_prologue(const float* h, const float* ffn_norm, const float* pre_ffw_norm_2,
+                          const float* gate_inp_scale, float* x_shared, float* x_moe, float* router_x, int H, int T,
+                          float eps, mrml_stream_t stream) {
+  if (H <= 0 || T < 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (T == 0) return MRML_OK;
+  if (!h || (!x_shared && !x_moe && !router_x) || !aligned16(h)) return MRML_ERR_INVALID_ARGUMENT;
+  if (mrml::rms_norm_rows_per_cta(H) == 0) return MRML_ERR_UNSUPPORTED;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_ffn_prologue(h, ffn_norm, pre_ffw_norm_2, gate_inp_scale, x_shared, x_moe, router_x, H, T,
+                                        eps, s));
+  return MRML_OK;
+}
+
+int mrml_moe_ffn_epilogue(const float* attn_res, const float* mlp_raw, const float* moe_raw,
+                          const float* post_ffw_norm_1, const float* post_ffw_norm_2, const float* post_ffw_norm,
+                          float layer_output_scale, float* hidden, int H, int T, float eps, mrml_stream_t stream) {
+  if (H <= 0 || T < 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (T == 0) return MRML_OK;
+  if (!attn_res || !moe_raw || !hidden) return MRML_ERR_INVALID_ARGUMENT;
+  if (mrml::rms_norm_rows_per_cta(2 * H) == 0) return MRML_ERR_UNSUPPORTED;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  MRML_LAUNCH(mrml::launch_ffn_epilogue(attn_res, mlp_raw, moe_raw, post_ffw_norm_1, post_ffw_norm_2, post_ffw_norm,
+                                        layer_output_scale, hidden, H, T, eps, s));
+  return MRML_OK;
+}
+
+size_t mrml_moe_dense_ffn_workspace_bytes(int H, int I, int T) {
+  if (H <= 0 || I <= 0 || T < 0) return 0;
+  return carve(nullptr, H, I, 1, 1, T).bytes + 2 * align256((size_t)T * 4);
+}
+
+int mrml_moe_dense_ffn(int wtype, const uint8_t* gate_up, const uint8_t* down, const float* x, float* out, int H,
+                       int I, int T, void* workspace, size_t workspace_bytes, mrml_stream_t stream) {
+  MRML_TRY(check_weights(wtype, H, I, 1, 1, T));
+  if (T == 0) return MRML_OK;
+  if (!gate_up || !down || !x || !out || !aligned16(gate_up) || !aligned16(down) || !aligned16(x))
+    return MRML_ERR_INVALID_ARGUMENT;
+  if (!workspace || ((uintptr_t)workspace & 255u) != 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < mrml_moe_dense_ffn_workspace_bytes(H, I, T)) return MRML_ERR_WORKSPACE_TOO_SMALL;
+  MRML_TRY(check_device());
+  const cudaStream_t s = (cudaStream_t)stream;
+  const Workspace w = carve(workspace, H, I, 1, 1, T);
+  int32_t* ids = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + w.bytes);
+  float* probs = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + w.bytes + align256((size_t)T * 4));
+  MRML_LAUNCH(mrml::launch_dense_routing(ids, probs, T, s));
+  return run_experts(w, wtype, gate_up, down, ids, probs, nullptr, x, out, H, I, 1, 1, T, s);
+}
+
 int mrml_moe_rms_norm(const float* x, const float* weight, float* out, int dim, int batch, float eps,
                       mrml_stream_t stream) {
   if (dim <= 0 || batch < 0) return MRML_ERR_INVALID_ARGUMENT;

@@ -74,6 +74,10 @@ SIGNATURES = {
     "mrml_moe_set_option": (_i, [_i, _i]),
     "mrml_moe_weights_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "mrml_moe_prepare_weights": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "mrml_moe_ffn_prologue": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp]),
+    "mrml_moe_ffn_epilogue": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _i, _i, _f, _vp]),
+    "mrml_moe_dense_ffn_workspace_bytes": (_sz, [_i, _i, _i]),
+    "mrml_moe_dense_ffn": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "mrml_moe_gguf_open": (_i, [_c.c_char_p, _c.POINTER(_vp)]),
     "mrml_moe_gguf_close": (_i, [_vp]),
     "mrml_moe_gguf_version": (_i, [_vp]),
@@ -280,6 +284,34 @@ def combine(ydown, pos, ids, probs, down_scale, out, H, K, T, stream=None):
         lib.mrml_moe_combine(_ptr(ydown), _ptr(pos), _ptr(ids), _ptr(probs), _ptr(down_scale), _ptr(out), H, K, T,
                              _stream_ptr(stream)),
     )
+
+
+def ffn_prologue(h, ffn_norm, pre_ffw_norm_2, gate_inp_scale, x_shared, x_moe, router_x, H, T, eps=1e-6,
+                 stream=None):
+    _check("mrml_moe_ffn_prologue",
+           load_library().mrml_moe_ffn_prologue(_ptr(h), _ptr(ffn_norm), _ptr(pre_ffw_norm_2), _ptr(gate_inp_scale),
+                                                _ptr(x_shared), _ptr(x_moe), _ptr(router_x), H, T, eps,
+                                                _stream_ptr(stream)))
+
+
+def ffn_epilogue(attn_res, mlp_raw, moe_raw, post1, post2, post, out_scale, hidden, H, T, eps=1e-6, stream=None):
+    _check("mrml_moe_ffn_epilogue",
+           load_library().mrml_moe_ffn_epilogue(_ptr(attn_res), _ptr(mlp_raw), _ptr(moe_raw), _ptr(post1),
+                                                _ptr(post2), _ptr(post), out_scale, _ptr(hidden), H, T, eps,
+                                                _stream_ptr(stream)))
+
+
+def new_dense_ffn_workspace(H, I, T, device=None):
+    import torch
+
+    n = load_library().mrml_moe_dense_ffn_workspace_bytes(H, I, T)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def dense_ffn(wtype, gate_up, down, x, out, H, I, T, ws, stream=None):
+    _check("mrml_moe_dense_ffn",
+           load_library().mrml_moe_dense_ffn(wtype, _ptr(gate_up), _ptr(down), _ptr(x), _ptr(out), H, I, T, _ptr(ws),
+                                             ws.numel(), _stream_ptr(stream)))
 
 
 def rms_norm(x, weight, out, dim, batch, eps, stream=None):

@@ -251,3 +251,41 @@ def test_golden_vectors_reproduce(oracle, synth, name):
     stored = np.load(os.path.join(here, "golden", f"{name}.npz"))
     for k in stored.files:
         assert np.array_equal(stored[k], fresh[k]), k
+
+
+def _rms_rows_f32(x, w, eps):
+    """ops.rs:24-49 in numpy float32 scalars (sequential sum, no fusing)."""
+    f = np.float32
+    out = np.zeros_like(x)
+    for t in range(x.shape[0]):
+        s = f(0)
+        for v in x[t]:
+            s = f(s + f(v * v))
+        scale = f(f(1) / np.sqrt(f(f(s / f(x.shape[1])) + f(eps))))
+        out[t] = x[t] * scale if w is None else (x[t] * scale) * w
+    return out
+
+
+def test_ffn_prologue_epilogue_restatement(oracle):
+    """The oracle's FFN prologue / epilogue (model.rs:1743-1784, 2176-2196)
+    against an independent numpy restatement, bit for bit."""
+    rng = np.random.default_rng(3)
+    T, H = 3, 96
+    f = np.float32
+    h = rng.standard_normal((T, H)).astype(f)
+    w1, w2, w3 = (1 + 0.1 * rng.standard_normal((3, H))).astype(f)
+    xs, xm, rx = oracle.ffn_prologue(h, w1, w2, w3)
+    assert np.array_equal(xs, _rms_rows_f32(h, w1, 1e-6))
+    assert np.array_equal(xm, _rms_rows_f32(h, w2, 1e-6))
+    inv = f(f(1) / np.sqrt(f(H)))
+    assert np.array_equal(rx, (_rms_rows_f32(h, None, 1e-6) * inv) * w3)
+
+    mlp = rng.standard_normal((T, H)).astype(f)
+    mo = (0.1 * rng.standard_normal((T, H))).astype(f)
+    comb = _rms_rows_f32(mlp, w1, 1e-6) + _rms_rows_f32(mo, w2, 1e-6)
+    want = (h + _rms_rows_f32(comb, w3, 1e-6)) * f(0.5)
+    assert np.array_equal(oracle.ffn_epilogue(h, mlp, mo, w1, w2, w3, 0.5), want)
+    # no shared MLP: its raw output reads as zeros
+    comb0 = _rms_rows_f32(np.zeros_like(mlp), w1, 1e-6) + _rms_rows_f32(mo, w2, 1e-6)
+    want0 = (h + _rms_rows_f32(comb0, w3, 1e-6)) * f(0.5)
+    assert np.array_equal(oracle.ffn_epilogue(h, None, mo, w1, w2, w3, 0.5), want0)
