@@ -464,10 +464,12 @@ def parity_check(ls, world, rank, n_check=64, seed=123):
 
 
 class StackSet:
-    """Config 5: a stack of 30 independent MoE layers of the config-2 shape
-    (Q4_0) with x_{l+1} = rms_norm(moe_l(x_l)) (weight 1, eps 1e-6; the norm
-    model.rs:2176-2196 applies after the MoE output), decode batch of 32
-    tokens in total.  With N > 1 every layer runs expert-parallel (T = 32/N
+    """Config 5: a stack of 30 independent MoE FFN blocks of the config-2
+    shape (Q4_0), decode batch of 32 tokens in total, each block as a Gemma-4
+    layer runs its FFN half without the attention and the shared MLP: the
+    fused prologue (model.rs:1719-1784: router input and experts' input, two
+    RMS norms of h), the MoE layer, and the fused epilogue (model.rs:
+    2176-2196: post-norms, residual add, layer scale) producing h_{l+1}.  With N > 1 every layer runs expert-parallel (T = 32/N
     home tokens per rank), one exchange object shared by the 30 layers.
     A step runs the whole stack; inputs are fresh N(0,1) batches."""
 
@@ -506,7 +508,10 @@ class StackSet:
             g = torch.Generator(device=device)
             g.manual_seed(seed * 1000 + 900 + l)
             W = torch.randn((E, H), generator=g, device=device).mul_(0.02)
-            self.layers.append((gu, dn, W))
+            # norm weights of the block: pre_ffw_norm_2, router scale, post_ffw_norm_2, post_ffw_norm
+            norms = [torch.randn(H, generator=g, device=device).mul_(0.1).add_(1.0) for _ in range(4)]
+            self.layers.append((gu, dn, W, norms))
+        self.seed = seed
         bb = 18
         self.layer_bytes = count * (2 * I * (H // 32) * bb + H * (I // 32) * bb)
         g = torch.Generator(device=device)
@@ -514,26 +519,98 @@ class StackSet:
         self.xs = [torch.randn((T, H), generator=g, device=device) for _ in range(n_inputs)]
         self.h = [torch.empty((T, H), device=device) for _ in range(2)]
         self.moe_out = torch.empty((T, H), device=device)
+        self.x_moe = torch.empty((T, H), device=device)
+        self.router_x = torch.empty((T, H), device=device)
         self.out = torch.empty((T, H), device=device)
 
     def step(self, i, x=None, out=None):
         m, H, T = self.moe, self.H, self.T
         h = self.xs[i % len(self.xs)] if x is None else x
         out = self.out if out is None else out
-        for l, (gu, dn, W) in enumerate(self.layers):
-            if self.ep is not None:
-                self.ep.forward(W, h, gu, dn, self.moe_out)
-            else:
-                m.forward(self.wcall, W, h, h, gu, dn, None, self.logits, self.ids, self.probs, self.moe_out, H,
-                          self.I, self.E, self.K, T, self.ws)
+        for l in range(len(self.layers)):
             nxt = out if l == len(self.layers) - 1 else self.h[l & 1]
-            m.rms_norm(self.moe_out, None, nxt, H, T, 1e-6)
+            self.layer_step(l, h, nxt)
             h = nxt
+
+    def layer_step(self, l, h, nxt):
+        """Block l on h (the same calls as step)."""
+        m, H, T = self.moe, self.H, self.T
+        gu, dn, W, (pre2, rscale, post2, post) = self.layers[l]
+        m.ffn_prologue(h, None, None, None, pre2, rscale, None, None, self.x_moe, self.router_x, H, T)
+        if self.ep is not None:
+            self.ep.forward(W, self.x_moe, gu, dn, self.moe_out, router_x=self.router_x)
+        else:
+            m.forward(self.wcall, W, self.router_x, self.x_moe, gu, dn, None, self.logits, self.ids, self.probs,
+                      self.moe_out, H, self.I, self.E, self.K, T, self.ws)
+        m.ffn_epilogue(h, None, self.moe_out, None, post2, post, nxt, 1.0, H, T)
+
+    def raw_layer_host(self, l):
+        """Layer l's GGUF-layout expert slabs (all E experts) on the host,
+        regenerated from the layer's seed."""
+        import torch
+
+        synth = _load("mrml_moe_b200_synth", os.path.join(ROOT, "qt_llama.cpp_b200", "synth.py"))
+        gu, dn = synth.expert_weights_device(self.seed * 1000 + 500 + l, self.wtype, self.H, self.I, self.E,
+                                             self.device, self.moe.quantize)
+        out = gu.cpu().numpy(), dn.cpu().numpy()
+        del gu, dn
+        torch.cuda.empty_cache()
+        return out
 
     capture = LayerSet.capture
 
     def n_kernels(self):
         return 0
+
+
+def stack_parity_check(ss, world, rank, layers=(0, 1, 29), n_check=4, seed=321):
+    """Config 5 outside the timed region: the stack runs block by block on
+    one input, and for each block in `layers` the oracle (the reference's CPU
+    FFN block, model.rs:1719-1784, 1804-1829, 2111-2196) recomputes a seeded
+    sample of tokens from the same block input; ids and outputs must be
+    identical.  Every rank takes part; rank 0 returns the record."""
+    import torch
+
+    oracle = _load("mrml_oracle", os.path.join(ROOT, "oracle", "oracle.py"))
+    H, I, E, K = ss.H, ss.I, ss.E, ss.K
+    h = ss.xs[0].clone()
+    nxt = torch.empty_like(h)
+    saved = {}
+    for l in range(len(ss.layers)):
+        ss.layer_step(l, h, nxt)
+        if l in layers:
+            torch.cuda.synchronize()
+            saved[l] = (all_gather_np(h, world), all_gather_np(nxt, world), all_gather_np(ss.ids, world))
+        h, nxt = nxt, h
+    ok, worst, n_ids_bad = True, 0.0, 0
+    idx = None
+    for l in layers:
+        # every rank regenerates in step (the quantiser runs on each device);
+        # only rank 0 checks
+        gu, dn = ss.raw_layer_host(l)
+        if rank != 0:
+            continue
+        x, y, ids = saved[l]
+        if idx is None:
+            idx = np.sort(np.random.default_rng(seed).choice(x.shape[0], size=min(n_check, x.shape[0]),
+                                                             replace=False))
+        W = ss.layers[l][2].cpu().numpy()
+        pre2, rscale, post2, post = [w.cpu().numpy() for w in ss.layers[l][3]]
+        _, _, xm, rx = oracle.ffn_prologue(x[idx], None, None, None, pre2, rscale)
+        _, r_ids, r_probs = oracle.router(W, rx, H, E, K, len(idx))
+        moe_raw = oracle.experts(ss.wtype, gu, dn, r_ids, r_probs, None, xm, H, I, E, K, len(idx),
+                                 os.cpu_count() or 1)
+        ref = oracle.ffn_epilogue(x[idx], None, moe_raw, None, post2, post, 1.0)
+        got = y[idx]
+        n_ids_bad += int(np.count_nonzero(np.any(ids[idx] != r_ids, axis=1)))
+        rel = float(np.linalg.norm(got.astype(np.float64) - ref) / max(np.linalg.norm(ref), 1e-30))
+        worst = max(worst, rel)
+        ok = ok and bool(np.array_equal(got, ref))
+    if rank != 0:
+        return None
+    return {"ok": ok and n_ids_bad == 0, "bit_exact": ok, "ids_exact": n_ids_bad == 0, "max_rel_l2": worst,
+            "layers_checked": list(layers), "tokens_checked_per_layer": int(len(idx)),
+            "reference": "oracle/ (the reference's CPU FFN block restated)"}
 
 
 def run_stack(args):
@@ -574,7 +651,8 @@ def run_stack(args):
         "data": "synthetic (seeded N(0,0.02) weights quantised with the reference's Q4_0 rules, fresh N(0,1) x)",
         "config": {"workload": "c5", "layers": nl, "hidden": ss.H, "experts": ss.E, "top_k": ss.K,
                    "expert_ffn": ss.I, "tokens_per_step": total_tokens, "home_tokens_per_rank": ss.T,
-                   "norm": "rms_norm(w=1, eps=1e-6) after every layer",
+                   "block": "fused FFN prologue (pre_ffw_norm_2, router input) + MoE + fused epilogue "
+                            "(post-norms, residual), model.rs:1719-1784 and 2176-2196",
                    "parallelism": (f"ep{world} (" + args.ep_exchange + " exchange)") if world > 1 else "single GPU",
                    "l2": f"inputs larger than L2: each step streams {nl} layers "
                          f"({nl * ss.layer_bytes / 1e6:.0f} MB of this rank's expert weights)"},
@@ -584,11 +662,13 @@ def run_stack(args):
         "e2e": {"value": round(total_tokens * args.steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         # per layer: the MoE launches (forward at world 1; router, expert
-        # shard and the exchange kernels under expert parallelism) + rms_norm
-        "gpu_launches": args.steps * nl * (1 + (len(forward_kernels(ss.T, ss.E, ss.K)) if world == 1 else
+        # shard and the exchange kernels under expert parallelism) + the
+        # prologue and epilogue
+        "gpu_launches": args.steps * nl * (2 + (len(forward_kernels(ss.T, ss.E, ss.K)) if world == 1 else
                                                (11 if args.ep_exchange == "p2p" else 7))),
         "clocks": clk.summary(),
     }
+    line["parity"] = stack_parity_check(ss, world, rank)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -998,11 +1078,15 @@ def run_reference(args):
     setup_s = time.perf_counter() - t_setup
     threads = os.cpu_count() or 1
 
+    nw = [(1.0 + synth.normal(1100 + j, H, 0.1)).astype(np.float32) for j in range(4)]
+
     def one_stack(i):
         h = xs[0][i % 32:i % 32 + 1]
         for _ in range(StackSet.N_LAYERS):
-            _, ids, probs = oracle.router(W, h, H, E, K, 1)
-            h = oracle.rms_norm(oracle.experts(wtype, gu, dn, ids, probs, None, h, H, I, E, K, 1, threads), None, 1e-6)
+            _, _, xm, rx = oracle.ffn_prologue(h, None, None, None, nw[0], nw[1])
+            _, ids, probs = oracle.router(W, rx, H, E, K, 1)
+            y = oracle.experts(wtype, gu, dn, ids, probs, None, xm, H, I, E, K, 1, threads)
+            h = oracle.ffn_epilogue(h, None, y, None, nw[2], nw[3], 1.0)
         return 1
 
     def one(i):

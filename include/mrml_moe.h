@@ -270,31 +270,35 @@ int mrml_moe_gguf_read(const void *file, const char *name, void *dst, size_t dst
 int mrml_moe_combine(const float *ydown, const int32_t *pos, const int32_t *ids, const float *probs,
                      const float *down_scale, float *out, int H, int K, int T, mrml_stream_t stream);
 
-/* The FFN prologue of a Gemma-4 MoE layer, fused (model.rs:1743-1784; the
- * reference's GPU form is rust_cuda_prepare_ffn_f32, cuda_ptx/kernels.rs:
- * 987-1033).  From the residual h[T][H], with one sum of squares per row
- * (s = 1 / sqrt(mean(h^2) + eps), ops.rs:24-49's order and rounding):
- *   x_shared = (h * s) * ffn_norm            the shared dense MLP's input
- *   x_moe    = (h * s) * pre_ffw_norm_2      the experts' input
- *   router_x = ((h * s) * (1 / sqrt(H))) * gate_inp_scale   the router's input
- * Bit-identical to the reference's three rms_norm calls and scaling.  Any
- * output may be NULL (not written); a NULL weight means 1.  h 16-byte
- * aligned; H <= 51200. */
-int mrml_moe_ffn_prologue(const float *h, const float *ffn_norm, const float *pre_ffw_norm_2,
-                          const float *gate_inp_scale, float *x_shared, float *x_moe, float *router_x, int H, int T,
-                          float eps, mrml_stream_t stream);
+/* The FFN prologue of a Gemma-4 MoE layer, fused: replaces
+ * launch_rust_prepare_ffn (cuda.rs:899-949, kernel rust_cuda_prepare_ffn_f32
+ * in cuda_ptx/kernels.rs:987-1033) with the same arguments, and computes
+ * what the reference's CPU path does (model.rs:1719-1784) bit for bit.
+ * Per row of `dim` floats (batch rows), eps 1e-6:
+ *   attn_res = hidden + rms_norm(attn, post_attn_norm)
+ *   shared   = rms_norm(attn_res, ffn_norm)          the shared dense MLP's input
+ *   moe      = rms_norm(attn_res, pre_ffw_norm_2)    the experts' input
+ *   router   = rms_norm(attn_res) * (1 / sqrt(dim)) * router_scale
+ * rms_norm as ops.rs:24-49 (sequential sum of squares, (x * s) * w).
+ * Extensions: attn NULL takes hidden as the residual; any output may be NULL
+ * (not written); a NULL weight means 1.  dim <= 51200. */
+int mrml_moe_ffn_prologue(const float *hidden, const float *attn, const float *post_attn_norm,
+                          const float *ffn_norm, const float *pre_ffw_norm_2, const float *router_scale,
+                          float *attn_res, float *shared, float *moe, float *router, int dim, int batch,
+                          mrml_stream_t stream);
 
-/* The FFN epilogue, fused (model.rs:2176-2196; rust_cuda_finish_ffn_f32,
- * cuda_ptx/kernels.rs:1036-1083):
- *   hidden = (attn_res + rms_norm(rms_norm(mlp_raw, post_ffw_norm_1)
- *                                 + rms_norm(moe_raw, post_ffw_norm_2), post_ffw_norm))
- *            * layer_output_scale
- * with the reference's roundings.  mlp_raw may be NULL (a layer without the
- * shared MLP: zeros); a NULL weight means 1.  hidden may alias attn_res.
- * H <= 25600. */
-int mrml_moe_ffn_epilogue(const float *attn_res, const float *mlp_raw, const float *moe_raw,
+/* The FFN epilogue, fused: replaces launch_rust_finish_ffn (cuda.rs:951-987,
+ * kernel rust_cuda_finish_ffn_f32 in cuda_ptx/kernels.rs:1036-1083) with the
+ * same arguments; the CPU path's arithmetic (model.rs:2176-2196):
+ *   output = (attn_res + rms_norm(rms_norm(dense, post_ffw_norm_1)
+ *                                 + rms_norm(moe, post_ffw_norm_2), post_ffw_norm))
+ *            * layer_scale
+ * Unlike the reference's kernel it leaves dense and moe unchanged.  dense
+ * may be NULL (a layer without the shared MLP: zeros); a NULL weight means
+ * 1; output may alias attn_res.  dim <= 25600. */
+int mrml_moe_ffn_epilogue(const float *attn_res, const float *dense, const float *moe,
                           const float *post_ffw_norm_1, const float *post_ffw_norm_2, const float *post_ffw_norm,
-                          float layer_output_scale, float *hidden, int H, int T, float eps, mrml_stream_t stream);
+                          float *output, float layer_scale, int dim, int batch, mrml_stream_t stream);
 
 /* The layer's shared dense GeGLU MLP (model.rs:2093-2109 on the CPU;
  * gemv_q4_0_geglu + gemv_q4_0 on the reference's GPU, model.rs:1889-1890):

@@ -317,25 +317,34 @@ void oracle_rms_norm(const float *x, const float *weight, float eps, float *out,
 
 /* ------------------------------------------------------ FFN prologue --- */
 
-void oracle_ffn_prologue(const float *h, const float *ffn_norm, const float *pre_ffw_norm_2,
-                         const float *gate_inp_scale, float *x_shared, float *x_moe, float *router_x, int H, int T,
-                         float eps) {
+void oracle_ffn_prologue(const float *hidden, const float *attn, const float *post_attn_norm,
+                         const float *ffn_norm, const float *pre_ffw_norm_2, const float *router_scale,
+                         float *attn_res, float *x_shared, float *x_moe, float *router_x, int H, int T, float eps) {
   float *tmp = (float *)malloc(sizeof(float) * (size_t)H);
+  float *res = (float *)malloc(sizeof(float) * (size_t)H);
   float inv_sqrt_dim = 1.0f / sqrtf((float)H); /* model.rs:1776 */
   for (int t = 0; t < T; t++) {
-    const float *row = h + (size_t)t * H;
     size_t o = (size_t)t * H;
-    if (x_shared) oracle_rms_norm(row, ffn_norm, eps, x_shared + o, H); /* model.rs:1751-1753 */
-    if (x_moe) oracle_rms_norm(row, pre_ffw_norm_2, eps, x_moe + o, H); /* model.rs:1760-1767 */
-    if (router_x) {                                                       /* model.rs:1774-1784 */
-      oracle_rms_norm(row, NULL, eps, tmp, H);
+    if (attn) { /* model.rs:1730-1739 */
+      oracle_rms_norm(attn + o, post_attn_norm, eps, tmp, H);
+      for (int i = 0; i < H; i++) res[i] = hidden[o + i] + tmp[i];
+    } else {
+      for (int i = 0; i < H; i++) res[i] = hidden[o + i];
+    }
+    if (attn_res)
+      for (int i = 0; i < H; i++) attn_res[o + i] = res[i];
+    if (x_shared) oracle_rms_norm(res, ffn_norm, eps, x_shared + o, H); /* model.rs:1751-1753 */
+    if (x_moe) oracle_rms_norm(res, pre_ffw_norm_2, eps, x_moe + o, H); /* model.rs:1760-1767 */
+    if (router_x) {                                                     /* model.rs:1774-1784 */
+      oracle_rms_norm(res, NULL, eps, tmp, H);
       for (int i = 0; i < H; i++) {
-        float scale = gate_inp_scale ? gate_inp_scale[i] : 1.0f;
+        float scale = router_scale ? router_scale[i] : 1.0f;
         router_x[o + i] = tmp[i] * inv_sqrt_dim * scale;
       }
     }
   }
   free(tmp);
+  free(res);
 }
 
 void oracle_ffn_epilogue(const float *attn_res, const float *mlp_raw, const float *moe_raw,

@@ -66,13 +66,14 @@ void oracle_geglu(const float *gate, const float *up, float *out, int n);
 void oracle_rms_norm(const float *x, const float *weight, float eps, float *out,
                      int n);
 
-/* FFN prologue of a MoE layer, model.rs:1743-1784 for T rows of H:
- * x_shared = rms_norm(h, ffn_norm), x_moe = rms_norm(h, pre_ffw_norm_2),
- * router_x[i] = rms_norm(h, none)[i] * (1 / sqrtf(H)) * gate_inp_scale[i].
- * A NULL output is skipped; a NULL weight means 1. */
-void oracle_ffn_prologue(const float *h, const float *ffn_norm, const float *pre_ffw_norm_2,
-                         const float *gate_inp_scale, float *x_shared, float *x_moe, float *router_x, int H, int T,
-                         float eps);
+/* FFN prologue of a MoE layer, model.rs:1719-1784 for T rows of H:
+ * attn_res = hidden + rms_norm(attn, post_attn_norm) (attn NULL: hidden),
+ * x_shared = rms_norm(attn_res, ffn_norm), x_moe = rms_norm(attn_res,
+ * pre_ffw_norm_2), router_x[i] = rms_norm(attn_res, none)[i] * (1 / sqrtf(H))
+ * * router_scale[i].  A NULL output is skipped; a NULL weight means 1. */
+void oracle_ffn_prologue(const float *hidden, const float *attn, const float *post_attn_norm,
+                         const float *ffn_norm, const float *pre_ffw_norm_2, const float *router_scale,
+                         float *attn_res, float *x_shared, float *x_moe, float *router_x, int H, int T, float eps);
 
 /* FFN epilogue, model.rs:2176-2196 for T rows of H:
  * hidden = (attn_res + rms_norm(rms_norm(mlp_raw, post_ffw_norm_1)

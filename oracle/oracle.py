@@ -49,7 +49,7 @@ def lib() -> ctypes.CDLL:
         L.oracle_gelu_approx.argtypes = [f]
         L.oracle_geglu.argtypes = [vp, vp, vp, i]
         L.oracle_rms_norm.argtypes = [vp, vp, f, vp, i]
-        L.oracle_ffn_prologue.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, f]
+        L.oracle_ffn_prologue.argtypes = [vp] * 10 + [i, i, f]
         L.oracle_ffn_epilogue.argtypes = [vp, vp, vp, vp, vp, vp, f, vp, i, i, f]
         L.oracle_moe_router.argtypes = [vp, vp, vp, vp, vp, i, i, i, i]
         L.oracle_moe_route_from_logits.argtypes = [vp, vp, vp, i, i, i]
@@ -115,14 +115,16 @@ def rms_norm(x, weight, eps):
     return out
 
 
-def ffn_prologue(h, ffn_norm, pre_ffw_norm_2, gate_inp_scale, eps=1e-6):
-    """(x_shared, x_moe, router_x) of model.rs:1743-1784 for [T, H] rows."""
-    h = _c(h, np.float32)
-    T, H = h.shape
-    outs = [np.zeros_like(h) for _ in range(3)]
-    ws = [None if w is None else _c(w, np.float32) for w in (ffn_norm, pre_ffw_norm_2, gate_inp_scale)]
-    lib().oracle_ffn_prologue(_p(h), *[None if w is None else _p(w) for w in ws], *[_p(o) for o in outs], H, T,
-                              ctypes.c_float(eps))
+def ffn_prologue(hidden, attn, post_attn_norm, ffn_norm, pre_ffw_norm_2, router_scale, eps=1e-6):
+    """(attn_res, x_shared, x_moe, router_x) of model.rs:1719-1784 for [T, H]
+    rows; attn None takes hidden as the residual."""
+    hidden = _c(hidden, np.float32)
+    T, H = hidden.shape
+    a = None if attn is None else _c(attn, np.float32)
+    outs = [np.zeros_like(hidden) for _ in range(4)]
+    ws = [None if w is None else _c(w, np.float32) for w in (post_attn_norm, ffn_norm, pre_ffw_norm_2, router_scale)]
+    lib().oracle_ffn_prologue(_p(hidden), None if a is None else _p(a), *[None if w is None else _p(w) for w in ws],
+                              *[_p(o) for o in outs], H, T, ctypes.c_float(eps))
     return tuple(outs)
 
 

@@ -897,34 +897,52 @@ __device__ __forceinline__ float rms_scale_seq(const float* row, int H, float ep
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), eps)));
 }
 
-// FFN prologue of a Gemma-4 MoE layer (model.rs:1743-1784; the reference's
-// GPU form is rust_cuda_prepare_ffn_f32, cuda_ptx/kernels.rs:987-1033).  From
-// the residual h, with one sum of squares (the three norms see the same row):
-//   x_shared = (h * s) * ffn_norm             (shared dense MLP input)
-//   x_moe    = (h * s) * pre_ffw_norm_2       (the experts' input)
-//   router_x = ((h * s) * (1/sqrt(H))) * gate_inp_scale   (router input)
-// each output optional, a missing weight meaning 1.  One warp per row.
-__global__ void ffn_prologue_kernel(const float* __restrict__ h, const float* __restrict__ ffn_norm,
+// FFN prologue of a Gemma-4 MoE layer (model.rs:1719-1784; the reference's
+// GPU form is rust_cuda_prepare_ffn_f32, cuda_ptx/kernels.rs:987-1033, whose
+// arguments it takes).  Per row, with the reference's CPU roundings:
+//   res      = hidden + (attn * s_a) * post_attn_norm   (attn absent: hidden)
+//   x_shared = (res * s) * ffn_norm             (shared dense MLP input)
+//   x_moe    = (res * s) * pre_ffw_norm_2       (the experts' input)
+//   router_x = ((res * s) * (1/sqrt(H))) * router_scale   (router input)
+// s_a, s the rms scales of attn and res (one sum of squares serves all three
+// norms).  Outputs optional, a missing weight meaning 1.  One warp per row.
+__global__ void ffn_prologue_kernel(const float* __restrict__ hidden, const float* __restrict__ attn,
+                                    const float* __restrict__ pan, const float* __restrict__ ffn_norm,
                                     const float* __restrict__ pre_norm2, const float* __restrict__ gis,
-                                    float* __restrict__ x_shared, float* __restrict__ x_moe,
-                                    float* __restrict__ router_x, int H, int T, float eps) {
+                                    float* __restrict__ attn_res, float* __restrict__ x_shared,
+                                    float* __restrict__ x_moe, float* __restrict__ router_x, int H, int T,
+                                    float eps) {
   extern __shared__ __align__(16) float rows_s[];
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
-  const float* xr = h + (size_t)t * H;
+  const size_t o = (size_t)t * H;
   float* row = rows_s + (size_t)warp * H;
-  for (int i = lane; i < H; i += 32) row[i] = xr[i];
+  if (attn) {
+    for (int i = lane; i < H; i += 32) row[i] = attn[o + i];
+    __syncwarp();
+    float sa = 0.f;
+    if (lane == 0) sa = rms_scale_seq(row, H, eps);
+    sa = __shfl_sync(0xffffffffu, sa, 0);
+    for (int i = lane; i < H; i += 32) {
+      float v = __fmul_rn(row[i], sa);
+      if (pan) v = __fmul_rn(v, pan[i]);
+      row[i] = __fadd_rn(hidden[o + i], v);
+    }
+  } else {
+    for (int i = lane; i < H; i += 32) row[i] = hidden[o + i];
+  }
   __syncwarp();
   float scale = 0.f;
   if (lane == 0) scale = rms_scale_seq(row, H, eps);
   scale = __shfl_sync(0xffffffffu, scale, 0);
   const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)H));
-  const size_t o = (size_t)t * H;
   for (int i = lane; i < H; i += 32) {
-    const float v = __fmul_rn(row[i], scale);
+    const float r0 = row[i];
+    if (attn_res) attn_res[o + i] = r0;
+    const float v = __fmul_rn(r0, scale);
     if (x_shared) x_shared[o + i] = ffn_norm ? __fmul_rn(v, ffn_norm[i]) : v;
     if (x_moe) x_moe[o + i] = pre_norm2 ? __fmul_rn(v, pre_norm2[i]) : v;
     if (router_x) {
@@ -1083,16 +1101,16 @@ cudaError_t launch_dense_routing(int32_t* ids, float* probs, int T, cudaStream_t
   return launch_pdl(dense_routing_kernel, dim3(std::min(148, (T + 255) / 256)), dim3(256), 0, s, ids, probs, T);
 }
 
-cudaError_t launch_ffn_prologue(const float* h, const float* ffn_norm, const float* pre_norm2, const float* gis,
-                                float* x_shared, float* x_moe, float* router_x, int H, int T, float eps,
-                                cudaStream_t s) {
+cudaError_t launch_ffn_prologue(const float* hidden, const float* attn, const float* pan, const float* ffn_norm,
+                                const float* pre_norm2, const float* gis, float* attn_res, float* x_shared,
+                                float* x_moe, float* router_x, int H, int T, float eps, cudaStream_t s) {
   static SmemOptIn cache;
   const int r = rms_norm_rows_per_cta(H);
   const size_t smem = (size_t)r * H * 4;
   const cudaError_t st = ensure_smem(ffn_prologue_kernel, smem, cache);
   if (st != cudaSuccess) return st;
-  return launch_pdl(ffn_prologue_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, h, ffn_norm, pre_norm2, gis,
-                    x_shared, x_moe, router_x, H, T, eps);
+  return launch_pdl(ffn_prologue_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, hidden, attn, pan, ffn_norm,
+                    pre_norm2, gis, attn_res, x_shared, x_moe, router_x, H, T, eps);
 }
 
 cudaError_t launch_ffn_epilogue(const float* attn_res, const float* mlp_raw, const float* moe_raw, const float* post1,

@@ -76,9 +76,9 @@ cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t*
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s);
 int rms_norm_rows_per_cta(int H);
 cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, int T, float eps, cudaStream_t s);
-cudaError_t launch_ffn_prologue(const float* h, const float* ffn_norm, const float* pre_norm2, const float* gis,
-                                float* x_shared, float* x_moe, float* router_x, int H, int T, float eps,
-                                cudaStream_t s);
+cudaError_t launch_ffn_prologue(const float* hidden, const float* attn, const float* pan, const float* ffn_norm,
+                                const float* pre_norm2, const float* gis, float* attn_res, float* x_shared,
+                                float* x_moe, float* router_x, int H, int T, float eps, cudaStream_t s);
 cudaError_t launch_ffn_epilogue(const float* attn_res, const float* mlp_raw, const float* moe_raw, const float* post1,
                                 const float* post2, const float* post, float out_scale, float* hidden, int H, int T,
                                 float eps, cudaStream_t s);

@@ -560,31 +560,34 @@ int mrml_moe_combine(const float* ydown, const int32_t* pos, const int32_t* ids,
   return MRML_OK;
 }
 
-int mrml_moe_ffn_prologue(const float* h, const float* ffn_norm, const float* pre_ffw_norm_2,
-                          const float* gate_inp_scale, float* x_shared, float* x_moe, float* router_x, int H, int T,
-                          float eps, mrml_stream_t stream) {
-  if (H <= 0 || T < 0) return MRML_ERR_INVALID_ARGUMENT;
-  if (T == 0) return MRML_OK;
-  if (!h || (!x_shared && !x_moe && !router_x) || !aligned16(h)) return MRML_ERR_INVALID_ARGUMENT;
-  if (mrml::rms_norm_rows_per_cta(H) == 0) return MRML_ERR_UNSUPPORTED;
+// model.rs:1730-1784 use eps = 1e-6 for every norm of the FFN block.
+constexpr float kFfnEps = 1e-6f;
+
+int mrml_moe_ffn_prologue(const float* hidden, const float* attn, const float* post_attn_norm, const float* ffn_norm,
+                          const float* pre_ffw_norm_2, const float* router_scale, float* attn_res, float* shared,
+                          float* moe, float* router, int dim, int batch, mrml_stream_t stream) {
+  if (dim <= 0 || batch < 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return MRML_OK;
+  if (!hidden || (!attn_res && !shared && !moe && !router)) return MRML_ERR_INVALID_ARGUMENT;
+  if (mrml::rms_norm_rows_per_cta(dim) == 0) return MRML_ERR_UNSUPPORTED;
   MRML_TRY(check_device());
   const cudaStream_t s = (cudaStream_t)stream;
-  MRML_LAUNCH(mrml::launch_ffn_prologue(h, ffn_norm, pre_ffw_norm_2, gate_inp_scale, x_shared, x_moe, router_x, H, T,
-                                        eps, s));
+  MRML_LAUNCH(mrml::launch_ffn_prologue(hidden, attn, post_attn_norm, ffn_norm, pre_ffw_norm_2, router_scale,
+                                        attn_res, shared, moe, router, dim, batch, kFfnEps, s));
   return MRML_OK;
 }
 
-int mrml_moe_ffn_epilogue(const float* attn_res, const float* mlp_raw, const float* moe_raw,
-                          const float* post_ffw_norm_1, const float* post_ffw_norm_2, const float* post_ffw_norm,
-                          float layer_output_scale, float* hidden, int H, int T, float eps, mrml_stream_t stream) {
-  if (H <= 0 || T < 0) return MRML_ERR_INVALID_ARGUMENT;
-  if (T == 0) return MRML_OK;
-  if (!attn_res || !moe_raw || !hidden) return MRML_ERR_INVALID_ARGUMENT;
-  if (mrml::rms_norm_rows_per_cta(2 * H) == 0) return MRML_ERR_UNSUPPORTED;
+int mrml_moe_ffn_epilogue(const float* attn_res, const float* dense, const float* moe, const float* post_ffw_norm_1,
+                          const float* post_ffw_norm_2, const float* post_ffw_norm, float* output, float layer_scale,
+                          int dim, int batch, mrml_stream_t stream) {
+  if (dim <= 0 || batch < 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return MRML_OK;
+  if (!attn_res || !moe || !output) return MRML_ERR_INVALID_ARGUMENT;
+  if (mrml::rms_norm_rows_per_cta(2 * dim) == 0) return MRML_ERR_UNSUPPORTED;
   MRML_TRY(check_device());
   const cudaStream_t s = (cudaStream_t)stream;
-  MRML_LAUNCH(mrml::launch_ffn_epilogue(attn_res, mlp_raw, moe_raw, post_ffw_norm_1, post_ffw_norm_2, post_ffw_norm,
-                                        layer_output_scale, hidden, H, T, eps, s));
+  MRML_LAUNCH(mrml::launch_ffn_epilogue(attn_res, dense, moe, post_ffw_norm_1, post_ffw_norm_2, post_ffw_norm,
+                                        layer_scale, output, dim, batch, kFfnEps, s));
   return MRML_OK;
 }
 

@@ -227,9 +227,13 @@ class ExpertParallelLayer:
             self.peer.close()
             self.peer = None
 
-    def forward(self, router_w, x_home, gate_up, down, out_home, down_scale: Optional[torch.Tensor] = None):
+    def forward(self, router_w, x_home, gate_up, down, out_home, down_scale: Optional[torch.Tensor] = None,
+                router_x: Optional[torch.Tensor] = None):
+        """One layer step; router_x is the router's input (model.rs:1774-1784)
+        when it differs from the experts' input x_home."""
         m = self.moe
-        m.router(router_w, x_home, self.logits, self.ids, self.probs, self.H, self.E, self.K, self.T, self.router_ws)
+        m.router(router_w, x_home if router_x is None else router_x, self.logits, self.ids, self.probs, self.H,
+                 self.E, self.K, self.T, self.router_ws)
         if self.peer is not None:
             args = (self.peer.slabs, self.rank, self.world, self.T, self.H)
             m.ep_dispatch(*args, self.E, self.K, x_home, self.ids, self.probs)

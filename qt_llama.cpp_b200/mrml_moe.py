@@ -74,8 +74,8 @@ SIGNATURES = {
     "mrml_moe_set_option": (_i, [_i, _i]),
     "mrml_moe_weights_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "mrml_moe_prepare_weights": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
-    "mrml_moe_ffn_prologue": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp]),
-    "mrml_moe_ffn_epilogue": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _i, _i, _f, _vp]),
+    "mrml_moe_ffn_prologue": (_i, [_vp] * 10 + [_i, _i, _vp]),
+    "mrml_moe_ffn_epilogue": (_i, [_vp] * 7 + [_f, _i, _i, _vp]),
     "mrml_moe_dense_ffn_workspace_bytes": (_sz, [_i, _i, _i]),
     "mrml_moe_dense_ffn": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "mrml_moe_gguf_open": (_i, [_c.c_char_p, _c.POINTER(_vp)]),
@@ -286,18 +286,22 @@ def combine(ydown, pos, ids, probs, down_scale, out, H, K, T, stream=None):
     )
 
 
-def ffn_prologue(h, ffn_norm, pre_ffw_norm_2, gate_inp_scale, x_shared, x_moe, router_x, H, T, eps=1e-6,
-                 stream=None):
+def ffn_prologue(hidden, attn, post_attn_norm, ffn_norm, pre_ffw_norm_2, router_scale, attn_res, shared, moe_in,
+                 router_in, dim, batch, stream=None):
+    """mrml_moe_ffn_prologue (the reference's prepare_ffn_batch argument
+    order); None for an absent input or output."""
     _check("mrml_moe_ffn_prologue",
-           load_library().mrml_moe_ffn_prologue(_ptr(h), _ptr(ffn_norm), _ptr(pre_ffw_norm_2), _ptr(gate_inp_scale),
-                                                _ptr(x_shared), _ptr(x_moe), _ptr(router_x), H, T, eps,
+           load_library().mrml_moe_ffn_prologue(*[_ptr(a) for a in (hidden, attn, post_attn_norm, ffn_norm,
+                                                                    pre_ffw_norm_2, router_scale, attn_res, shared,
+                                                                    moe_in, router_in)], dim, batch,
                                                 _stream_ptr(stream)))
 
 
-def ffn_epilogue(attn_res, mlp_raw, moe_raw, post1, post2, post, out_scale, hidden, H, T, eps=1e-6, stream=None):
+def ffn_epilogue(attn_res, dense, moe_out, post1, post2, post, output, layer_scale, dim, batch, stream=None):
+    """mrml_moe_ffn_epilogue (the reference's finish_ffn_batch order)."""
     _check("mrml_moe_ffn_epilogue",
-           load_library().mrml_moe_ffn_epilogue(_ptr(attn_res), _ptr(mlp_raw), _ptr(moe_raw), _ptr(post1),
-                                                _ptr(post2), _ptr(post), out_scale, _ptr(hidden), H, T, eps,
+           load_library().mrml_moe_ffn_epilogue(*[_ptr(a) for a in (attn_res, dense, moe_out, post1, post2, post,
+                                                                    output)], float(layer_scale), dim, batch,
                                                 _stream_ptr(stream)))
 
 
@@ -537,6 +541,29 @@ class MoeDevice:
         E = n_experts or self._infer_experts(gate_up, dim, exp_dim, wtype)
         ws = self.reserve(dim, exp_dim, E, n_active, batch)
         experts(wtype, gate_up, down, ids, weights, scales, input, output, dim, exp_dim, E, n_active, batch, ws)
+
+    # cuda.rs:2914-2947 (batch 1) and 2949-2985
+    def prepare_ffn(self, hidden, attn_proj, post_attn_norm, ffn_norm, pre_ffw_norm_2, router_scale, attn_res,
+                    shared_in, moe_in, router_in, dim):
+        ffn_prologue(hidden, attn_proj, post_attn_norm, ffn_norm, pre_ffw_norm_2, router_scale, attn_res, shared_in,
+                     moe_in, router_in, dim, 1)
+
+    def prepare_ffn_batch(self, hidden, attn, pan, ffn, pfn, router_scale, attn_res, shared, moe_in, router_in, dim,
+                          batch):
+        assert hidden.numel() == dim * batch
+        assert attn.numel() == dim * batch
+        ffn_prologue(hidden, attn, pan, ffn, pfn, router_scale, attn_res, shared, moe_in, router_in, dim, batch)
+
+    # cuda.rs:2987-3016 (batch 1) and 3018-3050
+    def finish_ffn(self, attn_res, dense, moe_out, post_ffw_norm_1, post_ffw_norm_2, post_ffw_norm, hidden_out,
+                   layer_scale, dim):
+        ffn_epilogue(attn_res, dense, moe_out, post_ffw_norm_1, post_ffw_norm_2, post_ffw_norm, hidden_out,
+                     layer_scale, dim, 1)
+
+    def finish_ffn_batch(self, attn_res, dense, moe_out, p1, p2, pf, output, scale, dim, batch):
+        assert attn_res.numel() == dim * batch
+        assert output.numel() == dim * batch
+        ffn_epilogue(attn_res, dense, moe_out, p1, p2, pf, output, scale, dim, batch)
 
     @staticmethod
     def _infer_experts(gate_up, dim, exp_dim, wtype):

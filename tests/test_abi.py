@@ -85,15 +85,13 @@ def test_invalid_arguments_rejected_without_a_gpu(moe):
     assert lib.mrml_moe_rms_norm(ctypes.c_void_p(0x1004), None, P, 64, 1, ctypes.c_float(1e-6), None) == -1
     assert lib.mrml_moe_rms_norm(P, None, P, 1 << 20, 1, ctypes.c_float(1e-6), None) == -2
     # FFN prologue / epilogue and the shared dense MLP.
-    eps = ctypes.c_float(1e-6)
-    assert lib.mrml_moe_ffn_prologue(P, None, None, None, None, None, None, 2816, 1, eps, None) == -1  # no output
-    assert lib.mrml_moe_ffn_prologue(ctypes.c_void_p(0x1004), None, None, None, P, None, None, 2816, 1, eps,
-                                     None) == -1
-    assert lib.mrml_moe_ffn_prologue(P, None, None, None, P, None, None, 1 << 20, 1, eps, None) == -2
-    assert lib.mrml_moe_ffn_prologue(None, None, None, None, None, None, None, 2816, 0, eps, None) == 0
-    assert lib.mrml_moe_ffn_epilogue(P, None, None, None, None, None, ctypes.c_float(1), P, 2816, 1, eps, None) == -1
-    assert lib.mrml_moe_ffn_epilogue(P, None, P, None, None, None, ctypes.c_float(1), P, 1 << 20, 1, eps,
-                                     None) == -2
+    N = None
+    assert lib.mrml_moe_ffn_prologue(P, P, N, N, N, N, N, N, N, N, 2816, 1, None) == -1  # no output
+    assert lib.mrml_moe_ffn_prologue(N, P, N, N, N, N, P, N, N, N, 2816, 1, None) == -1  # no hidden
+    assert lib.mrml_moe_ffn_prologue(P, N, N, N, N, N, P, N, N, N, 1 << 20, 1, None) == -2
+    assert lib.mrml_moe_ffn_prologue(N, N, N, N, N, N, N, N, N, N, 2816, 0, None) == 0
+    assert lib.mrml_moe_ffn_epilogue(P, N, N, N, N, N, P, ctypes.c_float(1), 2816, 1, None) == -1  # no moe
+    assert lib.mrml_moe_ffn_epilogue(P, N, P, N, N, N, P, ctypes.c_float(1), 1 << 20, 1, None) == -2
     assert lib.mrml_moe_dense_ffn_workspace_bytes(2816, 2112, 64) > 0
     assert lib.mrml_moe_dense_ffn_workspace_bytes(0, 2112, 64) == 0
     assert lib.mrml_moe_dense_ffn(2, P, P, P, P, 2816, 2100, 1, P, 1 << 30, None) == -1  # I % 32

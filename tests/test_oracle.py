@@ -272,9 +272,13 @@ def test_ffn_prologue_epilogue_restatement(oracle):
     rng = np.random.default_rng(3)
     T, H = 3, 96
     f = np.float32
-    h = rng.standard_normal((T, H)).astype(f)
-    w1, w2, w3 = (1 + 0.1 * rng.standard_normal((3, H))).astype(f)
-    xs, xm, rx = oracle.ffn_prologue(h, w1, w2, w3)
+    hid = rng.standard_normal((T, H)).astype(f)
+    attn = (0.5 * rng.standard_normal((T, H))).astype(f)
+    w0, w1, w2, w3 = (1 + 0.1 * rng.standard_normal((4, H))).astype(f)
+    res, xs, xm, rx = oracle.ffn_prologue(hid, attn, w0, w1, w2, w3)
+    h = hid + _rms_rows_f32(attn, w0, 1e-6)
+    assert np.array_equal(res, h)
+    assert np.array_equal(oracle.ffn_prologue(h, None, None, w1, None, None)[1], _rms_rows_f32(h, w1, 1e-6))
     assert np.array_equal(xs, _rms_rows_f32(h, w1, 1e-6))
     assert np.array_equal(xm, _rms_rows_f32(h, w2, 1e-6))
     inv = f(f(1) / np.sqrt(f(H)))
