@@ -189,7 +189,7 @@ int mrml_moe_experts_shard(int wtype, const uint8_t *gate_up, const uint8_t *dow
  * MRML_ERR_DEVICE_TIMEOUT's device code into the workspace's status word
  * (read with mrml_moe_device_status) and leaves the data it would have
  * produced untouched.  All ranks must make the same calls with the same
- * shapes; H a multiple of 32, E a multiple of N, N <= 16; the experts need
+ * shapes; H a multiple of 32, x 16-byte aligned, E a multiple of N, N <= 16; the experts need
  * the decode kernel's shapes (H a multiple of 256, I of 64).  The workspace
  * (mrml_moe_ep_workspace_bytes, 256-byte aligned, zeroed once with
  * mrml_moe_workspace_init) serves mrml_moe_ep_experts and

@@ -140,18 +140,20 @@ __device__ __forceinline__ unsigned int owner_mask(const int32_t* __restrict__ i
   return __reduce_or_sync(0xffffffffu, m);
 }
 
-// Dispatch push.  One warp per (home token, 32-element block): the block is
-// quantised to Q8_0 (quant.rs:193-228, as quantize_rows_kernel does) and its
-// 32 values and f16 scale are stored into every rank that owns one of the
-// token's experts.  Threads [0, T*K) of the grid also store the ids and
-// weights of all home tokens into every rank.
+// Dispatch push.  One warp per (home token, 128-element chunk of 4 quant
+// blocks): lane l holds elements [4l, 4l+4) of the chunk, so block l / 8 is
+// quantised to Q8_0 by 8 lanes (quant.rs:193-228, as quantize_rows_kernel
+// does) and the chunk's 128 value bytes leave as one coalesced 128-byte
+// store per destination: every rank that owns one of the token's experts.
+// Threads [0, T*K) of the grid also store the ids and weights of all home
+// tokens into every rank.
 __global__ void dispatch_push_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int E, int K,
                                      const float* __restrict__ x, const int32_t* __restrict__ ids,
                                      const float* __restrict__ probs) {
   Control* mine = reinterpret_cast<Control*>(slabs[rank]);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int par = mine->step & 1u;
-  const int lane = threadIdx.x & 31, nb = H / 32;
+  const int lane = threadIdx.x & 31, nb = H / 32, nch = (nb + 3) / 4;
   const size_t slot = ((size_t)par * N + rank) * T;  // first row of this rank's slot
   const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (gtid < (long long)T * K) {
@@ -163,31 +165,39 @@ __global__ void dispatch_push_kernel(uint8_t* const* __restrict__ slabs, int ran
     }
   }
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < (long long)T * nb;
+  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < (long long)T * nch;
        w += warps) {
-    const int t = (int)(w / nb), b = (int)(w % nb);
+    const int t = (int)(w / nch), c = (int)(w % nch);
     const unsigned int mask = owner_mask(ids, probs, t, K, E, N);
     if (mask == 0) continue;  // warp-uniform
-    const float v = x[(size_t)t * H + 32 * b + lane];
-    float amax = fabsf(v);
-    if (!(amax > 0.f)) amax = 0.f;
+    const int b = 4 * c + (lane >> 3);  // this lane's quant block
+    const bool in = b < nb;             // uniform over the block's 8 lanes
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (in) v = *reinterpret_cast<const float4*>(x + (size_t)t * H + 128 * c + 4 * (lane & 31));
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    float amax = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int i = 0; i < 4; ++i) {
+      const float a = fabsf(e[i]);
+      amax = fmaxf(amax, a > 0.f ? a : 0.f);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float scale = __fdiv_rn(amax, 127.0f);
     const uint32_t d16 = f32_to_f16_trunc(scale);
-    const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
-    float r = round_half_away(__fmul_rn(v, id));
-    if (r != r) r = 0.f;
-    r = fminf(fmaxf(r, -128.f), 127.f);
-    // four lanes' bytes into one word, held by the lane with (lane & 3) == 0
-    uint32_t word = ((uint32_t)(int)r & 0xffu) << (8 * (lane & 3));
-    word |= __shfl_xor_sync(0xffffffffu, word, 1);
-    word |= __shfl_xor_sync(0xffffffffu, word, 2);
+    const float inv = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float r = round_half_away(__fmul_rn(e[i], inv));
+      if (r != r) r = 0.f;
+      r = fminf(fmaxf(r, -128.f), 127.f);
+      word |= ((uint32_t)(int)r & 0xffu) << (8 * i);
+    }
     for (int q = 0; q < N; ++q) {
-      if (!(mask >> q & 1u)) continue;
-      if ((lane & 3) == 0)
-        reinterpret_cast<uint32_t*>(slabs[q] + L.q + (slot + t) * H + 32 * b)[lane >> 2] = word;
-      if (lane == 0) reinterpret_cast<uint16_t*>(slabs[q] + L.d)[(slot + t) * nb + b] = (uint16_t)d16;
+      if (!(mask >> q & 1u) || !in) continue;
+      reinterpret_cast<uint32_t*>(slabs[q] + L.q + (slot + t) * H + 128 * c)[lane] = word;
+      if ((lane & 7) == 0) reinterpret_cast<uint16_t*>(slabs[q] + L.d)[(slot + t) * nb + b] = (uint16_t)d16;
     }
   }
   push_done(mine, slabs, rank, N, 0);
@@ -266,43 +276,67 @@ __global__ void recv_gather_kernel(const uint8_t* const* __restrict__ rows, cons
   }
 }
 
-// Combine push.  One warp per received token slot j = src * T + t: if this
-// rank computed any of its pairs, the warp forms the slot-ordered partial
+// Combine push.  CTA (j, c) for received token slot j = src * T + t and
+// chunk c of kCombThreads float4 columns: if this rank computed any of the
+// token's pairs, each thread forms its 4 columns of the slot-ordered partial
 // (sum over k ascending of (alpha_k * ydown[pos]) * scale[id], from 0; the
-// single-device combine's arithmetic, model.rs:2163-2165) and stores it
+// single-device combine's arithmetic, model.rs:2163-2165) and stores them
 // into rank src's partial area.
-__global__ void combine_push_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int K,
-                                    const float* __restrict__ ydown, const int32_t* __restrict__ pos,
-                                    const int32_t* __restrict__ ids_all, const float* __restrict__ probs_all,
-                                    const float* __restrict__ down_scale) {
+constexpr int kCombThreads = 128;
+
+__global__ void __launch_bounds__(kCombThreads)
+    combine_push_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int K,
+                        const float* __restrict__ ydown, const int32_t* __restrict__ pos,
+                        const int32_t* __restrict__ ids_all, const float* __restrict__ probs_all,
+                        const float* __restrict__ down_scale) {
+  __shared__ int s_pos[kMaxTopK];
+  __shared__ float s_alpha[kMaxTopK], s_sc[kMaxTopK];
+  __shared__ int s_n;
   pdl_wait();
   Control* mine = reinterpret_cast<Control*>(slabs[rank]);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int par = mine->step & 1u;
-  const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long j = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); j < (long long)N * T;
-       j += warps) {
-    bool any = false;
-    for (int k = lane; k < K; k += 32) any |= pos[j * K + k] >= 0;
-    if (!__any_sync(0xffffffffu, any)) continue;
-    const int src = (int)(j / T), t = (int)(j % T);
-    float4* dst = reinterpret_cast<float4*>(slabs[src] + L.part) + (((size_t)par * N + rank) * T + t) * (H / 4);
-    for (int i4 = lane; i4 < H / 4; i4 += 32) {
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int k = 0; k < K; ++k) {
-        const int p = pos[j * K + k];
-        if (p < 0) continue;
-        const float alpha = probs_all[j * K + k];
-        const float sc = down_scale ? down_scale[ids_all[j * K + k]] : 1.0f;
-        const float4 y = reinterpret_cast<const float4*>(ydown + (size_t)p * H)[i4];
-        o.x = __fadd_rn(o.x, __fmul_rn(__fmul_rn(alpha, y.x), sc));
-        o.y = __fadd_rn(o.y, __fmul_rn(__fmul_rn(alpha, y.y), sc));
-        o.z = __fadd_rn(o.z, __fmul_rn(__fmul_rn(alpha, y.z), sc));
-        o.w = __fadd_rn(o.w, __fmul_rn(__fmul_rn(alpha, y.w), sc));
+  const long long j = blockIdx.x;
+  // the token's pairs here, in slot order
+  if (threadIdx.x < 32) {
+    int n = 0;
+    for (int k0 = 0; k0 < K; k0 += 32) {
+      const int k = k0 + (int)threadIdx.x;
+      const int p = k < K ? pos[j * K + k] : -1;
+      const unsigned int bal = __ballot_sync(0xffffffffu, p >= 0);
+      if (p >= 0) {
+        const int at = n + __popc(bal & ((1u << threadIdx.x) - 1u));
+        s_pos[at] = p;
+        s_alpha[at] = probs_all[j * K + k];
+        s_sc[at] = down_scale ? down_scale[ids_all[j * K + k]] : 1.0f;
       }
-      dst[i4] = o;
+      n += __popc(bal);
     }
+    if (threadIdx.x == 0) s_n = n;
+  }
+  __syncthreads();
+  const int n = s_n;
+  const int i4 = blockIdx.y * kCombThreads + threadIdx.x;
+  if (n > 0 && i4 < H / 4) {
+    const int src = (int)(j / T), t = (int)(j % T);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < n; k0 += 4) {
+      float4 y[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (k0 + u < n) y[u] = reinterpret_cast<const float4*>(ydown + (size_t)s_pos[k0 + u] * H)[i4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (k0 + u >= n) break;
+        const float a = s_alpha[k0 + u], sc = s_sc[k0 + u];
+        o.x = __fadd_rn(o.x, __fmul_rn(__fmul_rn(a, y[u].x), sc));
+        o.y = __fadd_rn(o.y, __fmul_rn(__fmul_rn(a, y[u].y), sc));
+        o.z = __fadd_rn(o.z, __fmul_rn(__fmul_rn(a, y[u].z), sc));
+        o.w = __fadd_rn(o.w, __fmul_rn(__fmul_rn(a, y[u].w), sc));
+      }
+    }
+    float4* dst = reinterpret_cast<float4*>(slabs[src] + L.part) + (((size_t)par * N + rank) * T + t) * (H / 4);
+    dst[i4] = o;
   }
   push_done(mine, slabs, rank, N, 1);
 }
@@ -310,48 +344,53 @@ __global__ void combine_push_kernel(uint8_t* const* __restrict__ slabs, int rank
 // Reduce: waits for the N combine pushes of this step, then out[t] = the
 // partials of the ranks that own one of t's experts, summed in rank order
 // (0 for a token with no pair); the last CTA to finish advances the step.
-// One warp per home token.  After a timeout `out` is left untouched.
-__global__ void combine_reduce_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int E, int K,
-                                      const int32_t* __restrict__ ids, const float* __restrict__ probs,
-                                      float4* __restrict__ out, unsigned int limit, int* __restrict__ err) {
+// CTA (t, c) per home token and chunk of float4 columns.  After a timeout
+// `out` is left untouched.
+__global__ void __launch_bounds__(kCombThreads)
+    combine_reduce_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int E, int K,
+                          const int32_t* __restrict__ ids, const float* __restrict__ probs, float4* __restrict__ out,
+                          unsigned int limit, int* __restrict__ err) {
   __shared__ int ok;
+  __shared__ unsigned int s_mask;
   uint8_t* mine_b = slabs[rank];
   Control* mine = reinterpret_cast<Control*>(mine_b);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int step = mine->step, par = step & 1u;
-  if (threadIdx.x == 0) ok = wait_counts(mine->comb, N, step + 1, limit, err) ? 1 : 0;
+  const int t = blockIdx.x;
+  if (threadIdx.x < 32) {
+    const unsigned int m = owner_mask(ids, probs, t, K, E, N);
+    if (threadIdx.x == 0) {
+      s_mask = m;
+      ok = wait_counts(mine->comb, N, step + 1, limit, err) ? 1 : 0;
+    }
+  }
   __syncthreads();
-  if (ok) {
-    const int lane = threadIdx.x & 31;
+  const int i4 = blockIdx.y * kCombThreads + threadIdx.x;
+  if (ok && i4 < H / 4) {
+    const unsigned int mask = s_mask;
     const float4* part = reinterpret_cast<const float4*>(mine_b + L.part) + (size_t)par * N * T * (H / 4);
-    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    for (long long t = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
-      const unsigned int mask = owner_mask(ids, probs, (int)t, K, E, N);
-      for (int i4 = lane; i4 < H / 4; i4 += 32) {
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        bool first = true;
-        for (int q = 0; q < N; ++q) {
-          if (!(mask >> q & 1u)) continue;
-          const float4 v = part[((size_t)q * T + t) * (H / 4) + i4];
-          if (first) {
-            o = v;
-            first = false;
-          } else {
-            o.x = __fadd_rn(o.x, v.x);
-            o.y = __fadd_rn(o.y, v.y);
-            o.z = __fadd_rn(o.z, v.z);
-            o.w = __fadd_rn(o.w, v.w);
-          }
-        }
-        out[(size_t)t * (H / 4) + i4] = o;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool first = true;
+    for (int q = 0; q < N; ++q) {
+      if (!(mask >> q & 1u)) continue;
+      const float4 v = part[((size_t)q * T + t) * (H / 4) + i4];
+      if (first) {
+        o = v;
+        first = false;
+      } else {
+        o.x = __fadd_rn(o.x, v.x);
+        o.y = __fadd_rn(o.y, v.y);
+        o.z = __fadd_rn(o.z, v.z);
+        o.w = __fadd_rn(o.w, v.w);
       }
     }
+    out[(size_t)t * (H / 4) + i4] = o;
   }
   // Every CTA has read the step count; the last one advances it.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned int n = gridDim.x;
+    const unsigned int n = gridDim.x * gridDim.y;
     if (atomicAdd(&mine->done_reduce, 1u) == n - 1) {
       mine->done_reduce = 0;
       mine->step = step + 1;
@@ -376,7 +415,7 @@ void ep_set_spin_limit(unsigned int limit) { ep::g_spin_limit.store(limit ? limi
 
 cudaError_t launch_ep_dispatch(uint8_t* const* slabs, int rank, int N, int T, int H, int E, int K, const float* x,
                                const int32_t* ids, const float* probs, cudaStream_t s) {
-  const long long warps = (long long)T * (H / 32);
+  const long long warps = (long long)T * ((H / 32 + 3) / 4);
   const int grid = std::max(ep::grid_for(warps, 8), ep::grid_for((long long)T * K, 256));
   ep::dispatch_push_kernel<<<grid, 256, 0, s>>>(slabs, rank, N, T, H, E, K, x, ids, probs);
   return cudaPeekAtLastError();
@@ -400,15 +439,17 @@ cudaError_t launch_ep_gather(int wtype, const uint8_t* const* rows, const int32_
 cudaError_t launch_ep_combine_push(uint8_t* const* slabs, int rank, int N, int T, int H, int K, const float* ydown,
                                    const int32_t* pos, const int32_t* ids_all, const float* probs_all,
                                    const float* down_scale, cudaStream_t s) {
-  return launch_pdl(ep::combine_push_kernel, dim3(ep::grid_for((long long)N * T, 8)), dim3(256), 0, s, slabs, rank,
-                    N, T, H, K, ydown, pos, ids_all, probs_all, down_scale);
+  const dim3 grid((unsigned)(N * T), (unsigned)((H / 4 + ep::kCombThreads - 1) / ep::kCombThreads));
+  return launch_pdl(ep::combine_push_kernel, grid, dim3(ep::kCombThreads), 0, s, slabs, rank, N, T, H, K, ydown, pos,
+                    ids_all, probs_all, down_scale);
 }
 
 cudaError_t launch_ep_reduce(uint8_t* const* slabs, int rank, int N, int T, int H, int E, int K, const int32_t* ids,
                              const float* probs, float* out, int* err, cudaStream_t s) {
-  ep::combine_reduce_kernel<<<ep::grid_for(T, 8), 256, 0, s>>>(slabs, rank, N, T, H, E, K, ids, probs,
-                                                                 reinterpret_cast<float4*>(out),
-                                                                 ep::g_spin_limit.load(), err);
+  const dim3 grid((unsigned)T, (unsigned)((H / 4 + ep::kCombThreads - 1) / ep::kCombThreads));
+  ep::combine_reduce_kernel<<<grid, ep::kCombThreads, 0, s>>>(slabs, rank, N, T, H, E, K, ids, probs,
+                                                               reinterpret_cast<float4*>(out),
+                                                               ep::g_spin_limit.load(), err);
   return cudaPeekAtLastError();
 }
 

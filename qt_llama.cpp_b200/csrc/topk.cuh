@@ -49,6 +49,29 @@ __device__ __forceinline__ void warp_topk(const float (&val)[PL], int E, int K, 
   __syncwarp();
 }
 
+// The reference's softmax over a token's K selected experts, already ordered
+// by (value desc, id asc) in cand / cval (one warp):
+// model.rs:1819-1829: p_k = expf(l_k - l_0), summed in k order, then divided
+// by max(sum, 1e-6).  Lanes compute the exponentials in parallel; lane 0
+// adds them in k order.
+__device__ inline void softmax_sorted(const int* cand, float* cval, int K, int t, int32_t* ids, float* probs) {
+  const int lane = threadIdx.x & 31;
+  const float max_l = cval[0];
+  __syncwarp();
+  for (int k = lane; k < K; k += 32) cval[k] = exp_f32(__fsub_rn(cval[k], max_l));
+  __syncwarp();
+  float sum = 0.f;
+  if (lane == 0)
+    for (int k = 0; k < K; ++k) sum = __fadd_rn(sum, cval[k]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  const float denom = sum > 1e-6f ? sum : 1e-6f;
+  for (int k = lane; k < K; k += 32) {
+    ids[(size_t)t * K + k] = cand[k];
+    probs[(size_t)t * K + k] = __fdiv_rn(cval[k], denom);
+  }
+  __syncwarp();
+}
+
 // Per-token selection tail: order Z (count candidates) by (value desc, id
 // asc), then the reference's softmax over the first K.
 __device__ inline void finish_token(int* cand, float* cval, int count, int K, int t, int32_t* ids, float* probs) {
@@ -68,23 +91,7 @@ __device__ inline void finish_token(int* cand, float* cval, int count, int K, in
     }
   }
   __syncwarp();
-  // model.rs:1819-1829: p_k = expf(l_k - l_0), summed in k order, then
-  // divided by max(sum, 1e-6).  Lanes compute the exponentials in parallel;
-  // lane 0 adds them in k order.
-  const float max_l = cval[0];
-  __syncwarp();
-  for (int k = lane; k < K; k += 32) cval[k] = exp_f32(__fsub_rn(cval[k], max_l));
-  __syncwarp();
-  float sum = 0.f;
-  if (lane == 0)
-    for (int k = 0; k < K; ++k) sum = __fadd_rn(sum, cval[k]);
-  sum = __shfl_sync(0xffffffffu, sum, 0);
-  const float denom = sum > 1e-6f ? sum : 1e-6f;
-  for (int k = lane; k < K; k += 32) {
-    ids[(size_t)t * K + k] = cand[k];
-    probs[(size_t)t * K + k] = __fdiv_rn(cval[k], denom);
-  }
-  __syncwarp();
+  softmax_sorted(cand, cval, K, t, ids, probs);
 }
 
 }  // namespace mrml

@@ -325,9 +325,11 @@ def c2_q4(cuda, moe, synth):
     return gu.cpu().numpy(), dn.cpu().numpy()
 
 
-@pytest.mark.parametrize("T", [1, 8, 64])
+@pytest.mark.parametrize("T", [1, 4, 8, 32, 64])
 def test_config2_forward(cuda, moe, oracle, synth, c2_q4, T, expert_path):
-    """Config 2: H=2816, E=128, K=8, I=704, Q4_0, T in {1, 8, 64}."""
+    """Config 2: H=2816, E=128, K=8, I=704, Q4_0, T in {1, 8, 64}, plus 4
+    and 32 (the largest batch whose experts the dispatch kernel selects
+    itself; config 5's per-layer batch)."""
     H, I, E, K = 2816, 704, 128, 8
     gu, dn = c2_q4
     W = synth.normal(33, E * H, 0.02).reshape(E, H)
