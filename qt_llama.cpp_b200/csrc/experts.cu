@@ -19,6 +19,8 @@
 // rows from HBM exactly once with the TMA bulk-copy engine, then applies it
 // to every token routed to that expert.  Integer block dots use dp4a; the
 // int32 block sum becomes an f32 through the 1.5*2^23 bit trick.
+#include <initializer_list>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "topk.cuh"
@@ -126,10 +128,14 @@ constexpr int kDispatchThreads = 1024;
 
 //
 // With `logits` (small batches: T = n_pairs / K <= 32 tokens, E <= 256) the
-// kernel first selects each token's experts itself, one warp per token, as
-// router_topk_kernel does, and writes ids and probs; the rest of the kernel
-// reads them back (global writes of the CTA are visible to it after the
-// barrier).  That saves the top-k launch on the decode path.
+// kernel first selects each token's experts itself and writes ids and probs;
+// the rest of the kernel reads them back (global writes of the CTA are
+// visible to it after the barrier).  That saves the top-k launch on the
+// decode path.  The selection is the same as router_topk_kernel's, computed
+// by rank: with the token's logits in shared memory, the thread of (t, e)
+// counts the experts that come before e in the (value desc, id asc) order,
+// and an expert of rank r < K lands in slot r; then one warp per token runs
+// the reference's softmax over the K slots.
 __global__ void __launch_bounds__(kDispatchThreads)
     dispatch_kernel(int32_t* ids, float* probs, int n_pairs, int E, int e_first, int e_total,
                     int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
@@ -137,32 +143,43 @@ __global__ void __launch_bounds__(kDispatchThreads)
                     int* __restrict__ n_units, int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn,
                     int* __restrict__ err, const float* __restrict__ logits, int K) {
   pdl_trigger();
+  // Dynamic shared memory (dispatch_smem_bytes): the counting sort's arrays,
+  // then, when the kernel selects the experts, the logits and the slots.
   extern __shared__ int32_t dsm[];
+  const int WS = E + 1;          // row stride of wcnt (odd: the scan's column reads hit distinct banks)
   int32_t* cnt = dsm;            // [E] totals
   int32_t* base = dsm + E;       // [E] running position of the next pair of expert e
   int32_t* ubase = dsm + 2 * E;  // [E] first gate/up unit of expert e (times mt)
-  int32_t* wcnt = dsm + 3 * E;   // [32][E] per-warp counts of the current chunk
-  int32_t* ubase_dn = dsm + 35 * E;  // [E] first down unit of expert e (times mt)
+  int32_t* ubase_dn = dsm + 3 * E;  // [E] first down unit of expert e (times mt)
+  int32_t* wcnt = dsm + 4 * E;   // [32][WS] per-warp counts of the current chunk
   __shared__ int s_npos;         // positions in use (padded segments)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // Shared memory is this CTA's own: cleared while the previous kernel ends.
-  for (int i = tid; i < E * 36; i += blockDim.x) dsm[i] = 0;
+  for (int i = tid; i < 4 * E + 32 * WS; i += blockDim.x) dsm[i] = 0;
   pdl_wait();
   if (logits != nullptr) {
-    __shared__ int tk_cand[kDispatchThreads / 32][kMaxCandidates];
-    __shared__ float tk_cval[kDispatchThreads / 32][kMaxCandidates];
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, T = n_pairs / K;
-    if (w < T) {
-      float val[8];
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int e = l + 32 * m;
-        val[m] = e < E ? logits[(size_t)w * E + e] : -INFINITY;
+    const int T = n_pairs / K;
+    float* lg = reinterpret_cast<float*>(dsm + 4 * E + 32 * WS);  // [T][E]
+    int* tk_cand = reinterpret_cast<int*>(lg + T * E);             // [T][K] experts by rank
+    float* tk_cval = reinterpret_cast<float*>(tk_cand + T * K);    // [T][K] their logits
+    for (int i = tid; i < T * E; i += blockDim.x) lg[i] = logits[i];
+    __syncthreads();
+    for (int i = tid; i < T * E; i += blockDim.x) {
+      const int t = i / E, e = i - t * E;
+      const float v = lg[i];
+      const float* row = lg + t * E;
+      int r = 0;
+      for (int f = 0; f < E; ++f) {
+        const float u = row[f];
+        r += (u > v || (u == v && f < e)) ? 1 : 0;
       }
-      uint32_t taken;
-      warp_topk<8>(val, E, K, tk_cand[w], tk_cval[w], taken);
-      finish_token(tk_cand[w], tk_cval[w], K, K, w, ids, probs);
+      if (r < K) {
+        tk_cand[t * K + r] = e;
+        tk_cval[t * K + r] = v;
+      }
     }
+    __syncthreads();
+    if (warp < T) softmax_sorted(tk_cand + warp * K, tk_cval + warp * K, K, warp, ids, probs);
   }
   __syncthreads();
   // The thread's first pair, read once for the count and the scatter.
@@ -246,29 +263,22 @@ __global__ void __launch_bounds__(kDispatchThreads)
   const int npos = s_npos;
   for (int i = tid; i < npos; i += blockDim.x) pair_at[i] = -1;
   // Work units: expert e owns units [ubase[e]*mt, (ubase[e] + nt_e)*mt) of
-  // each product, ordered (row tile m, position tile j), j fastest.  One
-  // thread per unit; the unit's expert is the last e with ubase[e]*mt <= u
-  // (experts without pairs share their successor's base and come first).
-  // base[] still holds the segment starts here.
+  // each product, ordered (row tile m, position tile j), j fastest.
+  // kDispatchThreads / E threads per expert write its units.  base[] still
+  // holds the segment starts here.
   {
-    for (int prod = 0; prod < 2; ++prod) {
-      const int mt = prod == 0 ? mt_gu : mt_dn, rows = prod == 0 ? rows_gu : 128;
-      const int NT = prod == 0 ? NT_gu : NT_dn;
-      const int32_t* ub = prod == 0 ? ubase : ubase_dn;
-      const int nu = ub[E - 1] + (cnt[E - 1] + NT - 1) / NT;
-      int4* units = prod == 0 ? units_gu : units_dn;
-      for (int u = tid; u < nu * mt; u += blockDim.x) {
-        int lo = 0, hi = E - 1;
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (ub[mid] * mt <= u)
-            lo = mid;
-          else
-            hi = mid - 1;
+    const int per = kDispatchThreads / E, e = tid / per, sub = tid - e * per;
+    if (e < E) {
+      const int c = cnt[e];
+      for (int prod = 0; prod < 2; ++prod) {
+        const int mt = prod == 0 ? mt_gu : mt_dn, rows = prod == 0 ? rows_gu : 128;
+        const int NT = prod == 0 ? NT_gu : NT_dn;
+        const int first = (prod == 0 ? ubase : ubase_dn)[e] * mt, nt = (c + NT - 1) / NT;
+        int4* units = prod == 0 ? units_gu : units_dn;
+        for (int local = sub; local < nt * mt; local += per) {
+          const int m = local / nt, j = local - m * nt;
+          units[first + local] = make_int4(e, base[e] + j * NT, min(NT, c - j * NT), m * rows);
         }
-        const int e = lo, c = cnt[e], nt = (c + NT - 1) / NT;
-        const int local = u - ub[e] * mt, m = local / nt, j = local - m * nt;
-        units[u] = make_int4(e, base[e] + j * NT, min(NT, c - j * NT), m * rows);
       }
     }
   }
@@ -284,30 +294,34 @@ __global__ void __launch_bounds__(kDispatchThreads)
     }
     const uint32_t peers = __match_any_sync(0xffffffffu, e);
     const int rank = __popc(peers & ((1u << lane) - 1u));
-    if (e >= 0 && rank == 0) wcnt[warp * E + e] = __popc(peers);
+    if (e >= 0 && rank == 0) wcnt[warp * WS + e] = __popc(peers);
     __syncthreads();
-    for (int x = tid; x < E; x += blockDim.x) {
-      int run = base[x];
-      for (int w = 0; w < 32; ++w) {
-        const int c = wcnt[w * E + x];
-        wcnt[w * E + x] = run;
-        run += c;
+    // per expert, an exclusive scan over the 32 warps' counts (lane = warp)
+    for (int x = warp; x < E; x += 32) {
+      const int c = wcnt[lane * WS + x];
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
       }
-      base[x] = run;
+      const int b = base[x];
+      wcnt[lane * WS + x] = b + incl - c;
+      __syncwarp();
+      if (lane == 31) base[x] = b + incl;
     }
     __syncthreads();
     if (e >= 0) {
-      const int dst = wcnt[warp * E + e] + rank;
+      const int dst = wcnt[warp * WS + e] + rank;
       pair_at[dst] = p;
       pos[p] = dst;
     }
     __syncthreads();
-    for (int i = tid; i < 32 * E; i += blockDim.x) wcnt[i] = 0;
+    for (int i = tid; i < 32 * WS; i += blockDim.x) wcnt[i] = 0;
     __syncthreads();
   }
 }
 
-// ---------------------------------------------------------------------------
 // Dispatch for large batches, in three launches over chunks of
 // kDispatchThreads pairs (the single-CTA kernel above walks the chunks one
 // after another; at 65k pairs that alone took ~0.3 ms).  The result is the
@@ -897,6 +911,37 @@ __device__ __forceinline__ float rms_scale_seq(const float* row, int H, float ep
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), eps)));
 }
 
+// Row kernels (FFN prologue / epilogue, RMS norm): one CTA of kRowThreads
+// threads per row.  The row is staged in shared memory, one thread runs each
+// sequential sum of squares over it (the order decides the rounding), and all
+// threads do the elementwise work, four elements at a time when `vec` (H a
+// multiple of 4 and every row pointer 16-byte aligned).
+constexpr int kRowThreads = 128;
+
+// Four consecutive elements of an optional weight (absent: 1).
+__device__ __forceinline__ float4 ld4w(const float* w, int i) {
+  return w ? *reinterpret_cast<const float4*>(w + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+}
+__device__ __forceinline__ float4 ld4(const float* p, int i) { return *reinterpret_cast<const float4*>(p + i); }
+__device__ __forceinline__ void st4(float* p, int i, float4 v) { *reinterpret_cast<float4*>(p + i) = v; }
+__device__ __forceinline__ float4 mul4(float4 a, float4 b) {
+  return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
+}
+__device__ __forceinline__ float4 mul4s(float4 a, float s) {
+  return make_float4(__fmul_rn(a.x, s), __fmul_rn(a.y, s), __fmul_rn(a.z, s), __fmul_rn(a.w, s));
+}
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+__device__ __forceinline__ void stage_row(float* dst, const float* src, int H, bool vec) {
+  if (vec) {
+    for (int i = 4 * threadIdx.x; i < H; i += 4 * kRowThreads) st4(dst, i, ld4(src, i));
+  } else {
+    for (int i = threadIdx.x; i < H; i += kRowThreads) dst[i] = src[i];
+  }
+}
+
 // FFN prologue of a Gemma-4 MoE layer (model.rs:1719-1784; the reference's
 // GPU form is rust_cuda_prepare_ffn_f32, cuda_ptx/kernels.rs:987-1033, whose
 // arguments it takes).  Per row, with the reference's CPU roundings:
@@ -905,49 +950,57 @@ __device__ __forceinline__ float rms_scale_seq(const float* row, int H, float ep
 //   x_moe    = (res * s) * pre_ffw_norm_2       (the experts' input)
 //   router_x = ((res * s) * (1/sqrt(H))) * router_scale   (router input)
 // s_a, s the rms scales of attn and res (one sum of squares serves all three
-// norms).  Outputs optional, a missing weight meaning 1.  One warp per row.
-__global__ void ffn_prologue_kernel(const float* __restrict__ hidden, const float* __restrict__ attn,
-                                    const float* __restrict__ pan, const float* __restrict__ ffn_norm,
-                                    const float* __restrict__ pre_norm2, const float* __restrict__ gis,
-                                    float* __restrict__ attn_res, float* __restrict__ x_shared,
-                                    float* __restrict__ x_moe, float* __restrict__ router_x, int H, int T,
-                                    float eps) {
-  extern __shared__ __align__(16) float rows_s[];
+// norms).  Outputs optional, a missing weight meaning 1.
+__global__ void __launch_bounds__(kRowThreads, 4)
+    ffn_prologue_kernel(const float* __restrict__ hidden, const float* __restrict__ attn,
+                        const float* __restrict__ pan, const float* __restrict__ ffn_norm,
+                        const float* __restrict__ pre_norm2, const float* __restrict__ gis,
+                        float* __restrict__ attn_res, float* __restrict__ x_shared, float* __restrict__ x_moe,
+                        float* __restrict__ router_x, int H, float eps, bool vec) {
+  extern __shared__ __align__(16) float row[];
+  __shared__ float s_scale;
   pdl_trigger();
   pdl_wait();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= T) return;
-  const size_t o = (size_t)t * H;
-  float* row = rows_s + (size_t)warp * H;
+  const size_t o = (size_t)blockIdx.x * H;
+  const int step = vec ? 4 * kRowThreads : kRowThreads, i0 = vec ? 4 * threadIdx.x : threadIdx.x;
   if (attn) {
-    for (int i = lane; i < H; i += 32) row[i] = attn[o + i];
-    __syncwarp();
-    float sa = 0.f;
-    if (lane == 0) sa = rms_scale_seq(row, H, eps);
-    sa = __shfl_sync(0xffffffffu, sa, 0);
-    for (int i = lane; i < H; i += 32) {
-      float v = __fmul_rn(row[i], sa);
-      if (pan) v = __fmul_rn(v, pan[i]);
-      row[i] = __fadd_rn(hidden[o + i], v);
+    stage_row(row, attn + o, H, vec);
+    __syncthreads();
+    if (threadIdx.x == 0) s_scale = rms_scale_seq(row, H, eps);
+    __syncthreads();
+    const float sa = s_scale;
+    for (int i = i0; i < H; i += step) {
+      if (vec) {
+        st4(row, i, add4(ld4(hidden + o, i), mul4(mul4s(ld4(row, i), sa), ld4w(pan, i))));
+      } else {
+        float v = __fmul_rn(row[i], sa);
+        if (pan) v = __fmul_rn(v, pan[i]);
+        row[i] = __fadd_rn(hidden[o + i], v);
+      }
     }
   } else {
-    for (int i = lane; i < H; i += 32) row[i] = hidden[o + i];
+    stage_row(row, hidden + o, H, vec);
   }
-  __syncwarp();
-  float scale = 0.f;
-  if (lane == 0) scale = rms_scale_seq(row, H, eps);
-  scale = __shfl_sync(0xffffffffu, scale, 0);
-  const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)H));
-  for (int i = lane; i < H; i += 32) {
-    const float r0 = row[i];
-    if (attn_res) attn_res[o + i] = r0;
-    const float v = __fmul_rn(r0, scale);
-    if (x_shared) x_shared[o + i] = ffn_norm ? __fmul_rn(v, ffn_norm[i]) : v;
-    if (x_moe) x_moe[o + i] = pre_norm2 ? __fmul_rn(v, pre_norm2[i]) : v;
-    if (router_x) {
-      const float r = __fmul_rn(v, inv_sqrt);
-      router_x[o + i] = gis ? __fmul_rn(r, gis[i]) : r;
+  __syncthreads();
+  if (threadIdx.x == 0) s_scale = rms_scale_seq(row, H, eps);
+  __syncthreads();
+  const float sc = s_scale, inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)H));
+  for (int i = i0; i < H; i += step) {
+    if (vec) {
+      const float4 r0 = ld4(row, i), v = mul4s(r0, sc);
+      if (attn_res) st4(attn_res + o, i, r0);
+      if (x_shared) st4(x_shared + o, i, mul4(v, ld4w(ffn_norm, i)));
+      if (x_moe) st4(x_moe + o, i, mul4(v, ld4w(pre_norm2, i)));
+      if (router_x) st4(router_x + o, i, mul4(mul4s(v, inv_sqrt), ld4w(gis, i)));
+    } else {
+      const float r0 = row[i], v = __fmul_rn(r0, sc);
+      if (attn_res) attn_res[o + i] = r0;
+      if (x_shared) x_shared[o + i] = ffn_norm ? __fmul_rn(v, ffn_norm[i]) : v;
+      if (x_moe) x_moe[o + i] = pre_norm2 ? __fmul_rn(v, pre_norm2[i]) : v;
+      if (router_x) {
+        const float r = __fmul_rn(v, inv_sqrt);
+        router_x[o + i] = gis ? __fmul_rn(r, gis[i]) : r;
+      }
     }
   }
 }
@@ -957,88 +1010,82 @@ __global__ void ffn_prologue_kernel(const float* __restrict__ hidden, const floa
 //   mlp_out = rms_norm(mlp_raw, post_ffw_norm_1)   (mlp_raw may be absent: 0)
 //   moe_out = rms_norm(moe_raw, post_ffw_norm_2)
 //   hidden  = (attn_res + rms_norm(mlp_out + moe_out, post_ffw_norm)) * out_scale
-// One warp per row; the two first sums of squares run in two lanes at once,
-// the third after them.  Shared memory: two rows per warp.
-__global__ void ffn_epilogue_kernel(const float* __restrict__ attn_res, const float* __restrict__ mlp_raw,
-                                    const float* __restrict__ moe_raw, const float* __restrict__ post1,
-                                    const float* __restrict__ post2, const float* __restrict__ post,
-                                    float out_scale, float* __restrict__ hidden, int H, int T, float eps) {
+// The two first sums of squares run in two warps at once, the third after
+// them.  Shared memory: two rows.
+__global__ void __launch_bounds__(kRowThreads, 4)
+    ffn_epilogue_kernel(const float* attn_res, const float* __restrict__ mlp_raw, const float* __restrict__ moe_raw,
+                        const float* __restrict__ post1, const float* __restrict__ post2,
+                        const float* __restrict__ post, float out_scale, float* hidden, int H, float eps, bool vec) {
   extern __shared__ __align__(16) float rows_s[];
+  __shared__ float s_sc[3];
   pdl_trigger();
   pdl_wait();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= T) return;
-  const size_t o = (size_t)t * H;
-  float* ma = rows_s + (size_t)warp * 2 * H;  // mlp row, then the combined row
-  float* mo = ma + H;                         // moe row
-  for (int i = lane; i < H; i += 32) {
-    ma[i] = mlp_raw ? mlp_raw[o + i] : 0.f;
-    mo[i] = moe_raw[o + i];
+  const size_t o = (size_t)blockIdx.x * H;
+  float* ma = rows_s;  // mlp row, then the combined row
+  float* mo = ma + H;  // moe row
+  const int step = vec ? 4 * kRowThreads : kRowThreads, i0 = vec ? 4 * threadIdx.x : threadIdx.x;
+  if (mlp_raw) {
+    stage_row(ma, mlp_raw + o, H, vec);
+  } else {
+    for (int i = threadIdx.x; i < H; i += kRowThreads) ma[i] = 0.f;
   }
-  __syncwarp();
-  float s = 0.f;
-  if (lane < 2) s = rms_scale_seq(lane == 0 ? ma : mo, H, eps);
-  const float s1 = __shfl_sync(0xffffffffu, s, 0), s2 = __shfl_sync(0xffffffffu, s, 1);
-  for (int i = lane; i < H; i += 32) {
-    float a = __fmul_rn(ma[i], s1);
-    if (post1) a = __fmul_rn(a, post1[i]);
-    float b = __fmul_rn(mo[i], s2);
-    if (post2) b = __fmul_rn(b, post2[i]);
-    ma[i] = __fadd_rn(a, b);
+  stage_row(mo, moe_raw + o, H, vec);
+  __syncthreads();
+  if (threadIdx.x == 0) s_sc[0] = rms_scale_seq(ma, H, eps);
+  if (threadIdx.x == 32) s_sc[1] = rms_scale_seq(mo, H, eps);
+  __syncthreads();
+  const float s1 = s_sc[0], s2 = s_sc[1];
+  for (int i = i0; i < H; i += step) {
+    if (vec) {
+      st4(ma, i, add4(mul4(mul4s(ld4(ma, i), s1), ld4w(post1, i)), mul4(mul4s(ld4(mo, i), s2), ld4w(post2, i))));
+    } else {
+      float a = __fmul_rn(ma[i], s1);
+      if (post1) a = __fmul_rn(a, post1[i]);
+      float b = __fmul_rn(mo[i], s2);
+      if (post2) b = __fmul_rn(b, post2[i]);
+      ma[i] = __fadd_rn(a, b);
+    }
   }
-  __syncwarp();
-  float s3 = 0.f;
-  if (lane == 0) s3 = rms_scale_seq(ma, H, eps);
-  s3 = __shfl_sync(0xffffffffu, s3, 0);
-  for (int i = lane; i < H; i += 32) {
-    float v = __fmul_rn(ma[i], s3);
-    if (post) v = __fmul_rn(v, post[i]);
-    hidden[o + i] = __fmul_rn(__fadd_rn(attn_res[o + i], v), out_scale);
+  __syncthreads();
+  if (threadIdx.x == 0) s_sc[2] = rms_scale_seq(ma, H, eps);
+  __syncthreads();
+  const float s3 = s_sc[2];
+  for (int i = i0; i < H; i += step) {
+    if (vec) {
+      const float4 v = mul4(mul4s(ld4(ma, i), s3), ld4w(post, i));
+      const float4 r = add4(ld4(attn_res + o, i), v);
+      st4(hidden + o, i, mul4s(r, out_scale));
+    } else {
+      float v = __fmul_rn(ma[i], s3);
+      if (post) v = __fmul_rn(v, post[i]);
+      hidden[o + i] = __fmul_rn(__fadd_rn(attn_res[o + i], v), out_scale);
+    }
   }
 }
 
 // RMS normalisation of T rows of H (ops.rs:24-49): sum_sq accumulated in
 // index order in f32 (x*x rounded, then added), mean = sum_sq / H,
-// scale = 1 / sqrt(mean + eps), out = (x * scale) * w.  One warp per row:
-// the warp stages the row in shared memory, lane 0 runs the reference's
-// sequential sum over it (the order decides the rounding), and the warp
-// scales the row.  Dynamic shared memory: rows_per_cta * H floats.
-__global__ void rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
-                                int H, int T, float eps) {
-  extern __shared__ __align__(16) float rows_s[];
+// scale = 1 / sqrt(mean + eps), out = (x * scale) * w.
+__global__ void __launch_bounds__(kRowThreads, 4)
+    rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out, int H,
+                    float eps, bool vec) {
+  extern __shared__ __align__(16) float row[];
+  __shared__ float s_scale;
   pdl_trigger();
   pdl_wait();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= T) return;
-  const float* xr = x + (size_t)t * H;
-  float* row = rows_s + (size_t)warp * H;
-  for (int i = lane; i < H; i += 32) row[i] = xr[i];
-  __syncwarp();
-  float scale = 0.f;
-  if (lane == 0) {
-    float s = 0.f;
-    int i = 0;
-    if ((H & 3) == 0) {
-#pragma unroll 8
-      for (; i < H; i += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(row + i);
-        s = __fadd_rn(s, __fmul_rn(v.x, v.x));
-        s = __fadd_rn(s, __fmul_rn(v.y, v.y));
-        s = __fadd_rn(s, __fmul_rn(v.z, v.z));
-        s = __fadd_rn(s, __fmul_rn(v.w, v.w));
-      }
+  const size_t o = (size_t)blockIdx.x * H;
+  stage_row(row, x + o, H, vec);
+  __syncthreads();
+  if (threadIdx.x == 0) s_scale = rms_scale_seq(row, H, eps);
+  __syncthreads();
+  const float sc = s_scale;
+  if (vec) {
+    for (int i = 4 * threadIdx.x; i < H; i += 4 * kRowThreads) st4(out + o, i, mul4(mul4s(ld4(row, i), sc), ld4w(w, i)));
+  } else {
+    for (int i = threadIdx.x; i < H; i += kRowThreads) {
+      const float v = __fmul_rn(row[i], sc);
+      out[o + i] = w ? __fmul_rn(v, w[i]) : v;
     }
-    for (; i < H; ++i) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
-    const float mean = __fdiv_rn(s, (float)H);
-    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  }
-  scale = __shfl_sync(0xffffffffu, scale, 0);
-  float* orow = out + (size_t)t * H;
-  for (int i = lane; i < H; i += 32) {
-    const float v = __fmul_rn(row[i], scale);
-    orow[i] = w ? __fmul_rn(v, w[i]) : v;
   }
 }
 
@@ -1071,19 +1118,25 @@ cudaError_t launch_geglu(const float* gate, const float* up, float* out, long lo
   return cudaPeekAtLastError();
 }
 
-int rms_norm_rows_per_cta(int H) {
-  int r = 8;
-  while (r > 1 && (size_t)r * H * 4 > 200 * 1024) r >>= 1;
-  return (size_t)r * H * 4 <= 200 * 1024 ? r : 0;
+// Rows up to 200 KiB of shared memory per CTA (one row; two for the
+// epilogue, which the caller asks for as 2 * H).
+int rms_norm_rows_per_cta(int H) { return H > 0 && (size_t)H * 4 <= 200 * 1024 ? 1 : 0; }
+
+namespace {
+bool vec_ok(int H, std::initializer_list<const void*> ptrs) {
+  if (H % 4 != 0) return false;
+  for (const void* p : ptrs)
+    if (((uintptr_t)p & 15) != 0) return false;
+  return true;
 }
+}  // namespace
 
 cudaError_t launch_rms_norm(const float* x, const float* w, float* out, int H, int T, float eps, cudaStream_t s) {
   static SmemOptIn cache;
-  const int r = rms_norm_rows_per_cta(H);
-  const size_t smem = (size_t)r * H * 4;
+  const size_t smem = (size_t)H * 4;
   const cudaError_t st = ensure_smem(rms_norm_kernel, smem, cache);
   if (st != cudaSuccess) return st;
-  return launch_pdl(rms_norm_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, x, w, out, H, T, eps);
+  return launch_pdl(rms_norm_kernel, dim3(T), dim3(kRowThreads), smem, s, x, w, out, H, eps, vec_ok(H, {x, w, out}));
 }
 
 // The routing of a dense FFN run as one expert: every token's one slot goes
@@ -1105,24 +1158,24 @@ cudaError_t launch_ffn_prologue(const float* hidden, const float* attn, const fl
                                 const float* pre_norm2, const float* gis, float* attn_res, float* x_shared,
                                 float* x_moe, float* router_x, int H, int T, float eps, cudaStream_t s) {
   static SmemOptIn cache;
-  const int r = rms_norm_rows_per_cta(H);
-  const size_t smem = (size_t)r * H * 4;
+  const size_t smem = (size_t)H * 4;
   const cudaError_t st = ensure_smem(ffn_prologue_kernel, smem, cache);
   if (st != cudaSuccess) return st;
-  return launch_pdl(ffn_prologue_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, hidden, attn, pan, ffn_norm,
-                    pre_norm2, gis, attn_res, x_shared, x_moe, router_x, H, T, eps);
+  const bool vec = vec_ok(H, {hidden, attn, pan, ffn_norm, pre_norm2, gis, attn_res, x_shared, x_moe, router_x});
+  return launch_pdl(ffn_prologue_kernel, dim3(T), dim3(kRowThreads), smem, s, hidden, attn, pan, ffn_norm, pre_norm2,
+                    gis, attn_res, x_shared, x_moe, router_x, H, eps, vec);
 }
 
 cudaError_t launch_ffn_epilogue(const float* attn_res, const float* mlp_raw, const float* moe_raw, const float* post1,
                                 const float* post2, const float* post, float out_scale, float* hidden, int H, int T,
                                 float eps, cudaStream_t s) {
   static SmemOptIn cache;
-  const int r = rms_norm_rows_per_cta(2 * H);
-  const size_t smem = (size_t)r * 2 * H * 4;
+  const size_t smem = (size_t)2 * H * 4;
   const cudaError_t st = ensure_smem(ffn_epilogue_kernel, smem, cache);
   if (st != cudaSuccess) return st;
-  return launch_pdl(ffn_epilogue_kernel, dim3((T + r - 1) / r), dim3(32 * r), smem, s, attn_res, mlp_raw, moe_raw,
-                    post1, post2, post, out_scale, hidden, H, T, eps);
+  const bool vec = vec_ok(H, {attn_res, mlp_raw, moe_raw, post1, post2, post, hidden});
+  return launch_pdl(ffn_epilogue_kernel, dim3(T), dim3(kRowThreads), smem, s, attn_res, mlp_raw, moe_raw, post1,
+                    post2, post, out_scale, hidden, H, eps, vec);
 }
 
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s) {
@@ -1149,9 +1202,13 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
   // with in the fused mode; otherwise it only reads them.
   int32_t* idp = logits ? ids_out : const_cast<int32_t*>(ids);
   float* prp = logits ? probs_out : const_cast<float*>(probs);
-  const size_t smem = (size_t)36 * E * sizeof(int32_t);
-  if (smem > 48 * 1024) {
-    cudaError_t st = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // the counting sort's arrays (4 [E] + [32][E+1] ints), then the selection's
+  // logits [T][E] and slots [T][K] (ids and values)
+  const size_t smem = (size_t)(4 * E + 32 * (E + 1)) * 4 +
+                      (logits ? (size_t)(n_pairs / K) * (E + 2 * K) * 4 : 0);
+  static SmemOptIn dispatch_cache;
+  {
+    const cudaError_t st = ensure_smem(dispatch_kernel, smem, dispatch_cache);
     if (st != cudaSuccess) return st;
   }
   if (!logits && chunk_cnt && n_pairs > kDispatchChunkedMin) {

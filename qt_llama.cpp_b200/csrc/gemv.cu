@@ -12,8 +12,8 @@
 //                pass to the gate warps through shared memory, which apply
 //                GeGLU and the Q8_0 quantisation of the down product's input.
 // Two compute forms: MMA = 1, warp-level mma.sync m16n8k32 block dots (the
-// automatic choice from two tokens per expert), and MMA = 0, dp4a with one
-// weight row per thread (single tokens).
+// automatic choice from a quarter of a (token, slot) pair per expert), and
+// MMA = 0, dp4a with one weight row per thread (the smallest batches).
 // The per-row f32 chain sum += (float)isum_b * (d_w * d_a) runs in block
 // order, as in the reference (quant.rs:335-369 / 564-577), so the results
 // are bit-identical to the tensor-core kernel and to the reference.
@@ -354,7 +354,7 @@ __device__ __forceinline__ void mma_block_rows2_half(const Frag& frag, const uin
 
 // The K chunks of one unit on the dp4a path, for compute thread row `c`:
 // NJ accumulators, of which the first nj hold tokens (NJ = 1 for the units
-// of a single token, the common case below two tokens per expert, so that
+// of a single token, the common case of the smallest batches, so that
 // their blocks carry no predicated work for absent tokens).  Ring indices
 // and phases advance as the caller's.  Returns false when a wait gave up.
 // Row `r` (0..15) of a packed record (PackedFrag's layout) as the raw

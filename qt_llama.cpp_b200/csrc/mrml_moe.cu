@@ -220,7 +220,11 @@ Route pick_route(int wtype, bool packed, int H, int I, int E, long long pairs) {
   const bool gv = mrml::gv_supported(wtype, H, I);
   const int forced = g_path.load(std::memory_order_relaxed);
   // Packed weights run on the decode kernel only (its MMA or dp4a form).
-  if (packed) return forced == 1 ? kRouteGemv : forced == 4 || pairs >= 2ll * E ? kRouteGemvMma : kRouteGemv;
+  // The MMA form from a quarter of a pair per expert: measured on B200 at
+  // config 2, T = 8 (half a pair per expert) it takes the layer step from
+  // 93 to 81 us; at T = 1 the dp4a form is faster (45 vs 49 us).
+  const bool mma_size = pairs * 4 >= E;
+  if (packed) return forced == 1 ? kRouteGemv : forced == 4 || mma_size ? kRouteGemvMma : kRouteGemv;
   switch (forced) {
     case 1: return gv ? kRouteGemv : kRouteGeneral;
     case 2: return tc ? kRouteTensor : (gv ? kRouteGemv : kRouteGeneral);
@@ -229,13 +233,12 @@ Route pick_route(int wtype, bool packed, int H, int I, int E, long long pairs) {
     default: break;
   }
   if (!gv) return tc && pairs > 16ll * E ? kRouteTensor : kRouteGeneral;
-  // A warp-level MMA covers 8 positions whatever the count: worth it once
-  // experts see about two tokens or more.  It also beats the tcgen05 kernel
+  // A warp-level MMA covers 8 positions whatever the count; it also beats the tcgen05 kernel
   // at every measured prefill size (config 3: 123 vs 169 us gate/up; the C2
   // layer at 2048 tokens, Q8_0: 1.40 vs 2.48 ms), because the exact f32
   // rescale per quant block, not the integer products, bounds both, and the
   // warp-level MMA leaves its sums in registers.
-  return pairs >= 2ll * E ? kRouteGemvMma : kRouteGemv;
+  return mma_size ? kRouteGemvMma : kRouteGemv;
 }
 
 // With topk_logits, the dispatch kernel first selects the experts from the
@@ -515,7 +518,7 @@ size_t mrml_moe_ep_workspace_bytes(int N, int T, int H, int I, int E, int K) {
 int mrml_moe_ep_dispatch(void* const* slabs, int rank, int N, int T, int H, int E, int K, const float* x,
                          const int32_t* ids, const float* probs, mrml_stream_t stream) {
   MRML_TRY(check_ep_args(slabs, rank, N, T, H, E, K));
-  if (!x || !ids || !probs) return MRML_ERR_INVALID_ARGUMENT;
+  if (!x || !ids || !probs || !aligned16(x)) return MRML_ERR_INVALID_ARGUMENT;
   MRML_TRY(check_device());
   const cudaStream_t s = (cudaStream_t)stream;
   MRML_LAUNCH(mrml::launch_ep_dispatch(reinterpret_cast<uint8_t* const*>(slabs), rank, N, T, H, E, K, x, ids, probs,
