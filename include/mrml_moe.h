@@ -314,6 +314,29 @@ size_t mrml_moe_dense_ffn_workspace_bytes(int H, int I, int T);
 int mrml_moe_dense_ffn(int wtype, const uint8_t *gate_up, const uint8_t *down, const float *x, float *out, int H,
                        int I, int T, void *workspace, size_t workspace_bytes, mrml_stream_t stream);
 
+/* One whole FFN block of a Gemma-4 MoE layer on the device-resident hidden
+ * state, in one capturable call (the body of the reference's captured
+ * per-layer FFN graph, capture_layer_ffn_graph model.rs:295-381 /
+ * enqueue_ffn_compute_for_capture cuda.rs:1885-1955, with the prepare and
+ * finish steps around it, model.rs:1719-2196):
+ *   mrml_moe_ffn_prologue(hidden, attn, ...) -> residual, MLP / MoE / router
+ *   inputs; mrml_moe_dense_ffn (if I_dense > 0); mrml_moe_forward;
+ *   mrml_moe_ffn_epilogue -> hidden (overwritten in place).
+ * Everything between lives in the workspace
+ * (mrml_moe_ffn_block_workspace_bytes, 256-byte aligned, cleared once with
+ * mrml_moe_workspace_init; mrml_moe_device_status reads its status word).
+ * dense_wtype is the shared MLP's weight type (its slabs as for
+ * mrml_moe_dense_ffn).  Bit-identical to the reference's CPU block.  Capture
+ * it once per layer and replay the graph per decode step. */
+size_t mrml_moe_ffn_block_workspace_bytes(int H, int I, int I_dense, int E, int K, int T);
+int mrml_moe_ffn_block(int wtype, int dense_wtype, float *hidden, const float *attn, const float *post_attn_norm,
+                       const float *ffn_norm, const float *pre_ffw_norm_2, const float *router_scale,
+                       const float *post_ffw_norm_1, const float *post_ffw_norm_2, const float *post_ffw_norm,
+                       float layer_scale, const float *router_w, const uint8_t *gate_up, const uint8_t *down,
+                       const float *down_scale, const uint8_t *dense_gate_up, const uint8_t *dense_down, int H, int I,
+                       int I_dense, int E, int K, int T, void *workspace, size_t workspace_bytes,
+                       mrml_stream_t stream);
+
 /* RMS normalisation of `batch` rows of `dim` floats: out = x / sqrt(mean(x^2)
  * + eps) * weight (weight may be NULL), with the reference's rounding: the
  * sum of squares in index order, then 1 / sqrt(sum / dim + eps) (ops.rs:24-49;

@@ -340,6 +340,15 @@ __device__ __forceinline__ Q8Block load_q8_block(const uint8_t* p) {
 
 __host__ __device__ constexpr int block_bytes(int wtype) { return wtype == kQ4_0 ? 18 : 34; }
 
+// Blocks per K chunk of the packed down weights (the decode kernel's down
+// stages; nb = I / 32): the largest divisor of nb up to 12, so that a unit's
+// rows stream in a few equal chunks (config 2: 22 = 2 x 11).
+__host__ __device__ constexpr int down_chunk_blocks(int nb) {
+  int c = nb < 12 ? nb : 12;
+  while (c > 1 && nb % c != 0) --c;
+  return c < 1 ? 1 : c;
+}
+
 // Activation operand layouts (quantised Q8_0 rows by position).  Positions
 // come in groups of 8; a group's block b is 256 bytes: two 16-byte halves
 // (elements 0..15 at +0, 16..31 at +128) of 8 positions (16 bytes apart),

@@ -393,8 +393,8 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const ui
     const uint8_t* sc = bt + P.kcb * GB;  // the blocks' group-major scale records
     if constexpr (PK) {
       // Stage: gate/up [part][tile 4][block kKC][RB] (thread c = part * 64 +
-      // 16 * tile + row); down [tile 8][block nb][RB].
-      const int nbs = MODE == kGateUp ? kKC : P.nb;
+      // 16 * tile + row); down [tile 8][block kcb][RB].
+      const int nbs = MODE == kGateUp ? kKC : P.kcb;
       const uint8_t* tile = src + (size_t)(c >> 4) * nbs * RB;
       for (int b = 0; b < nbs; ++b) {
         uint32_t d16, q[WQ4 ? 4 : 8], w[8];
@@ -460,7 +460,8 @@ __device__ __forceinline__ bool dp4a_chunks(const Params& P, GvBars* B, const ui
 // PK = 1: the weights are in the packed layout of mrml_moe_prepare_weights
 // (PackedFrag's records; per unit and K chunk contiguous), streamed with 1-D
 // bulk copies: gate/up [E][part][64-row group][K chunk][tile 4][block
-// kKC][record], down [E][128-row group][tile 8][block][record].
+// kKC][record], down [E][128-row group][K chunk][tile 8][block
+// down_chunk_blocks][record].
 template <int WQ4, int MODE, int MMA, int NG, int PK>
 __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
                                   ctas_per_sm(MMA, MODE, NG, WQ4, PK))
@@ -508,7 +509,7 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
   pdl_trigger();
   __syncthreads();
   const int n_units = *P.n_units;
-  const int nkc = MODE == kGateUp ? P.nb / kKC : 1;
+  const int nkc = MODE == kGateUp ? P.nb / kKC : P.nb / P.kcb;
 
   if (warp == 0) {
     // ----------------------------------------------------- weight producer
@@ -530,9 +531,11 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
             bulk_g2s(dst, gsrc, part, &B->raw_full[rs]);
             bulk_g2s(dst + part, gsrc + (size_t)ng * nc * part, part, &B->raw_full[rs]);
           } else if constexpr (PK) {
-            const uint32_t bytes = (uint32_t)(8 * P.nb * RB);
+            // down: the unit's K chunk kc, 8 tiles x kcb blocks, one run
+            const uint32_t bytes = (uint32_t)(8 * P.kcb * RB);
             mbar_arrive_expect_tx(&B->raw_full[rs], bytes);
-            bulk_g2s(dst, P.w_raw + ((size_t)e * (P.rows / 128) + m0 / 128) * bytes, bytes, &B->raw_full[rs]);
+            bulk_g2s(dst, P.w_raw + (((size_t)e * (P.rows / 128) + m0 / 128) * nkc + kc) * bytes, bytes,
+                     &B->raw_full[rs]);
           } else if constexpr (MODE == kGateUp) {
             mbar_arrive_expect_tx(&B->raw_full[rs], 2 * RG * kKC * BB);
             const int c0 = kc * kKC * BB / 2;
@@ -626,16 +629,17 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
             mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + bl * RB, kKC * RB}, bt + bl * GB, gs, sc + bl * SB, ss, one,
                                      g, t, acc);
         } else if constexpr (PK) {
-          const uint8_t* t0 = src + (size_t)(2 * cw) * P.nb * RB;
+          // down: this stage's K chunk of kcb blocks; warp cw's tiles 2cw, 2cw + 1
+          const uint8_t* t0 = src + (size_t)(2 * cw) * P.kcb * RB;
           if (NG == 1 && half) {
 #pragma unroll 2
-            for (int b = 0; b < P.nb; ++b)
-              mma_block_rows2_half<WQ4>(PackedFrag<WQ4>{t0 + b * RB, P.nb * RB}, bt + b * GB, sc + b * SB, one, g,
+            for (int b = 0; b < P.kcb; ++b)
+              mma_block_rows2_half<WQ4>(PackedFrag<WQ4>{t0 + b * RB, P.kcb * RB}, bt + b * GB, sc + b * SB, one, g,
                                         t, acch);
           } else {
 #pragma unroll 2
-            for (int b = 0; b < P.nb; ++b)
-              mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + b * RB, P.nb * RB}, bt + b * GB, gs, sc + b * SB, ss,
+            for (int b = 0; b < P.kcb; ++b)
+              mma_block_rows2<WQ4, NG>(PackedFrag<WQ4>{t0 + b * RB, P.kcb * RB}, bt + b * GB, gs, sc + b * SB, ss,
                                        one, g, t, acc);
           }
         } else if constexpr (MODE == kGateUp) {
@@ -947,8 +951,10 @@ std::atomic<int> g_gv_per_sm{0}, g_gv_ring{0};
 GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma, int ng, bool packed = false) {
   GvPlan p{};
   const int bb = block_bytes(wtype);
-  p.kcb = mode == tc::kGateUp ? tc::kKC : nb;
-  const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb : 2 * kGvRowsGateUp * row_bytes;
+  // down on packed weights streams K chunks (down_chunk_blocks); on GGUF rows a whole K per unit
+  p.kcb = mode == tc::kGateUp ? tc::kKC : (packed ? down_chunk_blocks(nb) : nb);
+  const int raw1 = mode == tc::kGateUp ? 2 * kGvRowsGateUp * tc::kKC * bb
+                                       : (packed ? 2 * kGvRowsGateUp * p.kcb * bb : 2 * kGvRowsGateUp * row_bytes);
   p.raw_bytes = (raw1 + 1023) & ~1023;
   const int bs_stage = p.kcb * ng * (256 + kActScaleBytes);
   const size_t xch_bytes = mode == tc::kGateUp ? (size_t)kGvTokens * ng * kGvRowsGateUp * 4 : 0;
@@ -960,9 +966,10 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   const int per_sm_max = per_sm_set > 0 ? per_sm_set : (many_units ? bound : 1);
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
     const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
-    // Down tiles hold a whole K (one stage per unit); several CTAs per SM
-    // overlap one another's loads, so a single stage each is allowed there.
-    const int rs_min = (per_sm > 1 && mode == tc::kGateUp) ? 2 : 1;
+    // GGUF down tiles hold a whole K (one stage per unit); several CTAs per
+    // SM overlap one another's loads, so a single stage each is allowed there.
+    // K-chunked stages (gate/up, packed down) double-buffer within a CTA.
+    const int rs_min = (per_sm > 1 && (mode == tc::kGateUp || packed)) ? 2 : 1;
     const int rs_max = ring_set > 0 ? ring_set : tc::kMaxRaw;
     for (int rs = rs_max; rs >= rs_min; --rs)
       for (int bs = 2; bs >= 1; --bs) {

@@ -96,7 +96,11 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
 constexpr int kDispatchChunkedMin = 8192;
 inline size_t dispatch_chunk_ints(long long n_pairs, int E) { return (size_t)((n_pairs + 1023) / 1024) * E; }
 // Whether launch_dispatch can select the experts itself (from `logits`) for
-// T tokens: the top-k of up to 256 experts, one warp per token.
+// T tokens: the top-k of up to 256 experts for up to kDispatchTopkMaxTokens
+// tokens.
+constexpr int kDispatchTopkMaxTokens = 32;
+// Batches with T * E up to this select by rank inside the dispatch kernel.
+constexpr int kDispatchRankSelectMax = 512;
 bool dispatch_topk_supported(int E, int K, int T);
 // The decode kernel's group-major operand from the per-token quantisation
 // (xq/xd/xsum of launch_quantize_rows) and the dispatch's pair_at; poff_end

@@ -467,7 +467,8 @@ int mrml_moe_forward(int wtype, const float* router_w, const float* router_x, co
   const Workspace w = carve(workspace, H, I, E, K, T);
   const cudaStream_t s = (cudaStream_t)stream;
   // Up to 32 tokens the dispatch kernel selects the experts itself (one
-  // launch fewer on the decode path); the selection is the same code.
+  // launch fewer on the decode path); the selection is the same ordering.
+  // (At 64 tokens its single CTA took longer than the separate top-k launch.)
   if (mrml::dispatch_topk_supported(E, K, T)) {
     MRML_LAUNCH(mrml::launch_router_logits(router_w, router_x, logits, H, E, T, w.status, s));
     return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s, 0, 0, logits, ids,
@@ -614,6 +615,74 @@ int mrml_moe_dense_ffn(int wtype, const uint8_t* gate_up, const uint8_t* down, c
   float* probs = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + w.bytes + align256((size_t)T * 4));
   MRML_LAUNCH(mrml::launch_dense_routing(ids, probs, T, s));
   return run_experts(w, wtype, gate_up, down, ids, probs, nullptr, x, out, H, I, 1, 1, T, s);
+}
+
+// The FFN block's workspace: the expert workspace (its status word first;
+// the shared MLP's call reuses the same bytes, one after the other on the
+// stream), then the block's activations [T][H] x 6, the router logits and
+// the selected ids / weights.
+namespace {
+struct BlockWs {
+  float *attn_res, *shared, *moe_in, *router_in, *mlp_out, *moe_out, *logits, *probs;
+  int32_t* ids;
+  size_t inner, bytes;
+};
+BlockWs carve_block(void* base, int H, int I, int I_dense, int E, int K, int T) {
+  BlockWs b{};
+  b.inner = carve(nullptr, H, I, E, K, T).bytes;
+  if (I_dense > 0) b.inner = std::max(b.inner, mrml_moe_dense_ffn_workspace_bytes(H, I_dense, T));
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = align256(b.inner);
+  auto take = [&](size_t n) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(n);
+    return r;
+  };
+  const size_t row = (size_t)T * H * 4;
+  b.attn_res = reinterpret_cast<float*>(take(row));
+  b.shared = reinterpret_cast<float*>(take(row));
+  b.moe_in = reinterpret_cast<float*>(take(row));
+  b.router_in = reinterpret_cast<float*>(take(row));
+  b.mlp_out = reinterpret_cast<float*>(take(row));
+  b.moe_out = reinterpret_cast<float*>(take(row));
+  b.logits = reinterpret_cast<float*>(take((size_t)T * E * 4));
+  b.ids = reinterpret_cast<int32_t*>(take((size_t)T * K * 4));
+  b.probs = reinterpret_cast<float*>(take((size_t)T * K * 4));
+  b.bytes = off;
+  return b;
+}
+}  // namespace
+
+size_t mrml_moe_ffn_block_workspace_bytes(int H, int I, int I_dense, int E, int K, int T) {
+  if (H <= 0 || I <= 0 || I_dense < 0 || E <= 0 || K <= 0 || T < 0) return 0;
+  return carve_block(nullptr, H, I, I_dense, E, K, T).bytes;
+}
+
+int mrml_moe_ffn_block(int wtype, int dense_wtype, float* hidden, const float* attn, const float* post_attn_norm,
+                       const float* ffn_norm, const float* pre_ffw_norm_2, const float* router_scale,
+                       const float* post_ffw_norm_1, const float* post_ffw_norm_2, const float* post_ffw_norm,
+                       float layer_scale, const float* router_w, const uint8_t* gate_up, const uint8_t* down,
+                       const float* down_scale, const uint8_t* dense_gate_up, const uint8_t* dense_down, int H, int I,
+                       int I_dense, int E, int K, int T, void* workspace, size_t workspace_bytes,
+                       mrml_stream_t stream) {
+  if (T < 0 || I_dense < 0) return MRML_ERR_INVALID_ARGUMENT;
+  if (T == 0) return MRML_OK;
+  const bool dense = I_dense > 0;
+  if (!hidden || !router_w || (dense && (!dense_gate_up || !dense_down))) return MRML_ERR_INVALID_ARGUMENT;
+  MRML_TRY(check_weights(wtype, H, I, E, K, T));
+  if (dense) MRML_TRY(check_weights(dense_wtype, H, I_dense, 1, 1, T));
+  if (!workspace || ((uintptr_t)workspace & 255u) != 0) return MRML_ERR_INVALID_ARGUMENT;
+  const BlockWs b = carve_block(workspace, H, I, I_dense, E, K, T);
+  if (workspace_bytes < b.bytes) return MRML_ERR_WORKSPACE_TOO_SMALL;
+  MRML_TRY(mrml_moe_ffn_prologue(hidden, attn, post_attn_norm, ffn_norm, pre_ffw_norm_2, router_scale, b.attn_res,
+                                 dense ? b.shared : nullptr, b.moe_in, b.router_in, H, T, stream));
+  if (dense)
+    MRML_TRY(mrml_moe_dense_ffn(dense_wtype, dense_gate_up, dense_down, b.shared, b.mlp_out, H, I_dense, T, workspace,
+                                b.inner, stream));
+  MRML_TRY(mrml_moe_forward(wtype, router_w, b.router_in, b.moe_in, gate_up, down, down_scale, b.logits, b.ids,
+                            b.probs, b.moe_out, H, I, E, K, T, workspace, b.inner, stream));
+  return mrml_moe_ffn_epilogue(b.attn_res, dense ? b.mlp_out : nullptr, b.moe_out, post_ffw_norm_1, post_ffw_norm_2,
+                               post_ffw_norm, hidden, layer_scale, H, T, stream);
 }
 
 int mrml_moe_rms_norm(const float* x, const float* weight, float* out, int dim, int batch, float eps,

@@ -18,8 +18,9 @@
 //   gate_up: [E][part: gate rows, up rows][64-row group][K chunk of 8
 //            blocks][tile 4][block 8][record]  (a unit's K chunk is one
 //            contiguous run per part);
-//   down:    [E][128-row group][tile 8][block][record]  (a unit's rows are
-//            one contiguous run).
+//   down:    [E][128-row group][K chunk of down_chunk_blocks(I/32) blocks]
+//            [tile 8][block][record]  (a unit's K chunk is one contiguous
+//            run).
 //
 // The values are the reference's bytes; only their order changes, so the
 // products are bit-identical to the raw layout's.
@@ -51,10 +52,10 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
     const int nG = rows_part / 64, nC = nb / 8;
     const int G = r / 64, j = (r % 64) / 16, c = b / 8, bl = b % 8;
     rec = (((((size_t)e * parts + p) * nG + G) * nC + c) * 4 + j) * 8 + bl;
-  } else {  // down: 128-row groups of 8 tiles, all blocks
-    const int nG = rows_part / 128;
-    const int G = r / 128, j = (r % 128) / 16;
-    rec = (((size_t)e * nG + G) * 8 + j) * nb + b;
+  } else {  // down: 128-row groups, K chunks of down_chunk_blocks(nb) blocks, 8 tiles
+    const int nG = rows_part / 128, kc = down_chunk_blocks(nb), nC = nb / kc;
+    const int G = r / 128, j = (r % 128) / 16, c = b / kc, bl = b % kc;
+    rec = ((((size_t)e * nG + G) * nC + c) * 8 + j) * kc + bl;
   }
   uint8_t* out = dst + rec * RB;
   const int rr = r % 16, g = rr & 7, h = rr >> 3;

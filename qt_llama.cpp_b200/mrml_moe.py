@@ -77,6 +77,8 @@ SIGNATURES = {
     "mrml_moe_ffn_prologue": (_i, [_vp] * 10 + [_i, _i, _vp]),
     "mrml_moe_ffn_epilogue": (_i, [_vp] * 7 + [_f, _i, _i, _vp]),
     "mrml_moe_dense_ffn_workspace_bytes": (_sz, [_i, _i, _i]),
+    "mrml_moe_ffn_block_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "mrml_moe_ffn_block": (_i, [_i, _i] + [_vp] * 9 + [_f] + [_vp] * 6 + [_i] * 6 + [_vp, _sz, _vp]),
     "mrml_moe_dense_ffn": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "mrml_moe_gguf_open": (_i, [_c.c_char_p, _c.POINTER(_vp)]),
     "mrml_moe_gguf_close": (_i, [_vp]),
@@ -316,6 +318,49 @@ def dense_ffn(wtype, gate_up, down, x, out, H, I, T, ws, stream=None):
     _check("mrml_moe_dense_ffn",
            load_library().mrml_moe_dense_ffn(wtype, _ptr(gate_up), _ptr(down), _ptr(x), _ptr(out), H, I, T, _ptr(ws),
                                              ws.numel(), _stream_ptr(stream)))
+
+
+def new_ffn_block_workspace(H, I, I_dense, E, K, T, device=None):
+    import torch
+
+    n = load_library().mrml_moe_ffn_block_workspace_bytes(H, I, I_dense, E, K, T)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def ffn_block(wtype, dense_wtype, hidden, attn, norms, layer_scale, router_w, gate_up, down, down_scale,
+              dense_gate_up, dense_down, H, I, I_dense, E, K, T, ws, stream=None):
+    """mrml_moe_ffn_block; norms = (post_attn_norm, ffn_norm, pre_ffw_norm_2,
+    router_scale, post_ffw_norm_1, post_ffw_norm_2, post_ffw_norm), None for 1."""
+    _check("mrml_moe_ffn_block",
+           load_library().mrml_moe_ffn_block(wtype, dense_wtype, _ptr(hidden), _ptr(attn), *[_ptr(n) for n in norms],
+                                             float(layer_scale), _ptr(router_w), _ptr(gate_up), _ptr(down),
+                                             _ptr(down_scale), _ptr(dense_gate_up), _ptr(dense_down), H, I, I_dense,
+                                             E, K, T, _ptr(ws), ws.numel(), _stream_ptr(stream)))
+
+
+class FfnBlockGraph:
+    """A layer's FFN block captured once as a CUDA graph and replayed per
+    decode step on the device-resident hidden state (the reference's
+    capture_layer_ffn_graph, model.rs:295-381, with the block's prepare and
+    finish steps inside).  `hidden` and `attn` are the static input buffers:
+    write the step's values into them, then replay(); hidden holds the block's
+    output afterwards."""
+
+    def __init__(self, wtype, dense_wtype, hidden, attn, norms, layer_scale, router_w, gate_up, down, down_scale,
+                 dense_gate_up, dense_down, H, I, I_dense, E, K, T):
+        import torch
+
+        self.args = (wtype, dense_wtype, hidden, attn, tuple(norms), layer_scale, router_w, gate_up, down, down_scale,
+                     dense_gate_up, dense_down, H, I, I_dense, E, K, T)
+        self.ws = new_ffn_block_workspace(H, I, I_dense, E, K, T, hidden.device)
+        self.stream = torch.cuda.Stream(hidden.device)
+        self.graph = torch.cuda.CUDAGraph()
+        self.stream.wait_stream(torch.cuda.current_stream(hidden.device))
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            ffn_block(*self.args, self.ws, stream=self.stream)
+
+    def replay(self):
+        self.graph.replay()
 
 
 def rms_norm(x, weight, out, dim, batch, eps, stream=None):

@@ -92,6 +92,16 @@ def test_invalid_arguments_rejected_without_a_gpu(moe):
     assert lib.mrml_moe_ffn_prologue(N, N, N, N, N, N, N, N, N, N, 2816, 0, None) == 0
     assert lib.mrml_moe_ffn_epilogue(P, N, N, N, N, N, P, ctypes.c_float(1), 2816, 1, None) == -1  # no moe
     assert lib.mrml_moe_ffn_epilogue(P, N, P, N, N, N, P, ctypes.c_float(1), 1 << 20, 1, None) == -2
+    assert lib.mrml_moe_ffn_block_workspace_bytes(2816, 704, 2112, 128, 8, 64) > 0
+    assert lib.mrml_moe_ffn_block_workspace_bytes(2816, 704, -1, 128, 8, 64) == 0
+    blk = lib.mrml_moe_ffn_block
+    nine = [P] + [None] * 8
+    assert blk(2, 2, *nine, ctypes.c_float(1), None, P, P, None, None, None, 2816, 704, 0, 128, 8, 1, P, 1 << 30,
+               None) == -1  # no router weights
+    assert blk(2, 2, *nine, ctypes.c_float(1), P, P, P, None, None, None, 2816, 704, 2112, 128, 8, 1, P, 1 << 30,
+               None) == -1  # a shared MLP without its slabs
+    assert blk(2, 2, *nine, ctypes.c_float(1), P, P, P, None, None, None, 2816, 704, 0, 128, 8, 1, P, 16,
+               None) == -3
     assert lib.mrml_moe_dense_ffn_workspace_bytes(2816, 2112, 64) > 0
     assert lib.mrml_moe_dense_ffn_workspace_bytes(0, 2112, 64) == 0
     assert lib.mrml_moe_dense_ffn(2, P, P, P, P, 2816, 2100, 1, P, 1 << 30, None) == -1  # I % 32

@@ -183,3 +183,48 @@ def test_ffn_layer_chain_bit_exact(cuda, moe, oracle, synth, T):
     assert_exact(d_moe.cpu().numpy(), moe_raw)
     assert_exact(d_mlp.cpu().numpy(), mlp_raw)
     assert_exact(d_h.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("T,with_dense", [(1, True), (8, True), (32, False)])
+def test_ffn_block_graph_replays_bit_exact(cuda, moe, oracle, synth, T, with_dense):
+    """The whole FFN block (mrml_moe_ffn_block) captured once as a CUDA graph
+    (FfnBlockGraph, the reference's capture_layer_ffn_graph) and replayed on
+    two decode steps of fresh hidden states: every replay equals the oracle's
+    CPU block (model.rs:1719-2196) bit for bit."""
+    import torch
+
+    H, I, E, K, Id = 2816, 704, 128, 8, 2112
+    wtype = 2
+    norms = [norm_weight(synth, 400 + i, H) for i in range(7)]
+    W = synth.normal(410, E * H, 0.02).reshape(E, H)
+    gu, dn = synth.expert_weights(411, wtype, H, I, E)
+    dscale = (1.0 + synth.normal(412, E, 0.05)).astype(np.float32)
+    g_gu, g_dn = moe.prepare_weights(wtype, dev(gu, cuda), dev(dn, cuda))
+    if with_dense:
+        dgu, ddn = synth.expert_weights(413, wtype, H, Id, 1)
+        g_dgu, g_ddn = moe.prepare_weights(wtype, dev(dgu, cuda), dev(ddn, cuda))
+    else:
+        g_dgu = g_ddn = None
+    layer_scale = 0.625
+    hidden = torch.empty((T, H), device=cuda)
+    attn = torch.empty((T, H), device=cuda)
+    d_norms = [dev(n, cuda) for n in norms]
+    wt = wtype | moe.MRML_PACKED
+    G = moe.FfnBlockGraph(wt, wt, hidden, attn, d_norms, layer_scale, dev(W, cuda), g_gu, g_dn, dev(dscale, cuda),
+                          g_dgu, g_ddn, H, I, Id if with_dense else 0, E, K, T)
+    for step in range(2):
+        h = (synth.normal(420 + 2 * step + T, T * H) * 1.5).reshape(T, H)
+        a = (synth.normal(421 + 2 * step + T, T * H) * 0.5).reshape(T, H)
+        hidden.copy_(dev(h, cuda))
+        attn.copy_(dev(a, cuda))
+        G.replay()
+        torch.cuda.synchronize()
+        st, _ = moe.device_status(G.ws)
+        assert st == 0
+        res, xs, xm, rx = oracle.ffn_prologue(h, a, *norms[:4])
+        _, ids, probs = oracle.router(W, rx, H, E, K, T)
+        moe_raw = oracle.experts(wtype, gu, dn, ids, probs, dscale, xm, H, I, E, K, T, n_threads=8)
+        mlp_raw = (oracle.experts(wtype, dgu, ddn, np.zeros((T, 1), np.int32), np.ones((T, 1), np.float32), None,
+                                  xs, H, Id, 1, 1, T, n_threads=8) if with_dense else None)
+        want = oracle.ffn_epilogue(res, mlp_raw, moe_raw, *norms[4:], layer_scale)
+        assert_exact(hidden.cpu().numpy(), want)

@@ -22,7 +22,8 @@ pytestmark = pytest.mark.gpu
 def repack_numpy(raw, wtype, which, H, I, E):
     """The packed layout, restated: records of (16-row tile, block) in MMA
     fragment order; gate_up grouped [E][part][64-row group][K chunk of 8
-    blocks][tile 4][block 8], down [E][128-row group][tile 8][block]."""
+    blocks][tile 4][block 8], down [E][128-row group][K chunk of kc
+    blocks][tile 8][block kc], kc the largest divisor of I/32 up to 12."""
     bb = 18 if wtype == 2 else 34
     rows_part, parts, nb = (I, 2, H // 32) if which == 0 else (H, 1, I // 32)
     blocks = np.asarray(raw, np.uint8).reshape(E, parts, rows_part, nb, bb)
@@ -41,10 +42,11 @@ def repack_numpy(raw, wtype, which, H, I, E):
                   + G[None, None, :, None]) * nC + c[None, None, None, :]) * 4 + j[None, None, :, None]) * 8
                + bl[None, None, None, :])
     else:
-        nG = rows_part // 128
-        G, j = r // 128, (r % 128) // 16
-        rec = (((np.arange(E)[:, None, None, None] * nG + G[None, None, :, None]) * 8 + j[None, None, :, None]) * nb
-               + b[None, None, None, :])
+        kc = max(c for c in range(1, min(nb, 12) + 1) if nb % c == 0)
+        nG, nC = rows_part // 128, nb // kc
+        G, j, c, bl = r // 128, (r % 128) // 16, b // kc, b % kc
+        rec = ((((np.arange(E)[:, None, None, None] * nG + G[None, None, :, None]) * nC + c[None, None, None, :]) * 8
+                + j[None, None, :, None]) * kc + bl[None, None, None, :])
         rec = np.broadcast_to(rec, (E, parts, rows_part, nb))
     rr = r % 16
     g, h = rr % 8, rr // 8
