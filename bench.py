@@ -580,7 +580,8 @@ def stack_parity_check(ss, world, rank, layers=(0, 1, 29), n_check=4, seed=321):
         ss.layer_step(l, h, nxt)
         if l in layers:
             torch.cuda.synchronize()
-            saved[l] = (all_gather_np(h, world), all_gather_np(nxt, world), all_gather_np(ss.ids, world))
+            ids = ss.ep.ids if ss.ep is not None else ss.ids
+        saved[l] = (all_gather_np(h, world), all_gather_np(nxt, world), all_gather_np(ids, world))
         h, nxt = nxt, h
     ok, worst, n_ids_bad = True, 0.0, 0
     idx = None
@@ -782,35 +783,84 @@ def time_kernels(ls, steps):
     return dict(zip(ls.kernels, totals))
 
 
-def time_e2e(ls, steps, warmup, world):
+def time_e2e(ls, steps, warmup, world, repeats=5):
     """Same steps through the public API with host buffers: every step copies
     its x from pinned host memory to the device, runs the layer and copies the
-    output back to pinned host memory.  Each step is a replayed CUDA graph of
-    those three stages (the reference's decode path captures its per-layer
-    FFN work the same way)."""
+    output back to pinned host memory.  Steps are independent batches, so the
+    copies run on two copy streams (in, out) and overlap the neighbouring
+    steps' compute (double-buffered device x and output, events between the
+    streams): step i's input copy overlaps step i-1's layer, its output copy
+    step i+1's.  The
+    `steps` steps are captured as one CUDA graph (the reference's decode path
+    captures its per-layer FFN work; one graph keeps the host out of the
+    loop), replayed `repeats` times after `warmup` replays of the graph; the
+    region is one replay (events, synchronize and barrier around it), median,
+    max over ranks."""
     import torch
 
     T, H = ls.T, ls.H
     G = 2 * ls.n_layers
     host_x = [ls.xs[g % len(ls.xs)].cpu().pin_memory() for g in range(G)]
     host_out = [torch.empty((T, H), dtype=torch.float32).pin_memory() for _ in range(G)]
-    dx = torch.empty((T, H), device=ls.device)
-    graphs = []
-    side = torch.cuda.Stream(device=ls.device)
-    for g in range(G):
-        with torch.cuda.stream(side):  # warm-up outside capture
-            dx.copy_(host_x[g], non_blocking=True)
-            ls.step(g, x=dx)
-            host_out[g].copy_(ls.out, non_blocking=True)
-        side.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            dx.copy_(host_x[g], non_blocking=True)
-            ls.step(g, x=dx)
-            host_out[g].copy_(ls.out, non_blocking=True)
-        graphs.append(graph)
-    ms = time_steps(ls, steps, warmup, world, graphs, repeats=5)
-    return ms, T * H * 4, T * H * 4
+    dx = [torch.empty((T, H), device=ls.device) for _ in range(2)]
+    dout = [torch.empty((T, H), device=ls.device) for _ in range(2)]
+    comp = torch.cuda.Stream(device=ls.device)
+    cin, cout = torch.cuda.Stream(device=ls.device), torch.cuda.Stream(device=ls.device)
+    x_ready = [torch.cuda.Event() for _ in range(2)]
+    y_ready = [torch.cuda.Event() for _ in range(2)]
+    x_free = [torch.cuda.Event() for _ in range(2)]
+    y_free = [torch.cuda.Event() for _ in range(2)]
+    fork, join_in, join_out = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
+
+    def run(n):
+        fork.record(comp)
+        cin.wait_event(fork)
+        cout.wait_event(fork)
+        for i in range(n):
+            b = i & 1
+            if i >= 2:
+                cin.wait_event(x_free[b])  # step i-2's layer has read dx[b]
+            with torch.cuda.stream(cin):
+                dx[b].copy_(host_x[i % G], non_blocking=True)
+            x_ready[b].record(cin)
+            comp.wait_event(x_ready[b])
+            if i >= 2:
+                comp.wait_event(y_free[b])  # step i-2's output copy has read dout[b]
+            with torch.cuda.stream(comp):
+                ls.step(i % G, x=dx[b], out=dout[b])
+            x_free[b].record(comp)
+            y_ready[b].record(comp)
+            cout.wait_event(y_ready[b])
+            with torch.cuda.stream(cout):
+                host_out[i % G].copy_(dout[b], non_blocking=True)
+            y_free[b].record(cout)
+        join_in.record(cin)
+        join_out.record(cout)
+        comp.wait_event(join_in)
+        comp.wait_event(join_out)
+
+    run(min(steps, 2 * G))  # warm the host-side caches outside capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=comp):
+        run(steps)
+    with torch.cuda.stream(comp):
+        for _ in range(max(1, warmup // steps + 1)):
+            graph.replay()
+    times = []
+    for r in range(repeats):
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(comp)
+        with torch.cuda.stream(comp):
+            graph.replay()
+        e1.record(comp)
+        torch.cuda.synchronize()
+        barrier(world)
+        times.append(max_over_ranks(e0.elapsed_time(e1), world))
+    del graph
+    return statistics.median(times), T * H * 4, T * H * 4
 
 
 def algorithmic_bytes(ls, unique, pairs):
