@@ -366,14 +366,14 @@ __host__ __device__ inline size_t act_scale_index(int b, int pos, int npad) { re
 
 // Group-major scale record of (position group, block), 128 bytes: for each
 // position pair (2t, 2t+1), t = 0..3,
-//   at 16t:      float {d(2t), d(2t), d(2t+1), d(2t+1)}
+//   at 16t:      float {d(2t), d(2t+1), d(2t), d(2t+1)}
 //   at 64 + 16t: int   {c(2t), c(2t+1), c(2t), c(2t+1)}
 // The decode kernel's m16n8k32 MMA gives lane t the block sums of rows g and
-// g+8 at columns 2t and 2t+1; its f32 chain runs on (row g, row g+8) pairs
-// of one column with packed f32x2 operations, so it reads each column's d
-// already duplicated (one 16-byte load for both columns), and the MMA's
-// accumulator seeds (rows g and g+8 x columns 2t, 2t+1) as one 16-byte load.
-// 16 bytes per position.
+// g+8 at columns 2t and 2t+1 in accumulator registers (row g: 2t, 2t+1; row
+// g+8: 2t, 2t+1); its f32 chain runs on those column pairs with packed f32x2
+// operations, so it reads the pair's d values with one 8-byte load, and the
+// MMA's accumulator seeds (rows g and g+8 x columns 2t, 2t+1) as one 16-byte
+// load.  16 bytes per position.
 constexpr int kActScaleBytes = 128;
 __host__ __device__ inline size_t act_scale_offset_gm(int b, int pos, int nb) {
   return ((size_t)(pos >> 3) * nb + b) * kActScaleBytes;
@@ -381,16 +381,16 @@ __host__ __device__ inline size_t act_scale_offset_gm(int b, int pos, int nb) {
 __device__ __forceinline__ void store_act_scale_gm(void* base, int b, int pos, int nb, float d, int corr) {
   uint8_t* rec = static_cast<uint8_t*>(base) + act_scale_offset_gm(b, pos, nb);
   const int j = pos & 7, t = j >> 1, k = j & 1;
-  float* dd = reinterpret_cast<float*>(rec) + 4 * t + 2 * k;
+  float* dd = reinterpret_cast<float*>(rec) + 4 * t + k;
   dd[0] = d;
-  dd[1] = d;
+  dd[2] = d;
   int* c = reinterpret_cast<int*>(rec + 64) + 4 * t + k;
   c[0] = corr;
   c[2] = corr;
 }
 // d and correction of position j (0..7) of a record.
 __device__ __forceinline__ float act_rec_d(const uint8_t* rec, int j) {
-  return reinterpret_cast<const float*>(rec)[4 * (j >> 1) + 2 * (j & 1)];
+  return reinterpret_cast<const float*>(rec)[4 * (j >> 1) + (j & 1)];
 }
 __device__ __forceinline__ int act_rec_corr(const uint8_t* rec, int j) {
   return reinterpret_cast<const int*>(rec + 64)[4 * (j >> 1) + (j & 1)];

@@ -110,6 +110,45 @@ __global__ void quantize_q4_0_gguf_kernel(const float* __restrict__ x, uint8_t* 
   }
 }
 
+// Token t's block b quantised to Q8_0 (quant.rs:193-228) and stored at every
+// position the token was routed to (quantize_scatter_kernel's layout); one
+// warp, lane = element.
+template <int WQ4>
+__device__ __forceinline__ void quantize_scatter_block(const float* __restrict__ x, const int32_t* __restrict__ pos,
+                                                       int t, int b, int H, int K, int npad, int group_major,
+                                                       int8_t* __restrict__ bq, int2* __restrict__ bsc) {
+  const int nb = H / 32, lane = threadIdx.x & 31;
+  const float v = x[(size_t)t * H + b * 32 + lane];
+  float amax = fabsf(v);
+  if (!(amax > 0.f)) amax = 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = __fdiv_rn(amax, 127.0f);
+  const uint32_t d16 = f32_to_f16_trunc(scale);
+  const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+  float r = round_half_away(__fmul_rn(v, id));
+  if (r != r) r = 0.f;
+  r = fminf(fmaxf(r, -128.f), 127.f);
+  const int q = (int)r;
+  int qsum = q;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+  const int2 sc = make_int2(__float_as_int(f16_bits_to_f32(d16)), WQ4 ? kMagicI - 8 * qsum : kMagicI);
+  for (int k = 0; k < K; ++k) {
+    const int p = pos[t * K + k];
+    if (p < 0) continue;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + act_group_offset(group_major, b, p >> 3, nb, npad) +
+                   (lane >> 4) * 128 + (p & 7) * 16 + (lane & 15);
+    *dst = (uint8_t)(int8_t)q;
+    if (lane == 0) {
+      if (group_major)
+        store_act_scale_gm(bsc, b, p, nb, __int_as_float(sc.x), sc.y);
+      else
+        bsc[act_scale_index(b, p, npad)] = sc;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Dispatch: a stable counting sort of the (token, slot) pairs p = t*K + k by
 // expert id, skipping slots with alpha <= 1e-4 (model.rs:2119).  Each
@@ -341,6 +380,136 @@ __global__ void __launch_bounds__(kDispatchThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Dispatch for the smallest batches (at most 32 pairs): the same outputs as
+// dispatch_kernel (stable counting sort by expert, segments padded to 16,
+// work units, the selection when asked), computed
+// without the block-wide scans: warp 0 holds one pair per lane, finds each
+// expert's pairs with a warp match and each segment's start by summing the
+// padded counts of the experts before it over the lanes; the other warps
+// then write the per-expert tables and the work units.
+// ---------------------------------------------------------------------------
+constexpr int kDispatchSmallThreads = 512;
+constexpr int kDispatchSmallPairs = 32;
+
+__global__ void __launch_bounds__(kDispatchSmallThreads)
+    dispatch_small_kernel(int32_t* ids, float* probs, int n_pairs, int E, int e_first, int e_total,
+                          int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
+                          int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
+                          int* __restrict__ n_units, int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn,
+                          int* __restrict__ err, const float* __restrict__ logits, int K) {
+  extern __shared__ float lg[];  // [T][E] logits (selection)
+  __shared__ int s_cand[kDispatchSmallPairs];
+  __shared__ float s_cval[kDispatchSmallPairs];
+  __shared__ int s_e[kDispatchSmallPairs], s_c[kDispatchSmallPairs], s_base[kDispatchSmallPairs];
+  __shared__ int s_ugu[kDispatchSmallPairs], s_udn[kDispatchSmallPairs], s_pos[kDispatchSmallPairs];
+  __shared__ int s_nlead, s_npos;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  pdl_trigger();
+  pdl_wait();
+  const int T = n_pairs / K;
+  if (logits != nullptr) {
+    for (int i = tid; i < T * E; i += blockDim.x) lg[i] = logits[i];
+    __syncthreads();
+    // rank of (t, e) in the (value desc, id asc) order (router_topk_kernel's)
+    for (int i = tid; i < T * E; i += blockDim.x) {
+      const int t = i / E, e = i - t * E;
+      const float v = lg[i];
+      const float* row = lg + t * E;
+      int r = 0;
+      for (int f = 0; f < E; ++f) {
+        const float u = row[f];
+        r += (u > v || (u == v && f < e)) ? 1 : 0;
+      }
+      if (r < K) {
+        s_cand[t * K + r] = e;
+        s_cval[t * K + r] = v;
+      }
+    }
+    __syncthreads();
+    if (warp < T) softmax_sorted(s_cand + warp * K, s_cval + warp * K, K, warp, ids, probs);
+    __syncthreads();
+  }
+  if (warp == 0) {
+    const unsigned int full = 0xffffffffu;
+    const bool have = lane < n_pairs;
+    const int id = have ? ids[lane] : 0;
+    const float pr = have ? probs[lane] : 0.f;
+    int e = -1;
+    if (have && pr > 0.0001f) {
+      if (id < 0 || id >= e_total)
+        set_error(err, kDevBadExpert);
+      else if (id - e_first >= 0 && id - e_first < E)
+        e = id - e_first;
+    }
+    const unsigned int grp = __match_any_sync(full, e);
+    const int c = __popc(grp), rk = __popc(grp & ((1u << lane) - 1u));
+    const bool lead = e >= 0 && rk == 0;
+    int base = 0, ugu = 0, udn = 0, npos = 0, tgu = 0, tdn = 0;
+    for (int q = 0; q < 32; ++q) {
+      const int eq = __shfl_sync(full, e, q), cq = __shfl_sync(full, c, q);
+      if (__shfl_sync(full, lead ? 1 : 0, q)) {
+        const int pad = (cq + 15) & ~15, nug = (cq + NT_gu - 1) / NT_gu, nud = (cq + NT_dn - 1) / NT_dn;
+        if (eq < e) {
+          base += pad;
+          ugu += nug;
+          udn += nud;
+        }
+        npos += pad;
+        tgu += nug;
+        tdn += nud;
+      }
+    }
+    const int p_here = e >= 0 ? base + rk : -1;
+    if (have) pos[lane] = p_here;
+    s_pos[lane] = p_here;
+    const unsigned int lm = __ballot_sync(full, lead);
+    if (lead) {
+      const int slot = __popc(lm & ((1u << lane) - 1u));
+      s_e[slot] = e;
+      s_c[slot] = c;
+      s_base[slot] = base;
+      s_ugu[slot] = ugu;
+      s_udn[slot] = udn;
+    }
+    if (lane == 0) {
+      s_nlead = __popc(lm);
+      s_npos = npos;
+      n_units[0] = tgu * mt_gu;
+      n_units[1] = tdn * mt_dn;
+    }
+  }
+  __syncthreads();
+  const int nl = s_nlead, npos = s_npos;
+  for (int x = tid; x <= E; x += blockDim.x) {
+    int cx = 0, px = 0;
+    for (int j = 0; j < nl; ++j) {
+      if (s_e[j] == x) cx = s_c[j];
+      if (s_e[j] < x) px += (s_c[j] + 15) & ~15;
+    }
+    if (x < E) cnt_out[x] = cx;
+    poff[x] = px;
+  }
+  for (int i = tid; i < npos; i += blockDim.x) pair_at[i] = -1;
+  __syncthreads();
+  if (tid < n_pairs && s_pos[tid] >= 0) pair_at[s_pos[tid]] = tid;
+  // work units of each present expert: (row tile m, position tile j), j fastest
+  for (int j = warp; j < nl; j += nwarps) {
+    const int e = s_e[j], c = s_c[j], b = s_base[j];
+    for (int prod = 0; prod < 2; ++prod) {
+      const int mt = prod == 0 ? mt_gu : mt_dn, rows = prod == 0 ? rows_gu : 128;
+      const int NT = prod == 0 ? NT_gu : NT_dn, ub = prod == 0 ? s_ugu[j] : s_udn[j];
+      const int nt = (c + NT - 1) / NT;
+      int4* units = prod == 0 ? units_gu : units_dn;
+      for (int local = lane; local < nt * mt; local += 32) {
+        const int m = local / nt, jj = local - m * nt;
+        units[ub * mt + local] = make_int4(e, b + jj * NT, min(NT, c - jj * NT), m * rows);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Dispatch for large batches, in three launches over chunks of
 // kDispatchThreads pairs (the single-CTA kernel above walks the chunks one
 // after another; at 65k pairs that alone took ~0.3 ms).  The result is the
@@ -564,39 +733,8 @@ __global__ void quantize_scatter_kernel(const float* __restrict__ x, const int32
   const int nb = H / 32;
   const long long total = (long long)T * nb;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const int lane = threadIdx.x & 31;
-  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
-    const int t = (int)(w / nb), b = (int)(w % nb);
-    const float v = x[(size_t)t * H + b * 32 + lane];
-    float amax = fabsf(v);
-    if (!(amax > 0.f)) amax = 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float scale = __fdiv_rn(amax, 127.0f);
-    const uint32_t d16 = f32_to_f16_trunc(scale);
-    const float id = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
-    float r = round_half_away(__fmul_rn(v, id));
-    if (r != r) r = 0.f;
-    r = fminf(fmaxf(r, -128.f), 127.f);
-    const int q = (int)r;
-    int qsum = q;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
-    const int2 sc = make_int2(__float_as_int(f16_bits_to_f32(d16)), WQ4 ? kMagicI - 8 * qsum : kMagicI);
-    for (int k = 0; k < K; ++k) {
-      const int p = pos[t * K + k];
-      if (p < 0) continue;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(bq) + act_group_offset(group_major, b, p >> 3, nb, npad) +
-                     (lane >> 4) * 128 + (p & 7) * 16 + (lane & 15);
-      *dst = (uint8_t)(int8_t)q;
-      if (lane == 0) {
-        if (group_major)
-          store_act_scale_gm(bsc, b, p, nb, __int_as_float(sc.x), sc.y);
-        else
-          bsc[act_scale_index(b, p, npad)] = sc;
-      }
-    }
-  }
+  for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps)
+    quantize_scatter_block<WQ4>(x, pos, (int)(w / nb), (int)(w % nb), H, K, npad, group_major, bq, bsc);
 }
 
 // Large batches: the layer input is quantised once per token
@@ -1230,6 +1368,12 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
   {
     const cudaError_t st = ensure_smem(dispatch_kernel, smem, dispatch_cache);
     if (st != cudaSuccess) return st;
+  }
+  if (n_pairs <= kDispatchSmallPairs && K > 0 && (!logits || (n_pairs / K) * E <= kDispatchRankSelectMax)) {
+    const size_t ssmem = logits ? (size_t)(n_pairs / K) * E * 4 : 0;
+    return launch_pdl(dispatch_small_kernel, dim3(1), dim3(kDispatchSmallThreads), ssmem, s, idp, prp, n_pairs, E,
+                      e_first, e_total, cnt, poff, pair_at, pos, units_gu, units_dn, n_units, NT_gu, NT_dn, mt_gu,
+                      rows_gu, mt_dn, err, logits, K);
   }
   if (!logits && chunk_cnt && n_pairs > kDispatchChunkedMin) {
     const int nchunks = (n_pairs + kDispatchThreads - 1) / kDispatchThreads;

@@ -105,7 +105,7 @@ __device__ __forceinline__ void block_words(const uint32_t* qs, uint32_t (&w)[8]
 template <int WQ4, int TT>
 __device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, const uint8_t* btile, const uint8_t* rec,
                                              int nj, float (&acc)[TT]) {
-  // Tokens in pairs: for even t the record holds {d(t), d(t), d(t+1),
+  // Tokens in pairs: for even t the record holds {d(t), d(t+1), d(t),
   // d(t+1)} and {corr(t), corr(t+1), ...} as 16-byte groups, one load each.
 #pragma unroll
   for (int t = 0; t < TT; t += 2) {
@@ -118,7 +118,7 @@ __device__ __forceinline__ void block_tokens(const uint32_t (&w)[8], float dw, c
           const uint8_t* a = btile + (t + k) * 16;
           const uint4 alo = *reinterpret_cast<const uint4*>(a);
           const uint4 ahi = *reinterpret_cast<const uint4*>(a + 128);
-          const float da = __int_as_float(k ? dd.z : dd.x);
+          const float da = __int_as_float(k ? dd.y : dd.x);
           const float f =
               __fsub_rn(__int_as_float(block_isum_bits<WQ4>(w, alo, ahi, k ? cc.y : cc.x)), kMagicF);  // exact
           acc[t + k] = __fadd_rn(acc[t + k], __fmul_rn(f, __fmul_rn(dw, da)));
@@ -279,24 +279,24 @@ struct PackedFrag {
 //   acc[8q + 4i + 2h + k] += isum * (d_w(row 16i + 8h + g) * d_a(8q + 2t + k))
 // grp: group 0's activations of the block, the next group gstride bytes on;
 // rec: group 0's group-major scale record (rstride bytes to the next), from
-// which lane t takes the duplicated d_a of columns 2t, 2t+1 and the
-// accumulator seeds with one 16-byte load each.  The chain runs on packed
-// (row g, row g+8) pairs of one column: the pair's d_w is the two rows'
-// scales side by side and the column's d_a comes duplicated, so no operand
-// is rearranged in registers.  A row fragment is loaded and unpacked once for
-// all NG groups.
+// which lane t takes the d_a pair of columns 2t, 2t+1 and the accumulator
+// seeds with one load each.  The chain runs on packed column pairs of one
+// row, the MMA's own accumulator register pairs (d0, d1) and (d2, d3): the
+// pair's d_w is the row's scale twice and d_a the record's pair, so no
+// accumulator is moved between registers.  A row fragment is loaded and
+// unpacked once for all NG groups.
 template <int WQ4, int NG, class Frag>
 __device__ __forceinline__ void mma_block_rows2(const Frag& frag, const uint8_t* grp, int gstride, const uint8_t* rec,
                                                 int rstride, uint64_t one, int g, int t, float (&acc)[8 * NG]) {
   uint32_t b0[NG], b1[NG];
   uint4 seed[NG];
-  ulonglong2 da[NG];
+  uint64_t da[NG];
 #pragma unroll
   for (int q = 0; q < NG; ++q) {
     b0[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + g * 16 + 4 * t);
     b1[q] = *reinterpret_cast<const uint32_t*>(grp + q * gstride + 128 + g * 16 + 4 * t);
     seed[q] = *reinterpret_cast<const uint4*>(rec + q * rstride + 64 + 16 * t);
-    da[q] = *reinterpret_cast<const ulonglong2*>(rec + q * rstride + 16 * t);
+    da[q] = *reinterpret_cast<const uint64_t*>(rec + q * rstride + 16 * t);
   }
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
 #pragma unroll
@@ -304,15 +304,18 @@ __device__ __forceinline__ void mma_block_rows2(const Frag& frag, const uint8_t*
     uint32_t a[4];
     uint64_t dw;
     frag(i, g, t, a, dw);
+    float dwg, dwg8;
+    f2_unpack(dw, dwg, dwg8);
+    const uint64_t dw0 = f2_pack(dwg, dwg), dw1 = f2_pack(dwg8, dwg8);
 #pragma unroll
     for (int q = 0; q < NG; ++q) {
       uint32_t d[4];
       mma_block<WQ4>(d, a, b0[q], b1[q], seed[q]);
-      const uint64_t f0 = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[2])), magic);  // exact
-      const uint64_t f1 = f2_sub(f2_pack(__uint_as_float(d[1]), __uint_as_float(d[3])), magic);
+      const uint64_t f0 = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
+      const uint64_t f1 = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
       float* aq = acc + 8 * q + 4 * i;
-      f2_acc(aq[0], aq[2], f2_mul(f0, f2_mul(dw, da[q].x)), one);
-      f2_acc(aq[1], aq[3], f2_mul(f1, f2_mul(dw, da[q].y)), one);
+      f2_acc(aq[0], aq[1], f2_mul(f0, f2_mul(dw0, da[q])), one);
+      f2_acc(aq[2], aq[3], f2_mul(f1, f2_mul(dw1, da[q])), one);
     }
   }
 }
@@ -343,13 +346,14 @@ __device__ __forceinline__ void mma_block_rows2_half(const Frag& frag, const uin
   uint32_t d[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) d[j] = hi ? d1[j] : d0[j];
-  const uint64_t dw = hi ? dw1 : dw0;
-  const ulonglong2 dd = *reinterpret_cast<const ulonglong2*>(rec + 16 * th);
+  float dwg, dwg8;
+  f2_unpack(hi ? dw1 : dw0, dwg, dwg8);
+  const uint64_t da = *reinterpret_cast<const uint64_t*>(rec + 16 * th);
   const uint64_t magic = f2_pack(kMagicF, kMagicF);
-  const uint64_t f0 = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[2])), magic);  // exact
-  const uint64_t f1 = f2_sub(f2_pack(__uint_as_float(d[1]), __uint_as_float(d[3])), magic);
-  f2_acc(acc[0], acc[2], f2_mul(f0, f2_mul(dw, dd.x)), one);
-  f2_acc(acc[1], acc[3], f2_mul(f1, f2_mul(dw, dd.y)), one);
+  const uint64_t f0 = f2_sub(f2_pack(__uint_as_float(d[0]), __uint_as_float(d[1])), magic);  // exact
+  const uint64_t f1 = f2_sub(f2_pack(__uint_as_float(d[2]), __uint_as_float(d[3])), magic);
+  f2_acc(acc[0], acc[1], f2_mul(f0, f2_mul(f2_pack(dwg, dwg), da)), one);
+  f2_acc(acc[2], acc[3], f2_mul(f1, f2_mul(f2_pack(dwg8, dwg8), da)), one);
 }
 
 // The K chunks of one unit on the dp4a path, for compute thread row `c`:
@@ -502,7 +506,8 @@ __global__ void __launch_bounds__(32 * (kComp0 + kCompWarps),
   }
   // Programmatic dependent launch: the work units and the weights were
   // complete before this grid started (the kernel before it waits for the
-  // dispatch before triggering this launch, and weights are never written),
+  // dispatch before triggering this launch, or is the dispatch kernel and
+  // then does not trigger early; weights are never written),
   // so the weight producer streams right away; only the activation producer
   // waits for the previous kernel (whose output it reads), and the compute
   // warps consume nothing that has not passed through it.

@@ -345,7 +345,8 @@ def test_config2_forward(cuda, moe, oracle, synth, c2_q4, T, expert_path):
 
 @pytest.mark.parametrize("wtype,H,I,E,K,T", [(8, 1024, 512, 16, 2, 64), (8, 2816, 704, 16, 8, 9), (2, 1024, 512, 16, 2, 33),
                                              (2, 64, 32, 1, 1, 5), (8, 96, 64, 4, 4, 3), (2, 256, 32, 3, 2, 40),
-                                             (8, 512, 160, 8, 8, 100), (2, 2816, 704, 32, 8, 300)])
+                                             (8, 512, 160, 8, 8, 100), (2, 2816, 704, 32, 8, 300),
+                                             (2, 2816, 704, 128, 8, 2), (8, 1024, 512, 16, 2, 1)])
 def test_experts_shapes(cuda, moe, oracle, synth, wtype, H, I, E, K, T, expert_path):
     gu, dn, W, x = make_layer_inputs(synth, wtype, H, I, E, T, seed=H + I + E)
     scale = (0.5 + synth.normal(77, E, 0.1)).astype(np.float32)
