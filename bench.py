@@ -583,7 +583,7 @@ def stack_parity_check(ss, world, rank, layers=(0, 1, 29), n_check=4, seed=321):
             ids = ss.ep.ids if ss.ep is not None else ss.ids
         saved[l] = (all_gather_np(h, world), all_gather_np(nxt, world), all_gather_np(ids, world))
         h, nxt = nxt, h
-    ok, worst, n_ids_bad = True, 0.0, 0
+    exact, worst, worst_abs, n_ids_bad = True, 0.0, 0.0, 0
     idx = None
     for l in layers:
         # every rank regenerates in step (the quantiser runs on each device);
@@ -605,11 +605,15 @@ def stack_parity_check(ss, world, rank, layers=(0, 1, 29), n_check=4, seed=321):
         got = y[idx]
         n_ids_bad += int(np.count_nonzero(np.any(ids[idx] != r_ids, axis=1)))
         rel = float(np.linalg.norm(got.astype(np.float64) - ref) / max(np.linalg.norm(ref), 1e-30))
-        worst = max(worst, rel)
-        ok = ok and bool(np.array_equal(got, ref))
+        mx = float(np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))
+        worst, worst_abs = max(worst, rel), max(worst_abs, mx)
+        exact = exact and bool(np.array_equal(got, ref))
     if rank != 0:
         return None
-    return {"ok": ok and n_ids_bad == 0, "bit_exact": ok, "ids_exact": n_ids_bad == 0, "max_rel_l2": worst,
+    # the task's bars (ids exact, max-abs <= 1e-3 max|ref|, rel-L2 <= 1e-4); under
+    # expert parallelism the rank-order sum of partials is not bit-identical
+    ok = n_ids_bad == 0 and worst <= 1e-4 and worst_abs <= 1e-3
+    return {"ok": ok, "bit_exact": exact, "ids_exact": n_ids_bad == 0, "max_rel_l2": worst, "max_abs_frac": worst_abs,
             "layers_checked": list(layers), "tokens_checked_per_layer": int(len(idx)),
             "reference": "oracle/ (the reference's CPU FFN block restated)"}
 

@@ -276,12 +276,13 @@ __global__ void recv_gather_kernel(const uint8_t* const* __restrict__ rows, cons
   }
 }
 
-// Combine push.  CTA (j, c) for received token slot j = src * T + t and
-// chunk c of kCombThreads float4 columns: if this rank computed any of the
-// token's pairs, each thread forms its 4 columns of the slot-ordered partial
-// (sum over k ascending of (alpha_k * ydown[pos]) * scale[id], from 0; the
-// single-device combine's arithmetic, model.rs:2163-2165) and stores them
-// into rank src's partial area.
+// Combine push.  CTAs (x, c) walk the received token slots j = src * T + t
+// (j = x, x + gridDim.x, ...) over chunk c of kCombThreads float4 columns: if
+// this rank computed any of the token's pairs, each thread forms its 4
+// columns of the slot-ordered partial (sum over k ascending of (alpha_k *
+// ydown[pos]) * scale[id], from 0; the single-device combine's arithmetic,
+// model.rs:2163-2165) and stores them into rank src's partial area.  A
+// bounded grid keeps the per-CTA system-scope release of push_done rare.
 constexpr int kCombThreads = 128;
 
 __global__ void __launch_bounds__(kCombThreads)
@@ -296,47 +297,49 @@ __global__ void __launch_bounds__(kCombThreads)
   Control* mine = reinterpret_cast<Control*>(slabs[rank]);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int par = mine->step & 1u;
-  const long long j = blockIdx.x;
-  // the token's pairs here, in slot order
-  if (threadIdx.x < 32) {
-    int n = 0;
-    for (int k0 = 0; k0 < K; k0 += 32) {
-      const int k = k0 + (int)threadIdx.x;
-      const int p = k < K ? pos[j * K + k] : -1;
-      const unsigned int bal = __ballot_sync(0xffffffffu, p >= 0);
-      if (p >= 0) {
-        const int at = n + __popc(bal & ((1u << threadIdx.x) - 1u));
-        s_pos[at] = p;
-        s_alpha[at] = probs_all[j * K + k];
-        s_sc[at] = down_scale ? down_scale[ids_all[j * K + k]] : 1.0f;
-      }
-      n += __popc(bal);
-    }
-    if (threadIdx.x == 0) s_n = n;
-  }
-  __syncthreads();
-  const int n = s_n;
   const int i4 = blockIdx.y * kCombThreads + threadIdx.x;
-  if (n > 0 && i4 < H / 4) {
-    const int src = (int)(j / T), t = (int)(j % T);
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k0 = 0; k0 < n; k0 += 4) {
-      float4 y[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (k0 + u < n) y[u] = reinterpret_cast<const float4*>(ydown + (size_t)s_pos[k0 + u] * H)[i4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (k0 + u >= n) break;
-        const float a = s_alpha[k0 + u], sc = s_sc[k0 + u];
-        o.x = __fadd_rn(o.x, __fmul_rn(__fmul_rn(a, y[u].x), sc));
-        o.y = __fadd_rn(o.y, __fmul_rn(__fmul_rn(a, y[u].y), sc));
-        o.z = __fadd_rn(o.z, __fmul_rn(__fmul_rn(a, y[u].z), sc));
-        o.w = __fadd_rn(o.w, __fmul_rn(__fmul_rn(a, y[u].w), sc));
+  for (long long j = blockIdx.x; j < (long long)N * T; j += gridDim.x) {
+    // the token's pairs here, in slot order
+    if (threadIdx.x < 32) {
+      int n = 0;
+      for (int k0 = 0; k0 < K; k0 += 32) {
+        const int k = k0 + (int)threadIdx.x;
+        const int p = k < K ? pos[j * K + k] : -1;
+        const unsigned int bal = __ballot_sync(0xffffffffu, p >= 0);
+        if (p >= 0) {
+          const int at = n + __popc(bal & ((1u << threadIdx.x) - 1u));
+          s_pos[at] = p;
+          s_alpha[at] = probs_all[j * K + k];
+          s_sc[at] = down_scale ? down_scale[ids_all[j * K + k]] : 1.0f;
+        }
+        n += __popc(bal);
       }
+      if (threadIdx.x == 0) s_n = n;
     }
-    float4* dst = reinterpret_cast<float4*>(slabs[src] + L.part) + (((size_t)par * N + rank) * T + t) * (H / 4);
-    dst[i4] = o;
+    __syncthreads();
+    const int n = s_n;
+    if (n > 0 && i4 < H / 4) {
+      const int src = (int)(j / T), t = (int)(j % T);
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k0 = 0; k0 < n; k0 += 4) {
+        float4 y[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (k0 + u < n) y[u] = reinterpret_cast<const float4*>(ydown + (size_t)s_pos[k0 + u] * H)[i4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (k0 + u >= n) break;
+          const float a = s_alpha[k0 + u], sc = s_sc[k0 + u];
+          o.x = __fadd_rn(o.x, __fmul_rn(__fmul_rn(a, y[u].x), sc));
+          o.y = __fadd_rn(o.y, __fmul_rn(__fmul_rn(a, y[u].y), sc));
+          o.z = __fadd_rn(o.z, __fmul_rn(__fmul_rn(a, y[u].z), sc));
+          o.w = __fadd_rn(o.w, __fmul_rn(__fmul_rn(a, y[u].w), sc));
+        }
+      }
+      float4* dst = reinterpret_cast<float4*>(slabs[src] + L.part) + (((size_t)par * N + rank) * T + t) * (H / 4);
+      dst[i4] = o;
+    }
+    __syncthreads();  // the slot list is rebuilt for the next token
   }
   push_done(mine, slabs, rank, N, 1);
 }
@@ -344,8 +347,8 @@ __global__ void __launch_bounds__(kCombThreads)
 // Reduce: waits for the N combine pushes of this step, then out[t] = the
 // partials of the ranks that own one of t's experts, summed in rank order
 // (0 for a token with no pair); the last CTA to finish advances the step.
-// CTA (t, c) per home token and chunk of float4 columns.  After a timeout
-// `out` is left untouched.
+// CTAs (x, c) walk the home tokens t = x, x + gridDim.x, ... over chunk c of
+// float4 columns.  After a timeout `out` is left untouched.
 __global__ void __launch_bounds__(kCombThreads)
     combine_reduce_kernel(uint8_t* const* __restrict__ slabs, int rank, int N, int T, int H, int E, int K,
                           const int32_t* __restrict__ ids, const float* __restrict__ probs, float4* __restrict__ out,
@@ -356,35 +359,36 @@ __global__ void __launch_bounds__(kCombThreads)
   Control* mine = reinterpret_cast<Control*>(mine_b);
   const Layout L = slab_layout(N, T, H, K);
   const unsigned int step = mine->step, par = step & 1u;
-  const int t = blockIdx.x;
-  if (threadIdx.x < 32) {
-    const unsigned int m = owner_mask(ids, probs, t, K, E, N);
-    if (threadIdx.x == 0) {
-      s_mask = m;
-      ok = wait_counts(mine->comb, N, step + 1, limit, err) ? 1 : 0;
-    }
-  }
+  if (threadIdx.x == 0) ok = wait_counts(mine->comb, N, step + 1, limit, err) ? 1 : 0;
   __syncthreads();
   const int i4 = blockIdx.y * kCombThreads + threadIdx.x;
-  if (ok && i4 < H / 4) {
-    const unsigned int mask = s_mask;
-    const float4* part = reinterpret_cast<const float4*>(mine_b + L.part) + (size_t)par * N * T * (H / 4);
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    bool first = true;
-    for (int q = 0; q < N; ++q) {
-      if (!(mask >> q & 1u)) continue;
-      const float4 v = part[((size_t)q * T + t) * (H / 4) + i4];
-      if (first) {
-        o = v;
-        first = false;
-      } else {
-        o.x = __fadd_rn(o.x, v.x);
-        o.y = __fadd_rn(o.y, v.y);
-        o.z = __fadd_rn(o.z, v.z);
-        o.w = __fadd_rn(o.w, v.w);
-      }
+  const float4* part = reinterpret_cast<const float4*>(mine_b + L.part) + (size_t)par * N * T * (H / 4);
+  for (int t = blockIdx.x; ok && t < T; t += gridDim.x) {
+    if (threadIdx.x < 32) {
+      const unsigned int m = owner_mask(ids, probs, t, K, E, N);
+      if (threadIdx.x == 0) s_mask = m;
     }
-    out[(size_t)t * (H / 4) + i4] = o;
+    __syncthreads();
+    const unsigned int mask = s_mask;
+    if (i4 < H / 4) {
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      bool first = true;
+      for (int q = 0; q < N; ++q) {
+        if (!(mask >> q & 1u)) continue;
+        const float4 v = part[((size_t)q * T + t) * (H / 4) + i4];
+        if (first) {
+          o = v;
+          first = false;
+        } else {
+          o.x = __fadd_rn(o.x, v.x);
+          o.y = __fadd_rn(o.y, v.y);
+          o.z = __fadd_rn(o.z, v.z);
+          o.w = __fadd_rn(o.w, v.w);
+        }
+      }
+      out[(size_t)t * (H / 4) + i4] = o;
+    }
+    __syncthreads();  // s_mask is rewritten for the next token
   }
   // Every CTA has read the step count; the last one advances it.
   __syncthreads();
@@ -439,14 +443,16 @@ cudaError_t launch_ep_gather(int wtype, const uint8_t* const* rows, const int32_
 cudaError_t launch_ep_combine_push(uint8_t* const* slabs, int rank, int N, int T, int H, int K, const float* ydown,
                                    const int32_t* pos, const int32_t* ids_all, const float* probs_all,
                                    const float* down_scale, cudaStream_t s) {
-  const dim3 grid((unsigned)(N * T), (unsigned)((H / 4 + ep::kCombThreads - 1) / ep::kCombThreads));
-  return launch_pdl(ep::combine_push_kernel, grid, dim3(ep::kCombThreads), 0, s, slabs, rank, N, T, H, K, ydown, pos,
-                    ids_all, probs_all, down_scale);
+  const int ny = (H / 4 + ep::kCombThreads - 1) / ep::kCombThreads;
+  const int nx = (int)std::min<long long>((long long)N * T, std::max(1, 148 * 8 / ny));
+  return launch_pdl(ep::combine_push_kernel, dim3((unsigned)nx, (unsigned)ny), dim3(ep::kCombThreads), 0, s, slabs,
+                    rank, N, T, H, K, ydown, pos, ids_all, probs_all, down_scale);
 }
 
 cudaError_t launch_ep_reduce(uint8_t* const* slabs, int rank, int N, int T, int H, int E, int K, const int32_t* ids,
                              const float* probs, float* out, int* err, cudaStream_t s) {
-  const dim3 grid((unsigned)T, (unsigned)((H / 4 + ep::kCombThreads - 1) / ep::kCombThreads));
+  const int ny = (H / 4 + ep::kCombThreads - 1) / ep::kCombThreads;
+  const dim3 grid((unsigned)std::min(T, std::max(1, 148 * 8 / ny)), (unsigned)ny);
   ep::combine_reduce_kernel<<<grid, ep::kCombThreads, 0, s>>>(slabs, rank, N, T, H, E, K, ids, probs,
                                                                reinterpret_cast<float4*>(out),
                                                                ep::g_spin_limit.load(), err);
