@@ -88,6 +88,11 @@ KERNELS = {
     # mrml_moe_forward at most 32 tokens (E <= 256, K <= 64): the dispatch
     # kernel selects the experts itself (the library's dispatch_topk_supported)
     "router_small": ["router_logits", "topk_dispatch", "quantize", "gate_up", "down", "combine"],
+    # speculative routing (--spec 1, up to 32 tokens when H % 128 == 0 and
+    # K < E): the exact router on the library's side stream, the intervals
+    # and the candidate dispatch on the caller's
+    "router_spec": ["router_logits", "router_topk", "router_bounds", "spec_dispatch", "quantize", "gate_up", "down",
+                    "combine"],
     "zipf_logits": ["route_from_logits", "dispatch", "quantize", "gate_up", "down", "combine"],
 }
 
@@ -101,10 +106,14 @@ def expert_kernels(T):
     return ["dispatch", "quantize", "gate_up", "down", "combine"]
 
 
-def forward_kernels(T, E, K):
+SPEC = {"on": False}  # --spec
+
+
+def forward_kernels(T, E, K, H=2816):
     """Launch list of one mrml_moe_forward call."""
     if T <= 32 and E <= 256 and K <= 64:
-        return KERNELS["router_small"]
+        spec = SPEC["on"] and H % 128 == 0 and K < E
+        return KERNELS["router_spec"] if spec else KERNELS["router_small"]
     return ["router_logits", "router_topk"] + expert_kernels(T)
 
 
@@ -252,7 +261,7 @@ class LayerSet:
         self.out = torch.empty(T, H, device=device)
         self.ws = moe.new_workspace(H, I, E, K, T, device)
         self.layer_bytes = layer_bytes
-        self.kernels = forward_kernels(T, E, K) if routing == "router" else ["route_from_logits"] + expert_kernels(T)
+        self.kernels = forward_kernels(T, E, K, H) if routing == "router" else ["route_from_logits"] + expert_kernels(T)
 
     def step(self, i, x=None, out=None):
         gu, dn, W = self.layers[i % self.n_layers]
@@ -669,7 +678,7 @@ def run_stack(args):
         # per layer: the MoE launches (forward at world 1; router, expert
         # shard and the exchange kernels under expert parallelism) + the
         # prologue and epilogue
-        "gpu_launches": args.steps * nl * (2 + (len(forward_kernels(ss.T, ss.E, ss.K)) if world == 1 else
+        "gpu_launches": args.steps * nl * (2 + (len(forward_kernels(ss.T, ss.E, ss.K, ss.H)) if world == 1 else
                                                (11 if args.ep_exchange == "p2p" else 7))),
         "clocks": clk.summary(),
     }
@@ -948,6 +957,8 @@ def run_ours(args):
     moe.load_library()
     if args.expert_path:
         moe.set_expert_path(args.expert_path)
+    moe.set_speculative_routing(args.spec == 1)
+    SPEC["on"] = args.spec == 1
     steps, warmup = args.steps, args.warmup
     hbm_peak, peak_kind = peaks()
 
@@ -1204,6 +1215,9 @@ def main():
                     help="expert-parallel exchange for --gpus N > 1")
     ap.add_argument("--expert-path", type=int, default=0,
                     help="MRML_OPTION_EXPERT_PATH: 0 automatic, 1 decode dp4a, 2 tcgen05, 3 general, 4 decode MMA")
+    ap.add_argument("--spec", type=int, default=0, choices=[0, 1],
+                    help="MRML_OPTION_SPECULATIVE_ROUTING: speculative routing up to 32 tokens (1) or the "
+                         "router on the critical path (0, the library's default)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -93,6 +93,17 @@ int mrml_moe_workspace_init(void *workspace, size_t workspace_bytes, mrml_stream
 int mrml_moe_router(const float *W, const float *x, float *logits, int32_t *ids, float *probs, int H, int E, int K,
                     int T, void *workspace, size_t workspace_bytes, mrml_stream_t stream);
 
+/* Intervals lo[T][E] <= logits <= hi[T][E] that contain mrml_moe_router's
+ * logits (the reference's sequential f32 dot products, model.rs:1804-1814),
+ * computed in parallel: exact f64 products and sums plus a rigorous bound on
+ * the sequential chain's rounding, rounded outward to f32.  The interval is
+ * about H * 2^-24 times the mean |prefix sum| wide.  mrml_moe_forward uses it
+ * to select candidate experts before the exact logits are ready (speculative
+ * routing).  No counterpart in the reference.  H a multiple of 128, W and x
+ * 16-byte aligned (else MRML_ERR_UNSUPPORTED). */
+int mrml_moe_router_logit_bounds(const float *W, const float *x, float *lo, float *hi, int H, int E, int T,
+                                 mrml_stream_t stream);
+
 /* mrml_moe_router for callers that cannot allocate device memory.  No
  * counterpart in the reference (its router always had a device buffer set
  * up by the caller).  Some callers can only use buffers they were given:
@@ -377,6 +388,14 @@ enum { MRML_OPTION_DECODE_CTAS_PER_SM = 2, MRML_OPTION_DECODE_RING = 3 };
  * default, over a second; 0 restores the default).  Lets a test make a wait
  * give up quickly. */
 enum { MRML_OPTION_EXCHANGE_SPIN_LIMIT = 4 };
+/* Speculative routing in mrml_moe_forward (and the FFN block) for batches of
+ * at most 32 tokens: 0 off (default), 1 on.  The dispatch then selects, from
+ * intervals that bound the router logits' rounding
+ * (mrml_moe_router_logit_bounds), the experts that can be in the top-K, and
+ * the exact router runs on a library-owned stream beside the expert
+ * products; results are identical either way.  Off by default: on B200 the
+ * join of the two streams cost about what the shorter critical path saved. */
+enum { MRML_OPTION_SPECULATIVE_ROUTING = 5 };
 int mrml_moe_set_option(int option, int value);
 
 /* Profiling hook for benchmarks.  With n_events > 0, the following calls on

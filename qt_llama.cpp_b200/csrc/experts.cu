@@ -19,6 +19,7 @@
 // rows from HBM exactly once with the TMA bulk-copy engine, then applies it
 // to every token routed to that expert.  Integer block dots use dp4a; the
 // int32 block sum becomes an f32 through the 1.5*2^23 bit trick.
+#include <cfloat>
 #include <initializer_list>
 
 #include "common.cuh"
@@ -165,6 +166,82 @@ __device__ __forceinline__ void quantize_scatter_block(const float* __restrict__
 // ---------------------------------------------------------------------------
 constexpr int kDispatchThreads = 1024;
 
+// ---------------------------------------------------------------------------
+// Speculative selection of one token's experts (one warp; E <= 256).  With
+// intervals [lo_e, hi_e] that contain the reference's router logits, the
+// experts whose hi_e reaches tau, the K-th largest lo, contain the reference's
+// top-K: an expert e with hi_e < tau lies strictly below K others.  They
+// become the token's candidate slots ids[t*C + j] (expert ids ascending,
+// weight 1; unused slots weight 0, which the counting sort skips).  When more
+// than C experts qualify (logits within the rounding bound of one another, or
+// a bound that is not finite), the warp computes the token's exact logits with
+// the router kernel's chain and takes the exact top-K (warp_topk, the router's
+// own selection).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float exact_router_logit(const float* __restrict__ w, const float* __restrict__ x, int H) {
+  float acc = 0.f;
+  for (int i = 0; i < H; ++i) acc = __fadd_rn(acc, __fmul_rn(x[i], w[i]));
+  return acc;
+}
+
+__device__ void spec_select_token(const SpecRoute& S, int E, int t, int* cand, float* cval, int32_t* ids,
+                                  float* probs) {
+  const unsigned int full = 0xffffffffu;
+  const int lane = threadIdx.x & 31, C = S.C, K = S.K;
+  float lo[8], hi[8];
+  bool bad = false;
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int e = lane + 32 * m;
+    lo[m] = e < E ? S.lo[(size_t)t * E + e] : -INFINITY;
+    hi[m] = e < E ? S.hi[(size_t)t * E + e] : -INFINITY;
+    if (e < E && !(fabsf(lo[m]) <= FLT_MAX && fabsf(hi[m]) <= FLT_MAX)) bad = true;
+  }
+  bad = __any_sync(full, bad);
+  uint32_t taken;
+  int count = 0;
+  float tau = 0.f;
+  if (!bad) {
+    warp_topk<8>(lo, E, K, cand, cval, taken);
+    tau = cval[K - 1];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) count += __popc(__ballot_sync(full, lane + 32 * m < E && hi[m] >= tau));
+  }
+  __syncwarp();
+  if (!bad && count <= C) {
+    int j = 0;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int e = lane + 32 * m;
+      const bool in = e < E && hi[m] >= tau;
+      const unsigned int b = __ballot_sync(full, in);
+      if (in) {
+        const int slot = j + __popc(b & ((1u << lane) - 1u));
+        ids[(size_t)t * C + slot] = e;
+        probs[(size_t)t * C + slot] = 1.0f;
+      }
+      j += __popc(b);
+    }
+    for (int slot = count + lane; slot < C; slot += 32) {
+      ids[(size_t)t * C + slot] = 0;
+      probs[(size_t)t * C + slot] = 0.f;
+    }
+    return;
+  }
+  float val[8];
+#pragma unroll 1
+  for (int m = 0; m < 8; ++m) {
+    const int e = lane + 32 * m;
+    val[m] = e < E ? exact_router_logit(S.W + (size_t)e * S.H, S.x + (size_t)t * S.H, S.H) : -INFINITY;
+  }
+  warp_topk<8>(val, E, K, cand, cval, taken);
+  for (int slot = lane; slot < C; slot += 32) {
+    ids[(size_t)t * C + slot] = slot < K ? cand[slot] : 0;
+    probs[(size_t)t * C + slot] = slot < K ? 1.0f : 0.f;
+  }
+}
+
+
 //
 // With `logits` (small batches: T = n_pairs / K <= kDispatchTopkMaxTokens, E <= 256) the
 // kernel first selects each token's experts itself and writes ids and probs;
@@ -178,7 +255,7 @@ __global__ void __launch_bounds__(kDispatchThreads)
                     int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
                     int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
                     int* __restrict__ n_units, int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn,
-                    int* __restrict__ err, const float* __restrict__ logits, int K) {
+                    int* __restrict__ err, const float* __restrict__ logits, int K, SpecRoute spec) {
   pdl_trigger();
   // Dynamic shared memory: the counting sort's arrays, then, when the kernel
   // selects the experts, each warp's slots.
@@ -194,7 +271,13 @@ __global__ void __launch_bounds__(kDispatchThreads)
   // Shared memory is this CTA's own: cleared while the previous kernel ends.
   for (int i = tid; i < 4 * E + 32 * WS; i += blockDim.x) dsm[i] = 0;
   pdl_wait();
-  if (logits != nullptr && (n_pairs / K) * E <= kDispatchRankSelectMax) {
+  if (spec.lo != nullptr) {
+    const int T = n_pairs / spec.C;
+    int* tk_cand = dsm + 4 * E + 32 * WS;                          // [32][K] one warp's slots
+    float* tk_cval = reinterpret_cast<float*>(tk_cand + 32 * spec.K);  // [32][K]
+    for (int t = warp; t < T; t += kDispatchThreads / 32)
+      spec_select_token(spec, E, t, tk_cand + warp * spec.K, tk_cval + warp * spec.K, ids, probs);
+  } else if (logits != nullptr && (n_pairs / K) * E <= kDispatchRankSelectMax) {
     // The smallest batches select by rank: with the logits in shared memory,
     // the thread of (t, e) counts the experts that come before e in the
     // (value desc, id asc) order, and an expert of rank r < K lands in slot
@@ -397,7 +480,7 @@ __global__ void __launch_bounds__(kDispatchSmallThreads)
                           int32_t* __restrict__ cnt_out, int32_t* __restrict__ poff, int32_t* __restrict__ pair_at,
                           int32_t* __restrict__ pos, int4* __restrict__ units_gu, int4* __restrict__ units_dn,
                           int* __restrict__ n_units, int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn,
-                          int* __restrict__ err, const float* __restrict__ logits, int K) {
+                          int* __restrict__ err, const float* __restrict__ logits, int K, SpecRoute spec) {
   extern __shared__ float lg[];  // [T][E] logits (selection)
   __shared__ int s_cand[kDispatchSmallPairs];
   __shared__ float s_cval[kDispatchSmallPairs];
@@ -407,8 +490,13 @@ __global__ void __launch_bounds__(kDispatchSmallThreads)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   pdl_trigger();
   pdl_wait();
-  const int T = n_pairs / K;
-  if (logits != nullptr) {
+  if (spec.lo != nullptr) {
+    // T * C <= 32: each token's K slots fit in s_cand / s_cval
+    if (warp < n_pairs / spec.C)
+      spec_select_token(spec, E, warp, s_cand + warp * spec.K, s_cval + warp * spec.K, ids, probs);
+    __syncthreads();
+  } else if (logits != nullptr) {
+    const int T = n_pairs / K;
     for (int i = tid; i < T * E; i += blockDim.x) lg[i] = logits[i];
     __syncthreads();
     // rank of (t, e) in the (value desc, id asc) order (router_topk_kernel's)
@@ -1048,6 +1136,41 @@ __global__ void combine_kernel(const float* __restrict__ ydown, const int32_t* _
   out[(size_t)t * H + i] = o;
 }
 
+// Combine after a speculative dispatch: the same sum, each slot's expert
+// found among the token's C candidates (their positions in pos[t*C + j]).
+__global__ void combine_spec_kernel(const float* __restrict__ ydown, const int32_t* __restrict__ pos,
+                                    const int32_t* __restrict__ cand, const int32_t* __restrict__ ids,
+                                    const float* __restrict__ probs, const float* __restrict__ down_scale,
+                                    float* __restrict__ out, int H, int K, int C, int T, int* __restrict__ err) {
+  __shared__ int s_p[kMaxCandidates];
+  __shared__ float s_f[kMaxCandidates];
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.y;
+  if (threadIdx.x < K) {
+    const int k = threadIdx.x, id = ids[t * K + k];
+    const float alpha = probs[t * K + k];
+    int p = -1;
+    if (alpha > 0.0001f) {
+      for (int j = 0; j < C; ++j)
+        if (cand[t * C + j] == id && pos[t * C + j] >= 0) p = pos[t * C + j];
+      if (p < 0 && blockIdx.x == 0) set_error(err, kDevBadExpert);
+    }
+    s_p[k] = p;
+    s_f[k] = p >= 0 && down_scale ? down_scale[id] : 1.0f;
+  }
+  __syncthreads();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H) return;
+  float o = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const int p = s_p[k];
+    if (p < 0) continue;
+    o = __fadd_rn(o, __fmul_rn(__fmul_rn(probs[t * K + k], ydown[(size_t)p * H + i]), s_f[k]));
+  }
+  out[(size_t)t * H + i] = o;
+}
+
 // 1 / sqrt(mean(row^2) + eps) with the reference's rounding (ops.rs:29-34):
 // squares summed in index order in f32 by one thread, over a row staged in
 // shared memory (H a multiple of 4 takes float4 loads; the order is the same).
@@ -1351,18 +1474,32 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
                             int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units,
                             int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s,
-                            const float* logits, int K, int32_t* ids_out, float* probs_out, int32_t* chunk_cnt) {
+                            const float* logits, int K, int32_t* ids_out, float* probs_out, int32_t* chunk_cnt,
+                            const SpecRoute* spec) {
+  SpecRoute sp{};
+  if (spec) {
+    // speculative selection: n_pairs = T * C candidate slots
+    sp = *spec;
+    if (logits || !sp.lo || !sp.hi || !sp.W || !sp.x || sp.C < sp.K || sp.C > E || n_pairs % sp.C != 0 ||
+        !dispatch_topk_supported(E, sp.K, n_pairs / sp.C) || !ids_out || !probs_out || e_first != 0 ||
+        e_total != E)
+      return cudaErrorInvalidValue;
+  }
   if (logits && (!dispatch_topk_supported(E, K, n_pairs / (K > 0 ? K : 1)) || n_pairs % K != 0 || !ids_out ||
                  !probs_out))
     return cudaErrorInvalidValue;
   // The kernel reads ids and probs through the same pointers it writes them
   // with in the fused mode; otherwise it only reads them.
-  int32_t* idp = logits ? ids_out : const_cast<int32_t*>(ids);
-  float* prp = logits ? probs_out : const_cast<float*>(probs);
+  const bool writes = logits || sp.lo;
+  int32_t* idp = writes ? ids_out : const_cast<int32_t*>(ids);
+  float* prp = writes ? probs_out : const_cast<float*>(probs);
   // the counting sort's arrays (4 [E] + [32][E+1] ints), then the selection's
   // slots ([32 warps][K] ids and values; by rank, [T][E] logits and [T][K] slots)
   const size_t T_sel = (size_t)n_pairs / (K > 0 ? K : 1);
-  const size_t sel = !logits ? 0 : T_sel * E <= (size_t)kDispatchRankSelectMax ? T_sel * (E + 2 * K) : 64 * (size_t)K;
+  const size_t sel = sp.lo ? 64 * (size_t)sp.K
+                    : !logits ? 0
+                    : T_sel * E <= (size_t)kDispatchRankSelectMax ? T_sel * (E + 2 * K)
+                                                                   : 64 * (size_t)K;
   const size_t smem = (size_t)(4 * E + 32 * (E + 1)) * 4 + sel * 4;
   static SmemOptIn dispatch_cache;
   {
@@ -1373,9 +1510,9 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
     const size_t ssmem = logits ? (size_t)(n_pairs / K) * E * 4 : 0;
     return launch_pdl(dispatch_small_kernel, dim3(1), dim3(kDispatchSmallThreads), ssmem, s, idp, prp, n_pairs, E,
                       e_first, e_total, cnt, poff, pair_at, pos, units_gu, units_dn, n_units, NT_gu, NT_dn, mt_gu,
-                      rows_gu, mt_dn, err, logits, K);
+                      rows_gu, mt_dn, err, logits, K, sp);
   }
-  if (!logits && chunk_cnt && n_pairs > kDispatchChunkedMin) {
+  if (!writes && chunk_cnt && n_pairs > kDispatchChunkedMin) {
     const int nchunks = (n_pairs + kDispatchThreads - 1) / kDispatchThreads;
     cudaError_t st = launch_pdl(dispatch_count_kernel, dim3(nchunks), dim3(kDispatchThreads), (size_t)E * 4, s, ids,
                                 probs, n_pairs, E, e_first, e_total, chunk_cnt, err);
@@ -1393,7 +1530,7 @@ cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs,
   }
   cudaError_t st = launch_pdl(dispatch_kernel, dim3(1), dim3(kDispatchThreads), smem, s, idp, prp, n_pairs, E, e_first,
                               e_total, cnt, poff, pair_at, pos, units_gu, units_dn, n_units, NT_gu, NT_dn, mt_gu,
-                              rows_gu, mt_dn, err, logits, K);
+                              rows_gu, mt_dn, err, logits, K, sp);
   if (st != cudaSuccess) return st;
   return cudaPeekAtLastError();
 }
@@ -1472,6 +1609,15 @@ cudaError_t launch_combine(const float* ydown, const int32_t* pos, const int32_t
                            const float* down_scale, float* out, int H, int K, int T, cudaStream_t s) {
   const dim3 grid((H + 255) / 256, T);
   return launch_pdl(combine_kernel, grid, dim3(256), 0, s, ydown, pos, ids, probs, down_scale, out, H, K, T);
+}
+
+cudaError_t launch_combine_spec(const float* ydown, const int32_t* pos, const int32_t* cand, const int32_t* ids,
+                                const float* probs, const float* down_scale, float* out, int H, int K, int C, int T,
+                                int* err, cudaStream_t s) {
+  if (K > kMaxCandidates || K > 256) return cudaErrorInvalidValue;
+  const dim3 grid((H + 255) / 256, T);
+  return launch_pdl(combine_spec_kernel, grid, dim3(256), 0, s, ydown, pos, cand, ids, probs, down_scale, out, H, K,
+                    C, T, err);
 }
 
 }  // namespace mrml

@@ -71,6 +71,12 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
                                  cudaStream_t s);
 cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, int E, int K, int T, cudaStream_t s);
+// Intervals [lo, hi] (f32, [T][E]) that contain the reference's router
+// logits, from parallel f64 sums and a rigorous bound on the sequential f32
+// chain's rounding (router.cu); H a multiple of 128, 16-byte aligned rows.
+bool router_bounds_supported(const float* W, const float* x, int H);
+cudaError_t launch_router_bounds(const float* W, const float* x, float* lo, float* hi, int H, int E, int T, int* err,
+                                 cudaStream_t s);
 cudaError_t launch_quantize_rows(const float* x, int8_t* xq, float* xd, int32_t* xsum, long long n_blocks,
                                  cudaStream_t s);
 cudaError_t launch_quantize_gguf(int wtype, const float* x, uint8_t* dst, long long n_blocks, cudaStream_t s);
@@ -84,12 +90,28 @@ cudaError_t launch_ffn_epilogue(const float* attn_res, const float* mlp_raw, con
                                 float eps, cudaStream_t s);
 cudaError_t launch_geglu(const float* gate, const float* up, float* out, long long n, cudaStream_t s);
 cudaError_t launch_dense_routing(int32_t* ids, float* probs, int T, cudaStream_t s);
+// Speculative selection (small batches): the router logits' intervals
+// [lo, hi] ([T][E], launch_router_bounds), the router's weights [E][H] and
+// inputs [T][H] for tokens whose intervals do not settle the choice, the
+// reference's K and the candidate slots C per token (K <= C <= E).
+struct SpecRoute {
+  const float* lo;
+  const float* hi;
+  const float* W;
+  const float* x;
+  int H, K, C;
+};
 cudaError_t launch_dispatch(const int32_t* ids, const float* probs, int n_pairs, int E, int e_first, int e_total,
                             int32_t* cnt, int32_t* poff,
                             int32_t* pair_at, int32_t* pos, int4* units_gu, int4* units_dn, int* n_units,
                             int NT_gu, int NT_dn, int mt_gu, int rows_gu, int mt_dn, int* err, cudaStream_t s,
                             const float* logits = nullptr, int K = 0, int32_t* ids_out = nullptr,
-                            float* probs_out = nullptr, int32_t* chunk_cnt = nullptr);
+                            float* probs_out = nullptr, int32_t* chunk_cnt = nullptr,
+                            const SpecRoute* spec = nullptr);
+// Candidate slots per token of the speculative selection: K plus a few for
+// experts whose logits lie within the rounding bound of the K-th.
+constexpr int kSpecExtraSlots = 4;
+inline int spec_slots(int E, int K) { return K + kSpecExtraSlots < E ? K + kSpecExtraSlots : E; }
 // Above this many pairs (and with chunk_cnt, dispatch_chunk_ints(n_pairs, E)
 // ints of scratch) the dispatch runs as three launches over chunks of 1024
 // pairs instead of one CTA; same result.
@@ -146,6 +168,13 @@ cudaError_t launch_gemm_tc(int mode, int wtype, int NT, const uint8_t* weights, 
                            int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s);
 cudaError_t launch_combine(const float* ydown, const int32_t* pos, const int32_t* ids, const float* probs,
                            const float* down_scale, float* out, int H, int K, int T, cudaStream_t s);
+// Combine after a speculative dispatch: pos and cand are [T][C] (the
+// candidates' positions and expert ids); each of the reference's K slots
+// (ids / probs, [T][K]) finds its expert among the token's candidates.  A
+// slot whose expert is missing sets the status word's bad-expert code.
+cudaError_t launch_combine_spec(const float* ydown, const int32_t* pos, const int32_t* cand, const int32_t* ids,
+                                const float* probs, const float* down_scale, float* out, int H, int K, int C, int T,
+                                int* err, cudaStream_t s);
 
 // Expert-parallel exchange over peer memory (ep_p2p.cu).
 constexpr int kEpMaxRanks = 16;

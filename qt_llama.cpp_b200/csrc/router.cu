@@ -332,6 +332,122 @@ __global__ void __launch_bounds__(32 * kTopkWarps)
   finish_token(S.cand[wl], S.cval[wl], K, K, t, ids, probs);
 }
 
+// ---------------------------------------------------------------------------
+// Router logit intervals for the small-batch forward (speculative routing).
+// The reference's logit is the chain s_i = fl(s_{i-1} + fl(p_i)), p_i =
+// x_i * w_i, i ascending (model.rs:1804-1814).  With u = 2^-24, t = 2^-149
+// and S_i the exact prefix sums, each step gives |s_i - s_{i-1} - fl(p_i)|
+// <= u/(1-u) |s_i| and |fl(p_i) - p_i| <= u |p_i| + t, so
+//   |s_n - S_n| <= u P + n t + u/(1-u) (sum_i |S_i| + n E_n),
+// P = sum |p_i|, E_n = gamma_{n+1} (P + n t) bounding every |s_i - S_i|.
+// Lane l of a warp takes a contiguous run of m = n/32 elements and sums
+// fl(p_i) along it in f32 (the runs' totals r_l, prefixes q_i); a warp scan
+// of the totals in f64 gives each run's offset o_l and the centre c.  Each
+// f32 run sum is within G = gamma_{m+1} P + m t of the exact one, so
+//   |c - S_n| <= G + n t   and   |S_i| <= |o_l| + |q_i| + 2 (G + n t),
+//   sum_i |S_i| <= sum_l (m |o_l| + sum_i |q_i|) + 2 n (G + n t).
+// The interval is c -/+ (both bounds), with a 1e-3 relative margin for the
+// f32 sums of magnitudes (relative error below 100 u) and the evaluation,
+// rounded outward to f32.
+// A CTA stages kBE experts' router rows and kBT tokens' inputs in shared
+// memory with bulk copies; warp w takes expert w against each token.
+// ---------------------------------------------------------------------------
+constexpr int kBE = 8, kBT = 4;
+
+__host__ __device__ inline size_t router_bounds_smem(int H) { return (size_t)(kBE + kBT) * H * sizeof(float); }
+
+__global__ void __launch_bounds__(32 * kBE)
+    router_bounds_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ lo,
+                         float* __restrict__ hi, int H, int E, int T, int* __restrict__ err) {
+  extern __shared__ __align__(16) float bsm[];
+  __shared__ __align__(8) uint64_t full;
+  float* Ws = bsm;           // [kBE][H]
+  float* Xs = bsm + kBE * H; // [kBT][H]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e0 = blockIdx.x * kBE, t0 = blockIdx.y * kBT;
+  const int ne = min(kBE, E - e0), nt = min(kBT, T - t0);
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    mbar_init(&full, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // the router weights are not written by earlier kernels; the inputs are
+    if (lane == 0) mbar_arrive_expect_tx(&full, (uint32_t)((ne + nt) * H * 4));
+    __syncwarp();
+    if (lane < ne) bulk_g2s(Ws + lane * H, W + (size_t)(e0 + lane) * H, H * 4, &full);
+    pdl_wait();
+    if (lane < nt) bulk_g2s(Xs + lane * H, x + (size_t)(t0 + lane) * H, H * 4, &full);
+  }
+  if (!mbar_wait_bounded(&full, 0, err)) {
+    if (threadIdx.x == 0) mbar_wait_bounded(&full, 0, err);  // let copies in flight land
+    return;
+  }
+  if (warp >= ne) return;
+  const int per = H / 32;  // H % 128 == 0: runs of a multiple of 4 elements
+  const float4* wr = reinterpret_cast<const float4*>(Ws + warp * H + lane * per);
+  float run[kBT], absl[kBT], absp[kBT];
+#pragma unroll
+  for (int j = 0; j < kBT; ++j) {
+    run[j] = 0.f;
+    absl[j] = 0.f;
+    absp[j] = 0.f;
+  }
+#pragma unroll 2
+  for (int q = 0; q < per / 4; ++q) {
+    const float4 b = wr[q];
+#pragma unroll
+    for (int j = 0; j < kBT; ++j) {
+      if (j < nt) {
+        const float4 a = reinterpret_cast<const float4*>(Xs + j * H + lane * per)[q];
+        const float p0 = __fmul_rn(a.x, b.x), p1 = __fmul_rn(a.y, b.y);
+        const float p2 = __fmul_rn(a.z, b.z), p3 = __fmul_rn(a.w, b.w);
+        run[j] = __fadd_rn(run[j], p0);
+        absl[j] = __fadd_rn(absl[j], fabsf(run[j]));
+        run[j] = __fadd_rn(run[j], p1);
+        absl[j] = __fadd_rn(absl[j], fabsf(run[j]));
+        run[j] = __fadd_rn(run[j], p2);
+        absl[j] = __fadd_rn(absl[j], fabsf(run[j]));
+        run[j] = __fadd_rn(run[j], p3);
+        absl[j] = __fadd_rn(absl[j], fabsf(run[j]));
+        absp[j] = __fadd_rn(absp[j], __fadd_rn(__fadd_rn(fabsf(p0), fabsf(p1)), __fadd_rn(fabsf(p2), fabsf(p3))));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kBT; ++j) {
+    if (j >= nt) break;
+    // exclusive scan of the runs' totals (f64): each run's offset
+    const double r = (double)run[j];
+    double incl = r;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const double off = incl - r;
+    double sabs = (double)per * fabs(off) + (double)absl[j], sump = (double)absp[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sabs += __shfl_xor_sync(0xffffffffu, sabs, o);
+      sump += __shfl_xor_sync(0xffffffffu, sump, o);
+    }
+    const double total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+      const double u = 0x1p-24, n = (double)H, m = (double)per, t = 0x1p-149;
+      const double gam_n = (n + 1.0) * u / (1.0 - (n + 1.0) * u), gam_m = (m + 1.0) * u / (1.0 - (m + 1.0) * u);
+      const double g = gam_m * sump + m * t + n * t;     // run-sum error, plus the f64 scan's below it
+      const double en = gam_n * (sump + n * t);
+      const double sum_s = sabs + 2.0 * n * g;
+      const double bnd = (u * sump + n * t + u / (1.0 - u) * (sum_s + n * en) + g) * 1.001 + 0x1p-140;
+      const size_t o = (size_t)(t0 + j) * E + e0 + warp;
+      lo[o] = __double2float_rd(total - bnd);
+      hi[o] = __double2float_ru(total + bnd);
+    }
+  }
+}
+
 // ------------------------------------------------------------ launchers ---
 
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
@@ -360,6 +476,20 @@ cudaError_t launch_router_logits(const float* W, const float* x, float* logits, 
   cudaError_t st = ensure_smem(router_logits_kernel, smem, cache);
   if (st != cudaSuccess) return st;
   return launch_pdl(router_logits_kernel, grid, dim3(32 * kRT), smem, s, W, x, logits, H, E, T, bulk ? 1 : 0, err);
+}
+
+bool router_bounds_supported(const float* W, const float* x, int H) {
+  return H > 0 && H % 128 == 0 && router_bounds_smem(H) <= 227 * 1024 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
+}
+
+cudaError_t launch_router_bounds(const float* W, const float* x, float* lo, float* hi, int H, int E, int T, int* err,
+                                 cudaStream_t s) {
+  static SmemOptIn cache;
+  const size_t smem = router_bounds_smem(H);
+  const cudaError_t st = ensure_smem(router_bounds_kernel, smem, cache);
+  if (st != cudaSuccess) return st;
+  const dim3 grid((E + kBE - 1) / kBE, (T + kBT - 1) / kBT);
+  return launch_pdl(router_bounds_kernel, grid, dim3(32 * kBE), smem, s, W, x, lo, hi, H, E, T, err);
 }
 
 cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, int E, int K, int T, cudaStream_t s) {

@@ -43,6 +43,7 @@ SIGNATURES = {
     "mrml_moe_router": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "mrml_moe_route_from_logits": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "mrml_moe_router_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "mrml_moe_router_logit_bounds": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mrml_moe_router_noalloc_status": (_i, [_vp]),
     "mrml_moe_experts": (
         _i,
@@ -159,6 +160,13 @@ def router(W, x, logits, ids, probs, H, E, K, T, ws, stream=None):
         lib.mrml_moe_router(_ptr(W), _ptr(x), _ptr(logits), _ptr(ids), _ptr(probs), H, E, K, T, _ptr(ws),
                             ws.numel(), _stream_ptr(stream)),
     )
+
+
+def router_logit_bounds(W, x, lo, hi, H, E, T, stream=None):
+    """Intervals [lo, hi] ([T][E]) that contain the router's exact logits."""
+    _check("mrml_moe_router_logit_bounds",
+           load_library().mrml_moe_router_logit_bounds(_ptr(W), _ptr(x), _ptr(lo), _ptr(hi), H, E, T,
+                                                       _stream_ptr(stream)))
 
 
 def router_noalloc(W, x, logits, ids, probs, H, E, K, T, stream=None):
@@ -410,6 +418,15 @@ def set_expert_path(path: int) -> None:
     """0 automatic, 1 pipelined CUDA-core kernels, 2 tcgen05 tensor cores,
     3 general CUDA-core kernels (process-wide)."""
     _check("mrml_moe_set_option", load_library().mrml_moe_set_option(OPTION_EXPERT_PATH, path))
+
+
+OPTION_SPECULATIVE_ROUTING = 5
+
+
+def set_speculative_routing(on: bool) -> None:
+    """Speculative routing of batches up to 32 tokens in forward (default off;
+    results are identical either way)."""
+    _check("mrml_moe_set_option", load_library().mrml_moe_set_option(OPTION_SPECULATIVE_ROUTING, 1 if on else 0))
 
 
 def device_status(ws, stream=None):
