@@ -68,8 +68,11 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// With prefetch_bytes > 0 (a multiple of 16, `prefetch` 16-byte aligned),
+// the decode-size router kernel also asks the L2 for those bytes (a hint for
+// the expert products that follow; ignored by the large-batch kernels).
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
-                                 cudaStream_t s);
+                                 cudaStream_t s, const uint8_t* prefetch = nullptr, size_t prefetch_bytes = 0);
 cudaError_t launch_router_topk(const float* logits, int32_t* ids, float* probs, int E, int K, int T, cudaStream_t s);
 // Intervals [lo, hi] (f32, [T][E]) that contain the reference's router
 // logits, from parallel f64 sums and a rigorous bound on the sequential f32

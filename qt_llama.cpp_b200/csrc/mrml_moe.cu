@@ -154,6 +154,10 @@ Workspace carve(void* base, int H, int I, int E, int K, int T) {
 // forced path; process-wide, set from any host thread.
 std::atomic<int> g_path{0};
 
+// Bytes of expert gate/up weights the router kernel asks the L2 for
+// (MRML_OPTION_L2_PREFETCH_MIB; 0 off).
+std::atomic<long long> g_prefetch_bytes{64ll << 20};
+
 // Speculative routing of small batches (MRML_OPTION_SPECULATIVE_ROUTING):
 // 0 off (default), 1 on.  Measured on B200 at config 2 it saved the router's
 // chain on the critical path (13.0 us serialised against the intervals'
@@ -268,9 +272,20 @@ int check_workspace(void* ws, size_t ws_bytes, int H, int I, int E, int K, int T
     MRML_TRY(cuda_status(expr));       \
   } while (0)
 
+// The L2 prefetch of mrml_moe_forward: the first experts' gate/up slabs
+// (the decode kernel's first wave of work units reads the experts in id
+// order), when the batch is likely to hit most experts (T*K >= E) and the
+// router launch is the decode-size kernel that carries it.
+size_t prefetch_bytes(int wtype, int H, int I, int E, int K, int T) {
+  if ((long long)T * K < E || T > 256) return 0;
+  const size_t slab = (size_t)E * 2 * I * (H / 32) * mrml::block_bytes(base_type(wtype));
+  const size_t want = (size_t)g_prefetch_bytes.load(std::memory_order_relaxed);
+  return std::min(slab, want) & ~(size_t)15;
+}
+
 int run_router(const Workspace& w, const float* W, const float* x, float* logits, int32_t* ids, float* probs, int H,
-               int E, int K, int T, cudaStream_t s) {
-  MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, H, E, T, w.status, s));
+               int E, int K, int T, cudaStream_t s, const uint8_t* prefetch = nullptr, size_t prefetch_bytes = 0) {
+  MRML_LAUNCH(mrml::launch_router_logits(W, x, logits, H, E, T, w.status, s, prefetch, prefetch_bytes));
   MRML_LAUNCH(mrml::launch_router_topk(logits, ids, probs, E, K, T, s));
   return MRML_OK;
 }
@@ -605,12 +620,13 @@ int mrml_moe_forward(int wtype, const float* router_w, const float* router_x, co
   // Up to 32 tokens the dispatch kernel selects the experts itself (one
   // launch fewer on the decode path); the selection is the same ordering.
   // (At 64 tokens its single CTA took longer than the separate top-k launch.)
+  const size_t pf = prefetch_bytes(wtype, H, I, E, K, T);
   if (mrml::dispatch_topk_supported(E, K, T)) {
-    MRML_LAUNCH(mrml::launch_router_logits(router_w, router_x, logits, H, E, T, w.status, s));
+    MRML_LAUNCH(mrml::launch_router_logits(router_w, router_x, logits, H, E, T, w.status, s, gate_up, pf));
     return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s, 0, 0, logits, ids,
                        probs);
   }
-  MRML_TRY(run_router(w, router_w, router_x, logits, ids, probs, H, E, K, T, s));
+  MRML_TRY(run_router(w, router_w, router_x, logits, ids, probs, H, E, K, T, s, gate_up, pf));
   return run_experts(w, wtype, gate_up, down, ids, probs, down_scale, x, out, H, I, E, K, T, s);
 }
 
@@ -879,6 +895,10 @@ int mrml_moe_set_option(int option, int value) {
     case MRML_OPTION_EXCHANGE_SPIN_LIMIT:
       if (value < 0) return MRML_ERR_INVALID_ARGUMENT;
       mrml::ep_set_spin_limit((unsigned int)value);
+      return MRML_OK;
+    case MRML_OPTION_L2_PREFETCH_MIB:
+      if (value < 0 || value > 4096) return MRML_ERR_INVALID_ARGUMENT;
+      g_prefetch_bytes.store((long long)value << 20, std::memory_order_relaxed);
       return MRML_OK;
     case MRML_OPTION_SPECULATIVE_ROUTING:
       if (value < 0 || value > 1) return MRML_ERR_INVALID_ARGUMENT;

@@ -144,9 +144,14 @@ __host__ __device__ inline size_t router_rows_smem(int H) {
   return (size_t)(kRE2 + kRT) * (size_t)(H + 4) * sizeof(float);
 }
 
+// With prefetch_bytes > 0, the CTAs also ask the L2 for that many bytes from
+// `prefetch` (split evenly, in 64 KiB bulk prefetches): the expert weights the
+// next products read first, fetched while the router, dispatch and quantise
+// launches leave the HBM idle.  A hint only; nothing waits for it.
 __global__ void __launch_bounds__(32 * kRT)
     router_logits_rows_kernel(const float* __restrict__ W, const float* __restrict__ x, float* __restrict__ logits,
-                              int H, int E, int T, int* __restrict__ err) {
+                              int H, int E, int T, int* __restrict__ err, const uint8_t* prefetch,
+                              size_t prefetch_bytes) {
   extern __shared__ __align__(16) float rsm[];
   __shared__ __align__(8) uint64_t full;
   const int pitch = H + 4;
@@ -173,6 +178,18 @@ __global__ void __launch_bounds__(32 * kRT)
   if (!mbar_wait_bounded(&full, 0, err)) {
     if (threadIdx.x == 0) mbar_wait_bounded(&full, 0, err);  // let copies in flight land
     return;
+  }
+  if (warp == 1 && prefetch_bytes > 0) {
+    // this CTA's share of the prefetch, one 64 KiB chunk per lane at a time,
+    // issued once the CTA's own rows have landed
+    constexpr size_t kChunk = 64 * 1024;
+    const size_t n_chunks = (prefetch_bytes + kChunk - 1) / kChunk;
+    const size_t nct = (size_t)gridDim.x * gridDim.y, cta = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
+    for (size_t c = cta + nct * lane; c < n_chunks; c += nct * 32) {
+      const size_t off = c * kChunk;
+      const uint32_t bytes = (uint32_t)(prefetch_bytes - off < kChunk ? prefetch_bytes - off : kChunk);
+      bulk_prefetch_l2(prefetch + off, bytes);
+    }
   }
   if (warp >= nt || lane >= ne) return;
   const float* wr = Ws + lane * pitch;
@@ -451,7 +468,7 @@ __global__ void __launch_bounds__(32 * kBE)
 // ------------------------------------------------------------ launchers ---
 
 cudaError_t launch_router_logits(const float* W, const float* x, float* logits, int H, int E, int T, int* err,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, const uint8_t* prefetch, size_t prefetch_bytes) {
   static SmemOptIn cache, cache_rows, cache_tiled;
   const bool aligned = (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
   // Large batches: the tiled kernel (throughput); decode batches: whole rows
@@ -468,7 +485,10 @@ cudaError_t launch_router_logits(const float* W, const float* x, float* logits, 
     const size_t smem = router_rows_smem(H);
     cudaError_t st = ensure_smem(router_logits_rows_kernel, smem, cache_rows);
     if (st != cudaSuccess) return st;
-    return launch_pdl(router_logits_rows_kernel, grid, dim3(32 * kRT), smem, s, W, x, logits, H, E, T, err);
+    // bulk prefetches want 16-byte addresses and sizes
+    const bool pf = prefetch && ((uintptr_t)prefetch & 15) == 0 && prefetch_bytes % 16 == 0;
+    return launch_pdl(router_logits_rows_kernel, grid, dim3(32 * kRT), smem, s, W, x, logits, H, E, T, err,
+                      pf ? prefetch : nullptr, pf ? prefetch_bytes : (size_t)0);
   }
   const dim3 grid((E + kRE - 1) / kRE, (T + kRT - 1) / kRT);
   const bool bulk = H % 4 == 0 && (((uintptr_t)W | (uintptr_t)x) & 15) == 0;
