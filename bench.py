@@ -74,6 +74,8 @@ WORKLOADS = {
     "c2_t64": (2, 2816, 704, 128, 8, 64, "router"),
     "c2_t8": (2, 2816, 704, 128, 8, 8, "router"),
     "c2_t1": (2, 2816, 704, 128, 8, 1, "router"),
+    "c2_t16": (2, 2816, 704, 128, 8, 16, "router"),
+    "c2_t32": (2, 2816, 704, 128, 8, 32, "router"),
     "c3_prefill": (8, 1024, 512, 16, 2, 2048, "zipf_logits"),
     "c1_t4": (8, 1024, 512, 16, 2, 4, "router"),
     "c2_t512": (2, 2816, 704, 128, 8, 512, "router"),

@@ -384,6 +384,8 @@ enum { MRML_OPTION_EXPERT_PATH = 1 };
 /* Tuning of the decode (CUDA-core) expert kernel: CTAs per SM (1..8) and
  * the depth of its weight ring (1..8); 0 restores the automatic choice. */
 enum { MRML_OPTION_DECODE_CTAS_PER_SM = 2, MRML_OPTION_DECODE_RING = 3 };
+/* CTAs per SM of the down product alone (1..8; 0: as the option above). */
+enum { MRML_OPTION_DECODE_CTAS_PER_SM_DOWN = 7 };
 /* Poll limit of the expert-parallel exchange's bounded waits (about 2^24 by
  * default, over a second; 0 restores the default).  Lets a test make a wait
  * give up quickly. */

@@ -951,9 +951,10 @@ struct GvPlan {
 // in flight on its own).
 // Tuning overrides (mrml_moe_set_option): CTAs per SM and weight-ring depth
 // of the decode kernel; 0 = automatic.
-std::atomic<int> g_gv_per_sm{0}, g_gv_ring{0};
+std::atomic<int> g_gv_per_sm{0}, g_gv_ring{0}, g_gv_per_sm_down{0};
 
-GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma, int ng, bool packed = false) {
+GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool mma, int ng, bool packed = false,
+               int per_sm_want = 0) {
   GvPlan p{};
   const int bb = block_bytes(wtype);
   // down on packed weights streams K chunks (down_chunk_blocks); on GGUF rows a whole K per unit
@@ -969,8 +970,10 @@ GvPlan gv_plan(int mode, int wtype, int nb, int row_bytes, bool many_units, bool
   // Measured on B200 at config 2, T = 1 (99 gate/up units): 42.4 us per layer
   // step against 45.2 us with one CTA's deepest ring (the whole SM).
   const int bound = gv::ctas_per_sm(mma, mode, ng, wtype == kQ4_0, packed);
-  const int per_sm_set = g_gv_per_sm.load(), ring_set = g_gv_ring.load();
-  const int per_sm_max = per_sm_set > 0 ? per_sm_set : (many_units ? bound : std::min(bound, 3));
+  const int down_set = mode == tc::kGateUp ? 0 : g_gv_per_sm_down.load();
+  const int per_sm_set = down_set > 0 ? down_set : g_gv_per_sm.load(), ring_set = g_gv_ring.load();
+  const int per_sm_auto = per_sm_want > 0 ? std::min(per_sm_want, bound) : (many_units ? bound : std::min(bound, 3));
+  const int per_sm_max = per_sm_set > 0 ? per_sm_set : per_sm_auto;
   for (int per_sm = per_sm_max; per_sm >= 1; --per_sm) {
     const size_t budget = kSmemLimit / per_sm - (per_sm > 1 ? 1024 : 0);
     // GGUF down tiles hold a whole K (one stage per unit); several CTAs per
@@ -1005,9 +1008,10 @@ cudaError_t gv_launch(const CUtensorMap& map, const tc::Params& P, size_t smem, 
 
 }  // namespace
 
-void gv_set_tuning(int per_sm, int ring) {
+void gv_set_tuning(int per_sm, int ring, int per_sm_down) {
   g_gv_per_sm = per_sm;
   g_gv_ring = ring;
+  g_gv_per_sm_down = per_sm_down;
 }
 
 bool gv_supported(int wtype, int H, int I) {
@@ -1056,7 +1060,7 @@ cudaError_t gv_dispatch(int mode, bool q4, bool mma, int ng, const CUtensorMap& 
 
 cudaError_t launch_gemv(int mode, int wtype, bool packed, bool mma, int ng, const uint8_t* weights, int H, int I,
                         int E, const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
-                        int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s) {
+                        int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s, int per_sm) {
   if (ng != 1 && !(ng == 2 && mma)) return cudaErrorInvalidValue;
   if (packed && !gv_packed_supported(wtype, H, I)) return cudaErrorInvalidValue;
   tc::Params P{};
@@ -1085,14 +1089,14 @@ cudaError_t launch_gemv(int mode, int wtype, bool packed, bool mma, int ng, cons
       P.w_raw = weights;
     else if (!tc_make_gate_up_map(&map, weights, wtype, H, I, E, kGvRowsGateUp))
       return cudaErrorInvalidValue;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng, packed);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng, packed, per_sm);
   } else {
     P.nb = I / 32;
     P.rows = H;
     P.row_bytes = (I / 32) * bb;
     P.w_raw = weights;
     P.y = y;
-    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng, packed);
+    pl = gv_plan(mode, wtype, P.nb, P.row_bytes, many, mma, ng, packed, per_sm);
   }
   if (pl.smem == 0) return cudaErrorInvalidValue;
   P.rs = pl.rs;

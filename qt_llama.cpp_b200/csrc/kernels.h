@@ -151,12 +151,14 @@ int tc_num_sms();
 constexpr int kGvTokens = 8;
 constexpr int kGvRowsGateUp = 64;
 bool gv_supported(int wtype, int H, int I);
-void gv_set_tuning(int per_sm, int ring);
+void gv_set_tuning(int per_sm, int ring, int per_sm_down);
 // ng: position groups of 8 per work unit (1, or 2 on the MMA form);
 // packed: the weights are in mrml_moe_prepare_weights' layout.
+// per_sm > 0 asks for that many CTAs per SM (at most the kernel's bound;
+// the tuning options still take precedence); 0 chooses automatically.
 cudaError_t launch_gemv(int mode, int wtype, bool packed, bool mma, int ng, const uint8_t* weights, int H, int I,
                         int E, const int8_t* bq, const int2* bsc, const int4* units, const int* n_units, int max_units,
-                        int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s);
+                        int npad, int8_t* out_q, int2* out_s, float* y, int* err, cudaStream_t s, int per_sm = 0);
 // Whether the packed layout (and the decode kernel on it) fits these shapes.
 bool gv_packed_supported(int wtype, int H, int I);
 // Repacks raw GGUF expert weights into the decode kernel's packed layout

@@ -2,6 +2,7 @@
 // include/mrml_moe.h): argument checks, the workspace layout and the order
 // of kernel launches on the caller's stream.
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <stdint.h>
 #include <stdio.h>
@@ -324,6 +325,25 @@ Route pick_route(int wtype, bool packed, int H, int I, int E, long long pairs) {
   return mma_size ? kRouteGemvMma : kRouteGemv;
 }
 
+// CTAs per SM of the decode kernel's two products (0: its automatic
+// choice), from the expected work units per SM: the experts hit, about
+// E (1 - exp(-pairs / E)), times the row tiles of each.  Measured on B200 at
+// config 2 (packed Q4_0, warp MMA, units of 8 positions, one device): 3 CTAs
+// with deeper rings for the down product from about 10 units per SM (T = 16,
+// 32 and 64: 0.1387 -> 0.1327 ms at T = 64) but not at T = 8 (7.5 per SM), and
+// for gate/up between 4.5 and 7.5 units per SM (T = 16: 0.1120 -> 0.1059 ms),
+// where the 5 of the automatic choice lost; elsewhere the automatic choice.
+void decode_ctas_per_sm(int wtype, bool packed, bool mma, int ng_gu, int ng_dn, int E, int e_total, long long pairs,
+                        int mt_gu, int mt_dn, int& per_gu, int& per_dn) {
+  per_gu = per_dn = 0;
+  if (!packed || !mma || wtype != MRML_Q4_0 || e_total != E || E <= 0) return;
+  const double hit = E * (1.0 - std::exp(-(double)pairs / E));
+  const double sms = (double)mrml::tc_num_sms();
+  const double u_gu = hit * mt_gu / sms, u_dn = hit * mt_dn / sms;
+  if (ng_gu == 1 && u_gu > 4.5 && u_gu <= 7.5) per_gu = 3;
+  if (ng_dn == 1 && u_dn > 10.0) per_dn = 3;
+}
+
 // With topk_logits, the dispatch kernel first selects the experts from the
 // router logits and writes ids/probs (ids_out/probs_out, the buffers that
 // ids/probs point to), replacing the top-k launch (small batches).
@@ -389,10 +409,12 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
                                        w.npad, nullptr, nullptr, w.ydown, w.status, s));
     } else {
       const bool mma = route == kRouteGemvMma;
+      int per_gu = 0, per_dn = 0;
+      decode_ctas_per_sm(wtype, packed, mma, ng_gu, ng_dn, E, e_total, pairs, mt_gu, mt_dn, per_gu, per_dn);
       MRML_LAUNCH(mrml::launch_gemv(0, wtype, packed, mma, ng_gu, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units,
-                                    mu_gu, w.npad, w.ab, w.as, nullptr, w.status, s));
+                                    mu_gu, w.npad, w.ab, w.as, nullptr, w.status, s, per_gu));
       MRML_LAUNCH(mrml::launch_gemv(1, wtype, packed, mma, ng_dn, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1,
-                                    mu_dn, w.npad, nullptr, nullptr, w.ydown, w.status, s));
+                                    mu_dn, w.npad, nullptr, nullptr, w.ydown, w.status, s, per_dn));
     }
   }
   if (spec) {
@@ -876,7 +898,7 @@ int mrml_moe_quantize_q4_0(const float* src, uint8_t* dst, size_t n, mrml_stream
 }
 
 int mrml_moe_set_option(int option, int value) {
-  static std::atomic<int> gv_per_sm{0}, gv_ring{0};
+  static std::atomic<int> gv_per_sm{0}, gv_ring{0}, gv_per_sm_down{0};
   switch (option) {
     case MRML_OPTION_EXPERT_PATH:
       if (value < 0 || value > 4) return MRML_ERR_INVALID_ARGUMENT;
@@ -885,12 +907,17 @@ int mrml_moe_set_option(int option, int value) {
     case MRML_OPTION_DECODE_CTAS_PER_SM:
       if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
       gv_per_sm.store(value);
-      mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load());
+      mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load(), gv_per_sm_down.load());
       return MRML_OK;
     case MRML_OPTION_DECODE_RING:
       if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
       gv_ring.store(value);
-      mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load());
+      mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load(), gv_per_sm_down.load());
+      return MRML_OK;
+    case MRML_OPTION_DECODE_CTAS_PER_SM_DOWN:
+      if (value < 0 || value > 8) return MRML_ERR_INVALID_ARGUMENT;
+      gv_per_sm_down.store(value);
+      mrml::gv_set_tuning(gv_per_sm.load(), gv_ring.load(), gv_per_sm_down.load());
       return MRML_OK;
     case MRML_OPTION_EXCHANGE_SPIN_LIMIT:
       if (value < 0) return MRML_ERR_INVALID_ARGUMENT;
