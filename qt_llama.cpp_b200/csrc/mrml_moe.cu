@@ -328,15 +328,16 @@ Route pick_route(int wtype, bool packed, int H, int I, int E, long long pairs) {
 // CTAs per SM of the decode kernel's two products (0: its automatic
 // choice), from the expected work units per SM: the experts hit, about
 // E (1 - exp(-pairs / E)), times the row tiles of each.  Measured on B200 at
-// config 2 (packed Q4_0, warp MMA, units of 8 positions, one device): 3 CTAs
-// with deeper rings for the down product from about 10 units per SM (T = 16,
-// 32 and 64: 0.1387 -> 0.1327 ms at T = 64) but not at T = 8 (7.5 per SM), and
-// for gate/up between 4.5 and 7.5 units per SM (T = 16: 0.1120 -> 0.1059 ms),
+// config 2 (packed Q4_0, warp MMA, units of 8 positions): 3 CTAs with deeper
+// rings for the down product from about 10 units per SM (T = 16, 32 and 64:
+// 0.1387 -> 0.1327 ms at T = 64) but not at T = 8 (7.5 per SM), and for
+// gate/up between 4.5 and 7.5 units per SM (T = 16: 0.1120 -> 0.1059 ms; the
+// expert shard of 2-GPU expert parallelism, 4.8 per SM: 0.1625 -> 0.1600 ms),
 // where the 5 of the automatic choice lost; elsewhere the automatic choice.
-void decode_ctas_per_sm(int wtype, bool packed, bool mma, int ng_gu, int ng_dn, int E, int e_total, long long pairs,
-                        int mt_gu, int mt_dn, int& per_gu, int& per_dn) {
+void decode_ctas_per_sm(int wtype, bool packed, bool mma, int ng_gu, int ng_dn, int E, long long pairs, int mt_gu,
+                        int mt_dn, int& per_gu, int& per_dn) {
   per_gu = per_dn = 0;
-  if (!packed || !mma || wtype != MRML_Q4_0 || e_total != E || E <= 0) return;
+  if (!packed || !mma || wtype != MRML_Q4_0 || E <= 0) return;
   const double hit = E * (1.0 - std::exp(-(double)pairs / E));
   const double sms = (double)mrml::tc_num_sms();
   const double u_gu = hit * mt_gu / sms, u_dn = hit * mt_dn / sms;
@@ -410,7 +411,7 @@ int run_experts(const Workspace& w, int wtype, const uint8_t* gate_up, const uin
     } else {
       const bool mma = route == kRouteGemvMma;
       int per_gu = 0, per_dn = 0;
-      decode_ctas_per_sm(wtype, packed, mma, ng_gu, ng_dn, E, e_total, pairs, mt_gu, mt_dn, per_gu, per_dn);
+      decode_ctas_per_sm(wtype, packed, mma, ng_gu, ng_dn, E, pairs, mt_gu, mt_dn, per_gu, per_dn);
       MRML_LAUNCH(mrml::launch_gemv(0, wtype, packed, mma, ng_gu, gate_up, H, I, E, w.xb, w.xs, w.units_gu, n_units,
                                     mu_gu, w.npad, w.ab, w.as, nullptr, w.status, s, per_gu));
       MRML_LAUNCH(mrml::launch_gemv(1, wtype, packed, mma, ng_dn, down, H, I, E, w.ab, w.as, w.units_dn, n_units + 1,
@@ -492,10 +493,12 @@ int run_ep_experts(void* ws, int wtype, const uint8_t* gate_up, const uint8_t* d
   MRML_LAUNCH(mrml::launch_ep_gather(wtype, x.rows, w.pair_at, w.poff + Ec, H, K, w.npad, w.xb, w.xs, s));
   const int mu_gu = units_bound(Ec, K, NT, NT_gu, I, rows_gu), mu_dn = units_bound(Ec, K, NT, NT_dn, H, 128);
   const bool mma = route == kRouteGemvMma;
+  int per_gu = 0, per_dn = 0;
+  decode_ctas_per_sm(wtype, packed, mma, ng_gu, ng_dn, Ec, pairs, mt_gu, mt_dn, per_gu, per_dn);
   MRML_LAUNCH(mrml::launch_gemv(0, wtype, packed, mma, ng_gu, gate_up, H, I, Ec, w.xb, w.xs, w.units_gu, n_units,
-                                mu_gu, w.npad, w.ab, w.as, nullptr, w.status, s));
+                                mu_gu, w.npad, w.ab, w.as, nullptr, w.status, s, per_gu));
   MRML_LAUNCH(mrml::launch_gemv(1, wtype, packed, mma, ng_dn, down, H, I, Ec, w.ab, w.as, w.units_dn, n_units + 1,
-                                mu_dn, w.npad, nullptr, nullptr, w.ydown, w.status, s));
+                                mu_dn, w.npad, nullptr, nullptr, w.ydown, w.status, s, per_dn));
   MRML_LAUNCH(mrml::launch_ep_combine_push(slabs, rank, N, T, H, K, w.ydown, w.pos, x.ids_all, x.probs_all,
                                            down_scale, s));
   return MRML_OK;
