@@ -399,10 +399,10 @@ enum { MRML_OPTION_EXCHANGE_SPIN_LIMIT = 4 };
  * join of the two streams cost about what the shorter critical path saved. */
 enum { MRML_OPTION_SPECULATIVE_ROUTING = 5 };
 /* MiB of expert gate/up weights that mrml_moe_forward's router launch asks
- * the L2 to fetch ahead (0..4096; default 64) when the batch is likely to hit
- * most experts (T * K >= E, T <= 256): the experts the products read first,
- * fetched while routing leaves the HBM idle.  A cache hint; results do not
- * depend on it. */
+ * the L2 to fetch ahead (0..4096; default 64) when the batch is likely to
+ * hit nearly every expert (T * K >= 2 E, T <= 256): the experts the products
+ * read first, fetched while routing leaves the HBM idle.  A cache hint;
+ * results do not depend on it. */
 enum { MRML_OPTION_L2_PREFETCH_MIB = 6 };
 int mrml_moe_set_option(int option, int value);
 
